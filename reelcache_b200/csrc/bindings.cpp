@@ -1,0 +1,27 @@
+// Python bindings of the reelcache_b200 native extension (CUDA kernels for sm_100a and the C++
+// host fast paths).
+#include <torch/extension.h>
+
+#include <vector>
+
+namespace rc {
+void gemm_bf16_tn(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epilogue,
+                  const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& gate,
+                  const c10::optional<at::Tensor>& resid, double alpha, int64_t bn,
+                  const c10::optional<at::Tensor>& status);
+void restore_launch(const at::Tensor& jobs, const std::vector<at::Tensor>& bases, const at::Tensor& prescale,
+                    const c10::optional<at::Tensor>& status);
+void rope_store_launch(const at::Tensor& jobs);
+}  // namespace rc
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "reelcache_b200 native kernels (sm_100a) and host fast paths";
+  m.def("gemm_bf16_tn", &rc::gemm_bf16_tn, "out = epilogue(alpha * A @ B^T) on tcgen05", py::arg("A"),
+        py::arg("B"), py::arg("out"), py::arg("epilogue") = 0, py::arg("bias") = py::none(),
+        py::arg("gate") = py::none(), py::arg("resid") = py::none(), py::arg("alpha") = 1.0, py::arg("bn") = 0,
+        py::arg("status") = py::none());
+  m.def("restore_launch", &rc::restore_launch, "fused restore over <= 16 jobs", py::arg("jobs"),
+        py::arg("bases"), py::arg("prescale"), py::arg("status") = py::none());
+  m.def("rope_store_launch", &rc::rope_store_launch, "dense RoPE + cast + strided store over <= 48 jobs",
+        py::arg("jobs"));
+}

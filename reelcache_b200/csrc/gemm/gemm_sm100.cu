@@ -1,0 +1,411 @@
+// Persistent warp-specialized tcgen05 GEMM for sm_100a: D[M, N] = A[M, K] * B[N, K]^T with bf16
+// operands (both K-major, i.e. torch's x @ W^T for a Linear weight W[N, K]), fp32 accumulation in
+// TMEM, and a fused epilogue (bias, tanh-GELU, gated residual, fp32 or bf16 output).
+//
+// Roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per stage, 128-byte swizzle.
+//   warp 1      TMEM owner and MMA issuer (one elected lane issues tcgen05.mma, 4 per K block).
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31),
+//               fused math, vectorized global stores.
+// The accumulator is double-buffered in TMEM (2 x BN fp32 columns) so the epilogue of tile t
+// overlaps the main loop of tile t+1.
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include "../common/host.h"
+#include "../common/sm100.cuh"
+
+namespace rc {
+namespace gemm {
+
+enum Epilogue : int {
+  kStore = 0,         // D = acc
+  kBias = 1,          // D = acc + bias[n]
+  kBiasGelu = 2,      // D = gelu_tanh(acc + bias[n])
+  kBiasGateResid = 3, // D = resid[m, n] + (acc + bias[n]) * gate[n]   (D may alias resid)
+};
+
+struct EpiParams {
+  void* out;              // [M, ldo] bf16 or fp32
+  const __nv_bfloat16* bias;  // [N] or null
+  const float* gate;      // [N] or null (gate = 1)
+  const __nv_bfloat16* resid; // [M, ldr] or null
+  int64_t ldo;
+  int64_t ldr;
+  float alpha;            // scale applied to acc before bias
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+constexpr int kGroupM = 8;
+
+template <int BN>
+struct Config {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
+  static constexpr int kTmemCols = (2 * BN) <= 256 ? 256 : 512;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
+  const float k1 = 0.044715f;
+  float u = k0 * (x + k1 * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(u));
+}
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m_idx, int& n_idx) {
+  const int per_group = kGroupM * num_n;
+  const int group = t / per_group;
+  const int first_m = group * kGroupM;
+  const int gsize = min(num_m - first_m, kGroupM);
+  const int r = t - group * per_group;
+  m_idx = first_m + r % gsize;
+  n_idx = r / gsize;
+}
+
+template <int BN, int EPI, bool OUT_F32>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                   int K, EpiParams ep, int* status) {
+  using Cfg = Config<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drained = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (M + kBM - 1) / kBM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int kblocks = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drained, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int m_idx, n_idx;
+        tile_coords(t, num_m, num_n, m_idx, n_idx);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, status, kTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = smem + stage * Cfg::kStageBytes;
+          uint8_t* b_dst = a_dst + Cfg::kABytes;
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          tma_load_2d(a_dst, &tmA, &full[stage], kb * kBK, m_idx * kBM);
+          tma_load_2d(b_dst, &tmB, &full[stage], kb * kBK, n_idx * BN);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    constexpr uint32_t idesc = make_idesc_f16(kBM, BN, /*bf16*/ 1);
+    int stage = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (lane == 0) ok = mbar_wait(&acc_empty[buf], acc_phase ^ 1, status, kTimeoutMma);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + buf * BN;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (lane == 0) ok = mbar_wait(&full[stage], phase, status, kTimeoutMma);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_addr = smem_u32(smem + stage * Cfg::kStageBytes);
+          const uint32_t b_addr = a_addr + Cfg::kABytes;
+          const uint64_t adesc = sw128_kmajor_desc(a_addr);
+          const uint64_t bdesc = sw128_kmajor_desc(b_addr);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // Advancing 16 bf16 (32 bytes) along K inside the swizzle atom: +2 in the >>4 address.
+            mma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) mma_commit(&acc_full[buf]);
+      __syncwarp();
+    }
+    // Drain: wait (bounded) until every MMA this thread issued has completed before TMEM is freed.
+    if (lane == 0) {
+      mma_commit(drained);
+      (void)mbar_wait(drained, 0, nullptr, 0);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- Epilogue ----------------
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      int m_idx, n_idx;
+      tile_coords(t, num_m, num_n, m_idx, n_idx);
+      const int buf = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&acc_full[buf], acc_phase, status, kTimeoutEpilogue);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int row = m_idx * kBM + quarter * 32 + lane;
+      const bool row_ok = row < M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n0 = n_idx * BN + c * 32;
+        if (n0 >= N) break;  // uniform across the warp
+        uint32_t raw[32];
+        tmem_ld_32x32b_x32(tmem_base + buf * BN + c * 32 + (static_cast<uint32_t>(quarter * 32) << 16), raw);
+        tmem_wait_ld();
+        if (!row_ok) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) * ep.alpha;
+        const bool full_chunk = (n0 + 32 <= N);
+        if (EPI != kStore) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int n = n0 + j;
+            if (full_chunk || n < N) {
+              if (ep.bias != nullptr) v[j] += __bfloat162float(ep.bias[n]);
+            }
+          }
+        }
+        if (EPI == kBiasGelu) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+        }
+        if (EPI == kBiasGateResid) {
+          const __nv_bfloat16* rrow = ep.resid + static_cast<int64_t>(row) * ep.ldr + n0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int n = n0 + j;
+            if (full_chunk || n < N) {
+              const float g = ep.gate != nullptr ? ep.gate[n] : 1.0f;
+              v[j] = __bfloat162float(rrow[j]) + v[j] * g;
+            }
+          }
+        }
+        if (OUT_F32) {
+          float* orow = reinterpret_cast<float*>(ep.out) + static_cast<int64_t>(row) * ep.ldo + n0;
+          if (full_chunk && (reinterpret_cast<uintptr_t>(orow) & 15) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(orow + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < N) orow[j] = v[j];
+          }
+        } else {
+          __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(ep.out) + static_cast<int64_t>(row) * ep.ldo + n0;
+          if (full_chunk && (reinterpret_cast<uintptr_t>(orow) & 15) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint4 pk;
+              pk.x = pack_bf16x2(v[j], v[j + 1]);
+              pk.y = pack_bf16x2(v[j + 2], v[j + 3]);
+              pk.z = pack_bf16x2(v[j + 4], v[j + 5]);
+              pk.w = pack_bf16x2(v[j + 6], v[j + 7]);
+              *reinterpret_cast<uint4*>(orow + j) = pk;
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < N) orow[j] = __float2bfloat16(v[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+template <int BN, int EPI, bool OUT_F32>
+void launch(const at::Tensor& A, const at::Tensor& B, int M, int N, int K, const EpiParams& ep, int* status,
+            cudaStream_t stream) {
+  using Cfg = Config<BN>;
+  CUtensorMap tmA = make_tmap_2d(A.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, A.stride(0) * 2, kBK, kBM,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tmB = make_tmap_2d(B.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, B.stride(0) * 2, kBK, BN,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
+  auto kernel = gemm_tn_kernel<BN, EPI, OUT_F32>;
+  static bool configured = false;  // per template instance
+  if (!configured) {
+    RC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+    configured = true;
+  }
+  const int num_tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  const int grid = std::min(num_tiles, sm_count(A.get_device()));
+  kernel<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, M, N, K, ep, status);
+  RC_CUDA(cudaGetLastError());
+}
+
+// Picks the N tile that wastes the least work over the 148-SM waves.
+int pick_bn(int M, int N, int sms) {
+  const int candidates[3] = {128, 192, 256};
+  int best = 256;
+  double best_cost = 1e30;
+  const int num_m = (M + kBM - 1) / kBM;
+  for (int bn : candidates) {
+    const int num_n = (N + bn - 1) / bn;
+    const long tiles = static_cast<long>(num_m) * num_n;
+    const long waves = (tiles + sms - 1) / sms;
+    // cost ~ waves * per-tile time (proportional to bn) + small penalty for narrow tiles (B re-reads)
+    double cost = static_cast<double>(waves) * bn * (1.0 + 16.0 / bn);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+template <int EPI, bool OUT_F32>
+void dispatch_bn(int bn, const at::Tensor& A, const at::Tensor& B, int M, int N, int K, const EpiParams& ep,
+                 int* status, cudaStream_t stream) {
+  switch (bn) {
+    case 128: launch<128, EPI, OUT_F32>(A, B, M, N, K, ep, status, stream); break;
+    case 192: launch<192, EPI, OUT_F32>(A, B, M, N, K, ep, status, stream); break;
+    default: launch<256, EPI, OUT_F32>(A, B, M, N, K, ep, status, stream); break;
+  }
+}
+
+}  // namespace gemm
+
+// out[M, N] = epilogue(alpha * A[M, K] @ B[N, K]^T). A and B bf16 with unit stride along K.
+void gemm_bf16_tn(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epilogue,
+                  const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& gate,
+                  const c10::optional<at::Tensor>& resid, double alpha, int64_t bn,
+                  const c10::optional<at::Tensor>& status) {
+  check_cuda_tensor(A, "A");
+  check_cuda_tensor(B, "B");
+  check_cuda_tensor(out, "out");
+  RC_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "A and B must be bfloat16");
+  RC_CHECK(A.dim() == 2 && B.dim() == 2 && out.dim() == 2, "A, B and out must be 2-D");
+  RC_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && out.stride(1) == 1, "inner dimensions must be contiguous");
+  const int M = static_cast<int>(A.size(0));
+  const int K = static_cast<int>(A.size(1));
+  const int N = static_cast<int>(B.size(0));
+  RC_CHECK(B.size(1) == K, "A and B disagree on K");
+  RC_CHECK(out.size(0) == M && out.size(1) == N, "out must be [M, N]");
+  RC_CHECK(K % 8 == 0, "K must be a multiple of 8 (16-byte TMA rows)");
+  RC_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
+  const bool out_f32 = out.scalar_type() == at::kFloat;
+  RC_CHECK(out_f32 || out.scalar_type() == at::kBFloat16, "out must be float32 or bfloat16");
+  c10::cuda::CUDAGuard guard(A.device());
+  gemm::EpiParams ep;
+  ep.out = out.data_ptr();
+  ep.ldo = out.stride(0);
+  ep.alpha = static_cast<float>(alpha);
+  ep.bias = nullptr;
+  ep.gate = nullptr;
+  ep.resid = nullptr;
+  ep.ldr = 0;
+  if (bias.has_value() && bias->defined()) {
+    RC_CHECK(bias->scalar_type() == at::kBFloat16 && bias->is_contiguous() && bias->numel() == N,
+             "bias must be a contiguous bfloat16 [N] vector");
+    ep.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  }
+  if (gate.has_value() && gate->defined()) {
+    RC_CHECK(gate->scalar_type() == at::kFloat && gate->is_contiguous() && gate->numel() == N,
+             "gate must be a contiguous float32 [N] vector");
+    ep.gate = gate->data_ptr<float>();
+  }
+  if (epilogue == gemm::kBiasGateResid) {
+    RC_CHECK(resid.has_value() && resid->defined(), "gated residual epilogue needs resid");
+    RC_CHECK(resid->scalar_type() == at::kBFloat16 && resid->dim() == 2 && resid->stride(1) == 1 &&
+                 resid->size(0) == M && resid->size(1) == N,
+             "resid must be a bfloat16 [M, N] matrix with unit inner stride");
+    RC_CHECK(!out_f32, "gated residual epilogue writes bfloat16");
+    ep.resid = reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr());
+    ep.ldr = resid->stride(0);
+  }
+  int* st = status_ptr(status);
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(A.get_device()).stream();
+  const int sms = sm_count(A.get_device());
+  const int tile_n = bn > 0 ? static_cast<int>(bn) : gemm::pick_bn(M, N, sms);
+  RC_CHECK(tile_n == 128 || tile_n == 192 || tile_n == 256, "bn must be 128, 192 or 256");
+  switch (epilogue) {
+    case gemm::kStore:
+      if (out_f32)
+        gemm::dispatch_bn<gemm::kStore, true>(tile_n, A, B, M, N, K, ep, st, stream);
+      else
+        gemm::dispatch_bn<gemm::kStore, false>(tile_n, A, B, M, N, K, ep, st, stream);
+      break;
+    case gemm::kBias:
+      if (out_f32)
+        gemm::dispatch_bn<gemm::kBias, true>(tile_n, A, B, M, N, K, ep, st, stream);
+      else
+        gemm::dispatch_bn<gemm::kBias, false>(tile_n, A, B, M, N, K, ep, st, stream);
+      break;
+    case gemm::kBiasGelu:
+      gemm::dispatch_bn<gemm::kBiasGelu, false>(tile_n, A, B, M, N, K, ep, st, stream);
+      break;
+    case gemm::kBiasGateResid:
+      gemm::dispatch_bn<gemm::kBiasGateResid, false>(tile_n, A, B, M, N, K, ep, st, stream);
+      break;
+    default:
+      RC_CHECK(false, "unknown epilogue");
+  }
+}
+
+}  // namespace rc
