@@ -12,6 +12,7 @@ void gemm_bf16_tn(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
 void restore_launch(const at::Tensor& jobs, const std::vector<at::Tensor>& bases, const at::Tensor& prescale,
                     const c10::optional<at::Tensor>& status);
 void rope_store_launch(const at::Tensor& jobs);
+void unpack_launch(const at::Tensor& jobs, int64_t device);
 }  // namespace rc
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -24,4 +25,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bases"), py::arg("prescale"), py::arg("status") = py::none());
   m.def("rope_store_launch", &rc::rope_store_launch, "dense RoPE + cast + strided store over <= 48 jobs",
         py::arg("jobs"));
+  m.def("unpack_launch", &rc::unpack_launch, "mosaic pictures -> dense uint8 [N, K_pad] over <= 48 jobs",
+        py::arg("jobs"), py::arg("device"));
 }

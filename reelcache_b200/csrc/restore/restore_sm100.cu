@@ -4,18 +4,20 @@
 //   native slot <- cast(RoPE(dequantize(unpack(pixels)) @ Q[:rank]))
 //
 // One persistent launch covers a group of jobs (one job = one chunk's K or V of one layer).
-// Work item = (job, 128-token tile, 256-channel tile). Roles (320 threads, one CTA per SM):
+// Work item = (job, 128-token tile, 256-channel tile). Roles (448 threads, one CTA per SM):
 //   warp 0      TMA producer of the basis tile Qt[256 channels x 64 rank] (fp16, 128-byte swizzle,
 //               no multicast) from the transposed, zero-padded device basis of the job.
 //   warp 1      TMEM owner + MMA issuer: per 64-rank block, 4 x tcgen05.mma kind::f16 for the high
 //               FP16 half of the coefficients and 4 for the low half (precision "fp16x2").
-//   warps 2..5  epilogue: tcgen05.ld, multiply by the exact inverse prescale, interleaved-pair RoPE
-//               on the three (t, h, w) sections from FP32 cos/sin tables, cast, strided store into
-//               the native [T, H, D] / [H, T, D] slot.
-//   warps 6..9  gather producers: read the 8-bit pixels through the reelcache.channel_tiles.v1
-//               mosaic (or a dense [N, rank] uint8 / fp32 coefficient matrix), dequantize exactly as
-//               `float(pixel) * scale + offset` with two roundings, prescale by an exact power of two,
-//               split into FP16 hi + lo and write both K-major 128-byte-swizzled A tiles to SMEM.
+//   warps 2..9  epilogue: warp w reads TMEM lane quarter (w % 4) and one 128-column half of the tile;
+//               multiplies by the exact inverse prescale, applies interleaved-pair RoPE on the three
+//               (t, h, w) sections from FP32 cos/sin tables (stored [pairs, rows]; loaded one
+//               32-column chunk ahead), casts and stores into the native [T, H, D] / [H, T, D] slot.
+//   warps 10..13 gather producers (thread = token row): read 64 rank columns of a dense uint8
+//               [N, K_pad] coefficient matrix as four 16-byte vectors (decoded pictures are first
+//               unpacked into that layout by csrc/restore/unpack.cu) or an fp32 matrix, dequantize
+//               exactly as `float(pixel) * scale + offset` with two roundings, prescale by an exact
+//               power of two, split into FP16 hi + lo and write both K-major 128-byte-swizzled A tiles.
 // Three pipeline stages of {A_hi 16 KB, A_lo 16 KB, B 32 KB}; accumulators double-buffered in TMEM.
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -34,14 +36,19 @@ constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;
 constexpr int kStages = 3;
-constexpr int kThreads = 320;
+constexpr int kGatherWarps = 4;
+constexpr int kEpilogueWarps = 8;
+constexpr int kGatherThreads = kGatherWarps * 32;
+constexpr int kGatherWarp0 = 2 + kEpilogueWarps;
+constexpr int kThreads = (kGatherWarp0 + kGatherWarps) * 32;  // 14 warps
 constexpr int kATileBytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBTileBytes = kBN * kBK * 2;   // 32 KB
 constexpr int kStageBytes = 2 * kATileBytes + kBTileBytes;
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+constexpr int kTableBytes = 2 * 2 * kBK * 4 + 16;  // double-buffered {scale, offset} + abort flags
+constexpr int kSmemBytes = kStages * kStageBytes + kTableBytes + 1024 + 256;
 constexpr int kTmemCols = 512;
 
-enum SourceKind : int { kPictures = 0, kMatrixU8 = 1, kMatrixF32 = 2 };
+enum SourceKind : int { kMatrixU8 = 1, kMatrixF32 = 2 };
 enum OutDtype : int { kOutBF16 = 0, kOutF16 = 1, kOutF32 = 2 };
 
 struct JobDesc {
@@ -82,71 +89,91 @@ __device__ __forceinline__ void decode_work(const Params& p, int w, int& j, int&
   n_tile = local - m_tile * p.jobs[j].n_tiles;
 }
 
-// Dequantized FP32 coefficient (token, k) of a job; 0 outside the rank. `pix` is the token's
-// (y * row_stride + x) picture offset and `frame` its frame (pictures only).
-__device__ __forceinline__ float load_coefficient(const JobDesc& jb, int token, int frame, int64_t pix, int k) {
-  if (k >= jb.rank) return 0.0f;
-  if (jb.src_kind == kPictures) {
-    const int segment = k / jb.slots;
-    int cell = k - segment * jb.slots;
-    const int plane = cell % jb.planes;
-    cell /= jb.planes;
-    const int cell_row = cell / jb.grid_cols;
-    const int cell_col = cell - cell_row * jb.grid_cols;
-    const int64_t off = jb.pic_off[segment * jb.frames + frame] + plane * jb.plane_stride +
-                        static_cast<int64_t>(cell_row) * jb.height * jb.pic_row_stride +
-                        static_cast<int64_t>(cell_col) * jb.width + pix;
-    const float p = static_cast<float>(__ldg(jb.src + off));
-    return __fadd_rn(__fmul_rn(p, __ldg(jb.scale + k)), __ldg(jb.offset + k));
+// Per-K-block affine table (scale, offset of the 64 rank columns), built by the first 64 gather
+// threads and double-buffered across K blocks.
+struct ColumnTable {
+  float scale[kBK];
+  float offset[kBK];
+};
+
+__device__ __forceinline__ void build_table(const JobDesc& jb, int k0, int t, ColumnTable* tab) {
+  if (t >= kBK) return;
+  const int k = k0 + t;
+  float sc = 0.0f, of = 0.0f;
+  if (k < jb.rank && jb.src_kind == kMatrixU8) {
+    sc = __ldg(jb.scale + k);
+    of = __ldg(jb.offset + k);
   }
-  if (jb.src_kind == kMatrixU8) {
-    const uint8_t* rowp = jb.src + static_cast<int64_t>(token) * jb.src_row_stride;
-    return __fadd_rn(__fmul_rn(static_cast<float>(__ldg(rowp + k)), __ldg(jb.scale + k)), __ldg(jb.offset + k));
-  }
-  const float* rowp = reinterpret_cast<const float*>(jb.src) + static_cast<int64_t>(token) * jb.src_row_stride;
-  return __ldg(rowp + k);
+  tab->scale[t] = sc;
+  tab->offset[t] = of;
 }
 
-// Gather + dequantize + split of one [128 x 64] coefficient block into the hi/lo A tiles.
-// Thread `row` (0..127) owns one token row of the tile and writes it 8 columns (16 bytes) at a time.
-__device__ __forceinline__ void gather_block(const JobDesc& jb, int row, int m0, int k0, uint8_t* a_hi,
-                                             uint8_t* a_lo) {
+__device__ __forceinline__ void split_store(const float (&v)[8], float prescale, int row, int col, uint8_t* a_hi,
+                                            uint8_t* a_lo) {
+  uint32_t hi[4], lo[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float s0 = v[2 * e] * prescale;
+    const float s1 = v[2 * e + 1] * prescale;
+    const __half h0 = __float2half_rn(s0);
+    const __half h1 = __float2half_rn(s1);
+    const __half l0 = __float2half_rn(s0 - __half2float(h0));
+    const __half l1 = __float2half_rn(s1 - __half2float(h1));
+    hi[e] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
+    lo[e] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+  }
+  const uint32_t off = sw128_offset_16bit(row, col);
+  *reinterpret_cast<uint4*>(a_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  *reinterpret_cast<uint4*>(a_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
+// Dequantize + split one token row (64 rank columns) of a [128 x 64] coefficient block into the
+// hi/lo A tiles. uint8 sources are read as 4 x 16-byte vectors (rows padded to 64 columns).
+__device__ __forceinline__ void gather_row(const JobDesc& jb, const ColumnTable* tab, int row, int m0, int k0,
+                                           uint8_t* a_hi, uint8_t* a_lo) {
   const int token = m0 + row;
   const bool valid = token < jb.tokens;
-  int frame = 0;
-  int64_t pix = 0;
-  if (valid && jb.src_kind == kPictures) {
-    const int per_frame = jb.height * jb.width;
-    frame = token / per_frame;
-    const int rem = token - frame * per_frame;
-    const int y = rem / jb.width;
-    pix = static_cast<int64_t>(y) * jb.pic_row_stride + (rem - y * jb.width);
-  }
-#pragma unroll 1
-  for (int c = 0; c < kBK / 8; ++c) {
-    float vals[8];
+  if (jb.src_kind == kMatrixU8) {
+    uint4 raw[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+    if (valid) {
+      const uint4* rowp = reinterpret_cast<const uint4*>(jb.src + static_cast<int64_t>(token) * jb.src_row_stride + k0);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) vals[i] = valid ? load_coefficient(jb, token, frame, pix, k0 + c * 8 + i) : 0.0f;
-    // Prescale by an exact power of two, then split into FP16 hi + lo.
-    uint32_t hi[4], lo[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float s0 = vals[2 * e] * jb.prescale;
-      const float s1 = vals[2 * e + 1] * jb.prescale;
-      const __half h0 = __float2half_rn(s0);
-      const __half h1 = __float2half_rn(s1);
-      const __half l0 = __float2half_rn(s0 - __half2float(h0));
-      const __half l1 = __float2half_rn(s1 - __half2float(h1));
-      hi[e] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
-      lo[e] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+      for (int i = 0; i < 4; ++i) raw[i] = __ldg(rowp + i);
     }
-    const uint32_t off = sw128_offset_16bit(row, c * 8);
-    *reinterpret_cast<uint4*>(a_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4*>(a_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 q = raw[c >> 1];
+      const uint32_t w0 = (c & 1) ? q.z : q.x;
+      const uint32_t w1 = (c & 1) ? q.w : q.y;
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t byte = ((e < 4 ? w0 : w1) >> ((e & 3) * 8)) & 0xffu;
+        const int kk = c * 8 + e;
+        v[e] = valid ? __fadd_rn(__fmul_rn(static_cast<float>(byte), tab->scale[kk]), tab->offset[kk]) : 0.0f;
+      }
+      split_store(v, jb.prescale, row, c * 8, a_hi, a_lo);
+    }
+  } else {
+    const float* rowp = reinterpret_cast<const float*>(jb.src) + static_cast<int64_t>(token) * jb.src_row_stride + k0;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int kk = c * 8 + e;
+        v[e] = (valid && k0 + kk < jb.rank) ? __ldg(rowp + kk) : 0.0f;
+      }
+      split_store(v, jb.prescale, row, c * 8, a_hi, a_lo);
+    }
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_constant__ Params p, int* status) {
+__device__ __forceinline__ void gather_barrier() {
+  asm volatile("bar.sync 1, %0;" ::"r"(kGatherThreads) : "memory");
+}
+
+__global__ void __maxnreg__(128) restore_kernel(const __grid_constant__ Params p, int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
@@ -161,12 +188,12 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1 + 4);  // TMA expect_tx arrival + one arrival per gather warp
+      mbar_init(&full[s], 1 + kGatherWarps);  // TMA expect_tx arrival + one arrival per gather warp
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], kEpilogueWarps);
     }
     mbar_init(drained, 1);
     fence_barrier_init();
@@ -256,9 +283,11 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
       (void)mbar_wait(drained, 0, nullptr, 0);
     }
     __syncwarp();
-  } else if (warp < 6) {
-    // ---------------- Epilogue ----------------
+  } else if (warp < kGatherWarp0) {
+    // ---------------- Epilogue (8 warps) ----------------
+    // Warp e = warp - 2 reads TMEM lane quarter (warp % 4) and the column half (e / 4) of the tile.
     const int quarter = warp & 3;
+    const int col_half = (warp - 2) >> 2;
     int local = 0;
     for (int w = blockIdx.x; w < p.total_work; w += gridDim.x, ++local) {
       int j, m_tile, n_tile;
@@ -266,11 +295,6 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
       const JobDesc& jb = p.jobs[j];
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      bool ok = true;
-      if (lane == 0) ok = mbar_wait(&acc_full[buf], acc_phase, status, kTimeoutEpilogue);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      tc_fence_after();
       const int token = m_tile * kBM + quarter * 32 + lane;
       const bool valid = token < jb.tokens;
       int frame = 0, y = 0, x = 0;
@@ -281,42 +305,60 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
         y = rem / jb.width;
         x = rem - y * jb.width;
       }
+      const int row_t = jb.rope_dense ? jb.row_t + token : jb.row_t + frame;
+      const int row_h = jb.row_h + y;
+      const int row_w = jb.row_w + x;
+      // RoPE factors of the next 32-column chunk, loaded one chunk ahead (first one before the wait).
+      float cs_next[16], sn_next[16];
+      auto load_rope = [&](int chunk, float (&cs)[16], float (&sn)[16]) {
+        const int n0 = n_tile * kBN + col_half * (kBN / 2) + chunk * 32;
+        const int d0 = n0 % jb.head_dim;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int pair = (d0 >> 1) + i;
+          const int trow = (jb.rope_dense || pair < jb.sec_t) ? row_t : (pair < jb.sec_t + jb.sec_h ? row_h : row_w);
+          const int64_t idx = static_cast<int64_t>(pair) * jb.rope_rs + trow;  // tables stored [pairs, rows]
+          cs[i] = (jb.rope && valid && n0 < jb.channels) ? __ldg(jb.cos + idx) : 1.0f;
+          sn[i] = (jb.rope && valid && n0 < jb.channels) ? __ldg(jb.sin + idx) : 0.0f;
+        }
+      };
+      load_rope(0, cs_next, sn_next);
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&acc_full[buf], acc_phase, status, kTimeoutEpilogue);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        const int n0 = n_tile * kBN + c * 32;
+      for (int c = 0; c < kBN / 64; ++c) {
+        const int n0 = n_tile * kBN + col_half * (kBN / 2) + c * 32;
         if (n0 >= jb.channels) break;  // uniform: channels is a multiple of 32 (checked on the host)
         uint32_t raw[32];
-        tmem_ld_32x32b_x32(tmem_base + buf * kBN + c * 32 + (static_cast<uint32_t>(quarter * 32) << 16), raw);
+        tmem_ld_32x32b_x32(tmem_base + buf * kBN + col_half * (kBN / 2) + c * 32 +
+                               (static_cast<uint32_t>(quarter * 32) << 16),
+                           raw);
+        float cs[16], sn[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          cs[i] = cs_next[i];
+          sn[i] = sn_next[i];
+        }
+        if (c + 1 < kBN / 64) load_rope(c + 1, cs_next, sn_next);
         tmem_wait_ld();
         if (!valid) continue;
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]) * jb.inverse;
-        const int head = n0 / jb.head_dim;
-        const int d0 = n0 - head * jb.head_dim;
         if (jb.rope) {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int pair = (d0 >> 1) + i;
-            int trow;
-            if (jb.rope_dense) {
-              trow = jb.row_t + token;
-            } else if (pair < jb.sec_t) {
-              trow = jb.row_t + frame;
-            } else if (pair < jb.sec_t + jb.sec_h) {
-              trow = jb.row_h + y;
-            } else {
-              trow = jb.row_w + x;
-            }
-            const int64_t idx = static_cast<int64_t>(trow) * jb.rope_rs + pair;
-            const float cs = __ldg(jb.cos + idx);
-            const float sn = __ldg(jb.sin + idx);
             const float e = v[2 * i];
             const float o = v[2 * i + 1];
-            v[2 * i] = e * cs - o * sn;
-            v[2 * i + 1] = e * sn + o * cs;
+            v[2 * i] = e * cs[i] - o * sn[i];
+            v[2 * i + 1] = e * sn[i] + o * cs[i];
           }
         }
+        const int head = n0 / jb.head_dim;
+        const int d0 = n0 - head * jb.head_dim;
         const int64_t base = static_cast<int64_t>(token) * jb.dst_ts + static_cast<int64_t>(head) * jb.dst_hs +
                              static_cast<int64_t>(d0) * jb.dst_ds;
         if (jb.out_dtype == kOutF32) {
@@ -350,21 +392,35 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   } else {
-    // ---------------- Gather producers ----------------
-    const int row = threadIdx.x - 192;  // 0..127
+    // ---------------- Gather producers (4 warps, thread = token row) ----------------
+    const int gt = threadIdx.x - kGatherWarp0 * 32;  // 0..127
+    const int row = gt;
+    ColumnTable* tables = reinterpret_cast<ColumnTable*>(smem + kStages * kStageBytes);
+    // Abort flags, double-buffered by iteration parity so a flag raised at iteration k+1 is never
+    // seen by a warp still finishing iteration k (every gather warp leaves at the same iteration).
+    volatile int* abort_flags = reinterpret_cast<volatile int*>(tables + 2);
+    if (gt < 2) abort_flags[gt] = 0;
+    gather_barrier();
     int stage = 0;
     uint32_t phase = 0;
+    int iter = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < p.total_work && ok; w += gridDim.x) {
       int j, m_tile, n_tile;
       decode_work(p, w, j, m_tile, n_tile);
       const JobDesc& jb = p.jobs[j];
-      for (int kb = 0; kb < jb.kblocks; ++kb) {
-        if (lane == 0) ok = mbar_wait(&empty[stage], phase ^ 1, status, kTimeoutGather);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
+      for (int kb = 0; kb < jb.kblocks; ++kb, ++iter) {
+        ColumnTable* tab = tables + (iter & 1);
+        build_table(jb, kb * kBK, gt, tab);
+        if (lane == 0) {
+          ok = mbar_wait(&empty[stage], phase ^ 1, status, kTimeoutGather);
+          if (!ok) abort_flags[iter & 1] = 1;
+        }
+        gather_barrier();  // table and abort flag visible to every gather thread
+        ok = abort_flags[iter & 1] == 0;
         if (!ok) break;
         uint8_t* a_hi = smem + stage * kStageBytes;
-        gather_block(jb, row, m_tile * kBM, kb * kBK, a_hi, a_hi + kATileBytes);
+        gather_row(jb, tab, row, m_tile * kBM, kb * kBK, a_hi, a_hi + kATileBytes);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full[stage]);
@@ -446,6 +502,12 @@ void restore_launch(const at::Tensor& jobs, const std::vector<at::Tensor>& bases
     jb.prescale = ps[2 * i];
     jb.inverse = ps[2 * i + 1];
     RC_CHECK(jb.tokens >= 1 && jb.rank >= 1, "job needs tokens and rank");
+    RC_CHECK(jb.src_kind == restore::kMatrixU8 || jb.src_kind == restore::kMatrixF32,
+             "source must be a uint8 or float32 coefficient matrix (pictures are unpacked first)");
+    RC_CHECK(jb.src_kind != restore::kMatrixU8 ||
+                 (reinterpret_cast<uintptr_t>(jb.src) % 16 == 0 && jb.src_row_stride % 16 == 0 &&
+                  jb.src_row_stride >= ((jb.rank + 63) / 64) * 64),
+             "uint8 coefficient rows must be 16-byte aligned and padded to a multiple of 64 columns");
     RC_CHECK(jb.channels % 32 == 0 && jb.head_dim % 32 == 0 && jb.channels % jb.head_dim == 0,
              "channels and head_dim must be multiples of 32");
     RC_CHECK(qt.size(0) == jb.channels && qt.size(1) % 64 == 0 && qt.size(1) >= jb.rank,

@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kThreads) rope_store_kernel(const __grid_const
       else if (pair < jb.sec_t) row = jb.row_t + frame;
       else if (pair < jb.sec_t + jb.sec_h) row = jb.row_h + y;
       else row = jb.row_w + x;
-      const int64_t idx = static_cast<int64_t>(row) * jb.rope_rs + pair;
+      const int64_t idx = static_cast<int64_t>(pair) * jb.rope_rs + row;  // tables stored [pairs, rows]
       const float cs = jb.cos[idx];
       const float sn = jb.sin[idx];
       const float e = v[2 * i], o = v[2 * i + 1];

@@ -345,6 +345,23 @@ class RopeTable:
             self._device_cache[device] = entry
         return entry[0], entry[1]
 
+    def kernel_tables_t(self, device, stream=None):
+        """Transposed FP32 ``(cos, sin)`` ``[pairs, rows]`` for the sm_100a kernels: lanes of a warp
+        hold consecutive tokens, so the rows they read for one pair are adjacent in memory."""
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        stamp = self._stamp()
+        key = ("t", device)
+        entry = self._device_cache.get(key)
+        if entry is None or entry[2] != stamp:
+            cos, sin = self.kernel_tables(device, stream)
+            ctx = torch.cuda.stream(stream) if (stream is not None and device.type == "cuda") else _null()
+            with torch.inference_mode(False), torch.no_grad(), ctx:
+                entry = (cos.t().contiguous(), sin.t().contiguous(), stamp)
+            self._device_cache[key] = entry
+        return entry[0], entry[1]
+
 
 @dataclass(frozen=True, eq=False)
 class RopePositions:
@@ -965,43 +982,85 @@ def _rope_fields(job, device, stream):
     if job.rope is None:
         return (0, 0, 0, 0, 0, 0, 0, 0, 0, 0, ())
     table = job.rope.table
-    cos, sin = table.kernel_tables(device, stream)
+    cos, sin = table.kernel_tables_t(device, stream)
     if table.sections is None:
-        return (1, 1, table.pairs, job.rope.rows, 0, 0, 0, 0, cos.data_ptr(), sin.data_ptr(), (cos, sin))
+        return (1, 1, table.rows, job.rope.rows, 0, 0, 0, 0, cos.data_ptr(), sin.data_ptr(), (cos, sin))
     t_row, h_row, w_row = job.rope.rows
     sec_t, sec_h, _ = table.sections
-    return (1, 0, table.pairs, t_row, h_row, w_row, sec_t, sec_h, cos.data_ptr(), sin.data_ptr(), (cos, sin))
+    return (1, 0, table.rows, t_row, h_row, w_row, sec_t, sec_h, cos.data_ptr(), sin.data_ptr(), (cos, sin))
+
+
+_COLUMN_TABLES = {}
+
+
+def _column_tables(layout, plane_stride, row_stride, k_pad):
+    """``(col_off, col_seg)`` int32 ``[k_pad]`` of a channel-tile layout: byte offset of each rank
+    column's mosaic cell inside a picture (-1 beyond the rank) and its segment."""
+    key = (layout["rank"], layout["planes"], tuple(layout["grid"]), layout["height"], layout["width"],
+           layout["channels_per_segment"], plane_stride, row_stride, k_pad)
+    hit = _COLUMN_TABLES.get(key)
+    if hit is not None:
+        return hit
+    rank, planes, (columns, _), height, width = (layout["rank"], layout["planes"], layout["grid"], layout["height"],
+                                                 layout["width"])
+    slots = layout["channels_per_segment"]
+    k = np.arange(k_pad, dtype=np.int64)
+    seg = k // slots
+    cell = k - seg * slots
+    plane = cell % planes
+    cell //= planes
+    cell_row, cell_col = cell // columns, cell % columns
+    off = plane * plane_stride + cell_row * height * row_stride + cell_col * width
+    off = np.where(k < rank, off, -1)
+    if off.max() >= 2 ** 31:
+        raise ConfigurationError("picture planes exceed the unpack kernel's 32-bit cell offsets")
+    hit = (off.astype(np.int32), np.where(k < rank, seg, 0).astype(np.int32))
+    if len(_COLUMN_TABLES) > 1024:
+        _COLUMN_TABLES.clear()
+    _COLUMN_TABLES[key] = hit
+    return hit
 
 
 def _fused_factor_group(jobs, device, precision, stream, keepalive):
+    """One unpack launch for the picture sources of the group (pictures -> dense uint8 [N, K_pad]),
+    then one fused restore launch over all jobs."""
     from .ops._ext import ext, status_word
 
     arena = _Arena()
     rows = []
     scales = []
     bases = []
+    unpack_rows = []
+    scratch_sizes = []
     for job in jobs:
         source = job.source
         row = [0] * 40
         rank = job.rank
         if isinstance(source, PictureSource):
             layout = source.layout
+            k_pad = (rank + 63) // 64 * 64
             addresses = np.array([[picture.data_ptr() for picture in segment] for segment in source.pictures],
                                  dtype=np.int64).reshape(-1)
-            row[1] = arena.add(addresses)
+            col_off, col_seg = _column_tables(layout, source.plane_stride, source.row_stride, k_pad)
+            unpack_rows.append([arena.add(addresses), arena.add(col_off), arena.add(col_seg), len(scratch_sizes),
+                                source.row_stride, job.tokens, k_pad, layout["frames"], layout["height"],
+                                layout["width"]])
+            scratch_sizes.append(job.tokens * k_pad)
+            row[0] = -len(scratch_sizes)  # patched to the scratch address below
             row[2] = arena.add(source.scale[:rank])
             row[3] = arena.add(source.offset[:rank])
-            row[8] = source.plane_stride
-            row[9] = source.row_stride
-            row[13] = 0
-            row[19] = layout["planes"]
-            row[20] = layout["grid"][0]
-            row[21] = layout["channels_per_segment"]
+            row[7] = k_pad
+            row[13] = 1
             bound = _affine_bound(source.scale[:rank], source.offset[:rank])
         elif source.quantized:
             values = source.values
-            if values.stride(1) != 1:
-                values = values.contiguous()
+            k_pad = (rank + 63) // 64 * 64
+            if (values.stride(1) != 1 or values.stride(0) % 16 or values.stride(0) < k_pad
+                    or values.data_ptr() % 16):
+                with torch.cuda.stream(stream):
+                    padded = torch.zeros((values.shape[0], k_pad), dtype=torch.uint8, device=device)
+                    padded[:, :rank].copy_(values[:, :rank])
+                values = padded
                 keepalive.append(values)
             row[0] = values.data_ptr()
             row[2] = arena.add(source.scale[:rank])
@@ -1051,15 +1110,32 @@ def _fused_factor_group(jobs, device, precision, stream, keepalive):
     keepalive.extend((host, dev))
     base = dev.data_ptr()
     for row, job in zip(rows, jobs):
-        for index in (1, 2, 3):
-            if isinstance(job.source, PictureSource) or (index != 1 and job.source.quantized):
-                row[index] += base
+        if isinstance(job.source, PictureSource) or job.source.quantized:
+            row[2] += base
+            row[3] += base
+    launches = 0
+    if unpack_rows:
+        offsets = np.cumsum([0] + [(size + 255) // 256 * 256 for size in scratch_sizes])
+        with torch.cuda.stream(stream):
+            scratch = torch.empty(int(offsets[-1]), dtype=torch.uint8, device=device)
+        keepalive.append(scratch)
+        for unpack_row in unpack_rows:
+            unpack_row[0] += base
+            unpack_row[1] += base
+            unpack_row[2] += base
+            unpack_row[3] = scratch.data_ptr() + int(offsets[unpack_row[3]])
+        for row in rows:
+            if row[0] < 0:
+                row[0] = scratch.data_ptr() + int(offsets[-row[0] - 1])
+        with torch.cuda.stream(stream):
+            ext().unpack_launch(torch.tensor(unpack_rows, dtype=torch.int64), device.index)
+        launches += 1
     keepalive.extend(bases)
     table = torch.tensor(rows, dtype=torch.int64)
     prescale = torch.tensor(scales, dtype=torch.float32)
     with torch.cuda.stream(stream):
         ext().restore_launch(table, bases, prescale, status_word(device))
-    return 1
+    return launches + 1
 
 
 def _fused_dense_group(jobs, device, stream, keepalive):
