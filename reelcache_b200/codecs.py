@@ -1,0 +1,288 @@
+"""Tensor codecs: RAW and factorized single-matrix packets and per-node coefficient packs
+(reference: reelcache/codecs.py:56-60 for the schema names, :621-1187 for single packets, :1369-1608 for
+node packs).
+
+* ``reelcache.tensor.v1`` RAW packets hold a matrix bit for bit (``values`` payload).
+* ``reelcache.tensor.v2`` factorized packets hold the 8-bit coefficients of ``A ~ P Q`` with their
+  per-column FP32 affine and a descriptor (shape, view rank, SHA-256) binding the FP16 basis prefix
+  they were encoded with; the basis bytes themselves live in the basis-version store.
+* ``reelcache.tensor_pack.v2`` node packs hold every matrix of one committed node as tiles of one
+  coefficient stream plus one affine payload. Tiles reference external basis versions.
+* ``reelcache.factor_pack.v1`` packs hold FP16 factors (the SVD-only baseline).
+
+Coefficient streams: ``hevc`` (all-intra QP-8 x265 through FFmpeg, the reference's contract; only
+where an encoder exists) or ``raw8`` (the same 8-bit mosaic-free coefficient rows, uncompressed, or
+``raw8+zlib``). Every stream decodes to the identical uint8 coefficients, so restores are bitwise
+the same whichever stream a pack uses.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import zlib
+from typing import Any, Mapping, Sequence
+
+import numpy as np
+import torch
+
+from . import _hevc
+from .errors import ConfigurationError, IntegrityError, UnsupportedError
+from .serialization import tensor_bytes, tensor_from_bytes
+from .types import CodecSpec, EncodedTensor, TensorContext, json_copy
+
+TENSOR_V1 = "reelcache.tensor.v1"
+TENSOR_V2 = "reelcache.tensor.v2"
+PACK_SCHEMA = "reelcache.tensor_pack.v2"
+FACTOR_PACK_SCHEMA = "reelcache.factor_pack.v1"
+STREAM_CODECS = ("raw8", "raw8+zlib", "hevc")
+REPRESENTATIONS = ("raw", "svd", "svd_hevc")
+
+
+def descriptor(basis: bytes, rank_view: int, channels: int) -> dict[str, Any]:
+    return {"shape": [rank_view, channels], "view_rank": rank_view, "dtype": "float16", "bytes": len(basis),
+            "sha256": hashlib.sha256(basis).hexdigest()}
+
+
+def default_stream_codec() -> str:
+    """``hevc`` when an FFmpeg with libx265 is reachable, else ``raw8``."""
+    return "hevc" if _hevc.ffmpeg_available() else "raw8"
+
+
+# ---------------------------------------------------------------------------------------------
+# Single-matrix packets
+# ---------------------------------------------------------------------------------------------
+
+
+def encode_raw(matrix: torch.Tensor, context: TensorContext) -> EncodedTensor:
+    """RAW packet: the canonical matrix bit for bit."""
+    if tuple(matrix.shape) != context.shape:
+        raise ConfigurationError("matrix shape differs from its context")
+    payload = tensor_bytes(matrix)
+    metadata = {"schema": TENSOR_V1, "representation": "raw", "context": context.to_dict(),
+                "dtype": str(matrix.dtype).removeprefix("torch."), "shape": list(matrix.shape),
+                "sha256": hashlib.sha256(payload).hexdigest()}
+    return EncodedTensor(metadata, {"values": payload}, metrics={"bytes": len(payload)})
+
+
+def quantize(coefficients: torch.Tensor, normalization: str = "per_channel", protected_fraction: float = 1.0):
+    """(pixels uint8 [N, r] numpy, affine float32 [2, records], layout) of FP32 coefficients; device
+    tensors are quantized on the device with the identical arithmetic (ops.quant)."""
+    if coefficients.is_cuda:
+        from .ops.quant import quantize_device
+        return quantize_device(coefficients, normalization, protected_fraction)
+    return _hevc.quantize_coefficients(coefficients.detach().float().cpu().numpy(), normalization,
+                                       protected_fraction)
+
+
+def encode_factorized(coefficients: torch.Tensor, basis_view: bytes, context: TensorContext, spec: CodecSpec, *,
+                      stream_codec: str | None = None, metrics: Mapping[str, Any] | None = None) -> EncodedTensor:
+    """``reelcache.tensor.v2`` packet of one matrix's coefficients (basis kept external)."""
+    rank = coefficients.shape[1]
+    if spec.kind not in ("svd", "svd_hevc") or spec.rank != rank:
+        raise ConfigurationError("factorized packets need an svd/svd_hevc spec at the coefficient rank")
+    stream_codec = stream_codec or ("raw8" if spec.kind == "svd" else default_stream_codec())
+    if stream_codec not in STREAM_CODECS:
+        raise ConfigurationError(f"stream codec must be one of {STREAM_CODECS}")
+    pixels, affine, layout = quantize(coefficients, spec.normalization, spec.protected_fraction)
+    stream = _encode_stream(np.ascontiguousarray(pixels), context, stream_codec, spec)
+    metadata = {"schema": TENSOR_V2, "representation": spec.kind, "context": context.to_dict(),
+                "codec": spec.to_dict(), "rank": rank, "normalization": layout, "stream_codec": stream_codec,
+                "basis": descriptor(basis_view, rank, context.channels),
+                "coefficients": {"shape": [int(pixels.shape[0]), rank],
+                                 "sha256": hashlib.sha256(np.ascontiguousarray(pixels).tobytes()).hexdigest()}}
+    payloads = {"stream": stream, "affine": np.ascontiguousarray(affine, dtype="<f4").tobytes()}
+    return EncodedTensor(metadata, payloads, basis=basis_view, metrics=dict(metrics or {}, bytes=len(stream)))
+
+
+def _encode_stream(pixels: np.ndarray, context: TensorContext, stream_codec: str, spec: CodecSpec) -> bytes:
+    if stream_codec == "raw8":
+        return pixels.tobytes()
+    if stream_codec == "raw8+zlib":
+        return zlib.compress(pixels.tobytes(), 1)
+    layout = _hevc.video_layout(context.frames, context.height, context.width, pixels.shape[1], spec.pix_fmt)
+    pictures = _hevc.mosaic_all(pixels, layout)
+    return _hevc.encode_pictures(pictures, spec.pix_fmt, ffmpeg_path=spec.ffmpeg_path,
+                                 inter_prediction=bool(spec.inter_prediction))
+
+
+def _decode_stream(stream: bytes, shape: Sequence[int], context: TensorContext, stream_codec: str,
+                   spec: CodecSpec) -> np.ndarray:
+    tokens, rank = shape
+    if stream_codec == "raw8":
+        data = stream
+    elif stream_codec == "raw8+zlib":
+        data = zlib.decompress(stream)
+    elif stream_codec == "hevc":
+        layout = _hevc.video_layout(context.frames, context.height, context.width, rank, spec.pix_fmt)
+        pictures = _hevc.decode_pictures(stream, pictures=layout["segments"] * layout["frames"],
+                                         height=layout["image_height"], width=layout["image_width"],
+                                         pix_fmt=spec.pix_fmt, ffmpeg_path=spec.ffmpeg_path)
+        return _hevc.unmosaic_all(pictures, layout)
+    else:
+        raise IntegrityError(f"unknown coefficient stream codec {stream_codec!r}")
+    if len(data) != tokens * rank:
+        raise IntegrityError("coefficient stream length differs from its shape")
+    return np.frombuffer(data, dtype=np.uint8).reshape(tokens, rank)
+
+
+def decode_coefficient_pixels(encoded: EncodedTensor) -> tuple[np.ndarray, np.ndarray, Mapping[str, Any]]:
+    """(pixels uint8 [N, r], affine, normalization layout) of a factorized packet, hash-checked."""
+    meta = encoded.metadata
+    if meta.get("schema") != TENSOR_V2:
+        raise IntegrityError("not a factorized tensor packet")
+    context = TensorContext.from_dict(meta["context"])
+    spec = CodecSpec.from_dict(meta["codec"])
+    pixels = _decode_stream(encoded.payloads["stream"], meta["coefficients"]["shape"], context, meta["stream_codec"],
+                            spec)
+    if hashlib.sha256(np.ascontiguousarray(pixels).tobytes()).hexdigest() != meta["coefficients"]["sha256"]:
+        raise IntegrityError("decoded coefficients differ from the packet digest")
+    affine = np.frombuffer(encoded.payloads["affine"], dtype="<f4").reshape(meta["normalization"]["affine_shape"])
+    return pixels, _hevc.validate_affine(affine.copy(), meta["normalization"], pixels.shape[1]), meta["normalization"]
+
+
+def decode_tensor(encoded: EncodedTensor, *, device: Any = "cpu", dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """The canonical matrix of a packet: RAW bitwise; factorized ``dequantize(P) @ Q`` (FP32)."""
+    meta = encoded.metadata
+    if meta.get("schema") == TENSOR_V1:
+        values = tensor_from_bytes(encoded.payloads["values"], dtype=meta["dtype"], shape=meta["shape"], device=device)
+        if hashlib.sha256(encoded.payloads["values"]).hexdigest() != meta["sha256"]:
+            raise IntegrityError("RAW packet payload differs from its digest")
+        return values
+    pixels, affine, layout = decode_coefficient_pixels(encoded)
+    if encoded.basis is None:
+        raise IntegrityError("factorized packets decode only with their attached basis view")
+    rank = pixels.shape[1]
+    channels = meta["basis"]["shape"][1]
+    coefficients = torch.from_numpy(_hevc.dequantize_coefficients(pixels, affine, layout)).to(device)
+    basis = torch.from_numpy(np.frombuffer(encoded.basis, dtype=np.float16).reshape(rank, channels).copy()).to(device)
+    return (coefficients @ basis.float()).to(dtype)
+
+
+def encode_tensor(matrix: torch.Tensor, context: TensorContext, spec: CodecSpec, *, basis: torch.Tensor | None = None,
+                  stream_codec: str | None = None) -> EncodedTensor:
+    """Encode one matrix: RAW, or factorized on ``basis`` (FP16 [r, C]) or on its own truncated
+    eigenbasis at ``spec.rank``."""
+    if spec.kind == "raw":
+        return encode_raw(matrix, context)
+    x = matrix.reshape(context.shape).float()
+    if basis is None:
+        g = x.t() @ x
+        values, vectors = torch.linalg.eigh(g.double())
+        order = torch.argsort(values, descending=True)[:spec.rank]
+        basis = vectors[:, order].t().contiguous().to(torch.float16)
+    basis = basis[:spec.rank].to(torch.float16)
+    coefficients = x @ basis.float().t().to(x.device)
+    view = basis.detach().cpu().numpy().tobytes()
+    return encode_factorized(coefficients, view, context, spec, stream_codec=stream_codec)
+
+
+# ---------------------------------------------------------------------------------------------
+# Node packs
+# ---------------------------------------------------------------------------------------------
+
+
+def encode_node_pack(tiles: Sequence[Mapping[str, Any]], *, stream_codec: str = "raw8",
+                     details: Mapping[str, Any] | None = None) -> EncodedTensor:
+    """One ``reelcache.tensor_pack.v2`` pack from already-quantized tiles.
+
+    Each tile: ``entry`` (JSON: key/stream), ``context`` (TensorContext), ``codec`` (CodecSpec),
+    ``pixels`` (uint8 numpy [N, r]), ``affine`` (float32 [2, records]), ``normalization`` (layout),
+    ``basis`` (descriptor dict, optionally with the version ref).
+    """
+    if stream_codec not in ("raw8", "raw8+zlib"):
+        raise UnsupportedError("node packs are written as raw8 / raw8+zlib coefficient streams here; "
+                               "HEVC packs need an HEVC encoder (ffmpeg/libx265 or NVENC), absent on this machine")
+    chunks, affines, entries = [], [], []
+    offset = 0
+    affine_records = 0
+    for index, tile in enumerate(tiles):
+        pixels = np.ascontiguousarray(tile["pixels"], dtype=np.uint8)
+        data = pixels.tobytes()
+        affine = np.ascontiguousarray(tile["affine"], dtype="<f4")
+        entries.append({
+            "tile": index, "entry": json_copy(tile["entry"]), "context": tile["context"].to_dict(),
+            "codec": tile["codec"].to_dict(), "rank": int(pixels.shape[1]), "normalization": tile["normalization"],
+            "coefficients": {"offset": offset, "bytes": len(data), "shape": [int(pixels.shape[0]), int(pixels.shape[1])],
+                             "sha256": hashlib.sha256(data).hexdigest()},
+            "affine": {"record": affine_records, "records": int(affine.shape[1])},
+            "basis": json_copy(tile["basis"]),
+        })
+        chunks.append(data)
+        affines.append(affine)
+        offset += len(data)
+        affine_records += affine.shape[1]
+    stream = b"".join(chunks)
+    if stream_codec == "raw8+zlib":
+        stream = zlib.compress(stream, 1)
+    affine_payload = (np.concatenate(affines, axis=1) if affines else np.zeros((2, 0), "<f4")).astype("<f4").tobytes()
+    metadata = {"schema": PACK_SCHEMA, "stream_codec": stream_codec, "tiles": entries,
+                "stream_bytes": len(stream), "raw_bytes": offset, "details": json_copy(dict(details or {}))}
+    return EncodedTensor(metadata, {"stream": stream, "affines": affine_payload},
+                         metrics={"bytes": len(stream) + len(affine_payload)})
+
+
+def validate_pack(metadata: Mapping[str, Any]) -> None:
+    if metadata.get("schema") != PACK_SCHEMA or metadata.get("stream_codec") not in STREAM_CODECS:
+        raise IntegrityError("unsupported node pack schema or stream codec")
+    offset = 0
+    for index, tile in enumerate(metadata["tiles"]):
+        coeff = tile["coefficients"]
+        if tile["tile"] != index or coeff["offset"] != offset or coeff["bytes"] != coeff["shape"][0] * coeff["shape"][1]:
+            raise IntegrityError("node pack tile table is inconsistent")
+        offset += coeff["bytes"]
+    if offset != metadata["raw_bytes"]:
+        raise IntegrityError("node pack byte count differs from its tiles")
+
+
+class DecodedPack:
+    """A node pack's decoded coefficient stream (uint8, host) and affines, with per-tile views."""
+
+    def __init__(self, metadata: Mapping[str, Any], stream: bytes, affines: bytes, *, verify: bool = True):
+        validate_pack(metadata)
+        self.metadata = metadata
+        data = zlib.decompress(stream) if metadata["stream_codec"] == "raw8+zlib" else stream
+        if metadata["stream_codec"] == "hevc":
+            raise UnsupportedError("HEVC node packs need an HEVC decoder (NVDEC or FFmpeg), absent on this machine")
+        if len(data) != metadata["raw_bytes"]:
+            raise IntegrityError("node pack stream length differs from its tiles")
+        self.raw = np.frombuffer(data, dtype=np.uint8)
+        total = sum(t["affine"]["records"] for t in metadata["tiles"])
+        self.affines = np.frombuffer(affines, dtype="<f4").reshape(2, total)
+        if verify:
+            for tile in metadata["tiles"]:
+                coeff = tile["coefficients"]
+                chunk = self.raw[coeff["offset"]:coeff["offset"] + coeff["bytes"]]
+                if hashlib.sha256(chunk.tobytes()).hexdigest() != coeff["sha256"]:
+                    raise IntegrityError(f"node pack tile {tile['tile']} differs from its digest")
+
+    @property
+    def tiles(self):
+        return self.metadata["tiles"]
+
+    def pixels(self, index: int) -> np.ndarray:
+        coeff = self.tiles[index]["coefficients"]
+        return self.raw[coeff["offset"]:coeff["offset"] + coeff["bytes"]].reshape(coeff["shape"])
+
+    def affine(self, index: int) -> np.ndarray:
+        record = self.tiles[index]["affine"]
+        return np.ascontiguousarray(self.affines[:, record["record"]:record["record"] + record["records"]])
+
+    def scale_offset(self, index: int) -> tuple[np.ndarray, np.ndarray]:
+        tile = self.tiles[index]
+        scale, offset = _hevc.expanded_affine(self.affine(index), tile["normalization"], tile["rank"])
+        return np.ascontiguousarray(scale, dtype=np.float32), np.ascontiguousarray(offset, dtype=np.float32)
+
+
+def encode_factor_pack(tiles: Sequence[Mapping[str, Any]]) -> EncodedTensor:
+    """``reelcache.factor_pack.v1``: FP16 coefficient matrices of the SVD-only baseline."""
+    chunks, entries = [], []
+    offset = 0
+    for index, tile in enumerate(tiles):
+        data = np.ascontiguousarray(tile["coefficients"], dtype=np.float16).tobytes()
+        entries.append({"tile": index, "entry": json_copy(tile["entry"]), "context": tile["context"].to_dict(),
+                        "rank": int(tile["coefficients"].shape[1]), "offset": offset, "bytes": len(data),
+                        "sha256": hashlib.sha256(data).hexdigest(), "basis": json_copy(tile["basis"])})
+        chunks.append(data)
+        offset += len(data)
+    return EncodedTensor({"schema": FACTOR_PACK_SCHEMA, "tiles": entries, "bytes": offset},
+                         {"factors": b"".join(chunks)}, metrics={"bytes": offset})

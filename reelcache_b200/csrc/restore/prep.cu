@@ -1,0 +1,130 @@
+// Basis preparation for the fused restore GEMM (sm_100a).
+//
+// The restore computes, per token n and channel c,
+//   y[n, c] = sum_k (p[n, k] * s[k] + o[k]) * Q[k, c]
+//           = sum_k (p[n, k] - 128) * (s[k] * Q[k, c])  +  sum_k (o[k] + 128 s[k]) * Q[k, c]
+// with p the 8-bit pixel, (s, o) the column's affine and Q the FP16 basis. The first term runs on
+// the tensor cores with the exact FP16 operand (p - 128) and the B operand s[k] * Q[k, c] * 2^e split
+// into FP16 hi + lo (two products, FP32 accumulation; 2^e is the job's exact power-of-two prescale);
+// the second is a per-channel bias. This kernel writes, per job, Bt[c, 0:K_pad] = hi,
+// Bt[c, K_pad:2 K_pad] = lo (K-major for TMA, zero beyond the rank) and bias[c] (FP64 accumulation,
+// fixed order: deterministic).
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include <cuda_fp16.h>
+
+#include "../common/host.h"
+
+namespace rc {
+namespace prep {
+
+constexpr int kMaxJobs = 48;
+constexpr int kThreads = 256;
+constexpr int kChannels = 32;   // channels per block (one warp-width of coalesced basis reads)
+constexpr int kKLanes = kThreads / kChannels;  // 8
+
+struct Job {
+  const __half* q;       // [R, C] basis rows
+  const float* scale;    // [rank]
+  const float* offset;   // [rank]
+  __half* bt;            // [C, 2 * k_pad]
+  float* bias;           // [C]
+  int64_t q_stride;      // elements between basis rows
+  int rank, k_pad, channels;
+  float prescale;
+};
+
+struct Params {
+  Job jobs[kMaxJobs];
+};
+
+__global__ void __launch_bounds__(kThreads) prep_kernel(const __grid_constant__ Params p) {
+  const Job& jb = p.jobs[blockIdx.y];
+  const int c0 = blockIdx.x * kChannels;
+  if (c0 >= jb.channels) return;
+  const int c = c0 + (threadIdx.x % kChannels);
+  const int lane_k = threadIdx.x / kChannels;
+  __shared__ double partial[kKLanes][kChannels];
+  double acc = 0.0;
+  const bool live_c = c < jb.channels;
+  for (int k0 = lane_k * 8; k0 < jb.k_pad; k0 += kKLanes * 8) {
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      float v[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int k = k0 + i + h;
+        float val = 0.0f;
+        if (live_c && k < jb.rank) {
+          const float q = __half2float(jb.q[static_cast<int64_t>(k) * jb.q_stride + c]);
+          const float s = jb.scale[k];
+          val = (s * jb.prescale) * q;
+          acc += (static_cast<double>(jb.offset[k]) + 128.0 * static_cast<double>(s)) * static_cast<double>(q);
+        }
+        v[h] = val;
+      }
+      const __half h0 = __float2half_rn(v[0]);
+      const __half h1 = __float2half_rn(v[1]);
+      const __half l0 = __float2half_rn(v[0] - __half2float(h0));
+      const __half l1 = __float2half_rn(v[1] - __half2float(h1));
+      hi[i / 2] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
+      lo[i / 2] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+    }
+    if (live_c) {
+      __half* row = jb.bt + static_cast<int64_t>(c) * 2 * jb.k_pad;
+      *reinterpret_cast<uint4*>(row + k0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(row + jb.k_pad + k0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+  }
+  partial[lane_k][threadIdx.x % kChannels] = acc;
+  __syncthreads();
+  if (threadIdx.x < kChannels && live_c) {
+    double sum = 0.0;
+#pragma unroll
+    for (int i = 0; i < kKLanes; ++i) sum += partial[i][threadIdx.x];
+    jb.bias[c] = static_cast<float>(sum);
+  }
+}
+
+}  // namespace prep
+
+// jobs: CPU int64 [n, 10]: q, scale, offset, bt, bias, q_stride, rank, k_pad, channels, prescale bits
+// (float32 bit pattern in the low 32 bits).
+void prep_launch(const at::Tensor& jobs, int64_t device) {
+  RC_CHECK(jobs.device().is_cpu() && jobs.scalar_type() == at::kLong && jobs.dim() == 2 && jobs.size(1) == 10,
+           "jobs must be a CPU int64 [n, 10] table");
+  const int n = static_cast<int>(jobs.size(0));
+  RC_CHECK(n >= 1 && n <= prep::kMaxJobs, "between 1 and 48 prep jobs per launch");
+  prep::Params p;
+  memset(&p, 0, sizeof(p));
+  const int64_t* f = jobs.data_ptr<int64_t>();
+  int max_channels = 0;
+  for (int i = 0; i < n; ++i) {
+    const int64_t* r = f + i * 10;
+    prep::Job& jb = p.jobs[i];
+    jb.q = reinterpret_cast<const __half*>(r[0]);
+    jb.scale = reinterpret_cast<const float*>(r[1]);
+    jb.offset = reinterpret_cast<const float*>(r[2]);
+    jb.bt = reinterpret_cast<__half*>(r[3]);
+    jb.bias = reinterpret_cast<float*>(r[4]);
+    jb.q_stride = r[5];
+    jb.rank = static_cast<int>(r[6]);
+    jb.k_pad = static_cast<int>(r[7]);
+    jb.channels = static_cast<int>(r[8]);
+    const uint32_t bits = static_cast<uint32_t>(r[9] & 0xffffffffll);
+    memcpy(&jb.prescale, &bits, 4);
+    RC_CHECK(jb.k_pad % 64 == 0 && jb.rank <= jb.k_pad && jb.rank >= 1, "k_pad must be a multiple of 64 >= rank");
+    RC_CHECK(reinterpret_cast<uintptr_t>(jb.bt) % 16 == 0, "prepared basis must be 16-byte aligned");
+    max_channels = std::max(max_channels, jb.channels);
+  }
+  c10::cuda::CUDAGuard guard(static_cast<int>(device));
+  dim3 grid((max_channels + prep::kChannels - 1) / prep::kChannels, n);
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(static_cast<int>(device)).stream();
+  prep::prep_kernel<<<grid, prep::kThreads, 0, stream>>>(p);
+  RC_CUDA(cudaGetLastError());
+}
+
+}  // namespace rc

@@ -1,14 +1,17 @@
-// Picture unpack for sm_100a (the counterpart of the reference's `_unpack_kernel`,
-// reelcache/restore_kernels.py:1517-1555): gathers the 8-bit coefficient pixels of each job's
-// reelcache.channel_tiles.v1 mosaic into a dense row-major uint8 matrix [N, K_pad] (zero beyond the
-// rank), the operand layout the fused restore GEMM streams with 16-byte loads.
+// Coefficient unpack for sm_100a (the counterpart of the reference's `_unpack_kernel`,
+// reelcache/restore_kernels.py:1517-1555): gathers each job's 8-bit coefficient pixels -- from the
+// reelcache.channel_tiles.v1 mosaic of decoded pictures, or from a dense uint8 [N, >= rank] matrix --
+// into the fused restore GEMM's A operand: a row-major FP16 matrix [N, K_pad] of centered pixels
+// (p - 128, exact in FP16), zero beyond the rank.
 //
-// One thread produces 16 consecutive rank columns of one token (one 16-byte store). Threads of a
-// warp hold consecutive tokens, so every pixel load of the warp reads neighbouring bytes of one
-// picture row. The per-column cell offsets and segments come from a host-built table.
+// One thread produces 8 consecutive rank columns of one token (one 16-byte store). Threads of a
+// warp hold consecutive tokens, so each pixel load of the warp reads neighbouring bytes of one
+// picture row (or one 8-byte slice per row of a dense matrix).
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
+
+#include <cuda_fp16.h>
 
 #include "../common/host.h"
 
@@ -19,60 +22,80 @@ constexpr int kMaxJobs = 48;
 constexpr int kThreads = 256;
 
 struct Job {
-  const int64_t* pic_addr;   // [segments * frames] absolute address of the matrix rectangle origin
-  const int32_t* col_off;    // [k_pad] byte offset of column k's cell inside a picture (-1 beyond rank)
-  const int32_t* col_seg;    // [k_pad] segment of column k
-  uint8_t* out;              // [tokens, k_pad]
-  int64_t row_stride;        // picture row stride (bytes)
-  int tokens, k_pad, frames, height, width;
+  const int64_t* pic_addr;   // pictures: [segments * frames] absolute address of the rectangle origin
+  const int32_t* col_off;    // pictures: [k_pad] byte offset of column k's cell in a picture (-1: none)
+  const int32_t* col_seg;    // pictures: [k_pad] segment of column k
+  const uint8_t* matrix;     // dense source [tokens, >= rank] (null for pictures)
+  __half* out;               // [tokens, k_pad]
+  int64_t row_stride;        // pictures: picture row stride; dense: matrix row stride (bytes)
+  int tokens, k_pad, rank, frames, height, width;
 };
 
 struct Params {
   Job jobs[kMaxJobs];
 };
 
+__device__ __forceinline__ uint32_t centered_pair(uint32_t a, uint32_t b) {
+  const __half2 h = __halves2half2(__int2half_rn(static_cast<int>(a) - 128), __int2half_rn(static_cast<int>(b) - 128));
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 __global__ void __launch_bounds__(kThreads) unpack_kernel(const __grid_constant__ Params p) {
   const Job& jb = p.jobs[blockIdx.y];
-  const int groups = jb.k_pad >> 4;
+  const int groups = jb.k_pad >> 3;
   const int64_t item = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   if (item >= static_cast<int64_t>(jb.tokens) * groups) return;
-  // token fastest: a warp covers 32 consecutive tokens of one 16-column group
-  const int group = static_cast<int>(item / jb.tokens);
+  const int group = static_cast<int>(item / jb.tokens);  // token fastest within a warp
   const int token = static_cast<int>(item - static_cast<int64_t>(group) * jb.tokens);
-  const int per_frame = jb.height * jb.width;
-  const int frame = token / per_frame;
-  const int rem = token - frame * per_frame;
-  const int y = rem / jb.width;
-  const int64_t pix = static_cast<int64_t>(y) * jb.row_stride + (rem - y * jb.width);
-  uint32_t words[4] = {0u, 0u, 0u, 0u};
-  int cur_seg = -1;
-  const uint8_t* base = nullptr;
+  uint32_t px[8];
+  bool live[8];
+  if (jb.matrix != nullptr) {
+    const uint8_t* rowp = jb.matrix + static_cast<int64_t>(token) * jb.row_stride + group * 8;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int k = group * 16 + i;
-    const int off = __ldg(jb.col_off + k);
-    uint32_t v = 0u;
-    if (off >= 0) {
-      const int seg = __ldg(jb.col_seg + k);
-      if (seg != cur_seg) {
-        cur_seg = seg;
-        base = reinterpret_cast<const uint8_t*>(__ldg(jb.pic_addr + seg * jb.frames + frame) + pix);
-      }
-      v = __ldg(base + off);
+    for (int i = 0; i < 8; ++i) {
+      live[i] = group * 8 + i < jb.rank;
+      px[i] = live[i] ? __ldg(rowp + i) : 128u;
     }
-    words[i >> 2] |= v << ((i & 3) * 8);
+  } else {
+    const int per_frame = jb.height * jb.width;
+    const int frame = token / per_frame;
+    const int rem = token - frame * per_frame;
+    const int y = rem / jb.width;
+    const int64_t pix = static_cast<int64_t>(y) * jb.row_stride + (rem - y * jb.width);
+    int cur_seg = -1;
+    const uint8_t* base = nullptr;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int k = group * 8 + i;
+      const int off = __ldg(jb.col_off + k);
+      live[i] = off >= 0;
+      px[i] = 128u;
+      if (live[i]) {
+        const int seg = __ldg(jb.col_seg + k);
+        if (seg != cur_seg) {
+          cur_seg = seg;
+          base = reinterpret_cast<const uint8_t*>(__ldg(jb.pic_addr + seg * jb.frames + frame) + pix);
+        }
+        px[i] = __ldg(base + off);
+      }
+    }
   }
-  *reinterpret_cast<uint4*>(jb.out + static_cast<int64_t>(token) * jb.k_pad + group * 16) =
-      make_uint4(words[0], words[1], words[2], words[3]);
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // columns beyond the rank hold 0 (their centered pixel would be 0 too: px = 128)
+    w[i] = centered_pair(px[2 * i], px[2 * i + 1]);
+  }
+  *reinterpret_cast<uint4*>(jb.out + static_cast<int64_t>(token) * jb.k_pad + group * 8) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 }  // namespace unpack
 
-// jobs: CPU int64 [n, 10]: pic_addr, col_off, col_seg, out, row_stride, tokens, k_pad, frames,
-// height, width. All pointers device addresses on the current device.
+// jobs: CPU int64 [n, 12]: pic_addr, col_off, col_seg, matrix, out, row_stride, tokens, k_pad, rank,
+// frames, height, width. Pointers are device addresses on `device`.
 void unpack_launch(const at::Tensor& jobs, int64_t device) {
-  RC_CHECK(jobs.device().is_cpu() && jobs.scalar_type() == at::kLong && jobs.dim() == 2 && jobs.size(1) == 10,
-           "jobs must be a CPU int64 [n, 10] table");
+  RC_CHECK(jobs.device().is_cpu() && jobs.scalar_type() == at::kLong && jobs.dim() == 2 && jobs.size(1) == 12,
+           "jobs must be a CPU int64 [n, 12] table");
   const int n = static_cast<int>(jobs.size(0));
   RC_CHECK(n >= 1 && n <= unpack::kMaxJobs, "between 1 and 48 unpack jobs per launch");
   unpack::Params p;
@@ -80,22 +103,24 @@ void unpack_launch(const at::Tensor& jobs, int64_t device) {
   const int64_t* f = jobs.data_ptr<int64_t>();
   int64_t max_items = 0;
   for (int i = 0; i < n; ++i) {
-    const int64_t* r = f + i * 10;
+    const int64_t* r = f + i * 12;
     unpack::Job& jb = p.jobs[i];
     jb.pic_addr = reinterpret_cast<const int64_t*>(r[0]);
     jb.col_off = reinterpret_cast<const int32_t*>(r[1]);
     jb.col_seg = reinterpret_cast<const int32_t*>(r[2]);
-    jb.out = reinterpret_cast<uint8_t*>(r[3]);
-    jb.row_stride = r[4];
-    jb.tokens = static_cast<int>(r[5]);
-    jb.k_pad = static_cast<int>(r[6]);
-    jb.frames = static_cast<int>(r[7]);
-    jb.height = static_cast<int>(r[8]);
-    jb.width = static_cast<int>(r[9]);
-    RC_CHECK(jb.k_pad % 16 == 0 && jb.k_pad > 0, "k_pad must be a positive multiple of 16");
+    jb.matrix = reinterpret_cast<const uint8_t*>(r[3]);
+    jb.out = reinterpret_cast<__half*>(r[4]);
+    jb.row_stride = r[5];
+    jb.tokens = static_cast<int>(r[6]);
+    jb.k_pad = static_cast<int>(r[7]);
+    jb.rank = static_cast<int>(r[8]);
+    jb.frames = static_cast<int>(r[9]);
+    jb.height = static_cast<int>(r[10]);
+    jb.width = static_cast<int>(r[11]);
+    RC_CHECK(jb.k_pad % 64 == 0 && jb.k_pad > 0 && jb.rank <= jb.k_pad, "k_pad must be a multiple of 64 >= rank");
     RC_CHECK(reinterpret_cast<uintptr_t>(jb.out) % 16 == 0, "unpack output must be 16-byte aligned");
-    RC_CHECK(jb.frames * jb.height * jb.width == jb.tokens, "grid does not match the token count");
-    max_items = std::max<int64_t>(max_items, static_cast<int64_t>(jb.tokens) * (jb.k_pad / 16));
+    RC_CHECK(jb.matrix != nullptr || jb.frames * jb.height * jb.width == jb.tokens, "grid does not match the tokens");
+    max_items = std::max<int64_t>(max_items, static_cast<int64_t>(jb.tokens) * (jb.k_pad / 8));
   }
   c10::cuda::CUDAGuard guard(static_cast<int>(device));
   dim3 grid(static_cast<unsigned>((max_items + unpack::kThreads - 1) / unpack::kThreads), n);

@@ -1,0 +1,253 @@
+"""Staged commit of one lineage node (reference: reelcache/lineage_commit.py:124-989).
+
+A :class:`CommitJob` is one node's archival work, split into stages that the archive pipeline can run
+on different threads:
+
+``plan``      the rank method on the planning device (share / augment / refit / fresh per matrix);
+``finalize``  device quantization of every coefficient tile (per-column covering FP32 affine, FP64
+              ``rint``) -- only uint8 tiles and affines cross PCIe;
+``encode``    one node pack (``reelcache.tensor_pack.v2``) of all tiles;
+``store``     basis versions, pack blobs/manifest, matrix records, execution state -- staged under a
+              store lease so a crash before publication leaves only collectable garbage;
+``build_node`` the immutable :class:`~reelcache_b200.types.ChunkNode` manifest.
+
+Publication (CAS of the lineage head) and registry training happen in
+:meth:`reelcache_b200.lineage.LineageRuntime.publish_job`.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import time
+from dataclasses import dataclass, field
+from typing import Any, Mapping, Sequence
+
+import numpy as np
+import torch
+
+from . import codecs
+from .errors import ConfigurationError, IntegrityError
+from .rank_method import MatrixPlan, RankMethodConfig, plan_chunk
+from .serialization import serialize_tensors
+from .types import (ActiveBasisBinding, CodecSpec, EnergyReport, FitObservation, MatrixKey, MatrixRecord,
+                    TensorContext, canonical_digest, entry_order, entry_parts, json_copy)
+
+_FINGERPRINT_PRIME = (1 << 61) - 1
+
+
+@dataclass(frozen=True)
+class ArchiveOptions:
+    """Archival path options (reference :124): node packing, the coefficient stream codec, tile rows of
+    the planner's verification, the planning memory budget and encode threads."""
+
+    packed: bool = True
+    stream_codec: str = "raw8"
+    tile_rows: int = 4096
+    plan_memory_bytes: int | None = None
+    encode_threads: int = 1
+    finalize_on_device: bool = True
+
+    def __post_init__(self):
+        if self.stream_codec not in codecs.STREAM_CODECS:
+            raise ConfigurationError(f"stream_codec must be one of {codecs.STREAM_CODECS}")
+
+
+def source_fingerprint(matrix: torch.Tensor) -> str:
+    """Exact content identity of a source matrix: SHA-256 of its dtype, shape and raw bytes."""
+    value = matrix.detach()
+    header = f"{str(value.dtype).removeprefix('torch.')}:{list(value.shape)}".encode()
+    digest = hashlib.sha256(header)
+    digest.update(value.contiguous().view(torch.uint8).reshape(-1).cpu().numpy().tobytes())
+    return digest.hexdigest()
+
+
+def source_fingerprints(matrices: Mapping[Any, torch.Tensor]) -> dict[Any, str]:
+    return {entry: source_fingerprint(matrix) for entry, matrix in matrices.items()}
+
+
+@dataclass
+class ParentState:
+    """The parent head's active bindings and the assembled FP16 rows of each active basis."""
+
+    node_ref: str
+    bindings: dict[Any, ActiveBasisBinding]
+    rows: dict[Any, torch.Tensor | None] = field(default_factory=dict)
+
+
+@dataclass
+class StagedTile:
+    entry: Any
+    context: TensorContext
+    plan: MatrixPlan
+    pixels: np.ndarray | None = None
+    affine: np.ndarray | None = None
+    normalization: Mapping[str, Any] | None = None
+
+
+class CommitJob:
+    """One node's archival work (see the module docstring for the stages)."""
+
+    def __init__(self, runtime, branch_id: str, node_kind: str, chunk_id: str, ranges, *, method: RankMethodConfig,
+                 parent: ParentState, expected_head: str, execution_state: Mapping[str, torch.Tensor] | None,
+                 device: Any, options: ArchiveOptions, epoch_id: str | None = None,
+                 details: Mapping[str, Any] | None = None, view=None):
+        self.runtime = runtime
+        self.branch_id = branch_id
+        self.node_kind = node_kind
+        self.chunk_id = chunk_id
+        self.ranges = ranges  # [(range_chunk_id, matrices, contexts)]
+        self.method = method
+        self.parent = parent
+        self.expected_head = expected_head
+        self.execution_state = execution_state
+        self.device = torch.device(device)
+        self.options = options
+        self.epoch_id = epoch_id
+        self.details = dict(details or {})
+        self.view = view
+        self.tiles: list[list[StagedTile]] = []
+        self.timings: dict[str, float] = {}
+        self.packs: list[codecs.EncodedTensor] = []
+        self.stored: dict[str, Any] | None = None
+        self.lease = None
+        self.observations: list[FitObservation] = []
+
+    # -- stages ------------------------------------------------------------------------------------------------
+
+    def plan(self) -> "CommitJob":
+        started = time.perf_counter()
+        bindings = dict(self.parent.bindings)
+        rows = dict(self.parent.rows)
+        for range_id, matrices, contexts in self.ranges:
+            plans = plan_chunk(matrices, contexts, self.method, self.view, bindings, rows, chunk_id=range_id,
+                               device=self.device)
+            staged = []
+            for entry in sorted(plans, key=entry_order):
+                plan = plans[entry]
+                staged.append(StagedTile(entry, contexts[entry], plan))
+                if plan.observation is not None:
+                    self.observations.append(plan.observation)
+                bindings[entry] = plan.binding
+                rows[entry] = plan.rows
+            self.tiles.append(staged)
+        self.timings["plan"] = time.perf_counter() - started
+        return self
+
+    def finalize(self) -> "CommitJob":
+        started = time.perf_counter()
+        spec = self.method.codec
+        for staged in self.tiles:
+            for tile in staged:
+                pixels, affine, layout = codecs.quantize(tile.plan.coefficients, spec.normalization,
+                                                         spec.protected_fraction)
+                tile.pixels, tile.affine, tile.normalization = np.ascontiguousarray(pixels), affine, layout
+                tile.plan.coefficients = None  # release the device coefficients
+        self.timings["finalize"] = time.perf_counter() - started
+        return self
+
+    def encode(self) -> "CommitJob":
+        started = time.perf_counter()
+        spec = self.method.codec
+        for staged in self.tiles:
+            tiles = []
+            for tile in staged:
+                key, stream = entry_parts(tile.entry)
+                rank = tile.plan.rank_view
+                view_bytes = tile.plan.rows.detach().cpu().contiguous().numpy().tobytes()
+                tiles.append({"entry": {"key": key.to_dict(), **({"stream": stream} if stream else {})},
+                              "context": tile.context, "codec": CodecSpec(**{**spec.to_dict(), "rank": rank,
+                                                                            "inter_prediction": spec.inter_prediction}),
+                              "pixels": tile.pixels, "affine": tile.affine, "normalization": tile.normalization,
+                              "basis": codecs.descriptor(view_bytes, rank, tile.context.channels)})
+            self.packs.append(codecs.encode_node_pack(tiles, stream_codec=self.options.stream_codec,
+                                                      details={"chunk_id": self.chunk_id}))
+        self.timings["encode"] = time.perf_counter() - started
+        return self
+
+    def store(self) -> "CommitJob":
+        """Write every object of the node (basis versions, packs, records, state) under a staging lease."""
+        started = time.perf_counter()
+        runtime = self.runtime
+        store = runtime.store
+        spec = self.method.codec
+        created: list[str] = []
+        results = []
+        bindings = dict(self.parent.bindings)
+        with store.transaction():
+            for staged, pack in zip(self.tiles, self.packs):
+                version_refs = {}
+                for tile in staged:
+                    plan = tile.plan
+                    binding = bindings.get(tile.entry, ActiveBasisBinding())
+                    if plan.decision in ("fresh", "refit", "zero_input"):
+                        ref, version = runtime.basis.put_root(tile.context.key, plan.new_rows.detach().cpu())
+                        new_binding = ActiveBasisBinding(ref, version.total_rank, version.group_id,
+                                                         plan.rank_view if plan.decision != "zero_input" else None,
+                                                         self.chunk_id if plan.decision != "zero_input" else None)
+                    elif plan.decision == "augment":
+                        ref, version = runtime.basis.put_extension(binding.version_ref, plan.new_rows.detach().cpu())
+                        new_binding = ActiveBasisBinding(ref, version.total_rank, version.group_id, binding.fresh_rank,
+                                                         binding.fresh_chunk_id, binding.coefficient_rate,
+                                                         binding.rate_identity,
+                                                         plan.binding.refit_debt if binding.fresh_rank else 0.0)
+                    else:
+                        ref = binding.version_ref
+                        new_binding = binding
+                    rate_identity = canonical_digest({"codec": spec.to_dict(), "stream": self.options.stream_codec,
+                                                      "shape": list(tile.context.shape)})
+                    # measured stream bytes per coefficient value of this pack
+                    rate = max(pack.metadata["stream_bytes"] / max(pack.metadata["raw_bytes"], 1), 1e-9)
+                    if new_binding.version_ref is not None and new_binding.fresh_rank is not None:
+                        new_binding = ActiveBasisBinding(new_binding.version_ref, new_binding.total_rank,
+                                                         new_binding.group_id, new_binding.fresh_rank,
+                                                         new_binding.fresh_chunk_id, rate, rate_identity,
+                                                         new_binding.refit_debt)
+                    version_refs[tile.entry] = ref
+                    bindings[tile.entry] = new_binding
+                blobs = {name: store.put(value) for name, value in pack.payloads.items()}
+                basis_refs = sorted({r for r in version_refs.values() if r is not None})
+                packet_ref = runtime.put_content({"type": "packet", "version": 1, "model": runtime.model.to_dict(),
+                                                  "metadata": pack.metadata, "payloads": blobs,
+                                                  "metrics": json_copy(pack.metrics or {}),
+                                                  "basis_storage": "external",
+                                                  "basis_versions": [version_refs[t.entry] for t in staged]},
+                                                 field="metrics", references=sorted(blobs.values()) + basis_refs)
+                records = {}
+                for index, tile in enumerate(staged):
+                    plan = tile.plan
+                    rank = plan.rank_view
+                    codec = CodecSpec(**{**spec.to_dict(), "rank": rank, "inter_prediction": spec.inter_prediction})
+                    key, stream = entry_parts(tile.entry)
+                    energy = plan.energy if plan.energy.rank_view == rank else EnergyReport(
+                        **{**plan.energy.to_dict(), "rank_view": rank})
+                    record = MatrixRecord(tile.context, codec, packet_ref, version_refs[tile.entry], rank, energy, None,
+                                          {**json_copy(plan.decision_record()),
+                                           "packet": {"tile": index, "stream_codec": self.options.stream_codec}},
+                                          packet_tile=index if codec.kind == "svd_hevc" and codec.inter_prediction is False
+                                          else None, stream=stream)
+                    records[tile.entry] = runtime.put_record(record)
+                results.append((packet_ref, records))
+            state_ref = None
+            if self.execution_state:
+                state_ref = store.put(serialize_tensors(dict(self.execution_state)))
+            created = list(store.created_objects)
+        if created:
+            self.lease = store.lease(created, purpose="staging", verify=False)
+        self.stored = {"ranges": results, "bindings": bindings, "execution_state": state_ref}
+        self.timings["store"] = time.perf_counter() - started
+        return self
+
+    def release(self) -> None:
+        if self.lease is not None:
+            self.lease.release()
+            self.lease = None
+
+    def plan_summary(self) -> dict[str, Any]:
+        decisions: dict[str, int] = {}
+        ranks = []
+        for staged in self.tiles:
+            for tile in staged:
+                decisions[tile.plan.decision] = decisions.get(tile.plan.decision, 0) + 1
+                ranks.append(tile.plan.rank_view)
+        return {"decisions": decisions, "mean_rank": float(np.mean(ranks)) if ranks else 0.0,
+                "max_rank": int(max(ranks)) if ranks else 0, "matrices": len(ranks)}

@@ -938,45 +938,6 @@ def transposed_basis(basis, stream=None):
     return qt
 
 
-def _prescale_exponent(bound):
-    if not bound > 0:
-        return 0
-    exponent = 14 - math.ceil(math.log2(max(bound, 1e-30)))
-    return int(min(max(exponent, -100), 100))
-
-
-def _affine_bound(scale, offset):
-    """Largest ``|float(p) * scale + offset|`` over pixels 0..255 (both ends), in FP32 like the kernel."""
-    top = (np.float32(255.0) * scale).astype(np.float32) + offset
-    return float(max(np.abs(offset).max(initial=0.0), np.abs(top.astype(np.float32)).max(initial=0.0)))
-
-
-class _Arena:
-    """Pinned host staging of the per-call device tables (picture offsets, affines), uploaded with
-    one copy on the execution stream."""
-
-    def __init__(self):
-        self.parts = []
-        self.size = 0
-
-    def add(self, array):
-        array = np.ascontiguousarray(array)
-        start = (self.size + 15) // 16 * 16
-        self.parts.append((start, array))
-        self.size = start + array.nbytes
-        return start
-
-    def upload(self, device, stream):
-        host = torch.empty(max(self.size, 16), dtype=torch.uint8, pin_memory=True)
-        view = host.numpy()
-        for start, array in self.parts:
-            view[start:start + array.nbytes] = np.frombuffer(array.tobytes(), dtype=np.uint8)
-        with torch.cuda.stream(stream):
-            dev = torch.empty_like(host, device=device)
-            dev.copy_(host, non_blocking=True)
-        return host, dev
-
-
 def _rope_fields(job, device, stream):
     """(rope, dense, row_stride, row_t, row_h, row_w, sec_t, sec_h, cos_ptr, sin_ptr, tensors)."""
     if job.rope is None:
@@ -990,152 +951,35 @@ def _rope_fields(job, device, stream):
     return (1, 0, table.rows, t_row, h_row, w_row, sec_t, sec_h, cos.data_ptr(), sin.data_ptr(), (cos, sin))
 
 
-_COLUMN_TABLES = {}
-
-
-def _column_tables(layout, plane_stride, row_stride, k_pad):
-    """``(col_off, col_seg)`` int32 ``[k_pad]`` of a channel-tile layout: byte offset of each rank
-    column's mosaic cell inside a picture (-1 beyond the rank) and its segment."""
-    key = (layout["rank"], layout["planes"], tuple(layout["grid"]), layout["height"], layout["width"],
-           layout["channels_per_segment"], plane_stride, row_stride, k_pad)
-    hit = _COLUMN_TABLES.get(key)
-    if hit is not None:
-        return hit
-    rank, planes, (columns, _), height, width = (layout["rank"], layout["planes"], layout["grid"], layout["height"],
-                                                 layout["width"])
-    slots = layout["channels_per_segment"]
-    k = np.arange(k_pad, dtype=np.int64)
-    seg = k // slots
-    cell = k - seg * slots
-    plane = cell % planes
-    cell //= planes
-    cell_row, cell_col = cell // columns, cell % columns
-    off = plane * plane_stride + cell_row * height * row_stride + cell_col * width
-    off = np.where(k < rank, off, -1)
-    if off.max() >= 2 ** 31:
-        raise ConfigurationError("picture planes exceed the unpack kernel's 32-bit cell offsets")
-    hit = (off.astype(np.int32), np.where(k < rank, seg, 0).astype(np.int32))
-    if len(_COLUMN_TABLES) > 1024:
-        _COLUMN_TABLES.clear()
-    _COLUMN_TABLES[key] = hit
-    return hit
-
-
 def _fused_factor_group(jobs, device, precision, stream, keepalive):
-    """One unpack launch for the picture sources of the group (pictures -> dense uint8 [N, K_pad]),
-    then one fused restore launch over all jobs."""
-    from .ops._ext import ext, status_word
+    """Describe the group's jobs to the launch plumbing (reelcache_b200/ops/restore.py)."""
+    from .ops.restore import launch_factor_group
 
-    arena = _Arena()
-    rows = []
-    scales = []
-    bases = []
-    unpack_rows = []
-    scratch_sizes = []
+    items = []
     for job in jobs:
         source = job.source
-        row = [0] * 40
-        rank = job.rank
+        view = job.destination
+        item = {"tokens": job.tokens, "rank": job.rank, "grid": job.grid, "basis": job.basis,
+                "basis_t": job.basis_t,
+                "dest": (view.address(), view.strides(), view.tensor.dtype, job.channels, view.head_dim)}
+        rope = _rope_fields(job, device, stream)
+        keepalive.extend(rope[10])
+        item["rope"] = rope
+        if job.basis.dtype != torch.float16:
+            with torch.cuda.stream(stream):
+                item["basis"] = job.basis[:job.rank].half().contiguous()
+            keepalive.append(item["basis"])
         if isinstance(source, PictureSource):
-            layout = source.layout
-            k_pad = (rank + 63) // 64 * 64
             addresses = np.array([[picture.data_ptr() for picture in segment] for segment in source.pictures],
                                  dtype=np.int64).reshape(-1)
-            col_off, col_seg = _column_tables(layout, source.plane_stride, source.row_stride, k_pad)
-            unpack_rows.append([arena.add(addresses), arena.add(col_off), arena.add(col_seg), len(scratch_sizes),
-                                source.row_stride, job.tokens, k_pad, layout["frames"], layout["height"],
-                                layout["width"]])
-            scratch_sizes.append(job.tokens * k_pad)
-            row[0] = -len(scratch_sizes)  # patched to the scratch address below
-            row[2] = arena.add(source.scale[:rank])
-            row[3] = arena.add(source.offset[:rank])
-            row[7] = k_pad
-            row[13] = 1
-            bound = _affine_bound(source.scale[:rank], source.offset[:rank])
+            item.update(kind="pictures", pictures=(addresses, source.plane_stride, source.row_stride, source.layout),
+                        scale=source.scale, offset=source.offset)
         elif source.quantized:
-            values = source.values
-            k_pad = (rank + 63) // 64 * 64
-            if (values.stride(1) != 1 or values.stride(0) % 16 or values.stride(0) < k_pad
-                    or values.data_ptr() % 16):
-                with torch.cuda.stream(stream):
-                    padded = torch.zeros((values.shape[0], k_pad), dtype=torch.uint8, device=device)
-                    padded[:, :rank].copy_(values[:, :rank])
-                values = padded
-                keepalive.append(values)
-            row[0] = values.data_ptr()
-            row[2] = arena.add(source.scale[:rank])
-            row[3] = arena.add(source.offset[:rank])
-            row[7] = values.stride(0)
-            row[13] = 1
-            bound = _affine_bound(source.scale[:rank], source.offset[:rank])
+            item.update(kind="u8", values=source.values, scale=source.scale, offset=source.offset)
         else:
-            values = source.values
-            if values.dtype != torch.float32 or values.stride(1) != 1:
-                with torch.cuda.stream(stream):
-                    values = values.float().contiguous()
-                keepalive.append(values)
-            row[0] = values.data_ptr()
-            row[7] = values.stride(0)
-            row[13] = 2
-            if source.bound is not None:
-                bound = float(source.bound)
-            else:
-                with torch.cuda.stream(stream):
-                    bound = float(values[:, :rank].abs().amax().item())
-        exponent = _prescale_exponent(bound)
-        scales.append((2.0 ** exponent, 2.0 ** -exponent))
-        view = job.destination
-        ts, hs, ds = view.strides()
-        row[4] = view.address()
-        row[10], row[11], row[12] = ts, hs, ds
-        row[14] = job.tokens
-        row[15] = rank
-        row[16], row[17], row[18] = job.grid
-        row[22] = _OUT_CODE[view.tensor.dtype]
-        row[23] = job.channels
-        row[24] = view.head_dim
-        rope = _rope_fields(job, device, stream)
-        row[25:33] = list(rope[:8])
-        row[5], row[6] = rope[8], rope[9]
-        keepalive.extend(rope[10])
-        row[33] = 1 if precision == "fp16x2" else 0
-        rows.append(row)
-        if job.basis_t is not None:
-            bases.append(job.basis_t)
-        else:
-            basis = job.basis if job.basis.dtype == torch.float16 else job.basis.half()
-            with torch.cuda.stream(stream):
-                bases.append(transposed_basis(basis))
-    host, dev = arena.upload(device, stream)
-    keepalive.extend((host, dev))
-    base = dev.data_ptr()
-    for row, job in zip(rows, jobs):
-        if isinstance(job.source, PictureSource) or job.source.quantized:
-            row[2] += base
-            row[3] += base
-    launches = 0
-    if unpack_rows:
-        offsets = np.cumsum([0] + [(size + 255) // 256 * 256 for size in scratch_sizes])
-        with torch.cuda.stream(stream):
-            scratch = torch.empty(int(offsets[-1]), dtype=torch.uint8, device=device)
-        keepalive.append(scratch)
-        for unpack_row in unpack_rows:
-            unpack_row[0] += base
-            unpack_row[1] += base
-            unpack_row[2] += base
-            unpack_row[3] = scratch.data_ptr() + int(offsets[unpack_row[3]])
-        for row in rows:
-            if row[0] < 0:
-                row[0] = scratch.data_ptr() + int(offsets[-row[0] - 1])
-        with torch.cuda.stream(stream):
-            ext().unpack_launch(torch.tensor(unpack_rows, dtype=torch.int64), device.index)
-        launches += 1
-    keepalive.extend(bases)
-    table = torch.tensor(rows, dtype=torch.int64)
-    prescale = torch.tensor(scales, dtype=torch.float32)
-    with torch.cuda.stream(stream):
-        ext().restore_launch(table, bases, prescale, status_word(device))
-    return launches + 1
+            item.update(kind="f32", values=source.values, bound=source.bound)
+        items.append(item)
+    return launch_factor_group(items, device, precision, stream, keepalive)
 
 
 def _fused_dense_group(jobs, device, stream, keepalive):
@@ -1210,7 +1054,10 @@ def reconstruct(jobs, *, backend="auto", precision="auto", stream=None, wait_eve
     cuda = device.type == "cuda"
     backend = _resolve_backend(backend, cuda)
     if precision == "auto":
-        precision = DEFAULT_PRECISION
+        # One FP16 product (relative error 2^-11) is below the 2^-8 rounding of a bfloat16 cache; wider
+        # destinations take the two-product split.
+        precision = "fp16" if all(job.destination.tensor.dtype == torch.bfloat16 for job in jobs) \
+            else DEFAULT_PRECISION
     if backend == "fused" and precision not in KERNEL_PRECISIONS:
         raise UnsupportedError(f"the fused sm_100a kernel runs {KERNEL_PRECISIONS}; use backend='reference' "
                                f"for {precision}")
@@ -1366,3 +1213,33 @@ def warmup(device, shapes, *, backend="auto", precision="auto", stream=None, **_
         reconstruct([job], backend=backend, precision=precision, stream=stream).release()
         count += 1
     return {"warmed": count}
+
+
+def kernel_error_bound(job, precision="fp16x2", out_dtype=None):
+    """Elementwise bound of the fused sm_100a kernel (same first-order form as :func:`error_bound`).
+
+    For 8-bit sources the kernel multiplies the exact centered pixel ``p - 128`` by the FP16 hi/lo split
+    of ``s[k] Q[k, c]`` and adds the bias ``sum_k (o[k] + 128 s[k]) Q[k, c]``, so its rounding is
+    charged to ``S' = sum_k (|a_k| + |o_k + 128 s_k|) |q_k|`` instead of ``sum_k |a_k| |q_k|`` (``a_k`` the
+    dequantized coefficient); float sources keep the reference's ``S``. Returns ``(y*, bound)`` in FP64.
+    """
+    values, magnitude = reference_values(job)
+    source = job.source
+    quantized = isinstance(source, PictureSource) or (isinstance(source, CoefficientSource) and source.quantized)
+    if quantized:
+        scale = torch.from_numpy(np.asarray(source.scale[:job.rank], dtype=np.float64))
+        offset = torch.from_numpy(np.asarray(source.offset[:job.rank], dtype=np.float64))
+        shifted = (offset + 128.0 * scale).abs().to(magnitude.device)
+        basis = job.basis[:job.rank].to(device=magnitude.device, dtype=torch.float64).abs()
+        extra = (shifted @ basis).expand(job.tokens, -1)
+        if job.rope is not None:
+            pairs = extra.reshape(job.tokens, -1, 2)
+            extra = (pairs[..., 0] + pairs[..., 1]).repeat_interleave(2, dim=-1)
+        magnitude = magnitude + extra
+    out_dtype = job.destination.tensor.dtype if out_dtype is None else out_dtype
+    unit = _UNIT_ROUNDOFF[out_dtype]
+    error = _gemm_gamma(precision, job.rank or 0) * magnitude
+    if job.rope is not None:
+        pairs = values.reshape(job.tokens, -1, 2).abs()
+        error = error + 2.0 ** -21 * (pairs[..., 0] + pairs[..., 1]).repeat_interleave(2, dim=-1)
+    return values, unit * values.abs() + (1 + unit) * error + _OUTPUT_FLOOR[out_dtype]

@@ -31,7 +31,7 @@ def run(device):
                                rope=rk.RopePositions(table, (0, 0, 0)))
     rk.reconstruct([job], backend="fused").release()
     _ext.check_status(device)
-    expect, bound = rk.error_bound(job, "fp16x2")
+    expect, bound = rk.kernel_error_bound(job, "fp16x2")
     got = cache[0].reshape(tokens, -1).double()
     assert bool(((got - expect).abs() <= bound).all()), "fused restore exceeded its error bound"
     a = torch.randn(256, 128, device=device, dtype=torch.bfloat16)

@@ -12,7 +12,7 @@ pytestmark = pytest.mark.gpu
 
 
 def _check(job, precision="fp16x2"):
-    values, bound = rk.error_bound(job, precision)
+    values, bound = rk.kernel_error_bound(job, precision)
     written = job.destination.slot(job.tokens).reshape(job.tokens, -1).double()
     excess = ((written - values).abs() - bound).max().item()
     assert excess <= 0, excess
@@ -40,10 +40,10 @@ def test_fused_group_of_jobs_k_and_v(cuda_device):
         job, _ = picture_job(cuda_device, rank=64 + 32 * chunk, heads=12, destination=cache, token_offset=4680 * chunk,
                              table=table, rope_rows=(3 * chunk, 0, 0), seed=chunk)
         jobs.append(job)
-    rk.reconstruct(jobs, backend="fused").synchronize()
+    rk.reconstruct(jobs, backend="fused").synchronize()  # auto precision: fp16 for bfloat16 caches
     _ext.check_status(cuda_device)
     for job in jobs:
-        _check(job)
+        _check(job, "fp16")
 
 
 @pytest.mark.parametrize("layout", ["THD", "BHTD"])
