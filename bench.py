@@ -1,0 +1,381 @@
+"""Headline benchmark: KV restore of an archived CausVid-shaped history.
+
+Workload (synthetic data, random-init weights of the named architecture): a CausVid-shaped causal DiT
+(30 x 1536, 12 x 128 heads, FFN 8960, 480p -> 4680 tokens per 3-latent-frame chunk, text [512, 4096])
+generates ``--chunks`` chunks; every chunk's clean pre-RoPE K and V of all 30 layers is archived
+through the lineage API (rank method on the GPU, K 98 % / V 95 % energy, 8-bit coefficient packs).
+One timed step = "rewind to chunk 4 and resume": restore the history of chunks 0..3 (18720 tokens,
+30 layers, K and V) into a fresh native KV cache.
+
+``value`` (device-timed, CUDA events on the restore stream): restored native KV bytes / time of the
+fused sm_100a restore (unpack + basis preparation + one tcgen05 GEMM per layer), coefficient tiles
+resident on the device. ``e2e``: the same restore through the public API (LineageRestorer.restore)
+from pinned host memory -- the step's H2D of the coefficient packs is inside the timed region --
+overlapped with the first denoising step of the next chunk, followed by a D2H read of that step's
+latents; ``ttfc_ms`` is that step's wall time on the device clock.
+
+``--impl reference`` runs the reference implementation's own restore kernels (restore_kernels.reconstruct,
+Triton) from ``baseline/_ref`` on identical synthetic picture sources (same geometry, ranks, affines).
+Multi-GPU runs (torchrun) are data-parallel: every rank restores its own session; the value is the
+aggregate (sum of bytes / max time over ranks).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "KV restore GB/s (rewind-to-chunk-4 resume; p50 TTFC and archived chunks/s reported alongside)"
+BASELINE_PUBLISHED = None  # the reference publishes no absolute restore GB/s
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--chunks", type=int, default=5, help="chunks generated and archived before the timed steps")
+    ap.add_argument("--history", type=int, default=4, help="chunks restored per step (rewind target)")
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--layers", type=int, default=30)
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi SM clock / throttle-reason samples during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        fields = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={fields}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *args):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 8:
+                    continue
+                try:
+                    sm.append(float(parts[0]))
+                    smax.append(float(parts[1]))
+                except ValueError:
+                    continue
+                for name, value in zip(names, parts[4:8]):
+                    if value.lower() == "active":
+                        reasons.add(name)
+        except OSError:
+            pass
+        finally:
+            if self.path and os.path.exists(self.path):
+                os.unlink(self.path)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return rank, world, local
+
+
+def reduce_max(value, world):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def build_archive(args, device):
+    """Generate ``args.chunks`` chunks with the DiT and archive every chunk's clean K/V."""
+    import torch
+    sys.path.insert(0, ROOT)
+    from reelcache_b200.lineage import LineageRuntime
+    from reelcache_b200.lineage_commit import ArchiveOptions
+    from reelcache_b200.models.causal_wan import CAUSVID, CausalWanDiT, KVCache
+    from reelcache_b200.models.sampler import ChunkGenerator
+    from reelcache_b200.predictor_registry import RankPredictorRegistry
+    from reelcache_b200.rank_method import RankMethodConfig
+    from reelcache_b200.store import ObjectStore
+    from reelcache_b200.types import CodecSpec, MatrixKey, ModelIdentity, TensorContext, energy_targets
+
+    cfg = CAUSVID if args.layers == 30 else CAUSVID.scaled(layers=args.layers)
+    model = CausalWanDiT(cfg, device, seed=0)
+    identity = ModelIdentity("causvid-wan2.1-1.3b-synthetic", "random-init-seed0", cfg.layers, cfg.dim, "BTHD",
+                             "bfloat16")
+    root = tempfile.mkdtemp(prefix="reelcache-bench-")
+    store = ObjectStore(root)
+    runtime = LineageRuntime(store, identity, registry=RankPredictorRegistry("bench"))
+    runtime.create_lineage("session")
+    method = RankMethodConfig(energy_targets("causvid"), CodecSpec("svd_hevc", 32), solver="topk_rr")
+    options = ArchiveOptions(stream_codec="raw8")
+    gen = torch.Generator(device=device).manual_seed(1)
+    context = torch.randn((cfg.text_len, cfg.text_dim), generator=gen, device=device)
+    text_kv = model.encode_text(context)
+    cache = KVCache(cfg, args.chunks + 1, device)
+    sampler = ChunkGenerator(model, cache, text_kv, seed=2)
+    nodes = []
+    archive_seconds = 0.0
+    ranks = []
+    for index in range(args.chunks):
+        latents = sampler.denoise(index)
+        captured = {}
+
+        def capture(layer, k_pre, v):
+            captured[MatrixKey(layer, "K")] = k_pre.clone()
+            captured[MatrixKey(layer, "V")] = v.clone()
+
+        sampler.commit_clean(index, latents, capture=capture)
+        contexts = {key: TensorContext(identity, key, index * cfg.chunk_tokens, cfg.frames_per_chunk, cfg.grid_h,
+                                       cfg.grid_w, "pre_rope" if key.target == "K" else "none")
+                    for key in captured}
+        torch.cuda.synchronize()
+        started = time.perf_counter()
+        commit = runtime.commit_node("session", f"chunk-{index}", captured, contexts, method=method, device=device,
+                                     options=options)
+        archive_seconds += time.perf_counter() - started
+        ranks.append(commit.plan["mean_rank"])
+        nodes.append(commit.node_ref)
+    return {"cfg": cfg, "model": model, "runtime": runtime, "nodes": nodes, "text_kv": text_kv, "context": context,
+            "archive_seconds": archive_seconds, "ranks": ranks, "store_root": root}
+
+
+def run_ours(args, rank, world, local):
+    import torch
+    from reelcache_b200.archive_restore import LineageRestorer
+    from reelcache_b200.models.causal_wan import KVCache
+    from reelcache_b200.models.sampler import ChunkGenerator
+    from reelcache_b200.ops import _ext
+
+    device = torch.device("cuda", local)
+    state = build_archive(args, device)
+    cfg, model, runtime = state["cfg"], state["model"], state["runtime"]
+    target = state["nodes"][args.history - 1]
+    restorer = LineageRestorer(runtime, device)
+    restorer.prewarm(target)
+    cache = KVCache(cfg, args.history + 1, device)
+    stream = torch.cuda.Stream(device)
+
+    def destination(layer, which):
+        return cache.k[layer] if which == "K" else cache.v[layer]
+
+    def rope(piece):
+        chunk = piece.entry.token_start // cfg.chunk_tokens
+        return model.rope, (cfg.frames_per_chunk * chunk, 0, 0)
+
+    restored_bytes = 2 * cfg.layers * args.history * cfg.chunk_tokens * cfg.dim * 2
+    # ---- device-timed restore: coefficient tiles resident on the device ----
+    program = restorer.build_program(target, destination, rope, stream=stream)
+    with torch.cuda.stream(stream):
+        program.prepare()
+    torch.cuda.synchronize()
+
+    def device_step():
+        with torch.cuda.stream(stream):
+            program.run_aux(stream)  # unpack + basis preparation of every job, each step
+            for layer in range(cfg.layers):
+                program.launch(layer, stream)
+
+    def timed(fn, steps, warmup, s):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(s)
+        for _ in range(steps):
+            fn()
+        stop.record(s)
+        torch.cuda.synchronize()
+        barrier(world)
+        return start.elapsed_time(stop) / steps
+
+    with ClockSampler(local) as clocks:
+        ms_device = timed(device_step, args.steps, args.warmup, stream)
+    clock_summary = clocks.summary()
+    _ext.check_status(device)
+    launches_per_step = sum(len(program.blobs[g]) for g in program.blobs) + len(program.aux[0]) + len(program.aux[1])
+
+    # ---- end to end: public API restore from pinned host packs, overlapped with the first denoise step ----
+    sampler = ChunkGenerator(model, cache, state["text_kv"], seed=3)
+    h2d = sum(restorer.prepared_pack(item.packet_ref).nbytes for item in restorer.history(target))
+    latent_bytes = cfg.in_dim * cfg.frames_per_chunk * cfg.latent_height * cfg.latent_width * 4
+
+    def e2e_step():
+        result = restorer.restore(target, destination, rope, stream=stream, overlapped=True)
+        latents = sampler.denoise(args.history, layer_wait=result.wait)
+        host = latents.to("cpu", non_blocking=False)
+        result.join()
+        return host
+
+    main = torch.cuda.current_stream(device)
+    ms_e2e = timed(e2e_step, max(1, args.steps // 2), max(1, args.warmup - 1), main)
+    # TTFC distribution (device clock per step)
+    samples = []
+    for _ in range(3):
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(main)
+        e2e_step()
+        e.record(main)
+        torch.cuda.synchronize()
+        samples.append(s.elapsed_time(e))
+    ttfc_p50 = float(np.median(samples))
+    ms_device = reduce_max(ms_device, world)
+    ms_e2e = reduce_max(ms_e2e, world)
+    archived_per_s = args.chunks / max(state["archive_seconds"], 1e-9)
+    value = world * restored_bytes / (ms_device * 1e-3) / 1e9
+    e2e_value = world * restored_bytes / (ms_e2e * 1e-3) / 1e9
+    return {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms_device, 4),
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "ms_per_step": round(ms_e2e, 3),
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(latent_bytes),
+                "includes": "H2D of the history's coefficient packs + restore overlapped with the first denoise "
+                            "step of the next chunk (3 DiT forwards) + D2H of its latents"},
+        "ttfc_p50_ms": round(ttfc_p50, 2), "archived_chunks_per_s": round(archived_per_s, 4),
+        "mean_rank": round(float(np.mean(state["ranks"])), 1), "gpu_launches": launches_per_step,
+        "clocks": clock_summary, "restored_bytes_per_step": restored_bytes,
+    }
+
+
+def run_reference(args, rank, world, local):
+    """The reference's own Triton restore (restore_kernels.reconstruct) on identical picture sources."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "reelcache")):
+        return {"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}
+    sys.path.insert(0, ref_dir)
+    try:
+        import torch
+        from reelcache import restore_kernels as rrk
+        from reelcache import _hevc as rhevc
+    except Exception as error:  # noqa: BLE001
+        return {"impl": "reference", "unavailable": f"reference import failed: {type(error).__name__}: {error}"}
+    device = torch.device("cuda", local)
+    layers, chunks, heads, dim = args.layers, args.history, 12, 128
+    frames, height, width, rank_cols = 3, 30, 52, 256
+    tokens = frames * height * width
+    rng = np.random.default_rng(0)
+    cache_k = [torch.zeros((1, chunks * tokens, heads, dim), dtype=torch.bfloat16, device=device) for _ in range(layers)]
+    cache_v = [torch.zeros_like(cache_k[0]) for _ in range(layers)]
+    table = rrk.RopeTable.from_complex(torch.polar(torch.ones(1024, 64), torch.rand(1024, 64) * 6.28).to(device))
+    jobs_by_layer = []
+    keep = []
+    for layer in range(layers):
+        jobs = []
+        for c in range(chunks):
+            for which, cache in (("K", cache_k), ("V", cache_v)):
+                values = rng.standard_normal((tokens, rank_cols)).astype(np.float32)
+                pixels, affine, norm = rhevc.quantize_coefficients(values, "per_channel")
+                lay = rhevc.video_layout(frames, height, width, rank_cols, "yuv444p")
+                canvases = torch.from_numpy(np.concatenate([rhevc._mosaic(pixels.reshape(frames, height, width, -1), lay, s)
+                                                            for s in range(lay["segments"])])).to(device)
+                scale, offset = rrk.expand_affine(affine, norm, rank_cols)
+                indices = [[s * frames + f for f in range(frames)] for s in range(lay["segments"])]
+                src = rrk.PictureSource.from_canvases(canvases, lay, indices, (0, 0), scale, offset)
+                basis = (torch.randn(rank_cols, heads * dim, device=device) / 40).half()
+                keep.extend((canvases, basis))
+                rope = rrk.RopePositions(table, (3 * c, 0, 0)) if which == "K" else None
+                jobs.append(rrk.ReconstructionJob(src, rrk.NativeView(cache[layer], "BTHD", c * tokens),
+                                                  (frames, height, width), basis, rope=rope))
+        jobs_by_layer.append(jobs)
+    stream = torch.cuda.Stream(device)
+
+    def step():
+        handles = [rrk.reconstruct(jobs, stream=stream) for jobs in jobs_by_layer]
+        return handles
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        stop.record(stream)
+        torch.cuda.synchronize()
+    ms = reduce_max(start.elapsed_time(stop) / args.steps, world)
+    restored = 2 * layers * chunks * tokens * heads * dim * 2
+    return {"metric": METRIC, "value": round(world * restored / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(ms, 4), "impl": "reference", "clocks": clocks.summary(),
+            "note": "reference Triton restore_kernels.reconstruct (auto backend/precision) on picture sources, rank 256"}
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_setup(args)
+    if args.impl == "reference":
+        out = run_reference(args, rank, world, local)
+    else:
+        out = run_ours(args, rank, world, local)
+    if "unavailable" not in out:
+        out.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                    "scaling": "weak", "vs_baseline": None if BASELINE_PUBLISHED is None else out["value"] / BASELINE_PUBLISHED,
+                    "dtype": "bf16", "data": "synthetic (random-init CausVid-shaped DiT generates the archived history)",
+                    "config": {"model": "CausVid-shaped causal DiT (Wan2.1-T2V-1.3B geometry), random-init bf16",
+                               "global_batch": world, "seq_len": args.history * 4680, "parallelism": f"dp{world}",
+                               "history_chunks": args.history, "tokens_per_chunk": 4680,
+                               "l2": "each step writes 3.45 GB of KV, far larger than the 126 MB L2"}})
+        out.setdefault("impl", args.impl)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

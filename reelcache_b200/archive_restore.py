@@ -1,0 +1,288 @@
+"""Restore of a lineage node's attended history into native KV caches (reference:
+reelcache/archive_restore.py:72-1479).
+
+:class:`LineageRestorer` resolves a node's history (newest version of every attended range on its
+ancestor path), keeps decoded node packs in pinned host memory (the prepared-packet cache / decoded
+tier: restores skip entropy decoding) and FP16 basis prefixes on the device (:class:`DeviceBasisCache`),
+copies the history's 8-bit coefficient tiles to the device with one asynchronous copy per pack, and
+reconstructs every layer with the fused sm_100a kernels (ops/restore.py): unpack + basis preparation
+for all jobs, then one tcgen05 GEMM launch per layer that writes ``RoPE(dequant(P) @ Q)`` into the
+cache. Layers are marked on a :class:`~reelcache_b200.overlapped_restore.LayerReadiness` so the first
+forward of the next chunk waits only for the layer it is about to attend over.
+"""
+
+from __future__ import annotations
+
+import threading
+import time
+from collections import OrderedDict
+from dataclasses import dataclass, field
+from typing import Any, Callable, Mapping, Sequence
+
+import numpy as np
+import torch
+
+from .cache_epochs import ResolvedPiece
+from .errors import CapacityError, ConfigurationError, IntegrityError, UnsupportedError
+from .lineage import LineageRuntime
+from .ops.restore import RestoreProgram
+from .overlapped_restore import LayerReadiness, OverlappedRestore, start_overlapped_restore
+from .restore_kernels import RopeTable
+from .types import MatrixKey, entry_parts
+
+
+class DeviceBasisCache:
+    """FP16 basis prefixes ``[rank, C]`` on one device by (version ref, rank), LRU under a byte budget
+    (plus max |Q| of each, for the restore's exact prescale)."""
+
+    def __init__(self, runtime: LineageRuntime, device, *, budget_bytes: int = 4 << 30):
+        self.runtime = runtime
+        self.device = torch.device(device)
+        self.budget = budget_bytes
+        self._lock = threading.Lock()
+        self._entries: OrderedDict = OrderedDict()
+        self.bytes = 0
+        self.hits = 0
+        self.misses = 0
+
+    def get(self, version_ref: str, rank: int, stream=None) -> tuple[torch.Tensor, float]:
+        key = (version_ref, rank)
+        with self._lock:
+            hit = self._entries.get(key)
+            if hit is not None:
+                self._entries.move_to_end(key)
+                self.hits += 1
+                return hit
+        rows = self.runtime.basis.assemble(version_ref, rank)
+        qmax = float(np.abs(rows.numpy().astype(np.float32)).max(initial=0.0))
+        ctx = torch.cuda.stream(stream) if stream is not None else _Null()
+        with ctx:
+            device_rows = rows.pin_memory().to(self.device, non_blocking=True) if self.device.type == "cuda" \
+                else rows.to(self.device)
+        entry = (device_rows, qmax)
+        with self._lock:
+            self.misses += 1
+            self._entries[key] = entry
+            self.bytes += device_rows.numel() * 2
+            while self.bytes > self.budget and len(self._entries) > 1:
+                _, (old, _) = self._entries.popitem(last=False)
+                self.bytes -= old.numel() * 2
+        return entry
+
+    def stats(self) -> dict[str, int]:
+        return {"entries": len(self._entries), "bytes": self.bytes, "hits": self.hits, "misses": self.misses}
+
+
+@dataclass
+class PreparedPack:
+    """A node pack's decoded coefficient tiles in (pinned) host memory, and its affines."""
+
+    packet_ref: str
+    raw: torch.Tensor              # uint8 [raw_bytes] (pinned when possible)
+    tiles: list
+    scales: list
+    offsets: list
+    nbytes: int
+
+    def tile_view(self, device_raw: torch.Tensor, index: int) -> torch.Tensor:
+        coeff = self.tiles[index]["coefficients"]
+        tokens, rank = coeff["shape"]
+        return device_raw[coeff["offset"]:coeff["offset"] + coeff["bytes"]].view(tokens, rank)
+
+
+@dataclass
+class HistoryEntry:
+    piece: ResolvedPiece
+    packet_ref: str
+    tiles: dict  # entry -> (tile index, record)
+
+
+@dataclass
+class RestoreResult:
+    node_ref: str
+    readiness: LayerReadiness
+    handle: OverlappedRestore | None
+    stats: dict = field(default_factory=dict)
+
+    def wait(self, layer: int, stream=None) -> None:
+        self.readiness.wait(layer, stream)
+
+    def join(self):
+        if self.handle is not None:
+            self.handle.join()
+        return self.stats
+
+
+class LineageRestorer:
+    """Restores lineage nodes into caches with the fused sm_100a path."""
+
+    def __init__(self, runtime: LineageRuntime, device, *, precision: str = "auto",
+                 prepared_budget_bytes: int = 4 << 30, basis_budget_bytes: int = 4 << 30, pin_memory: bool = True):
+        self.runtime = runtime
+        self.device = torch.device(device)
+        self.precision = precision
+        self.bases = DeviceBasisCache(runtime, self.device, budget_bytes=basis_budget_bytes)
+        self.prepared_budget = prepared_budget_bytes
+        self.pin_memory = pin_memory and self.device.type == "cuda"
+        self._prepared: OrderedDict = OrderedDict()
+        self._prepared_bytes = 0
+        self._lock = threading.Lock()
+        self._histories: dict = {}
+        self.stats_ = {"restores": 0, "packs_prepared": 0, "h2d_bytes": 0}
+
+    # -- preparation ---------------------------------------------------------------------------------------------
+
+    def prepared_pack(self, packet_ref: str) -> PreparedPack:
+        """Decoded pack in pinned host memory (cached, LRU under the prepared budget)."""
+        with self._lock:
+            hit = self._prepared.get(packet_ref)
+            if hit is not None:
+                self._prepared.move_to_end(packet_ref)
+                return hit
+        _, pack = self.runtime.node_pack(packet_ref)
+        raw = torch.from_numpy(np.ascontiguousarray(pack.raw))
+        if self.pin_memory:
+            raw = raw.pin_memory()
+        scales, offsets = [], []
+        for index in range(len(pack.tiles)):
+            s, o = pack.scale_offset(index)
+            scales.append(s)
+            offsets.append(o)
+        prepared = PreparedPack(packet_ref, raw, list(pack.tiles), scales, offsets, raw.numel())
+        with self._lock:
+            self._prepared[packet_ref] = prepared
+            self._prepared_bytes += prepared.nbytes
+            self.stats_["packs_prepared"] += 1
+            while self._prepared_bytes > self.prepared_budget and len(self._prepared) > 1:
+                _, old = self._prepared.popitem(last=False)
+                self._prepared_bytes -= old.nbytes
+        return prepared
+
+    def history(self, node_ref: str, ranges: Sequence[tuple[int, int]] | None = None) -> list[HistoryEntry]:
+        """Resolved history of a node: per attended piece its pack and tile of every matrix entry."""
+        key = (node_ref, None if ranges is None else tuple(map(tuple, ranges)))
+        hit = self._histories.get(key)
+        if hit is not None:
+            return hit
+        entries = []
+        for piece in self.runtime.resolve_history(node_ref, ranges):
+            tiles = {}
+            packet_ref = None
+            for entry, record_ref in piece.entry.records:
+                record = self.runtime.load_record(record_ref)
+                if record.codec.kind == "raw":
+                    raise UnsupportedError("RAW history restores through RawLineageRestorer")
+                packet_ref = record.packet_ref
+                tiles[entry] = (record.decision["packet"]["tile"], record)
+            entries.append(HistoryEntry(piece, packet_ref, tiles))
+        self._histories[key] = entries
+        return entries
+
+    def prewarm(self, node_ref: str, ranges=None) -> int:
+        entries = self.history(node_ref, ranges)
+        for item in entries:
+            self.prepared_pack(item.packet_ref)
+        for item in entries:
+            for _, record in item.tiles.values():
+                self.bases.get(record.basis_version_ref, record.rank_view)
+        return len(entries)
+
+    # -- restore -------------------------------------------------------------------------------------------------
+
+    def build_program(self, node_ref: str, destination: Callable[[int, str], torch.Tensor],
+                      rope: Callable[[ResolvedPiece], tuple[RopeTable, tuple]], *, stream=None, ranges=None,
+                      stream_label: str | None = None, layers: Sequence[int] | None = None) -> RestoreProgram:
+        """Plan the restore of ``node_ref``: H2D of the history's packs (on ``stream``) and one job per
+        (layer, K/V, piece). ``destination(layer, "K"|"V")`` returns the native BTHD cache tensor
+        ``[1, capacity, heads, head_dim]``; ``rope(piece)`` returns the (table, (t_row, h_row, w_row)) of its positions."""
+        stream = stream or torch.cuda.current_stream(self.device)
+        entries = self.history(node_ref, ranges)
+        model = self.runtime.model
+        layers = range(model.layers) if layers is None else layers
+        device_raw = {}
+        precision = self.precision
+        with torch.cuda.stream(stream):
+            for item in entries:
+                if item.packet_ref in device_raw:
+                    continue
+                prepared = self.prepared_pack(item.packet_ref)
+                device_raw[item.packet_ref] = prepared.raw.to(self.device, non_blocking=True)
+                self.stats_["h2d_bytes"] += prepared.nbytes
+        program = None
+        for layer in layers:
+            for target in ("K", "V"):
+                cache = destination(layer, target)  # native BTHD cache [1, capacity, heads, head_dim]
+                head_dim = cache.shape[-1]
+                rows = cache[0]
+                if program is None:
+                    if precision == "auto":
+                        precision = "fp16" if rows.dtype == torch.bfloat16 else "fp16x2"
+                    program = RestoreProgram(self.device, stream, precision=precision)
+                    program.keepalive.extend(device_raw.values())
+                key = MatrixKey(layer, target)
+                entry_key = key if stream_label is None else (key, stream_label)
+                for item in entries:
+                    piece = item.piece
+                    tile_index, record = item.tiles[entry_key]
+                    prepared = self.prepared_pack(item.packet_ref)
+                    values = prepared.tile_view(device_raw[item.packet_ref], tile_index)
+                    tokens = piece.token_end - piece.token_start
+                    context = record.context
+                    if piece.offset or tokens != context.token_count:
+                        values = values[piece.offset:piece.offset + tokens]
+                        if tokens % (context.height * context.width):
+                            raise UnsupportedError("partial-frame history ranges are not restorable by the fused path")
+                    frames = tokens // (context.height * context.width)
+                    grid = (frames, context.height, context.width)
+                    basis, qmax = self.bases.get(record.basis_version_ref, record.rank_view, stream)
+                    slot = rows[piece.token_start:piece.token_end]  # [tokens, heads, head_dim]
+                    job = {"kind": "u8", "values": values, "tokens": tokens, "rank": record.rank_view,
+                           "grid": grid, "basis": basis, "qmax": qmax, "scale": prepared.scales[tile_index],
+                           "offset": prepared.offsets[tile_index],
+                           "dest": (slot.data_ptr(), (slot.stride(0), slot.stride(1), slot.stride(2)), slot.dtype,
+                                    slot.shape[1] * slot.shape[2], head_dim),
+                           "rope": None}
+                    if target == "K" and context.key_space == "pre_rope":
+                        table, rope_rows = rope(piece)
+                        first = piece.offset // (context.height * context.width)
+                        rope_rows = (rope_rows[0] + first, rope_rows[1], rope_rows[2])
+                        cos, sin = table.token_tables(rope_rows, grid, self.device, stream)
+                        program.keepalive.extend((cos, sin))
+                        job["rope"] = (cos.data_ptr(), sin.data_ptr(), cos.shape[1])
+                    program.add(job, group=layer)
+        return program
+
+    def restore(self, node_ref: str, destination, rope, *, stream=None, overlapped: bool = True, ranges=None,
+                readiness: LayerReadiness | None = None, thread: bool = False) -> RestoreResult:
+        """Restore ``node_ref``'s history; returns a :class:`RestoreResult` whose readiness marks each layer
+        (the caller's forward waits per layer). All GPU work runs on ``stream`` (default: a side stream)."""
+        started = time.perf_counter()
+        model = self.runtime.model
+        stream = stream or torch.cuda.Stream(self.device)
+        readiness = readiness or LayerReadiness(model.layers)
+        program = self.build_program(node_ref, destination, rope, stream=stream, ranges=ranges)
+        with torch.cuda.stream(stream):
+            program.prepare()
+        self.stats_["restores"] += 1
+
+        def issue(layer):
+            program.launch(layer, stream)
+
+        handle = start_overlapped_restore(issue, model.layers, stream=stream, thread=thread and overlapped,
+                                          readiness=readiness)
+        stats = {"jobs": len(program.jobs), "launches": program.launches, "prepare_seconds": time.perf_counter() - started}
+        result = RestoreResult(node_ref, readiness, handle, stats)
+        result.program = program
+        return result
+
+    def stats(self) -> dict[str, Any]:
+        return {**self.stats_, "prepared_packs": len(self._prepared), "prepared_bytes": self._prepared_bytes,
+                "bases": self.bases.stats()}
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *args):
+        return False

@@ -9,10 +9,18 @@ void gemm_bf16_tn(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
                   const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& gate,
                   const c10::optional<at::Tensor>& resid, double alpha, int64_t bn,
                   const c10::optional<at::Tensor>& status);
-void restore_launch(const at::Tensor& jobs, const std::vector<at::Tensor>& a_ops, const std::vector<at::Tensor>& b_ops,
-                    const at::Tensor& inverse, const c10::optional<at::Tensor>& status);
+at::Tensor restore_build(const at::Tensor& jobs, const std::vector<at::Tensor>& a_ops,
+                         const std::vector<at::Tensor>& b_ops, const at::Tensor& inverse);
+void restore_run(const at::Tensor& blob, int64_t device, const c10::optional<at::Tensor>& status);
 void prep_launch(const at::Tensor& jobs, int64_t device);
 void colminmax(const at::Tensor& p, at::Tensor& lo, at::Tensor& hi, at::Tensor& bad);
+void ln_modulate(const at::Tensor& x, at::Tensor& y, const c10::optional<at::Tensor>& shift,
+                 const c10::optional<at::Tensor>& scale, const c10::optional<at::Tensor>& weight,
+                 const c10::optional<at::Tensor>& bias, double eps);
+void qkv_norm_rope(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk, const at::Tensor& cos_tok,
+                   const at::Tensor& sin_tok, at::Tensor& q_out, const c10::optional<at::Tensor>& k_pre,
+                   at::Tensor& k_cache, at::Tensor& v_cache, int64_t head_dim, double eps);
+void rms_norm(const at::Tensor& x, at::Tensor& y, const at::Tensor& w, double eps);
 void quantize_columns(const at::Tensor& p, const at::Tensor& scale, const at::Tensor& offset, at::Tensor& out);
 void rope_store_launch(const at::Tensor& jobs);
 void unpack_launch(const at::Tensor& jobs, int64_t device);
@@ -24,12 +32,22 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("B"), py::arg("out"), py::arg("epilogue") = 0, py::arg("bias") = py::none(),
         py::arg("gate") = py::none(), py::arg("resid") = py::none(), py::arg("alpha") = 1.0, py::arg("bn") = 0,
         py::arg("status") = py::none());
-  m.def("restore_launch", &rc::restore_launch, "fused restore GEMM over <= 16 jobs", py::arg("jobs"),
-        py::arg("a_ops"), py::arg("b_ops"), py::arg("inverse"), py::arg("status") = py::none());
+  m.def("restore_build", &rc::restore_build, "launch parameters of a fused restore over <= 16 jobs",
+        py::arg("jobs"), py::arg("a_ops"), py::arg("b_ops"), py::arg("inverse"));
+  m.def("restore_run", &rc::restore_run, "launch a fused restore from restore_build parameters", py::arg("blob"),
+        py::arg("device"), py::arg("status") = py::none());
   m.def("colminmax", &rc::colminmax, "per-column extrema of FP32 coefficients", py::arg("p"), py::arg("lo"),
         py::arg("hi"), py::arg("bad"));
   m.def("quantize_columns", &rc::quantize_columns, "FP64 rint quantization of coefficients to uint8",
         py::arg("p"), py::arg("scale"), py::arg("offset"), py::arg("out"));
+  m.def("ln_modulate", &rc::ln_modulate, "y = LayerNorm(x) * (1 + scale) + shift", py::arg("x"), py::arg("y"),
+        py::arg("shift") = py::none(), py::arg("scale") = py::none(), py::arg("weight") = py::none(),
+        py::arg("bias") = py::none(), py::arg("eps") = 1e-6);
+  m.def("qkv_norm_rope", &rc::qkv_norm_rope, "q/k RMSNorm + RoPE from fused qkv into q and KV-cache slots",
+        py::arg("qkv"), py::arg("wq"), py::arg("wk"), py::arg("cos_tok"), py::arg("sin_tok"), py::arg("q_out"),
+        py::arg("k_pre"), py::arg("k_cache"), py::arg("v_cache"), py::arg("head_dim"), py::arg("eps") = 1e-6);
+  m.def("rms_norm", &rc::rms_norm, "y = RMSNorm(x) * w", py::arg("x"), py::arg("y"), py::arg("w"),
+        py::arg("eps") = 1e-6);
   m.def("prep_launch", &rc::prep_launch, "scaled hi/lo basis + bias preparation over <= 48 jobs", py::arg("jobs"),
         py::arg("device"));
   m.def("rope_store_launch", &rc::rope_store_launch, "dense RoPE + cast + strided store over <= 48 jobs",

@@ -1,0 +1,302 @@
+// DiT block elementwise kernels for sm_100a (memory-bound; one warp per token row, FP32 statistics):
+//
+//   ln_modulate      y = LayerNorm(x) * (1 + scale) + shift          (AdaLN; optional affine weight/bias)
+//   qkv_norm_rope    from the fused QKV projection [T, 3C]: q = RoPE(RMSNorm(q) * wq),
+//                    k_pre = RMSNorm(k) * wk (normalized pre-RoPE K, the archival capture),
+//                    k = RoPE(k_pre) and v written straight into the KV-cache slots
+//   rms_norm         y = RMSNorm(x) * w over the full row (cross-attention q / context k)
+//
+// RMSNorm spans all heads (Wan's qk-norm over the model width). RoPE rotates interleaved pairs with
+// per-token FP32 cos/sin tables [T, head_dim / 2].
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include <cuda_bf16.h>
+
+#include "../common/host.h"
+
+namespace rc {
+namespace norms {
+
+constexpr int kMaxVec = 8;  // up to 8 x 16 bytes (64 bf16) per lane: rows up to 2048 channels
+
+__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&v);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// x, y: [rows, C] bf16 (row strides ldx, ldy); shift/scale: fp32 [C] (null = 0); weight/bias: fp32 [C]
+template <int VEC>
+__global__ void ln_modulate_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, __nv_bfloat16* __restrict__ y,
+                                   int64_t ldy, int rows, int C, const float* __restrict__ shift,
+                                   const float* __restrict__ scale, const float* __restrict__ weight,
+                                   const float* __restrict__ bias, float eps) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float v[VEC * 8];
+  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(row) * ldx);
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < C) unpack8(src[i * 32 + lane], v + i * 8);
+    else
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i * 8 + e] = 0.0f;
+  }
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VEC * 8; ++i) s += v[i];
+  const float mean = warp_sum(s) / C;
+  float q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < C)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = v[i * 8 + e] - mean;
+        q += d * d;
+      }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / C + eps);
+  uint4* dst = reinterpret_cast<uint4*>(y + static_cast<int64_t>(row) * ldy);
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    const int c0 = (i * 32 + lane) * 8;
+    if (c0 >= C) continue;
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int c = c0 + e;
+      float t = (v[i * 8 + e] - mean) * rstd;
+      if (weight != nullptr) t = t * weight[c] + bias[c];
+      const float sc = scale != nullptr ? scale[c] : 0.0f;
+      const float sh = shift != nullptr ? shift[c] : 0.0f;
+      o[e] = t * (1.0f + sc) + sh;
+    }
+    dst[i * 32 + lane] = pack8(o);
+  }
+}
+
+// RMS-normalize one row of C channels held as VEC x 8 values per lane; returns the normalized values
+template <int VEC>
+__device__ __forceinline__ void rms_row(float* v, int C, int lane, const float* __restrict__ w, float eps) {
+  float q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VEC * 8; ++i) q += v[i] * v[i];
+  const float r = rsqrtf(warp_sum(q) / C + eps);
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    const int c0 = (i * 32 + lane) * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[i * 8 + e] = c0 + e < C ? v[i * 8 + e] * r * w[c0 + e] : 0.0f;
+  }
+}
+
+template <int VEC>
+__device__ __forceinline__ void load_row(const __nv_bfloat16* p, int C, int lane, float* v) {
+  const uint4* src = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < C) unpack8(src[i * 32 + lane], v + i * 8);
+    else
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i * 8 + e] = 0.0f;
+  }
+}
+
+template <int VEC>
+__device__ __forceinline__ void store_row(__nv_bfloat16* p, int C, int lane, const float* v) {
+  uint4* dst = reinterpret_cast<uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < C) dst[i * 32 + lane] = pack8(v + i * 8);
+  }
+}
+
+// rotate interleaved pairs: channel c (even) pairs with c + 1, pair index (c % head_dim) / 2
+template <int VEC>
+__device__ __forceinline__ void rope_row(float* v, int C, int lane, int head_dim, const float* __restrict__ cs,
+                                         const float* __restrict__ sn) {
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    const int c0 = (i * 32 + lane) * 8;
+    if (c0 >= C) continue;
+    const int pair0 = (c0 % head_dim) >> 1;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float c = cs[pair0 + e], s = sn[pair0 + e];
+      const float a = v[i * 8 + 2 * e], b = v[i * 8 + 2 * e + 1];
+      v[i * 8 + 2 * e] = a * c - b * s;
+      v[i * 8 + 2 * e + 1] = a * s + b * c;
+    }
+  }
+}
+
+// One warp per token: qkv row [3C] -> q_out [C], k_pre [C], k_cache [C], v_cache [C]
+template <int VEC>
+__global__ void qkv_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ld_qkv, int rows, int C,
+                                     int head_dim, const float* __restrict__ wq, const float* __restrict__ wk,
+                                     const float* __restrict__ cos_tok, const float* __restrict__ sin_tok,
+                                     __nv_bfloat16* __restrict__ q_out, int64_t ld_q,
+                                     __nv_bfloat16* __restrict__ k_pre, int64_t ld_kp,
+                                     __nv_bfloat16* __restrict__ k_cache, int64_t ld_k,
+                                     __nv_bfloat16* __restrict__ v_cache, int64_t ld_v, float eps) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const __nv_bfloat16* src = qkv + static_cast<int64_t>(row) * ld_qkv;
+  const float* cs = cos_tok + static_cast<int64_t>(row) * (head_dim / 2);
+  const float* sn = sin_tok + static_cast<int64_t>(row) * (head_dim / 2);
+  float v[VEC * 8];
+  // q
+  load_row<VEC>(src, C, lane, v);
+  rms_row<VEC>(v, C, lane, wq, eps);
+  rope_row<VEC>(v, C, lane, head_dim, cs, sn);
+  store_row<VEC>(q_out + static_cast<int64_t>(row) * ld_q, C, lane, v);
+  // k
+  load_row<VEC>(src + C, C, lane, v);
+  rms_row<VEC>(v, C, lane, wk, eps);
+  if (k_pre != nullptr) store_row<VEC>(k_pre + static_cast<int64_t>(row) * ld_kp, C, lane, v);
+  rope_row<VEC>(v, C, lane, head_dim, cs, sn);
+  store_row<VEC>(k_cache + static_cast<int64_t>(row) * ld_k, C, lane, v);
+  // v
+  load_row<VEC>(src + 2 * C, C, lane, v);
+  store_row<VEC>(v_cache + static_cast<int64_t>(row) * ld_v, C, lane, v);
+}
+
+template <int VEC>
+__global__ void rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, __nv_bfloat16* __restrict__ y,
+                                int64_t ldy, int rows, int C, const float* __restrict__ w, float eps) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float v[VEC * 8];
+  load_row<VEC>(x + static_cast<int64_t>(row) * ldx, C, lane, v);
+  rms_row<VEC>(v, C, lane, w, eps);
+  store_row<VEC>(y + static_cast<int64_t>(row) * ldy, C, lane, v);
+}
+
+}  // namespace norms
+
+namespace {
+const float* opt_f32(const c10::optional<at::Tensor>& t, int64_t n, const char* name) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  RC_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == n,
+           std::string(name) + " must be a contiguous CUDA float32 vector of the row width");
+  return t->data_ptr<float>();
+}
+
+void check_rows(const at::Tensor& t, const char* name) {
+  RC_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.stride(1) == 1 &&
+               t.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+           std::string(name) + " must be a 16-byte aligned CUDA bfloat16 [rows, C] matrix");
+}
+}  // namespace
+
+#define RC_VEC_DISPATCH(C, KERNEL, ...)                                        \
+  do {                                                                         \
+    const int vec = ((C) + 255) / 256;                                         \
+    RC_CHECK((C) % 8 == 0 && vec >= 1 && vec <= norms::kMaxVec, "row width must be a multiple of 8, <= 2048"); \
+    switch (vec) {                                                             \
+      case 1: KERNEL<1><<<grid, 256, 0, stream>>>(__VA_ARGS__); break;         \
+      case 2: KERNEL<2><<<grid, 256, 0, stream>>>(__VA_ARGS__); break;         \
+      case 3: KERNEL<3><<<grid, 256, 0, stream>>>(__VA_ARGS__); break;         \
+      case 4: KERNEL<4><<<grid, 256, 0, stream>>>(__VA_ARGS__); break;         \
+      case 5: KERNEL<5><<<grid, 256, 0, stream>>>(__VA_ARGS__); break;         \
+      case 6: KERNEL<6><<<grid, 256, 0, stream>>>(__VA_ARGS__); break;         \
+      case 7: KERNEL<7><<<grid, 256, 0, stream>>>(__VA_ARGS__); break;         \
+      default: KERNEL<8><<<grid, 256, 0, stream>>>(__VA_ARGS__); break;        \
+    }                                                                          \
+    RC_CUDA(cudaGetLastError());                                               \
+  } while (0)
+
+void ln_modulate(const at::Tensor& x, at::Tensor& y, const c10::optional<at::Tensor>& shift,
+                 const c10::optional<at::Tensor>& scale, const c10::optional<at::Tensor>& weight,
+                 const c10::optional<at::Tensor>& bias, double eps) {
+  check_rows(x, "x");
+  check_rows(y, "y");
+  const int rows = static_cast<int>(x.size(0));
+  const int C = static_cast<int>(x.size(1));
+  RC_CHECK(y.size(0) == rows && y.size(1) == C, "y must match x");
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(x.get_device()).stream();
+  dim3 grid((rows + 7) / 8);
+  RC_VEC_DISPATCH(C, norms::ln_modulate_kernel, reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                  reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), rows, C, opt_f32(shift, C, "shift"),
+                  opt_f32(scale, C, "scale"), opt_f32(weight, C, "weight"), opt_f32(bias, C, "bias"),
+                  static_cast<float>(eps));
+}
+
+void qkv_norm_rope(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk, const at::Tensor& cos_tok,
+                   const at::Tensor& sin_tok, at::Tensor& q_out, const c10::optional<at::Tensor>& k_pre,
+                   at::Tensor& k_cache, at::Tensor& v_cache, int64_t head_dim, double eps) {
+  check_rows(qkv, "qkv");
+  check_rows(q_out, "q_out");
+  check_rows(k_cache, "k_cache");
+  check_rows(v_cache, "v_cache");
+  const int rows = static_cast<int>(qkv.size(0));
+  const int C = static_cast<int>(qkv.size(1) / 3);
+  RC_CHECK(qkv.size(1) == 3 * C && q_out.size(1) == C && k_cache.size(1) == C && v_cache.size(1) == C &&
+               q_out.size(0) == rows && k_cache.size(0) == rows && v_cache.size(0) == rows,
+           "qkv is [T, 3C]; outputs are [T, C]");
+  RC_CHECK(cos_tok.is_cuda() && cos_tok.scalar_type() == at::kFloat && cos_tok.is_contiguous() &&
+               cos_tok.size(0) == rows && cos_tok.size(1) * 2 == head_dim && sin_tok.sizes() == cos_tok.sizes() &&
+               sin_tok.is_contiguous(),
+           "cos/sin must be float32 [T, head_dim / 2] per-token tables");
+  __nv_bfloat16* kp = nullptr;
+  int64_t ld_kp = 0;
+  if (k_pre.has_value() && k_pre->defined()) {
+    check_rows(*k_pre, "k_pre");
+    kp = reinterpret_cast<__nv_bfloat16*>(k_pre->data_ptr());
+    ld_kp = k_pre->stride(0);
+  }
+  c10::cuda::CUDAGuard guard(qkv.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(qkv.get_device()).stream();
+  dim3 grid((rows + 7) / 8);
+  RC_VEC_DISPATCH(C, norms::qkv_norm_rope_kernel, reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
+                  qkv.stride(0), rows, C, static_cast<int>(head_dim), opt_f32(wq, C, "wq"), opt_f32(wk, C, "wk"),
+                  cos_tok.data_ptr<float>(), sin_tok.data_ptr<float>(),
+                  reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), q_out.stride(0), kp, ld_kp,
+                  reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()), k_cache.stride(0),
+                  reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), v_cache.stride(0), static_cast<float>(eps));
+}
+
+void rms_norm(const at::Tensor& x, at::Tensor& y, const at::Tensor& w, double eps) {
+  check_rows(x, "x");
+  check_rows(y, "y");
+  const int rows = static_cast<int>(x.size(0));
+  const int C = static_cast<int>(x.size(1));
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(x.get_device()).stream();
+  dim3 grid((rows + 7) / 8);
+  RC_VEC_DISPATCH(C, norms::rms_norm_kernel, reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                  reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), rows, C, opt_f32(w, C, "w"),
+                  static_cast<float>(eps));
+}
+
+}  // namespace rc

@@ -5,20 +5,23 @@
 //
 // computed as  acc = A @ Bt^T  with  A[n, k] = p[n, k] - 128  (exact FP16, unpack.cu) and
 // Bt = hi/lo FP16 split of s[k] * Q[k, c] * 2^e (prep.cu), then  y = acc * 2^-e + bias[c]  with the
-// per-channel bias sum_k (o[k] + 128 s[k]) Q[k, c] (precision "u8x2"; "u8" uses the hi half only).
+// per-channel bias sum_k (o[k] + 128 s[k]) Q[k, c]; "fp16x2" runs both halves, "fp16" the hi half.
 //
 // One persistent launch covers a group of jobs (one job = one chunk's K or V of one layer).
-// Work item = (job, 128-token tile, 256-channel tile). Roles (320 threads, one CTA per SM):
-//   warp 0      TMA producer: per K block the A tile [128 x 64] and the B tile [256 x 64] of the
-//               hi half, then (two passes) the same A tile again with the lo half of B; 128-byte
-//               swizzle, no multicast; 4 stages of 48 KB.
+// Work item = (job, 128-token tile, 256-channel tile); each CTA owns a contiguous range of items.
+// Roles (320 threads, one CTA per SM):
+//   warp 0      TMA producer: per K block the A tile [128 x 64] and the B tile [256 x 64] (hi half,
+//               then the lo half in a second pass); 128-byte swizzle, no multicast; 4 stages of 48 KB.
 //   warp 1      TMEM owner and MMA issuer (4 x tcgen05.mma kind::f16 per K block).
-//   warps 2..9  epilogue: warp w reads TMEM lane quarter (w % 4) and one 128-column half of the
-//               tile; applies scale + bias, interleaved-pair RoPE on the (t, h, w) sections from FP32
-//               cos/sin tables stored [pairs, rows] (loaded one 32-column chunk ahead), casts and
-//               stores into the native [T, H, D] / [H, T, D] slot.
+//   warps 2..9  epilogue: warp w reads TMEM lane quarter (w % 4) and one 128-column half of the tile;
+//               applies scale + bias and interleaved-pair RoPE from per-token FP32 cos/sin tables
+//               [tokens, pairs] (16-byte loads, one 32-column chunk ahead), casts, and writes each
+//               32 x 32 block to a 64-byte-swizzled SMEM buffer that a TMA bulk store (double-buffered
+//               per warp) copies into the native cache slot; layouts whose channels are not contiguous
+//               take per-thread strided stores instead.
 // Accumulators are double-buffered in TMEM (2 x 256 columns) so the epilogue of one tile overlaps
-// the main loop of the next.
+// the main loop of the next. The launch parameters (tensor maps included) are built once on the host
+// (restore_build) and launched any number of times (restore_run).
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
@@ -41,7 +44,9 @@ constexpr int kThreads = (2 + kEpilogueWarps) * 32;
 constexpr int kATileBytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBTileBytes = kBN * kBK * 2;   // 32 KB
 constexpr int kStageBytes = kATileBytes + kBTileBytes;
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+constexpr int kOutBufBytes = 32 * 32 * 2;    // one 32 x 32 16-bit output block
+constexpr int kOutBytes = kEpilogueWarps * 2 * kOutBufBytes;
+constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + 1024 + 256;
 constexpr int kTmemCols = 512;
 
 enum OutDtype : int { kOutBF16 = 0, kOutF16 = 1, kOutF32 = 2 };
@@ -49,20 +54,20 @@ enum OutDtype : int { kOutBF16 = 0, kOutF16 = 1, kOutF32 = 2 };
 struct JobDesc {
   void* dst;                // element (token 0, head 0, dim 0) of the destination slot
   const float* bias;        // [channels]
-  const float* cos;         // RoPE tables [pairs, rows] fp32 (null: no rotation)
+  const float* cos;         // per-token RoPE tables [tokens, pairs] fp32 (null: no rotation)
   const float* sin;
   int64_t dst_ts, dst_hs, dst_ds;  // destination element strides (token, head, dim)
   int tokens, kblocks, passes;     // passes: 2 = hi + lo, 1 = hi only
   int a_kblocks, b_kblocks;        // K blocks held by the A / B operands (coordinates wrap)
-  int frames, height, width;
   int out_dtype, channels, head_dim, n_tiles, work_begin;
-  int rope, rope_dense, rope_rs, row_t, row_h, row_w, sec_t, sec_h;
+  int rope, pairs, tma_store;
   float inverse;
 };
 
 struct Params {
   CUtensorMap a_maps[kMaxJobs];  // A [tokens, k_pad] fp16, box 64 x 128
-  CUtensorMap b_maps[kMaxJobs];  // Bt [channels, 2 * k_pad] fp16, box 64 x 256
+  CUtensorMap b_maps[kMaxJobs];  // Bt [channels, k_pad or 2 k_pad] fp16, box 64 x 256
+  CUtensorMap o_maps[kMaxJobs];  // destination [tokens, channels] 16-bit, box 32 x 32, 64-byte swizzle
   JobDesc jobs[kMaxJobs];
   int num_jobs;
   int total_work;
@@ -78,10 +83,25 @@ __device__ __forceinline__ void decode_work(const Params& p, int w, int& j, int&
   n_tile = local - m_tile * p.jobs[j].n_tiles;
 }
 
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
 __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_constant__ Params p, int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint8_t* out_smem = smem + kStages * kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(out_smem + kOutBytes);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
   uint64_t* acc_empty = acc_full + 2;
@@ -90,6 +110,10 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Each CTA owns a contiguous range of work items: consecutive tiles mostly share one job's tensor
+  // maps (descriptor-cache hits) and A tile (L2 hits).
+  const int work_lo = static_cast<int>((static_cast<int64_t>(p.total_work) * blockIdx.x) / gridDim.x);
+  const int work_hi = static_cast<int>((static_cast<int64_t>(p.total_work) * (blockIdx.x + 1)) / gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -116,10 +140,16 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int w = blockIdx.x; w < p.total_work && ok; w += gridDim.x) {
+      int last_job = -1;
+      for (int w = work_lo; w < work_hi && ok; ++w) {
         int j, m_tile, n_tile;
         decode_work(p, w, j, m_tile, n_tile);
         const JobDesc& jb = p.jobs[j];
+        if (j != last_job) {
+          tma_prefetch_desc(&p.a_maps[j]);
+          tma_prefetch_desc(&p.b_maps[j]);
+          last_job = j;
+        }
         const int steps = jb.kblocks * jb.passes;
         for (int s = 0; s < steps; ++s) {
           if (!mbar_wait(&empty[stage], phase ^ 1, status, kTimeoutProducer)) {
@@ -146,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
     uint32_t phase = 0;
     int local = 0;
     bool ok = true;
-    for (int w = blockIdx.x; w < p.total_work && ok; w += gridDim.x, ++local) {
+    for (int w = work_lo; w < work_hi && ok; ++w, ++local) {
       int j, m_tile, n_tile;
       decode_work(p, w, j, m_tile, n_tile);
       const int steps = p.jobs[j].kblocks * p.jobs[j].passes;
@@ -190,38 +220,41 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
     // ---------------- Epilogue (8 warps) ----------------
     const int quarter = warp & 3;
     const int col_half = (warp - 2) >> 2;
+    uint8_t* my_out = out_smem + (warp - 2) * 2 * kOutBufBytes;
     int local = 0;
-    for (int w = blockIdx.x; w < p.total_work; w += gridDim.x, ++local) {
+    int block = 0;  // output blocks written by this warp (selects the staging buffer)
+    for (int w = work_lo; w < work_hi; ++w, ++local) {
       int j, m_tile, n_tile;
       decode_work(p, w, j, m_tile, n_tile);
       const JobDesc& jb = p.jobs[j];
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      const int token = m_tile * kBM + quarter * 32 + lane;
+      const int row0 = m_tile * kBM + quarter * 32;
+      const int token = row0 + lane;
       const bool valid = token < jb.tokens;
-      int frame = 0, y = 0, x = 0;
-      if (valid) {
-        const int per_frame = jb.height * jb.width;
-        frame = token / per_frame;
-        const int rem = token - frame * per_frame;
-        y = rem / jb.width;
-        x = rem - y * jb.width;
-      }
-      const int row_t = jb.rope_dense ? jb.row_t + token : jb.row_t + frame;
-      const int row_h = jb.row_h + y;
-      const int row_w = jb.row_w + x;
       const bool do_rope = jb.rope && valid;
+      const float* cos_row = jb.cos + static_cast<int64_t>(do_rope ? token : 0) * jb.pairs;
+      const float* sin_row = jb.sin + static_cast<int64_t>(do_rope ? token : 0) * jb.pairs;
       float cs_next[16], sn_next[16];
       auto load_rope = [&](int chunk) {
         const int n0 = n_tile * kBN + col_half * (kBN / 2) + chunk * 32;
         const int pair0 = (n0 % jb.head_dim) >> 1;
+        if (do_rope) {
+          const float4* c4 = reinterpret_cast<const float4*>(cos_row + pair0);
+          const float4* s4 = reinterpret_cast<const float4*>(sin_row + pair0);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int pair = pair0 + i;
-          const int trow = (jb.rope_dense || pair < jb.sec_t) ? row_t : (pair < jb.sec_t + jb.sec_h ? row_h : row_w);
-          const int64_t idx = static_cast<int64_t>(pair) * jb.rope_rs + trow;
-          cs_next[i] = do_rope ? __ldg(jb.cos + idx) : 1.0f;
-          sn_next[i] = do_rope ? __ldg(jb.sin + idx) : 0.0f;
+          for (int i = 0; i < 4; ++i) {
+            const float4 c = __ldg(c4 + i);
+            const float4 s = __ldg(s4 + i);
+            cs_next[4 * i] = c.x; cs_next[4 * i + 1] = c.y; cs_next[4 * i + 2] = c.z; cs_next[4 * i + 3] = c.w;
+            sn_next[4 * i] = s.x; sn_next[4 * i + 1] = s.y; sn_next[4 * i + 2] = s.z; sn_next[4 * i + 3] = s.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            cs_next[i] = 1.0f;
+            sn_next[i] = 0.0f;
+          }
         }
       };
       if (n_tile * kBN + col_half * (kBN / 2) < jb.channels) load_rope(0);
@@ -256,7 +289,6 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
           bias[4 * i + 3] = b.w;
         }
         tmem_wait_ld();
-        if (!valid) continue;
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = fmaf(__uint_as_float(raw[i]), jb.inverse, bias[i]);
@@ -267,6 +299,31 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
           v[2 * i] = e * cs[i] - o * sn[i];
           v[2 * i + 1] = e * sn[i] + o * cs[i];
         }
+        if (jb.tma_store) {
+          // 32 x 32 16-bit block -> 64-byte-swizzled staging buffer -> TMA bulk store.
+          uint8_t* ob = my_out + (block & 1) * kOutBufBytes;
+          if (lane == 0) bulk_wait_read<1>();  // the store that used this buffer two blocks ago has read it
+          __syncwarp();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = jb.out_dtype == kOutBF16 ? pack_bf16x2(v[2 * i], v[2 * i + 1]) : pack_f16x2(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t phys = static_cast<uint32_t>(q) ^ ((static_cast<uint32_t>(lane) >> 1) & 3u);
+            *reinterpret_cast<uint4*>(ob + lane * 64 + phys * 16) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < jb.tokens) {
+            tma_store_2d(&p.o_maps[j], ob, n0, row0);
+            bulk_commit();
+          }
+          ++block;
+          continue;
+        }
+        if (!valid) continue;
         const int head = n0 / jb.head_dim;
         const int d0 = n0 - head * jb.head_dim;
         const int64_t base = static_cast<int64_t>(token) * jb.dst_ts + static_cast<int64_t>(head) * jb.dst_hs +
@@ -301,6 +358,9 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
+    // every bulk store must have finished reading its staging buffer before the CTA exits
+    if (lane == 0) bulk_wait_read<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -311,12 +371,12 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
 
 }  // namespace restore
 
-// Launches one fused restore over a group of jobs. `jobs` is a CPU int64 [n, 40] table (field order
-// in reelcache_b200/restore_kernels.py, _restore_row); `a_ops` the per-job centered FP16 pixels
-// [tokens, k_pad] and `b_ops` the prepared [channels, 2 * k_pad] FP16 bases; `inverse` the exact
-// inverse prescales (CPU float32 [n]).
-void restore_launch(const at::Tensor& jobs, const std::vector<at::Tensor>& a_ops, const std::vector<at::Tensor>& b_ops,
-                    const at::Tensor& inverse, const c10::optional<at::Tensor>& status) {
+// Builds the launch parameters of one fused restore over <= 16 jobs (tensor maps encoded once) and
+// returns them as a CPU byte tensor for restore_run. `jobs` is a CPU int64 [n, 40] table (field
+// order: reelcache_b200/ops/restore.py, RestoreProgram.prepare); `a_ops` the per-job A operands and
+// `b_ops` the prepared B operands; `inverse` the exact inverse prescales (CPU float32 [n]).
+at::Tensor restore_build(const at::Tensor& jobs, const std::vector<at::Tensor>& a_ops, const std::vector<at::Tensor>& b_ops,
+                         const at::Tensor& inverse) {
   RC_CHECK(jobs.device().is_cpu() && jobs.scalar_type() == at::kLong && jobs.dim() == 2 && jobs.size(1) == 40,
            "jobs must be a CPU int64 [num_jobs, 40] table");
   const int n = static_cast<int>(jobs.size(0));
@@ -324,10 +384,10 @@ void restore_launch(const at::Tensor& jobs, const std::vector<at::Tensor>& a_ops
   RC_CHECK(static_cast<int>(a_ops.size()) == n && static_cast<int>(b_ops.size()) == n, "one A and B operand per job");
   RC_CHECK(inverse.device().is_cpu() && inverse.scalar_type() == at::kFloat && inverse.numel() == n,
            "inverse must be a CPU float32 [num_jobs] vector");
+  at::Tensor blob = at::zeros({static_cast<int64_t>(sizeof(restore::Params))}, at::TensorOptions().dtype(at::kByte));
+  restore::Params& p = *reinterpret_cast<restore::Params*>(blob.data_ptr<uint8_t>());
   const int64_t* f = jobs.data_ptr<int64_t>();
   const float* inv = inverse.data_ptr<float>();
-  restore::Params p;
-  memset(&p, 0, sizeof(p));
   int work = 0;
   const int device = a_ops[0].get_device();
   for (int i = 0; i < n; ++i) {
@@ -349,20 +409,11 @@ void restore_launch(const at::Tensor& jobs, const std::vector<at::Tensor>& a_ops
     jb.dst_ds = r[6];
     jb.tokens = static_cast<int>(r[7]);
     jb.passes = static_cast<int>(r[8]);
-    jb.frames = static_cast<int>(r[9]);
-    jb.height = static_cast<int>(r[10]);
-    jb.width = static_cast<int>(r[11]);
     jb.out_dtype = static_cast<int>(r[12]);
     jb.channels = static_cast<int>(r[13]);
     jb.head_dim = static_cast<int>(r[14]);
     jb.rope = static_cast<int>(r[15]);
-    jb.rope_dense = static_cast<int>(r[16]);
-    jb.rope_rs = static_cast<int>(r[17]);
-    jb.row_t = static_cast<int>(r[18]);
-    jb.row_h = static_cast<int>(r[19]);
-    jb.row_w = static_cast<int>(r[20]);
-    jb.sec_t = static_cast<int>(r[21]);
-    jb.sec_h = static_cast<int>(r[22]);
+    jb.pairs = static_cast<int>(r[17]);
     jb.inverse = inv[i];
     const int64_t k_pad = std::min(a.size(1), b.size(1));
     RC_CHECK(k_pad % 64 == 0 && (a.size(1) == k_pad || a.size(1) == 2 * k_pad) &&
@@ -372,8 +423,10 @@ void restore_launch(const at::Tensor& jobs, const std::vector<at::Tensor>& a_ops
     RC_CHECK(jb.passes == 1 || jb.passes == 2, "passes must be 1 or 2");
     RC_CHECK(jb.channels % 32 == 0 && jb.head_dim % 32 == 0 && jb.channels % jb.head_dim == 0,
              "channels and head_dim must be multiples of 32");
-    RC_CHECK(jb.frames * jb.height * jb.width == jb.tokens, "grid does not match the token count");
     RC_CHECK(reinterpret_cast<uintptr_t>(jb.bias) % 16 == 0, "bias must be 16-byte aligned");
+    RC_CHECK(!jb.rope || (reinterpret_cast<uintptr_t>(jb.cos) % 16 == 0 && reinterpret_cast<uintptr_t>(jb.sin) % 16 == 0 &&
+                          jb.pairs * 2 == jb.head_dim),
+             "RoPE token tables must be 16-byte aligned [tokens, head_dim / 2] float32 rows");
     jb.kblocks = static_cast<int>(k_pad / restore::kBK);
     jb.a_kblocks = static_cast<int>(a.size(1) / restore::kBK);
     jb.b_kblocks = static_cast<int>(b.size(1) / restore::kBK);
@@ -385,18 +438,34 @@ void restore_launch(const at::Tensor& jobs, const std::vector<at::Tensor>& a_ops
                                restore::kBK, restore::kBM, CU_TENSOR_MAP_SWIZZLE_128B);
     p.b_maps[i] = make_tmap_2d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b.size(1), b.size(0), b.stride(0) * 2,
                                restore::kBK, restore::kBN, CU_TENSOR_MAP_SWIZZLE_128B);
+    // TMA stores need channels contiguous inside each token row (BTHD / THD caches)
+    jb.tma_store = jb.out_dtype != restore::kOutF32 && jb.dst_ds == 1 && jb.dst_hs == jb.head_dim &&
+                   reinterpret_cast<uintptr_t>(jb.dst) % 16 == 0 && (jb.dst_ts * 2) % 16 == 0;
+    if (jb.tma_store)
+      p.o_maps[i] = make_tmap_2d(jb.dst, jb.out_dtype == restore::kOutBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                 2, jb.channels, jb.tokens, jb.dst_ts * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   }
   p.num_jobs = n;
   p.total_work = work;
-  c10::cuda::CUDAGuard guard(device);
+  return blob;
+}
+
+void restore_run(const at::Tensor& blob, int64_t device, const c10::optional<at::Tensor>& status) {
+  RC_CHECK(blob.device().is_cpu() && blob.scalar_type() == at::kByte &&
+               blob.numel() == static_cast<int64_t>(sizeof(restore::Params)),
+           "restore_run takes the byte tensor returned by restore_build");
+  const restore::Params& p = *reinterpret_cast<const restore::Params*>(blob.data_ptr<uint8_t>());
+  const int dev = static_cast<int>(device);
+  c10::cuda::CUDAGuard guard(dev);
   static bool configured[64] = {false};
-  if (!configured[device]) {
+  if (!configured[dev]) {
     RC_CUDA(cudaFuncSetAttribute(restore::restore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  restore::kSmemBytes));
-    configured[device] = true;
+    configured[dev] = true;
   }
-  const int grid = std::min(work, sm_count(device));
-  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(device).stream();
+  const int grid = std::min(p.total_work, sm_count(dev));
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
   restore::restore_kernel<<<grid, restore::kThreads, restore::kSmemBytes, stream>>>(p, status_ptr(status));
   RC_CUDA(cudaGetLastError());
 }

@@ -1,17 +1,20 @@
 """Launch plumbing of the fused sm_100a restore (csrc/restore/{unpack,prep,restore_sm100}.cu).
 
-A launch group of factorized jobs runs as three kernels on the execution stream:
+A set of factorized jobs runs as three kernels on the execution stream:
 
 1. ``unpack``: 8-bit coefficients (mosaic pictures or a dense uint8 matrix) -> A = centered FP16
    pixels ``p - 128`` ``[N, K_pad]`` (exact), zero beyond the rank;
 2. ``prep``: per job, Bt = FP16 hi/lo split of ``s[k] * Q[k, c] * 2^e`` ``[C, 2 K_pad]`` and the
    per-channel bias ``sum_k (o[k] + 128 s[k]) Q[k, c]`` (FP64 accumulation);
-3. ``restore``: persistent TMA -> tcgen05 GEMM ``acc = A @ Bt^T`` (two FP16 products), epilogue
-   ``acc * 2^-e + bias``, RoPE, cast, strided store into the native slots.
+3. ``restore``: persistent TMA -> tcgen05 GEMM ``acc = A @ Bt^T`` (one or two FP16 products), epilogue
+   ``acc * 2^-e + bias``, RoPE from per-token tables, cast, strided store into the native slots.
 
 Float coefficient sources take A = FP16 hi/lo split of ``P * 2^e`` ``[N, 2 K_pad]`` against the plain
-transposed basis ``[C, K_pad]`` (no bias). Scratch operands come from the caching allocator on the
-execution stream and are kept alive by the caller's handle.
+transposed basis ``[C, K_pad]`` (no bias).
+
+:class:`RestoreProgram` plans many jobs once (scratch, operand preparation for every job in a few
+batched launches) and then launches the GEMM group by group (e.g. one layer at a time, overlapped
+with a forward), so the per-layer host cost is one native call.
 """
 
 from __future__ import annotations
@@ -27,6 +30,8 @@ from ._ext import ext, status_word
 
 _OUT_CODE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 _COLUMN_TABLES: dict = {}
+MAX_RESTORE_JOBS = 16
+MAX_AUX_JOBS = 48
 
 
 def k_pad_of(rank: int) -> int:
@@ -107,132 +112,185 @@ def basis_max_abs(basis: torch.Tensor) -> float:
     return hit
 
 
-def launch_factor_group(items, device, precision, stream, keepalive):
-    """Run one fused restore over ``items``: dicts with keys ``kind`` ("pictures" | "u8" | "f32"),
-    ``tokens``, ``rank``, ``grid`` (frames, height, width), ``basis`` (FP16 [R, C]), ``basis_t``
-    (optional FP16 [C, k_pad]), ``qmax`` (optional), ``scale``/``offset`` (host float32 [rank]),
-    ``dest`` (address, (ts, hs, ds), dtype, channels, head_dim), ``rope`` (8 ints + cos/sin pointers)
-    and the source (``pictures`` (addresses, plane_stride, row_stride, layout) | ``values``).
-    Returns the number of kernel launches."""
-    passes = 2 if precision in ("fp16x2",) else 1
-    arena = HostArena()
-    unpack_rows, prep_rows = [], []
-    a_ops, b_ops, inverse, rows = [], [], [], []
-    sizes = []  # (a_elems, b_elems, bias_elems) of scratch per item
-    plan = []
-    for item in items:
-        rank, tokens = item["rank"], item["tokens"]
-        k_pad = k_pad_of(rank)
-        channels = item["dest"][3]
-        if item["kind"] == "f32":
-            a_elems, b_elems, bias_elems = tokens * 2 * k_pad, 0, channels
-        else:
-            a_elems, b_elems, bias_elems = tokens * k_pad, channels * 2 * k_pad, channels
-        plan.append((k_pad, a_elems, b_elems, bias_elems))
-    # one scratch allocation: FP16 operands then FP32 biases (each slice 256-byte aligned)
-    offsets = []
-    cursor = 0
-    for k_pad, a_elems, b_elems, bias_elems in plan:
-        a_off = cursor
-        cursor += (a_elems * 2 + 255) // 256 * 256
-        b_off = cursor
-        cursor += (b_elems * 2 + 255) // 256 * 256
-        bias_off = cursor
-        cursor += (bias_elems * 4 + 255) // 256 * 256
-        offsets.append((a_off, b_off, bias_off))
-    with torch.cuda.stream(stream):
-        scratch = torch.empty(max(cursor, 256), dtype=torch.uint8, device=device)
-    keepalive.append(scratch)
-    base_scratch = scratch.data_ptr()
-    pending_unpack = []
-    pending_prep = []
-    for item, (k_pad, a_elems, b_elems, bias_elems), (a_off, b_off, bias_off) in zip(items, plan, offsets):
-        rank, tokens, channels = item["rank"], item["tokens"], item["dest"][3]
-        bias_view = scratch[bias_off:bias_off + bias_elems * 4].view(torch.float32)
-        if item["kind"] == "f32":
-            values = item["values"]
-            bound = item.get("bound")
-            with torch.cuda.stream(stream):
-                if bound is None:
-                    bound = float(values[:, :rank].abs().amax().item())
-                e = prescale_exponent(bound)
-                a = scratch[a_off:a_off + a_elems * 2].view(torch.float16).view(tokens, 2 * k_pad)
-                a.zero_()
-                scaled = values[:, :rank].float() * (2.0 ** e)
-                hi = scaled.half()
-                a[:, :rank] = hi
-                a[:, k_pad:k_pad + rank] = (scaled - hi.float()).half()
-                bias_view.zero_()
-                b = item.get("basis_t")
-                if b is None:
-                    from ..restore_kernels import transposed_basis
-                    b = transposed_basis(item["basis"])
-            keepalive.append(b)
-            if b.shape[1] != k_pad:
-                b = b[:, :k_pad]
-        else:
-            qmax = item.get("qmax")
-            if qmax is None:
-                qmax = basis_max_abs(item["basis"])
-            smax = float(np.abs(item["scale"]).max(initial=0.0))
-            e = prescale_exponent(smax * qmax)
-            a = scratch[a_off:a_off + a_elems * 2].view(torch.float16).view(tokens, k_pad)
-            b = scratch[b_off:b_off + b_elems * 2].view(torch.float16).view(channels, 2 * k_pad)
-            if item["kind"] == "pictures":
-                addresses, plane_stride, row_stride, layout = item["pictures"]
-                col_off, col_seg = column_tables(layout, plane_stride, row_stride, k_pad)
-                frames, height, width = item["grid"]
-                pending_unpack.append([arena.add(addresses), arena.add(col_off), arena.add(col_seg), 0, a.data_ptr(),
-                                       row_stride, tokens, k_pad, rank, frames, height, width])
+class RestoreProgram:
+    """Jobs planned once, prepared in batched launches, restored group by group.
+
+    Each job (``add``) is a dict: ``kind`` ("pictures" | "u8" | "f32"), ``tokens``, ``rank``, ``grid``
+    (frames, height, width), ``basis`` (FP16 [R, C]), optional ``basis_t`` (FP16 [C, k_pad]) and
+    ``qmax``, ``scale``/``offset`` (host float32 [>= rank]), ``dest`` (address, (ts, hs, ds), dtype,
+    channels, head_dim), ``rope`` (cos address, sin address, pairs) or None, and the source
+    (``pictures``: (addresses, plane_stride, row_stride, layout) | ``values``: device tensor).
+    """
+
+    def __init__(self, device, stream, *, precision: str = "fp16"):
+        self.device = torch.device(device)
+        self.stream = stream
+        self.passes = 2 if precision == "fp16x2" else 1
+        self.jobs: list[dict] = []
+        self.groups: dict = {}
+        self.keepalive: list = []
+        self.prepared = False
+        self.launches = 0
+
+    def add(self, job: dict, group=0) -> None:
+        if self.prepared:
+            raise ConfigurationError("jobs cannot be added after prepare()")
+        self.groups.setdefault(group, []).append(len(self.jobs))
+        self.jobs.append(job)
+
+    def prepare(self) -> "RestoreProgram":
+        """Allocate scratch, run unpack + prep for every job (batched), build every restore table."""
+        stream, device = self.stream, self.device
+        plan = []
+        cursor = 0
+        for job in self.jobs:
+            rank, tokens, channels = job["rank"], job["tokens"], job["dest"][3]
+            k_pad = k_pad_of(rank)
+            if job["kind"] == "f32":
+                sizes = (tokens * 2 * k_pad * 2, 0, channels * 4)
             else:
-                values = item["values"]
-                frames, height, width = item["grid"]
-                pending_unpack.append([-1, -1, -1, values.data_ptr(), a.data_ptr(), values.stride(0), tokens, k_pad,
-                                       rank, frames, height, width])
-            basis = item["basis"]
-            scale_off = arena.add(np.ascontiguousarray(item["scale"][:rank], dtype=np.float32))
-            offset_off = arena.add(np.ascontiguousarray(item["offset"][:rank], dtype=np.float32))
-            bits = struct.unpack("<I", struct.pack("<f", float(2.0 ** e)))[0]
-            pending_prep.append([basis.data_ptr(), scale_off, offset_off, b.data_ptr(), bias_view.data_ptr(),
-                                 basis.stride(0), rank, k_pad, channels, bits])
-            keepalive.append(basis)
-        address, (ts, hs, ds), dtype, channels, head_dim = item["dest"]
-        rope = item["rope"]
-        row = [0] * 40
-        row[0] = address
-        row[1] = bias_view.data_ptr()
-        row[2], row[3] = rope[8], rope[9]
-        row[4], row[5], row[6] = ts, hs, ds
-        row[7] = tokens
-        row[8] = passes
-        row[9], row[10], row[11] = item["grid"]
-        row[12] = _OUT_CODE[dtype]
-        row[13] = channels
-        row[14] = head_dim
-        row[15:23] = list(rope[:8])
-        rows.append(row)
-        a_ops.append(a)
-        b_ops.append(b)
-        inverse.append(2.0 ** -e)
-    launches = 0
-    if pending_unpack or pending_prep:
-        host, dev = arena.upload(device, stream)
-        keepalive.extend((host, dev))
-        base = dev.data_ptr()
-        for row in pending_unpack:
-            for index in (0, 1, 2):
-                row[index] = 0 if row[index] < 0 else row[index] + base
-        for row in pending_prep:
-            row[1] += base
-            row[2] += base
+                sizes = (tokens * k_pad * 2, channels * 2 * k_pad * 2, channels * 4)
+            offsets = []
+            for size in sizes:
+                offsets.append(cursor)
+                cursor += (size + 255) // 256 * 256
+            plan.append((k_pad, offsets))
         with torch.cuda.stream(stream):
-            if pending_unpack:
-                ext().unpack_launch(torch.tensor(pending_unpack, dtype=torch.int64), device.index)
-                launches += 1
-            if pending_prep:
-                ext().prep_launch(torch.tensor(pending_prep, dtype=torch.int64), device.index)
-                launches += 1
-    with torch.cuda.stream(stream):
-        ext().restore_launch(torch.tensor(rows, dtype=torch.int64), a_ops, b_ops,
-                             torch.tensor(inverse, dtype=torch.float32), status_word(device))
-    return launches + 1
+            scratch = torch.empty(max(cursor, 256), dtype=torch.uint8, device=device)
+        self.keepalive.append(scratch)
+        arena = HostArena()
+        unpack_rows, prep_rows = [], []
+        self.a_ops, self.b_ops, self.inverse, self.rows = [], [], [], []
+        for job, (k_pad, (a_off, b_off, bias_off)) in zip(self.jobs, plan):
+            rank, tokens, channels = job["rank"], job["tokens"], job["dest"][3]
+            bias_view = scratch[bias_off:bias_off + channels * 4].view(torch.float32)
+            if job["kind"] == "f32":
+                values = job["values"]
+                bound = job.get("bound")
+                with torch.cuda.stream(stream):
+                    if bound is None:
+                        bound = float(values[:, :rank].abs().amax().item())
+                    e = prescale_exponent(bound)
+                    a = scratch[a_off:a_off + tokens * 2 * k_pad * 2].view(torch.float16).view(tokens, 2 * k_pad)
+                    a.zero_()
+                    scaled = values[:, :rank].float() * (2.0 ** e)
+                    hi = scaled.half()
+                    a[:, :rank] = hi
+                    a[:, k_pad:k_pad + rank] = (scaled - hi.float()).half()
+                    bias_view.zero_()
+                    b = job.get("basis_t")
+                    if b is None:
+                        from ..restore_kernels import transposed_basis
+                        b = transposed_basis(job["basis"])
+                self.keepalive.append(b)
+                b = b[:, :k_pad]
+            else:
+                qmax = job.get("qmax")
+                if qmax is None:
+                    qmax = basis_max_abs(job["basis"])
+                smax = float(np.abs(job["scale"][:rank]).max(initial=0.0))
+                e = prescale_exponent(smax * qmax)
+                a = scratch[a_off:a_off + tokens * k_pad * 2].view(torch.float16).view(tokens, k_pad)
+                b = scratch[b_off:b_off + channels * 2 * k_pad * 2].view(torch.float16).view(channels, 2 * k_pad)
+                frames, height, width = job["grid"]
+                if job["kind"] == "pictures":
+                    addresses, plane_stride, row_stride, layout = job["pictures"]
+                    col_off, col_seg = column_tables(layout, plane_stride, row_stride, k_pad)
+                    unpack_rows.append([arena.add(addresses), arena.add(col_off), arena.add(col_seg), 0,
+                                        a.data_ptr(), row_stride, tokens, k_pad, rank, frames, height, width])
+                else:
+                    values = job["values"]
+                    self.keepalive.append(values)
+                    unpack_rows.append([-1, -1, -1, values.data_ptr(), a.data_ptr(), values.stride(0), tokens,
+                                        k_pad, rank, frames, height, width])
+                basis = job["basis"]
+                scale_off = arena.add(np.ascontiguousarray(job["scale"][:rank], dtype=np.float32))
+                offset_off = arena.add(np.ascontiguousarray(job["offset"][:rank], dtype=np.float32))
+                bits = struct.unpack("<I", struct.pack("<f", float(2.0 ** e)))[0]
+                prep_rows.append([basis.data_ptr(), scale_off, offset_off, b.data_ptr(), bias_view.data_ptr(),
+                                  basis.stride(0), rank, k_pad, channels, bits])
+                self.keepalive.append(basis)
+            address, (ts, hs, ds), dtype, channels, head_dim = job["dest"]
+            row = [0] * 40
+            row[0] = address
+            row[1] = bias_view.data_ptr()
+            rope = job.get("rope")
+            if rope is not None:  # per-token tables [tokens, pairs]: (cos address, sin address, pairs)
+                row[2], row[3] = rope[0], rope[1]
+                row[15], row[17] = 1, rope[2]
+            row[4], row[5], row[6] = ts, hs, ds
+            row[7] = tokens
+            row[8] = self.passes
+            row[9], row[10], row[11] = job["grid"]
+            row[12] = _OUT_CODE[dtype]
+            row[13] = channels
+            row[14] = head_dim
+            self.rows.append(row)
+            self.a_ops.append(a)
+            self.b_ops.append(b)
+            self.inverse.append(2.0 ** -e)
+        if unpack_rows or prep_rows:
+            host, dev = arena.upload(device, stream)
+            self.keepalive.extend((host, dev))
+            base = dev.data_ptr()
+            for row in unpack_rows:
+                for index in (0, 1, 2):
+                    row[index] = 0 if row[index] < 0 else row[index] + base
+            for row in prep_rows:
+                row[1] += base
+                row[2] += base
+        self.aux = ([torch.tensor(unpack_rows[i:i + MAX_AUX_JOBS], dtype=torch.int64)
+                     for i in range(0, len(unpack_rows), MAX_AUX_JOBS)],
+                    [torch.tensor(prep_rows[i:i + MAX_AUX_JOBS], dtype=torch.int64)
+                     for i in range(0, len(prep_rows), MAX_AUX_JOBS)])
+        self.run_aux(stream)
+        # launch parameters (tensor maps included) encoded once per batch of <= 16 jobs
+        self.blobs = {}
+        for group, indices in self.groups.items():
+            blobs = []
+            for i in range(0, len(indices), MAX_RESTORE_JOBS):
+                chunk = indices[i:i + MAX_RESTORE_JOBS]
+                blobs.append(ext().restore_build(torch.tensor([self.rows[j] for j in chunk], dtype=torch.int64),
+                                                 [self.a_ops[j] for j in chunk], [self.b_ops[j] for j in chunk],
+                                                 torch.tensor([self.inverse[j] for j in chunk], dtype=torch.float32)))
+            self.blobs[group] = blobs
+        self.keepalive.extend(self.a_ops)
+        self.keepalive.extend(self.b_ops)
+        self.prepared = True
+        return self
+
+    def run_aux(self, stream=None) -> int:
+        """(Re-)run the operand preparation of every job: unpack of the 8-bit sources and basis prep."""
+        unpack_tables, prep_tables = self.aux
+        with torch.cuda.stream(stream or self.stream):
+            for table in unpack_tables:
+                ext().unpack_launch(table, self.device.index)
+            for table in prep_tables:
+                ext().prep_launch(table, self.device.index)
+        self.launches += len(unpack_tables) + len(prep_tables)
+        return len(unpack_tables) + len(prep_tables)
+
+    def launch(self, group=0, stream=None) -> int:
+        """Launch the restore GEMM of one group on ``stream`` (default: the program's stream)."""
+        if not self.prepared:
+            self.prepare()
+        status = status_word(self.device)
+        with torch.cuda.stream(stream or self.stream):
+            for blob in self.blobs[group]:
+                ext().restore_run(blob, self.device.index, status)
+        self.launches += len(self.blobs[group])
+        return len(self.blobs[group])
+
+    def launch_all(self, stream=None) -> int:
+        return sum(self.launch(group, stream) for group in self.groups)
+
+
+def launch_factor_group(items, device, precision, stream, keepalive):
+    """Plan, prepare and launch ``items`` (see :class:`RestoreProgram`); returns the launch count."""
+    program = RestoreProgram(device, stream, precision=precision)
+    for item in items:
+        program.add(item)
+    program.prepare()
+    program.launch_all()
+    keepalive.append(program)
+    return program.launches

@@ -345,6 +345,45 @@ class RopeTable:
             self._device_cache[device] = entry
         return entry[0], entry[1]
 
+    def token_tables(self, positions_rows, grid, device, stream=None):
+        """Per-token FP32 ``(cos, sin)`` ``[tokens, pairs]`` of one chunk's positions (cached per
+        positions, grid and device): the fused restore epilogue reads each token's 16-pair slices
+        with 16-byte loads instead of resolving the three axis sections per pair."""
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        stamp = self._stamp()
+        key = ("tok", device, positions_rows if isinstance(positions_rows, int) else tuple(positions_rows),
+               tuple(grid))
+        entry = self._device_cache.get(key)
+        if entry is None or entry[2] != stamp:
+            cos, sin = self.kernel_tables(device, stream)
+            frames, height, width = grid
+            tokens = frames * height * width
+            ctx = torch.cuda.stream(stream) if (stream is not None and device.type == "cuda") else _null()
+            with torch.inference_mode(False), torch.no_grad(), ctx:
+                if self.sections is None:
+                    first = positions_rows
+                    out_cos = cos[first:first + tokens].contiguous()
+                    out_sin = sin[first:first + tokens].contiguous()
+                else:
+                    index = torch.arange(tokens, device=device)
+                    coordinates = (index // (height * width), (index % (height * width)) // width, index % width)
+                    out_cos = torch.empty((tokens, self.pairs), dtype=torch.float32, device=device)
+                    out_sin = torch.empty_like(out_cos)
+                    column = 0
+                    for axis, pairs in enumerate(self.sections):
+                        rows = positions_rows[axis] + coordinates[axis]
+                        out_cos[:, column:column + pairs] = cos[rows, column:column + pairs]
+                        out_sin[:, column:column + pairs] = sin[rows, column:column + pairs]
+                        column += pairs
+            entry = (out_cos, out_sin, stamp)
+            if len(self._device_cache) > 256:
+                for stale in [k for k in self._device_cache if isinstance(k, tuple) and k and k[0] == "tok"][:128]:
+                    del self._device_cache[stale]
+            self._device_cache[key] = entry
+        return entry[0], entry[1]
+
     def kernel_tables_t(self, device, stream=None):
         """Transposed FP32 ``(cos, sin)`` ``[pairs, rows]`` for the sm_100a kernels: lanes of a warp
         hold consecutive tokens, so the rows they read for one pair are adjacent in memory."""
@@ -962,9 +1001,12 @@ def _fused_factor_group(jobs, device, precision, stream, keepalive):
         item = {"tokens": job.tokens, "rank": job.rank, "grid": job.grid, "basis": job.basis,
                 "basis_t": job.basis_t,
                 "dest": (view.address(), view.strides(), view.tensor.dtype, job.channels, view.head_dim)}
-        rope = _rope_fields(job, device, stream)
-        keepalive.extend(rope[10])
-        item["rope"] = rope
+        if job.rope is None:
+            item["rope"] = None
+        else:
+            cos, sin = job.rope.table.token_tables(job.rope.rows, job.grid, device, stream)
+            keepalive.extend((cos, sin))
+            item["rope"] = (cos.data_ptr(), sin.data_ptr(), cos.shape[1])
         if job.basis.dtype != torch.float16:
             with torch.cuda.stream(stream):
                 item["basis"] = job.basis[:job.rank].half().contiguous()
