@@ -11,13 +11,16 @@ One timed step = "rewind to chunk 4 and resume": restore the history of chunks 0
 fused sm_100a restore (unpack + basis preparation + one tcgen05 GEMM per layer), coefficient tiles
 resident on the device. ``e2e``: the same restore through the public API (LineageRestorer.restore)
 from pinned host memory -- the step's H2D of the coefficient packs is inside the timed region --
-overlapped with the first denoising step of the next chunk, followed by a D2H read of that step's
-latents; ``ttfc_ms`` is that step's wall time on the device clock.
+followed by a D2H read of a checksum of the restored cache. ``ttfc_p50_ms``: rewind-and-resume time to
+the first denoised chunk (restore overlapped layer by layer with the first denoising step, D2H of its
+latents), device clock, median of 3.
 
 ``--impl reference`` runs the reference implementation's own restore kernels (restore_kernels.reconstruct,
-Triton) from ``baseline/_ref`` on identical synthetic picture sources (same geometry, ranks, affines).
-Multi-GPU runs (torchrun) are data-parallel: every rank restores its own session; the value is the
-aggregate (sum of bytes / max time over ranks).
+Triton) from ``baseline/_ref`` on synthetic picture sources of the same geometry and the same per-matrix
+ranks (``bench_rank_profile.json``: the ranks this repository's rank method picks for the default
+archive, written by ``--write-rank-profile``), with the same e2e bracket (H2D of its coefficient
+pictures, D2H of a checksum). Multi-GPU runs (torchrun) are data-parallel: every rank restores its own
+session; the value is the aggregate (sum of bytes / max time over ranks).
 """
 
 from __future__ import annotations
@@ -43,11 +46,16 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--chunks", type=int, default=5, help="chunks generated and archived before the timed steps")
+    ap.add_argument("--chunks", type=int, default=12, help="chunks generated and archived before the timed steps")
     ap.add_argument("--history", type=int, default=4, help="chunks restored per step (rewind target)")
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--layers", type=int, default=30)
+    ap.add_argument("--write-rank-profile", action="store_true",
+                    help="write the archive's per-matrix ranks to bench_rank_profile.json")
     return ap.parse_args()
+
+
+RANK_PROFILE = os.path.join(ROOT, "bench_rank_profile.json")
 
 
 class ClockSampler:
@@ -191,6 +199,23 @@ def build_archive(args, device):
             "archive_seconds": archive_seconds, "ranks": ranks, "store_root": root}
 
 
+def write_rank_profile(restorer, target, cfg):
+    """Per-matrix ranks of the restored history: {"K": [[layer ranks] per chunk], "V": ...}."""
+    from reelcache_b200.types import entry_parts
+
+    profile = {"K": [], "V": []}
+    for item in restorer.history(target):
+        ranks = {"K": [0] * cfg.layers, "V": [0] * cfg.layers}
+        for entry, (_, record) in item.tiles.items():
+            key, _ = entry_parts(entry)
+            ranks[key.target][key.layer] = int(record.rank_view)
+        for which in ("K", "V"):
+            profile[which].append(ranks[which])
+    with open(RANK_PROFILE, "w") as handle:
+        json.dump({"source": "rank method on the default bench archive (K 98 % / V 95 % energy)", **profile},
+                  handle)
+
+
 def run_ours(args, rank, world, local):
     import torch
     from reelcache_b200.archive_restore import LineageRestorer
@@ -248,31 +273,56 @@ def run_ours(args, rank, world, local):
     _ext.check_status(device)
     launches_per_step = sum(len(program.blobs[g]) for g in program.blobs) + len(program.aux[0]) + len(program.aux[1])
 
-    # ---- end to end: public API restore from pinned host packs, overlapped with the first denoise step ----
-    sampler = ChunkGenerator(model, cache, state["text_kv"], seed=3)
+    # ---- end to end: public API restore from pinned host packs, then a D2H checksum of the cache ----
     h2d = sum(restorer.prepared_pack(item.packet_ref).nbytes for item in restorer.history(target))
-    latent_bytes = cfg.in_dim * cfg.frames_per_chunk * cfg.latent_height * cfg.latent_width * 4
 
     def e2e_step():
+        result = restorer.restore(target, destination, rope, stream=stream, overlapped=False)
+        result.join()
+        main.wait_stream(stream)
+        probe = torch.stack([cache.k[layer][0, -cfg.chunk_tokens - 1, 0, :4].float() for layer in (0, cfg.layers - 1)]
+                            + [cache.v[layer][0, -cfg.chunk_tokens - 1, 0, :4].float() for layer in (0, cfg.layers - 1)])
+        return probe.to("cpu")
+
+    main = torch.cuda.current_stream(device)
+    d2h = 4 * 4 * 4
+    ms_e2e = timed(e2e_step, max(1, args.steps // 2), max(3, args.warmup), main)
+
+    # ---- TTFC: rewind to the target, resume; restore overlapped with the first denoising step ----
+    sampler = ChunkGenerator(model, cache, state["text_kv"], seed=3)
+
+    def resume_step():
         result = restorer.restore(target, destination, rope, stream=stream, overlapped=True)
         latents = sampler.denoise(args.history, layer_wait=result.wait)
         host = latents.to("cpu", non_blocking=False)
         result.join()
         return host
 
-    main = torch.cuda.current_stream(device)
-    ms_e2e = timed(e2e_step, max(1, args.steps // 2), max(1, args.warmup - 1), main)
-    # TTFC distribution (device clock per step)
+    for _ in range(2):
+        resume_step()
     samples = []
     for _ in range(3):
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(main)
-        e2e_step()
+        resume_step()
         e.record(main)
         torch.cuda.synchronize()
         samples.append(s.elapsed_time(e))
     ttfc_p50 = float(np.median(samples))
+    # the same first denoising step without a restore in front of it (cache already resident)
+    nosamples = []
+    for _ in range(3):
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(main)
+        sampler.denoise(args.history).to("cpu")
+        e.record(main)
+        torch.cuda.synchronize()
+        nosamples.append(s.elapsed_time(e))
+    first_step_ms = float(np.median(nosamples))
+    if args.write_rank_profile and rank == 0:
+        write_rank_profile(restorer, target, cfg)
     ms_device = reduce_max(ms_device, world)
     ms_e2e = reduce_max(ms_e2e, world)
     archived_per_s = args.chunks / max(state["archive_seconds"], 1e-9)
@@ -281,17 +331,41 @@ def run_ours(args, rank, world, local):
     return {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms_device, 4),
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "ms_per_step": round(ms_e2e, 3),
-                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(latent_bytes),
-                "includes": "H2D of the history's coefficient packs + restore overlapped with the first denoise "
-                            "step of the next chunk (3 DiT forwards) + D2H of its latents"},
-        "ttfc_p50_ms": round(ttfc_p50, 2), "archived_chunks_per_s": round(archived_per_s, 4),
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "includes": "LineageRestorer.restore from pinned host coefficient packs (H2D inside) + D2H of a "
+                            "checksum of the restored cache"},
+        "ttfc_p50_ms": round(ttfc_p50, 2), "first_step_without_restore_ms": round(first_step_ms, 2),
+        "archived_chunks_per_s": round(archived_per_s, 4),
         "mean_rank": round(float(np.mean(state["ranks"])), 1), "gpu_launches": launches_per_step,
         "clocks": clock_summary, "restored_bytes_per_step": restored_bytes,
     }
 
 
+def load_rank_profile(layers, chunks):
+    """Per-(chunk, layer) ranks for K and V from bench_rank_profile.json (None when absent or too small)."""
+    try:
+        with open(RANK_PROFILE) as handle:
+            profile = json.load(handle)
+        if len(profile["K"]) < chunks or any(len(row) < layers for row in profile["K"] + profile["V"]):
+            return None
+        return profile
+    except (OSError, ValueError, KeyError, TypeError):
+        return None
+
+
+def wan_freqs(head_dim=128, positions=1024, theta=10000.0):
+    """Complex Wan 3-axis RoPE frequencies [positions, head_dim // 2] (plain torch, benchmark setup)."""
+    import torch
+    dims = (head_dim - 4 * (head_dim // 6), 2 * (head_dim // 6), 2 * (head_dim // 6))
+    grid = torch.arange(positions, dtype=torch.float64)
+    angles = torch.cat([torch.outer(grid, 1.0 / theta ** (torch.arange(0, d, 2, dtype=torch.float64) / d))
+                        for d in dims], dim=1)
+    return torch.polar(torch.ones_like(angles), angles)
+
+
 def run_reference(args, rank, world, local):
-    """The reference's own Triton restore (restore_kernels.reconstruct) on identical picture sources."""
+    """The reference's own Triton restore (restore_kernels.reconstruct) on picture sources of the same
+    geometry and per-matrix ranks."""
     ref_dir = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref_dir, "reelcache")):
         return {"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}
@@ -304,54 +378,87 @@ def run_reference(args, rank, world, local):
         return {"impl": "reference", "unavailable": f"reference import failed: {type(error).__name__}: {error}"}
     device = torch.device("cuda", local)
     layers, chunks, heads, dim = args.layers, args.history, 12, 128
-    frames, height, width, rank_cols = 3, 30, 52, 256
+    frames, height, width = 3, 30, 52
     tokens = frames * height * width
+    profile = load_rank_profile(layers, chunks)
     rng = np.random.default_rng(0)
     cache_k = [torch.zeros((1, chunks * tokens, heads, dim), dtype=torch.bfloat16, device=device) for _ in range(layers)]
     cache_v = [torch.zeros_like(cache_k[0]) for _ in range(layers)]
-    table = rrk.RopeTable.from_complex(torch.polar(torch.ones(1024, 64), torch.rand(1024, 64) * 6.28).to(device))
+    table = rrk.RopeTable.from_complex(wan_freqs(dim).to(device))
     jobs_by_layer = []
     keep = []
+    host_pictures, device_pictures = [], []
+    ranks = []
     for layer in range(layers):
         jobs = []
         for c in range(chunks):
             for which, cache in (("K", cache_k), ("V", cache_v)):
-                values = rng.standard_normal((tokens, rank_cols)).astype(np.float32)
+                rank_cols = profile[which][c][layer] if profile is not None else 64
+                ranks.append(rank_cols)
+                spectrum = (np.arange(1, rank_cols + 1, dtype=np.float32) ** -0.5)
+                values = rng.standard_normal((tokens, rank_cols)).astype(np.float32) * spectrum
                 pixels, affine, norm = rhevc.quantize_coefficients(values, "per_channel")
                 lay = rhevc.video_layout(frames, height, width, rank_cols, "yuv444p")
-                canvases = torch.from_numpy(np.concatenate([rhevc._mosaic(pixels.reshape(frames, height, width, -1), lay, s)
-                                                            for s in range(lay["segments"])])).to(device)
+                host = torch.from_numpy(np.concatenate([rhevc._mosaic(pixels.reshape(frames, height, width, -1), lay, s)
+                                                        for s in range(lay["segments"])])).pin_memory()
+                canvases = host.to(device)
+                host_pictures.append(host)
+                device_pictures.append(canvases)
                 scale, offset = rrk.expand_affine(affine, norm, rank_cols)
                 indices = [[s * frames + f for f in range(frames)] for s in range(lay["segments"])]
                 src = rrk.PictureSource.from_canvases(canvases, lay, indices, (0, 0), scale, offset)
                 basis = (torch.randn(rank_cols, heads * dim, device=device) / 40).half()
-                keep.extend((canvases, basis))
+                keep.append(basis)
                 rope = rrk.RopePositions(table, (3 * c, 0, 0)) if which == "K" else None
                 jobs.append(rrk.ReconstructionJob(src, rrk.NativeView(cache[layer], "BTHD", c * tokens),
                                                   (frames, height, width), basis, rope=rope))
         jobs_by_layer.append(jobs)
     stream = torch.cuda.Stream(device)
+    main_stream = torch.cuda.current_stream(device)
 
     def step():
-        handles = [rrk.reconstruct(jobs, stream=stream) for jobs in jobs_by_layer]
-        return handles
+        return [rrk.reconstruct(jobs, stream=stream) for jobs in jobs_by_layer]
 
-    for _ in range(args.warmup):
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            for host, dev in zip(host_pictures, device_pictures):
+                dev.copy_(host, non_blocking=True)
         step()
-    torch.cuda.synchronize()
-    barrier(world)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        start.record(stream)
-        for _ in range(args.steps):
-            step()
-        stop.record(stream)
+        main_stream.wait_stream(stream)
+        probe = torch.stack([cache_k[layer][0, -1, 0, :4].float() for layer in (0, layers - 1)]
+                            + [cache_v[layer][0, -1, 0, :4].float() for layer in (0, layers - 1)])
+        return probe.to("cpu")
+
+    def timed(fn, steps, warmup, s):
+        for _ in range(warmup):
+            fn()
         torch.cuda.synchronize()
-    ms = reduce_max(start.elapsed_time(stop) / args.steps, world)
+        barrier(world)
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(s)
+        for _ in range(steps):
+            fn()
+        stop.record(s)
+        torch.cuda.synchronize()
+        barrier(world)
+        return start.elapsed_time(stop) / steps
+
+    with ClockSampler(local) as clocks:
+        ms = timed(step, args.steps, args.warmup, stream)
+    ms_e2e = timed(e2e_step, max(1, args.steps // 2), max(3, args.warmup), main_stream)
+    ms = reduce_max(ms, world)
+    ms_e2e = reduce_max(ms_e2e, world)
     restored = 2 * layers * chunks * tokens * heads * dim * 2
+    h2d = sum(t.numel() for t in host_pictures)
     return {"metric": METRIC, "value": round(world * restored / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "ms_per_step": round(ms, 4), "impl": "reference", "clocks": clocks.summary(),
-            "note": "reference Triton restore_kernels.reconstruct (auto backend/precision) on picture sources, rank 256"}
+            "ms_per_step": round(ms, 4),
+            "e2e": {"value": round(world * restored / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 64,
+                    "includes": "H2D of the coefficient pictures from pinned memory + reconstruct + D2H checksum"},
+            "impl": "reference", "clocks": clocks.summary(), "mean_rank": round(float(np.mean(ranks)), 1),
+            "note": "reference Triton restore_kernels.reconstruct (auto backend/precision) on picture sources; ranks "
+                    + ("from bench_rank_profile.json" if profile is not None else "64 (no rank profile)")}
 
 
 def main():

@@ -27,7 +27,7 @@ from .errors import CapacityError, ConfigurationError, IntegrityError, Unsupport
 from .lineage import LineageRuntime
 from .ops.restore import RestoreProgram
 from .overlapped_restore import LayerReadiness, OverlappedRestore, start_overlapped_restore
-from .restore_kernels import RopeTable
+from .restore_kernels import RopePositions, RopeTable, restore_rope_item
 from .types import MatrixKey, entry_parts
 
 
@@ -246,9 +246,8 @@ class LineageRestorer:
                         table, rope_rows = rope(piece)
                         first = piece.offset // (context.height * context.width)
                         rope_rows = (rope_rows[0] + first, rope_rows[1], rope_rows[2])
-                        cos, sin = table.token_tables(rope_rows, grid, self.device, stream)
-                        program.keepalive.extend((cos, sin))
-                        job["rope"] = (cos.data_ptr(), sin.data_ptr(), cos.shape[1])
+                        job["rope"] = restore_rope_item(RopePositions(table, rope_rows), grid, self.device, stream,
+                                                        program.keepalive)
                     program.add(job, group=layer)
         return program
 

@@ -11,14 +11,19 @@
 // Work item = (job, 128-token tile, 256-channel tile); each CTA owns a contiguous range of items.
 // Roles (320 threads, one CTA per SM):
 //   warp 0      TMA producer: per K block the A tile [128 x 64] and the B tile [256 x 64] (hi half,
-//               then the lo half in a second pass); 128-byte swizzle, no multicast; 4 stages of 48 KB.
+//               then the lo half in a second pass); 128-byte swizzle, no multicast; 3 stages of 48 KB.
 //   warp 1      TMEM owner and MMA issuer (4 x tcgen05.mma kind::f16 per K block).
 //   warps 2..9  epilogue: warp w reads TMEM lane quarter (w % 4) and one 128-column half of the tile;
-//               applies scale + bias and interleaved-pair RoPE from per-token FP32 cos/sin tables
-//               [tokens, pairs] (16-byte loads, one 32-column chunk ahead), casts, and writes each
-//               32 x 32 block to a 64-byte-swizzled SMEM buffer that a TMA bulk store (double-buffered
-//               per warp) copies into the native cache slot; layouts whose channels are not contiguous
-//               take per-thread strided stores instead.
+//               applies scale + bias and interleaved-pair RoPE, casts, and writes each 32 x 32 block
+//               to a 64-byte-swizzled SMEM buffer that a TMA bulk store (double-buffered per warp)
+//               copies into the native cache slot; layouts whose channels are not contiguous take
+//               per-thread strided stores instead.
+// RoPE and bias operands live in shared memory per job: the 3-axis (frame, row, column) tables are
+// separable, so a job needs only its T x Pt + H x Ph + W x Pw (cos, sin) entries, not one row per
+// token; the 8 epilogue warps load them cooperatively when the job changes (mbarrier handshake,
+// bounded waits). Lanes of a warp hold consecutive tokens, so the frame and row sections are
+// broadcast reads and the column section is conflict-free. Dense (non-separable) tables fall back to
+// per-token FP32 rows [tokens, pairs] read from global memory.
 // Accumulators are double-buffered in TMEM (2 x 256 columns) so the epilogue of one tile overlaps
 // the main loop of the next. The launch parameters (tensor maps included) are built once on the host
 // (restore_build) and launched any number of times (restore_run).
@@ -38,7 +43,7 @@ constexpr int kMaxJobs = 16;
 constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kEpilogueWarps = 8;
 constexpr int kThreads = (2 + kEpilogueWarps) * 32;
 constexpr int kATileBytes = kBM * kBK * 2;   // 16 KB
@@ -46,21 +51,28 @@ constexpr int kBTileBytes = kBN * kBK * 2;   // 32 KB
 constexpr int kStageBytes = kATileBytes + kBTileBytes;
 constexpr int kOutBufBytes = 32 * 32 * 2;    // one 32 x 32 16-bit output block
 constexpr int kOutBytes = kEpilogueWarps * 2 * kOutBufBytes;
-constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + 1024 + 256;
+constexpr int kRopeEntries = 5120;          // (cos, sin) float2 entries of one job's separable tables
+constexpr int kBiasSmem = 2048;             // channels whose bias is staged in shared memory
+constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + kRopeEntries * 8 + kBiasSmem * 4 + 1024 + 256;
+static_assert(kSmemBytes <= 232448, "shared memory budget of one CTA");
 constexpr int kTmemCols = 512;
 
 enum OutDtype : int { kOutBF16 = 0, kOutF16 = 1, kOutF32 = 2 };
+enum RopeMode : int { kRopeNone = 0, kRopeTokens = 1, kRopePacked = 2 };
 
 struct JobDesc {
   void* dst;                // element (token 0, head 0, dim 0) of the destination slot
   const float* bias;        // [channels]
-  const float* cos;         // per-token RoPE tables [tokens, pairs] fp32 (null: no rotation)
-  const float* sin;
+  const float* cos;         // kRopeTokens: per-token tables [tokens, pairs] fp32;
+  const float* sin;         // kRopePacked: cos = (cos, sin) pairs of the T, H, W sections back to back
   int64_t dst_ts, dst_hs, dst_ds;  // destination element strides (token, head, dim)
   int tokens, kblocks, passes;     // passes: 2 = hi + lo, 1 = hi only
   int a_kblocks, b_kblocks;        // K blocks held by the A / B operands (coordinates wrap)
   int out_dtype, channels, head_dim, n_tiles, work_begin;
   int rope, pairs, tma_store;
+  int sec_t, sec_th;               // kRopePacked: pairs [0, sec_t) frame, [sec_t, sec_th) row, rest column
+  int grid_h, grid_w, off_h, off_w, entries;
+  int bias_smem;                   // bias staged in shared memory (channels <= kBiasSmem)
   float inverse;
 };
 
@@ -101,11 +113,15 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* out_smem = smem + kStages * kStageBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(out_smem + kOutBytes);
+  float2* rope_smem = reinterpret_cast<float2*>(out_smem + kOutBytes);
+  float* bias_smem = reinterpret_cast<float*>(rope_smem + kRopeEntries);
+  uint64_t* full = reinterpret_cast<uint64_t*>(bias_smem + kBiasSmem);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
   uint64_t* acc_empty = acc_full + 2;
-  uint64_t* drained = acc_empty + 2;
+  uint64_t* tab_free = acc_empty + 2;   // every epilogue thread is done with the current job's tables
+  uint64_t* tab_ready = tab_free + 1;   // every epilogue thread has stored its share of the next ones
+  uint64_t* drained = tab_ready + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -124,6 +140,8 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], kEpilogueWarps);
     }
+    mbar_init(tab_free, kEpilogueWarps * 32);
+    mbar_init(tab_ready, kEpilogueWarps * 32);
     mbar_init(drained, 1);
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -220,44 +238,58 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
     // ---------------- Epilogue (8 warps) ----------------
     const int quarter = warp & 3;
     const int col_half = (warp - 2) >> 2;
+    const int et = threadIdx.x - 64;  // 0 .. 255 among the epilogue threads
     uint8_t* my_out = out_smem + (warp - 2) * 2 * kOutBufBytes;
     int local = 0;
     int block = 0;  // output blocks written by this warp (selects the staging buffer)
+    int table_job = -1, table_loads = 0;
     for (int w = work_lo; w < work_hi; ++w, ++local) {
       int j, m_tile, n_tile;
       decode_work(p, w, j, m_tile, n_tile);
       const JobDesc& jb = p.jobs[j];
+      if (j != table_job) {
+        // Job change (the same tile sequence for all 8 warps): wait until every epilogue thread is
+        // done with the previous job's shared tables, store this job's share, publish.
+        bool ok = true;
+        if (table_loads > 0) {
+          mbar_arrive(tab_free);
+          ok = mbar_wait(tab_free, (table_loads - 1) & 1, status, kTimeoutEpilogue);
+        }
+        if (__all_sync(0xffffffffu, ok)) {
+          if (jb.rope == kRopePacked) {
+            const float2* src = reinterpret_cast<const float2*>(jb.cos);
+            for (int i = et; i < jb.entries; i += kEpilogueWarps * 32) rope_smem[i] = __ldg(src + i);
+          }
+          if (jb.bias_smem) {
+            for (int i = et; i < jb.channels; i += kEpilogueWarps * 32) bias_smem[i] = __ldg(jb.bias + i);
+          }
+          mbar_arrive(tab_ready);
+          ok = mbar_wait(tab_ready, table_loads & 1, status, kTimeoutEpilogue);
+        }
+        if (!__all_sync(0xffffffffu, ok)) break;
+        table_job = j;
+        ++table_loads;
+      }
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       const int row0 = m_tile * kBM + quarter * 32;
       const int token = row0 + lane;
       const bool valid = token < jb.tokens;
-      const bool do_rope = jb.rope && valid;
-      const float* cos_row = jb.cos + static_cast<int64_t>(do_rope ? token : 0) * jb.pairs;
-      const float* sin_row = jb.sin + static_cast<int64_t>(do_rope ? token : 0) * jb.pairs;
-      float cs_next[16], sn_next[16];
-      auto load_rope = [&](int chunk) {
-        const int n0 = n_tile * kBN + col_half * (kBN / 2) + chunk * 32;
-        const int pair0 = (n0 % jb.head_dim) >> 1;
-        if (do_rope) {
-          const float4* c4 = reinterpret_cast<const float4*>(cos_row + pair0);
-          const float4* s4 = reinterpret_cast<const float4*>(sin_row + pair0);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float4 c = __ldg(c4 + i);
-            const float4 s = __ldg(s4 + i);
-            cs_next[4 * i] = c.x; cs_next[4 * i + 1] = c.y; cs_next[4 * i + 2] = c.z; cs_next[4 * i + 3] = c.w;
-            sn_next[4 * i] = s.x; sn_next[4 * i + 1] = s.y; sn_next[4 * i + 2] = s.z; sn_next[4 * i + 3] = s.w;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            cs_next[i] = 1.0f;
-            sn_next[i] = 0.0f;
-          }
-        }
-      };
-      if (n_tile * kBN + col_half * (kBN / 2) < jb.channels) load_rope(0);
+      const int tok = valid ? token : 0;
+      // kRopePacked: entry of pair q is base(q) + q with one base per section
+      int base_t = 0, base_h = 0, base_w = 0;
+      if (jb.rope == kRopePacked) {
+        const int hw = jb.grid_h * jb.grid_w;
+        const int f = tok / hw;
+        const int rem = tok - f * hw;
+        const int y = rem / jb.grid_w;
+        const int x = rem - y * jb.grid_w;
+        base_t = f * jb.sec_t;
+        base_h = jb.off_h + y * (jb.sec_th - jb.sec_t) - jb.sec_t;
+        base_w = jb.off_w + x * (jb.pairs - jb.sec_th) - jb.sec_th;
+      }
+      const float* cos_row = jb.cos + static_cast<int64_t>(tok) * jb.pairs;
+      const float* sin_row = jb.sin + static_cast<int64_t>(tok) * jb.pairs;
       bool ok = true;
       if (lane == 0) ok = mbar_wait(&acc_full[buf], acc_phase, status, kTimeoutEpilogue);
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -271,33 +303,62 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
         tmem_ld_32x32b_x32(tmem_base + buf * kBN + col_half * (kBN / 2) + c * 32 +
                                (static_cast<uint32_t>(quarter * 32) << 16),
                            raw);
-        float cs[16], sn[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          cs[i] = cs_next[i];
-          sn[i] = sn_next[i];
-        }
-        if (c + 1 < kBN / 64 && n0 + 32 < jb.channels) load_rope(c + 1);
-        const float4* bias4 = reinterpret_cast<const float4*>(jb.bias + n0);
         float bias[32];
+        if (jb.bias_smem) {
+          const float4* bias4 = reinterpret_cast<const float4*>(bias_smem + n0);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 b = __ldg(bias4 + i);
-          bias[4 * i] = b.x;
-          bias[4 * i + 1] = b.y;
-          bias[4 * i + 2] = b.z;
-          bias[4 * i + 3] = b.w;
+          for (int i = 0; i < 8; ++i) {
+            const float4 b = bias4[i];
+            bias[4 * i] = b.x; bias[4 * i + 1] = b.y; bias[4 * i + 2] = b.z; bias[4 * i + 3] = b.w;
+          }
+        } else {
+          const float4* bias4 = reinterpret_cast<const float4*>(jb.bias + n0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 b = __ldg(bias4 + i);
+            bias[4 * i] = b.x; bias[4 * i + 1] = b.y; bias[4 * i + 2] = b.z; bias[4 * i + 3] = b.w;
+          }
+        }
+        const int pair0 = (n0 % jb.head_dim) >> 1;
+        float cs[16], sn[16];
+        if (jb.rope == kRopePacked) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int q = pair0 + i;
+            const int e = q + (q < jb.sec_t ? base_t : (q < jb.sec_th ? base_h : base_w));
+            const float2 v = rope_smem[e];
+            cs[i] = v.x;
+            sn[i] = v.y;
+          }
+        } else if (jb.rope == kRopeTokens && valid) {
+          const float4* c4 = reinterpret_cast<const float4*>(cos_row + pair0);
+          const float4* s4 = reinterpret_cast<const float4*>(sin_row + pair0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 cv = __ldg(c4 + i);
+            const float4 sv = __ldg(s4 + i);
+            cs[4 * i] = cv.x; cs[4 * i + 1] = cv.y; cs[4 * i + 2] = cv.z; cs[4 * i + 3] = cv.w;
+            sn[4 * i] = sv.x; sn[4 * i + 1] = sv.y; sn[4 * i + 2] = sv.z; sn[4 * i + 3] = sv.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            cs[i] = 1.0f;
+            sn[i] = 0.0f;
+          }
         }
         tmem_wait_ld();
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = fmaf(__uint_as_float(raw[i]), jb.inverse, bias[i]);
+        if (jb.rope != kRopeNone) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float e = v[2 * i];
-          const float o = v[2 * i + 1];
-          v[2 * i] = e * cs[i] - o * sn[i];
-          v[2 * i + 1] = e * sn[i] + o * cs[i];
+          for (int i = 0; i < 16; ++i) {
+            const float e = v[2 * i];
+            const float o = v[2 * i + 1];
+            v[2 * i] = e * cs[i] - o * sn[i];
+            v[2 * i + 1] = e * sn[i] + o * cs[i];
+          }
         }
         if (jb.tma_store) {
           // 32 x 32 16-bit block -> 64-byte-swizzled staging buffer -> TMA bulk store.
@@ -414,6 +475,13 @@ at::Tensor restore_build(const at::Tensor& jobs, const std::vector<at::Tensor>& 
     jb.head_dim = static_cast<int>(r[14]);
     jb.rope = static_cast<int>(r[15]);
     jb.pairs = static_cast<int>(r[17]);
+    jb.sec_t = static_cast<int>(r[18]);
+    jb.sec_th = static_cast<int>(r[18] + r[19]);
+    jb.entries = static_cast<int>(r[20]);
+    jb.grid_h = static_cast<int>(r[10]);
+    jb.grid_w = static_cast<int>(r[11]);
+    jb.off_h = static_cast<int>(r[9] * r[18]);
+    jb.off_w = static_cast<int>(r[9] * r[18] + r[10] * r[19]);
     jb.inverse = inv[i];
     const int64_t k_pad = std::min(a.size(1), b.size(1));
     RC_CHECK(k_pad % 64 == 0 && (a.size(1) == k_pad || a.size(1) == 2 * k_pad) &&
@@ -424,9 +492,20 @@ at::Tensor restore_build(const at::Tensor& jobs, const std::vector<at::Tensor>& 
     RC_CHECK(jb.channels % 32 == 0 && jb.head_dim % 32 == 0 && jb.channels % jb.head_dim == 0,
              "channels and head_dim must be multiples of 32");
     RC_CHECK(reinterpret_cast<uintptr_t>(jb.bias) % 16 == 0, "bias must be 16-byte aligned");
-    RC_CHECK(!jb.rope || (reinterpret_cast<uintptr_t>(jb.cos) % 16 == 0 && reinterpret_cast<uintptr_t>(jb.sin) % 16 == 0 &&
-                          jb.pairs * 2 == jb.head_dim),
+    RC_CHECK(jb.rope >= restore::kRopeNone && jb.rope <= restore::kRopePacked, "unknown RoPE mode");
+    RC_CHECK(jb.rope != restore::kRopeTokens ||
+                 (reinterpret_cast<uintptr_t>(jb.cos) % 16 == 0 && reinterpret_cast<uintptr_t>(jb.sin) % 16 == 0 &&
+                  jb.pairs * 2 == jb.head_dim),
              "RoPE token tables must be 16-byte aligned [tokens, head_dim / 2] float32 rows");
+    if (jb.rope == restore::kRopePacked) {
+      RC_CHECK(jb.pairs * 2 == jb.head_dim && jb.sec_t >= 0 && jb.sec_th >= jb.sec_t && jb.sec_th <= jb.pairs,
+               "RoPE sections must split head_dim / 2 pairs");
+      RC_CHECK(jb.grid_h >= 1 && jb.grid_w >= 1 && r[9] * r[10] * r[11] == jb.tokens, "grid must cover the tokens");
+      RC_CHECK(jb.entries == r[9] * r[18] + r[10] * r[19] + r[11] * (jb.pairs - jb.sec_th) &&
+                   jb.entries <= restore::kRopeEntries && reinterpret_cast<uintptr_t>(jb.cos) % 8 == 0,
+               "packed RoPE tables: T*Pt + H*Ph + W*Pw (cos, sin) entries, at most 5120, 8-byte aligned");
+    }
+    jb.bias_smem = jb.channels <= restore::kBiasSmem;
     jb.kblocks = static_cast<int>(k_pad / restore::kBK);
     jb.a_kblocks = static_cast<int>(a.size(1) / restore::kBK);
     jb.b_kblocks = static_cast<int>(b.size(1) / restore::kBK);

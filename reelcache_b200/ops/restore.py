@@ -118,7 +118,7 @@ class RestoreProgram:
     Each job (``add``) is a dict: ``kind`` ("pictures" | "u8" | "f32"), ``tokens``, ``rank``, ``grid``
     (frames, height, width), ``basis`` (FP16 [R, C]), optional ``basis_t`` (FP16 [C, k_pad]) and
     ``qmax``, ``scale``/``offset`` (host float32 [>= rank]), ``dest`` (address, (ts, hs, ds), dtype,
-    channels, head_dim), ``rope`` (cos address, sin address, pairs) or None, and the source
+    channels, head_dim), ``rope`` (restore_kernels.restore_rope_item) or None, and the source
     (``pictures``: (addresses, plane_stride, row_stride, layout) | ``values``: device tensor).
     """
 
@@ -215,9 +215,12 @@ class RestoreProgram:
             row[0] = address
             row[1] = bias_view.data_ptr()
             rope = job.get("rope")
-            if rope is not None:  # per-token tables [tokens, pairs]: (cos address, sin address, pairs)
-                row[2], row[3] = rope[0], rope[1]
-                row[15], row[17] = 1, rope[2]
+            if rope is not None and rope[0] == "packed":  # separable tables staged in shared memory
+                row[2], row[17], row[18], row[19], row[20] = rope[1], rope[2], rope[3], rope[4], rope[5]
+                row[15] = 2
+            elif rope is not None:  # per-token FP32 rows [tokens, pairs]
+                row[2], row[3], row[17] = rope[1], rope[2], rope[3]
+                row[15] = 1
             row[4], row[5], row[6] = ts, hs, ds
             row[7] = tokens
             row[8] = self.passes

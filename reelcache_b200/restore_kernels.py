@@ -114,6 +114,25 @@ def expand_affine(affine, normalization, rank):
     return scale, offset
 
 
+# (cos, sin) entries of one job's separable tables that the fused epilogue stages in shared memory
+PACKED_ROPE_ENTRIES = 5120
+
+
+def restore_rope_item(positions, grid, device, stream, keepalive):
+    """RoPE description of one fused-restore job: ``("packed", address, pairs, sec_t, sec_h,
+    entries)`` for separable tables that fit in shared memory, else ``("tokens", cos address, sin
+    address, pairs)`` with per-token FP32 rows."""
+    table = positions.table
+    packed = table.packed_tables(positions.rows, grid, device, stream)
+    if packed is not None:
+        pack, (sec_t, sec_h, entries) = packed
+        keepalive.append(pack)
+        return ("packed", pack.data_ptr(), table.pairs, sec_t, sec_h, entries)
+    cos, sin = table.token_tables(positions.rows, grid, device, stream)
+    keepalive.extend((cos, sin))
+    return ("tokens", cos.data_ptr(), sin.data_ptr(), table.pairs)
+
+
 def wan_sections(pairs):
     """Wan / LongCat 3-D split of ``pairs = head_dim // 2`` into (t, h, w) pair counts."""
     _int(pairs, "pairs", minimum=1)
@@ -383,6 +402,43 @@ class RopeTable:
                     del self._device_cache[stale]
             self._device_cache[key] = entry
         return entry[0], entry[1]
+
+    def packed_tables(self, positions_rows, grid, device, stream=None):
+        """Separable tables of one chunk as FP32 ``(cos, sin)`` pairs ``[T*Pt + H*Ph + W*Pw, 2]``:
+        frame section rows ``t_row .. t_row + T``, then the row section, then the column section
+        (cached per positions, grid and device). The fused restore epilogue keeps these in shared
+        memory; ``None`` for dense tables or more than ``PACKED_ROPE_ENTRIES`` entries."""
+        if self.sections is None:
+            return None
+        frames, height, width = grid
+        sec_t, sec_h, sec_w = self.sections
+        entries = frames * sec_t + height * sec_h + width * sec_w
+        if entries > PACKED_ROPE_ENTRIES:
+            return None
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        stamp = self._stamp()
+        key = ("pack", device, tuple(positions_rows), tuple(grid))
+        entry = self._device_cache.get(key)
+        if entry is None or entry[1] != stamp:
+            cos, sin = self.kernel_tables(device, stream)
+            ctx = torch.cuda.stream(stream) if (stream is not None and device.type == "cuda") else _null()
+            with torch.inference_mode(False), torch.no_grad(), ctx:
+                parts, column = [], 0
+                for axis, (count, pairs) in enumerate(zip(grid, self.sections)):
+                    first = positions_rows[axis]
+                    block = torch.stack((cos[first:first + count, column:column + pairs],
+                                         sin[first:first + count, column:column + pairs]), dim=-1)
+                    parts.append(block.reshape(-1, 2))
+                    column += pairs
+                pack = torch.cat(parts).contiguous()
+            entry = (pack, stamp)
+            if len(self._device_cache) > 256:
+                for stale in [k for k in self._device_cache if isinstance(k, tuple) and k and k[0] == "pack"][:128]:
+                    del self._device_cache[stale]
+            self._device_cache[key] = entry
+        return entry[0], (sec_t, sec_h, entries)
 
     def kernel_tables_t(self, device, stream=None):
         """Transposed FP32 ``(cos, sin)`` ``[pairs, rows]`` for the sm_100a kernels: lanes of a warp
@@ -1004,9 +1060,7 @@ def _fused_factor_group(jobs, device, precision, stream, keepalive):
         if job.rope is None:
             item["rope"] = None
         else:
-            cos, sin = job.rope.table.token_tables(job.rope.rows, job.grid, device, stream)
-            keepalive.extend((cos, sin))
-            item["rope"] = (cos.data_ptr(), sin.data_ptr(), cos.shape[1])
+            item["rope"] = restore_rope_item(job.rope, job.grid, device, stream, keepalive)
         if job.basis.dtype != torch.float16:
             with torch.cuda.stream(stream):
                 item["basis"] = job.basis[:job.rank].half().contiguous()

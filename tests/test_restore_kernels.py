@@ -45,3 +45,31 @@ def test_rope_wan_sections():
     table = rk.RopeTable.wan(128, 16)
     assert table.sections == (22, 21, 21)
     assert table.pairs == 64
+
+
+def test_packed_rope_tables_match_token_tables():
+    table = rk.RopeTable.wan(128, 64)
+    grid, rows = (3, 5, 7), (4, 2, 1)
+    pack, (sec_t, sec_h, entries) = table.packed_tables(rows, grid, "cpu")
+    cos, sin = table.token_tables(rows, grid, "cpu")
+    frames, height, width = grid
+    assert entries == frames * sec_t + height * sec_h + width * (table.pairs - sec_t - sec_h) == pack.shape[0]
+    off_h, off_w = frames * sec_t, frames * sec_t + height * sec_h
+    for n in range(frames * height * width):
+        f, rem = divmod(n, height * width)
+        y, x = divmod(rem, width)
+        for q in range(table.pairs):
+            if q < sec_t:
+                e = f * sec_t + q
+            elif q < sec_t + sec_h:
+                e = off_h + y * sec_h + q - sec_t
+            else:
+                e = off_w + x * (table.pairs - sec_t - sec_h) + q - sec_t - sec_h
+            assert pack[e, 0] == cos[n, q] and pack[e, 1] == sin[n, q]
+
+
+def test_packed_rope_tables_fall_back():
+    dense = rk.RopeTable.from_cos_sin(torch.rand(64, 64), torch.rand(64, 64))
+    assert dense.packed_tables(0, (1, 2, 2), "cpu") is None
+    wide = rk.RopeTable.wan(128, 4096)
+    assert wide.packed_tables((0, 0, 0), (1, 2, rk.PACKED_ROPE_ENTRIES), "cpu") is None

@@ -67,6 +67,24 @@ def test_fused_float_and_uint8_coefficients(cuda_device):
     _check(ujob)
 
 
+@pytest.mark.parametrize("kind", ["dense_table", "wide_grid"])
+def test_fused_token_rope_fallback(cuda_device, kind):
+    """Tables the epilogue cannot stage in shared memory take the per-token FP32 row path."""
+    from reelcache_b200.ops import _ext
+
+    if kind == "dense_table":
+        angles = torch.rand(4 * 30 * 52 + 8, 64, dtype=torch.float64) * 6.0
+        table = rk.RopeTable.from_cos_sin(torch.cos(angles).to(cuda_device), torch.sin(angles).to(cuda_device))
+        job, _ = picture_job(cuda_device, rank=96, heads=2, table=table, rope_rows=5, frames=3)
+    else:
+        table = rk.RopeTable.wan(128, 6000, device=cuda_device)
+        job, _ = picture_job(cuda_device, rank=64, heads=2, table=table, frames=1, height=2, width=5400)
+        assert table.packed_tables((0, 0, 0), job.grid, cuda_device) is None
+    rk.reconstruct([job], backend="fused", precision="fp16x2").synchronize()
+    _ext.check_status(cuda_device)
+    _check(job)
+
+
 def test_dense_rope_store(cuda_device):
     from reelcache_b200.ops import _ext
 
