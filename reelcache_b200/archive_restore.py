@@ -91,6 +91,15 @@ class PreparedPack:
 
 
 @dataclass
+class _RestorePlan:
+    program: RestoreProgram
+    device_raw: dict
+    copies: list
+    nbytes: int
+    done: Any = None  # event after the plan's last launch
+
+
+@dataclass
 class HistoryEntry:
     piece: ResolvedPiece
     packet_ref: str
@@ -117,7 +126,8 @@ class LineageRestorer:
     """Restores lineage nodes into caches with the fused sm_100a path."""
 
     def __init__(self, runtime: LineageRuntime, device, *, precision: str = "auto",
-                 prepared_budget_bytes: int = 4 << 30, basis_budget_bytes: int = 4 << 30, pin_memory: bool = True):
+                 prepared_budget_bytes: int = 4 << 30, basis_budget_bytes: int = 4 << 30, pin_memory: bool = True,
+                 plan_budget_bytes: int = 2 << 30):
         self.runtime = runtime
         self.device = torch.device(device)
         self.precision = precision
@@ -128,7 +138,11 @@ class LineageRestorer:
         self._prepared_bytes = 0
         self._lock = threading.Lock()
         self._histories: dict = {}
-        self.stats_ = {"restores": 0, "packs_prepared": 0, "h2d_bytes": 0}
+        self._plans: OrderedDict = OrderedDict()
+        self._plan_bytes = 0
+        self.plan_budget = plan_budget_bytes
+        self._copies = None
+        self.stats_ = {"restores": 0, "packs_prepared": 0, "h2d_bytes": 0, "plans_built": 0, "plan_hits": 0}
 
     # -- preparation ---------------------------------------------------------------------------------------------
 
@@ -191,23 +205,26 @@ class LineageRestorer:
 
     def build_program(self, node_ref: str, destination: Callable[[int, str], torch.Tensor],
                       rope: Callable[[ResolvedPiece], tuple[RopeTable, tuple]], *, stream=None, ranges=None,
-                      stream_label: str | None = None, layers: Sequence[int] | None = None) -> RestoreProgram:
-        """Plan the restore of ``node_ref``: H2D of the history's packs (on ``stream``) and one job per
-        (layer, K/V, piece). ``destination(layer, "K"|"V")`` returns the native BTHD cache tensor
+                      stream_label: str | None = None, layers: Sequence[int] | None = None,
+                      device_raw: dict | None = None) -> RestoreProgram:
+        """Plan the restore of ``node_ref``: one job per (layer, K/V, piece) reading the history's packs
+        from ``device_raw`` (packet ref -> device uint8 copy of the pack; default: copied now on
+        ``stream``). ``destination(layer, "K"|"V")`` returns the native BTHD cache tensor
         ``[1, capacity, heads, head_dim]``; ``rope(piece)`` returns the (table, (t_row, h_row, w_row)) of its positions."""
         stream = stream or torch.cuda.current_stream(self.device)
         entries = self.history(node_ref, ranges)
         model = self.runtime.model
         layers = range(model.layers) if layers is None else layers
-        device_raw = {}
         precision = self.precision
-        with torch.cuda.stream(stream):
-            for item in entries:
-                if item.packet_ref in device_raw:
-                    continue
-                prepared = self.prepared_pack(item.packet_ref)
-                device_raw[item.packet_ref] = prepared.raw.to(self.device, non_blocking=True)
-                self.stats_["h2d_bytes"] += prepared.nbytes
+        if device_raw is None:
+            device_raw = {}
+            with torch.cuda.stream(stream):
+                for item in entries:
+                    if item.packet_ref in device_raw:
+                        continue
+                    prepared = self.prepared_pack(item.packet_ref)
+                    device_raw[item.packet_ref] = prepared.raw.to(self.device, non_blocking=True)
+                    self.stats_["h2d_bytes"] += prepared.nbytes
         program = None
         for layer in layers:
             for target in ("K", "V"):
@@ -251,28 +268,117 @@ class LineageRestorer:
                     program.add(job, group=layer)
         return program
 
+    def _plan_key(self, node_ref, destination, rope, ranges):
+        """Identity of a restore plan: the node, its ranges, every destination tensor (address, shape,
+        strides, dtype) and every piece's RoPE table and positions."""
+        model = self.runtime.model
+        dests = []
+        for layer in range(model.layers):
+            for target in ("K", "V"):
+                t = destination(layer, target)
+                dests.append((t.data_ptr(), tuple(t.shape), t.stride(), t.dtype))
+        ropes = []
+        for item in self.history(node_ref, ranges):
+            table, rows = rope(item.piece)
+            ropes.append((id(table), table._stamp(), tuple(rows)))
+        return (node_ref, None if ranges is None else tuple(map(tuple, ranges)), tuple(dests), tuple(ropes))
+
+    def _layer_copies(self, entries, layer_count):
+        """Per layer, the (packet ref, byte range) covering that layer's tiles in each pack."""
+        copies = []
+        for layer in range(layer_count):
+            spans = {}
+            for item in entries:
+                prepared = self.prepared_pack(item.packet_ref)
+                for target in ("K", "V"):
+                    found = [v for k, v in item.tiles.items() if entry_parts(k)[0] == MatrixKey(layer, target)]
+                    for tile_index, _ in found:
+                        coeff = prepared.tiles[tile_index]["coefficients"]
+                        lo, hi = coeff["offset"], coeff["offset"] + coeff["bytes"]
+                        old = spans.get(item.packet_ref)
+                        spans[item.packet_ref] = (lo, hi) if old is None else (min(old[0], lo), max(old[1], hi))
+            copies.append(sorted(spans.items()))
+        return copies
+
+    def _plan(self, node_ref, destination, rope, stream, ranges):
+        key = self._plan_key(node_ref, destination, rope, ranges)
+        with self._lock:
+            plan = self._plans.get(key)
+            if plan is not None:
+                self._plans.move_to_end(key)
+                self.stats_["plan_hits"] += 1
+                return plan
+        entries = self.history(node_ref, ranges)
+        device_raw = {}
+        for item in entries:
+            if item.packet_ref not in device_raw:
+                prepared = self.prepared_pack(item.packet_ref)
+                device_raw[item.packet_ref] = torch.empty(prepared.nbytes, dtype=torch.uint8, device=self.device)
+        program = self.build_program(node_ref, destination, rope, stream=stream, ranges=ranges, device_raw=device_raw)
+        with torch.cuda.stream(stream):
+            program.prepare(run_aux=False)
+        plan = _RestorePlan(program, device_raw, self._layer_copies(entries, self.runtime.model.layers),
+                            sum(t.numel() for t in device_raw.values()) + program.scratch_bytes)
+        with self._lock:
+            self._plans[key] = plan
+            self._plan_bytes += plan.nbytes
+            self.stats_["plans_built"] += 1
+            while self._plan_bytes > self.plan_budget and len(self._plans) > 1:
+                _, old = self._plans.popitem(last=False)
+                self._plan_bytes -= old.nbytes
+        return plan
+
     def restore(self, node_ref: str, destination, rope, *, stream=None, overlapped: bool = True, ranges=None,
                 readiness: LayerReadiness | None = None, thread: bool = False) -> RestoreResult:
         """Restore ``node_ref``'s history; returns a :class:`RestoreResult` whose readiness marks each layer
-        (the caller's forward waits per layer). All GPU work runs on ``stream`` (default: a side stream)."""
+        (the caller's forward waits per layer). All GPU work runs on ``stream`` (default: a side stream).
+
+        Per layer, the pack bytes of that layer's tiles are copied host->device on a copy stream while
+        the previous layer restores; the layer's unpack, basis preparation and fused GEMM then run on
+        ``stream``. Plans (job tables, tensor maps, device staging of the packs) are built once per
+        (node, destinations, RoPE positions) and relaunched; a relaunch first waits for the previous
+        use of its staging to finish."""
         started = time.perf_counter()
         model = self.runtime.model
         stream = stream or torch.cuda.Stream(self.device)
         readiness = readiness or LayerReadiness(model.layers)
-        program = self.build_program(node_ref, destination, rope, stream=stream, ranges=ranges)
-        with torch.cuda.stream(stream):
-            program.prepare()
+        plan = self._plan(node_ref, destination, rope, stream, ranges)
+        program = plan.program
+        copy_stream = self._copy_stream()
+        if plan.done is not None:
+            copy_stream.wait_event(plan.done)
+        events = []
+        with torch.cuda.stream(copy_stream):
+            for layer in range(model.layers):
+                for packet_ref, (lo, hi) in plan.copies[layer]:
+                    host = self.prepared_pack(packet_ref).raw
+                    plan.device_raw[packet_ref][lo:hi].copy_(host[lo:hi], non_blocking=True)
+                    self.stats_["h2d_bytes"] += hi - lo
+                event = torch.cuda.Event()
+                event.record(copy_stream)
+                events.append(event)
         self.stats_["restores"] += 1
 
         def issue(layer):
-            program.launch(layer, stream)
+            stream.wait_event(events[layer])
+            program.launch(layer, stream, aux=True)
+
+        def finish():
+            done = torch.cuda.Event()
+            done.record(stream)
+            plan.done = done
 
         handle = start_overlapped_restore(issue, model.layers, stream=stream, thread=thread and overlapped,
-                                          readiness=readiness)
+                                          readiness=readiness, finish=finish)
         stats = {"jobs": len(program.jobs), "launches": program.launches, "prepare_seconds": time.perf_counter() - started}
         result = RestoreResult(node_ref, readiness, handle, stats)
         result.program = program
         return result
+
+    def _copy_stream(self):
+        if self._copies is None:
+            self._copies = torch.cuda.Stream(self.device)
+        return self._copies
 
     def stats(self) -> dict[str, Any]:
         return {**self.stats_, "prepared_packs": len(self._prepared), "prepared_bytes": self._prepared_bytes,

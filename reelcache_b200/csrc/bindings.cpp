@@ -11,7 +11,7 @@ void gemm_bf16_tn(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
                   const c10::optional<at::Tensor>& status);
 at::Tensor restore_build(const at::Tensor& jobs, const std::vector<at::Tensor>& a_ops,
                          const std::vector<at::Tensor>& b_ops, const at::Tensor& inverse);
-void restore_run(const at::Tensor& blob, int64_t device, const c10::optional<at::Tensor>& status);
+void restore_run(const at::Tensor& blob, int64_t device, const c10::optional<at::Tensor>& status, int64_t ablate);
 void prep_launch(const at::Tensor& jobs, int64_t device);
 void colminmax(const at::Tensor& p, at::Tensor& lo, at::Tensor& hi, at::Tensor& bad);
 void ln_modulate(const at::Tensor& x, at::Tensor& y, const c10::optional<at::Tensor>& shift,
@@ -35,7 +35,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("restore_build", &rc::restore_build, "launch parameters of a fused restore over <= 16 jobs",
         py::arg("jobs"), py::arg("a_ops"), py::arg("b_ops"), py::arg("inverse"));
   m.def("restore_run", &rc::restore_run, "launch a fused restore from restore_build parameters", py::arg("blob"),
-        py::arg("device"), py::arg("status") = py::none());
+        py::arg("device"), py::arg("status") = py::none(), py::arg("ablate") = 0);
   m.def("colminmax", &rc::colminmax, "per-column extrema of FP32 coefficients", py::arg("p"), py::arg("lo"),
         py::arg("hi"), py::arg("bad"));
   m.def("quantize_columns", &rc::quantize_columns, "FP64 rint quantization of coefficients to uint8",

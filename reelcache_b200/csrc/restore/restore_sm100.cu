@@ -9,21 +9,22 @@
 //
 // One persistent launch covers a group of jobs (one job = one chunk's K or V of one layer).
 // Work item = (job, 128-token tile, 256-channel tile); each CTA owns a contiguous range of items.
-// Roles (320 threads, one CTA per SM):
+// Roles (576 threads, one CTA per SM):
 //   warp 0      TMA producer: per K block the A tile [128 x 64] and the B tile [256 x 64] (hi half,
-//               then the lo half in a second pass); 128-byte swizzle, no multicast; 3 stages of 48 KB.
+//               then the lo half in a second pass); 128-byte swizzle, no multicast; 2 stages of 48 KB.
 //   warp 1      TMEM owner and MMA issuer (4 x tcgen05.mma kind::f16 per K block).
-//   warps 2..9  epilogue: warp w reads TMEM lane quarter (w % 4) and one 128-column half of the tile;
-//               applies scale + bias and interleaved-pair RoPE, casts, and writes each 32 x 32 block
-//               to a 64-byte-swizzled SMEM buffer that a TMA bulk store (double-buffered per warp)
-//               copies into the native cache slot; layouts whose channels are not contiguous take
-//               per-thread strided stores instead.
+//   warps 2..17 epilogue: warp w reads TMEM lane quarter (w % 4) and one 64-column quarter of the
+//               tile with a single 64-column tcgen05.ld (one load latency per tile and warp: the
+//               TMEM read latency, not arithmetic, bounds a short-K tile), applies scale + bias and
+//               interleaved-pair RoPE in place, casts, and writes its 32 x 64 block to a 128-byte-
+//               swizzled SMEM buffer that one TMA bulk store copies into the native cache slot;
+//               layouts whose channels are not contiguous take per-thread strided stores instead.
 // RoPE and bias operands live in shared memory per job: the 3-axis (frame, row, column) tables are
 // separable, so a job needs only its T x Pt + H x Ph + W x Pw (cos, sin) entries, not one row per
 // token; the 8 epilogue warps load them cooperatively when the job changes (mbarrier handshake,
 // bounded waits). Lanes of a warp hold consecutive tokens, so the frame and row sections are
 // broadcast reads and the column section is conflict-free. Dense (non-separable) tables fall back to
-// per-token FP32 rows [tokens, pairs] read from global memory.
+// per-token FP32 rows [tokens, pairs] read from global memory. The per-job tables arrive by bulk copy.
 // Accumulators are double-buffered in TMEM (2 x 256 columns) so the epilogue of one tile overlaps
 // the main loop of the next. The launch parameters (tensor maps included) are built once on the host
 // (restore_build) and launched any number of times (restore_run).
@@ -43,20 +44,20 @@ constexpr int kMaxJobs = 16;
 constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;
-constexpr int kStages = 3;
-constexpr int kEpilogueWarps = 8;
-constexpr int kThreads = (2 + kEpilogueWarps) * 32;
+constexpr int kAStages = 4;                    // A tiles [128 x 64] stream through a 4-deep ring
+constexpr int kBSlots = 2;                     // B tiles [256 x 64]: resident across a run, else a 2-deep ring
+constexpr int kEpilogueWarps = 16;             // 4 TMEM lane quarters x 4 column quarters of 64
+constexpr int kEpiCols = kBN / 4;              // accumulator columns of one epilogue warp
+constexpr int kEpiWarp0 = 2;                   // warp 0: TMA producer, warp 1: MMA issuer
+constexpr int kThreads = (kEpiWarp0 + kEpilogueWarps) * 32;
 constexpr int kATileBytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBTileBytes = kBN * kBK * 2;   // 32 KB
-constexpr int kStageBytes = kATileBytes + kBTileBytes;
-constexpr int kOutBufBytes = 32 * 32 * 2;    // one 32 x 32 16-bit output block
-constexpr int kOutBytes = kEpilogueWarps * 2 * kOutBufBytes;
-constexpr int kRopeEntries = 5120;          // (cos, sin) float2 entries of one job's separable tables
-constexpr int kBiasSmem = 2048;             // channels whose bias is staged in shared memory
-constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + kRopeEntries * 8 + kBiasSmem * 4 + 1024 + 256;
-static_assert(kSmemBytes <= 232448, "shared memory budget of one CTA");
+constexpr int kOutBufBytes = 32 * kEpiCols * 2;  // one 32 x 64 16-bit output block (128-byte rows)
+constexpr int kOutBytes = kEpilogueWarps * kOutBufBytes;
 constexpr int kTmemCols = 512;
-
+constexpr int kRopeEntries = 2944;          // (cos, sin) float2 entries of one job's separable tables
+constexpr int kBiasSmem = 2048;             // channels whose bias is staged in shared memory
+constexpr int kOperandBytes = kAStages * kATileBytes + kBSlots * kBTileBytes;
 enum OutDtype : int { kOutBF16 = 0, kOutF16 = 1, kOutF32 = 2 };
 enum RopeMode : int { kRopeNone = 0, kRopeTokens = 1, kRopePacked = 2 };
 
@@ -67,32 +68,68 @@ struct JobDesc {
   const float* sin;         // kRopePacked: cos = (cos, sin) pairs of the T, H, W sections back to back
   int64_t dst_ts, dst_hs, dst_ds;  // destination element strides (token, head, dim)
   int tokens, kblocks, passes;     // passes: 2 = hi + lo, 1 = hi only
+  int m_tiles;
   int a_kblocks, b_kblocks;        // K blocks held by the A / B operands (coordinates wrap)
   int out_dtype, channels, head_dim, n_tiles, work_begin;
   int rope, pairs, tma_store;
   int sec_t, sec_th;               // kRopePacked: pairs [0, sec_t) frame, [sec_t, sec_th) row, rest column
   int grid_h, grid_w, off_h, off_w, entries;
+  uint32_t hw_magic, w_magic;      // multiply-shift division by grid_h * grid_w and by grid_w
+  int hw_shift, w_shift;
   int bias_smem;                   // bias staged in shared memory (channels <= kBiasSmem)
   float inverse;
 };
 
+static_assert(sizeof(JobDesc) % 8 == 0, "job descriptors are copied as words and keep 8-byte fields aligned");
+constexpr int kSmemBytes = kOperandBytes + kOutBytes + kRopeEntries * 8 + kBiasSmem * 4 +
+                           kMaxJobs * static_cast<int>(sizeof(JobDesc)) + 1024 + 256;
+static_assert(kSmemBytes <= 232448, "shared memory budget of one CTA");
+
 struct Params {
   CUtensorMap a_maps[kMaxJobs];  // A [tokens, k_pad] fp16, box 64 x 128
   CUtensorMap b_maps[kMaxJobs];  // Bt [channels, k_pad or 2 k_pad] fp16, box 64 x 256
-  CUtensorMap o_maps[kMaxJobs];  // destination [tokens, channels] 16-bit, box 32 x 32, 64-byte swizzle
+  CUtensorMap o_maps[kMaxJobs];  // destination [tokens, channels] 16-bit, box 64 x 32, 128-byte swizzle
   JobDesc jobs[kMaxJobs];
   int num_jobs;
   int total_work;
+  int out_dtype;  // shared by every job of the launch (selects the kernel instantiation)
+  int ablate;     // measurement only: 1 drops the stores, 2 also the math, 3 the RoPE table reads,
+                  // 4 the TMEM reads, 5 also the MMAs, 7 also the tcgen05 commits, 8 also the TMA loads
 };
 
-__device__ __forceinline__ void decode_work(const Params& p, int w, int& j, int& m_tile, int& n_tile) {
-  j = 0;
+// Work cursor over (job, n_tile, m_tile) with m fastest: consecutive work items of a CTA share the B
+// tile (job, n_tile), which stays resident. Decoded once per CTA, then advanced without loops or
+// divisions (a per-tile search over the jobs sat on every role's critical path). Job descriptors are
+// read from the CTA's shared-memory copy.
+// n / d for 0 <= n < 2^24 by multiply-shift: magic = ceil(2^shift / d), shift = 24 + ceil(log2 d)
+// (Granlund-Montgomery; exact for n < 2^24). Integer pipes only.
+__device__ __forceinline__ int div_magic(int n, uint32_t magic, int shift) {
+  return static_cast<int>((static_cast<uint64_t>(static_cast<uint32_t>(n)) * magic) >> shift);
+}
+
+struct Cursor {
+  int j, n, m;
+};
+
+__device__ __forceinline__ Cursor cursor_at(const JobDesc* jobs, int num_jobs, int w) {
+  Cursor c{0, 0, 0};
 #pragma unroll 1
-  for (int i = 1; i < p.num_jobs; ++i)
-    if (w >= p.jobs[i].work_begin) j = i;
-  const int local = w - p.jobs[j].work_begin;
-  m_tile = local / p.jobs[j].n_tiles;
-  n_tile = local - m_tile * p.jobs[j].n_tiles;
+  for (int i = 1; i < num_jobs; ++i)
+    if (w >= jobs[i].work_begin) c.j = i;
+  const int local = w - jobs[c.j].work_begin;
+  c.n = local / jobs[c.j].m_tiles;
+  c.m = local - c.n * jobs[c.j].m_tiles;
+  return c;
+}
+
+__device__ __forceinline__ void cursor_next(const JobDesc* jobs, Cursor& c) {
+  if (++c.m == jobs[c.j].m_tiles) {
+    c.m = 0;
+    if (++c.n == jobs[c.j].n_tiles) {
+      c.n = 0;
+      ++c.j;
+    }
+  }
 }
 
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int c0, int c1) {
@@ -109,15 +146,21 @@ __device__ __forceinline__ void bulk_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
+template <int OUT>
 __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_constant__ Params p, int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* out_smem = smem + kStages * kStageBytes;
+  uint8_t* a_ring = smem;
+  uint8_t* b_slots = smem + kAStages * kATileBytes;
+  uint8_t* out_smem = smem + kOperandBytes;
   float2* rope_smem = reinterpret_cast<float2*>(out_smem + kOutBytes);
   float* bias_smem = reinterpret_cast<float*>(rope_smem + kRopeEntries);
-  uint64_t* full = reinterpret_cast<uint64_t*>(bias_smem + kBiasSmem);
-  uint64_t* empty = full + kStages;
-  uint64_t* acc_full = empty + kStages;
+  JobDesc* jobs = reinterpret_cast<JobDesc*>(bias_smem + kBiasSmem);
+  uint64_t* afull = reinterpret_cast<uint64_t*>(jobs + kMaxJobs);
+  uint64_t* aempty = afull + kAStages;
+  uint64_t* bfull = aempty + kAStages;
+  uint64_t* bempty = bfull + kBSlots;
+  uint64_t* acc_full = bempty + kBSlots;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* tab_free = acc_empty + 2;   // every epilogue thread is done with the current job's tables
   uint64_t* tab_ready = tab_free + 1;   // every epilogue thread has stored its share of the next ones
@@ -131,17 +174,28 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
   const int work_lo = static_cast<int>((static_cast<int64_t>(p.total_work) * blockIdx.x) / gridDim.x);
   const int work_hi = static_cast<int>((static_cast<int64_t>(p.total_work) * (blockIdx.x + 1)) / gridDim.x);
 
+  const int num_jobs = p.num_jobs;
+  {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(p.jobs);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(jobs);
+    const int words = num_jobs * static_cast<int>(sizeof(JobDesc) / 4);
+    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+  }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(&afull[s], 1);
+      mbar_init(&aempty[s], 1);
+    }
+    for (int s = 0; s < kBSlots; ++s) {
+      mbar_init(&bfull[s], 1);
+      mbar_init(&bempty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], kEpilogueWarps);
     }
     mbar_init(tab_free, kEpilogueWarps * 32);
-    mbar_init(tab_ready, kEpilogueWarps * 32);
+    mbar_init(tab_ready, 1);
     mbar_init(drained, 1);
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -154,35 +208,69 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
+    // B tiles: a job whose tile needs at most kBSlots distinct B blocks keeps them resident for a
+    // run of consecutive work items with the same (job, n_tile) and loads them once per run; other
+    // jobs stream one B block per step through the slots as a ring. The MMA warp replays the same
+    // decisions, so both sides agree on every slot's load count (the barrier parity).
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
+      int astage = 0;
+      uint32_t aphase = 0;
+      uint32_t bload = 0;  // per-slot load counts, one bit of parity each (slot d: bit d)
+      int bseq = 0;
       bool ok = true;
-      int last_job = -1;
-      for (int w = work_lo; w < work_hi && ok; ++w) {
-        int j, m_tile, n_tile;
-        decode_work(p, w, j, m_tile, n_tile);
-        const JobDesc& jb = p.jobs[j];
+      int last_job = -1, run_job = -1, run_n = -1;
+      Cursor cur = cursor_at(jobs, num_jobs, work_lo);
+      for (int w = work_lo; w < work_hi && ok; ++w, cursor_next(jobs, cur)) {
+        const int j = cur.j, m_tile = cur.m, n_tile = cur.n;
+        const JobDesc& jb = jobs[j];
         if (j != last_job) {
           tma_prefetch_desc(&p.a_maps[j]);
           tma_prefetch_desc(&p.b_maps[j]);
           last_job = j;
         }
         const int steps = jb.kblocks * jb.passes;
-        for (int s = 0; s < steps; ++s) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, status, kTimeoutProducer)) {
-            ok = false;
-            break;
+        const int distinct = steps < jb.b_kblocks ? steps : jb.b_kblocks;
+        const bool resident = distinct <= kBSlots;
+        if (resident && (j != run_job || n_tile != run_n)) {
+          for (int d = 0; d < distinct && ok; ++d) {
+            ok = mbar_wait(&bempty[d], ((bload >> d) & 1u) ^ 1u, status, kTimeoutProducer);
+            if (!ok) break;
+            bload ^= 1u << d;
+            if (p.ablate == 8) {  // measurement: no data movement
+              mbar_arrive(&bfull[d]);
+              continue;
+            }
+            mbar_arrive_expect_tx(&bfull[d], kBTileBytes);
+            tma_load_2d(b_slots + d * kBTileBytes, &p.b_maps[j], &bfull[d], d * kBK, n_tile * kBN);
           }
-          uint8_t* a_dst = smem + stage * kStageBytes;
-          mbar_arrive_expect_tx(&full[stage], kStageBytes);
+        }
+        run_job = j;
+        run_n = n_tile;
+        for (int s = 0; s < steps && ok; ++s) {
+          ok = mbar_wait(&aempty[astage], aphase ^ 1, status, kTimeoutProducer);
+          if (!ok) break;
           // 8-bit sources: A [N, k_pad] is read twice, B [C, 2 k_pad] holds the hi then the lo half.
           // Float sources: A [N, 2 k_pad] holds hi then lo, B [C, k_pad] is read twice.
-          tma_load_2d(a_dst, &p.a_maps[j], &full[stage], (s % jb.a_kblocks) * kBK, m_tile * kBM);
-          tma_load_2d(a_dst + kATileBytes, &p.b_maps[j], &full[stage], (s % jb.b_kblocks) * kBK, n_tile * kBN);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1;
+          if (p.ablate == 8) {
+            mbar_arrive(&afull[astage]);
+          } else {
+            mbar_arrive_expect_tx(&afull[astage], kATileBytes);
+            tma_load_2d(a_ring + astage * kATileBytes, &p.a_maps[j], &afull[astage], (s % jb.a_kblocks) * kBK,
+                        m_tile * kBM);
+          }
+          if (++astage == kAStages) {
+            astage = 0;
+            aphase ^= 1;
+          }
+          if (!resident) {
+            const int slot = bseq & 1;
+            ok = mbar_wait(&bempty[slot], ((bload >> slot) & 1u) ^ 1u, status, kTimeoutProducer);
+            if (!ok) break;
+            bload ^= 1u << slot;
+            ++bseq;
+            mbar_arrive_expect_tx(&bfull[slot], kBTileBytes);
+            tma_load_2d(b_slots + slot * kBTileBytes, &p.b_maps[j], &bfull[slot], (s % jb.b_kblocks) * kBK,
+                        n_tile * kBN);
           }
         }
       }
@@ -190,80 +278,121 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     constexpr uint32_t idesc = make_idesc_f16(kBM, kBN, /*f16*/ 0);
-    int stage = 0;
-    uint32_t phase = 0;
+    int astage = 0;
+    uint32_t aphase = 0;
+    uint32_t bcons = 0;  // per-slot consumption parities (slot d: bit d)
+    int bseq = 0;
     int local = 0;
     bool ok = true;
-    for (int w = work_lo; w < work_hi && ok; ++w, ++local) {
-      int j, m_tile, n_tile;
-      decode_work(p, w, j, m_tile, n_tile);
-      const int steps = p.jobs[j].kblocks * p.jobs[j].passes;
+    int run_job = -1, run_n = -1;
+    Cursor cur = cursor_at(jobs, num_jobs, work_lo);
+    for (int w = work_lo; w < work_hi && ok; ++w, ++local, cursor_next(jobs, cur)) {
+      const int j = cur.j, m_tile = cur.m, n_tile = cur.n;
+      const JobDesc& jb = jobs[j];
+      const int steps = jb.kblocks * jb.passes;
+      const int distinct = steps < jb.b_kblocks ? steps : jb.b_kblocks;
+      const bool resident = distinct <= kBSlots;
+      const bool run_ends = w + 1 == work_hi || m_tile + 1 == jb.m_tiles;
+      const bool run_starts = j != run_job || n_tile != run_n;
+      run_job = j;
+      run_n = n_tile;
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (lane == 0) ok = mbar_wait(&acc_empty[buf], acc_phase ^ 1, status, kTimeoutMma);
+      if (lane == 0 && ok && resident && run_starts) {
+        for (int d = 0; d < distinct && ok; ++d) {
+          ok = mbar_wait(&bfull[d], (bcons >> d) & 1u, status, kTimeoutMma);
+          bcons ^= 1u << d;
+        }
+      }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + buf * kBN;
       for (int s = 0; s < steps; ++s) {
-        if (lane == 0) ok = mbar_wait(&full[stage], phase, status, kTimeoutMma);
+        int slot = resident ? s % jb.b_kblocks : (bseq & 1);
+        if (lane == 0) {
+          ok = mbar_wait(&afull[astage], aphase, status, kTimeoutMma);
+          if (ok && !resident) {
+            ok = mbar_wait(&bfull[slot], (bcons >> slot) & 1u, status, kTimeoutMma);
+            bcons ^= 1u << slot;
+          }
+        }
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t base = smem_u32(smem + stage * kStageBytes);
-          const uint64_t adesc = sw128_kmajor_desc(base);
-          const uint64_t bdesc = sw128_kmajor_desc(base + kATileBytes);
+          const uint64_t adesc = sw128_kmajor_desc(smem_u32(a_ring + astage * kATileBytes));
+          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(b_slots + slot * kBTileBytes));
+          if (p.ablate < 5) {
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)
-            mma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (s > 0 || k > 0) ? 1u : 0u);
-          mma_commit(&empty[stage]);
+            for (int k = 0; k < kBK / 16; ++k)
+              mma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (s > 0 || k > 0) ? 1u : 0u);
+          }
+          if (p.ablate >= 7) {  // measurement: plain arrivals instead of tcgen05.commit
+            mbar_arrive(&aempty[astage]);
+            if (!resident) mbar_arrive(&bempty[slot]);
+          } else {
+            mma_commit(&aempty[astage]);
+            if (!resident) mma_commit(&bempty[slot]);
+          }
         }
         __syncwarp();
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1;
+        if (!resident) ++bseq;
+        if (++astage == kAStages) {
+          astage = 0;
+          aphase ^= 1;
         }
       }
       if (!ok) break;
-      if (lane == 0) mma_commit(&acc_full[buf]);
+      if (lane == 0) {
+        if (p.ablate >= 7) {
+          if (resident && run_ends)
+            for (int d = 0; d < distinct; ++d) mbar_arrive(&bempty[d]);
+          mbar_arrive(&acc_full[buf]);
+        } else {
+          if (resident && run_ends)
+            for (int d = 0; d < distinct; ++d) mma_commit(&bempty[d]);  // the run's last MMAs release its B
+          mma_commit(&acc_full[buf]);
+        }
+      }
       __syncwarp();
     }
-    if (lane == 0) {
+    if (lane == 0) {  // every issued MMA has completed before TMEM is released
       mma_commit(drained);
       (void)mbar_wait(drained, 0, nullptr, 0);
     }
     __syncwarp();
-  } else {
-    // ---------------- Epilogue (8 warps) ----------------
-    const int quarter = warp & 3;
-    const int col_half = (warp - 2) >> 2;
-    const int et = threadIdx.x - 64;  // 0 .. 255 among the epilogue threads
-    uint8_t* my_out = out_smem + (warp - 2) * 2 * kOutBufBytes;
+  } else if (warp >= kEpiWarp0) {
+    // ---------------- Epilogue (16 warps) ----------------
+    const int quarter = warp & 3;       // TMEM lanes 32 * quarter .. + 32 (hardware lane-access rule)
+    const int ew = warp - kEpiWarp0;    // 0 .. 15
+    const int cq = ew >> 2;             // column quarter of the tile
+    const int et = threadIdx.x - kEpiWarp0 * 32;  // 0 .. 511 among the epilogue threads
+    uint8_t* my_out = out_smem + ew * kOutBufBytes;
     int local = 0;
-    int block = 0;  // output blocks written by this warp (selects the staging buffer)
     int table_job = -1, table_loads = 0;
-    for (int w = work_lo; w < work_hi; ++w, ++local) {
-      int j, m_tile, n_tile;
-      decode_work(p, w, j, m_tile, n_tile);
-      const JobDesc& jb = p.jobs[j];
+    bool stored = false;  // this warp has a bulk store in flight from my_out
+    Cursor cur = cursor_at(jobs, num_jobs, work_lo);
+    for (int w = work_lo; w < work_hi; ++w, ++local, cursor_next(jobs, cur)) {
+      const int j = cur.j, m_tile = cur.m, n_tile = cur.n;
+      const JobDesc& jb = jobs[j];
       if (j != table_job) {
-        // Job change (the same tile sequence for all 8 warps): wait until every epilogue thread is
-        // done with the previous job's shared tables, store this job's share, publish.
+        // Job change (the same tile sequence for every epilogue warp): wait until every epilogue
+        // thread is done with the previous job's shared tables, store this job's share, publish.
         bool ok = true;
         if (table_loads > 0) {
           mbar_arrive(tab_free);
           ok = mbar_wait(tab_free, (table_loads - 1) & 1, status, kTimeoutEpilogue);
         }
         if (__all_sync(0xffffffffu, ok)) {
-          if (jb.rope == kRopePacked) {
-            const float2* src = reinterpret_cast<const float2*>(jb.cos);
-            for (int i = et; i < jb.entries; i += kEpilogueWarps * 32) rope_smem[i] = __ldg(src + i);
+          if (et == 0) {  // one bulk copy per table, completion counted in bytes on tab_ready
+            const uint32_t rope_bytes = jb.rope == kRopePacked ? static_cast<uint32_t>((jb.entries + 1) & ~1) * 8u : 0u;
+            const uint32_t bias_bytes = jb.bias_smem ? static_cast<uint32_t>(jb.channels) * 4u : 0u;
+            mbar_arrive_expect_tx(tab_ready, rope_bytes + bias_bytes);
+            if (rope_bytes) bulk_load_g2s(rope_smem, jb.cos, rope_bytes, tab_ready);
+            if (bias_bytes) bulk_load_g2s(bias_smem, jb.bias, bias_bytes, tab_ready);
           }
-          if (jb.bias_smem) {
-            for (int i = et; i < jb.channels; i += kEpilogueWarps * 32) bias_smem[i] = __ldg(jb.bias + i);
-          }
-          mbar_arrive(tab_ready);
           ok = mbar_wait(tab_ready, table_loads & 1, status, kTimeoutEpilogue);
         }
         if (!__all_sync(0xffffffffu, ok)) break;
@@ -276,141 +405,161 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
       const int token = row0 + lane;
       const bool valid = token < jb.tokens;
       const int tok = valid ? token : 0;
-      // kRopePacked: entry of pair q is base(q) + q with one base per section
-      int base_t = 0, base_h = 0, base_w = 0;
-      if (jb.rope == kRopePacked) {
-        const int hw = jb.grid_h * jb.grid_w;
-        const int f = tok / hw;
-        const int rem = tok - f * hw;
-        const int y = rem / jb.grid_w;
-        const int x = rem - y * jb.grid_w;
-        base_t = f * jb.sec_t;
-        base_h = jb.off_h + y * (jb.sec_th - jb.sec_t) - jb.sec_t;
-        base_w = jb.off_w + x * (jb.pairs - jb.sec_th) - jb.sec_th;
-      }
-      const float* cos_row = jb.cos + static_cast<int64_t>(tok) * jb.pairs;
-      const float* sin_row = jb.sin + static_cast<int64_t>(tok) * jb.pairs;
+      const int nq = n_tile * kBN + cq * kEpiCols;  // first channel of this warp's block
       bool ok = true;
       if (lane == 0) ok = mbar_wait(&acc_full[buf], acc_phase, status, kTimeoutEpilogue);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < kBN / 64; ++c) {
-        const int n0 = n_tile * kBN + col_half * (kBN / 2) + c * 32;
-        if (n0 >= jb.channels) break;  // uniform: channels is a multiple of 32 (checked on the host)
-        uint32_t raw[32];
-        tmem_ld_32x32b_x32(tmem_base + buf * kBN + col_half * (kBN / 2) + c * 32 +
-                               (static_cast<uint32_t>(quarter * 32) << 16),
-                           raw);
-        float bias[32];
-        if (jb.bias_smem) {
-          const float4* bias4 = reinterpret_cast<const float4*>(bias_smem + n0);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 b = bias4[i];
-            bias[4 * i] = b.x; bias[4 * i + 1] = b.y; bias[4 * i + 2] = b.z; bias[4 * i + 3] = b.w;
-          }
-        } else {
-          const float4* bias4 = reinterpret_cast<const float4*>(jb.bias + n0);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 b = __ldg(bias4 + i);
-            bias[4 * i] = b.x; bias[4 * i + 1] = b.y; bias[4 * i + 2] = b.z; bias[4 * i + 3] = b.w;
-          }
+      if (nq < jb.channels && p.ablate < 4) {
+        uint32_t r[64];
+        tmem_ld_32x32b_x64(tmem_base + buf * kBN + cq * kEpiCols + (static_cast<uint32_t>(quarter * 32) << 16), r);
+        // RoPE operands: entry of pair q is base(q) + q with one base per section (kRopePacked)
+        const int rope = jb.rope;
+        const int sec_t = jb.sec_t, sec_th = jb.sec_th;
+        int base_t = 0, base_h = 0, base_w = 0;
+        if (rope == kRopePacked) {
+          const int grid_w = jb.grid_w;
+          const int hw = jb.grid_h * grid_w;
+          const int f = div_magic(tok, jb.hw_magic, jb.hw_shift);
+          const int rem = tok - f * hw;
+          const int y = div_magic(rem, jb.w_magic, jb.w_shift);
+          const int x = rem - y * grid_w;
+          base_t = f * sec_t;
+          base_h = jb.off_h + y * (sec_th - sec_t) - sec_t;
+          base_w = jb.off_w + x * (jb.pairs - sec_th) - sec_th;
         }
-        const int pair0 = (n0 % jb.head_dim) >> 1;
-        float cs[16], sn[16];
-        if (jb.rope == kRopePacked) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int q = pair0 + i;
-            const int e = q + (q < jb.sec_t ? base_t : (q < jb.sec_th ? base_h : base_w));
-            const float2 v = rope_smem[e];
-            cs[i] = v.x;
-            sn[i] = v.y;
-          }
-        } else if (jb.rope == kRopeTokens && valid) {
-          const float4* c4 = reinterpret_cast<const float4*>(cos_row + pair0);
-          const float4* s4 = reinterpret_cast<const float4*>(sin_row + pair0);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float4 cv = __ldg(c4 + i);
-            const float4 sv = __ldg(s4 + i);
-            cs[4 * i] = cv.x; cs[4 * i + 1] = cv.y; cs[4 * i + 2] = cv.z; cs[4 * i + 3] = cv.w;
-            sn[4 * i] = sv.x; sn[4 * i + 1] = sv.y; sn[4 * i + 2] = sv.z; sn[4 * i + 3] = sv.w;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            cs[i] = 1.0f;
-            sn[i] = 0.0f;
-          }
-        }
+        const float2* tab_t = rope_smem + base_t;
+        const float2* tab_h = rope_smem + base_h;
+        const float2* tab_w = rope_smem + base_w;
+        const bool bias_in_smem = jb.bias_smem != 0;
+        const float2* bias2 = bias_in_smem ? reinterpret_cast<const float2*>(bias_smem + nq)
+                                           : reinterpret_cast<const float2*>(jb.bias + nq);
+        const float inv = jb.inverse;
+        const int head_dim = jb.head_dim;
         tmem_wait_ld();
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = fmaf(__uint_as_float(raw[i]), jb.inverse, bias[i]);
-        if (jb.rope != kRopeNone) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float e = v[2 * i];
-            const float o = v[2 * i + 1];
-            v[2 * i] = e * cs[i] - o * sn[i];
-            v[2 * i + 1] = e * sn[i] + o * cs[i];
-          }
-        }
-        if (jb.tma_store) {
-          // 32 x 32 16-bit block -> 64-byte-swizzled staging buffer -> TMA bulk store.
-          uint8_t* ob = my_out + (block & 1) * kOutBufBytes;
-          if (lane == 0) bulk_wait_read<1>();  // the store that used this buffer two blocks ago has read it
-          __syncwarp();
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pk[i] = jb.out_dtype == kOutBF16 ? pack_bf16x2(v[2 * i], v[2 * i + 1]) : pack_f16x2(v[2 * i], v[2 * i + 1]);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t phys = static_cast<uint32_t>(q) ^ ((static_cast<uint32_t>(lane) >> 1) & 3u);
-            *reinterpret_cast<uint4*>(ob + lane * 64 + phys * 16) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && row0 < jb.tokens) {
-            tma_store_2d(&p.o_maps[j], ob, n0, row0);
-            bulk_commit();
-          }
-          ++block;
-          continue;
-        }
-        if (!valid) continue;
-        const int head = n0 / jb.head_dim;
-        const int d0 = n0 - head * jb.head_dim;
-        const int64_t base = static_cast<int64_t>(token) * jb.dst_ts + static_cast<int64_t>(head) * jb.dst_hs +
-                             static_cast<int64_t>(d0) * jb.dst_ds;
-        if (jb.out_dtype == kOutF32) {
-          float* out = reinterpret_cast<float*>(jb.dst) + base;
-          if (jb.dst_ds == 1 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(out + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-          } else {
-            for (int i = 0; i < 32; ++i) out[static_cast<int64_t>(i) * jb.dst_ds] = v[i];
-          }
+        if (p.ablate == 2) {
+          if (__uint_as_float(r[0] ^ r[63]) == 1.2345e-30f && lane == 40) *reinterpret_cast<uint32_t*>(jb.dst) = r[0];
         } else {
-          uint16_t* out = reinterpret_cast<uint16_t*>(jb.dst) + base;
-          uint32_t pk[16];
+          // pair i (columns 2i, 2i+1) -> packed 16-bit pair written back into r[i] (r[i] is read by
+          // pair i / 2 <= i, so the in-place order is safe).
+          auto finish = [&](int i, float c, float sn) {
+            const float2 b = bias_in_smem ? bias2[i] : __ldg(bias2 + i);
+            const float e = fmaf(__uint_as_float(r[2 * i]), inv, b.x);
+            const float o = fmaf(__uint_as_float(r[2 * i + 1]), inv, b.y);
+            const float re = e * c - o * sn;
+            const float ro = e * sn + o * c;
+            if constexpr (OUT == kOutF32) {
+              r[2 * i] = __float_as_uint(re);
+              r[2 * i + 1] = __float_as_uint(ro);
+            } else {
+              r[i] = OUT == kOutBF16 ? pack_bf16x2(re, ro) : pack_f16x2(re, ro);
+            }
+          };
+          const bool wan128 = rope == kRopePacked && head_dim == 128 && sec_t == 22 && sec_th == 43;
+          if (wan128 && (nq & 127) == 0) {  // pairs 0..31: frame section below 22, then row section
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pk[i] = jb.out_dtype == kOutBF16 ? pack_bf16x2(v[2 * i], v[2 * i + 1]) : pack_f16x2(v[2 * i], v[2 * i + 1]);
-          if (jb.dst_ds == 1 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+            for (int i = 0; i < 32; ++i) {
+              const float2 v = i < 22 ? tab_t[i] : tab_h[i];
+              finish(i, v.x, v.y);
+            }
+          } else if (wan128) {  // pairs 32..63: row section below 43, then column section
 #pragma unroll
-            for (int i = 0; i < 16; i += 4)
-              *reinterpret_cast<uint4*>(out + 2 * i) = make_uint4(pk[i], pk[i + 1], pk[i + 2], pk[i + 3]);
+            for (int i = 0; i < 32; ++i) {
+              const float2 v = 32 + i < 43 ? tab_h[32 + i] : tab_w[32 + i];
+              finish(i, v.x, v.y);
+            }
+          } else if (rope == kRopePacked) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int pair0 = ((nq + 32 * h) % head_dim) >> 1;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int q = pair0 + i;
+                const float2 v = q < sec_t ? tab_t[q] : (q < sec_th ? tab_h[q] : tab_w[q]);
+                finish(16 * h + i, v.x, v.y);
+              }
+            }
+          } else if (rope == kRopeTokens) {
+            const float* cos_row = jb.cos + static_cast<int64_t>(tok) * jb.pairs;
+            const float* sin_row = jb.sin + static_cast<int64_t>(tok) * jb.pairs;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int pair0 = ((nq + 32 * h) % jb.head_dim) >> 1;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) finish(16 * h + i, __ldg(cos_row + pair0 + i), __ldg(sin_row + pair0 + i));
+            }
           } else {
-            for (int i = 0; i < 16; ++i) {
-              out[static_cast<int64_t>(2 * i) * jb.dst_ds] = static_cast<uint16_t>(pk[i] & 0xffffu);
-              out[static_cast<int64_t>(2 * i + 1) * jb.dst_ds] = static_cast<uint16_t>(pk[i] >> 16);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) finish(i, 1.0f, 0.0f);
+          }
+          if constexpr (OUT != kOutF32) {
+            if (p.ablate == 1) {
+              uint32_t x = 0;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) x ^= r[i];
+              if (x == 0x9e3779b9u && lane == 40) *reinterpret_cast<uint32_t*>(jb.dst) = x;
+            } else if (jb.tma_store) {
+              // 32 x 64 16-bit block -> 128-byte-swizzled staging buffer -> one TMA bulk store.
+              if (stored) {
+                if (lane == 0) bulk_wait_read<0>();  // this warp's previous store has read the buffer
+                __syncwarp();
+              }
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const uint32_t phys = static_cast<uint32_t>(q) ^ (static_cast<uint32_t>(lane) & 7u);
+                *reinterpret_cast<uint4*>(my_out + lane * 128 + phys * 16) =
+                    make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+              }
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0 && row0 < jb.tokens) {
+                tma_store_2d(&p.o_maps[j], my_out, nq, row0);
+                bulk_commit();
+              }
+              stored = true;
+            } else if (valid) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int n0 = nq + 32 * h;
+                if (n0 >= jb.channels) break;
+                const int head = n0 / jb.head_dim;
+                const int d0 = n0 - head * jb.head_dim;
+                uint16_t* out = reinterpret_cast<uint16_t*>(jb.dst) + static_cast<int64_t>(token) * jb.dst_ts +
+                                static_cast<int64_t>(head) * jb.dst_hs + static_cast<int64_t>(d0) * jb.dst_ds;
+                if (jb.dst_ds == 1 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+#pragma unroll
+                  for (int i = 0; i < 16; i += 4)
+                    *reinterpret_cast<uint4*>(out + 2 * i) =
+                        make_uint4(r[16 * h + i], r[16 * h + i + 1], r[16 * h + i + 2], r[16 * h + i + 3]);
+                } else {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) {
+                    out[static_cast<int64_t>(2 * i) * jb.dst_ds] = static_cast<uint16_t>(r[16 * h + i] & 0xffffu);
+                    out[static_cast<int64_t>(2 * i + 1) * jb.dst_ds] = static_cast<uint16_t>(r[16 * h + i] >> 16);
+                  }
+                }
+              }
+            }
+          } else if (valid) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int n0 = nq + 32 * h;
+              if (n0 >= jb.channels) break;
+              const int head = n0 / jb.head_dim;
+              const int d0 = n0 - head * jb.head_dim;
+              float* out = reinterpret_cast<float*>(jb.dst) + static_cast<int64_t>(token) * jb.dst_ts +
+                           static_cast<int64_t>(head) * jb.dst_hs + static_cast<int64_t>(d0) * jb.dst_ds;
+              if (jb.dst_ds == 1 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                  *reinterpret_cast<float4*>(out + i) =
+                      make_float4(__uint_as_float(r[32 * h + i]), __uint_as_float(r[32 * h + i + 1]),
+                                  __uint_as_float(r[32 * h + i + 2]), __uint_as_float(r[32 * h + i + 3]));
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) out[static_cast<int64_t>(i) * jb.dst_ds] = __uint_as_float(r[32 * h + i]);
+              }
             }
           }
         }
@@ -428,6 +577,14 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+// Host side of div_magic: shift = 24 + ceil(log2 d), magic = ceil(2^shift / d) (< 2^25).
+inline void magic_for(int d, uint32_t& magic, int& shift) {
+  int log2d = 0;
+  while ((1ll << log2d) < d) ++log2d;
+  shift = 24 + log2d;
+  magic = static_cast<uint32_t>(((1ull << shift) + static_cast<uint64_t>(d) - 1) / static_cast<uint64_t>(d));
 }
 
 }  // namespace restore
@@ -483,6 +640,11 @@ at::Tensor restore_build(const at::Tensor& jobs, const std::vector<at::Tensor>& 
     jb.off_h = static_cast<int>(r[9] * r[18]);
     jb.off_w = static_cast<int>(r[9] * r[18] + r[10] * r[19]);
     jb.inverse = inv[i];
+    if (jb.rope == restore::kRopePacked) {
+      RC_CHECK(jb.tokens < (1 << 24), "packed RoPE jobs hold fewer than 2^24 tokens");
+      restore::magic_for(jb.grid_h * jb.grid_w, jb.hw_magic, jb.hw_shift);
+      restore::magic_for(jb.grid_w, jb.w_magic, jb.w_shift);
+    }
     const int64_t k_pad = std::min(a.size(1), b.size(1));
     RC_CHECK(k_pad % 64 == 0 && (a.size(1) == k_pad || a.size(1) == 2 * k_pad) &&
                  (b.size(1) == k_pad || b.size(1) == 2 * k_pad),
@@ -502,8 +664,9 @@ at::Tensor restore_build(const at::Tensor& jobs, const std::vector<at::Tensor>& 
                "RoPE sections must split head_dim / 2 pairs");
       RC_CHECK(jb.grid_h >= 1 && jb.grid_w >= 1 && r[9] * r[10] * r[11] == jb.tokens, "grid must cover the tokens");
       RC_CHECK(jb.entries == r[9] * r[18] + r[10] * r[19] + r[11] * (jb.pairs - jb.sec_th) &&
-                   jb.entries <= restore::kRopeEntries && reinterpret_cast<uintptr_t>(jb.cos) % 8 == 0,
-               "packed RoPE tables: T*Pt + H*Ph + W*Pw (cos, sin) entries, at most 5120, 8-byte aligned");
+                   jb.entries <= restore::kRopeEntries && reinterpret_cast<uintptr_t>(jb.cos) % 16 == 0,
+               "packed RoPE tables: T*Pt + H*Ph + W*Pw (cos, sin) entries (storage padded to an even count), "
+               "at most 2944, 16-byte aligned");
     }
     jb.bias_smem = jb.channels <= restore::kBiasSmem;
     jb.kblocks = static_cast<int>(k_pad / restore::kBK);
@@ -511,8 +674,9 @@ at::Tensor restore_build(const at::Tensor& jobs, const std::vector<at::Tensor>& 
     jb.b_kblocks = static_cast<int>(b.size(1) / restore::kBK);
     RC_CHECK(jb.passes == 1 || (jb.a_kblocks + jb.b_kblocks == 3 * jb.kblocks), "two passes need one doubled operand");
     jb.n_tiles = (jb.channels + restore::kBN - 1) / restore::kBN;
+    jb.m_tiles = (jb.tokens + restore::kBM - 1) / restore::kBM;
     jb.work_begin = work;
-    work += ((jb.tokens + restore::kBM - 1) / restore::kBM) * jb.n_tiles;
+    work += jb.m_tiles * jb.n_tiles;
     p.a_maps[i] = make_tmap_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.size(1), a.size(0), a.stride(0) * 2,
                                restore::kBK, restore::kBM, CU_TENSOR_MAP_SWIZZLE_128B);
     p.b_maps[i] = make_tmap_2d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b.size(1), b.size(0), b.stride(0) * 2,
@@ -523,29 +687,53 @@ at::Tensor restore_build(const at::Tensor& jobs, const std::vector<at::Tensor>& 
     if (jb.tma_store)
       p.o_maps[i] = make_tmap_2d(jb.dst, jb.out_dtype == restore::kOutBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                                 2, jb.channels, jb.tokens, jb.dst_ts * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+                                 2, jb.channels, jb.tokens, jb.dst_ts * 2, restore::kEpiCols, 32,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
   }
   p.num_jobs = n;
   p.total_work = work;
+  p.out_dtype = p.jobs[0].out_dtype;
+  for (int i = 1; i < n; ++i) RC_CHECK(p.jobs[i].out_dtype == p.out_dtype, "jobs of one launch share the output dtype");
   return blob;
 }
 
-void restore_run(const at::Tensor& blob, int64_t device, const c10::optional<at::Tensor>& status) {
+void restore_run(const at::Tensor& blob, int64_t device, const c10::optional<at::Tensor>& status, int64_t ablate) {
   RC_CHECK(blob.device().is_cpu() && blob.scalar_type() == at::kByte &&
                blob.numel() == static_cast<int64_t>(sizeof(restore::Params)),
            "restore_run takes the byte tensor returned by restore_build");
-  const restore::Params& p = *reinterpret_cast<const restore::Params*>(blob.data_ptr<uint8_t>());
+  const restore::Params& stored = *reinterpret_cast<const restore::Params*>(blob.data_ptr<uint8_t>());
+  const restore::Params* params = &stored;
+  restore::Params variant;
+  if (ablate != 0) {  // measurement variants (see Params::ablate)
+    variant = stored;
+    variant.ablate = static_cast<int>(ablate);
+    params = &variant;
+  }
+  const restore::Params& p = *params;
   const int dev = static_cast<int>(device);
   c10::cuda::CUDAGuard guard(dev);
   static bool configured[64] = {false};
   if (!configured[dev]) {
-    RC_CUDA(cudaFuncSetAttribute(restore::restore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 restore::kSmemBytes));
+    RC_CUDA(cudaFuncSetAttribute(restore::restore_kernel<restore::kOutBF16>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, restore::kSmemBytes));
+    RC_CUDA(cudaFuncSetAttribute(restore::restore_kernel<restore::kOutF16>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, restore::kSmemBytes));
+    RC_CUDA(cudaFuncSetAttribute(restore::restore_kernel<restore::kOutF32>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, restore::kSmemBytes));
     configured[dev] = true;
   }
   const int grid = std::min(p.total_work, sm_count(dev));
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
-  restore::restore_kernel<<<grid, restore::kThreads, restore::kSmemBytes, stream>>>(p, status_ptr(status));
+  switch (p.out_dtype) {
+    case restore::kOutBF16:
+      restore::restore_kernel<restore::kOutBF16><<<grid, restore::kThreads, restore::kSmemBytes, stream>>>(p, status_ptr(status));
+      break;
+    case restore::kOutF16:
+      restore::restore_kernel<restore::kOutF16><<<grid, restore::kThreads, restore::kSmemBytes, stream>>>(p, status_ptr(status));
+      break;
+    default:
+      restore::restore_kernel<restore::kOutF32><<<grid, restore::kThreads, restore::kSmemBytes, stream>>>(p, status_ptr(status));
+  }
   RC_CUDA(cudaGetLastError());
 }
 

@@ -18,6 +18,7 @@ from dataclasses import dataclass, field
 from typing import Any, Callable, Generic, TypeVar
 
 from .errors import CapacityError, ConfigurationError, StateError
+from .telemetry import current_telemetry
 
 T = TypeVar("T")
 
@@ -41,6 +42,7 @@ class _JobState:
     status: str = "queued"
     error: str | None = None
     observed: bool = False
+    telemetry: Any = None
 
     def summary(self) -> dict:
         queued = (self.started if self.started is not None else (self.finished or time.monotonic())) - self.submitted
@@ -135,7 +137,8 @@ class BoundedExecutor:
                     raise CapacityError("timed out waiting for executor admission")
                 self._cv.wait(left)
             state = _JobState(self._next, label or getattr(function, "__name__", type(function).__name__),
-                              staging_bytes, time.monotonic(), function, args, kwargs)
+                              staging_bytes, time.monotonic(), function, args, kwargs,
+                              telemetry=current_telemetry())
             self._next += 1
             self._pending[state.job_id] = state
             self._staging += staging_bytes
@@ -158,7 +161,10 @@ class BoundedExecutor:
             state.status = "running"
             function, args, kwargs = state.function, state.args, state.kwargs
             state.function, state.args, state.kwargs = None, (), {}
-        return function(*args, **kwargs)
+        if state.telemetry is None:
+            return function(*args, **kwargs)
+        with state.telemetry.capture():  # the submitter's collector follows the job into the worker
+            return function(*args, **kwargs)
 
     def _finish(self, state: _JobState, future: Future) -> None:
         with self._cv:

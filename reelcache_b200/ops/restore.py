@@ -131,6 +131,7 @@ class RestoreProgram:
         self.keepalive: list = []
         self.prepared = False
         self.launches = 0
+        self.scratch_bytes = 0
 
     def add(self, job: dict, group=0) -> None:
         if self.prepared:
@@ -138,8 +139,10 @@ class RestoreProgram:
         self.groups.setdefault(group, []).append(len(self.jobs))
         self.jobs.append(job)
 
-    def prepare(self) -> "RestoreProgram":
-        """Allocate scratch, run unpack + prep for every job (batched), build every restore table."""
+    def prepare(self, run_aux: bool = True) -> "RestoreProgram":
+        """Allocate scratch, build every unpack / prep / restore table and (``run_aux``) run unpack + prep
+        for every job in batched launches; otherwise each group's preparation runs with its launch
+        (``launch(group, aux=True)``)."""
         stream, device = self.stream, self.device
         plan = []
         cursor = 0
@@ -158,8 +161,10 @@ class RestoreProgram:
         with torch.cuda.stream(stream):
             scratch = torch.empty(max(cursor, 256), dtype=torch.uint8, device=device)
         self.keepalive.append(scratch)
+        self.scratch_bytes = scratch.numel()
         arena = HostArena()
         unpack_rows, prep_rows = [], []
+        unpack_owner, prep_owner = [], []  # job index of every row
         self.a_ops, self.b_ops, self.inverse, self.rows = [], [], [], []
         for job, (k_pad, (a_off, b_off, bias_off)) in zip(self.jobs, plan):
             rank, tokens, channels = job["rank"], job["tokens"], job["dest"][3]
@@ -196,17 +201,20 @@ class RestoreProgram:
                 if job["kind"] == "pictures":
                     addresses, plane_stride, row_stride, layout = job["pictures"]
                     col_off, col_seg = column_tables(layout, plane_stride, row_stride, k_pad)
+                    unpack_owner.append(len(self.rows))
                     unpack_rows.append([arena.add(addresses), arena.add(col_off), arena.add(col_seg), 0,
                                         a.data_ptr(), row_stride, tokens, k_pad, rank, frames, height, width])
                 else:
                     values = job["values"]
                     self.keepalive.append(values)
+                    unpack_owner.append(len(self.rows))
                     unpack_rows.append([-1, -1, -1, values.data_ptr(), a.data_ptr(), values.stride(0), tokens,
                                         k_pad, rank, frames, height, width])
                 basis = job["basis"]
                 scale_off = arena.add(np.ascontiguousarray(job["scale"][:rank], dtype=np.float32))
                 offset_off = arena.add(np.ascontiguousarray(job["offset"][:rank], dtype=np.float32))
                 bits = struct.unpack("<I", struct.pack("<f", float(2.0 ** e)))[0]
+                prep_owner.append(len(self.rows))
                 prep_rows.append([basis.data_ptr(), scale_off, offset_off, b.data_ptr(), bias_view.data_ptr(),
                                   basis.stride(0), rank, k_pad, channels, bits])
                 self.keepalive.append(basis)
@@ -242,17 +250,28 @@ class RestoreProgram:
             for row in prep_rows:
                 row[1] += base
                 row[2] += base
-        self.aux = ([torch.tensor(unpack_rows[i:i + MAX_AUX_JOBS], dtype=torch.int64)
-                     for i in range(0, len(unpack_rows), MAX_AUX_JOBS)],
-                    [torch.tensor(prep_rows[i:i + MAX_AUX_JOBS], dtype=torch.int64)
-                     for i in range(0, len(prep_rows), MAX_AUX_JOBS)])
-        self.run_aux(stream)
+        self.aux = _aux_tables(unpack_rows, prep_rows)
+        group_of = {}
+        for group, indices in self.groups.items():
+            for index in indices:
+                group_of[index] = group
+        self.group_aux = {}
+        for group in self.groups:
+            self.group_aux[group] = _aux_tables(
+                [row for row, owner in zip(unpack_rows, unpack_owner) if group_of[owner] == group],
+                [row for row, owner in zip(prep_rows, prep_owner) if group_of[owner] == group])
+        if run_aux:
+            self.run_aux(stream)
         # launch parameters (tensor maps included) encoded once per batch of <= 16 jobs
         self.blobs = {}
         for group, indices in self.groups.items():
             blobs = []
-            for i in range(0, len(indices), MAX_RESTORE_JOBS):
-                chunk = indices[i:i + MAX_RESTORE_JOBS]
+            by_dtype: dict = {}
+            for index in indices:  # one launch covers jobs of one output dtype
+                by_dtype.setdefault(self.rows[index][12], []).append(index)
+            batches = [same[i:i + MAX_RESTORE_JOBS] for same in by_dtype.values()
+                       for i in range(0, len(same), MAX_RESTORE_JOBS)]
+            for chunk in batches:
                 blobs.append(ext().restore_build(torch.tensor([self.rows[j] for j in chunk], dtype=torch.int64),
                                                  [self.a_ops[j] for j in chunk], [self.b_ops[j] for j in chunk],
                                                  torch.tensor([self.inverse[j] for j in chunk], dtype=torch.float32)))
@@ -262,9 +281,10 @@ class RestoreProgram:
         self.prepared = True
         return self
 
-    def run_aux(self, stream=None) -> int:
-        """(Re-)run the operand preparation of every job: unpack of the 8-bit sources and basis prep."""
-        unpack_tables, prep_tables = self.aux
+    def run_aux(self, stream=None, group=None) -> int:
+        """(Re-)run the operand preparation of every job (or of one group's jobs): unpack of the 8-bit
+        sources and basis prep."""
+        unpack_tables, prep_tables = self.aux if group is None else self.group_aux[group]
         with torch.cuda.stream(stream or self.stream):
             for table in unpack_tables:
                 ext().unpack_launch(table, self.device.index)
@@ -273,11 +293,14 @@ class RestoreProgram:
         self.launches += len(unpack_tables) + len(prep_tables)
         return len(unpack_tables) + len(prep_tables)
 
-    def launch(self, group=0, stream=None) -> int:
-        """Launch the restore GEMM of one group on ``stream`` (default: the program's stream)."""
+    def launch(self, group=0, stream=None, *, aux: bool = False) -> int:
+        """Launch the restore GEMM of one group on ``stream`` (default: the program's stream); ``aux``
+        first runs the group's unpack + basis preparation."""
         if not self.prepared:
             self.prepare()
         status = status_word(self.device)
+        if aux:
+            self.run_aux(stream, group)
         with torch.cuda.stream(stream or self.stream):
             for blob in self.blobs[group]:
                 ext().restore_run(blob, self.device.index, status)
@@ -286,6 +309,13 @@ class RestoreProgram:
 
     def launch_all(self, stream=None) -> int:
         return sum(self.launch(group, stream) for group in self.groups)
+
+
+def _aux_tables(unpack_rows, prep_rows):
+    return ([torch.tensor(unpack_rows[i:i + MAX_AUX_JOBS], dtype=torch.int64)
+             for i in range(0, len(unpack_rows), MAX_AUX_JOBS)],
+            [torch.tensor(prep_rows[i:i + MAX_AUX_JOBS], dtype=torch.int64)
+             for i in range(0, len(prep_rows), MAX_AUX_JOBS)])
 
 
 def launch_factor_group(items, device, precision, stream, keepalive):

@@ -115,7 +115,7 @@ def expand_affine(affine, normalization, rank):
 
 
 # (cos, sin) entries of one job's separable tables that the fused epilogue stages in shared memory
-PACKED_ROPE_ENTRIES = 5120
+PACKED_ROPE_ENTRIES = 2944
 
 
 def restore_rope_item(positions, grid, device, stream, keepalive):
@@ -432,6 +432,8 @@ class RopeTable:
                                          sin[first:first + count, column:column + pairs]), dim=-1)
                     parts.append(block.reshape(-1, 2))
                     column += pairs
+                if entries % 2:  # storage padded to whole 16-byte units (the kernel bulk-copies it)
+                    parts.append(torch.zeros((1, 2), dtype=torch.float32, device=device))
                 pack = torch.cat(parts).contiguous()
             entry = (pack, stamp)
             if len(self._device_cache) > 256:
