@@ -16,6 +16,7 @@
 #include <cuda_fp16.h>
 
 #include "../common/host.h"
+#include "restore_one.h"
 
 namespace rc {
 namespace prep {
@@ -125,6 +126,29 @@ void prep_launch(const at::Tensor& jobs, int64_t device) {
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream(static_cast<int>(device)).stream();
   prep::prep_kernel<<<grid, prep::kThreads, 0, stream>>>(p);
   RC_CUDA(cudaGetLastError());
+}
+
+// Allocation-free launch of one job (restore_one.h).
+const char* prep_one(const __half* q, int64_t q_stride, const float* scale, const float* offset, __half* bt,
+                     float* bias, int rank, int k_pad, int channels, float prescale, cudaStream_t stream) {
+  if (k_pad % 64 != 0 || rank < 1 || rank > k_pad || channels < 1) return "prep: bad job geometry";
+  if (reinterpret_cast<uintptr_t>(bt) % 16 != 0) return "prep: prepared basis must be 16-byte aligned";
+  prep::Params p;
+  memset(&p, 0, sizeof(p));
+  prep::Job& jb = p.jobs[0];
+  jb.q = q;
+  jb.scale = scale;
+  jb.offset = offset;
+  jb.bt = bt;
+  jb.bias = bias;
+  jb.q_stride = q_stride;
+  jb.rank = rank;
+  jb.k_pad = k_pad;
+  jb.channels = channels;
+  jb.prescale = prescale;
+  dim3 grid((channels + prep::kChannels - 1) / prep::kChannels, 1);
+  prep::prep_kernel<<<grid, prep::kThreads, 0, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "prep: launch failed";
 }
 
 }  // namespace rc

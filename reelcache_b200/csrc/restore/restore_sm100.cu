@@ -36,6 +36,7 @@
 
 #include "../common/host.h"
 #include "../common/sm100.cuh"
+#include "restore_one.h"
 
 namespace rc {
 namespace restore {
@@ -735,6 +736,134 @@ void restore_run(const at::Tensor& blob, int64_t device, const c10::optional<at:
       restore::restore_kernel<restore::kOutF32><<<grid, restore::kThreads, restore::kSmemBytes, stream>>>(p, status_ptr(status));
   }
   RC_CUDA(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free single-job launch (restore_one.h): the same kernel and parameters as
+// restore_build + restore_run for one u8-sourced job, built on the stack without tensors or
+// exceptions.
+// ---------------------------------------------------------------------------------------------
+
+namespace {
+
+EncodeTiledFn g_encode_one = nullptr;
+
+bool tmap_one(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+  if (g_encode_one == nullptr || reinterpret_cast<uintptr_t>(base) % 16 != 0 || row_bytes % 16 != 0) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t elem_strides[2] = {1, 1};
+  return g_encode_one(map, dtype, 2, const_cast<void*>(base), dims, strides, box, elem_strides,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+const char* restore_one_setup(int device) {
+  if (g_encode_one == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult query;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &query) != cudaSuccess ||
+        query != cudaDriverEntryPointSuccess)
+      return "restore: cuTensorMapEncodeTiled is unavailable";
+    g_encode_one = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  int current = -1;
+  if (cudaGetDevice(&current) != cudaSuccess) return "restore: no current device";
+  if (current != device && cudaSetDevice(device) != cudaSuccess) return "restore: cannot select the device";
+  const void* kernels[3] = {reinterpret_cast<const void*>(restore::restore_kernel<restore::kOutBF16>),
+                            reinterpret_cast<const void*>(restore::restore_kernel<restore::kOutF16>),
+                            reinterpret_cast<const void*>(restore::restore_kernel<restore::kOutF32>)};
+  const char* error = nullptr;
+  for (const void* fn : kernels)
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, restore::kSmemBytes) != cudaSuccess)
+      error = "restore: cannot reserve the kernel's shared memory";
+  if (current != device) cudaSetDevice(current);
+  return error;
+}
+
+const char* restore_launch_one(const RestoreOneArgs& a, int device, cudaStream_t stream) {
+  using namespace restore;
+  if (a.k_pad % kBK != 0 || a.k_pad <= 0 || (a.passes != 1 && a.passes != 2) || a.tokens < 1)
+    return "restore: bad job geometry";
+  if (a.channels % 32 != 0 || a.head_dim % 32 != 0 || a.channels % a.head_dim != 0)
+    return "restore: channels and head_dim must be multiples of 32";
+  if (a.out_dtype < kOutBF16 || a.out_dtype > kOutF32) return "restore: unknown output dtype";
+  if (reinterpret_cast<uintptr_t>(a.bias) % 16 != 0) return "restore: bias must be 16-byte aligned";
+  Params p;
+  memset(&p, 0, sizeof(p));
+  JobDesc& jb = p.jobs[0];
+  jb.dst = a.dst;
+  jb.bias = a.bias;
+  jb.dst_ts = a.dst_ts;
+  jb.dst_hs = a.dst_hs;
+  jb.dst_ds = a.dst_ds;
+  jb.tokens = a.tokens;
+  jb.passes = a.passes;
+  jb.out_dtype = a.out_dtype;
+  jb.channels = a.channels;
+  jb.head_dim = a.head_dim;
+  jb.pairs = a.head_dim / 2;
+  jb.inverse = a.inverse;
+  if (a.rope_pack != nullptr) {
+    const int pairs = a.head_dim / 2;
+    if (a.sec_t < 0 || a.sec_h < 0 || a.sec_t + a.sec_h > pairs || a.grid_h < 1 || a.grid_w < 1 ||
+        static_cast<int64_t>(a.grid_t) * a.grid_h * a.grid_w != a.tokens || a.tokens >= (1 << 24))
+      return "restore: RoPE sections or grid do not match the job";
+    if (a.rope_entries != a.grid_t * a.sec_t + a.grid_h * a.sec_h + a.grid_w * (pairs - a.sec_t - a.sec_h) ||
+        a.rope_entries > kRopeEntries || reinterpret_cast<uintptr_t>(a.rope_pack) % 16 != 0)
+      return "restore: packed RoPE tables must hold T*Pt + H*Ph + W*Pw entries (<= 2944), 16-byte aligned";
+    jb.rope = kRopePacked;
+    jb.cos = reinterpret_cast<const float*>(a.rope_pack);
+    jb.sec_t = a.sec_t;
+    jb.sec_th = a.sec_t + a.sec_h;
+    jb.entries = a.rope_entries;
+    jb.grid_h = a.grid_h;
+    jb.grid_w = a.grid_w;
+    jb.off_h = a.grid_t * a.sec_t;
+    jb.off_w = a.grid_t * a.sec_t + a.grid_h * a.sec_h;
+    magic_for(a.grid_h * a.grid_w, jb.hw_magic, jb.hw_shift);
+    magic_for(a.grid_w, jb.w_magic, jb.w_shift);
+  }
+  jb.kblocks = a.k_pad / kBK;
+  jb.a_kblocks = jb.kblocks;
+  jb.b_kblocks = 2 * jb.kblocks;
+  jb.n_tiles = (a.channels + kBN - 1) / kBN;
+  jb.m_tiles = (a.tokens + kBM - 1) / kBM;
+  jb.work_begin = 0;
+  jb.bias_smem = a.channels <= kBiasSmem;
+  if (!tmap_one(&p.a_maps[0], a.a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.k_pad, a.tokens, static_cast<uint64_t>(a.k_pad) * 2,
+                kBK, kBM) ||
+      !tmap_one(&p.b_maps[0], a.bt, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2 * a.k_pad, a.channels,
+                static_cast<uint64_t>(a.k_pad) * 4, kBK, kBN))
+    return "restore: operand tensor maps could not be encoded (run the setup first)";
+  jb.tma_store = a.out_dtype != kOutF32 && a.dst_ds == 1 && a.dst_hs == a.head_dim &&
+                 reinterpret_cast<uintptr_t>(a.dst) % 16 == 0 && (a.dst_ts * 2) % 16 == 0;
+  if (jb.tma_store &&
+      !tmap_one(&p.o_maps[0], a.dst, a.out_dtype == kOutBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                a.channels, a.tokens, static_cast<uint64_t>(a.dst_ts) * 2, kEpiCols, 32))
+    return "restore: destination tensor map could not be encoded";
+  p.num_jobs = 1;
+  p.total_work = jb.m_tiles * jb.n_tiles;
+  p.out_dtype = a.out_dtype;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return "restore: no device";
+  const int grid = p.total_work < sms ? p.total_work : sms;
+  switch (a.out_dtype) {
+    case kOutBF16:
+      restore_kernel<kOutBF16><<<grid, kThreads, kSmemBytes, stream>>>(p, a.status);
+      break;
+    case kOutF16:
+      restore_kernel<kOutF16><<<grid, kThreads, kSmemBytes, stream>>>(p, a.status);
+      break;
+    default:
+      restore_kernel<kOutF32><<<grid, kThreads, kSmemBytes, stream>>>(p, a.status);
+  }
+  return cudaGetLastError() == cudaSuccess ? nullptr : "restore: launch failed";
 }
 
 }  // namespace rc

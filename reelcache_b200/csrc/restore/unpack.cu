@@ -14,6 +14,7 @@
 #include <cuda_fp16.h>
 
 #include "../common/host.h"
+#include "restore_one.h"
 
 namespace rc {
 namespace unpack {
@@ -127,6 +128,29 @@ void unpack_launch(const at::Tensor& jobs, int64_t device) {
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream(static_cast<int>(device)).stream();
   unpack::unpack_kernel<<<grid, unpack::kThreads, 0, stream>>>(p);
   RC_CUDA(cudaGetLastError());
+}
+
+// Allocation-free launch of one dense uint8 job (restore_one.h).
+const char* unpack_u8_one(const uint8_t* matrix, int64_t row_stride, __half* out, int tokens, int k_pad, int rank,
+                          cudaStream_t stream) {
+  if (k_pad % 64 != 0 || k_pad <= 0 || rank < 1 || rank > k_pad || tokens < 1) return "unpack: bad job geometry";
+  if (reinterpret_cast<uintptr_t>(out) % 16 != 0) return "unpack: output must be 16-byte aligned";
+  unpack::Params p;
+  memset(&p, 0, sizeof(p));
+  unpack::Job& jb = p.jobs[0];
+  jb.matrix = matrix;
+  jb.out = out;
+  jb.row_stride = row_stride;
+  jb.tokens = tokens;
+  jb.k_pad = k_pad;
+  jb.rank = rank;
+  jb.frames = 1;
+  jb.height = 1;
+  jb.width = tokens;
+  const int64_t items = static_cast<int64_t>(tokens) * (k_pad / 8);
+  dim3 grid(static_cast<unsigned>((items + unpack::kThreads - 1) / unpack::kThreads), 1);
+  unpack::unpack_kernel<<<grid, unpack::kThreads, 0, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "unpack: launch failed";
 }
 
 }  // namespace rc
