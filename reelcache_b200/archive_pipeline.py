@@ -1,0 +1,336 @@
+"""Ordered asynchronous archival of complete clean chunks (the counterpart of reference
+reelcache/archive_pipeline.py; behaviour from its module docstring, lines 1-61).
+
+Generation keeps going while archival runs behind it with two frontiers per lineage: the
+**generated** frontier (the newest submitted chunk) and the **published** frontier (the lineage head
+in the store). A submitted chunk is a checkpoint only once it is published.
+
+* One **fitter thread** plans each chunk on the GPU (rank method, basis reuse/extension) against its
+  lineage's published head and finalizes its coefficients; chunks of one lineage are planned in
+  submission order, each after its predecessor is published (its parent state).
+* **Encode workers** (a :class:`BoundedExecutor`) build and store the node packs.
+* The **publisher** publishes stored chunks strictly in order per lineage with a compare-and-swap of
+  the head, then trains the predictor registry.
+* Bounded: at most ``max_unpublished`` submitted-but-unpublished chunks per pipeline; ``submit`` waits
+  up to ``submit_timeout`` for room, then raises :class:`CapacityError`. With a raw tier the tier holds
+  the sources (``admit``) and its own budgets apply.
+* A failure of chunk ``n`` fails every later chunk of its lineage and is raised by ``submit``,
+  ``drain`` and the tickets until :meth:`reset` acknowledges it. :meth:`cancel` retires a lineage's
+  unpublished work; :meth:`close` drains (or cancels) everything.
+* :meth:`defer_gpu_work` (a context manager) holds new planning while a memory-critical section runs
+  (e.g. a VAE decode next to archival); restores in flight can be yielded to the same way.
+"""
+
+from __future__ import annotations
+
+import threading
+import time
+from collections import deque
+from contextlib import contextmanager
+from dataclasses import dataclass, field
+from typing import Any, Mapping
+
+import torch
+
+from .errors import CapacityError, ConfigurationError, StateError
+from .execution import BoundedExecutor
+from .lineage import LineageRuntime
+from .lineage_commit import ArchiveOptions
+from .rank_method import RankMethodConfig
+
+
+@dataclass
+class ArchiveTicket:
+    lineage: str
+    chunk_id: str
+    index: int
+    matrices: Any = None
+    contexts: Any = None
+    execution_state: Any = None
+    raw_token: int | None = None
+    state: str = "queued"          # queued | planning | encoding | stored | published | failed | cancelled
+    node_ref: str | None = None
+    error: BaseException | None = None
+    plan: dict | None = None
+    timings: dict = field(default_factory=dict)
+    submitted: float = field(default_factory=time.monotonic)
+    _done: threading.Event = field(default_factory=threading.Event)
+    _job: Any = None
+
+    def done(self) -> bool:
+        return self._done.is_set()
+
+    def result(self, timeout: float | None = None) -> str:
+        if not self._done.wait(timeout):
+            raise TimeoutError(f"archival of {self.lineage}/{self.chunk_id} is still running")
+        if self.state != "published":
+            raise StateError(f"archival of {self.lineage}/{self.chunk_id} {self.state}: {self.error}")
+        return self.node_ref
+
+
+class ArchivePipeline:
+    def __init__(self, runtime: LineageRuntime, *, method: RankMethodConfig, device: Any = "cuda",
+                 options: ArchiveOptions | None = None, raw_tier=None, max_unpublished: int = 4,
+                 submit_timeout: float | None = None, encode_workers: int = 1, registry=None):
+        if type(max_unpublished) is not int or max_unpublished < 1:
+            raise ConfigurationError("max_unpublished must be a positive integer")
+        self.runtime = runtime
+        self.method = method
+        self.device = torch.device(device)
+        self.options = options or ArchiveOptions()
+        self.raw_tier = raw_tier
+        self.registry = registry
+        self.max_unpublished = max_unpublished
+        self.submit_timeout = submit_timeout
+        self.cv = threading.Condition()
+        self._queue: deque[ArchiveTicket] = deque()
+        self._tickets: dict[str, list[ArchiveTicket]] = {}
+        self._failed: dict[str, BaseException] = {}
+        self._generated: dict[str, int] = {}
+        self._defer = 0
+        self._closed = False
+        self._counts = {"submitted": 0, "published": 0, "failed": 0, "cancelled": 0, "backpressure_waits": 0,
+                        "backpressure_seconds": 0.0}
+        self._stream = torch.cuda.Stream(self.device, priority=-1) if self.device.type == "cuda" else None
+        self._encoders = BoundedExecutor(max_workers=encode_workers, max_pending=max(2, 2 * encode_workers))
+        self._fitter = threading.Thread(target=self._fitter_loop, name="reelcache-fitter", daemon=True)
+        self._fitter.start()
+
+    # -- producer side ------------------------------------------------------------------------------------------
+
+    def _unpublished(self) -> int:
+        return sum(1 for tickets in self._tickets.values() for t in tickets if not t.done())
+
+    def submit(self, lineage: str, chunk_id: str, matrices: Mapping[Any, torch.Tensor], contexts, *,
+               execution_state=None, capture_event=None, holder: Any = None) -> ArchiveTicket:
+        """Queue one clean chunk. The tensors are owned by the pipeline (or its raw tier) from here on;
+        ``capture_event`` orders planning after the producer's capture writes."""
+        deadline = None if self.submit_timeout is None else time.monotonic() + self.submit_timeout
+        with self.cv:
+            if self._closed:
+                raise StateError("archive pipeline is closed")
+            if lineage in self._failed:
+                raise StateError(f"lineage {lineage} has a failed archival: {self._failed[lineage]}")
+            waited = None
+            while self._unpublished() >= self.max_unpublished:
+                if waited is None:
+                    waited = time.monotonic()
+                    self._counts["backpressure_waits"] += 1
+                left = None if deadline is None else deadline - time.monotonic()
+                if left is not None and left <= 0:
+                    raise CapacityError("archival backlog is full (max_unpublished)")
+                self.cv.wait(0.05 if left is None else min(left, 0.05))
+                if lineage in self._failed:
+                    raise StateError(f"lineage {lineage} has a failed archival: {self._failed[lineage]}")
+            if waited is not None:
+                self._counts["backpressure_seconds"] += time.monotonic() - waited
+            index = self._generated.get(lineage, 0)
+            self._generated[lineage] = index + 1
+            ticket = ArchiveTicket(lineage, chunk_id, index, matrices, contexts, execution_state)
+            ticket.timings["capture_event"] = capture_event
+            self._tickets.setdefault(lineage, []).append(ticket)
+            self._counts["submitted"] += 1
+        if self.raw_tier is not None:
+            ticket.raw_token = self.raw_tier.admit(matrices, chunk_id, holder)
+            ticket.matrices = None  # the tier owns the sources now
+        with self.cv:
+            self._queue.append(ticket)
+            self.cv.notify_all()
+        return ticket
+
+    # -- fitter / encoders / publisher ----------------------------------------------------------------------------
+
+    def _next(self) -> ArchiveTicket | None:
+        with self.cv:
+            while True:
+                if self._closed and not self._queue:
+                    return None
+                for ticket in list(self._queue):
+                    earlier = [t for t in self._tickets[ticket.lineage] if t.index < ticket.index]
+                    if any(not t.done() for t in earlier):
+                        continue  # planned after its predecessor is published
+                    if self._defer:
+                        break
+                    self._queue.remove(ticket)
+                    return ticket
+                self.cv.wait(0.05)
+
+    def _fitter_loop(self) -> None:
+        while True:
+            ticket = self._next()
+            if ticket is None:
+                return
+            if ticket.state == "cancelled":
+                continue
+            try:
+                self._plan(ticket)
+            except BaseException as error:  # noqa: BLE001 - delivered to the ticket and its lineage
+                self._fail(ticket, error)
+
+    def _plan(self, ticket: ArchiveTicket) -> None:
+        started = time.perf_counter()
+        ticket.state = "planning"
+        event = ticket.timings.pop("capture_event", None)
+        ctx = torch.cuda.stream(self._stream) if self._stream is not None else _Null()
+        with ctx:
+            if event is not None and self._stream is not None:
+                self._stream.wait_event(event)
+            matrices = ticket.matrices if ticket.raw_token is None else self.raw_tier.source(ticket.raw_token)
+            job = self.runtime.prepare_commit("chunk", ticket.lineage, ticket.chunk_id,
+                                              [(ticket.chunk_id, matrices, ticket.contexts)], method=self.method,
+                                              registry=self.registry, execution_state=ticket.execution_state,
+                                              device=self.device, options=self.options)
+            job.plan().finalize()
+            if self._stream is not None:
+                self._stream.synchronize()
+        ticket._job = job
+        ticket.matrices = None
+        ticket.timings["plan_seconds"] = time.perf_counter() - started
+        ticket.state = "encoding"
+        self._encoders.submit(self._encode_and_publish, ticket, block=True)
+
+    def _encode_and_publish(self, ticket: ArchiveTicket) -> None:
+        try:
+            started = time.perf_counter()
+            job = ticket._job
+            job.encode().store()
+            ticket.timings["encode_seconds"] = time.perf_counter() - started
+            ticket.state = "stored"
+            with self.cv:
+                if ticket.state == "cancelled" or ticket.lineage in self._failed:
+                    raise StateError("cancelled")
+            commit = self.runtime.publish_job(job, job.expected_head, registry=self.registry)
+            ticket.node_ref = commit.node_ref
+            ticket.plan = commit.plan
+            job.release()
+            ticket._job = None
+            if ticket.raw_token is not None:
+                self.raw_tier.published(ticket.raw_token, commit.node_ref)
+            with self.cv:
+                ticket.state = "published"
+                self._counts["published"] += 1
+                ticket._done.set()
+                self.cv.notify_all()
+        except BaseException as error:  # noqa: BLE001
+            self._fail(ticket, error)
+
+    def _fail(self, ticket: ArchiveTicket, error: BaseException) -> None:
+        with self.cv:
+            cancelled = ticket.state == "cancelled"
+            if not cancelled:
+                self._failed.setdefault(ticket.lineage, error)
+            for t in self._tickets.get(ticket.lineage, []):
+                if t.index >= ticket.index and not t.done():
+                    t.state = "cancelled" if cancelled else "failed"
+                    t.error = error
+                    self._counts["cancelled" if cancelled else "failed"] += 1
+                    if t in self._queue:
+                        self._queue.remove(t)
+                    if t._job is not None:
+                        t._job.release()
+                        t._job = None
+                    if t.raw_token is not None and self.raw_tier is not None:
+                        self.raw_tier.failed(t.raw_token)
+                    t._done.set()
+            self.cv.notify_all()
+
+    # -- control --------------------------------------------------------------------------------------------------
+
+    def frontiers(self, lineage: str) -> dict:
+        with self.cv:
+            tickets = self._tickets.get(lineage, [])
+            published = [t for t in tickets if t.state == "published"]
+            return {"generated": self._generated.get(lineage, 0),
+                    "published": published[-1].node_ref if published else self.runtime.lineage_head(lineage),
+                    "unpublished": sum(1 for t in tickets if not t.done()),
+                    "failed": None if lineage not in self._failed else str(self._failed[lineage])}
+
+    def drain(self, lineage: str | None = None, timeout: float | None = None) -> float:
+        """Wait until every submitted chunk (of ``lineage``) is published; returns the seconds waited."""
+        started = time.monotonic()
+        deadline = None if timeout is None else started + timeout
+        with self.cv:
+            while True:
+                lineages = [lineage] if lineage is not None else list(self._tickets)
+                failed = [name for name in lineages if name in self._failed]
+                if failed:
+                    raise StateError(f"lineage {failed[0]} has a failed archival: {self._failed[failed[0]]}")
+                if all(t.done() for name in lineages for t in self._tickets.get(name, [])):
+                    return time.monotonic() - started
+                left = None if deadline is None else deadline - time.monotonic()
+                if left is not None and left <= 0:
+                    raise TimeoutError("archival drain timed out")
+                self.cv.wait(0.05 if left is None else min(0.05, left))
+
+    def cancel(self, lineage: str) -> int:
+        """Retire the lineage's unpublished work (queued or not yet stored); returns the count."""
+        with self.cv:
+            pending = [t for t in self._tickets.get(lineage, []) if not t.done() and t.state in ("queued", "encoding")]
+            for t in pending:
+                t.state = "cancelled"
+        for t in pending:
+            self._fail(t, StateError("cancelled"))
+        return len(pending)
+
+    def forget(self, lineage: str, timeout: float | None = 60.0) -> None:
+        """Cancel the lineage's unpublished work, wait for what is already publishing, and drop every
+        record of it (a deleted session)."""
+        self.cancel(lineage)
+        deadline = None if timeout is None else time.monotonic() + timeout
+        with self.cv:
+            while any(not t.done() for t in self._tickets.get(lineage, [])):
+                left = None if deadline is None else deadline - time.monotonic()
+                if left is not None and left <= 0:
+                    raise TimeoutError(f"archival of {lineage} did not settle")
+                self.cv.wait(0.05 if left is None else min(0.05, left))
+            self._tickets.pop(lineage, None)
+            self._failed.pop(lineage, None)
+            self._generated.pop(lineage, None)
+
+    def reset(self, lineage: str) -> BaseException | None:
+        """Acknowledge a lineage's failure so new chunks may be submitted again."""
+        with self.cv:
+            self._tickets[lineage] = [t for t in self._tickets.get(lineage, []) if t.state == "published"]
+            self._generated[lineage] = len(self._tickets[lineage])
+            return self._failed.pop(lineage, None)
+
+    @contextmanager
+    def defer_gpu_work(self):
+        """Hold new planning on the GPU while the body runs (memory-critical sections)."""
+        with self.cv:
+            self._defer += 1
+        try:
+            yield
+        finally:
+            with self.cv:
+                self._defer -= 1
+                self.cv.notify_all()
+
+    def stats(self) -> dict:
+        with self.cv:
+            return {**self._counts, "unpublished": self._unpublished(), "lineages": len(self._tickets),
+                    "failed_lineages": sorted(self._failed), "encoders": self._encoders.stats()}
+
+    def close(self, *, drain: bool = True, timeout: float | None = None) -> None:
+        if drain:
+            try:
+                self.drain(timeout=timeout)
+            except (StateError, TimeoutError):
+                pass
+        with self.cv:
+            for lineage in list(self._tickets):
+                for t in self._tickets[lineage]:
+                    if not t.done():
+                        t.state = "cancelled"
+            self._closed = True
+            self.cv.notify_all()
+        self._fitter.join(timeout=30)
+        self._encoders.close(cancel_pending=True)
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *args):
+        return False

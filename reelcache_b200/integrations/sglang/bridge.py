@@ -1,0 +1,176 @@
+"""The serving bridge: the engine seam between a chunked video-generation engine and the archive
+(the counterpart of reference reelcache/integrations/sglang/bridge.py:875-3173).
+
+A request (``request``) runs one action on a session -- create / resume / rewind / fork -- and then
+generates chunks:
+
+1. **Restore**: the session's resident cache is reused when it already holds the target path
+   (``resident_reuse``; a rewind onto a prefix of the resident path is free); otherwise the attended
+   history (:func:`build_visibility_plan`) is installed from the raw tier or the archive, overlapped
+   layer by layer with the first denoising forward (``overlap_restore``).
+2. **Generate**: per chunk, the engine's clean forward hands every layer's pre-RoPE K / V to a
+   :class:`CleanChunkBuilder`.
+3. **Commit**: the sealed chunk goes to the asynchronous archive (``durability="always"`` drains
+   after every chunk; ``"pause"`` makes ``pause``/``checkpoint`` the durability points).
+
+``request`` returns a report: time to first chunk (``ttfc_ms``, host wall clock and, on CUDA, device
+events), the restore's route and statistics, the archive tickets and frontiers.
+"""
+
+from __future__ import annotations
+
+import threading
+import time
+from typing import Any
+
+import torch
+
+from ...errors import ConfigurationError, StateError
+from .capture import CleanChunkBuilder
+from .config import ReelCacheRuntimeConfig
+from .lineage_archive import LineageSessionArchive
+from .nodes import chunk_nodes
+from .profiles import ModelProfile
+from .session import SGLangSessionController
+from .visibility import build_visibility_plan
+from .workload_telemetry import WorkloadTelemetry
+
+ACTIONS = ("create", "resume", "rewind", "fork")
+
+
+class CausalWanKVBridge:
+    def __init__(self, config: ReelCacheRuntimeConfig, engine, profile: ModelProfile, *, cache_chunks: int = 16):
+        self.config = config
+        self.engine = engine
+        self.profile = profile
+        self.device = torch.device(engine.device)
+        self.archive = LineageSessionArchive(config, engine.identity, profile, self.device)
+        self.sessions = SGLangSessionController(self.archive)
+        self.cache_chunks = cache_chunks
+        self.telemetry = WorkloadTelemetry(enabled=config.workload_telemetry)
+        self._lock = threading.RLock()
+
+    # -- requests -------------------------------------------------------------------------------------------------
+
+    def request(self, session_id: str, *, chunks: int = 1, action: str = "resume", checkpoint: Any = None,
+                source: str | None = None, seed: int = 0) -> dict:
+        if action not in ACTIONS:
+            raise ConfigurationError(f"action must be one of {ACTIONS}")
+        if type(chunks) is not int or chunks < 0:
+            raise ConfigurationError("chunks must be a nonnegative integer")
+        started = time.perf_counter()
+        span = self.telemetry.begin(session_id, action)
+        with self._lock:
+            if action == "create":
+                state = self.sessions.create(session_id)
+            elif action == "fork":
+                if source is None:
+                    raise ConfigurationError("fork needs a source session")
+                state = self.sessions.fork(source, session_id, checkpoint=checkpoint)
+            elif action == "rewind":
+                state = self.sessions.rewind(session_id, checkpoint)
+            else:
+                state = self.sessions.get(session_id, required=False) or self.sessions.create(session_id)
+            self.sessions.check_ready(state)
+            state.status = "running"
+        try:
+            report = self._run(state, chunks, seed, started, span)
+        except BaseException:
+            state.status = "failed" if state.failure is not None else "idle"
+            raise
+        state.status = "idle"
+        report["action"] = action
+        report["wall_ms"] = (time.perf_counter() - started) * 1e3
+        self.telemetry.end(span, report)
+        return report
+
+    def _run(self, state, chunks: int, seed: int, started: float, span) -> dict:
+        start_chunk = state.generated
+        need = start_chunk + chunks
+        cache = state.resident
+        route = "resident"
+        install = None
+        restore_stats: dict = {}
+        if not (self.config.resident_reuse and cache is not None and state.resident_chunks >= start_chunk
+                and need <= self._capacity(cache)):
+            cache = self.engine.new_cache(max(need, self.cache_chunks))
+            route = "none"
+            if start_chunk > 0:
+                published = len(self.sessions.chunks(state.session_id))
+                if published < start_chunk:
+                    self.archive.drain(state.session_id)  # the history to restore must be published
+                head = self.sessions.head(state.session_id)
+                plan = build_visibility_plan(self.profile, chunk_nodes(self.archive.runtime, head), start_chunk)
+                span.mark("restore_issue")
+                install = self.engine.install(cache, self.archive, head, plan, overlapped=self.config.overlap_restore)
+                route = "archive"
+        cuda = self.device.type == "cuda"
+        first_event = None
+        if cuda:
+            start_event = torch.cuda.Event(enable_timing=True)
+            start_event.record()
+        latents = None
+        tickets = []
+        ttfc_ms = None
+        for i in range(chunks):
+            index = start_chunk + i
+            frames, (h, w) = self.profile.chunk_frames, self.profile.grid
+            builder = CleanChunkBuilder(self.engine.identity, index, index * self.profile.chunk_tokens, frames, h, w,
+                                        self.profile.cfg_streams)
+            wait = install.wait if (install is not None and i == 0) else None
+            latents = self.engine.generate_chunk(cache, index, builder, request_seed=seed, layer_wait=wait)
+            if i == 0:
+                if install is not None:
+                    restore_stats = install.join() or install.stats
+                if cuda:
+                    first_event = torch.cuda.Event(enable_timing=True)
+                    first_event.record()
+                    first_event.synchronize()
+                ttfc_ms = (time.perf_counter() - started) * 1e3
+                span.mark("first_chunk")
+            matrices, contexts = builder.seal()
+            capture_event = None
+            if cuda:
+                capture_event = torch.cuda.Event()
+                capture_event.record()
+            ticket = self.archive.commit_chunk(state.session_id, f"chunk-{index}", matrices, contexts,
+                                               capture_event=capture_event)
+            tickets.append(ticket)
+            state.pending.append(ticket)
+            state.generated = index + 1
+            if self.config.durability == "always":
+                self.archive.drain(state.session_id)
+        state.resident = cache
+        state.resident_chunks = state.generated
+        self.sessions.reconcile(state)
+        report = {"session": state.session_id, "start_chunk": start_chunk, "chunks": chunks, "route": route,
+                  "ttfc_ms": ttfc_ms, "restore": restore_stats, "generated": state.generated,
+                  "tickets": [t.chunk_id for t in tickets], "frontiers": self.archive.pipeline.frontiers(state.session_id),
+                  "latents": latents}
+        if cuda and first_event is not None:
+            report["ttfc_gpu_ms"] = start_event.elapsed_time(first_event)
+        return report
+
+    def _capacity(self, cache) -> int:
+        """Chunks of history a cache can hold."""
+        rows = cache["k"][0].shape[0] if isinstance(cache, dict) else cache.k[0].shape[1]
+        return rows // self.profile.chunk_tokens
+
+    # -- controls -----------------------------------------------------------------------------------------------
+
+    def pause(self, session_id: str, timeout: float | None = None) -> dict:
+        return self.sessions.pause(session_id, timeout=timeout)
+
+    def checkpoint(self, session_id: str, name: str | None = None, timeout: float | None = None) -> dict:
+        return self.sessions.checkpoint(session_id, name, timeout=timeout)
+
+    def close(self, session_id: str, *, delete: bool = False) -> dict:
+        return self.sessions.close(session_id, delete=delete)
+
+    def drop_resident(self, session_id: str) -> None:
+        state = self.sessions.get(session_id)
+        state.resident = None
+        state.resident_chunks = 0
+
+    def shutdown(self) -> None:
+        self.archive.close()

@@ -1,0 +1,170 @@
+"""Per-session archival and restore for the serving bridge (the counterpart of reference
+reelcache/integrations/sglang/lineage_archive.py:428-1626).
+
+One lineage per session over one content-addressed store. Commits go through the asynchronous
+:class:`ArchivePipeline` (rank method on the fit device, node packs, strict in-order publication);
+captured sources wait in the :class:`RawChunkTier` until published and stay as an evictable lossless
+cache. Restores prefer the raw tier (``raw_restore="prefer"``) and otherwise decode the archive: on a
+GPU with the fused sm_100a restore (:class:`LineageRestorer`, layer by layer, overlapped with the
+first forward), elsewhere with the reference decode.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import torch
+
+from ...archive_pipeline import ArchivePipeline
+from ...archive_restore import LineageRestorer
+from ...errors import ConfigurationError
+from ...lineage import LineageRuntime
+from ...lineage_commit import ArchiveOptions
+from ...predictor_registry import RankPredictorRegistry
+from ...rank_method import RankMethodConfig
+from ...raw_tier import RawChunkTier
+from ...store import ObjectStore
+from ...types import CodecSpec, EnergyTargets, MatrixKey, ModelIdentity, energy_targets
+from .config import ReelCacheRuntimeConfig
+from .profiles import ModelProfile
+
+
+def method_for(config: ReelCacheRuntimeConfig, profile: ModelProfile, fit_device) -> RankMethodConfig:
+    if config.energy_key is not None:
+        targets = EnergyTargets("custom", config.energy_key, config.energy_value, True, "explicit energy fractions")
+    else:
+        targets = energy_targets(config.energy_profile or profile.energy_profile)
+    fixed = {}
+    if config.rank_policy == "fixed_uniform":
+        fixed = {"fixed_rank_k": config.uniform_rank, "fixed_rank_v": config.uniform_rank}
+    elif config.rank_policy == "fixed_fraction":
+        fractions = config.rank_fractions()
+        fixed = {"fixed_rank_k": max(1, round(fractions["K"] * profile.channels)),
+                 "fixed_rank_v": max(1, round(fractions["V"] * profile.channels))}
+    return RankMethodConfig(targets, CodecSpec("svd_hevc", 32, normalization=config.normalization),
+                            reuse=config.reuse, refit=config.refit, refit_rule=config.refit_rule,
+                            rate_lag=config.rate_lag, matmul_precision=config.matmul_precision or "fp32", **fixed)
+
+
+class LineageSessionArchive:
+    def __init__(self, config: ReelCacheRuntimeConfig, identity: ModelIdentity, profile: ModelProfile, device):
+        self.config = config
+        self.profile = profile
+        self.device = torch.device(device)
+        self.store = ObjectStore(config.store_root, max_bytes=config.max_store_bytes, verify_reads=config.verify_reads,
+                                 on_damage="keep" if config.on_open_error == "quarantine" else "raise")
+        self.registry = RankPredictorRegistry(config.predictor_registry_id)
+        self.runtime = LineageRuntime(self.store, identity, registry=self.registry)
+        fit_device = self.device if config.fit_device == "cuda" and self.device.type == "cuda" else torch.device("cpu")
+        self.method = method_for(config, profile, fit_device)
+        self.raw_tier = None
+        if config.raw_tier:
+            gpu = config.gpu_raw_budget_bytes
+            if gpu is None:
+                gpu = (4 << 30) if self.device.type == "cuda" else (256 << 20)
+            host = config.host_raw_budget_bytes if config.host_raw_budget_bytes is not None else (8 << 30)
+            self.raw_tier = RawChunkTier(self.device, gpu_budget_bytes=gpu, host_budget_bytes=host,
+                                         host_pinned=config.host_raw_pinned, retain=config.raw_tier_retain,
+                                         promote=config.raw_tier_promote)
+        self.pipeline = ArchivePipeline(self.runtime, method=self.method, device=fit_device,
+                                        options=ArchiveOptions(), raw_tier=self.raw_tier,
+                                        max_unpublished=config.max_unpublished, submit_timeout=config.submit_timeout,
+                                        encode_workers=config.resolved_encode_workers(), registry=self.registry)
+        self.restorer = LineageRestorer(self.runtime, self.device, prepared_budget_bytes=config.prepared_budget_bytes,
+                                        basis_budget_bytes=config.basis_budget_bytes) \
+            if self.device.type == "cuda" else None
+        self.stats_ = {"raw_installs": 0, "archive_installs": 0, "commits": 0}
+
+    # -- lineages -------------------------------------------------------------------------------------------------
+
+    def create(self, session_id: str) -> str:
+        self.runtime.create_lineage(session_id)
+        return self.runtime.lineage_head(session_id)
+
+    def exists(self, session_id: str) -> bool:
+        return ("lineages/" + session_id) in self.store.list_refs("lineages/")
+
+    def head(self, session_id: str) -> str:
+        return self.runtime.lineage_head(session_id)
+
+    def fork(self, node_ref: str, session_id: str) -> None:
+        self.runtime.fork_lineage(node_ref, session_id)
+
+    def rewind(self, session_id: str, node_ref: str) -> None:
+        self.pipeline.drain(session_id)
+        self.runtime.rewind_lineage(session_id, node_ref)
+
+    def delete(self, session_id: str) -> None:
+        self.pipeline.forget(session_id)
+        self.runtime.delete_lineage(session_id)
+        if self.raw_tier is not None:
+            self.raw_tier.release_holder(session_id, drop=True)
+
+    def commit_chunk(self, session_id: str, chunk_id: str, matrices, contexts, *, execution_state=None,
+                     capture_event=None):
+        self.stats_["commits"] += 1
+        return self.pipeline.submit(session_id, chunk_id, matrices, contexts, execution_state=execution_state,
+                                    capture_event=capture_event, holder=session_id)
+
+    def drain(self, session_id: str | None = None, timeout: float | None = None) -> float:
+        return self.pipeline.drain(session_id, timeout)
+
+    # -- restore --------------------------------------------------------------------------------------------------
+
+    def _raw_span(self, node_ref: str, key: MatrixKey, offset: int, length: int):
+        if self.raw_tier is None or self.config.raw_restore != "prefer":
+            return None
+        lease = self.raw_tier.lookup(node_ref)
+        if lease is None:
+            return None
+        try:
+            tensor = lease.tensors.get(key)
+            return None if tensor is None else tensor[offset:offset + length].clone()
+        finally:
+            lease.release()
+
+    def install_dense(self, cache: dict, head_ref: str, plan, layers: int) -> dict:
+        """Dense pre-RoPE history into a synthetic engine's cache: raw tier first, then the archive."""
+        raw = archive = 0
+        for layer in range(layers):
+            for target, rows in (("K", cache["k"][layer]), ("V", cache["v"][layer])):
+                key = MatrixKey(layer, target)
+                for span in plan.spans:
+                    piece = self._raw_span(span.node_ref, key, span.node_offset, span.length)
+                    if piece is None:
+                        piece = self.runtime.acquire_node_history(
+                            head_ref, key, ranges=[(span.token_start, span.token_start + span.length)],
+                            device=rows.device, dtype=rows.dtype)
+                        archive += 1
+                    else:
+                        raw += 1
+                    rows[span.slot_start:span.slot_start + span.length] = piece.to(rows.dtype)
+        cache["end"] = plan.spans[-1].slot_start + plan.spans[-1].length if plan.spans else 0
+        self.stats_["raw_installs"] += raw
+        self.stats_["archive_installs"] += archive
+        return {"raw_spans": raw, "archive_spans": archive, "attended_tokens": plan.attended_tokens}
+
+    def restore_into(self, head_ref: str, destination, rope, plan, *, overlapped: bool = True):
+        """Fused sm_100a restore of the plan's history into native caches (GPU)."""
+        if self.restorer is None:
+            raise ConfigurationError("the fused restore needs a CUDA device")
+        self.stats_["archive_installs"] += len(plan.spans)
+        return self.restorer.restore(head_ref, destination, rope, overlapped=overlapped, ranges=plan.ranges(),
+                                     thread=overlapped)
+
+    # -- lifecycle ------------------------------------------------------------------------------------------------
+
+    def gc(self) -> dict:
+        self.drain()
+        return self.store.collect_garbage()
+
+    def stats(self) -> dict[str, Any]:
+        return {**self.stats_, "pipeline": self.pipeline.stats(),
+                "raw_tier": None if self.raw_tier is None else self.raw_tier.stats(),
+                "restorer": None if self.restorer is None else self.restorer.stats()}
+
+    def close(self) -> None:
+        self.pipeline.close(drain=True)
+        if self.raw_tier is not None:
+            self.raw_tier.close()
+        self.store.close()
