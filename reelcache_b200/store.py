@@ -147,7 +147,7 @@ class ReadAhead:
                 self._pending.append(object_id)
                 count += 1
         if count:
-            self._futures.append(self._store._pool().submit(self._fill))
+            self._futures.append(self._store._ahead_pool().submit(self._fill))
         return count
 
     def _fill(self) -> None:
@@ -464,21 +464,33 @@ class ObjectStore:
         if not path.exists():
             raise IntegrityError(f"missing immutable object file: {object_id}")
 
-    def _get(self, object_id: str, *, verify: bool | None = None) -> bytes:
-        path = self.path_for(object_id)
+    def _index_row(self, object_id: str):
+        """The object's index row (kind, size); caller holds the store lock (SQLite runs on the caller's
+        thread only: the connection is shared)."""
         row = self._db.execute("SELECT kind, size FROM objects WHERE id=?", (object_id,)).fetchone()
         if row is None:
             raise IntegrityError(f"missing immutable object: {object_id}")
         if object_id in self._evicted:
             raise EvictedObjectError(f"object payload was evicted: {object_id}")
-        verify = (self.verify_reads if verify is None else verify) or object_id in self._quarantined
+        return row
+
+    def _read_object(self, object_id: str) -> bytes:
+        """File read of one object (no index access: safe on the reader pool)."""
         try:
-            data = self._read_file(path)
+            return self._read_file(self.path_for(object_id))
         except OSError as exc:
             with self._io_lock:
                 self.io_stats_["errors"] += 1
                 self.io_stats_["last_error"] = str(exc)
             raise IntegrityError(f"cannot read immutable object: {object_id}") from exc
+
+    def _get(self, object_id: str, *, verify: bool | None = None, data: bytes | None = None, row=None) -> bytes:
+        self.path_for(object_id)
+        if row is None:
+            row = self._index_row(object_id)
+        verify = (self.verify_reads if verify is None else verify) or object_id in self._quarantined
+        if data is None:
+            data = self._read_object(object_id)
         if len(data) != row[1]:
             self._fail(object_id, "size differs from the index")
         if verify:
@@ -502,10 +514,19 @@ class ObjectStore:
     get_bytes = get
 
     def _pool(self) -> ThreadPoolExecutor:
+        """File reads of get_many (they never take the store lock)."""
         with self._pool_guard:
             if self._readers is None:
                 self._readers = ThreadPoolExecutor(max_workers=8, thread_name_prefix="reelcache-store-read")
             return self._readers
+
+    def _ahead_pool(self) -> ThreadPoolExecutor:
+        """Read-ahead workers (they take the store lock per object, so they never share get_many's pool,
+        whose caller holds that lock while it waits for its reads)."""
+        with self._pool_guard:
+            if getattr(self, "_ahead", None) is None:
+                self._ahead = ThreadPoolExecutor(max_workers=4, thread_name_prefix="reelcache-store-ahead")
+            return self._ahead
 
     def get_many(self, object_ids: Iterable[str], *, verify: bool | None = None,
                  read_ahead: ReadAhead | None = None) -> dict[str, bytes]:
@@ -519,14 +540,14 @@ class ObjectStore:
                     result[object_id] = data
         rest = [i for i in ids if i not in result]
         with self.transaction():
-            for object_id in rest:
-                self.path_for(object_id)
+            rows = {object_id: (self.path_for(object_id), self._index_row(object_id))[1] for object_id in rest}
             if len(rest) <= 1:
                 for object_id in rest:
-                    result[object_id] = self._get(object_id, verify=verify)
+                    result[object_id] = self._get(object_id, verify=verify, row=rows[object_id])
             else:
-                for object_id, data in zip(rest, self._pool().map(lambda i: self._get(i, verify=verify), rest)):
-                    result[object_id] = data
+                # parallel file reads; index lookups and checks stay on this thread
+                for object_id, data in zip(rest, self._pool().map(self._read_object, rest)):
+                    result[object_id] = self._get(object_id, verify=verify, data=data, row=rows[object_id])
         return {object_id: result[object_id] for object_id in ids}
 
     def read_ahead(self, object_ids: Iterable[str] = (), *, max_bytes: int) -> ReadAhead:
@@ -937,6 +958,8 @@ class ObjectStore:
             self._lock_file.close()
         if self._readers is not None:
             self._readers.shutdown(wait=False)
+        if getattr(self, "_ahead", None) is not None:
+            self._ahead.shutdown(wait=False)
 
     def __enter__(self) -> ObjectStore:
         return self
