@@ -1,0 +1,193 @@
+"""Distributed components on CPU with Gloo process groups (world size 2 and 3): the failure-agreement
+transport, Ulysses / context-parallel exchanges, factor sharding (both reconstruction modes) and the
+tiered sequence-parallel history. Failures are made on the host: a rank that raises, a rank that
+cancels."""
+
+import os
+import socket
+import tempfile
+import traceback
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _entry(rank, world, port, fn_name, args, errors):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        timeout = 5 if fn_name == "w_dead_peer" else 60
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout))
+        globals()[fn_name](rank, world, *args)
+    except BaseException:  # noqa: BLE001
+        errors.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def run(fn_name, world=2, *args):
+    ctx = mp.get_context("spawn")
+    errors = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_entry, args=(r, world, port, fn_name, args, errors)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+        if p.is_alive():
+            p.kill()
+            raise AssertionError("a rank hung")
+    failures = []
+    while not errors.empty():
+        failures.append(errors.get())
+    assert not failures, "\n".join(f"rank {r}:\n{tb}" for r, tb in failures)
+
+
+# ---- workers (module level so spawn can pickle them by name) ----------------------------------------------------
+
+def w_transport(rank, world):
+    from reelcache_b200.parallel.distributed import CollectiveCancelled, DistributedOwner, KVLayout, PeerFailure
+    t = DistributedOwner(device="cpu", max_wire_bytes=64)
+    assert t.broadcast_json({"x": 1}) == {"x": 1}
+    heads = 2 * world
+    layout = KVLayout(tokens=10, kv_heads=heads, head_dim=3, world_size=world)
+    full = torch.arange(10 * heads * 3, dtype=torch.float32).reshape(10, heads * 3)
+    g = t.gather_matrix(full[layout.rows(rank)].clone(), layout, source_layout="rows")
+    h = t.gather_matrix(full[:, layout.columns(rank)].clone(), layout, source_layout="heads")
+    if rank == 0:
+        assert torch.equal(g, full) and torch.equal(h, full)
+    else:
+        assert g is None and h is None
+    mine = t.local_columns(layout, lambda cols: full[:, cols].contiguous(), dtype=torch.float32)
+    assert torch.equal(mine, full[:, layout.columns(rank)])
+    moved = t.transfer_tensor(full * 2 if rank == 1 else None, source=1, destination=0)
+    assert (rank != 0) or torch.equal(moved, full * 2)
+    assert t.counters.payload_messages_sent + t.counters.payload_messages_received > 0
+    # a local failure on one rank is raised on every rank before any payload moves
+    with pytest.raises(PeerFailure):
+        t.checkpoint("step", error=ValueError("boom") if rank == 1 else None)
+    with pytest.raises(CollectiveCancelled):
+        t.checkpoint("cancel", cancelled=(rank == 0))
+    with pytest.raises(PeerFailure):
+        t.owner_call("owner", lambda: 1 / 0)
+
+
+def w_ulysses(rank, world):
+    from reelcache_b200.parallel.context_parallel import RowShard, gather_tokens, optimal_split, ulysses_in, ulysses_out
+    assert optimal_split(4, 44, 82) == (2, 2)
+    frames, height, width, heads, d = 2, 4, 6, 4, 3
+    shards = [RowShard(r, world, frames, height, width) for r in range(world)]
+    tokens = frames * height * width
+    full = torch.arange(tokens * heads * d, dtype=torch.float32).reshape(tokens, heads, d)
+    local = shards[rank].local(full)
+    seq = ulysses_in(local, None)
+    order = torch.cat([s.token_index() for s in shards])
+    hw = heads // world
+    assert torch.equal(seq, full[order][:, rank * hw:(rank + 1) * hw])
+    back = ulysses_out(seq, None)
+    assert torch.equal(back, local)
+    assert torch.equal(gather_tokens(local, shards), full)
+
+
+def w_factor(rank, world, mode, granularity):
+    from reelcache_b200.parallel.distributed import DistributedOwner, KVLayout
+    from reelcache_b200.parallel.factor_sharding import FactorShardDomain, FactorShardSpec, NativeOwners, row_shard_gram
+    from reelcache_b200.types import MatrixKey
+    t = DistributedOwner(device="cpu")
+    layout = KVLayout(tokens=24, kv_heads=4, head_dim=8, world_size=world)
+    g = torch.Generator().manual_seed(3)
+    full = torch.randn(24, 6, generator=g) @ torch.randn(6, 32, generator=g)
+    gram = row_shard_gram(full[layout.rows(rank)])
+    assert torch.allclose(gram, full.double().t() @ full.double(), atol=1e-8)
+    spec = FactorShardSpec(world, granularity=granularity, block_rows=2)
+    domain = FactorShardDomain(t, spec, NativeOwners(layout, "heads"))
+    for layer in range(2):
+        for target in ("K", "V"):
+            key = MatrixKey(layer, target)
+            domain.fit_and_scatter(key, full if rank == 0 else None, 6)
+            mine = domain.reconstruct(key, mode=mode)
+            assert torch.allclose(mine, full[:, layout.columns(rank)], atol=1e-4), (mode, key)
+
+
+def w_sp_history(rank, world, root):
+    from reelcache_b200.lineage import LineageRuntime
+    from reelcache_b200.parallel.distributed import DistributedOwner
+    from reelcache_b200.parallel.sp_kv import SPTieredHistory
+    from reelcache_b200.store import ObjectStore
+    from tests.lineage_support import FRAMES, HEIGHT, MODEL, TOKENS, WIDTH, chunk, method, relative_error
+    t = DistributedOwner(device="cpu")
+    store = ObjectStore(root)
+    runtime = LineageRuntime(store, MODEL)
+    if rank == 0:
+        runtime.create_lineage("sp")
+    t.checkpoint("created")
+    heads = 2
+    head_dim = MODEL.channels_for("K") // heads
+    per_chunk = 2 * MODEL.layers * TOKENS * (MODEL.channels_for("K") // world) * 4
+    hist = SPTieredHistory(t, runtime, "sp", layers=MODEL.layers, kv_heads=heads, head_dim=head_dim,
+                           chunk_tokens=TOKENS, grid=(FRAMES, HEIGHT, WIDTH), hot_budget_bytes=per_chunk,
+                           method=method())
+    sources = []
+    for index in range(3):
+        matrices, _ = chunk(index)
+        sources.append(matrices)
+        cols = slice(rank * (MODEL.channels_for("K") // world), (rank + 1) * (MODEL.channels_for("K") // world))
+        local = {(k.layer, k.target): v[:, cols].contiguous() for k, v in matrices.items()}
+        hist.capture(index, local)
+    assert hist.hot_chunks() == [2]  # budget of one chunk: the two oldest went cold on every rank
+    from reelcache_b200.types import MatrixKey
+    for layer in range(MODEL.layers):
+        got = hist.load_layer(layer)
+        for target in ("K", "V"):
+            expect = torch.cat([s[MatrixKey(layer, target)] for s in sources])[:, cols]
+            assert relative_error(got[target], expect) < 0.1
+    assert hist.stats["cold_decodes"] > 0
+    store.close()
+
+
+def w_dead_peer(rank, world):
+    """Rank 1 leaves between steps (no collective in flight); rank 0's next checkpoint fails within the
+    process group's short timeout instead of blocking."""
+    from reelcache_b200.parallel.distributed import DistributedOwner, PeerFailure
+    import torch.distributed as dist
+    t = DistributedOwner(device="cpu")
+    t.checkpoint("step0")
+    if rank == 1:
+        dist.destroy_process_group()
+        os._exit(0)
+    with pytest.raises(PeerFailure):
+        t.checkpoint("step1")
+    with pytest.raises(PeerFailure):  # the transport is marked broken for good
+        t.checkpoint("step2")
+
+
+def test_dead_peer_detected():
+    run("w_dead_peer", 2)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_transport_failure_agreement(world):
+    run("w_transport", world)
+
+
+def test_ulysses_and_context_parallel():
+    run("w_ulysses", 2)
+
+
+@pytest.mark.parametrize("mode,granularity", [("factors", "matrix"), ("partials", "matrix"), ("factors", "rows")])
+def test_factor_sharding(mode, granularity):
+    run("w_factor", 2, mode, granularity)
+
+
+def test_sp_tiered_history(tmp_path):
+    run("w_sp_history", 2, str(tmp_path / "store"))
