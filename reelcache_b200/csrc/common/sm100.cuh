@@ -1,5 +1,5 @@
 // Blackwell (sm_100a) device primitives shared by every tensor-core kernel in this package:
-// mbarriers with bounded waits, TMA tile loads (never with cluster multicast), tcgen05 TMEM
+// mbarriers with bounded waits, TMA tile loads (plain, one destination CTA), tcgen05 TMEM
 // allocation / MMA / commit / load, and the shared-memory and instruction descriptors of
 // `tcgen05.mma.cta_group::1.kind::f16`.
 //

@@ -151,6 +151,8 @@ class RestoreProgram:
             k_pad = k_pad_of(rank)
             if job["kind"] == "f32":
                 sizes = (tokens * 2 * k_pad * 2, 0, channels * 4)
+            elif job["kind"] == "a16":  # A already unpacked (e.g. in a peer's symmetric buffer)
+                sizes = (0, channels * 2 * k_pad * 2, channels * 4)
             else:
                 sizes = (tokens * k_pad * 2, channels * 2 * k_pad * 2, channels * 4)
             offsets = []
@@ -195,10 +197,16 @@ class RestoreProgram:
                     qmax = basis_max_abs(job["basis"])
                 smax = float(np.abs(job["scale"][:rank]).max(initial=0.0))
                 e = prescale_exponent(smax * qmax)
-                a = scratch[a_off:a_off + tokens * k_pad * 2].view(torch.float16).view(tokens, k_pad)
+                if job["kind"] != "a16":
+                    a = scratch[a_off:a_off + tokens * k_pad * 2].view(torch.float16).view(tokens, k_pad)
                 b = scratch[b_off:b_off + channels * 2 * k_pad * 2].view(torch.float16).view(channels, 2 * k_pad)
                 frames, height, width = job["grid"]
-                if job["kind"] == "pictures":
+                if job["kind"] == "a16":
+                    a = job["a"]  # FP16 [tokens, k_pad] centered pixels, produced elsewhere
+                    if a.dtype != torch.float16 or tuple(a.shape) != (tokens, k_pad):
+                        raise ConfigurationError("a16 jobs take an FP16 [tokens, k_pad] A operand")
+                    self.keepalive.append(a)
+                elif job["kind"] == "pictures":
                     addresses, plane_stride, row_stride, layout = job["pictures"]
                     col_off, col_seg = column_tables(layout, plane_stride, row_stride, k_pad)
                     unpack_owner.append(len(self.rows))
