@@ -50,6 +50,10 @@ def parse():
     ap.add_argument("--history", type=int, default=4, help="chunks restored per step (rewind target)")
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--layers", type=int, default=30)
+    ap.add_argument("--mode", default="dp", choices=("dp", "sp"),
+                    help="dp: every rank restores its own session (config 2); sp: Ulysses sequence-parallel restore "
+                         "of one long history, every rank its head slice, A operands read from peer memory (config 3)")
+    ap.add_argument("--sp-chunks", type=int, default=24, help="history chunks of the sp mode (24 = 112k tokens)")
     ap.add_argument("--write-rank-profile", action="store_true",
                     help="write the archive's per-matrix ranks to bench_rank_profile.json")
     return ap.parse_args()
@@ -461,21 +465,141 @@ def run_reference(args, rank, world, local):
                     + ("from bench_rank_profile.json" if profile is not None else "64 (no rank profile)")}
 
 
+def run_sp(args, rank, world, local):
+    """Ulysses SP restore of a ``--sp-chunks`` history: tiles round-robin over ranks, every rank restores
+    its head columns of every tile with the fused peer-memory restore (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+    from reelcache_b200 import restore_kernels as rk
+    from reelcache_b200.ops import _ext
+    from reelcache_b200.ops.peer_restore import PeerRestoreDomain, column_basis, plan_tiles
+    from reelcache_b200.ops.restore import RestoreProgram
+    from reelcache_b200.restore_kernels import restore_rope_item
+
+    device = torch.device("cuda", local)
+    layers, chunks, heads, head_dim = args.layers, args.sp_chunks, 12, 128
+    frames, h, w = 3, 30, 52
+    tokens, channels = frames * h * w, heads * head_dim
+    if heads < world:
+        return {"impl": "ours", "unavailable": f"{heads} heads cannot cover {world} ranks"}
+    first, last = rank * heads // world, (rank + 1) * heads // world  # uneven splits: 12 heads over 8 ranks
+    local_heads = last - first
+    cols = slice(first * head_dim, last * head_dim)
+    profile = load_rank_profile(layers, 4)
+    gen = torch.Generator(device=device).manual_seed(0)
+    table = rk.RopeTable.wan(head_dim, 4 * chunks, device=device)
+    shapes, meta = [], []
+    for layer in range(layers):
+        for c in range(chunks):
+            for which in ("K", "V"):
+                rank_k = profile[which][c % 4][layer] if profile is not None else 64
+                shapes.append((len(shapes) % world, tokens, rank_k))
+                meta.append((layer, c, which, rank_k))
+    tiles = plan_tiles(shapes)
+    capacity = max((t.offset + t.nbytes for t in tiles if t.owner == rank), default=256)
+    capacity = max(capacity, 256)
+    if world > 1:
+        cap = torch.tensor([capacity], dtype=torch.int64, device=device)
+        dist.all_reduce(cap, op=dist.ReduceOp.MAX)
+        capacity = int(cap.item())
+        domain = PeerRestoreDomain(None, device, capacity)
+    else:
+        domain = None
+        buffer = torch.empty(capacity, dtype=torch.uint8, device=device)
+    sources, keep = {}, []
+    cache_k = [torch.zeros((1, chunks * tokens, local_heads, head_dim), dtype=torch.bfloat16, device=device)
+               for _ in range(layers)]
+    cache_v = [torch.zeros_like(cache_k[0]) for _ in range(layers)]
+    stream = torch.cuda.current_stream(device)
+    program = RestoreProgram(device, stream, precision="fp16")
+    unpack_rows = []
+    for i, (tile, (layer, c, which, rank_k)) in enumerate(zip(tiles, meta)):
+        if tile.owner == rank:
+            src = torch.randint(0, 256, (tokens, rank_k), generator=gen, device=device, dtype=torch.uint8)
+            sources[i] = src
+            out = (domain.buffer if domain is not None else buffer)[tile.offset:tile.offset + tile.nbytes]
+            unpack_rows.append([0, 0, 0, src.data_ptr(), out.data_ptr(), src.stride(0), tokens, tile.k_pad, rank_k,
+                                1, 1, tokens])
+        basis = (torch.randn(rank_k, channels, generator=gen, device=device) / 40).half()
+        b = column_basis(basis, rank_k, cols)
+        keep.append(b)
+        scale = np.full(rank_k, 0.02, dtype=np.float32)
+        offset = np.full(rank_k, -2.5, dtype=np.float32)
+        dest = (cache_k if which == "K" else cache_v)[layer][0, c * tokens:(c + 1) * tokens]
+        rope = restore_rope_item(rk.RopePositions(table, (3 * c, 0, 0)), (frames, h, w), device, None, keep) \
+            if which == "K" else None
+        a = domain.a_view(tile) if domain is not None else \
+            buffer[tile.offset:tile.offset + tile.nbytes].view(torch.float16).view(tokens, tile.k_pad)
+        program.add({"kind": "a16", "a": a, "tokens": tokens, "rank": rank_k, "grid": (frames, h, w), "basis": b,
+                     "qmax": float(b.abs().amax().item()), "scale": scale, "offset": offset, "rope": rope,
+                     "dest": (dest.data_ptr(), (dest.stride(0), dest.stride(1), dest.stride(2)), dest.dtype,
+                              local_heads * head_dim, head_dim)}, group=layer)
+    unpack_tables = [torch.tensor(unpack_rows[i:i + 48], dtype=torch.int64) for i in range(0, len(unpack_rows), 48)]
+    program.prepare(run_aux=False)
+    torch.cuda.synchronize()
+
+    def step():
+        for table_rows in unpack_tables:  # owners stage their tiles (unpack into the symmetric buffer)
+            _ext.ext().unpack_launch(table_rows, local)
+        if world > 1:
+            torch.cuda.synchronize()
+            dist.barrier()
+        program.run_aux(stream)
+        program.launch_all(stream)
+        if world > 1:
+            torch.cuda.synchronize()
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        stop.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = reduce_max(start.elapsed_time(stop) / args.steps, world)
+    _ext.check_status(device)
+    restored = 2 * layers * chunks * tokens * channels * 2
+    remote = sum(t.nbytes for t in tiles if t.owner != rank)
+    launches = len(unpack_tables) + len(program.aux[0]) + len(program.aux[1]) + \
+        sum(len(b) for b in program.blobs.values())
+    return {"metric": METRIC, "value": round(restored / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(ms, 4), "gpu_launches": launches, "clocks": clocks.summary(),
+            "restored_bytes_per_step": restored, "remote_a_bytes_per_rank": remote,
+            "note": f"Ulysses SP{world}: {chunks}-chunk history; every rank restores its heads ({heads} heads split "
+                    f"{heads // world}-{-(-heads // world)} per rank) of every tile, A operands read by the fused "
+                    "restore straight from the owners' symmetric buffers",
+            "scaling_kind": "strong"}
+
+
 def main():
     args = parse()
     rank, world, local = dist_setup(args)
     if args.impl == "reference":
-        out = run_reference(args, rank, world, local)
+        out = run_reference(args, rank, world, local) if args.mode == "dp" else \
+            {"impl": "reference", "unavailable": "the sp mode has no reference arm (its SP restore needs the "
+                                                 "reference's full SGLang engine)"}
+    elif args.mode == "sp":
+        out = run_sp(args, rank, world, local)
     else:
         out = run_ours(args, rank, world, local)
     if "unavailable" not in out:
+        sp = args.mode == "sp"
         out.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-                    "scaling": "weak", "vs_baseline": None if BASELINE_PUBLISHED is None else out["value"] / BASELINE_PUBLISHED,
+                    "scaling": "strong" if sp else "weak",
+                    "vs_baseline": None if BASELINE_PUBLISHED is None else out["value"] / BASELINE_PUBLISHED,
                     "dtype": "bf16", "data": "synthetic (random-init CausVid-shaped DiT generates the archived history)",
                     "config": {"model": "CausVid-shaped causal DiT (Wan2.1-T2V-1.3B geometry), random-init bf16",
-                               "global_batch": world, "seq_len": args.history * 4680, "parallelism": f"dp{world}",
-                               "history_chunks": args.history, "tokens_per_chunk": 4680,
-                               "l2": "each step writes 3.45 GB of KV, far larger than the 126 MB L2"}})
+                               "global_batch": 1 if sp else world,
+                               "seq_len": (args.sp_chunks if sp else args.history) * 4680,
+                               "parallelism": f"sp{world}" if sp else f"dp{world}",
+                               "history_chunks": args.sp_chunks if sp else args.history, "tokens_per_chunk": 4680,
+                               "l2": "each step writes >= 3.45 GB of KV, far larger than the 126 MB L2"}})
         out.setdefault("impl", args.impl)
     if rank == 0:
         print(json.dumps(out), flush=True)

@@ -41,7 +41,7 @@
 namespace rc {
 namespace restore {
 
-constexpr int kMaxJobs = 16;
+constexpr int kMaxJobs = 48;                   // launch parameters stay below the 32 KB limit
 constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;
@@ -56,7 +56,7 @@ constexpr int kBTileBytes = kBN * kBK * 2;   // 32 KB
 constexpr int kOutBufBytes = 32 * kEpiCols * 2;  // one 32 x 64 16-bit output block (128-byte rows)
 constexpr int kOutBytes = kEpilogueWarps * kOutBufBytes;
 constexpr int kTmemCols = 512;
-constexpr int kRopeEntries = 2944;          // (cos, sin) float2 entries of one job's separable tables
+constexpr int kRopeEntries = 3072;          // (cos, sin) float2 entries of one job's separable tables
 constexpr int kBiasSmem = 2048;             // channels whose bias is staged in shared memory
 constexpr int kOperandBytes = kAStages * kATileBytes + kBSlots * kBTileBytes;
 enum OutDtype : int { kOutBF16 = 0, kOutF16 = 1, kOutF32 = 2 };
@@ -81,9 +81,7 @@ struct JobDesc {
   float inverse;
 };
 
-static_assert(sizeof(JobDesc) % 8 == 0, "job descriptors are copied as words and keep 8-byte fields aligned");
-constexpr int kSmemBytes = kOperandBytes + kOutBytes + kRopeEntries * 8 + kBiasSmem * 4 +
-                           kMaxJobs * static_cast<int>(sizeof(JobDesc)) + 1024 + 256;
+constexpr int kSmemBytes = kOperandBytes + kOutBytes + kRopeEntries * 8 + kBiasSmem * 4 + 1024 + 256;
 static_assert(kSmemBytes <= 232448, "shared memory budget of one CTA");
 
 struct Params {
@@ -100,8 +98,7 @@ struct Params {
 
 // Work cursor over (job, n_tile, m_tile) with m fastest: consecutive work items of a CTA share the B
 // tile (job, n_tile), which stays resident. Decoded once per CTA, then advanced without loops or
-// divisions (a per-tile search over the jobs sat on every role's critical path). Job descriptors are
-// read from the CTA's shared-memory copy.
+// divisions (a per-tile search over the jobs sat on every role's critical path).
 // n / d for 0 <= n < 2^24 by multiply-shift: magic = ceil(2^shift / d), shift = 24 + ceil(log2 d)
 // (Granlund-Montgomery; exact for n < 2^24). Integer pipes only.
 __device__ __forceinline__ int div_magic(int n, uint32_t magic, int shift) {
@@ -156,8 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
   uint8_t* out_smem = smem + kOperandBytes;
   float2* rope_smem = reinterpret_cast<float2*>(out_smem + kOutBytes);
   float* bias_smem = reinterpret_cast<float*>(rope_smem + kRopeEntries);
-  JobDesc* jobs = reinterpret_cast<JobDesc*>(bias_smem + kBiasSmem);
-  uint64_t* afull = reinterpret_cast<uint64_t*>(jobs + kMaxJobs);
+  const JobDesc* jobs = p.jobs;
+  uint64_t* afull = reinterpret_cast<uint64_t*>(bias_smem + kBiasSmem);
   uint64_t* aempty = afull + kAStages;
   uint64_t* bfull = aempty + kAStages;
   uint64_t* bempty = bfull + kBSlots;
@@ -176,12 +173,6 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
   const int work_hi = static_cast<int>((static_cast<int64_t>(p.total_work) * (blockIdx.x + 1)) / gridDim.x);
 
   const int num_jobs = p.num_jobs;
-  {
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(p.jobs);
-    uint32_t* dst = reinterpret_cast<uint32_t*>(jobs);
-    const int words = num_jobs * static_cast<int>(sizeof(JobDesc) / 4);
-    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
-  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kAStages; ++s) {
       mbar_init(&afull[s], 1);
@@ -590,7 +581,7 @@ inline void magic_for(int d, uint32_t& magic, int& shift) {
 
 }  // namespace restore
 
-// Builds the launch parameters of one fused restore over <= 16 jobs (tensor maps encoded once) and
+// Builds the launch parameters of one fused restore over <= 48 jobs (tensor maps encoded once) and
 // returns them as a CPU byte tensor for restore_run. `jobs` is a CPU int64 [n, 40] table (field
 // order: reelcache_b200/ops/restore.py, RestoreProgram.prepare); `a_ops` the per-job A operands and
 // `b_ops` the prepared B operands; `inverse` the exact inverse prescales (CPU float32 [n]).
@@ -599,7 +590,7 @@ at::Tensor restore_build(const at::Tensor& jobs, const std::vector<at::Tensor>& 
   RC_CHECK(jobs.device().is_cpu() && jobs.scalar_type() == at::kLong && jobs.dim() == 2 && jobs.size(1) == 40,
            "jobs must be a CPU int64 [num_jobs, 40] table");
   const int n = static_cast<int>(jobs.size(0));
-  RC_CHECK(n >= 1 && n <= restore::kMaxJobs, "between 1 and 16 jobs per launch");
+  RC_CHECK(n >= 1 && n <= restore::kMaxJobs, "between 1 and 48 jobs per launch");
   RC_CHECK(static_cast<int>(a_ops.size()) == n && static_cast<int>(b_ops.size()) == n, "one A and B operand per job");
   RC_CHECK(inverse.device().is_cpu() && inverse.scalar_type() == at::kFloat && inverse.numel() == n,
            "inverse must be a CPU float32 [num_jobs] vector");
@@ -667,7 +658,7 @@ at::Tensor restore_build(const at::Tensor& jobs, const std::vector<at::Tensor>& 
       RC_CHECK(jb.entries == r[9] * r[18] + r[10] * r[19] + r[11] * (jb.pairs - jb.sec_th) &&
                    jb.entries <= restore::kRopeEntries && reinterpret_cast<uintptr_t>(jb.cos) % 16 == 0,
                "packed RoPE tables: T*Pt + H*Ph + W*Pw (cos, sin) entries (storage padded to an even count), "
-               "at most 2944, 16-byte aligned");
+               "at most 3072, 16-byte aligned");
     }
     jb.bias_smem = jb.channels <= restore::kBiasSmem;
     jb.kblocks = static_cast<int>(k_pad / restore::kBK);
@@ -815,7 +806,7 @@ const char* restore_launch_one(const RestoreOneArgs& a, int device, cudaStream_t
       return "restore: RoPE sections or grid do not match the job";
     if (a.rope_entries != a.grid_t * a.sec_t + a.grid_h * a.sec_h + a.grid_w * (pairs - a.sec_t - a.sec_h) ||
         a.rope_entries > kRopeEntries || reinterpret_cast<uintptr_t>(a.rope_pack) % 16 != 0)
-      return "restore: packed RoPE tables must hold T*Pt + H*Ph + W*Pw entries (<= 2944), 16-byte aligned";
+      return "restore: packed RoPE tables must hold T*Pt + H*Ph + W*Pw entries (<= 3072), 16-byte aligned";
     jb.rope = kRopePacked;
     jb.cos = reinterpret_cast<const float*>(a.rope_pack);
     jb.sec_t = a.sec_t;

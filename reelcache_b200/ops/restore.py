@@ -30,7 +30,7 @@ from ._ext import ext, status_word
 
 _OUT_CODE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 _COLUMN_TABLES: dict = {}
-MAX_RESTORE_JOBS = 16
+MAX_RESTORE_JOBS = 48
 MAX_AUX_JOBS = 48
 
 
@@ -270,7 +270,7 @@ class RestoreProgram:
                 [row for row, owner in zip(prep_rows, prep_owner) if group_of[owner] == group])
         if run_aux:
             self.run_aux(stream)
-        # launch parameters (tensor maps included) encoded once per batch of <= 16 jobs
+        # launch parameters (tensor maps included) encoded once per batch of <= 48 jobs
         self.blobs = {}
         for group, indices in self.groups.items():
             blobs = []

@@ -115,7 +115,7 @@ def expand_affine(affine, normalization, rank):
 
 
 # (cos, sin) entries of one job's separable tables that the fused epilogue stages in shared memory
-PACKED_ROPE_ENTRIES = 2944
+PACKED_ROPE_ENTRIES = 3072
 
 
 def restore_rope_item(positions, grid, device, stream, keepalive):
