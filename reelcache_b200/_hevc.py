@@ -298,8 +298,22 @@ def align(value, alignment=CANVAS_ALIGNMENT):
 
 
 def start_code_positions(stream):
-    """Offsets of every ``00 00 01`` start code (the payload begins 3 bytes later)."""
-    return [m.start() for m in _START_CODE.finditer(bytes(stream))]
+    """Offsets of every ``00 00 01`` start code (the payload begins 3 bytes later); the native scanner
+    (memchr over the stream, no Python-level copy of matches) when the extension is built."""
+    data = bytes(stream)
+    native = _native_scanner()
+    if native is not None and len(data) >= 4096:
+        import torch
+        return native(torch.frombuffer(bytearray(data), dtype=torch.uint8))
+    return [m.start() for m in _START_CODE.finditer(data)]
+
+
+def _native_scanner():
+    try:
+        from .ops._ext import ext
+        return ext().start_codes
+    except Exception:  # noqa: BLE001 - the host fast path is optional
+        return None
 
 
 def nal_units(stream):

@@ -5,6 +5,9 @@
 #include <vector>
 
 namespace rc {
+int64_t pread_many(const std::vector<std::string>& paths, const std::vector<int64_t>& offsets,
+                   const std::vector<int64_t>& sizes, const std::vector<int64_t>& dest, int64_t threads);
+std::vector<int64_t> start_codes(const at::Tensor& data);
 void gemm_bf16_tn(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epilogue,
                   const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& gate,
                   const c10::optional<at::Tensor>& resid, double alpha, int64_t bn,
@@ -54,4 +57,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("jobs"));
   m.def("unpack_launch", &rc::unpack_launch, "mosaic pictures -> dense uint8 [N, K_pad] over <= 48 jobs",
         py::arg("jobs"), py::arg("device"));
+  m.def("pread_many", &rc::pread_many, "parallel positioned reads into host memory (GIL released)",
+        py::arg("paths"), py::arg("offsets"), py::arg("sizes"), py::arg("dest"), py::arg("threads") = 8);
+  m.def("start_codes", &rc::start_codes, "Annex-B start-code offsets of a CPU uint8 tensor", py::arg("data"));
 }

@@ -1,0 +1,142 @@
+"""Restore tiers on CPU: the staging engine (native parallel pread + hash checks), the decoder pool and
+decoded tier behind the packed-decode restorer, archive eviction under a budget, device-pressure trims
+and runtime telemetry."""
+
+import pytest
+import torch
+
+from reelcache_b200 import restore_kernels as rk
+from reelcache_b200.decoded_tier import DecodedTier
+from reelcache_b200.decoder_pool import DecoderPool
+from reelcache_b200.device_pressure import DeviceTrimRegistry
+from reelcache_b200.errors import CapacityError, IntegrityError
+from reelcache_b200.integrations.sglang.archive_eviction import ArchiveEviction
+from reelcache_b200.lineage import LineageRuntime
+from reelcache_b200.packed_decode import PackedRestorer
+from reelcache_b200.restore_staging import StagingEngine
+from reelcache_b200.store import ObjectStore
+from reelcache_b200.telemetry import RuntimeTelemetry, span
+from reelcache_b200.types import MatrixKey
+
+from .lineage_support import MODEL, TOKENS, chunk, method, relative_error
+
+
+@pytest.fixture
+def archived(tmp_path):
+    store = ObjectStore(tmp_path / "store", verify_reads=True)
+    runtime = LineageRuntime(store, MODEL)
+    runtime.create_lineage("main")
+    nodes, sources = [], []
+    for index in range(3):
+        m, c = chunk(index)
+        sources.append(m)
+        nodes.append(runtime.commit_node("main", f"c{index}", m, c, method=method()).node_ref)
+    yield runtime, nodes, sources
+    store.close()
+
+
+def test_staging_engine_reads_and_verifies(archived, tmp_path):
+    runtime, nodes, _ = archived
+    ids = sorted({ref for ref in runtime.store.references(nodes[-1])})
+    blobs = [i for i in ids if not i.startswith("manifest:")] or ids
+    engine = StagingEngine(runtime.store, pinned_bytes=8 << 20, threads=4)
+    staged = engine.stage(blobs)
+    for object_id in blobs:
+        assert staged.bytes(object_id) == runtime.store.get(object_id)
+    staged.release()
+    # corrupt one payload: the staged hash check refuses it
+    victim = next(i for i in runtime.store.list_refs() and blobs)
+    path = runtime.store.path_for(victim)
+    data = bytearray(path.read_bytes())
+    data[0] ^= 0xFF
+    path.write_bytes(bytes(data))
+    with pytest.raises(IntegrityError):
+        engine.stage([victim])
+
+
+def test_packed_restorer_with_decoder_pool_and_tier(archived):
+    runtime, nodes, sources = archived
+    pool = DecoderPool(2)
+    tier = DecodedTier(64 << 20, route="all")
+    restorer = PackedRestorer(runtime, pool, decoded_tier=tier, device="cpu")
+    pieces = restorer.plan(nodes[-1])
+    # warm the tier with one pack's decoded tiles (as an archival validation decode would)
+    first = restorer.prepared(restorer.runtime.load_record(pieces[0].entry.records[0][1]).packet_ref)
+    tier.offer(first.digest, [pool.decode_stream(first.stream, first.stream_codec, first.raw_shape).wait()])
+    batch = restorer.submit(pieces, MODEL.layers)
+    assert first.packet_ref in batch.routed
+    heads, head_dim = 2, MODEL.channels_for("K") // 2
+    caches = {(l, t): torch.zeros((1, 3 * TOKENS, heads, head_dim)) for l in range(MODEL.layers) for t in "KV"}
+    table = rk.RopeTable.wan(head_dim, 32)
+    for layer in range(MODEL.layers):
+        handle = restorer.reconstruct(batch, pieces, layer, lambda l, w: caches[(l, w)],
+                                      lambda piece: (table, (2 * (piece.token_start // TOKENS), 0, 0)))
+        handle.synchronize()
+    restorer.release(batch)
+    for layer in range(MODEL.layers):
+        got = caches[(layer, "V")].reshape(3 * TOKENS, -1)
+        expect = torch.cat([s[MatrixKey(layer, "V")] for s in sources])
+        assert relative_error(got, expect) < 0.1
+    assert pool.stats()["decoded"] >= 2 and tier.stats()["routed"] == 1
+    pool.close()
+
+
+def test_decoded_tier_deficit_route():
+    tier = DecodedTier(1 << 20, route="deficit", layer_ms=(1.5, 0.0, None), decode_gbps=1.0)
+    for i in range(4):
+        tier.bind(f"p{i}", f"d{i}")
+        tier.offer(f"d{i}", [torch.zeros(1000, dtype=torch.uint8).numpy()])
+    # 4 packs of 30 MB over 30 layers: 4 ms of decode per layer vs a 0.85 x 1.5 ms budget -> route the oldest 3
+    routed = tier.route([(f"p{i}", 30_000_000) for i in range(4)], layers=30)
+    assert routed == ["p0", "p1", "p2"]
+    tier.release(routed)
+    assert tier.forget_packets(["p0"]) == 1
+
+
+def test_archive_eviction_budget(archived):
+    runtime, nodes, _ = archived
+    store = runtime.store
+    sizes = {}
+    objects = {}
+    for ref in nodes:
+        payload = [o for o in store.references(ref) if not o.startswith("manifest:")]
+        packet = runtime.load_node(ref).packet_ref
+        payload += [o for o in store.references(packet) if not o.startswith("manifest:")]
+        objects[ref] = set(payload)
+        sizes[ref] = sum(store.object_size(o) for o in objects[ref])
+    budget = sum(sizes.values()) + 1
+    evictor = ArchiveEviction(store, budget)
+    for ref in nodes:
+        evictor.published(ref, objects[ref])
+    assert evictor.live_bytes <= budget
+    evictor.touch([nodes[0]])  # node 0 is now the most recently used
+    with evictor.pin([nodes[1]]):
+        evictor.reserve(sizes[nodes[2]] // 2 + 1)  # evicts the least recently used unpinned node: node 2
+    assert evictor.evicted(nodes[2]) and not evictor.evicted(nodes[1])
+    with pytest.raises(CapacityError):
+        evictor.reserve(budget * 10)
+
+
+def test_device_pressure_and_telemetry():
+    registry = DeviceTrimRegistry()
+    freed = []
+
+    class Cache:
+        def trim(self, reason):
+            freed.append(reason)
+            return 100
+
+    cache = Cache()
+    registry.register("restorer:test", cache.trim)
+    registry.register("decoder_pool", lambda reason: 1 / 0)
+    result = registry.trim("oom", empty_cache=lambda: None)
+    assert result["bytes"] == 100 and freed == ["oom"]
+    assert result["trims"][0]["name"] == "decoder_pool" and "error" in result["trims"][0]
+    del cache
+    assert [r["name"] for r in registry.registered()] == ["decoder_pool"]
+    collector = RuntimeTelemetry()
+    with collector.capture():
+        with span("store.read", nbytes=10):
+            pass
+    snap = collector.snapshot()
+    assert snap["stages"]["store.read"]["completed_bytes"] == 10
