@@ -1,0 +1,97 @@
+"""LongCat-shaped DiT on CPU (tiny geometry, plain-torch ops): context-parallel forward over Gloo equals
+the single-rank forward, and the conditioning-cache seam archives a built cache as a segment node and
+restores it (this rank's rows under CP)."""
+
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+TINY = dict(layers=2, dim=128, heads=4, head_dim=32, ffn=256, text_dim=64, text_len=8, in_channels=4,
+            latent_height=8, latent_width=12)
+
+
+def _model():
+    from reelcache_b200.models.longcat import LongCatConfig, LongCatDiT
+    return LongCatDiT(LongCatConfig(**TINY), "cpu", seed=1, use_kernels=False, max_frames=16)
+
+
+def _inputs(model, frames=2, seed=2):
+    g = torch.Generator().manual_seed(seed)
+    latents = torch.randn(model.cfg.in_channels, frames, model.cfg.latent_height, model.cfg.latent_width, generator=g)
+    text = model.encode_text(torch.randn(model.cfg.text_len, model.cfg.text_dim, generator=g))
+    return latents, text
+
+
+def _cp_worker(rank, world, port, errors):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        from reelcache_b200.models.longcat import ConditioningCacheEpoch
+        model = _model()
+        latents, text = _inputs(model)
+        cond, _ = _inputs(model, frames=1, seed=5)
+        epoch = ConditioningCacheEpoch("e0", 0, 0, 1)
+        full_cache = model.build_conditioning_cache(cond, text, epoch)
+        local_cache = model.build_conditioning_cache(cond, text, epoch, cp_group=dist.group.WORLD)
+        ref = model.forward(latents, 0.5, text, first_frame=1, cache=full_cache)
+        got = model.forward(latents, 0.5, text, first_frame=1, cache=local_cache, cp_group=dist.group.WORLD)
+        assert torch.allclose(got, ref, atol=2e-2, rtol=2e-2), (got - ref).abs().max()
+    except BaseException:  # noqa: BLE001
+        errors.put((rank, traceback.format_exc()))
+    finally:
+        if torch.distributed.is_initialized():
+            torch.distributed.destroy_process_group()
+
+
+def test_context_parallel_matches_single_rank():
+    ctx = mp.get_context("spawn")
+    errors = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_cp_worker, args=(r, 2, port, errors)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+    failures = []
+    while not errors.empty():
+        failures.append(errors.get())
+    assert not failures, "\n".join(tb for _, tb in failures)
+
+
+def test_conditioning_cache_seam(tmp_path):
+    from reelcache_b200.lineage import LineageRuntime
+    from reelcache_b200.models.longcat import ConditioningCacheEpoch, ReelCacheConditioningCacheBackend
+    from reelcache_b200.rank_method import RankMethodConfig
+    from reelcache_b200.store import ObjectStore
+    from reelcache_b200.types import CodecSpec, ModelIdentity, energy_targets
+    model = _model()
+    cfg = model.cfg
+    store = ObjectStore(tmp_path / "store")
+    identity = ModelIdentity("longcat-tiny", "seed1", cfg.layers, cfg.dim, "BTHD", "bfloat16")
+    runtime = LineageRuntime(store, identity)
+    runtime.create_lineage("session")
+    method = RankMethodConfig(energy_targets("longcat_720p"), CodecSpec("svd_hevc", 32), solver="gram_eigh")
+    backend = ReelCacheConditioningCacheBackend(runtime, "session", method, head_dim=cfg.head_dim, grid=cfg.grid)
+    latents, text = _inputs(model)
+    cond, _ = _inputs(model, frames=2, seed=9)
+    epoch = ConditioningCacheEpoch("seg-0", 0, 0, 2)
+    assert backend.restore(epoch) is None
+    built = model.build_conditioning_cache(cond, text, epoch)
+    backend.on_cache_built(built)
+    restored = backend.restore(epoch)
+    assert restored is not None and restored.tokens == built.tokens
+    for a, b in zip(built.k, restored.k):
+        rel = float((a.float() - b.float()).norm() / a.float().norm())
+        assert rel < 0.2
+    ref = model.forward(latents, 0.5, text, first_frame=2, cache=built)
+    got = model.forward(latents, 0.5, text, first_frame=2, cache=restored)
+    assert float((got - ref).norm() / ref.norm()) < 0.1
+    store.close()
