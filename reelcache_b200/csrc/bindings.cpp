@@ -27,6 +27,14 @@ void rms_norm(const at::Tensor& x, at::Tensor& y, const at::Tensor& w, double ep
 void quantize_columns(const at::Tensor& p, const at::Tensor& scale, const at::Tensor& offset, at::Tensor& out);
 void rope_store_launch(const at::Tensor& jobs);
 void unpack_launch(const at::Tensor& jobs, int64_t device);
+void split_bf16x3(const at::Tensor& x, at::Tensor& out, int64_t kp, const std::vector<int64_t>& parts);
+void jacobi_eigh(const at::Tensor& a, at::Tensor& values, at::Tensor& vectors, at::Tensor& info, at::Tensor& sweeps,
+                 int64_t max_sweeps, double tol);
+void sq_partials(const at::Tensor& x, const c10::optional<at::Tensor>& r, double scale, at::Tensor& out);
+void fingerprint_partials(const at::Tensor& bits, at::Tensor& out, int64_t row_start, int64_t prime);
+void dot2_gemm(const at::Tensor& x, const at::Tensor& rows, at::Tensor& out);
+void gemm_bf16_promoted(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, double alpha,
+                        const c10::optional<at::Tensor>& status);
 }  // namespace rc
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -35,7 +43,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("B"), py::arg("out"), py::arg("epilogue") = 0, py::arg("bias") = py::none(),
         py::arg("gate") = py::none(), py::arg("resid") = py::none(), py::arg("alpha") = 1.0, py::arg("bn") = 0,
         py::arg("status") = py::none());
-  m.def("restore_build", &rc::restore_build, "launch parameters of a fused restore over <= 16 jobs",
+  m.def("restore_build", &rc::restore_build, "launch parameters of a fused restore over <= 48 jobs",
         py::arg("jobs"), py::arg("a_ops"), py::arg("b_ops"), py::arg("inverse"));
   m.def("restore_run", &rc::restore_run, "launch a fused restore from restore_build parameters", py::arg("blob"),
         py::arg("device"), py::arg("status") = py::none(), py::arg("ablate") = 0);
@@ -60,4 +68,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("pread_many", &rc::pread_many, "parallel positioned reads into host memory (GIL released)",
         py::arg("paths"), py::arg("offsets"), py::arg("sizes"), py::arg("dest"), py::arg("threads") = 8);
   m.def("start_codes", &rc::start_codes, "Annex-B start-code offsets of a CPU uint8 tensor", py::arg("data"));
+  m.def("split_bf16x3", &rc::split_bf16x3, "FP32 -> K-concatenated bf16 hi/mid/lo segments", py::arg("x"),
+        py::arg("out"), py::arg("kp"), py::arg("parts"));
+  m.def("jacobi_eigh", &rc::jacobi_eigh, "batched FP32 Jacobi eigendecomposition (n <= 160)", py::arg("a"),
+        py::arg("values"), py::arg("vectors"), py::arg("info"), py::arg("sweeps"), py::arg("max_sweeps"),
+        py::arg("tol"));
+  m.def("sq_partials", &rc::sq_partials, "FP64 partial sums of (x/s)^2 and ((x-r)/s)^2 per 8 rows", py::arg("x"),
+        py::arg("r"), py::arg("scale"), py::arg("out"));
+  m.def("fingerprint_partials", &rc::fingerprint_partials, "exact int64 fingerprint partials per 8 rows",
+        py::arg("bits"), py::arg("out"), py::arg("row_start"), py::arg("prime"));
+  m.def("gemm_bf16_promoted", &rc::gemm_bf16_promoted,
+        "out = alpha * A @ B^T (bf16, K-major) with TMEM partials promoted to FP32 registers every 128 K",
+        py::arg("A"), py::arg("B"), py::arg("out"), py::arg("alpha") = 1.0, py::arg("status") = py::none());
+  m.def("dot2_gemm", &rc::dot2_gemm, "compensated FP32 GEMM out = x @ rows^T", py::arg("x"), py::arg("rows"),
+        py::arg("out"));
 }

@@ -52,17 +52,84 @@ class ArchiveOptions:
             raise ConfigurationError(f"stream_codec must be one of {codecs.STREAM_CODECS}")
 
 
+FINGERPRINT_PRIME = 2147483629
+#: Elements per fingerprint row tile of the host path (int64 temporaries cover one tile, not the matrix).
+FINGERPRINT_TILE_ELEMENTS = 1 << 24
+#: (column multiplier, row multiplier, square) of the three checksums of each 16-bit part.
+FINGERPRINT_COMBINATIONS = ((37, 101, False), (613, 211, False), (1, 17, True))
+
+
+def _fingerprint_terms_host(source: torch.Tensor) -> torch.Tensor:
+    rows, columns = source.shape
+    wide = source.element_size() == 4
+    column = torch.arange(columns, dtype=torch.int64)
+    weights = [(column * a + 7) % 1021 + 1 for a, _, _ in FINGERPRINT_COMBINATIONS]
+    totals = torch.zeros(6 if wide else 3, dtype=torch.int64)
+    tile_rows = max(1, FINGERPRINT_TILE_ELEMENTS // columns)
+    for start in range(0, rows, tile_rows):
+        bits = source[start:start + tile_rows].contiguous().view(torch.int32 if wide else torch.int16).to(torch.int64)
+        parts = [bits & 0xFFFF, bits >> 16] if wide else [bits]
+        row = torch.arange(start, start + bits.shape[0], dtype=torch.int64)
+        index = 0
+        for part in parts:
+            for (_, b, square), weight in zip(FINGERPRINT_COMBINATIONS, weights):
+                term = part * part if square else part
+                per_row = (term * weight).sum(1).remainder(FINGERPRINT_PRIME)
+                totals[index] += (per_row * ((row * b + 3) % 1019 + 1)).sum()
+                index += 1
+    return totals.remainder(FINGERPRINT_PRIME)
+
+
+def fingerprint_terms(matrix: torch.Tensor) -> torch.Tensor:
+    """Exact modular checksums of a matrix's bit patterns: for each 16-bit part (the value, or the low and high
+    halves of a 32-bit pattern) and combination ``(a, b, square)``, ``sum_rows ((sum_c t(c) w_a(c)) mod p)
+    w_b(row)`` with ``w_a(c) = (a c + 7) mod 1021 + 1`` and ``w_b(r) = (b r + 3) mod 1019 + 1``. CUDA matrices
+    use the fused kernel (csrc/fit/fitter.cu); the host path computes the same integers."""
+    if matrix.ndim != 2 or matrix.numel() == 0:
+        raise ConfigurationError("source fingerprints take a nonempty matrix")
+    if matrix.element_size() not in (2, 4):
+        raise ConfigurationError("source fingerprints support 16- and 32-bit element types")
+    rows, columns = matrix.shape
+    if rows > (1 << 22) or columns > (1 << 14):
+        raise ConfigurationError("source fingerprint geometry exceeds its overflow-free range")
+    source = matrix.detach()
+    if source.is_cuda:
+        from .ops import _ext
+        if _ext.available():
+            from .ops.fitter import fingerprint_partials
+            wide = source.element_size() == 4
+            return fingerprint_partials(source, 0, FINGERPRINT_PRIME).sum(0)[:6 if wide else 3].remainder(
+                FINGERPRINT_PRIME)
+    return _fingerprint_terms_host(source.cpu())
+
+
+def _fingerprint_text(matrix: torch.Tensor, values) -> str:
+    rows, columns = matrix.shape
+    return f"fp1:{rows}x{columns}:{matrix.dtype}:" + "".join(f"{int(v):08x}" for v in values)
+
+
 def source_fingerprint(matrix: torch.Tensor) -> str:
-    """Exact content identity of a source matrix: SHA-256 of its dtype, shape and raw bytes."""
-    value = matrix.detach()
-    header = f"{str(value.dtype).removeprefix('torch.')}:{list(value.shape)}".encode()
-    digest = hashlib.sha256(header)
-    digest.update(value.contiguous().view(torch.uint8).reshape(-1).cpu().numpy().tobytes())
-    return digest.hexdigest()
+    """Exact, device-independent integer fingerprint of a matrix's bit patterns (``fp1:RxC:dtype:hex``); it
+    binds observations to their content without a host copy of the matrix (not an integrity hash). Same
+    string form and checksums as reference reelcache/lineage_commit.py:197-271."""
+    return _fingerprint_text(matrix, fingerprint_terms(matrix).tolist())
 
 
 def source_fingerprints(matrices: Mapping[Any, torch.Tensor]) -> dict[Any, str]:
-    return {entry: source_fingerprint(matrix) for entry, matrix in matrices.items()}
+    """Fingerprints of many matrices with one device-to-host read per device."""
+    terms = {entry: fingerprint_terms(matrix) for entry, matrix in matrices.items()}
+    out = {}
+    by_device: dict = {}
+    for entry, value in terms.items():
+        by_device.setdefault(value.device, []).append(entry)
+    for entries in by_device.values():
+        flat = torch.cat([terms[e] for e in entries]).tolist()
+        offset = 0
+        for entry in entries:
+            count = int(terms[entry].numel())
+            out[entry] = _fingerprint_text(matrices[entry], flat[offset:offset + count])
+            offset += count
+    return out
 
 
 @dataclass

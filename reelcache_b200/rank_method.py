@@ -19,8 +19,10 @@ Conventions: canonical matrices ``A[N, C]``; stored row bases ``Q[r, C]`` in FP1
   inherited span and verified on ``A``. The refit rule (``paper``: refit iff the augmented chunk is
   estimated to store more bytes than a fresh fit; ``cumulative``: ski-rental debt) may start a new group.
 
-Energies are accumulated in FP64. The Gram products of bf16 sources run on the sm_100a tcgen05 GEMM
-(bf16 products are exact, FP32 accumulation); fp32 sources use IEEE-FP32 matmuls.
+Energies are accumulated in FP64 (fused square-sum kernel on CUDA). The Gram products of bf16 sources run on
+the sm_100a tcgen05 GEMM (bf16 products are exact, FP32 accumulation); every other product is FP32-accurate
+(:func:`reelcache_b200.exact_blas.mm`: split-bf16 tcgen05 GEMM on CUDA), and the Rayleigh-Ritz eigenproblems
+run on the batched Jacobi kernel (FP64 LAPACK on the host).
 """
 
 from __future__ import annotations
@@ -32,6 +34,7 @@ from typing import Any, Mapping
 
 import torch
 
+from . import exact_blas
 from .errors import ConfigurationError
 from .predictor_registry import RegistryView
 from .types import (RANK_BUCKET, ActiveBasisBinding, CodecSpec, EnergyReport, EnergyTargets, FitObservation,
@@ -130,18 +133,43 @@ class RankMethodConfig:
 
 
 def gram(x: torch.Tensor) -> torch.Tensor:
-    """FP32 ``X^T X`` of ``x[N, C]``: tcgen05 GEMM for bf16 CUDA sources (exact products, FP32
-    accumulation), IEEE-FP32 matmul otherwise."""
+    """FP32 ``X^T X`` of ``x[N, C]``: one tcgen05 bf16 GEMM for bf16 CUDA sources (exact products,
+    partials promoted to IEEE FP32 adds every 128 rows), the FP32-accurate split GEMM of :mod:`exact_blas`
+    otherwise."""
     if x.is_cuda and x.dtype == torch.bfloat16 and x.shape[0] % 8 == 0:
         from .ops import _ext
         if _ext.available():
-            from .ops.gemm import matmul_tn
+            from .ops.fitter import matmul_promoted
             xt = x.t().contiguous()
-            g = matmul_tn(xt, xt, out_dtype=torch.float32)
+            g = matmul_promoted(xt, xt)
             return 0.5 * (g + g.t())
-    xf = x.float()
-    g = xf.t() @ xf
-    return 0.5 * (g + g.t())
+    return exact_blas.gram(x)
+
+
+def _sum_squares(x: torch.Tensor, r: torch.Tensor | None = None) -> torch.Tensor:
+    """Device FP64 ``[sum x^2, sum (x - r)^2]`` (the fused square-sum kernel on CUDA)."""
+    if x.is_cuda:
+        from .ops import _ext
+        if _ext.available():
+            from .ops.fitter import sq_partials
+            return sq_partials(x, r).sum(0)[:2]
+    xf = x.double()
+    resid = (xf - r.double()).square().sum() if r is not None else torch.zeros((), dtype=torch.float64)
+    return torch.stack([xf.square().sum(), resid])
+
+
+def _rr_eigh(t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Descending eigenvalues (FP64) and column eigenvectors (FP32) of a symmetric ``k x k`` matrix: the
+    sm_100a Jacobi kernel on CUDA for k <= 160, FP64 LAPACK/cuSOLVER otherwise."""
+    from .gpu_fitting import JACOBI_MAX_N, jacobi_rows_eigh
+    if t.is_cuda and t.shape[0] <= JACOBI_MAX_N:
+        from .ops import _ext
+        if _ext.available():
+            values, rows = jacobi_rows_eigh(t.float().unsqueeze(0))
+            return values[0].flip(0).double(), rows[0].flip(0).t().contiguous()
+    values, vectors = torch.linalg.eigh(t.double())
+    order = torch.argsort(values, descending=True)
+    return values[order], vectors[:, order].float()
 
 
 def _orthonormalize(b: torch.Tensor) -> torch.Tensor:
@@ -163,9 +191,9 @@ def anchor_sketch(g: torch.Tensor, m: int, q: int, gen: torch.Generator) -> torc
     """``orth(G^(q+1) Omega)`` with a private Gaussian ``Omega[C, m]``."""
     channels = g.shape[0]
     omega = torch.randn((channels, min(m, channels)), generator=gen, dtype=torch.float32).to(g.device)
-    s = _orthonormalize(g @ omega)
+    s = _orthonormalize(exact_blas.mm(g, omega))
     for _ in range(q):
-        s = _orthonormalize(g @ s)
+        s = _orthonormalize(exact_blas.mm(g, s))
     return s
 
 
@@ -173,7 +201,7 @@ def span_energy(g: torch.Tensor, s: torch.Tensor, total: float) -> float:
     """``||A S||^2 / ||A||^2 = trace(S^T G S) / trace(G)`` for column-orthonormal ``S``."""
     if total <= 0:
         return 1.0
-    return float(((g @ s) * s).sum(dtype=torch.float64)) / total
+    return float((exact_blas.mm(g, s) * s).sum(dtype=torch.float64)) / total
 
 
 def fp16_rows(directions: torch.Tensor) -> torch.Tensor:
@@ -185,13 +213,15 @@ def stored_energy(x: torch.Tensor, rows: torch.Tensor, total: float, tile_rows: 
     """Energy of the actual stored representation: FP16 ``rows``, FP32 ``P = A Q^T``, direct residual
     ``||A - P Q||^2`` accumulated in FP64 over row tiles. Returns (energy, P)."""
     q = rows.float()
+    qt = q.t()
     coefficients = torch.empty((x.shape[0], rows.shape[0]), dtype=torch.float32, device=x.device)
-    residual = torch.zeros((), dtype=torch.float64, device=x.device)
+    residual = None
     for start in range(0, x.shape[0], tile_rows):
-        a = x[start:start + tile_rows].float()
-        p = a @ q.t()
+        a = x[start:start + tile_rows]
+        p = exact_blas.mm(a, qt)
         coefficients[start:start + tile_rows] = p
-        residual += (a - p @ q).square().sum(dtype=torch.float64)
+        part = _sum_squares(a, exact_blas.mm(p, q))[1]
+        residual = part if residual is None else residual + part
     if total <= 0:
         return 1.0, coefficients
     return 1.0 - float(residual) / total, coefficients
@@ -223,15 +253,14 @@ def fit_directions(g: torch.Tensor, wanted: int, cfg: RankMethodConfig, gen: tor
     if warm is not None:
         cols = min(k, warm.shape[1])
         start[:, :cols] = warm[:, :cols]
-    b = _orthonormalize(g @ start)
+    b = _orthonormalize(exact_blas.mm(g, start))
     for _ in range(cfg.topk_steps):
-        b = _orthonormalize(g @ b)
-    t = b.t() @ g @ b
+        b = _orthonormalize(exact_blas.mm(g, b))
+    t = exact_blas.mm(b.t(), exact_blas.mm(g, b))
     t = 0.5 * (t + t.t())
-    values, vectors = torch.linalg.eigh(t.double())
-    order = torch.argsort(values, descending=True)
-    directions = (b.double() @ vectors[:, order]).float()
-    return Fit(_orthonormalize(directions), values[order].clamp_min(0), False)
+    values, vectors = _rr_eigh(t)
+    directions = exact_blas.mm(b, vectors)
+    return Fit(_orthonormalize(directions), values.clamp_min(0), False)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -343,7 +372,7 @@ def plan_matrix(matrix: torch.Tensor, context: TensorContext, cfg: RankMethodCon
     x = matrix.reshape(context.token_count, context.channels)
     tokens, channels = x.shape
     target = cfg.targets.for_target(key.target)
-    total = float(x.float().square().sum(dtype=torch.float64))
+    total = float(_sum_squares(x)[0])
     fingerprint = model_fingerprint or context.model.fingerprint
     pkey_fresh = PredictorKey(fingerprint, key.layer, key.target, tokens, channels, cfg.solver, "sketch", "fresh")
     pkey_resid = replace(pkey_fresh, regime="residual")
@@ -403,8 +432,8 @@ def plan_matrix(matrix: torch.Tensor, context: TensorContext, cfg: RankMethodCon
                               {"inherited_energy": energy_all, "planner_seconds": time.perf_counter() - started})
         # augment: fit the residual at (E_t - e) / (1 - e)
         q = inherited_rows.float()
-        residual = x.float() - coefficients_all @ q
-        r_total = float(residual.square().sum(dtype=torch.float64))
+        residual = x.float() - exact_blas.mm(coefficients_all, q)
+        r_total = float(_sum_squares(residual)[0])
         residual_target = min(max((target - energy_all) / max(1.0 - energy_all, 1e-300), 1e-6), 1.0)
         rg = gram(residual)
         new, report, coefficients, fields, details = _fresh(
@@ -413,7 +442,7 @@ def plan_matrix(matrix: torch.Tensor, context: TensorContext, cfg: RankMethodCon
         # re-orthogonalize the new rows against the inherited span (two Gram-Schmidt passes in FP32)
         w = new.float()
         for _ in range(2):
-            w = w - (w @ q.t()) @ q
+            w = w - exact_blas.mm(exact_blas.mm(w, q.t()), q)
         w = _orthonormalize(w.t()).t()
         new = w.to(torch.float16)
         rows = torch.cat([inherited_rows, new], 0)
