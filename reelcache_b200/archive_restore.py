@@ -186,6 +186,8 @@ class LineageRestorer:
                 record = self.runtime.load_record(record_ref)
                 if record.codec.kind == "raw":
                     raise UnsupportedError("RAW history restores through RawLineageRestorer")
+                if record.codec.kind == "svd":
+                    raise UnsupportedError("SVD-only (factor pack) history restores through FactorLineageRestorer")
                 packet_ref = record.packet_ref
                 tiles[entry] = (record.decision["packet"]["tile"], record)
             entries.append(HistoryEntry(piece, packet_ref, tiles))
@@ -391,3 +393,177 @@ class _Null:
 
     def __exit__(self, *args):
         return False
+
+
+# ---------------------------------------------------------------------------------------------------------
+# Restorers of the other representations (reference reelcache/archive_restore.py:1325 SoftwareLineageRestorer,
+# :1396 RawLineageRestorer; reelcache/factor_packs.py:673 FactorLineageRestorer): the same ``restore`` contract
+# as LineageRestorer, built from per-layer ReconstructionJobs run by restore_kernels.reconstruct (the fused
+# sm_100a kernels on CUDA, the reference path on the host).
+# ---------------------------------------------------------------------------------------------------------
+
+
+class JobLineageRestorer:
+    """Base of the per-layer job restorers: ``_prepare(pieces)`` loads what the history needs once, ``_source``
+    gives the (source, basis) of one piece's matrix."""
+
+    kinds: tuple = ()
+
+    def __init__(self, runtime: LineageRuntime, device, *, pin_memory: bool = True):
+        self.runtime = runtime
+        self.device = torch.device(device)
+        self.pin_memory = pin_memory and self.device.type == "cuda"
+        self._bases: dict = {}
+        self.stats_ = {"restores": 0, "jobs": 0, "h2d_bytes": 0}
+
+    def _basis(self, record) -> torch.Tensor:
+        key = (record.basis_version_ref, record.rank_view)
+        hit = self._bases.get(key)
+        if hit is None:
+            hit = self.runtime.basis.assemble(record.basis_version_ref, record.rank_view).to(self.device)
+            self._bases[key] = hit
+        return hit
+
+    def _check(self, record) -> None:
+        if record.codec.kind not in self.kinds:
+            raise UnsupportedError(f"{type(self).__name__} restores {self.kinds} histories, not {record.codec.kind}")
+
+    def _prepare(self, pieces) -> None:
+        return None
+
+    def _source(self, piece, record, rows: slice):
+        raise NotImplementedError
+
+    def jobs(self, pieces, layer: int, destination, rope, *, stream_label: str | None = None) -> list:
+        from . import restore_kernels as rk
+        jobs = []
+        for piece in pieces:
+            tokens = piece.token_end - piece.token_start
+            for target in ("K", "V"):
+                record = self.runtime.load_record(piece.record(MatrixKey(layer, target), stream_label))
+                self._check(record)
+                context = record.context
+                plane = context.height * context.width
+                if piece.offset % plane or tokens % plane:
+                    raise UnsupportedError("partial-frame history ranges are not restorable")
+                source, basis = self._source(piece, record, slice(piece.offset, piece.offset + tokens))
+                view = rk.NativeView(destination(layer, target), "BTHD", piece.token_start)
+                positions = None
+                if target == "K" and context.key_space == "pre_rope":
+                    table, rows = rope(piece)
+                    first = piece.offset // plane
+                    positions = rk.RopePositions(table, (rows[0] + first, rows[1], rows[2]))
+                jobs.append(rk.ReconstructionJob(source, view, (tokens // plane, context.height, context.width),
+                                                 basis, rope=positions))
+        return jobs
+
+    def restore(self, node_ref: str, destination, rope, *, stream=None, overlapped: bool = True, ranges=None,
+                readiness: LayerReadiness | None = None, thread: bool = False,
+                stream_label: str | None = None) -> RestoreResult:
+        """Restore ``node_ref``'s attended history layer by layer (marking ``readiness``)."""
+        from . import restore_kernels as rk
+        started = time.perf_counter()
+        model = self.runtime.model
+        cuda = self.device.type == "cuda"
+        if cuda and stream is None:
+            stream = torch.cuda.Stream(self.device)
+        readiness = readiness or LayerReadiness(model.layers)
+        pieces = self.runtime.resolve_history(node_ref, ranges)
+        for piece in pieces:  # refuse other representations before any work is issued
+            for _, record_ref in piece.entry.records:
+                self._check(self.runtime.load_record(record_ref))
+        self._prepare(pieces)
+        handles = []
+
+        def issue(layer):
+            jobs = self.jobs(pieces, layer, destination, rope, stream_label=stream_label)
+            if jobs:
+                handles.append(rk.reconstruct(jobs, stream=stream))
+                self.stats_["jobs"] += len(jobs)
+
+        self.stats_["restores"] += 1
+        handle = start_overlapped_restore(issue, model.layers, stream=stream if cuda else None,
+                                          thread=thread and overlapped, readiness=readiness)
+        result = RestoreResult(node_ref, readiness, handle, {"pieces": len(pieces),
+                                                             "prepare_seconds": time.perf_counter() - started})
+        result.handles = handles
+        return result
+
+    def stats(self) -> dict[str, Any]:
+        return dict(self.stats_)
+
+
+class RawLineageRestorer(JobLineageRestorer):
+    """Exact RAW histories: each record's dense pre-RoPE matrix is read once from its RAW packet into (pinned)
+    host memory, copied to the device and installed with RoPE by the dense restore kernel (bitwise the stored
+    values, up to the cache dtype)."""
+
+    kinds = ("raw",)
+
+    def __init__(self, runtime: LineageRuntime, device, *, budget_bytes: int = 8 << 30, pin_memory: bool = True):
+        super().__init__(runtime, device, pin_memory=pin_memory)
+        self.budget = budget_bytes
+        self._dense: OrderedDict = OrderedDict()
+        self._bytes = 0
+
+    def dense(self, record) -> torch.Tensor:
+        from . import codecs
+        from .types import EncodedTensor
+        hit = self._dense.get(record.packet_ref)
+        if hit is not None:
+            self._dense.move_to_end(record.packet_ref)
+            return hit
+        packet = self.runtime.load_packet(record.packet_ref)
+        blobs = self.runtime.store.get_many(list(packet["payloads"].values()))
+        payloads = {name: blobs[ref] for name, ref in packet["payloads"].items()}
+        values = codecs.decode_tensor(EncodedTensor(packet["metadata"], payloads), device="cpu")
+        values = values.reshape(record.context.token_count, record.context.channels).contiguous()
+        if self.pin_memory:
+            values = values.pin_memory()
+        self._dense[record.packet_ref] = values
+        self._bytes += values.numel() * values.element_size()
+        while self._bytes > self.budget and len(self._dense) > 1:
+            _, old = self._dense.popitem(last=False)
+            self._bytes -= old.numel() * old.element_size()
+        return values
+
+    def _source(self, piece, record, rows: slice):
+        from . import restore_kernels as rk
+        values = self.dense(record)[rows]
+        if values.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            values = values.float()
+        if self.device.type == "cuda":
+            values = values.to(self.device, non_blocking=self.pin_memory)
+            self.stats_["h2d_bytes"] += values.numel() * values.element_size()
+        return rk.DenseSource(values), None
+
+
+class SoftwareLineageRestorer(JobLineageRestorer):
+    """Node-pack (``svd_hevc``) histories decoded in software on the host (the stream codec's CPU decoder; no
+    prepared-pack cache, decoder pool or staging): the uint8 coefficient tiles and their affines feed the same
+    reconstruction jobs. The portable path (any device) and the oracle of the GPU restorer."""
+
+    kinds = ("svd_hevc",)
+
+    def __init__(self, runtime: LineageRuntime, device, *, pin_memory: bool = False):
+        super().__init__(runtime, device, pin_memory=pin_memory)
+        self._packs: dict = {}
+
+    def _prepare(self, pieces) -> None:
+        self._packs = {}
+        for piece in pieces:
+            for _, record_ref in piece.entry.records:
+                record = self.runtime.load_record(record_ref)
+                if record.codec.kind == "svd_hevc" and record.packet_ref not in self._packs:
+                    self._packs[record.packet_ref] = self.runtime.node_pack(record.packet_ref)[1]
+
+    def _source(self, piece, record, rows: slice):
+        from . import restore_kernels as rk
+        pack = self._packs[record.packet_ref]
+        index = record.decision["packet"]["tile"]
+        pixels = torch.from_numpy(np.array(pack.pixels(index)[rows], copy=True))
+        scale, offset = pack.scale_offset(index)
+        if self.device.type == "cuda":
+            pixels = pixels.to(self.device)
+            self.stats_["h2d_bytes"] += pixels.numel()
+        return rk.CoefficientSource(pixels, scale, offset), self._basis(record)

@@ -284,5 +284,30 @@ def encode_factor_pack(tiles: Sequence[Mapping[str, Any]]) -> EncodedTensor:
                         "sha256": hashlib.sha256(data).hexdigest(), "basis": json_copy(tile["basis"])})
         chunks.append(data)
         offset += len(data)
-    return EncodedTensor({"schema": FACTOR_PACK_SCHEMA, "tiles": entries, "bytes": offset},
+    return EncodedTensor({"schema": FACTOR_PACK_SCHEMA, "tiles": entries, "bytes": offset, "stream_bytes": offset,
+                          "raw_bytes": offset // 2, "stream_codec": "fp16"},
                          {"factors": b"".join(chunks)}, metrics={"bytes": offset})
+
+
+class FactorPack:
+    """Decoded view of a ``reelcache.factor_pack.v1`` packet: per tile its FP16 ``[tokens, rank]`` factors."""
+
+    def __init__(self, metadata: Mapping[str, Any], factors: bytes, *, verify: bool = True):
+        if metadata.get("schema") != FACTOR_PACK_SCHEMA:
+            raise IntegrityError("packet is not a factor pack")
+        if len(factors) != int(metadata["bytes"]):
+            raise IntegrityError("factor pack size differs from its manifest")
+        self.metadata = metadata
+        self.tiles = list(metadata["tiles"])
+        self.raw = np.frombuffer(factors, dtype=np.uint8)
+        if verify:
+            for tile in self.tiles:
+                chunk = factors[tile["offset"]:tile["offset"] + tile["bytes"]]
+                if hashlib.sha256(chunk).hexdigest() != tile["sha256"]:
+                    raise IntegrityError(f"factor pack tile {tile['tile']} fails its hash")
+
+    def factors(self, index: int) -> np.ndarray:
+        tile = self.tiles[index]
+        rank = int(tile["rank"])
+        view = self.raw[tile["offset"]:tile["offset"] + tile["bytes"]].view(np.float16)
+        return view.reshape(-1, rank)

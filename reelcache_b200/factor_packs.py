@@ -1,0 +1,98 @@
+"""FP16 factor packs of the SVD-only baseline representation (the counterpart of reference
+reelcache/factor_packs.py:68-720: ``FactorRestorer`` :462, ``FactorLineageRestorer`` :673).
+
+A ``svd`` node stores, per matrix, its FP16 coefficients ``P[N, r]`` in one ``reelcache.factor_pack.v1``
+packet (tiles with offsets and SHA-256 digests; :class:`reelcache_b200.codecs.FactorPack`) and its basis rows
+in the shared basis-version store. Reconstruction is ``P @ Q``: :class:`FactorRestorer` gives dense matrices
+(FP32-accurate products on CUDA), :class:`FactorLineageRestorer` restores a node's attended history into
+native caches through the fused sm_100a restore kernel (float coefficients: the hi/lo-split FP16 operand,
+RoPE and the cast in the epilogue), with the :class:`~reelcache_b200.archive_restore.LineageRestorer`
+contract.
+"""
+
+from __future__ import annotations
+
+from collections import OrderedDict
+from typing import Any
+
+import numpy as np
+import torch
+
+from .archive_restore import JobLineageRestorer
+from .errors import UnsupportedError
+from .lineage import LineageRuntime
+from .types import MatrixKey
+
+
+class FactorRestorer:
+    """Dense reconstructions of ``svd`` records (decoded packs cached LRU under a byte budget)."""
+
+    def __init__(self, runtime: LineageRuntime, device="cpu", *, budget_bytes: int = 4 << 30):
+        self.runtime = runtime
+        self.device = torch.device(device)
+        self.budget = budget_bytes
+        self._packs: OrderedDict = OrderedDict()
+        self._bytes = 0
+
+    def pack(self, packet_ref: str):
+        hit = self._packs.get(packet_ref)
+        if hit is not None:
+            self._packs.move_to_end(packet_ref)
+            return hit
+        _, pack = self.runtime.factor_pack(packet_ref)
+        self._packs[packet_ref] = pack
+        self._bytes += pack.raw.nbytes
+        while self._bytes > self.budget and len(self._packs) > 1:
+            _, old = self._packs.popitem(last=False)
+            self._bytes -= old.raw.nbytes
+        return pack
+
+    def factors(self, record) -> np.ndarray:
+        """FP16 ``[tokens, rank]`` coefficients of one record."""
+        if record.codec.kind != "svd":
+            raise UnsupportedError("factor restores take svd records")
+        return self.pack(record.packet_ref).factors(record.decision["packet"]["tile"])
+
+    def reconstruct(self, record_ref: str, *, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        """Dense ``[tokens, C]`` pre-RoPE matrix ``P @ Q`` of one record."""
+        from .exact_blas import mm
+        record = self.runtime.load_record(record_ref)
+        p = torch.from_numpy(self.factors(record).astype(np.float32)).to(self.device)
+        q = self.runtime.basis.assemble(record.basis_version_ref, record.rank_view).to(self.device).float()
+        return mm(p, q).to(dtype)
+
+    def history(self, node_ref: str, key: MatrixKey, *, stream: str | None = None, ranges=None) -> torch.Tensor:
+        """Dense history of one matrix over the node's attended ranges."""
+        parts = []
+        for piece in self.runtime.resolve_history(node_ref, ranges):
+            full = self.reconstruct(piece.record(key, stream))
+            parts.append(full[piece.offset:piece.offset + piece.token_end - piece.token_start])
+        if not parts:
+            return torch.zeros((0, self.runtime.model.channels_for(key)), device=self.device)
+        return torch.cat(parts)
+
+
+class FactorLineageRestorer(JobLineageRestorer):
+    """Restores ``svd`` node histories into native caches with the fused restore kernel."""
+
+    kinds = ("svd",)
+
+    def __init__(self, runtime: LineageRuntime, device, *, budget_bytes: int = 4 << 30):
+        super().__init__(runtime, device)
+        self.factors = FactorRestorer(runtime, device, budget_bytes=budget_bytes)
+
+    def _source(self, piece, record, rows: slice):
+        from . import restore_kernels as rk
+        host = np.array(self.factors.factors(record)[rows], copy=True)
+        bound = float(np.abs(host.astype(np.float32)).max(initial=0.0))
+        values = torch.from_numpy(host)
+        if self.device.type == "cuda":
+            values = values.to(self.device)
+            self.stats_["h2d_bytes"] += values.numel() * 2
+        return rk.CoefficientSource(values, bound=bound), self._basis(record)
+
+    def stats(self) -> dict[str, Any]:
+        return {**self.stats_, "packs": len(self.factors._packs), "pack_bytes": self.factors._bytes}
+
+
+__all__ = ["FactorLineageRestorer", "FactorRestorer"]

@@ -452,6 +452,14 @@ class LineageRuntime:
                                   verify=verify)
         return packet, pack
 
+    def factor_pack(self, packet_ref: str, *, verify: bool = True) -> tuple[Mapping[str, Any], codecs.FactorPack]:
+        """(packet manifest, decoded FP16 factor pack) of an SVD-only node."""
+        packet = self.load_packet(packet_ref)
+        if packet["metadata"].get("schema") != codecs.FACTOR_PACK_SCHEMA:
+            raise IntegrityError("packet is not a factor pack")
+        return packet, codecs.FactorPack(packet["metadata"], self.store.get(packet["payloads"]["factors"]),
+                                         verify=verify)
+
     def execution_state(self, node_ref: str, *, device: Any = "cpu") -> dict[str, torch.Tensor]:
         node = self.load_node(node_ref)
         if node.execution_state_ref is None:
@@ -473,6 +481,13 @@ class LineageRuntime:
                 blobs = {name: self.store.get(ref) for name, ref in packet["payloads"].items()}
                 from .types import EncodedTensor
                 values = codecs.decode_tensor(EncodedTensor(packet["metadata"], blobs), device=device).float()
+            elif record.codec.kind == "svd":
+                if record.packet_ref not in packs:
+                    packs[record.packet_ref] = self.factor_pack(record.packet_ref)[1]
+                factors = packs[record.packet_ref].factors(record.decision["packet"]["tile"])
+                coefficients = torch.from_numpy(factors.astype(np.float32)).to(device)
+                basis = self.basis.assemble(record.basis_version_ref, record.rank_view).to(device).float()
+                values = coefficients @ basis
             else:
                 if record.packet_ref not in packs:
                     packs[record.packet_ref] = self.node_pack(record.packet_ref)[1]
@@ -497,7 +512,8 @@ class LineageRuntime:
             packet = self.load_packet(packet_ref)
             sizes = self.store.object_sizes(packet["payloads"].values())
             for name, ref in packet["payloads"].items():
-                key = {"stream": "stream_bytes", "affines": "affine_bytes"}.get(name, "raw_bytes")
+                key = {"stream": "stream_bytes", "affines": "affine_bytes", "factors": "stream_bytes"}.get(
+                    name, "raw_bytes")
                 total[key] += sizes.get(ref, 0)
         parent = self.load_node(node.parent_ref) if node.parent_ref else None
         before = {b.version_ref for _, b in parent.active_basis} if parent else set()

@@ -147,6 +147,7 @@ class StagedTile:
     context: TensorContext
     plan: MatrixPlan
     pixels: np.ndarray | None = None
+    factors: np.ndarray | None = None      # FP16 coefficients of the SVD-only representation
     affine: np.ndarray | None = None
     normalization: Mapping[str, Any] | None = None
 
@@ -205,6 +206,10 @@ class CommitJob:
         spec = self.method.codec
         for staged in self.tiles:
             for tile in staged:
+                if spec.kind == "svd":  # SVD-only baseline: FP16 factors, no quantization
+                    tile.factors = tile.plan.coefficients.detach().to(torch.float16).cpu().numpy()
+                    tile.plan.coefficients = None
+                    continue
                 pixels, affine, layout = codecs.quantize(tile.plan.coefficients, spec.normalization,
                                                          spec.protected_fraction)
                 tile.pixels, tile.affine, tile.normalization = np.ascontiguousarray(pixels), affine, layout
@@ -225,9 +230,13 @@ class CommitJob:
                               "context": tile.context, "codec": CodecSpec(**{**spec.to_dict(), "rank": rank,
                                                                             "inter_prediction": spec.inter_prediction}),
                               "pixels": tile.pixels, "affine": tile.affine, "normalization": tile.normalization,
-                              "basis": codecs.descriptor(view_bytes, rank, tile.context.channels)})
-            self.packs.append(codecs.encode_node_pack(tiles, stream_codec=self.options.stream_codec,
-                                                      details={"chunk_id": self.chunk_id}))
+                              "basis": codecs.descriptor(view_bytes, rank, tile.context.channels),
+                              "coefficients": tile.factors})
+            if spec.kind == "svd":
+                self.packs.append(codecs.encode_factor_pack(tiles))
+            else:
+                self.packs.append(codecs.encode_node_pack(tiles, stream_codec=self.options.stream_codec,
+                                                          details={"chunk_id": self.chunk_id}))
         self.timings["encode"] = time.perf_counter() - started
         return self
 
@@ -289,7 +298,8 @@ class CommitJob:
                         **{**plan.energy.to_dict(), "rank_view": rank})
                     record = MatrixRecord(tile.context, codec, packet_ref, version_refs[tile.entry], rank, energy, None,
                                           {**json_copy(plan.decision_record()),
-                                           "packet": {"tile": index, "stream_codec": self.options.stream_codec}},
+                                           "packet": {"tile": index, "stream_codec": "fp16" if spec.kind == "svd"
+                                                     else self.options.stream_codec}},
                                           packet_tile=index if codec.kind == "svd_hevc" and codec.inter_prediction is False
                                           else None, stream=stream)
                     records[tile.entry] = runtime.put_record(record)

@@ -148,7 +148,7 @@ def test_planner_uses_jacobi_and_fitter_gram_batched():
     plans = plan_chunk(matrices, contexts, cfg, None, {}, {})
     assert gpu_fitting.STATS["jacobi_calls"] > before
     for key, plan in plans.items():
-        assert plan.report.stored_factor_energy >= cfg.targets.for_target(key.target) - 1e-6
+        assert plan.energy.stored_factor_energy >= cfg.targets.for_target(key.target) - 1e-6
     uuid = "GPU-" + str(torch.cuda.get_device_properties(0).uuid).removeprefix("GPU-")
     fitter = gpu_fitting.GPUFitter(gpu_id=0, gpu_uuid=uuid, method="gram_batched")
     items = {key: (matrices[key].float(), contexts[key], 24) for key in matrices}
