@@ -88,6 +88,14 @@ class ArchivePipeline:
         self._failed: dict[str, BaseException] = {}
         self._generated: dict[str, int] = {}
         self._defer = 0
+        # generation holds (generation-first archival): key -> {"opened": t, "record": {...}}
+        self._holds: dict[Any, dict] = {}
+        self._planning = False          # a node is on the GPU (planning / finalization)
+        self._drain_waiters = 0
+        self.hold_max_age = 30.0
+        self.hold_max_backlog = max(1, max_unpublished // 2)
+        self._defer_counts = {"holds_opened": 0, "held_seconds": 0.0, "inflight_waits": 0,
+                              "inflight_wait_seconds": 0.0, "inflight_overlaps": 0, "starvation_overrides": 0}
         self._closed = False
         self._counts = {"submitted": 0, "published": 0, "failed": 0, "cancelled": 0, "backpressure_waits": 0,
                         "backpressure_seconds": 0.0}
@@ -149,9 +157,10 @@ class ArchivePipeline:
                     earlier = [t for t in self._tickets[ticket.lineage] if t.index < ticket.index]
                     if any(not t.done() for t in earlier):
                         continue  # planned after its predecessor is published
-                    if self._defer:
+                    if self._defer or self._held():
                         break
                     self._queue.remove(ticket)
+                    self._planning = True
                     return ticket
                 self.cv.wait(0.05)
 
@@ -166,6 +175,10 @@ class ArchivePipeline:
                 self._plan(ticket)
             except BaseException as error:  # noqa: BLE001 - delivered to the ticket and its lineage
                 self._fail(ticket, error)
+            finally:
+                with self.cv:
+                    self._planning = False
+                    self.cv.notify_all()
 
     def _plan(self, ticket: ArchiveTicket) -> None:
         started = time.perf_counter()
@@ -250,17 +263,22 @@ class ArchivePipeline:
         started = time.monotonic()
         deadline = None if timeout is None else started + timeout
         with self.cv:
-            while True:
-                lineages = [lineage] if lineage is not None else list(self._tickets)
-                failed = [name for name in lineages if name in self._failed]
-                if failed:
-                    raise StateError(f"lineage {failed[0]} has a failed archival: {self._failed[failed[0]]}")
-                if all(t.done() for name in lineages for t in self._tickets.get(name, [])):
-                    return time.monotonic() - started
-                left = None if deadline is None else deadline - time.monotonic()
-                if left is not None and left <= 0:
-                    raise TimeoutError("archival drain timed out")
-                self.cv.wait(0.05 if left is None else min(0.05, left))
+            self._drain_waiters += 1  # a waiting caller overrides generation holds
+            self.cv.notify_all()
+            try:
+                while True:
+                    lineages = [lineage] if lineage is not None else list(self._tickets)
+                    failed = [name for name in lineages if name in self._failed]
+                    if failed:
+                        raise StateError(f"lineage {failed[0]} has a failed archival: {self._failed[failed[0]]}")
+                    if all(t.done() for name in lineages for t in self._tickets.get(name, [])):
+                        return time.monotonic() - started
+                    left = None if deadline is None else deadline - time.monotonic()
+                    if left is not None and left <= 0:
+                        raise TimeoutError("archival drain timed out")
+                    self.cv.wait(0.05 if left is None else min(0.05, left))
+            finally:
+                self._drain_waiters -= 1
 
     def cancel(self, lineage: str) -> int:
         """Retire the lineage's unpublished work (queued or not yet stored); returns the count."""
@@ -306,10 +324,72 @@ class ArchivePipeline:
                 self._defer -= 1
                 self.cv.notify_all()
 
+    # -- generation holds ---------------------------------------------------------------------------------------
+
+    def _held(self) -> bool:
+        """Whether an open generation hold keeps new GPU archival work from starting (called under ``cv``).
+        The starvation guard lets work through when the oldest hold is older than ``hold_max_age``, the
+        queued backlog reaches ``hold_max_backlog`` or a caller waits in :meth:`drain`."""
+        if not self._holds:
+            return False
+        oldest = min(h["opened"] for h in self._holds.values())
+        if (time.monotonic() - oldest > self.hold_max_age or len(self._queue) >= self.hold_max_backlog
+                or self._drain_waiters):
+            self._defer_counts["starvation_overrides"] += 1
+            return False
+        return True
+
+    def open_generation(self, key: Any, *, inflight: str = "wait", timeout: float | None = 60.0) -> dict:
+        """Open a generation hold: no new GPU archival work starts until :meth:`close_generation`. With
+        ``inflight="wait"`` a node already on the GPU finishes first (the wait is returned as
+        ``archival_defer_wait``); ``"overlap"`` opens at once and records the overlap."""
+        if inflight not in ("wait", "overlap"):
+            raise ConfigurationError("inflight must be 'wait' or 'overlap'")
+        record = {"archival_defer_wait": 0.0, "inflight_overlaps": 0}
+        with self.cv:
+            if key in self._holds:
+                return self._holds[key]["record"]
+            self._holds[key] = {"opened": time.monotonic(), "record": record}
+            self._defer_counts["holds_opened"] += 1
+            if self._planning:
+                if inflight == "overlap":
+                    record["inflight_overlaps"] = 1
+                    self._defer_counts["inflight_overlaps"] += 1
+                else:
+                    started = time.monotonic()
+                    deadline = None if timeout is None else started + timeout
+                    while self._planning and (deadline is None or time.monotonic() < deadline):
+                        self.cv.wait(0.01)
+                    waited = time.monotonic() - started
+                    record["archival_defer_wait"] = waited
+                    self._defer_counts["inflight_waits"] += 1
+                    self._defer_counts["inflight_wait_seconds"] += waited
+        return record
+
+    def close_generation(self, key: Any) -> dict | None:
+        with self.cv:
+            hold = self._holds.pop(key, None)
+            if hold is None:
+                return None
+            held = time.monotonic() - hold["opened"]
+            hold["record"]["held_seconds"] = held
+            self._defer_counts["held_seconds"] += held
+            self.cv.notify_all()
+            return hold["record"]
+
+    @contextmanager
+    def generation(self, key: Any, *, inflight: str = "wait"):
+        record = self.open_generation(key, inflight=inflight)
+        try:
+            yield record
+        finally:
+            self.close_generation(key)
+
     def stats(self) -> dict:
         with self.cv:
             return {**self._counts, "unpublished": self._unpublished(), "lineages": len(self._tickets),
-                    "failed_lineages": sorted(self._failed), "encoders": self._encoders.stats()}
+                    "failed_lineages": sorted(self._failed), "encoders": self._encoders.stats(),
+                    "generation_defer": {**self._defer_counts, "open_holds": len(self._holds)}}
 
     def close(self, *, drain: bool = True, timeout: float | None = None) -> None:
         if drain:

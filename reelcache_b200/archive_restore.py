@@ -208,11 +208,13 @@ class LineageRestorer:
     def build_program(self, node_ref: str, destination: Callable[[int, str], torch.Tensor],
                       rope: Callable[[ResolvedPiece], tuple[RopeTable, tuple]], *, stream=None, ranges=None,
                       stream_label: str | None = None, layers: Sequence[int] | None = None,
-                      device_raw: dict | None = None) -> RestoreProgram:
+                      device_raw: dict | None = None, slot_of: Callable[[ResolvedPiece], int] | None = None
+                      ) -> RestoreProgram:
         """Plan the restore of ``node_ref``: one job per (layer, K/V, piece) reading the history's packs
         from ``device_raw`` (packet ref -> device uint8 copy of the pack; default: copied now on
         ``stream``). ``destination(layer, "K"|"V")`` returns the native BTHD cache tensor
-        ``[1, capacity, heads, head_dim]``; ``rope(piece)`` returns the (table, (t_row, h_row, w_row)) of its positions."""
+        ``[1, capacity, heads, head_dim]``; ``rope(piece)`` returns the (table, (t_row, h_row, w_row)) of its positions;
+        ``slot_of(piece)`` the first cache row of the piece (default: its global token index)."""
         stream = stream or torch.cuda.current_stream(self.device)
         entries = self.history(node_ref, ranges)
         model = self.runtime.model
@@ -254,7 +256,8 @@ class LineageRestorer:
                     frames = tokens // (context.height * context.width)
                     grid = (frames, context.height, context.width)
                     basis, qmax = self.bases.get(record.basis_version_ref, record.rank_view, stream)
-                    slot = rows[piece.token_start:piece.token_end]  # [tokens, heads, head_dim]
+                    first_row = piece.token_start if slot_of is None else slot_of(piece)
+                    slot = rows[first_row:first_row + tokens]  # [tokens, heads, head_dim]
                     job = {"kind": "u8", "values": values, "tokens": tokens, "rank": record.rank_view,
                            "grid": grid, "basis": basis, "qmax": qmax, "scale": prepared.scales[tile_index],
                            "offset": prepared.offsets[tile_index],
@@ -270,7 +273,7 @@ class LineageRestorer:
                     program.add(job, group=layer)
         return program
 
-    def _plan_key(self, node_ref, destination, rope, ranges):
+    def _plan_key(self, node_ref, destination, rope, ranges, slot_of=None):
         """Identity of a restore plan: the node, its ranges, every destination tensor (address, shape,
         strides, dtype) and every piece's RoPE table and positions."""
         model = self.runtime.model
@@ -282,7 +285,8 @@ class LineageRestorer:
         ropes = []
         for item in self.history(node_ref, ranges):
             table, rows = rope(item.piece)
-            ropes.append((id(table), table._stamp(), tuple(rows)))
+            ropes.append((id(table), table._stamp(), tuple(rows),
+                          None if slot_of is None else slot_of(item.piece)))
         return (node_ref, None if ranges is None else tuple(map(tuple, ranges)), tuple(dests), tuple(ropes))
 
     def _layer_copies(self, entries, layer_count):
@@ -302,8 +306,8 @@ class LineageRestorer:
             copies.append(sorted(spans.items()))
         return copies
 
-    def _plan(self, node_ref, destination, rope, stream, ranges):
-        key = self._plan_key(node_ref, destination, rope, ranges)
+    def _plan(self, node_ref, destination, rope, stream, ranges, slot_of=None):
+        key = self._plan_key(node_ref, destination, rope, ranges, slot_of)
         with self._lock:
             plan = self._plans.get(key)
             if plan is not None:
@@ -316,7 +320,8 @@ class LineageRestorer:
             if item.packet_ref not in device_raw:
                 prepared = self.prepared_pack(item.packet_ref)
                 device_raw[item.packet_ref] = torch.empty(prepared.nbytes, dtype=torch.uint8, device=self.device)
-        program = self.build_program(node_ref, destination, rope, stream=stream, ranges=ranges, device_raw=device_raw)
+        program = self.build_program(node_ref, destination, rope, stream=stream, ranges=ranges, device_raw=device_raw,
+                                     slot_of=slot_of)
         with torch.cuda.stream(stream):
             program.prepare(run_aux=False)
         plan = _RestorePlan(program, device_raw, self._layer_copies(entries, self.runtime.model.layers),
@@ -331,7 +336,8 @@ class LineageRestorer:
         return plan
 
     def restore(self, node_ref: str, destination, rope, *, stream=None, overlapped: bool = True, ranges=None,
-                readiness: LayerReadiness | None = None, thread: bool = False) -> RestoreResult:
+                readiness: LayerReadiness | None = None, thread: bool = False,
+                slot_of: Callable[[ResolvedPiece], int] | None = None) -> RestoreResult:
         """Restore ``node_ref``'s history; returns a :class:`RestoreResult` whose readiness marks each layer
         (the caller's forward waits per layer). All GPU work runs on ``stream`` (default: a side stream).
 
@@ -344,7 +350,7 @@ class LineageRestorer:
         model = self.runtime.model
         stream = stream or torch.cuda.Stream(self.device)
         readiness = readiness or LayerReadiness(model.layers)
-        plan = self._plan(node_ref, destination, rope, stream, ranges)
+        plan = self._plan(node_ref, destination, rope, stream, ranges, slot_of)
         program = plan.program
         copy_stream = self._copy_stream()
         if plan.done is not None:
@@ -434,7 +440,8 @@ class JobLineageRestorer:
     def _source(self, piece, record, rows: slice):
         raise NotImplementedError
 
-    def jobs(self, pieces, layer: int, destination, rope, *, stream_label: str | None = None) -> list:
+    def jobs(self, pieces, layer: int, destination, rope, *, stream_label: str | None = None,
+             slot_of: Callable[[ResolvedPiece], int] | None = None) -> list:
         from . import restore_kernels as rk
         jobs = []
         for piece in pieces:
@@ -447,7 +454,8 @@ class JobLineageRestorer:
                 if piece.offset % plane or tokens % plane:
                     raise UnsupportedError("partial-frame history ranges are not restorable")
                 source, basis = self._source(piece, record, slice(piece.offset, piece.offset + tokens))
-                view = rk.NativeView(destination(layer, target), "BTHD", piece.token_start)
+                first_row = piece.token_start if slot_of is None else slot_of(piece)
+                view = rk.NativeView(destination(layer, target), "BTHD", first_row)
                 positions = None
                 if target == "K" and context.key_space == "pre_rope":
                     table, rows = rope(piece)
@@ -459,7 +467,8 @@ class JobLineageRestorer:
 
     def restore(self, node_ref: str, destination, rope, *, stream=None, overlapped: bool = True, ranges=None,
                 readiness: LayerReadiness | None = None, thread: bool = False,
-                stream_label: str | None = None) -> RestoreResult:
+                stream_label: str | None = None, slot_of: Callable[[ResolvedPiece], int] | None = None
+                ) -> RestoreResult:
         """Restore ``node_ref``'s attended history layer by layer (marking ``readiness``)."""
         from . import restore_kernels as rk
         started = time.perf_counter()
@@ -476,7 +485,7 @@ class JobLineageRestorer:
         handles = []
 
         def issue(layer):
-            jobs = self.jobs(pieces, layer, destination, rope, stream_label=stream_label)
+            jobs = self.jobs(pieces, layer, destination, rope, stream_label=stream_label, slot_of=slot_of)
             if jobs:
                 handles.append(rk.reconstruct(jobs, stream=stream))
                 self.stats_["jobs"] += len(jobs)

@@ -19,6 +19,7 @@ events), the restore's route and statistics, the archive tickets and frontiers.
 
 from __future__ import annotations
 
+import contextlib
 import threading
 import time
 from typing import Any
@@ -28,6 +29,7 @@ import torch
 from ...errors import ConfigurationError, StateError
 from .capture import CleanChunkBuilder
 from .config import ReelCacheRuntimeConfig
+from .generation_defer import GenerationDefer
 from .lineage_archive import LineageSessionArchive
 from .nodes import chunk_nodes
 from .profiles import ModelProfile
@@ -48,6 +50,9 @@ class CausalWanKVBridge:
         self.sessions = SGLangSessionController(self.archive)
         self.cache_chunks = cache_chunks
         self.telemetry = WorkloadTelemetry(enabled=config.workload_telemetry)
+        self.defer = GenerationDefer.from_config(config, getattr(self.archive, "pipeline", None))
+        self._requests = 0
+        self._current = None
         self._lock = threading.RLock()
 
     # -- requests -------------------------------------------------------------------------------------------------
@@ -60,6 +65,11 @@ class CausalWanKVBridge:
             raise ConfigurationError("chunks must be a nonnegative integer")
         started = time.perf_counter()
         span = self.telemetry.begin(session_id, action)
+        self._requests += 1
+        key = (session_id, self._requests)
+        self._current = key
+        if self.defer is not None:
+            self.defer.begin(key)
         with self._lock:
             if action == "create":
                 state = self.sessions.create(session_id)
@@ -74,17 +84,21 @@ class CausalWanKVBridge:
             self.sessions.check_ready(state)
             state.status = "running"
         try:
-            report = self._run(state, chunks, seed, started, span)
+            report = self._run(state, chunks, seed, started, span, key)
         except BaseException:
             state.status = "failed" if state.failure is not None else "idle"
+            if self.defer is not None:
+                self.defer.finish(key)
             raise
         state.status = "idle"
+        if self.defer is not None:
+            report["archival_defer"] = self.defer.finish(key)
         report["action"] = action
         report["wall_ms"] = (time.perf_counter() - started) * 1e3
         self.telemetry.end(span, report)
         return report
 
-    def _run(self, state, chunks: int, seed: int, started: float, span) -> dict:
+    def _run(self, state, chunks: int, seed: int, started: float, span, key=None) -> dict:
         start_chunk = state.generated
         need = start_chunk + chunks
         cache = state.resident
@@ -122,6 +136,8 @@ class CausalWanKVBridge:
             if i == 0:
                 if install is not None:
                     restore_stats = install.join() or install.stats
+                if self.defer is not None:
+                    self.defer.after_restore(key)  # generation starts once the restore has returned
                 if cuda:
                     first_event = torch.cuda.Event(enable_timing=True)
                     first_event.record()
@@ -156,6 +172,21 @@ class CausalWanKVBridge:
         rows = cache["k"][0].shape[0] if isinstance(cache, dict) else cache.k[0].shape[1]
         return rows // self.profile.chunk_tokens
 
+    @contextlib.contextmanager
+    def memory_critical_section(self, reason: str = "decode", key=None):
+        """A memory-critical section of the current request (the engine's VAE decode): new GPU archival work
+        is deferred inside it (``defer_archival_during_decode``), and a decode seam closes the request's
+        generation hold at its exit."""
+        key = key if key is not None else self._current
+        defer_gpu = (self.config.defer_archival_during_decode and getattr(self.archive, "pipeline", None)
+                     is not None)
+        with contextlib.ExitStack() as stack:
+            if defer_gpu:
+                stack.enter_context(self.archive.pipeline.defer_gpu_work())
+            if self.defer is not None and key is not None:
+                stack.enter_context(self.defer.decode_seam(key, reason))
+            yield
+
     # -- controls -----------------------------------------------------------------------------------------------
 
     def pause(self, session_id: str, timeout: float | None = None) -> dict:
@@ -173,4 +204,6 @@ class CausalWanKVBridge:
         state.resident_chunks = 0
 
     def shutdown(self) -> None:
+        if self.defer is not None:
+            self.defer.close()
         self.archive.close()

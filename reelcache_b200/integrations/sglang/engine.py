@@ -121,17 +121,23 @@ class CausalWanEngine:
         return latents
 
     def install(self, cache, archive, head_ref: str, plan, *, overlapped: bool = True) -> InstallResult:
+        from .restore import LineageInstall
         cfg = self.model.cfg
 
         def destination(layer, which):
             return cache.k[layer] if which == "K" else cache.v[layer]
 
-        def rope(piece):
-            chunk = piece.entry.token_start // cfg.chunk_tokens
-            return self.model.rope, (cfg.frames_per_chunk * chunk, 0, 0)
+        install = LineageInstall(plan=plan, destination=destination,
+                                 rope_rows=lambda chunk: (cfg.frames_per_chunk * chunk, 0, 0), table=self.model.rope,
+                                 tokens_per_frame=cfg.grid_h * cfg.grid_w)
+        result = archive.restore_into(head_ref, install, plan, overlapped=overlapped)
 
-        result = archive.restore_into(head_ref, destination, rope, plan, overlapped=overlapped)
-        return InstallResult(lambda layer: result.wait(layer), result.join, result.stats)
+        def join():
+            stats = result.join()
+            result.lease.close()
+            return stats
+
+        return InstallResult(lambda layer: result.wait(layer), join, result.stats)
 
 
 def model_identity_for(profile: ModelProfile, fingerprint: str) -> ModelIdentity:

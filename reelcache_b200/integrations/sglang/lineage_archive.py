@@ -144,13 +144,57 @@ class LineageSessionArchive:
         self.stats_["archive_installs"] += archive
         return {"raw_spans": raw, "archive_spans": archive, "attended_tokens": plan.attended_tokens}
 
-    def restore_into(self, head_ref: str, destination, rope, plan, *, overlapped: bool = True):
-        """Fused sm_100a restore of the plan's history into native caches (GPU)."""
+    def restore_into(self, head_ref: str, install, plan, *, overlapped: bool = True):
+        """Install the plan's history into native caches (GPU): spans whose nodes the raw tier still holds go
+        through the dense RoPE-and-store kernel (exact captured rows), the rest through the fused sm_100a
+        restorer (``install`` is a :class:`~.restore.LineageInstall`). Returns a restore result whose
+        readiness covers both sources; ``result.lease`` owns the raw-tier pins until the install completes."""
+        from ...archive_restore import RestoreResult
+        from ...overlapped_restore import LayerReadiness
+        from .restore import AttentionKVLease, restore_dense
+        from .visibility import VisibilityPlan
         if self.restorer is None:
             raise ConfigurationError("the fused restore needs a CUDA device")
-        self.stats_["archive_installs"] += len(plan.spans)
-        return self.restorer.restore(head_ref, destination, rope, overlapped=overlapped, ranges=plan.ranges(),
-                                     thread=overlapped)
+        lease = AttentionKVLease(description={"head": head_ref, "attended_tokens": plan.attended_tokens})
+        raw_spans, archive_spans, leases = [], [], {}
+        for span in plan.spans:
+            raw = None
+            if self.raw_tier is not None and self.config.raw_restore == "prefer":
+                raw = leases.get(span.node_ref) or self.raw_tier.lookup(span.node_ref)
+            if raw is not None:
+                if span.node_ref not in leases:
+                    leases[span.node_ref] = raw
+                    lease.track(finalizer=raw.release)
+                raw_spans.append(span)
+            else:
+                archive_spans.append(span)
+        sources = (("restore",) if archive_spans else ()) + (("raw",) if raw_spans else ())
+        layers = self.profile.num_layers
+        readiness = LayerReadiness(layers, sources=sources or ("restore",))
+        stream = torch.cuda.Stream(self.device)
+        result = None
+        if raw_spans:
+            sub = VisibilityPlan(plan.next_chunk, tuple(raw_spans))
+            restore_dense(lease, plan=sub, destination=install.destination,
+                          rope=lambda span: (install.table, install._rope_rows(span.chunk_index)),
+                          rows_of=lambda span, key: leases[span.node_ref].tensors[key][
+                              span.node_offset:span.node_offset + span.length],
+                          grid=self.profile.grid, layers=layers, stream=stream, readiness=readiness)
+            self.stats_["raw_installs"] += len(raw_spans)
+        if archive_spans:
+            sub = VisibilityPlan(plan.next_chunk, tuple(archive_spans))
+            archive_install = type(install)(plan=sub, destination=install.destination, rope_rows=install._rope_rows,
+                                            table=install.table, tokens_per_frame=install.tokens_per_frame)
+            result = archive_install.restore(self.restorer, head_ref, overlapped=overlapped, thread=overlapped,
+                                             readiness=readiness, stream=stream)
+            result.lease = lease
+            self.stats_["archive_installs"] += len(archive_spans)
+        if result is None:
+            result = RestoreResult(head_ref, readiness, None, {"raw_spans": len(raw_spans)})
+            result.lease = lease
+        result.stats["raw_spans"] = len(raw_spans)
+        result.stats["archive_spans"] = len(archive_spans)
+        return result
 
     # -- lifecycle ------------------------------------------------------------------------------------------------
 
