@@ -414,3 +414,166 @@ class _Null:
 
     def __exit__(self, *args):
         return False
+
+
+class RawArchive:
+    """Exact RAW archival of clean chunks with the producer interface of :class:`ArchivePipeline` (the
+    counterpart of reference reelcache/archive_pipeline.py:2685 ``RawArchive`` and the write-behind RAW
+    session archive of reelcache/integrations/sglang/archive.py).
+
+    Synchronous (default): ``submit`` commits the chunk's captured pre-RoPE K/V bit for bit
+    (:meth:`LineageRuntime.commit_raw_node`) before it returns, so tickets are already published.
+    ``write_behind=True`` (``representation="raw_offload"``): the captured tensors are adopted by the raw tier and
+    one ordered background writer commits them; the tier entry becomes evictable only after its node is
+    published, and ``submit`` waits only while the writer's queue is full. RAW is the identity reference of the
+    capture / restore / install path, not a compression path."""
+
+    def __init__(self, runtime: LineageRuntime, *, raw_tier=None, write_behind: bool = False, max_unwritten: int = 4):
+        if type(max_unwritten) is not int or max_unwritten < 1:
+            raise ConfigurationError("max_unwritten must be a positive integer")
+        if write_behind and raw_tier is None:
+            raise ConfigurationError("write-behind RAW archival needs a raw tier")
+        self.runtime, self.raw_tier, self.write_behind = runtime, raw_tier, write_behind
+        self.max_unpublished = max_unwritten
+        self.cv = threading.Condition()
+        self._queue: deque[ArchiveTicket] = deque()
+        self._tickets: dict[str, list[ArchiveTicket]] = {}
+        self._failed: dict[str, BaseException] = {}
+        self._closed = False
+        self._counts = {"submitted": 0, "published": 0, "failed": 0, "payload_bytes": 0, "commit_seconds": 0.0,
+                        "writer_waits": 0}
+        self._writer = None
+        if write_behind:
+            self._writer = threading.Thread(target=self._writer_loop, name="reelcache-raw-writer", daemon=True)
+            self._writer.start()
+
+    def _commit(self, ticket: ArchiveTicket, matrices) -> None:
+        started = time.perf_counter()
+        commit = self.runtime.commit_raw_node(ticket.lineage, ticket.chunk_id, matrices, ticket.contexts,
+                                              execution_state=ticket.execution_state)
+        ticket.node_ref = commit.node_ref
+        ticket.state = "published"
+        with self.cv:
+            self._counts["published"] += 1
+            self._counts["commit_seconds"] += time.perf_counter() - started
+            self._counts["payload_bytes"] += sum(m.numel() * m.element_size() for m in matrices.values())
+        if ticket.raw_token is not None:
+            self.raw_tier.published(ticket.raw_token, commit.node_ref)
+        ticket._done.set()
+
+    def submit(self, lineage: str, chunk_id: str, matrices: Mapping[Any, torch.Tensor], contexts, *,
+               execution_state=None, capture_event=None, holder: Any = None) -> ArchiveTicket:
+        if self._closed:
+            raise StateError("the RAW archive is closed")
+        if lineage in self._failed:
+            raise StateError(f"lineage {lineage} has a failed archival: {self._failed[lineage]}")
+        if capture_event is not None:
+            capture_event.synchronize()
+        with self.cv:
+            index = len(self._tickets.setdefault(lineage, []))
+            ticket = ArchiveTicket(lineage, chunk_id, index, None, contexts, execution_state)
+            self._tickets[lineage].append(ticket)
+            self._counts["submitted"] += 1
+        if not self.write_behind:
+            try:
+                self._commit(ticket, matrices)
+            except BaseException as error:  # noqa: BLE001 - delivered to the ticket and raised
+                self._fail(ticket, error)
+                raise
+            return ticket
+        with self.cv:
+            while sum(1 for t in self._queue if not t.done()) >= self.max_unpublished and not self._closed:
+                self._counts["writer_waits"] += 1
+                self.cv.wait(0.05)
+        ticket.raw_token = self.raw_tier.admit(matrices, chunk_id, holder)
+        with self.cv:
+            self._queue.append(ticket)
+            self.cv.notify_all()
+        return ticket
+
+    def _writer_loop(self) -> None:
+        while True:
+            with self.cv:
+                while not self._queue and not self._closed:
+                    self.cv.wait(0.05)
+                if not self._queue:
+                    return
+                ticket = self._queue[0]
+            try:
+                if ticket.lineage in self._failed:
+                    raise StateError("an earlier chunk of the lineage failed")
+                self._commit(ticket, self.raw_tier.source(ticket.raw_token))
+            except BaseException as error:  # noqa: BLE001 - delivered to the ticket and its lineage
+                self._fail(ticket, error)
+            with self.cv:
+                self._queue.popleft()
+                self.cv.notify_all()
+
+    def _fail(self, ticket: ArchiveTicket, error: BaseException) -> None:
+        ticket.state, ticket.error = "failed", error
+        with self.cv:
+            self._failed.setdefault(ticket.lineage, error)
+            self._counts["failed"] += 1
+        if ticket.raw_token is not None:
+            self.raw_tier.failed(ticket.raw_token)
+        ticket._done.set()
+
+    def frontiers(self, lineage: str) -> dict:
+        with self.cv:
+            tickets = self._tickets.get(lineage, [])
+            published = [t for t in tickets if t.state == "published"]
+            return {"generated": len(tickets), "published": len(published),
+                    "published_ref": published[-1].node_ref if published else None,
+                    "error": None if lineage not in self._failed else repr(self._failed[lineage])}
+
+    def drain(self, lineage: str | None = None, timeout: float | None = None) -> float:
+        started = time.monotonic()
+        with self.cv:
+            tickets = [t for name, ts in self._tickets.items() if lineage in (None, name) for t in ts]
+        for ticket in tickets:
+            left = None if timeout is None else max(0.0, timeout - (time.monotonic() - started))
+            if not ticket._done.wait(left):
+                raise TimeoutError("RAW write-behind drain timed out")
+        if lineage is not None and lineage in self._failed:
+            raise StateError(f"lineage {lineage} has a failed archival: {self._failed[lineage]}")
+        return time.monotonic() - started
+
+    def cancel(self, lineage: str) -> int:
+        return 0  # every submitted chunk is (or will be) written in order
+
+    def forget(self, lineage: str, timeout: float | None = 60.0) -> None:
+        self.drain(lineage, timeout)
+        with self.cv:
+            self._tickets.pop(lineage, None)
+
+    def reset(self, lineage: str) -> BaseException | None:
+        with self.cv:
+            self._tickets[lineage] = [t for t in self._tickets.get(lineage, []) if t.state == "published"]
+            return self._failed.pop(lineage, None)
+
+    @contextmanager
+    def defer_gpu_work(self):
+        yield
+
+    def open_generation(self, key: Any, **_) -> dict:
+        return {"archival_defer_wait": 0.0, "inflight_overlaps": 0}
+
+    def close_generation(self, key: Any) -> dict | None:
+        return None
+
+    def stats(self) -> dict:
+        with self.cv:
+            return {**self._counts, "representation": "raw_offload" if self.write_behind else "raw",
+                    "unwritten": len(self._queue), "failed_lineages": sorted(self._failed)}
+
+    def close(self, *, drain: bool = True, timeout: float | None = None) -> None:
+        if drain:
+            try:
+                self.drain(timeout=timeout)
+            except (StateError, TimeoutError):
+                pass
+        with self.cv:
+            self._closed = True
+            self.cv.notify_all()
+        if self._writer is not None:
+            self._writer.join(timeout=30)

@@ -15,8 +15,9 @@ from typing import Any
 
 import torch
 
-from ...archive_pipeline import ArchivePipeline
-from ...archive_restore import LineageRestorer
+from ...archive_pipeline import ArchivePipeline, RawArchive
+from ...archive_restore import LineageRestorer, RawLineageRestorer
+from ...factor_packs import FactorLineageRestorer
 from ...errors import ConfigurationError
 from ...lineage import LineageRuntime
 from ...lineage_commit import ArchiveOptions
@@ -41,7 +42,8 @@ def method_for(config: ReelCacheRuntimeConfig, profile: ModelProfile, fit_device
         fractions = config.rank_fractions()
         fixed = {"fixed_rank_k": max(1, round(fractions["K"] * profile.channels)),
                  "fixed_rank_v": max(1, round(fractions["V"] * profile.channels))}
-    return RankMethodConfig(targets, CodecSpec("svd_hevc", 32, normalization=config.normalization),
+    kind = "svd" if config.representation == "svd" else "svd_hevc"
+    return RankMethodConfig(targets, CodecSpec(kind, 32, normalization=config.normalization),
                             reuse=config.reuse, refit=config.refit, refit_rule=config.refit_rule,
                             rate_lag=config.rate_lag, matmul_precision=config.matmul_precision or "fp32", **fixed)
 
@@ -66,13 +68,27 @@ class LineageSessionArchive:
             self.raw_tier = RawChunkTier(self.device, gpu_budget_bytes=gpu, host_budget_bytes=host,
                                          host_pinned=config.host_raw_pinned, retain=config.raw_tier_retain,
                                          promote=config.raw_tier_promote)
-        self.pipeline = ArchivePipeline(self.runtime, method=self.method, device=fit_device,
-                                        options=ArchiveOptions(), raw_tier=self.raw_tier,
-                                        max_unpublished=config.max_unpublished, submit_timeout=config.submit_timeout,
-                                        encode_workers=config.resolved_encode_workers(), registry=self.registry)
-        self.restorer = LineageRestorer(self.runtime, self.device, prepared_budget_bytes=config.prepared_budget_bytes,
-                                        basis_budget_bytes=config.basis_budget_bytes) \
-            if self.device.type == "cuda" else None
+        representation = config.representation
+        if representation in ("raw", "raw_offload"):
+            self.pipeline = RawArchive(self.runtime, raw_tier=self.raw_tier,
+                                       write_behind=representation == "raw_offload",
+                                       max_unwritten=config.max_unpublished)
+        else:
+            self.pipeline = ArchivePipeline(self.runtime, method=self.method, device=fit_device,
+                                            options=ArchiveOptions(), raw_tier=self.raw_tier,
+                                            max_unpublished=config.max_unpublished,
+                                            submit_timeout=config.submit_timeout,
+                                            encode_workers=config.resolved_encode_workers(), registry=self.registry)
+        self.restorer = None
+        if self.device.type == "cuda":
+            if representation in ("raw", "raw_offload"):
+                self.restorer = RawLineageRestorer(self.runtime, self.device)
+            elif representation == "svd":
+                self.restorer = FactorLineageRestorer(self.runtime, self.device)
+            else:
+                self.restorer = LineageRestorer(self.runtime, self.device,
+                                                prepared_budget_bytes=config.prepared_budget_bytes,
+                                                basis_budget_bytes=config.basis_budget_bytes)
         self.stats_ = {"raw_installs": 0, "archive_installs": 0, "commits": 0}
 
     # -- lineages -------------------------------------------------------------------------------------------------

@@ -109,3 +109,28 @@ def test_controls_errors(tmp_path):
         assert "fork" in caps["ops"]
     finally:
         bridge.shutdown()
+
+
+@pytest.mark.parametrize("representation,raw_tier,bound", [("raw", False, 1e-7), ("raw_offload", True, 1e-7),
+                                                           ("svd", False, 0.05)])
+def test_other_representations_restore(tmp_path, representation, raw_tier, bound):
+    """RAW (synchronous and write-behind) and SVD-only factor-pack archives restore the session history."""
+    bridge = make_bridge(tmp_path, representation=representation, raw_tier=raw_tier, raw_restore="off"
+                         if raw_tier else "prefer")
+    try:
+        bridge.request("a", chunks=3, action="create", seed=7)
+        resident = bridge.sessions.get("a").resident
+        bridge.pause("a")
+        bridge.drop_resident("a")
+        report = bridge.request("a", chunks=0, seed=7)
+        assert report["route"] == "archive"
+        restored = bridge.sessions.get("a").resident
+        tokens = 3 * TINY.chunk_tokens
+        for layer in range(TINY.num_layers):
+            for which in ("k", "v"):
+                a, b = resident[which][layer][:tokens], restored[which][layer][:tokens]
+                assert float((a - b).norm() / a.norm()) < bound
+        stats = bridge.archive.stats()["pipeline"]
+        assert stats.get("representation", representation) == representation or representation == "svd"
+    finally:
+        bridge.shutdown()
