@@ -95,3 +95,67 @@ def test_conditioning_cache_seam(tmp_path):
     got = model.forward(latents, 0.5, text, first_frame=2, cache=restored)
     assert float((got - ref).norm() / ref.norm()) < 0.1
     store.close()
+
+
+def test_epoch_tiers_planning_gate_and_session_provider(tmp_path):
+    import threading
+    import time
+
+    from reelcache_b200.lineage import LineageRuntime
+    from reelcache_b200.models.longcat import ConditioningCacheEpoch, ReelCacheConditioningCacheBackend
+    from reelcache_b200.models.longcat_session import (EpochRawTiers, HostFull, LongCatSessionProvider, PlanningGate,
+                                                       gated_plan_chunk)
+    from reelcache_b200.rank_method import RankMethodConfig, plan_chunk
+    from reelcache_b200.store import ObjectStore
+    from reelcache_b200.types import CodecSpec, ModelIdentity, energy_targets
+    model = _model()
+    cfg = model.cfg
+    store = ObjectStore(tmp_path / "store")
+    identity = ModelIdentity("longcat-tiny", "seed1", cfg.layers, cfg.dim, "BTHD", "bfloat16")
+    runtime = LineageRuntime(store, identity)
+    runtime.create_lineage("s")
+    method = RankMethodConfig(energy_targets("longcat_720p"), CodecSpec("svd_hevc", 32), solver="gram_eigh")
+    backend = ReelCacheConditioningCacheBackend(runtime, "s", method, head_dim=cfg.head_dim, grid=cfg.grid)
+    tiers = EpochRawTiers(host_raw_budget_bytes=1 << 30, pin_memory=False)
+    provider = LongCatSessionProvider(model, backend, tiers)
+    cond, text = _inputs(model, frames=2, seed=4)
+    built, tier = provider.segment_cache("s", 0, cond, text, first_frame=0)
+    assert tier == "built"
+    again, tier = provider.segment_cache("s", 1, cond, text, first_frame=2)  # same content: the host tier serves it
+    assert tier == "host_raw" and torch.equal(again.k[0], built.k[0])
+    cond2, _ = _inputs(model, frames=2, seed=8)
+    provider.segment_cache("s", 2, cond2, text, first_frame=4)
+    assert [b["segment"] for b in provider.boundaries("s")] == [0, 1, 2]
+    kept = provider.resume("s", 1, new_session="fork")
+    assert [b["segment"] for b in provider.boundaries("fork")] == [0, 1] and len(kept) == 2
+    # the host tier evicts only published epochs; with no room for unpublished ones it refuses
+    small = EpochRawTiers(host_raw_budget_bytes=1, host_slots=1, pin_memory=False)
+    small.capture("a", built)
+    with pytest.raises(HostFull):
+        small.capture("b", built)
+    small.published("a", "node-a")
+    assert small.stats()["entries"] == 0 and small.stats()["evictions"] == 1
+    # planning gate: a section waits for the unit in progress; a unit waits for an open section
+    gate = PlanningGate()
+    order = []
+
+    def unit():
+        with gate.unit():
+            order.append("unit-start")
+            time.sleep(0.2)
+            order.append("unit-end")
+
+    worker = threading.Thread(target=unit)
+    worker.start()
+    time.sleep(0.05)
+    with gate.section(release_memory=False):
+        order.append("section")
+    worker.join()
+    assert order == ["unit-start", "unit-end", "section"]
+    # gated planning equals ungated planning
+    from .lineage_support import chunk, method as lm
+    matrices, contexts = chunk(0)
+    a = plan_chunk(matrices, contexts, lm(), None, {}, {})
+    b = gated_plan_chunk(gate, matrices, contexts, lm(), None, {}, {})
+    assert all(torch.equal(a[k].rows, b[k].rows) for k in a)
+    store.close()

@@ -171,6 +171,42 @@ def w_dead_peer(rank, world):
         t.checkpoint("step2")
 
 
+def w_row_archive(rank, world, root):
+    from reelcache_b200.errors import IntegrityError
+    from reelcache_b200.parallel.context_parallel import RowShard
+    from reelcache_b200.parallel.distributed import DistributedOwner
+    from reelcache_b200.parallel.row_shard_archive import RowShardedCacheArchive, TieredRowArchive
+    from reelcache_b200.store import ObjectStore
+    from reelcache_b200.types import MatrixKey
+    t = DistributedOwner(device="cpu")
+    frames, height, width, channels = 2, 4, 6, 16
+    shards = [RowShard(r, world, frames, height, width) for r in range(world)]
+    indices = [s.token_index() for s in shards]
+    tokens = frames * height * width
+    g = torch.Generator().manual_seed(3)
+    full = {MatrixKey(l, tg): (torch.randn(tokens, 4, generator=g) @ torch.randn(4, channels, generator=g))
+            for l in range(2) for tg in ("K", "V")}
+    store = ObjectStore(f"{root}/rank{rank}")
+    archive = RowShardedCacheArchive(t, store, indices, tokens=tokens, channels=channels, energy_target=0.999)
+    tiers = TieredRowArchive(archive, host_raw_budget_bytes=1 << 20)
+    local = {k: v[indices[rank]] for k, v in full.items()}
+    tiers.capture("e0", local)
+    assert tiers.flush() == ["e0"]
+    # every rank's fragment holds only the matrices it owns (whole-matrix owners alternate by layer/target)
+    tier, rows = tiers.install("e0")
+    assert tier == "host_raw" and torch.equal(rows[MatrixKey(1, "V")], local[MatrixKey(1, "V")])
+    # a staging failure on one rank rolls every rank back to the compressed archive
+    tier, rows = tiers.install("e0", fail_preflight=(rank == 1))
+    assert tier == "compressed" and tiers.last_restore_tier["rollback"]
+    for key, value in rows.items():
+        assert float((value - local[key]).norm() / local[key].norm()) < 1e-4
+    # after eviction of the host copy the tiers agree on the compressed archive
+    tiers.entries.clear()
+    tier, _ = tiers.install("e0")
+    assert tier == "compressed"
+    store.close()
+
+
 def test_dead_peer_detected():
     run("w_dead_peer", 2)
 
@@ -191,3 +227,7 @@ def test_factor_sharding(mode, granularity):
 
 def test_sp_tiered_history(tmp_path):
     run("w_sp_history", 2, str(tmp_path / "store"))
+
+
+def test_row_sharded_cache_archive_and_tiers(tmp_path):
+    run("w_row_archive", 2, str(tmp_path))
