@@ -155,3 +155,15 @@ def test_planner_uses_jacobi_and_fitter_gram_batched():
     fitter.prefit(items)
     factors = fitter.fit(items[MatrixKey(0, "K")][0], contexts[MatrixKey(0, "K")], 24)
     assert fitter.prefit_stats["hits"] == 1 and factors.metrics["projection_relative_residual"] < 0.05
+
+
+@pytest.mark.parametrize("rank", [37, 64, 300])
+def test_device_finalization_matches_host(rank):
+    import numpy as np
+    from reelcache_b200.node_packets import finalize_tile
+    g = torch.Generator().manual_seed(rank)
+    coefficients = torch.randn(3 * 30 * 52, rank, generator=g) * 3
+    host = finalize_tile(coefficients, (3, 30, 52))
+    device = finalize_tile(coefficients.cuda(), (3, 30, 52)).to_host()
+    assert np.array_equal(device.canvas, host.canvas)
+    assert np.array_equal(device.affine, host.affine)
