@@ -140,3 +140,38 @@ def test_device_pressure_and_telemetry():
             pass
     snap = collector.snapshot()
     assert snap["stages"]["store.read"]["completed_bytes"] == 10
+
+
+def test_layer_prefetch_packed_prefetch_and_paired_decode(archived):
+    from reelcache_b200.prefetch import LayerPrefetcher, PackedLayerPrefetcher, PairedDecoder
+    runtime, nodes, sources = archived
+    channels = MODEL.channels_for("K")
+    prefetch = LayerPrefetcher(runtime, device="cpu", layers=MODEL.layers, channels=channels,
+                               native_dtype=torch.float32, max_bytes=1 << 26)
+    prefetch.begin(nodes[-1])
+    for layer in range(MODEL.layers):
+        tensors = prefetch.acquire(layer)
+        expect = torch.cat([s[MatrixKey(layer, "V")] for s in sources])
+        assert relative_error(tensors[("V", None)], expect) < 0.1
+        prefetch.release(layer)
+    assert prefetch.stats()["layers"] == MODEL.layers
+    prefetch.close()
+    pool = DecoderPool(2)
+    restorer = PackedRestorer(runtime, pool, device="cpu")
+    packed = PackedLayerPrefetcher(restorer, depth=1)
+    packed.begin(nodes[-1], layers=MODEL.layers)
+    heads, head_dim = 2, channels // 2
+    caches = {(l, t): torch.zeros((1, 3 * TOKENS, heads, head_dim)) for l in range(MODEL.layers) for t in "KV"}
+    table = rk.RopeTable.wan(head_dim, 32)
+    for layer in range(packed.layers):
+        packed.restore(layer, lambda l, w: caches[(l, w)],
+                       lambda piece: (table, (2 * (piece.token_start // TOKENS), 0, 0))).synchronize()
+    packed.end()
+    got = caches[(0, "V")].reshape(3 * TOKENS, -1)
+    assert relative_error(got, torch.cat([s[MatrixKey(0, "V")] for s in sources])) < 0.1
+    prep = restorer.prepared(restorer.runtime.load_record(restorer.plan(nodes[-1])[0].entry.records[0][1]).packet_ref)
+    paired = PairedDecoder(pool, max_output_bytes=1 << 26)
+    k, v = paired.decode_pair((prep.stream, prep.stream_codec, prep.raw_shape), (prep.stream, prep.stream_codec,
+                                                                                prep.raw_shape))
+    assert k.tobytes() == v.tobytes() and paired.stats()["pairs"] == 1
+    pool.close()
