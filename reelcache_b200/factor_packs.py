@@ -80,16 +80,36 @@ class FactorLineageRestorer(JobLineageRestorer):
     def __init__(self, runtime: LineageRuntime, device, *, budget_bytes: int = 4 << 30):
         super().__init__(runtime, device)
         self.factors = FactorRestorer(runtime, device, budget_bytes=budget_bytes)
+        self._device_packs: dict = {}
+        self._bounds: dict = {}
+
+    def _prepare(self, pieces) -> None:
+        """Each factor pack the history needs goes to the device once per restore (one pinned H2D copy)."""
+        self._device_packs = {}
+        for piece in pieces:
+            for _, record_ref in piece.entry.records:
+                record = self.runtime.load_record(record_ref)
+                if record.packet_ref in self._device_packs:
+                    continue
+                pack = self.factors.pack(record.packet_ref)
+                raw = torch.from_numpy(np.array(pack.raw, copy=True))
+                if self.device.type == "cuda":
+                    raw = raw.pin_memory().to(self.device, non_blocking=True)
+                    self.stats_["h2d_bytes"] += raw.numel()
+                self._device_packs[record.packet_ref] = raw
 
     def _source(self, piece, record, rows: slice):
         from . import restore_kernels as rk
-        host = np.array(self.factors.factors(record)[rows], copy=True)
-        bound = float(np.abs(host.astype(np.float32)).max(initial=0.0))
-        values = torch.from_numpy(host)
-        if self.device.type == "cuda":
-            values = values.to(self.device)
-            self.stats_["h2d_bytes"] += values.numel() * 2
-        return rk.CoefficientSource(values, bound=bound), self._basis(record)
+        pack = self.factors.pack(record.packet_ref)
+        index = record.decision["packet"]["tile"]
+        tile = pack.tiles[index]
+        rank = int(tile["rank"])
+        raw = self._device_packs[record.packet_ref]
+        values = raw[tile["offset"]:tile["offset"] + tile["bytes"]].view(torch.float16).view(-1, rank)[rows]
+        key = (record.packet_ref, index)
+        if key not in self._bounds:  # bound of the whole tile (covers every row range), computed once on the host
+            self._bounds[key] = float(np.abs(pack.factors(index).astype(np.float32)).max(initial=0.0))
+        return rk.CoefficientSource(values, bound=self._bounds[key]), self._basis(record)
 
     def stats(self) -> dict[str, Any]:
         return {**self.stats_, "packs": len(self.factors._packs), "pack_bytes": self.factors._bytes}
