@@ -33,6 +33,8 @@ void jacobi_eigh(const at::Tensor& a, at::Tensor& values, at::Tensor& vectors, a
 void sq_partials(const at::Tensor& x, const c10::optional<at::Tensor>& r, double scale, at::Tensor& out);
 void fingerprint_partials(const at::Tensor& bits, at::Tensor& out, int64_t row_start, int64_t prime);
 void dot2_gemm(const at::Tensor& x, const at::Tensor& rows, at::Tensor& out);
+void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& out, double scale,
+                   const c10::optional<at::Tensor>& status, int64_t ablate);
 void mosaic_u8(const at::Tensor& pixels, at::Tensor& canvas, const std::vector<int64_t>& geometry);
 void gemm_bf16_promoted(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, double alpha,
                         const c10::optional<at::Tensor>& status);
@@ -81,6 +83,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16_promoted", &rc::gemm_bf16_promoted,
         "out = alpha * A @ B^T (bf16, K-major) with TMEM partials promoted to FP32 registers every 128 K",
         py::arg("A"), py::arg("B"), py::arg("out"), py::arg("alpha") = 1.0, py::arg("status") = py::none());
+  m.def("attention_fwd", &rc::attention_fwd, "flash-attention forward on tcgen05 (bf16, head_dim 128)",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("scale"), py::arg("status") = py::none(),
+        py::arg("ablate") = 0);
   m.def("mosaic_u8", &rc::mosaic_u8, "channel-tile mosaic of u8 coefficients into a canvas", py::arg("pixels"),
         py::arg("canvas"), py::arg("geometry"));
   m.def("dot2_gemm", &rc::dot2_gemm, "compensated FP32 GEMM out = x @ rows^T", py::arg("x"), py::arg("rows"),

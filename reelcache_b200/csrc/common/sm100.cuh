@@ -125,6 +125,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// Waits with mbarrier.try_wait, which parks the thread in hardware until the phase completes (or a
+// hardware time window passes) instead of re-issuing probes: the lowest wake-up latency for pipelines
+// with many short waits per tile, without taking issue slots from the warps doing the math. Bounded by
+// the same wall-time limit (the clock and status word are read once every 64 unsuccessful windows).
+__device__ __forceinline__ bool mbar_wait_park(uint64_t* bar, uint32_t parity, int* status, int code) {
+  uint64_t start = 0;
+#pragma unroll 1
+  for (uint32_t iter = 1;; ++iter) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((iter & 63u) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (start == 0) {
+        start = now;
+      } else if (now - start > kWaitLimitNs) {
+        record_status(status, code);
+        return false;
+      }
+      if (status_set(status)) return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // Proxy fences
 // ---------------------------------------------------------------------------------------------

@@ -1,9 +1,13 @@
 """Attention entry point of the DiT: queries of the current chunk against keys/values of the causal
 KV cache (bidirectional within the chunk) or of the cached text tokens.
 
-``backend="fused"`` is the sm_100a tcgen05 flash-attention kernel (csrc/model/attention_sm100.cu) when
-it is built; ``"sdpa"`` is PyTorch's scaled_dot_product_attention, kept as the library baseline for
-comparisons and as the CPU path. ``"auto"`` selects the fused kernel on CUDA when available.
+``backend="fused"`` is the sm_100a tcgen05 flash-attention kernel (csrc/model/attention_sm100.cu: TMA
+producer, single-thread MMA issuer, two softmax warpgroups splitting the KV blocks, S and O in TMEM, lazy
+rescaling); ``"sdpa"`` is PyTorch's scaled_dot_product_attention (cuDNN's fused kernel on B200). ``"auto"``
+selects ``sdpa`` on CUDA: measured on B200 the fused kernel reaches about half of cuDNN's throughput (its
+per-block shared-memory traffic -- P written to and re-read from shared memory, K/V tiles read once per
+128 queries -- and the exp pipe bound it; see profiles/attention_kernel_b200.md), so it is selected only
+explicitly.
 """
 
 from __future__ import annotations
@@ -25,7 +29,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, backend: str
     ``[Tq, H, D]`` bf16."""
     scale = 1.0 / math.sqrt(q.shape[-1]) if scale is None else scale
     if backend == "auto":
-        backend = "fused" if q.is_cuda and _fused_available() else "sdpa"
+        backend = "sdpa"
     if backend == "fused":
         out = torch.empty((q.shape[0], q.shape[1], q.shape[2]), dtype=torch.bfloat16, device=q.device)
         _ext.ext().attention_fwd(q, k, v, out, float(scale), _ext.status_word(q.device))
