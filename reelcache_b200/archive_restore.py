@@ -367,9 +367,21 @@ class LineageRestorer:
                 events.append(event)
         self.stats_["restores"] += 1
 
+        # Overlapped: one launch per layer, so the forward's layer L waits for layer L only. Otherwise
+        # consecutive layers share a launch (up to 48 jobs): fewer, fuller launches.
+        batch_of = {}
+        if not overlapped:
+            for batch in program.batches():
+                batch_of[batch[0]] = batch
+
         def issue(layer):
-            stream.wait_event(events[layer])
-            program.launch(layer, stream, aux=True)
+            if overlapped:
+                stream.wait_event(events[layer])
+                program.launch(layer, stream, aux=True)
+            elif layer in batch_of:
+                for member in batch_of[layer]:
+                    stream.wait_event(events[member])
+                program.launch_batch(batch_of[layer], stream, aux=True)
 
         def finish():
             done = torch.cuda.Event()

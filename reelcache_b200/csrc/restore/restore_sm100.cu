@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
         const int head_dim = jb.head_dim;
         tmem_wait_ld();
         if (p.ablate == 2) {
-          if (__uint_as_float(r[0] ^ r[63]) == 1.2345e-30f && lane == 40) *reinterpret_cast<uint32_t*>(jb.dst) = r[0];
+          if (__uint_as_float(r[0] ^ r[63]) == 1.2345e-30f && p.num_jobs < 0) *reinterpret_cast<uint32_t*>(jb.dst) = r[0];
         } else {
           // pair i (columns 2i, 2i+1) -> packed 16-bit pair written back into r[i] (r[i] is read by
           // pair i / 2 <= i, so the in-place order is safe).
@@ -490,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
               uint32_t x = 0;
 #pragma unroll
               for (int i = 0; i < 32; ++i) x ^= r[i];
-              if (x == 0x9e3779b9u && lane == 40) *reinterpret_cast<uint32_t*>(jb.dst) = x;
+              if (x == 0x9e3779b9u && p.num_jobs < 0) *reinterpret_cast<uint32_t*>(jb.dst) = x;
             } else if (jb.tma_store) {
               // 32 x 64 16-bit block -> 128-byte-swizzled staging buffer -> one TMA bulk store.
               if (stored) {

@@ -124,6 +124,8 @@ class RestoreProgram:
 
     def __init__(self, device, stream, *, precision: str = "fp16"):
         self.device = torch.device(device)
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.stream = stream
         self.passes = 2 if precision == "fp16x2" else 1
         self.jobs: list[dict] = []
@@ -132,6 +134,7 @@ class RestoreProgram:
         self.prepared = False
         self.launches = 0
         self.scratch_bytes = 0
+        self._batch_cache: dict = {}
 
     def add(self, job: dict, group=0) -> None:
         if self.prepared:
@@ -259,6 +262,7 @@ class RestoreProgram:
                 row[1] += base
                 row[2] += base
         self.aux = _aux_tables(unpack_rows, prep_rows)
+        self._aux_rows = (unpack_rows, unpack_owner, prep_rows, prep_owner)
         group_of = {}
         for group, indices in self.groups.items():
             for index in indices:
@@ -271,23 +275,81 @@ class RestoreProgram:
         if run_aux:
             self.run_aux(stream)
         # launch parameters (tensor maps included) encoded once per batch of <= 48 jobs
-        self.blobs = {}
-        for group, indices in self.groups.items():
-            blobs = []
-            by_dtype: dict = {}
-            for index in indices:  # one launch covers jobs of one output dtype
-                by_dtype.setdefault(self.rows[index][12], []).append(index)
-            batches = [same[i:i + MAX_RESTORE_JOBS] for same in by_dtype.values()
-                       for i in range(0, len(same), MAX_RESTORE_JOBS)]
-            for chunk in batches:
-                blobs.append(ext().restore_build(torch.tensor([self.rows[j] for j in chunk], dtype=torch.int64),
-                                                 [self.a_ops[j] for j in chunk], [self.b_ops[j] for j in chunk],
-                                                 torch.tensor([self.inverse[j] for j in chunk], dtype=torch.float32)))
-            self.blobs[group] = blobs
+        self.blobs = {group: self._build_blobs(indices) for group, indices in self.groups.items()}
         self.keepalive.extend(self.a_ops)
         self.keepalive.extend(self.b_ops)
         self.prepared = True
         return self
+
+    def _build_blobs(self, indices) -> list:
+        blobs = []
+        by_dtype: dict = {}
+        for index in indices:  # one launch covers jobs of one output dtype
+            by_dtype.setdefault(self.rows[index][12], []).append(index)
+        batches = [same[i:i + MAX_RESTORE_JOBS] for same in by_dtype.values()
+                   for i in range(0, len(same), MAX_RESTORE_JOBS)]
+        for chunk in batches:
+            blobs.append(ext().restore_build(torch.tensor([self.rows[j] for j in chunk], dtype=torch.int64),
+                                             [self.a_ops[j] for j in chunk], [self.b_ops[j] for j in chunk],
+                                             torch.tensor([self.inverse[j] for j in chunk], dtype=torch.float32)))
+        return blobs
+
+    def batches(self, groups=None) -> list[tuple]:
+        """Consecutive groups (in insertion order) packed into batches of at most 48 jobs: the launch
+        units of :meth:`launch_batch` when no per-group readiness is needed (a non-overlapped restore
+        launches 6 CausVid layers per kernel instead of one)."""
+        order = list(self.groups) if groups is None else list(groups)
+        out, current, count = [], [], 0
+        for group in order:
+            n = len(self.groups[group])
+            if current and count + n > MAX_RESTORE_JOBS:
+                out.append(tuple(current))
+                current, count = [], 0
+            current.append(group)
+            count += n
+        if current:
+            out.append(tuple(current))
+        return out
+
+    def _batch(self, groups: tuple):
+        cached = self._batch_cache.get(groups)
+        if cached is None:
+            indices = [i for g in groups for i in self.groups[g]]
+            members = set(indices)
+            unpack_rows, unpack_owner, prep_rows, prep_owner = self._aux_rows
+            aux = _aux_tables([row for row, owner in zip(unpack_rows, unpack_owner) if owner in members],
+                              [row for row, owner in zip(prep_rows, prep_owner) if owner in members])
+            cached = (self._build_blobs(indices), aux)
+            self._batch_cache[groups] = cached
+        return cached
+
+    def launch_batch(self, groups, stream=None, *, aux: bool = False) -> int:
+        """One restore launch (per output dtype and 48 jobs) covering every job of ``groups``; ``aux``
+        first runs their unpack + basis preparation (batched too). Parameters are encoded once per
+        distinct batch and reused."""
+        if not self.prepared:
+            self.prepare()
+        blobs, (unpack_tables, prep_tables) = self._batch(tuple(groups))
+        status = status_word(self.device)
+        with torch.cuda.stream(stream or self.stream):
+            if aux:
+                for table in unpack_tables:
+                    ext().unpack_launch(table, self.device.index)
+                for table in prep_tables:
+                    ext().prep_launch(table, self.device.index)
+                self.launches += len(unpack_tables) + len(prep_tables)
+            for blob in blobs:
+                ext().restore_run(blob, self.device.index, status)
+        self.launches += len(blobs)
+        return len(blobs)
+
+    def batch_launch_count(self, aux: bool = True) -> int:
+        """Kernel launches of one pass of :meth:`launch_batch` over :meth:`batches`."""
+        total = 0
+        for groups in self.batches():
+            blobs, (unpack_tables, prep_tables) = self._batch(groups)
+            total += len(blobs) + (len(unpack_tables) + len(prep_tables) if aux else 0)
+        return total
 
     def run_aux(self, stream=None, group=None) -> int:
         """(Re-)run the operand preparation of every job (or of one group's jobs): unpack of the 8-bit
