@@ -38,6 +38,15 @@ void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
 void mosaic_u8(const at::Tensor& pixels, at::Tensor& canvas, const std::vector<int64_t>& geometry);
 void gemm_bf16_promoted(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, double alpha,
                         const c10::optional<at::Tensor>& status);
+void ulysses_qkv(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias,
+                 const std::vector<at::Tensor>& dst_q, const std::vector<at::Tensor>& dst_k,
+                 const std::vector<at::Tensor>& dst_v, int64_t rank, int64_t head_dim,
+                 const c10::optional<at::Tensor>& status);
+void ulysses_out(const std::vector<at::Tensor>& o_owners, const at::Tensor& w, const c10::optional<at::Tensor>& bias,
+                 const c10::optional<at::Tensor>& gate, at::Tensor& out, int64_t rank, int64_t n_loc,
+                 int64_t epilogue, const at::Tensor& stage, const at::Tensor& tile_flags, int64_t call,
+                 const c10::optional<at::Tensor>& status);
+void peer_barrier(const at::Tensor& flags, int64_t rank, int64_t epoch, const c10::optional<at::Tensor>& status);
 }  // namespace rc
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -46,6 +55,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("B"), py::arg("out"), py::arg("epilogue") = 0, py::arg("bias") = py::none(),
         py::arg("gate") = py::none(), py::arg("resid") = py::none(), py::arg("alpha") = 1.0, py::arg("bn") = 0,
         py::arg("status") = py::none());
+  m.def("ulysses_qkv", &rc::ulysses_qkv, "QKV projection GEMM with the Ulysses head scatter fused (peer stores)",
+        py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("dst_q"), py::arg("dst_k"), py::arg("dst_v"),
+        py::arg("rank"), py::arg("head_dim"), py::arg("status") = py::none());
+  m.def("ulysses_out", &rc::ulysses_out, "output projection GEMM with the Ulysses token gather fused (peer TMA loads)",
+        py::arg("o_owners"), py::arg("w"), py::arg("bias"), py::arg("gate"), py::arg("out"), py::arg("rank"),
+        py::arg("n_loc"), py::arg("epilogue"), py::arg("stage"), py::arg("tile_flags"), py::arg("call"),
+        py::arg("status") = py::none());
+  m.def("peer_barrier", &rc::peer_barrier, "bounded device-side barrier over peer flag words", py::arg("flags"),
+        py::arg("rank"), py::arg("epoch"), py::arg("status") = py::none());
   m.def("restore_build", &rc::restore_build, "launch parameters of a fused restore over <= 48 jobs",
         py::arg("jobs"), py::arg("a_ops"), py::arg("b_ops"), py::arg("inverse"));
   m.def("restore_run", &rc::restore_run, "launch a fused restore from restore_build parameters", py::arg("blob"),

@@ -28,6 +28,11 @@ import torch
 import torch.nn.functional as F
 
 from ..parallel.context_parallel import RowShard, gather_tokens, ulysses_in, ulysses_out
+
+
+def dist_rank(group) -> int:
+    import torch.distributed as dist
+    return dist.get_rank(group)
 from ..restore_kernels import RopeTable
 
 
@@ -216,12 +221,35 @@ class LongCatDiT:
 
     # -- forward --------------------------------------------------------------------------------------------------
 
+    def _ulysses_cache(self, cache: LongCatConditioningCache, shards, cp_group):
+        """Per layer, the conditioning cache in Ulysses layout ``[all cache rows, heads / cp, d]`` (rank-major,
+        RoPE applied to K): one NCCL all-to-all per layer and epoch, reused by every forward of the epoch."""
+        key = (id(cache), cache.epoch.epoch_id)
+        memo = getattr(self, "_ulysses_memo", None)
+        if memo is not None and memo[0] == key:
+            return memo[1]
+        cshards = [RowShard(sh.rank, sh.cp, cache.epoch.frames, *self.cfg.grid) for sh in shards]
+        rank = dist_rank(cp_group)
+        cos_c, sin_c = self.rope_tables(cache.epoch.first_frame, cache.epoch.frames, cshards[rank])
+        layers = [(ulysses_in(_rope(cache.k[layer].to(self.dtype), cos_c, sin_c).contiguous(), cp_group),
+                   ulysses_in(cache.v[layer].to(self.dtype).contiguous(), cp_group)) for layer in range(len(self.blocks))]
+        self._ulysses_memo = (key, layers)
+        return layers
+
     def forward(self, latents: torch.Tensor, t: float, text: torch.Tensor, *, first_frame: int = 0,
-                cache: LongCatConditioningCache | None = None, cp_group=None, return_kv: bool = False):
+                cache: LongCatConditioningCache | None = None, cp_group=None, return_kv: bool = False,
+                ulysses=None):
         """Flow prediction ``[C, F, H, W]`` (FP32) of ``latents`` (frames ``first_frame..``) attending to the
-        conditioning cache; ``return_kv`` also returns this forward's per-layer pre-RoPE (K, V)."""
+        conditioning cache; ``return_kv`` also returns this forward's per-layer pre-RoPE (K, V).
+
+        ``ulysses``: a :class:`~reelcache_b200.parallel.ulysses_fused.FusedUlysses` of ``cp_group`` -- the
+        self-attention's all-to-alls then run fused into the QKV and output-projection GEMMs over NVLink
+        peer memory (q/k norm and RoPE after the scatter, on this rank's heads of every token) instead of
+        NCCL around the GEMMs."""
         import torch.distributed as dist
         cfg = self.cfg
+        if ulysses is not None and (cp_group is None or return_kv):
+            raise ValueError("the fused Ulysses path needs a context-parallel group and no K/V capture")
         frames = latents.shape[1]
         shard = shards = None
         if cp_group is not None:
@@ -238,11 +266,27 @@ class LongCatDiT:
             cshard = None if shard is None else RowShard(shard.rank, shard.cp, cache.epoch.frames, *cfg.grid)
             cos_c, sin_c = self.rope_tables(cache.epoch.first_frame, cache.epoch.frames, cshard)
         n, h, hd = x.shape[0], cfg.heads, cfg.head_dim
+        if ulysses is not None:  # RoPE rows of every rank's tokens in rank-major (gathered) order
+            tables = [self.rope_tables(first_frame, frames, sh) for sh in shards]
+            cos_g, sin_g = torch.cat([c for c, _ in tables]), torch.cat([s_ for _, s_ in tables])
+            cache_u = self._ulysses_cache(cache, shards, cp_group) if cache is not None else None
         kvs = []
         for layer, blk in enumerate(self.blocks):
             mod = self.ops.linear(F.silu(temb.float()).to(self.dtype), blk["ada_w"], blk["ada_b"],
                                   out_dtype=torch.float32).reshape(6, cfg.dim)
             y = F.layer_norm(x, (cfg.dim,), eps=cfg.eps) * (1 + mod[1]) + mod[0]
+            if ulysses is not None:
+                rows = ulysses.world * n
+                q_u, k_u, _ = ulysses.qkv(y.to(self.dtype), blk["qkv_w"], blk["qkv_b"])
+                q = _rope(self.ops.rms_norm_heads(q_u, blk["q_norm"], cfg.eps), cos_g, sin_g)
+                k_u.copy_(_rope(self.ops.rms_norm_heads(k_u, blk["k_norm"], cfg.eps), cos_g, sin_g))
+                if cache_u is not None:
+                    ulysses.set_cache(*cache_u[layer])
+                k_all, v_all = ulysses.kv_all(rows)
+                ulysses.local["o"][:rows].copy_(self.ops.attention(q, k_all, v_all).reshape(rows, -1))
+                ulysses.out(x, blk["proj_w"], blk["proj_b"], mod[2])
+                self._cross_and_ffn(x, blk, mod, text, n)
+                continue
             qkv = self.ops.linear(y.to(self.dtype), blk["qkv_w"], blk["qkv_b"]).reshape(n, 3, h, hd)
             q = self.ops.rms_norm_heads(qkv[:, 0], blk["q_norm"], cfg.eps)
             k = self.ops.rms_norm_heads(qkv[:, 1], blk["k_norm"], cfg.eps)
@@ -261,18 +305,7 @@ class LongCatDiT:
             else:
                 o = self.ops.attention(q, k_all, v_all)
             x = x + mod[2] * self.ops.linear(o.reshape(n, cfg.dim), blk["proj_w"], blk["proj_b"]).float()
-            # cross-attention over the text (local rows)
-            y = F.layer_norm(x, (cfg.dim,), eps=cfg.eps).to(self.dtype)
-            cq = self.ops.rms_norm_heads(self.ops.linear(y, blk["cq_w"], blk["cq_b"]).reshape(n, h, hd),
-                                         blk["cq_norm"], cfg.eps)
-            ckv = self.ops.linear(text, blk["ckv_w"], blk["ckv_b"]).reshape(-1, 2, h, hd)
-            ck = self.ops.rms_norm_heads(ckv[:, 0], blk["ck_norm"], cfg.eps)
-            co = self.ops.attention(cq, ck, ckv[:, 1])
-            x = x + self.ops.linear(co.reshape(n, cfg.dim), blk["cproj_w"], blk["cproj_b"]).float()
-            # SwiGLU FFN
-            y = (F.layer_norm(x, (cfg.dim,), eps=cfg.eps) * (1 + mod[4]) + mod[3]).to(self.dtype)
-            hidden = (F.silu(self.ops.linear(y, blk["w1"]).float()) * self.ops.linear(y, blk["w3"]).float()).to(self.dtype)
-            x = x + mod[5] * self.ops.linear(hidden, blk["w2"]).float()
+            self._cross_and_ffn(x, blk, mod, text, n)
         fmod = self.ops.linear(F.silu(temb.float()).to(self.dtype), self.final_ada_w, self.final_ada_b,
                                out_dtype=torch.float32).reshape(2, cfg.dim)
         y = (F.layer_norm(x, (cfg.dim,), eps=cfg.eps) * (1 + fmod[1]) + fmod[0]).to(self.dtype)
@@ -281,6 +314,21 @@ class LongCatDiT:
             out = gather_tokens(out, shards, cp_group)
         pred = self.unpatchify(out, frames)
         return (pred, kvs) if return_kv else pred
+
+    def _cross_and_ffn(self, x: torch.Tensor, blk: dict, mod: torch.Tensor, text: torch.Tensor, n: int) -> None:
+        """Cross-attention over the text and the SwiGLU FFN on this rank's rows, in place on ``x``."""
+        cfg = self.cfg
+        h, hd = cfg.heads, cfg.head_dim
+        y = F.layer_norm(x, (cfg.dim,), eps=cfg.eps).to(self.dtype)
+        cq = self.ops.rms_norm_heads(self.ops.linear(y, blk["cq_w"], blk["cq_b"]).reshape(n, h, hd),
+                                     blk["cq_norm"], cfg.eps)
+        ckv = self.ops.linear(text, blk["ckv_w"], blk["ckv_b"]).reshape(-1, 2, h, hd)
+        ck = self.ops.rms_norm_heads(ckv[:, 0], blk["ck_norm"], cfg.eps)
+        co = self.ops.attention(cq, ck, ckv[:, 1])
+        x.add_(self.ops.linear(co.reshape(n, cfg.dim), blk["cproj_w"], blk["cproj_b"]).float())
+        y = (F.layer_norm(x, (cfg.dim,), eps=cfg.eps) * (1 + mod[4]) + mod[3]).to(self.dtype)
+        hidden = (F.silu(self.ops.linear(y, blk["w1"]).float()) * self.ops.linear(y, blk["w3"]).float()).to(self.dtype)
+        x.add_(mod[5] * self.ops.linear(hidden, blk["w2"]).float())
 
     def build_conditioning_cache(self, cond_latents: torch.Tensor, text: torch.Tensor, epoch: ConditioningCacheEpoch,
                                  *, cp_group=None) -> LongCatConditioningCache:

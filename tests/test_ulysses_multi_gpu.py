@@ -1,0 +1,69 @@
+"""Fused Ulysses on 2+ GPUs (NVLink peer memory): the LongCat-shaped DiT's context-parallel forward with the
+all-to-alls fused into the projection GEMMs equals the same forward with NCCL all-to-alls, with and without a
+conditioning cache. Skipped unless the box has at least two GPUs."""
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        return sock.getsockname()[1]
+
+
+def _worker(rank, world, port, result_path):
+    import datetime
+    import torch.distributed as dist
+    from reelcache_b200.models.longcat import ConditioningCacheEpoch, LongCatConfig, LongCatDiT
+    from reelcache_b200.parallel.ulysses_fused import FusedUlysses
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=device)
+    try:
+        heads = 2 * world
+        cfg = LongCatConfig(layers=2, dim=heads * 128, heads=heads, head_dim=128, ffn=1024, text_dim=256, text_len=16,
+                            latent_height=16, latent_width=32, frames_per_chunk=2)
+        model = LongCatDiT(cfg, device, seed=3)
+        gen = torch.Generator(device=device).manual_seed(0)
+        latents = torch.randn((cfg.in_channels, 2, cfg.latent_height, cfg.latent_width), generator=gen, device=device)
+        cond = torch.randn((cfg.in_channels, 2, cfg.latent_height, cfg.latent_width), generator=gen, device=device)
+        text = model.encode_text(torch.randn((cfg.text_len, cfg.text_dim), generator=gen, device=device))
+        epoch = ConditioningCacheEpoch("e0", 0, 0, 2)
+        cache = model.build_conditioning_cache(cond, text, epoch, cp_group=dist.group.WORLD)
+        tokens = 2 * cfg.tokens_per_frame
+        errors = []
+        for use_cache in (False, True):
+            c = cache if use_cache else None
+            ref = model.forward(latents, 0.5, text, first_frame=2, cache=c, cp_group=dist.group.WORLD)
+            fused = FusedUlysses(None, device, heads=cfg.heads, head_dim=cfg.head_dim, rows=tokens,
+                                 cache_rows=tokens if use_cache else 0)
+            got = model.forward(latents, 0.5, text, first_frame=2, cache=c, cp_group=dist.group.WORLD, ulysses=fused)
+            torch.cuda.synchronize()
+            fused.check()
+            errors.append(float((got - ref).norm() / ref.norm()))
+            fused.close()
+        if rank == 0:
+            with open(result_path, "w") as handle:
+                handle.write(",".join(str(e) for e in errors))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_fused_ulysses_forward_matches_nccl(tmp_path, world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    result = tmp_path / "errors.txt"
+    mp.spawn(_worker, args=(world, _free_port(), str(result)), nprocs=world, join=True)
+    errors = [float(v) for v in result.read_text().split(",")]
+    assert all(e < 2e-2 for e in errors), errors
