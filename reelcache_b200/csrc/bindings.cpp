@@ -47,6 +47,9 @@ void ulysses_out(const std::vector<at::Tensor>& o_owners, const at::Tensor& w, c
                  int64_t epilogue, const at::Tensor& stage, const at::Tensor& tile_flags, int64_t call,
                  const c10::optional<at::Tensor>& status);
 void peer_barrier(const at::Tensor& flags, int64_t rank, int64_t epoch, const c10::optional<at::Tensor>& status);
+void gram_reduce_scatter(const at::Tensor& xt, int64_t matrices, const std::vector<at::Tensor>& partials,
+                         const at::Tensor& owners, const at::Tensor& slots, int64_t rank,
+                         const c10::optional<at::Tensor>& status);
 }  // namespace rc
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -64,6 +67,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("status") = py::none());
   m.def("peer_barrier", &rc::peer_barrier, "bounded device-side barrier over peer flag words", py::arg("flags"),
         py::arg("rank"), py::arg("epoch"), py::arg("status") = py::none());
+  m.def("gram_reduce_scatter", &rc::gram_reduce_scatter,
+        "upper-triangular partial Grams of this rank's token shard stored into the owners' buffers (peer stores)",
+        py::arg("xt"), py::arg("matrices"), py::arg("partials"), py::arg("owners"), py::arg("slots"), py::arg("rank"),
+        py::arg("status") = py::none());
   m.def("restore_build", &rc::restore_build, "launch parameters of a fused restore over <= 48 jobs",
         py::arg("jobs"), py::arg("a_ops"), py::arg("b_ops"), py::arg("inverse"));
   m.def("restore_run", &rc::restore_run, "launch a fused restore from restore_build parameters", py::arg("blob"),

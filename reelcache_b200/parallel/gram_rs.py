@@ -1,0 +1,124 @@
+"""Sequence-parallel Gram fit with the reduce-scatter fused into the Gram GEMM over NVLink peer memory (the
+B200 counterpart of reference reelcache/factor_sharding.py:445 ``row_shard_gram`` -- a local Gram and an
+all-reduce over NCCL -- and of the owner-fit gather of factor_sharding.py:1501-1543).
+
+Every rank holds a token shard of each captured matrix; the fit of matrix ``b`` runs on ``owners[b]`` and
+needs ``G_b = sum_r X_{b,r}^T X_{b,r}``. One kernel per rank (csrc/dist/gram_rs.cu) computes the
+upper-triangular 128 x 128 tiles of its partial Grams with FP32-level accuracy (tensor-core partials promoted
+to IEEE adds every 128 tokens) and stores each tile into the owner's symmetric buffer
+``partials[rank][slot]`` as it finishes (NVLink stores for a peer owner), so the transfer overlaps the GEMM and
+only half of each symmetric Gram crosses NVLink. After a bounded device barrier the owner sums the ranks'
+partials in rank order in FP64 and mirrors the upper triangle: deterministic, FP32-accurate Grams.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ..errors import ConfigurationError
+from ..ops._ext import check_status, ext, status_word
+
+
+class GramReduceScatter:
+    def __init__(self, group, device, *, channels: int, max_slots: int):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        if channels % 128:
+            raise ConfigurationError("channels must be a multiple of 128")
+        self.group = group
+        self.device = torch.device(device)
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ConfigurationError("the fused Gram reduce-scatter addresses at most 8 ranks")
+        self.channels, self.max_slots = channels, max_slots
+        part_elems = self.world * max_slots * channels * channels
+        self._flags_offset = part_elems * 4
+        total = self._flags_offset + 256
+        name = group.group_name if group is not None else dist.group.WORLD.group_name
+        if hasattr(symm, "enable_symm_mem_for_group"):
+            try:
+                symm.enable_symm_mem_for_group(name)
+            except Exception:  # noqa: BLE001 - newer releases enable it implicitly
+                pass
+        self.buffer = symm.empty(total, dtype=torch.uint8, device=self.device)
+        self.buffer.zero_()
+        self.handle = symm.rendezvous(self.buffer, group if group is not None else name)
+        shape = (self.world, max_slots, channels, channels)
+        self.partials = []
+        flags = []
+        for peer in range(self.world):
+            if peer == self.rank:
+                self.partials.append(self.buffer[:self._flags_offset].view(torch.float32).view(shape))
+                flags.append(self.buffer[self._flags_offset:self._flags_offset + 4 * self.world].view(torch.int32))
+            else:
+                self.partials.append(self.handle.get_buffer(peer, shape, torch.float32, 0))
+                flags.append(self.handle.get_buffer(peer, (self.world,), torch.int32, self._flags_offset // 4))
+        self.flag_table = torch.tensor([f.data_ptr() for f in flags], dtype=torch.int64, device=self.device)
+        self.epoch = 0
+        self.status = status_word(self.device)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+
+    @staticmethod
+    def slots_for(owners: list[int]) -> list[int]:
+        """Slot of every matrix in its owner's buffer (order of appearance per owner)."""
+        count: dict[int, int] = {}
+        out = []
+        for owner in owners:
+            out.append(count.get(owner, 0))
+            count[owner] = out[-1] + 1
+        return out
+
+    def run(self, xt: torch.Tensor, owners: list[int]) -> dict[int, torch.Tensor]:
+        """``xt``: this rank's shards as X^T stacked ``[B * C, tokens]`` bf16; returns ``{b: G_b}`` (FP32
+        ``[C, C]``) for the matrices this rank owns."""
+        matrices = len(owners)
+        if xt.shape[1] % 8:
+            xt = torch.nn.functional.pad(xt, (0, -xt.shape[1] % 8))  # zero tokens add nothing to a Gram
+        slots = self.slots_for(owners)
+        if max(slots) >= self.max_slots:
+            raise ConfigurationError("more matrices per owner than the buffer has slots")
+        ext().gram_reduce_scatter(xt.contiguous(), matrices, self.partials,
+                                  torch.tensor(owners, dtype=torch.int64), torch.tensor(slots, dtype=torch.int64),
+                                  self.rank, self.status)
+        self.epoch += 1
+        ext().peer_barrier(self.flag_table, self.rank, self.epoch, self.status)
+        out = {}
+        local = self.partials[self.rank]
+        for b, (owner, slot) in enumerate(zip(owners, slots)):
+            if owner == self.rank:
+                out[b] = symmetric_from_upper(local[:, slot].double().sum(0)).float()
+        return out
+
+    def check(self) -> None:
+        check_status(self.device)
+
+    def close(self) -> None:
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self.partials = []
+        self.handle = None
+        self.buffer = None
+
+
+def stacked_transpose(shards: list[torch.Tensor]) -> torch.Tensor:
+    """This rank's token shards ``[tokens, C]`` of the batch's matrices as X^T stacked ``[B * C, tokens_pad]``
+    bf16, the token count padded with zero columns to a multiple of 8 (zero tokens add nothing to a Gram)."""
+    tokens = shards[0].shape[0]
+    pad = -tokens % 8
+    out = torch.zeros((len(shards) * shards[0].shape[1], tokens + pad), dtype=torch.bfloat16, device=shards[0].device)
+    for b, x in enumerate(shards):
+        c = x.shape[1]
+        out[b * c:(b + 1) * c, :tokens].copy_(x.t())
+    return out
+
+
+def symmetric_from_upper(s: torch.Tensor) -> torch.Tensor:
+    """The symmetric matrix whose upper triangle (diagonal included) is that of ``s``."""
+    return torch.triu(s) + torch.triu(s, 1).t()
+
+
+__all__ = ["GramReduceScatter", "stacked_transpose", "symmetric_from_upper"]

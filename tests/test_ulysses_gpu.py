@@ -96,3 +96,32 @@ def test_peer_barrier_single_rank_and_timeout():
     status.zero_()
     torch.zeros(1, device="cuda").add_(1)  # the context still runs work
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("world", [1, 3])
+def test_gram_reduce_scatter_matches_fp64(world):
+    """Partial Grams of every emulated rank's token shard land in the owners' buffers; the owner's rank-order
+    sum (mirrored upper triangle) equals the FP64 Gram of all shards to FP32 accuracy."""
+    E = _ext()
+    from reelcache_b200.parallel.gram_rs import GramReduceScatter, symmetric_from_upper
+    torch.manual_seed(2)
+    channels, matrices = 256, 4
+    owners = [b % world for b in range(matrices)][::-1]
+    slots = GramReduceScatter.slots_for(owners)
+    shards = [[torch.randn(100 + 24 * r, channels, device="cuda").bfloat16() for _ in range(matrices)]
+              for r in range(world)]
+    partials = [torch.zeros(world, max(slots) + 1, channels, channels, device="cuda") for _ in range(world)]
+    status = E.status_word("cuda")
+    from reelcache_b200.parallel.gram_rs import stacked_transpose
+    for r in range(world):
+        xt = stacked_transpose(shards[r])  # token count padded with zero columns to a multiple of 8
+        assert xt.shape[1] % 8 == 0
+        E.ext().gram_reduce_scatter(xt, matrices, partials, torch.tensor(owners), torch.tensor(slots), r, status)
+    torch.cuda.synchronize()
+    E.check_status("cuda")
+    for b in range(matrices):
+        full = torch.cat([shards[r][b] for r in range(world)]).double()
+        ref = full.t() @ full
+        got = symmetric_from_upper(partials[owners[b]][:, slots[b]].double().sum(0))
+        err = float((got - ref).norm() / ref.norm())
+        assert err < 1e-6, (b, err)
