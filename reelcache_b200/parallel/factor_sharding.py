@@ -64,9 +64,18 @@ class FactorShardSpec:
                 "block_rows": self.block_rows}
 
 
-def row_shard_gram(local_rows: torch.Tensor, group=None) -> torch.Tensor:
-    """``X^T X`` of a matrix whose token rows are sharded across ranks (all-reduce of local Grams, FP64)."""
+def row_shard_gram(local_rows: torch.Tensor, group=None, *, fused=None, owner: int = 0) -> torch.Tensor | None:
+    """``X^T X`` of a matrix whose token rows are sharded across ranks.
+
+    Default: all-reduce of the local FP64 Grams (every rank gets it). ``fused``: a
+    :class:`~reelcache_b200.parallel.gram_rs.GramReduceScatter` -- the partial Grams (bf16 rows, FP32-accurate)
+    travel straight from the Gram kernel into ``owner``'s buffer over NVLink; ``owner`` gets the FP32 Gram and
+    the other ranks ``None``."""
     import torch.distributed as dist
+    if fused is not None:
+        from .gram_rs import stacked_transpose
+        grams = fused.run(stacked_transpose([local_rows.to(torch.bfloat16)]), [owner])
+        return grams.get(0)
     x = local_rows.double()
     g = x.t() @ x
     if dist.is_available() and dist.is_initialized():
