@@ -231,3 +231,19 @@ def test_sp_tiered_history(tmp_path):
 
 def test_row_sharded_cache_archive_and_tiers(tmp_path):
     run("w_row_archive", 2, str(tmp_path))
+
+
+def test_gram_rs_host_helpers():
+    """Slots per owner follow the order of appearance; the stacked X^T pads tokens with zero columns (which add
+    nothing to a Gram); the mirrored upper triangle of a symmetric matrix's partial sum is the matrix."""
+    from reelcache_b200.parallel.gram_rs import GramReduceScatter, stacked_transpose, symmetric_from_upper
+    assert GramReduceScatter.slots_for([0, 1, 0, 2, 1, 0]) == [0, 0, 1, 0, 1, 2]
+    torch.manual_seed(0)
+    shards = [torch.randn(13, 4), torch.randn(13, 4)]
+    xt = stacked_transpose(shards)
+    assert xt.shape == (8, 16) and xt.dtype == torch.bfloat16
+    assert torch.equal(xt[:4, :13], shards[0].t().bfloat16()) and not xt[:, 13:].any()
+    x = xt[:4].double()
+    gram = x @ x.t()
+    upper_only = torch.triu(gram) + torch.tril(torch.full_like(gram, 7.0), -1)
+    assert torch.allclose(symmetric_from_upper(upper_only), gram)
