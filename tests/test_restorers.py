@@ -91,3 +91,18 @@ def test_factor_pack_storage_and_dense_history(tmp_path):
     # representation-specific restorers refuse other kinds
     with pytest.raises(UnsupportedError):
         _restore(RawLineageRestorer(runtime, "cpu"), runtime, node, 2)
+
+
+def test_rank_report_of_a_lineage(tmp_path):
+    """The rank-study report walks the head's path: one entry per node with per-layer K/V ranks, energy against
+    the targets, bytes and a compression ratio above 1; comparing a report with itself shows equal columns."""
+    from reelcache_b200.rank_report import compare, lineage_report, main
+    runtime, node, _ = _commit(tmp_path, "svd_hevc")
+    report = lineage_report(runtime, node)
+    assert report["summary"]["nodes"] == 3 and report["summary"]["compression_ratio"] > 1
+    first = report["nodes"][0]
+    assert len(first["ranks"]["K"]) == MODEL.layers and first["energy"]["K"]["targets_met"] == MODEL.layers
+    same = compare(report, report)
+    assert all(row["bytes_a"] == row["bytes_b"] for row in same["nodes"])
+    runtime.store.close()
+    main(["--store", str(tmp_path / "svd_hevc"), "--node", node])
