@@ -355,32 +355,35 @@ class LineageRestorer:
         copy_stream = self._copy_stream()
         if plan.done is not None:
             copy_stream.wait_event(plan.done)
-        events = []
+        # Overlapped: one launch per layer, so the forward's layer L waits for layer L only. Otherwise
+        # consecutive layers share a launch (up to 48 jobs) and their pack bytes one copy per pack: fewer,
+        # fuller launches and copies (the host issues a handful of copies instead of one per layer and pack).
+        units = [(layer,) for layer in range(model.layers)] if overlapped else program.batches()
+        events = {}
         with torch.cuda.stream(copy_stream):
-            for layer in range(model.layers):
-                for packet_ref, (lo, hi) in plan.copies[layer]:
+            for unit in units:
+                spans: dict[str, tuple[int, int]] = {}
+                for layer in unit:
+                    for packet_ref, (lo, hi) in plan.copies[layer]:
+                        old = spans.get(packet_ref)
+                        spans[packet_ref] = (lo, hi) if old is None else (min(old[0], lo), max(old[1], hi))
+                for packet_ref, (lo, hi) in spans.items():
                     host = self.prepared_pack(packet_ref).raw
                     plan.device_raw[packet_ref][lo:hi].copy_(host[lo:hi], non_blocking=True)
                     self.stats_["h2d_bytes"] += hi - lo
                 event = torch.cuda.Event()
                 event.record(copy_stream)
-                events.append(event)
+                for layer in unit:
+                    events[layer] = event
         self.stats_["restores"] += 1
-
-        # Overlapped: one launch per layer, so the forward's layer L waits for layer L only. Otherwise
-        # consecutive layers share a launch (up to 48 jobs): fewer, fuller launches.
-        batch_of = {}
-        if not overlapped:
-            for batch in program.batches():
-                batch_of[batch[0]] = batch
+        batch_of = {unit[0]: unit for unit in units}
 
         def issue(layer):
             if overlapped:
                 stream.wait_event(events[layer])
                 program.launch(layer, stream, aux=True)
             elif layer in batch_of:
-                for member in batch_of[layer]:
-                    stream.wait_event(events[member])
+                stream.wait_event(events[layer])
                 program.launch_batch(batch_of[layer], stream, aux=True)
 
         def finish():
