@@ -29,6 +29,7 @@ def main(argv=None):
     ap.add_argument("--rate", type=float, default=2.0)
     ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--realtime", action="store_true", help="honour the Poisson arrival times")
+    ap.add_argument("--resident-gb", type=float, default=40.0, help="budget of the sessions' resident caches")
     ap.add_argument("--out", type=Path)
     args = ap.parse_args(argv)
     sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
@@ -45,14 +46,16 @@ def main(argv=None):
     spec = WorkloadSpec(sessions=args.sessions, rate_per_s=args.rate, requests=args.requests,
                         min_history=args.min_history, max_history=args.max_history)
     with tempfile.TemporaryDirectory(prefix="reelcache-sessions-") as root:
-        config = ReelCacheRuntimeConfig(store_root=root, fit_device="cuda", encode_workers=2)
+        config = ReelCacheRuntimeConfig(store_root=root, fit_device="cuda", encode_workers=2,
+                                        max_resident_bytes=int(args.resident_gb * (1 << 30)))
         bridge = create_sglang_backend(config, (model, text_kv), cache_chunks=args.max_history + 4)
         try:
             result = run(bridge, spec, realtime=args.realtime)
         finally:
             bridge.shutdown()
     summary = result.summary()
-    summary.update(device=torch.cuda.get_device_name(0), layers=cfg.layers, spec=vars(args) | {"out": None})
+    summary.update(device=torch.cuda.get_device_name(0), layers=cfg.layers, spec=vars(args) | {"out": None},
+                   resident_evictions=bridge.resident_evictions)
     text = json.dumps(summary, indent=1, default=str)
     print(text)
     if args.out:

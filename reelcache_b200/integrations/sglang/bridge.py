@@ -52,6 +52,8 @@ class CausalWanKVBridge:
         self.telemetry = WorkloadTelemetry(enabled=config.workload_telemetry)
         self.defer = GenerationDefer.from_config(config, getattr(self.archive, "pipeline", None))
         self._requests = 0
+        self._uses = 0
+        self.resident_evictions = 0
         self._current = None
         self._lock = threading.RLock()
 
@@ -107,7 +109,10 @@ class CausalWanKVBridge:
         restore_stats: dict = {}
         if not (self.config.resident_reuse and cache is not None and state.resident_chunks >= start_chunk
                 and need <= self._capacity(cache)):
-            cache = self.engine.new_cache(max(need, self.cache_chunks))
+            capacity = max(need, self.cache_chunks)
+            state.resident = None  # replaced below; its memory may be reused
+            self._make_resident_room(capacity * self._chunk_bytes(), keep=state)
+            cache = self.engine.new_cache(capacity)
             route = "none"
             if start_chunk > 0:
                 published = len(self.sessions.chunks(state.session_id))
@@ -158,6 +163,8 @@ class CausalWanKVBridge:
                 self.archive.drain(state.session_id)
         state.resident = cache
         state.resident_chunks = state.generated
+        self._uses += 1
+        state.resident_used = self._uses
         self.sessions.reconcile(state)
         report = {"session": state.session_id, "start_chunk": start_chunk, "chunks": chunks, "route": route,
                   "ttfc_ms": ttfc_ms, "restore": restore_stats, "generated": state.generated,
@@ -166,6 +173,30 @@ class CausalWanKVBridge:
         if cuda and first_event is not None:
             report["ttfc_gpu_ms"] = start_event.elapsed_time(first_event)
         return report
+
+    def _chunk_bytes(self) -> int:
+        """Bytes of one chunk of native K/V history (16-bit cache)."""
+        p = self.profile
+        return 2 * p.num_layers * p.chunk_tokens * p.num_heads * p.head_dim * 2 * max(1, len(p.cfg_streams or ()))
+
+    @staticmethod
+    def _cache_bytes(cache) -> int:
+        tensors = (list(cache["k"]) + list(cache["v"])) if isinstance(cache, dict) else (list(cache.k) + list(cache.v))
+        return sum(t.numel() * t.element_size() for t in tensors)
+
+    def _make_resident_room(self, nbytes: int, *, keep) -> None:
+        """Drop the least recently used sessions' resident caches (never ``keep``'s) until ``nbytes`` more fit
+        under ``max_resident_bytes``; a dropped session restores from the raw tier or the archive next time."""
+        budget = self.config.max_resident_bytes
+        holders = sorted((s for s in self.sessions.resident_states() if s is not keep), key=lambda s: s.resident_used)
+        total = sum(self._cache_bytes(s.resident) for s in holders)
+        for victim in holders:
+            if total + nbytes <= budget:
+                break
+            total -= self._cache_bytes(victim.resident)
+            victim.resident = None
+            victim.resident_chunks = 0
+            self.resident_evictions += 1
 
     def _capacity(self, cache) -> int:
         """Chunks of history a cache can hold."""

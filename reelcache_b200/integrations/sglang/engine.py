@@ -30,7 +30,7 @@ from .profiles import ModelProfile
 class InstallResult:
     """Handle of an installed (possibly still running) history restore."""
 
-    wait: Callable[[int], None]
+    wait: Callable[..., None]  # wait(layer[, stream])
     join: Callable[[], Any]
     stats: dict
 
@@ -137,7 +137,8 @@ class CausalWanEngine:
             result.lease.close()
             return stats
 
-        return InstallResult(lambda layer: result.wait(layer), join, result.stats)
+        # the DiT calls wait(layer, stream): the stream is ordered after the layer's restore events
+        return InstallResult(lambda layer, stream=None: result.wait(layer, stream), join, result.stats)
 
 
 def model_identity_for(profile: ModelProfile, fingerprint: str) -> ModelIdentity:

@@ -37,6 +37,7 @@ class SGLangSessionState:
     generated: int = 0                 # chunks submitted (generated frontier)
     resident: Any = None               # engine cache currently holding this session's history
     resident_chunks: int = 0           # chunks of history the resident cache holds (of the generated path)
+    resident_used: int = 0             # request counter of the last use of the resident cache (LRU order)
     pending: list = field(default_factory=list)   # archive tickets not yet published
     failure: BaseException | None = None
     pause_requested: bool = False
@@ -62,6 +63,11 @@ class SGLangSessionController:
         self._states: dict[str, SGLangSessionState] = {}
 
     # -- lookup ---------------------------------------------------------------------------------------------------
+
+    def resident_states(self) -> list[SGLangSessionState]:
+        """Sessions holding a resident engine cache."""
+        with self._lock:
+            return [state for state in self._states.values() if state.resident is not None]
 
     def get(self, session_id: str, *, required: bool = True) -> SGLangSessionState | None:
         with self._lock:

@@ -45,11 +45,18 @@ def matmul_promoted(a: torch.Tensor, b: torch.Tensor, *, alpha: float = 1.0) -> 
     return out
 
 
+#: A bf16 left operand is its own hi part (mid = lo = 0): three segments a x (lo, mid, hi of b) carry every
+#: nonzero cross product of the six, so the GEMM's K halves with the same result.
+SPLIT_A_BF16 = (0, 0, 0)
+SPLIT_B_BF16 = (2, 1, 0)
+
+
 def mm_fp32(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """FP32-accurate ``a @ b`` (``a[M, K]``, ``b[K, N]``): split-bf16 operands, one tcgen05 GEMM with promoted
     accumulation."""
-    a_split, _ = split_operand(a, SPLIT_A)
-    b_split, _ = split_operand(b.t(), SPLIT_B)
+    parts_a, parts_b = (SPLIT_A_BF16, SPLIT_B_BF16) if a.dtype == torch.bfloat16 else (SPLIT_A, SPLIT_B)
+    a_split, _ = split_operand(a, parts_a)
+    b_split, _ = split_operand(b.t(), parts_b)
     return matmul_promoted(a_split, b_split)
 
 

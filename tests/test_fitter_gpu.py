@@ -39,6 +39,18 @@ def test_split_gemm_is_fp32_accurate(m, k, n):
     assert torch.equal(got_t, got)
 
 
+def test_split_gemm_with_bf16_left_operand_matches_the_six_product_path():
+    """A bf16 left operand takes the three-segment split; the result equals the six-segment split of the same
+    values converted to FP32 (the three dropped products are exactly zero) and stays FP32-accurate."""
+    from reelcache_b200 import exact_blas
+    g = torch.Generator(device="cuda").manual_seed(7)
+    a = torch.randn(4680, 1536, device="cuda", generator=g).bfloat16()
+    b = torch.randn(1536, 64, device="cuda", generator=g)
+    got = exact_blas.mm(a, b)
+    assert torch.allclose(got, exact_blas.mm(a.float(), b), rtol=2e-6, atol=1e-5)
+    assert _err(got, a.double() @ b.double()) < 2e-6
+
+
 @pytest.mark.parametrize("k", [64, 4680, 28080])
 def test_promoted_accumulation_matches_sgemm(k):
     from reelcache_b200.ops.fitter import matmul_promoted

@@ -82,3 +82,26 @@ def test_longcat_kernels_match_torch_path(cuda_device):
         outs.append(model.forward(latents, 0.7, text, first_frame=1, cache=cache))
     rel = float((outs[0] - outs[1]).norm() / outs[1].norm())
     assert rel < 0.05, rel
+
+
+def test_bridge_with_the_dit_restores_a_fork_from_the_archive(cuda_device, tmp_path):
+    """The serving bridge around the fused-kernel DiT: a session is created, paused (durable archive) and forked
+    from an earlier checkpoint -- a restore overlapped with the first denoising step, the DiT waiting per layer
+    (with its stream) on the restore -- and the fork's first chunk is generated."""
+    from reelcache_b200.integrations.sglang import ReelCacheRuntimeConfig, create_sglang_backend
+    from reelcache_b200.models.causal_wan import CausalWanDiT
+    cfg = _small()
+    model = CausalWanDiT(cfg, cuda_device, seed=3)
+    text_kv = model.encode_text(torch.randn(cfg.text_len, cfg.text_dim, device=cuda_device,
+                                            generator=torch.Generator(device=cuda_device).manual_seed(1)))
+    config = ReelCacheRuntimeConfig(store_root=str(tmp_path / "store"), fit_device="cuda", encode_workers=1)
+    bridge = create_sglang_backend(config, (model, text_kv), cache_chunks=6)
+    try:
+        first = bridge.request("s", chunks=3, action="create", seed=1)
+        assert first["generated"] == 3
+        bridge.pause("s")
+        fork = bridge.request("f", chunks=1, action="fork", source="s", checkpoint=2, seed=1)
+        assert fork["route"] in ("archive", "raw_tier") and fork["start_chunk"] == 2
+        assert fork["ttfc_ms"] is not None and fork["ttfc_ms"] > 0
+    finally:
+        bridge.shutdown()

@@ -134,3 +134,20 @@ def test_other_representations_restore(tmp_path, representation, raw_tier, bound
         assert stats.get("representation", representation) == representation or representation == "svd"
     finally:
         bridge.shutdown()
+
+
+def test_resident_caches_stay_under_the_budget(tmp_path):
+    """``max_resident_bytes`` bounds the sessions' resident engine caches: creating more sessions than fit drops
+    the least recently used residents, and a dropped session's next request restores its history instead."""
+    bridge = make_bridge(tmp_path, max_resident_bytes=2 * 8 * 2 * TINY.num_layers * TINY.chunk_tokens
+                         * TINY.num_heads * TINY.head_dim * 2)
+    try:
+        for name in ("a", "b", "c"):
+            bridge.request(name, chunks=2, action="create", seed=1)
+            bridge.pause(name)
+        holders = [s.session_id for s in bridge.sessions.resident_states()]
+        assert "c" in holders and len(holders) <= 2 and bridge.resident_evictions >= 1
+        report = bridge.request("a", chunks=1, seed=1)
+        assert report["route"] == "archive" and report["start_chunk"] == 2
+    finally:
+        bridge.shutdown()
