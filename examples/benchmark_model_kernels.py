@@ -24,6 +24,8 @@ def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--tokens", type=int, default=4680)
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--only", choices=("all", "norms"), default="all",
+                    help="norms: only the memory-bound ops (a short run for profiling)")
     ap.add_argument("--out", type=Path)
     args = ap.parse_args(argv)
     root = Path(__file__).resolve().parents[1]
@@ -91,7 +93,9 @@ def main(argv=None):
     record("dense_rope_store", timed(lambda i: rk.reconstruct([jobs[i]], backend="fused"), len(jobs)),
            nbytes=2 * T * C * 2)
     # the block's GEMMs: tcgen05 kernel vs cuBLAS (bf16 in, bf16 out)
-    for name, n, k in (("qkv", 3 * C, C), ("out_proj", C, C), ("ffn_up", F, C), ("ffn_down", C, F)):
+    gemms = () if args.only == "norms" else ((("qkv", 3 * C, C), ("out_proj", C, C), ("ffn_up", F, C),
+                                               ("ffn_down", C, F)))
+    for name, n, k in gemms:
         a_ring = ring(lambda: torch.randn(T, k, device=device).bfloat16(), T * k * 2)
         wt = (torch.randn(n, k, device=device) / k ** 0.5).bfloat16()
         outs = [torch.empty(T, n, device=device, dtype=torch.bfloat16) for _ in range(2)]
@@ -101,11 +105,11 @@ def main(argv=None):
         record(f"gemm_{name}_cublas", timed(lambda i: torch.matmul(a_ring[i], wt.t(), out=outs[i % 2]), len(a_ring)),
                flops=flops)
     # raw-tier staging: one chunk's 60 K/V matrices device -> pinned host -> device on a side stream
-    mats = [torch.randn(T, C, device=device).bfloat16() for _ in range(60)]
-    hosts = [torch.empty(T, C, dtype=torch.bfloat16, pin_memory=True) for _ in range(60)]
+    mats = [torch.randn(T, C, device=device).bfloat16() for _ in range(60 if args.only == "all" else 0)]
+    hosts = [torch.empty(T, C, dtype=torch.bfloat16, pin_memory=True) for _ in range(len(mats))]
     side = torch.cuda.Stream(device)
     nbytes = 60 * T * C * 2
-    for direction in ("d2h", "h2d"):
+    for direction in ("d2h", "h2d") if mats else ():
         def copy_all(_):
             with torch.cuda.stream(side):
                 for m, h in zip(mats, hosts):
