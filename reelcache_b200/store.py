@@ -244,6 +244,9 @@ class ObjectStore:
                           "existing_calls": 0, "existing_bytes": 0, "errors": 0, "last_error": None}
         self._evicted: set[str] = set()
         self._unevicted: list[str] = []
+        # objects whose whole subtree a reference update already checked in this process (immutable content:
+        # the next update only walks what is new below them)
+        self._verified: set[str] = set()
         try:
             with self._lock:
                 fcntl.flock(self._lock_file, fcntl.LOCK_EX)
@@ -698,8 +701,13 @@ class ObjectStore:
     # -- graph walks, audits -------------------------------------------------------------------------------------
 
     def _walk(self, object_ids: Iterable[str], *, verify: bool, damaged: dict[str, str] | None = None,
-              force: bool = False) -> set[str]:
-        """Every object reachable from ``object_ids``; checks existence (and content when verifying)."""
+              force: bool = False, cached: bool = False) -> set[str]:
+        """Every object reachable from ``object_ids``; checks existence (and content when verifying).
+
+        ``cached`` (reference updates only; the returned set is then not the full reachable set): an object
+        whose subtree an earlier cached walk of this process checked is only checked to still exist -- the
+        collector never removes a child that an existing manifest references -- and its subtree is not
+        walked again, so publishing a node costs the new objects, not the whole history."""
         seen: set[str] = set()
         stack = list(object_ids)
         while stack:
@@ -707,6 +715,9 @@ class ObjectStore:
             if object_id in seen:
                 continue
             seen.add(object_id)
+            if cached and object_id in self._verified:
+                self._require(object_id)
+                continue
             try:
                 self.path_for(object_id)
                 if object_id.startswith("manifest:"):
@@ -728,6 +739,8 @@ class ObjectStore:
                 damaged[object_id] = str(exc)
                 stack.extend(row[0] for row in self._db.execute(
                     "SELECT child FROM edges WHERE parent=?", (object_id,)))
+        if cached:
+            self._verified |= seen
         return seen
 
     def verify(self, object_id: str, *, recursive: bool = True) -> None:
@@ -765,7 +778,7 @@ class ObjectStore:
             current = self.get_ref(name)
             if expected is not _ANY and current != expected:
                 raise StateError(f"reference changed concurrently: {name}")
-            self._walk([object_id], verify=True)
+            self._walk([object_id], verify=True, cached=True)
             self._db.execute("INSERT INTO refs VALUES (?, ?) ON CONFLICT(name) DO UPDATE SET "
                              "object_id=excluded.object_id", (name, object_id))
 
@@ -883,6 +896,7 @@ class ObjectStore:
                 self._db.execute("DELETE FROM objects WHERE id=?", (object_id,))
                 self._events.append(("deleted", object_id))
             self._evicted.difference_update(dead)
+            self._verified.difference_update(dead)
         with self.transaction():
             removed, reclaimed = self._recover_files()
             self._recovered_staging.difference_update(recovered)

@@ -88,13 +88,18 @@ def test_bridge_with_the_dit_restores_a_fork_from_the_archive(cuda_device, tmp_p
     """The serving bridge around the fused-kernel DiT: a session is created, paused (durable archive) and forked
     from an earlier checkpoint -- a restore overlapped with the first denoising step, the DiT waiting per layer
     (with its stream) on the restore -- and the fork's first chunk is generated."""
-    from reelcache_b200.integrations.sglang import ReelCacheRuntimeConfig, create_sglang_backend
+    import dataclasses
+    from reelcache_b200.integrations.sglang import ReelCacheRuntimeConfig, create_sglang_backend, get_profile
     from reelcache_b200.models.causal_wan import CausalWanDiT
     cfg = _small()
+    profile = dataclasses.replace(get_profile("causvid"), name="causvid-small", num_layers=cfg.layers,
+                                  num_heads=cfg.heads, head_dim=cfg.head_dim, chunk_frames=cfg.frames_per_chunk,
+                                  grid=(cfg.grid_h, cfg.grid_w))
     model = CausalWanDiT(cfg, cuda_device, seed=3)
     text_kv = model.encode_text(torch.randn(cfg.text_len, cfg.text_dim, device=cuda_device,
                                             generator=torch.Generator(device=cuda_device).manual_seed(1)))
-    config = ReelCacheRuntimeConfig(store_root=str(tmp_path / "store"), fit_device="cuda", encode_workers=1)
+    config = ReelCacheRuntimeConfig(store_root=str(tmp_path / "store"), fit_device="cuda", encode_workers=1,
+                                    profile_fields=profile.to_dict())
     bridge = create_sglang_backend(config, (model, text_kv), cache_chunks=6)
     try:
         first = bridge.request("s", chunks=3, action="create", seed=1)

@@ -121,3 +121,24 @@ def test_telemetry_sidecar_not_in_content(tmp_path):
         store.put_telemetry(m, {"seconds": 1.5})
         assert store.telemetry(m) == {"seconds": 1.5}
         assert store.put_manifest({"a": 1}) == m
+
+
+def test_reference_updates_walk_only_new_objects(tmp_path):
+    """A reference update checks each new object once: a chain of nodes published one after another walks only
+    what each node adds (the checked history is not read again), and collection after the updates still keeps
+    every reachable object."""
+    with ObjectStore(tmp_path / "s") as store:
+        head = None
+        for i in range(5):
+            blob = store.put(f"payload {i}".encode())
+            head = store.put_manifest({"i": i}, references=[blob] + ([head] if head else []))
+            store.set_ref("heads/main", head)
+        reads = []
+        original = store._manifest
+        store._manifest = lambda object_id: (reads.append(object_id), original(object_id))[1]
+        blob = store.put(b"payload 5")
+        top = store.put_manifest({"i": 5}, references=[blob, head])
+        store.set_ref("heads/main", top)
+        store._manifest = original
+        assert head not in reads  # the previous head's subtree was checked by the previous update
+        assert store.collect_garbage()["live_objects"] == 12
