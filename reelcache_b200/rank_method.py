@@ -209,7 +209,7 @@ def fp16_rows(directions: torch.Tensor) -> torch.Tensor:
     return directions.t().contiguous().to(torch.float16)
 
 
-def stored_energy(x: torch.Tensor, rows: torch.Tensor, total: float, tile_rows: int = 4096) -> tuple[float, torch.Tensor]:
+def stored_energy(x: torch.Tensor, rows: torch.Tensor, total: float, tile_rows: int = 16384) -> tuple[float, torch.Tensor]:
     """Energy of the actual stored representation: FP16 ``rows``, FP32 ``P = A Q^T``, direct residual
     ``||A - P Q||^2`` accumulated in FP64 over row tiles. Returns (energy, P)."""
     q = rows.float()
