@@ -85,12 +85,14 @@ class GramReduceScatter:
                                   self.rank, self.status)
         self.epoch += 1
         ext().peer_barrier(self.flag_table, self.rank, self.epoch, self.status)
-        out = {}
-        local = self.partials[self.rank]
-        for b, (owner, slot) in enumerate(zip(owners, slots)):
-            if owner == self.rank:
-                out[b] = symmetric_from_upper(local[:, slot].double().sum(0)).float()
-        return out
+        owned = [b for b, owner in enumerate(owners) if owner == self.rank]
+        if not owned:
+            return {}
+        # every owned matrix at once: rank-order FP64 sum of the partials, then the mirrored upper triangle
+        index = torch.tensor([slots[b] for b in owned], device=self.device)
+        sums = self.partials[self.rank].index_select(1, index).double().sum(0)
+        grams = symmetric_from_upper(sums).float()
+        return {b: grams[i] for i, b in enumerate(owned)}
 
     def check(self) -> None:
         check_status(self.device)
@@ -117,8 +119,8 @@ def stacked_transpose(shards: list[torch.Tensor]) -> torch.Tensor:
 
 
 def symmetric_from_upper(s: torch.Tensor) -> torch.Tensor:
-    """The symmetric matrix whose upper triangle (diagonal included) is that of ``s``."""
-    return torch.triu(s) + torch.triu(s, 1).t()
+    """The symmetric matrix (or batch of matrices) whose upper triangle (diagonal included) is that of ``s``."""
+    return torch.triu(s) + torch.triu(s, 1).transpose(-1, -2)
 
 
 __all__ = ["GramReduceScatter", "stacked_transpose", "symmetric_from_upper"]
