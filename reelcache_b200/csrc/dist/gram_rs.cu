@@ -6,7 +6,7 @@
 // by a reduce (or all-reduce) over NCCL of the full C x C FP32 Gram. Here one persistent kernel computes,
 // for a batch of matrices stacked as X^T [B * C, n_r] (bf16, K-major), every UPPER-TRIANGULAR 128 x 128 tile
 // of X_r^T X_r (a Gram is symmetric, so half the tiles and half the NVLink bytes) with the tensor-core
-// partials promoted to IEEE FP32 adds every 128 tokens (gemm_exact.cu: FP32-level accuracy), and the
+// partials promoted to IEEE FP32 adds every 256 tokens (as gemm_exact.cu does every 128: FP32-level accuracy), and the
 // epilogue stores each finished tile straight into the owner's symmetric partial buffer
 // partials[rank][slot][C][C] (peer stores when the owner is another rank), so a tile's transfer overlaps
 // the MMAs of the next. After a device barrier the owner sums the P partials in rank order (deterministic)
@@ -32,7 +32,7 @@ constexpr int kMaxMatrices = 64;
 constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kBK = 64;
-constexpr int kChunk = 2;  // K-blocks per TMEM partial (128 tokens)
+constexpr int kChunk = 4;  // K-blocks per TMEM partial (256 tokens: still FP32-level, half the promotions)
 constexpr int kBufs = 4;
 constexpr int kThreads = 192;
 constexpr int kABytes = kBM * kBK * 2;

@@ -5,7 +5,7 @@ all-reduce over NCCL -- and of the owner-fit gather of factor_sharding.py:1501-1
 Every rank holds a token shard of each captured matrix; the fit of matrix ``b`` runs on ``owners[b]`` and
 needs ``G_b = sum_r X_{b,r}^T X_{b,r}``. One kernel per rank (csrc/dist/gram_rs.cu) computes the
 upper-triangular 128 x 128 tiles of its partial Grams with FP32-level accuracy (tensor-core partials promoted
-to IEEE adds every 128 tokens) and stores each tile into the owner's symmetric buffer
+to IEEE adds every 256 tokens) and stores each tile into the owner's symmetric buffer
 ``partials[rank][slot]`` as it finishes (NVLink stores for a peer owner), so the transfer overlaps the GEMM and
 only half of each symmetric Gram crosses NVLink. After a bounded device barrier the owner sums the ranks'
 partials in rank order in FP64 and mirrors the upper triangle: deterministic, FP32-accurate Grams.

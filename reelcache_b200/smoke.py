@@ -29,7 +29,7 @@ def run(device):
     table = rk.RopeTable.wan(head_dim, 32, device=device)
     job = rk.ReconstructionJob(source, rk.NativeView(cache), (frames, height, width), basis,
                                rope=rk.RopePositions(table, (0, 0, 0)))
-    rk.reconstruct([job], backend="fused").release()
+    rk.reconstruct([job], backend="fused", precision="fp16x2").release()  # the precision its bound describes
     _ext.check_status(device)
     expect, bound = rk.kernel_error_bound(job, "fp16x2")
     got = cache[0].reshape(tokens, -1).double()
