@@ -190,13 +190,15 @@ __global__ void __launch_bounds__(kThreads, 1) gram_rs_kernel(const __grid_const
         if (!ok) break;
         tc_fence_after();
         const uint32_t taddr = tmem_base + buf * kBN + (static_cast<uint32_t>(quarter * 32) << 16);
+        // 32-column slices, the next one's TMEM read in flight while this one is added
+        uint32_t raw[2][32];
+        tmem_ld_32x32b_x32(taddr, raw[0]);
 #pragma unroll
         for (int q = 0; q < kBN / 32; ++q) {
-          uint32_t raw[32];
-          tmem_ld_32x32b_x32(taddr + q * 32, raw);
           tmem_wait_ld();
+          if (q + 1 < kBN / 32) tmem_ld_32x32b_x32(taddr + (q + 1) * 32, raw[(q + 1) & 1]);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[q * 32 + j] = __fadd_rn(acc[q * 32 + j], __uint_as_float(raw[j]));
+          for (int j = 0; j < 32; ++j) acc[q * 32 + j] = __fadd_rn(acc[q * 32 + j], __uint_as_float(raw[q & 1][j]));
         }
         tc_fence_before();
         __syncwarp();

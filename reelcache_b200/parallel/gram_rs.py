@@ -8,7 +8,7 @@ upper-triangular 128 x 128 tiles of its partial Grams with FP32-level accuracy (
 to IEEE adds every 256 tokens) and stores each tile into the owner's symmetric buffer
 ``partials[rank][slot]`` as it finishes (NVLink stores for a peer owner), so the transfer overlaps the GEMM and
 only half of each symmetric Gram crosses NVLink. After a bounded device barrier the owner sums the ranks'
-partials in rank order in FP64 and mirrors the upper triangle: deterministic, FP32-accurate Grams.
+partials in rank order in FP32 and mirrors the upper triangle: deterministic, FP32-accurate Grams.
 """
 
 from __future__ import annotations
@@ -88,11 +88,15 @@ class GramReduceScatter:
         owned = [b for b, owner in enumerate(owners) if owner == self.rank]
         if not owned:
             return {}
-        # every owned matrix at once: rank-order FP64 sum of the partials, then the mirrored upper triangle
-        index = torch.tensor([slots[b] for b in owned], device=self.device)
-        sums = self.partials[self.rank].index_select(1, index).double().sum(0)
-        grams = symmetric_from_upper(sums).float()
-        return {b: grams[i] for i, b in enumerate(owned)}
+        # every owned matrix at once (an owner's slots are 0 .. n - 1): FP32 sum of the ranks' partials in rank
+        # order, then the mirrored upper triangle
+        local = self.partials[self.rank]
+        count = len(owned)
+        sums = local[0, :count].clone()
+        for rank in range(1, self.world):
+            sums += local[rank, :count]
+        grams = symmetric_from_upper(sums)
+        return {b: grams[slots[b]] for b in owned}
 
     def check(self) -> None:
         check_status(self.device)
