@@ -379,9 +379,11 @@ class ReelCacheConditioningCacheBackend:
         self.stats["built"] += 1
         return commit.node_ref
 
-    def restore(self, epoch: ConditioningCacheEpoch) -> LongCatConditioningCache | None:
+    def restore(self, epoch: ConditioningCacheEpoch, node_ref: str | None = None) -> LongCatConditioningCache | None:
+        """``node_ref`` names the segment node directly (a fork or a resumed session restores another session's
+        epoch, whose id differs); otherwise the node this backend committed for ``epoch``."""
         from ..types import MatrixKey
-        node = self.segments.get(epoch.epoch_id)
+        node = node_ref or self.segments.get(epoch.epoch_id)
         if node is None:
             self.stats["missed"] += 1
             return None

@@ -248,6 +248,7 @@ class LongCatSessionProvider:
         self.gate = gate or PlanningGate()
         self.store = backend.runtime.store
         self.reports: list[SegmentReport] = []
+        self.nodes: dict[str, str] = {}      # content key -> archived segment node (built here or read from records)
 
     def _ref(self, session_id: str) -> str:
         return f"{SESSION_PREFIX}{session_id}"
@@ -274,12 +275,14 @@ class LongCatSessionProvider:
                                        int(cond_latents.shape[1]))
         device = self.backend.device
         hit = self.tiers.lookup(key, device)
-        node_ref = self.tiers.node_of(key)
+        node_ref = self.tiers.node_of(key) or self.nodes.get(key)
         if hit is not None:
             tier, cache = hit
             cache = LongCatConditioningCache(epoch, cache.k, cache.v)
         else:
-            cache = self.backend.restore(epoch)
+            # the archived node of the same content restores under this session's epoch id (forks and resumed
+            # sessions reach another session's segment node through the content key)
+            cache = self.backend.restore(epoch, node_ref=node_ref)
             tier = "compressed_cold" if cache is not None else "built"
             if cache is None:
                 with self.gate.section():
@@ -288,7 +291,9 @@ class LongCatSessionProvider:
                 node_ref = self.backend.on_cache_built(cache)
                 self.tiers.published(key, node_ref)
             else:
-                node_ref = self.backend.segments.get(epoch.epoch_id)
+                node_ref = node_ref or self.backend.segments.get(epoch.epoch_id)
+        if node_ref is not None:
+            self.nodes[key] = node_ref
         if tier in ("built", "compressed_cold"):
             self.tiers.records["hits"][tier] += 1
         self._record(session_id, {"segment": segment_index, "epoch": epoch.epoch_id, "first_frame": first_frame,
@@ -304,6 +309,9 @@ class LongCatSessionProvider:
         if not 0 <= boundary < len(boundaries):
             raise ConfigurationError(f"session {session_id} has no boundary {boundary}")
         kept = boundaries[:boundary + 1]
+        for b in kept:
+            if b.get("node_ref") and b.get("content_key"):
+                self.nodes.setdefault(b["content_key"], b["node_ref"])
         target = new_session or session_id
         head, last = kept[:-1], kept[-1]
         self._record(target, last, base=head)

@@ -128,6 +128,15 @@ def test_epoch_tiers_planning_gate_and_session_provider(tmp_path):
     assert [b["segment"] for b in provider.boundaries("s")] == [0, 1, 2]
     kept = provider.resume("s", 1, new_session="fork")
     assert [b["segment"] for b in provider.boundaries("fork")] == [0, 1] and len(kept) == 2
+    # a fork whose epoch left every raw tier restores the archived node of the same content (its epoch id differs)
+    provider.tiers = EpochRawTiers(host_raw_budget_bytes=0, pin_memory=False)
+    forked, tier = provider.segment_cache("fork", 2, cond2, text, first_frame=4, base=kept)
+    assert tier == "compressed_cold" and backend.stats["restored"] == 1
+    assert forked.epoch.epoch_id.startswith("fork:2:") and forked.tokens == built.tokens
+    fresh = LongCatSessionProvider(model, backend, EpochRawTiers(host_raw_budget_bytes=0, pin_memory=False))
+    fresh.resume("s", 2, new_session="fork2")     # a new provider learns the nodes from the session record
+    _, tier = fresh.segment_cache("fork2", 2, cond2, text, first_frame=4)
+    assert tier == "compressed_cold"
     # the host tier evicts only published epochs; with no room for unpublished ones it refuses
     small = EpochRawTiers(host_raw_budget_bytes=1, host_slots=1, pin_memory=False)
     small.capture("a", built)
