@@ -468,11 +468,13 @@ class LineageRuntime:
 
     def acquire_node_history(self, node_ref: str, key: MatrixKey, *, ranges: Sequence[tuple[int, int]] | None = None,
                              stream: str | None = None, device: Any = "cpu",
-                             dtype: torch.dtype = torch.float32) -> torch.Tensor:
-        """Dense pre-RoPE history ``[T, C]`` of one matrix (FP32 ``dequantize(P) @ Q``; RAW bitwise)."""
+                             dtype: torch.dtype = torch.float32, packs: dict | None = None) -> torch.Tensor:
+        """Dense pre-RoPE history ``[T, C]`` of one matrix (FP32 ``dequantize(P) @ Q``; RAW bitwise). ``packs``
+        carries the parsed packets from one call to the next, so restoring every matrix of a node parses each
+        packet once instead of once per matrix."""
         pieces = self.resolve_history(node_ref, ranges)
         parts = []
-        packs: dict[str, Any] = {}
+        packs = {} if packs is None else packs
         for piece in pieces:
             record_ref = piece.record(key, stream)
             record = self.load_record(record_ref)

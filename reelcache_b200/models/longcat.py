@@ -388,9 +388,10 @@ class ReelCacheConditioningCacheBackend:
             self.stats["missed"] += 1
             return None
         ks, vs = [], []
+        packs: dict = {}
         for layer in range(self.runtime.model.layers):
-            k = self.runtime.acquire_node_history(node, MatrixKey(layer, "K"), device=self.device, dtype=torch.bfloat16)
-            v = self.runtime.acquire_node_history(node, MatrixKey(layer, "V"), device=self.device, dtype=torch.bfloat16)
+            k, v = (self.runtime.acquire_node_history(node, MatrixKey(layer, t), device=self.device,
+                                                      dtype=torch.bfloat16, packs=packs) for t in ("K", "V"))
             if self.cp_shard is not None:
                 index = RowShard(self.cp_shard.rank, self.cp_shard.cp, epoch.frames, *self.grid).token_index()
                 k, v = k.index_select(0, index.to(k.device)), v.index_select(0, index.to(v.device))

@@ -67,8 +67,11 @@ class EpochEntry:
 
 def _copy_cache(cache: LongCatConditioningCache, device, *, pin: bool = False) -> LongCatConditioningCache:
     def move(t):
-        out = t.detach().to(device, copy=True)
-        return out.pin_memory() if pin and out.device.type == "cpu" and torch.cuda.is_available() else out
+        if pin and torch.device(device).type == "cpu" and torch.cuda.is_available():
+            # one copy straight into page-locked memory (not a pageable copy followed by a pinned one)
+            out = torch.empty(t.shape, dtype=t.dtype, device="cpu", pin_memory=True)
+            return out.copy_(t.detach())
+        return t.detach().to(device, copy=True)
     return LongCatConditioningCache(cache.epoch, [move(k) for k in cache.k], [move(v) for v in cache.v])
 
 
