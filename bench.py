@@ -38,7 +38,7 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "KV restore GB/s (rewind-to-chunk-4 resume; p50 TTFC and archived chunks/s reported alongside)"
-BASELINE_PUBLISHED = None  # the reference publishes no absolute restore GB/s
+BASELINE_PUBLISHED = None  # the reference publishes no absolute restore GB/s figure
 
 
 def parse():
@@ -277,6 +277,21 @@ def run_ours(args, rank, world, local):
     clock_summary = clocks.summary()
     _ext.check_status(device)
     launches_per_step = program.batch_launch_count(aux=True)
+    # the single-FP16-product mode of the same restore (reported beside the fp16x2 headline, paired with the
+    # reference arm's precision="fp16")
+    program16 = LineageRestorer(runtime, device, precision="fp16").build_program(target, destination, rope,
+                                                                                 stream=stream)
+    with torch.cuda.stream(stream):
+        program16.prepare()
+    batches16 = program16.batches()
+
+    def device_step16():
+        with torch.cuda.stream(stream):
+            for batch in batches16:
+                program16.launch_batch(batch, stream, aux=True)
+
+    ms_device16 = reduce_max(timed(device_step16, args.steps, args.warmup, stream), world)
+    del program16
 
     # ---- end to end: public API restore from pinned host packs, then a D2H checksum of the cache ----
     h2d = sum(restorer.prepared_pack(item.packet_ref).nbytes for item in restorer.history(target))
@@ -339,6 +354,9 @@ def run_ours(args, rank, world, local):
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "includes": "LineageRestorer.restore from pinned host coefficient packs (H2D inside) + D2H of a "
                             "checksum of the restored cache"},
+        "precision": "fp16x2",
+        "fp16_pair": {"value": round(world * restored_bytes / (ms_device16 * 1e-3) / 1e9, 2), "unit": "GB/s",
+                      "ms_per_step": round(ms_device16, 4), "precision": "fp16"},
         "ttfc_p50_ms": round(ttfc_p50, 2), "first_step_without_restore_ms": round(first_step_ms, 2),
         "archived_chunks_per_s": round(archived_per_s, 4),
         "mean_rank": round(float(np.mean(state["ranks"])), 1), "gpu_launches": launches_per_step,
@@ -421,8 +439,8 @@ def run_reference(args, rank, world, local):
     stream = torch.cuda.Stream(device)
     main_stream = torch.cuda.current_stream(device)
 
-    def step():
-        return [rrk.reconstruct(jobs, stream=stream) for jobs in jobs_by_layer]
+    def step(precision="fp16x2"):
+        return [rrk.reconstruct(jobs, stream=stream, precision=precision) for jobs in jobs_by_layer]
 
     def e2e_step():
         with torch.cuda.stream(stream):
@@ -452,6 +470,7 @@ def run_reference(args, rank, world, local):
     with ClockSampler(local) as clocks:
         ms = timed(step, args.steps, args.warmup, stream)
     ms_e2e = timed(e2e_step, max(1, args.steps // 2), max(3, args.warmup), main_stream)
+    ms16 = reduce_max(timed(lambda: step("fp16"), args.steps, args.warmup, stream), world)
     ms = reduce_max(ms, world)
     ms_e2e = reduce_max(ms_e2e, world)
     restored = 2 * layers * chunks * tokens * heads * dim * 2
@@ -462,7 +481,11 @@ def run_reference(args, rank, world, local):
                     "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 64,
                     "includes": "H2D of the coefficient pictures from pinned memory + reconstruct + D2H checksum"},
             "impl": "reference", "clocks": clocks.summary(), "mean_rank": round(float(np.mean(ranks)), 1),
-            "note": "reference Triton restore_kernels.reconstruct (auto backend/precision) on picture sources; ranks "
+            "precision": "fp16x2",
+            "fp16_pair": {"value": round(world * restored / (ms16 * 1e-3) / 1e9, 2), "unit": "GB/s",
+                          "ms_per_step": round(ms16, 4), "precision": "fp16"},
+            "note": "reference Triton restore_kernels.reconstruct (auto backend, precision fp16x2 = its default) on "
+                    "picture sources; ranks "
                     + ("from bench_rank_profile.json" if profile is not None else "64 (no rank profile)")}
 
 

@@ -27,7 +27,7 @@ from .errors import CapacityError, ConfigurationError, IntegrityError, Unsupport
 from .lineage import LineageRuntime
 from .ops.restore import RestoreProgram
 from .overlapped_restore import LayerReadiness, OverlappedRestore, start_overlapped_restore
-from .restore_kernels import RopePositions, RopeTable, restore_rope_item
+from .restore_kernels import DEFAULT_PRECISION, RopePositions, RopeTable, restore_rope_item
 from .types import MatrixKey, entry_parts
 
 
@@ -154,7 +154,7 @@ class LineageRestorer:
                 self._prepared.move_to_end(packet_ref)
                 return hit
         _, pack = self.runtime.node_pack(packet_ref)
-        raw = torch.from_numpy(np.ascontiguousarray(pack.raw))
+        raw = torch.from_numpy(np.array(pack.raw, dtype=np.uint8, copy=True))
         if self.pin_memory:
             raw = raw.pin_memory()
         scales, offsets = [], []
@@ -237,7 +237,7 @@ class LineageRestorer:
                 rows = cache[0]
                 if program is None:
                     if precision == "auto":
-                        precision = "fp16" if rows.dtype == torch.bfloat16 else "fp16x2"
+                        precision = DEFAULT_PRECISION
                     program = RestoreProgram(self.device, stream, precision=precision)
                     program.keepalive.extend(device_raw.values())
                 key = MatrixKey(layer, target)

@@ -236,7 +236,7 @@ class LongCatDiT:
         self._ulysses_memo = (key, layers)
         return layers
 
-    def forward(self, latents: torch.Tensor, t: float, text: torch.Tensor, *, first_frame: int = 0,
+    def forward(self, latents: torch.Tensor, t: float, text: torch.Tensor | None, *, first_frame: int = 0,
                 cache: LongCatConditioningCache | None = None, cp_group=None, return_kv: bool = False,
                 ulysses=None):
         """Flow prediction ``[C, F, H, W]`` (FP32) of ``latents`` (frames ``first_frame..``) attending to the
@@ -316,25 +316,32 @@ class LongCatDiT:
         return (pred, kvs) if return_kv else pred
 
     def _cross_and_ffn(self, x: torch.Tensor, blk: dict, mod: torch.Tensor, text: torch.Tensor, n: int) -> None:
-        """Cross-attention over the text and the SwiGLU FFN on this rank's rows, in place on ``x``."""
+        """Cross-attention over the text (skipped when ``text`` is None) and the SwiGLU FFN on this rank's
+        rows, in place on ``x``."""
         cfg = self.cfg
         h, hd = cfg.heads, cfg.head_dim
-        y = F.layer_norm(x, (cfg.dim,), eps=cfg.eps).to(self.dtype)
-        cq = self.ops.rms_norm_heads(self.ops.linear(y, blk["cq_w"], blk["cq_b"]).reshape(n, h, hd),
-                                     blk["cq_norm"], cfg.eps)
-        ckv = self.ops.linear(text, blk["ckv_w"], blk["ckv_b"]).reshape(-1, 2, h, hd)
-        ck = self.ops.rms_norm_heads(ckv[:, 0], blk["ck_norm"], cfg.eps)
-        co = self.ops.attention(cq, ck, ckv[:, 1])
-        x.add_(self.ops.linear(co.reshape(n, cfg.dim), blk["cproj_w"], blk["cproj_b"]).float())
+        if text is not None:
+            y = F.layer_norm(x, (cfg.dim,), eps=cfg.eps).to(self.dtype)
+            cq = self.ops.rms_norm_heads(self.ops.linear(y, blk["cq_w"], blk["cq_b"]).reshape(n, h, hd),
+                                         blk["cq_norm"], cfg.eps)
+            ckv = self.ops.linear(text, blk["ckv_w"], blk["ckv_b"]).reshape(-1, 2, h, hd)
+            ck = self.ops.rms_norm_heads(ckv[:, 0], blk["ck_norm"], cfg.eps)
+            co = self.ops.attention(cq, ck, ckv[:, 1])
+            x.add_(self.ops.linear(co.reshape(n, cfg.dim), blk["cproj_w"], blk["cproj_b"]).float())
         y = (F.layer_norm(x, (cfg.dim,), eps=cfg.eps) * (1 + mod[4]) + mod[3]).to(self.dtype)
         hidden = (F.silu(self.ops.linear(y, blk["w1"]).float()) * self.ops.linear(y, blk["w3"]).float()).to(self.dtype)
         x.add_(mod[5] * self.ops.linear(hidden, blk["w2"]).float())
 
-    def build_conditioning_cache(self, cond_latents: torch.Tensor, text: torch.Tensor, epoch: ConditioningCacheEpoch,
+    def build_conditioning_cache(self, cond_latents: torch.Tensor, epoch: ConditioningCacheEpoch,
                                  *, cp_group=None) -> LongCatConditioningCache:
-        """One forward over the conditioning latents at ``t = 0`` returning their per-layer pre-RoPE K/V."""
-        _, kvs = self.forward(cond_latents, 0.0, text, first_frame=epoch.first_frame, cp_group=cp_group,
-                              return_kv=True)
+        """One forward over the conditioning latents at ``t = 0`` returning their per-layer pre-RoPE K/V.
+
+        The forward skips cross-attention (no text) and places the frames at segment-local positions
+        (first frame 0), as reference reelcache_sglang_models/longcat_video/dit_core.py:452 does: the cache
+        then depends only on the weights and the latents, which is what makes the content key of a segment
+        (model fingerprint, latents digest, grid) identify it across sessions, prompts and video offsets.
+        The epoch's ``first_frame`` is applied at read time, when RoPE rotates the cached K."""
+        _, kvs = self.forward(cond_latents, 0.0, None, first_frame=0, cp_group=cp_group, return_kv=True)
         return LongCatConditioningCache(epoch, [k for k, _ in kvs], [v for _, v in kvs])
 
     def flops_per_forward(self, tokens: int, cache_tokens: int) -> float:

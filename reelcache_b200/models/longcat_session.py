@@ -289,7 +289,7 @@ class LongCatSessionProvider:
             tier = "compressed_cold" if cache is not None else "built"
             if cache is None:
                 with self.gate.section():
-                    cache = self.model.build_conditioning_cache(cond_latents, text, epoch)
+                    cache = self.model.build_conditioning_cache(cond_latents, epoch)
                 self.tiers.capture(key, cache)
                 node_ref = self.backend.on_cache_built(cache)
                 self.tiers.published(key, node_ref)

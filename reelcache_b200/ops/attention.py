@@ -6,8 +6,7 @@ producer, single-thread MMA issuer, two softmax warpgroups splitting the KV bloc
 rescaling); ``"sdpa"`` is PyTorch's scaled_dot_product_attention (cuDNN's fused kernel on B200). ``"auto"``
 selects ``sdpa`` on CUDA: measured on B200 the fused kernel reaches about half of cuDNN's throughput (its
 per-block shared-memory traffic -- P written to and re-read from shared memory, K/V tiles read once per
-128 queries -- and the exp pipe bound it; see profiles/attention_kernel_b200.md), so it is selected only
-explicitly.
+128 queries -- and the exp pipe bound it), so it is selected only explicitly.
 """
 
 from __future__ import annotations

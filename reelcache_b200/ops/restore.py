@@ -122,7 +122,7 @@ class RestoreProgram:
     (``pictures``: (addresses, plane_stride, row_stride, layout) | ``values``: device tensor).
     """
 
-    def __init__(self, device, stream, *, precision: str = "fp16"):
+    def __init__(self, device, stream, *, precision: str = "fp16x2"):
         self.device = torch.device(device)
         if self.device.type == "cuda" and self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())

@@ -80,6 +80,11 @@ class GramReduceScatter:
         slots = self.slots_for(owners)
         if max(slots) >= self.max_slots:
             raise ConfigurationError("more matrices per owner than the buffer has slots")
+        # Entry barrier: an owner sums the previous call's partials on its stream after that call's exit
+        # barrier, so no rank may store this call's tiles into a peer's slots until every owner has passed
+        # that sum (the sum precedes this barrier on the owner's stream).
+        self.epoch += 1
+        ext().peer_barrier(self.flag_table, self.rank, self.epoch, self.status)
         ext().gram_reduce_scatter(xt.contiguous(), matrices, self.partials,
                                   torch.tensor(owners, dtype=torch.int64), torch.tensor(slots, dtype=torch.int64),
                                   self.rank, self.status)

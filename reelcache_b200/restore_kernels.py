@@ -1152,10 +1152,9 @@ def reconstruct(jobs, *, backend="auto", precision="auto", stream=None, wait_eve
     cuda = device.type == "cuda"
     backend = _resolve_backend(backend, cuda)
     if precision == "auto":
-        # One FP16 product (relative error 2^-11) is below the 2^-8 rounding of a bfloat16 cache; wider
-        # destinations take the two-product split.
-        precision = "fp16" if all(job.destination.tensor.dtype == torch.bfloat16 for job in jobs) \
-            else DEFAULT_PRECISION
+        # Every destination dtype takes the two-product split: its error bound does not depend on the
+        # cancellation in sum_k a_k q_k, which a single FP16 product's bound does.
+        precision = DEFAULT_PRECISION
     if backend == "fused" and precision not in KERNEL_PRECISIONS:
         raise UnsupportedError(f"the fused sm_100a kernel runs {KERNEL_PRECISIONS}; use backend='reference' "
                                f"for {precision}")

@@ -37,8 +37,8 @@ def _cp_worker(rank, world, port, errors):
         latents, text = _inputs(model)
         cond, _ = _inputs(model, frames=1, seed=5)
         epoch = ConditioningCacheEpoch("e0", 0, 0, 1)
-        full_cache = model.build_conditioning_cache(cond, text, epoch)
-        local_cache = model.build_conditioning_cache(cond, text, epoch, cp_group=dist.group.WORLD)
+        full_cache = model.build_conditioning_cache(cond, epoch)
+        local_cache = model.build_conditioning_cache(cond, epoch, cp_group=dist.group.WORLD)
         ref = model.forward(latents, 0.5, text, first_frame=1, cache=full_cache)
         got = model.forward(latents, 0.5, text, first_frame=1, cache=local_cache, cp_group=dist.group.WORLD)
         assert torch.allclose(got, ref, atol=2e-2, rtol=2e-2), (got - ref).abs().max()
@@ -84,7 +84,7 @@ def test_conditioning_cache_seam(tmp_path):
     cond, _ = _inputs(model, frames=2, seed=9)
     epoch = ConditioningCacheEpoch("seg-0", 0, 0, 2)
     assert backend.restore(epoch) is None
-    built = model.build_conditioning_cache(cond, text, epoch)
+    built = model.build_conditioning_cache(cond, epoch)
     backend.on_cache_built(built)
     restored = backend.restore(epoch)
     assert restored is not None and restored.tokens == built.tokens
@@ -168,3 +168,20 @@ def test_epoch_tiers_planning_gate_and_session_provider(tmp_path):
     b = gated_plan_chunk(gate, matrices, contexts, lm(), None, {}, {})
     assert all(torch.equal(a[k].rows, b[k].rows) for k in a)
     store.close()
+
+
+def test_conditioning_cache_depends_only_on_latents():
+    """Sessions share an archived segment through its content key (model, latents digest, grid), so the cache
+    must not depend on the prompt or on where the segment sits in the video: two builds from the same latents
+    with different epochs (first frames) are identical, and the content key ignores the text."""
+    from reelcache_b200.models.longcat import ConditioningCacheEpoch
+    from reelcache_b200.models.longcat_session import content_key
+    model = _model()
+    cond, _ = _inputs(model, frames=2, seed=9)
+    a = model.build_conditioning_cache(cond, ConditioningCacheEpoch("a", 0, 0, 2))
+    b = model.build_conditioning_cache(cond, ConditioningCacheEpoch("b", 3, 6, 2))
+    for x, y in zip(a.k + a.v, b.k + b.v):
+        assert torch.equal(x, y)
+    other, _ = _inputs(model, frames=2, seed=10)
+    assert content_key("m", cond, model.cfg.grid) == content_key("m", cond.clone(), model.cfg.grid)
+    assert content_key("m", cond, model.cfg.grid) != content_key("m", other, model.cfg.grid)

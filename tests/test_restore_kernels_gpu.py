@@ -40,10 +40,10 @@ def test_fused_group_of_jobs_k_and_v(cuda_device):
         job, _ = picture_job(cuda_device, rank=64 + 32 * chunk, heads=12, destination=cache, token_offset=4680 * chunk,
                              table=table, rope_rows=(3 * chunk, 0, 0), seed=chunk)
         jobs.append(job)
-    rk.reconstruct(jobs, backend="fused").synchronize()  # auto precision: fp16 for bfloat16 caches
+    rk.reconstruct(jobs, backend="fused").synchronize()  # auto precision: the two-product fp16x2 split
     _ext.check_status(cuda_device)
     for job in jobs:
-        _check(job, "fp16")
+        _check(job, "fp16x2")
 
 
 @pytest.mark.parametrize("layout", ["THD", "BHTD"])

@@ -38,7 +38,7 @@ def _worker(rank, world, port, result_path):
         cond = torch.randn((cfg.in_channels, 2, cfg.latent_height, cfg.latent_width), generator=gen, device=device)
         text = model.encode_text(torch.randn((cfg.text_len, cfg.text_dim), generator=gen, device=device))
         epoch = ConditioningCacheEpoch("e0", 0, 0, 2)
-        cache = model.build_conditioning_cache(cond, text, epoch, cp_group=dist.group.WORLD)
+        cache = model.build_conditioning_cache(cond, epoch, cp_group=dist.group.WORLD)
         tokens = 2 * cfg.tokens_per_frame
         errors = []
         for use_cache in (False, True):
@@ -55,20 +55,24 @@ def _worker(rank, world, port, result_path):
         from reelcache_b200.parallel.gram_rs import GramReduceScatter
         channels, matrices = 256, 3
         owners = [b % world for b in range(matrices)]
-        gen_r = torch.Generator(device=device).manual_seed(10 + rank)
-        shards = [torch.randn(96, channels, device=device, generator=gen_r).bfloat16() for _ in range(matrices)]
         grs = GramReduceScatter(None, device, channels=channels, max_slots=matrices)
-        grams = grs.run(torch.cat([x.t() for x in shards]).contiguous(), owners)
+        gram_err = 0.0
+        # several calls back to back with different inputs: a call must not overwrite partials an owner is
+        # still summing from the previous call
+        for call in range(4):
+            gen_r = torch.Generator(device=device).manual_seed(10 + 97 * call + rank)
+            shards = [torch.randn(96 + 32 * call, channels, device=device, generator=gen_r).bfloat16()
+                      for _ in range(matrices)]
+            grams = grs.run(torch.cat([x.t() for x in shards]).contiguous(), owners)
+            gathered = [[torch.empty_like(x) for _ in range(world)] for x in shards]
+            for b in range(matrices):
+                dist.all_gather(gathered[b], shards[b])
+            for b, gram in grams.items():
+                full = torch.cat(gathered[b]).double()
+                ref = full.t() @ full
+                gram_err = max(gram_err, float((gram.double() - ref).norm() / ref.norm()))
         torch.cuda.synchronize()
         grs.check()
-        gathered = [[torch.empty_like(x) for _ in range(world)] for x in shards]
-        for b in range(matrices):
-            dist.all_gather(gathered[b], shards[b])
-        gram_err = 0.0
-        for b, gram in grams.items():
-            full = torch.cat(gathered[b]).double()
-            ref = full.t() @ full
-            gram_err = max(gram_err, float((gram.double() - ref).norm() / ref.norm()))
         errors.append(gram_err)
         grs.close()
         if rank == 0:

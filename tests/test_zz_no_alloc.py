@@ -1,6 +1,9 @@
-"""The allocation-free C entry point ``rc_restore_u8_noalloc`` (csrc/restore/noalloc.h) against the
-existing fused restore entry point (``restore_kernels.reconstruct``): same kernels, same parameters,
-so the restored slots are bitwise identical, on two calls in a row that reuse the fixed scratch.
+"""The allocation-free C entry point ``rc_restore_u8_noalloc`` (csrc/restore/noalloc.h), for callers that
+cannot allocate device memory (an engine that owns all of it, code running while the allocator is locked or
+trimming), against the existing fused restore entry point (``restore_kernels.reconstruct``): same kernels,
+same parameters, so the restored slots are bitwise identical, on two calls in a row that reuse the fixed
+scratch; both are also checked against the kernel's documented elementwise error bound, for one and two
+FP16 products and for bfloat16 and FP32 destinations, and the calls leave torch's allocator untouched.
 Collected last so it also runs after every other GPU test in one process."""
 
 import ctypes
@@ -50,12 +53,16 @@ def _job(device, seed, rank, rope):
     return grid, tokens, heads, head_dim, pixels, scale, offset, basis, table, rows
 
 
-def _restore_both(fn, device, seed, rank, rope):
+_DTYPE_CODES = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+
+
+def _restore_both(fn, device, seed, rank, rope, passes=1, out_dtype=torch.bfloat16):
     grid, tokens, heads, head_dim, pixels, scale, offset, basis, table, rows = _job(device, seed, rank, rope)
-    expected = torch.zeros((1, tokens, heads, head_dim), dtype=torch.bfloat16, device=device)
+    expected = torch.zeros((1, tokens, heads, head_dim), dtype=out_dtype, device=device)
+    precision = "fp16x2" if passes == 2 else "fp16"
     job = rk.ReconstructionJob(rk.CoefficientSource(pixels, scale, offset), rk.NativeView(expected), grid, basis,
                                rope=rk.RopePositions(table, rows) if rope else None)
-    rk.reconstruct([job], backend="fused", precision="fp16").synchronize()
+    rk.reconstruct([job], backend="fused", precision=precision).synchronize()
 
     got = torch.full_like(expected, float("nan"))
     scale_d = torch.from_numpy(scale).to(device)
@@ -69,21 +76,28 @@ def _restore_both(fn, device, seed, rank, rope):
     view = rk.NativeView(got)
     c.destination = view.address()
     c.dst_token_stride, c.dst_head_stride, c.dst_dim_stride = view.strides()
-    c.out_dtype, c.channels, c.head_dim = 0, heads * head_dim, head_dim
+    c.out_dtype, c.channels, c.head_dim = _DTYPE_CODES[out_dtype], heads * head_dim, head_dim
     keep = []
     if rope:
         pack, (sec_t, sec_h, entries) = table.packed_tables(rows, grid, device)
         keep.append(pack)
         c.rope_pack, c.sec_t, c.sec_h, c.rope_entries = pack.data_ptr(), sec_t, sec_h, entries
     c.grid_t, c.grid_h, c.grid_w = grid
-    c.passes = 1
+    c.passes = passes
     c.status = status.data_ptr()
     error = ctypes.create_string_buffer(256)
     stream = torch.cuda.current_stream(device)
+    torch.cuda.synchronize(device)
+    allocated = torch.cuda.memory_allocated(device)
     code = fn(ctypes.byref(c), device.index, ctypes.c_void_p(stream.cuda_stream), error, len(error))
     assert code == 0, error.value.decode()
+    assert torch.cuda.memory_allocated(device) == allocated  # nothing drawn from torch's allocator
     torch.cuda.synchronize(device)
     assert int(status.item()) == 0
+    # the documented bound of the fused kernel, checked on what the allocation-free call wrote
+    values, bound = rk.kernel_error_bound(job, precision)
+    written = got.reshape(tokens, -1).double()
+    assert float(((written - values).abs() - bound).max()) <= 0
     return expected, got
 
 
@@ -93,6 +107,14 @@ def test_noalloc_matches_fused_entry_point_twice(cuda_device):
     assert fn(None, cuda_device.index, None, None, 0) == 0
     for seed, rank, rope in ((1, 64, True), (2, 200, False)):
         expected, got = _restore_both(fn, cuda_device, seed, rank, rope)
+        assert torch.equal(got, expected)
+
+
+@pytest.mark.parametrize("passes,out_dtype", [(2, torch.bfloat16), (2, torch.float32), (1, torch.float32)])
+def test_noalloc_precisions_and_destinations(cuda_device, passes, out_dtype):
+    fn = _entry()
+    for seed, rank, rope in ((3, 96, True), (4, 257, True)):
+        expected, got = _restore_both(fn, cuda_device, seed, rank, rope, passes=passes, out_dtype=out_dtype)
         assert torch.equal(got, expected)
 
 
