@@ -50,9 +50,11 @@ def parse():
     ap.add_argument("--history", type=int, default=4, help="chunks restored per step (rewind target)")
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--layers", type=int, default=30)
-    ap.add_argument("--mode", default="dp", choices=("dp", "sp"),
-                    help="dp: every rank restores its own session (config 2); sp: Ulysses sequence-parallel restore "
-                         "of one long history, every rank its head slice, A operands read from peer memory (config 3)")
+    ap.add_argument("--mode", default="auto", choices=("auto", "dp", "sp"),
+                    help="dp: every rank restores its own session (config 2); sp: sequence-parallel restore of one "
+                         "24-chunk history over all ranks (config 3); auto: dp on one GPU, sp on several")
+    ap.add_argument("--sp-layout", default="sequence", choices=("sequence", "heads", "rows"),
+                    help="native layout of the sp mode: contiguous chunk ranges, head slices or row slices")
     ap.add_argument("--sp-chunks", type=int, default=24, help="history chunks of the sp mode (24 = 112k tokens)")
     ap.add_argument("--write-rank-profile", action="store_true",
                     help="write the archive's per-matrix ranks to bench_rank_profile.json")
@@ -489,125 +491,224 @@ def run_reference(args, rank, world, local):
                     + ("from bench_rank_profile.json" if profile is not None else "64 (no rank profile)")}
 
 
-def run_sp(args, rank, world, local):
-    """Ulysses SP restore of a ``--sp-chunks`` history: tiles round-robin over ranks, every rank restores
-    its head columns of every tile with the fused peer-memory restore (strong scaling)."""
+def sp_shapes(args, profile):
+    """``(chunk, layer, target, tokens, rank)`` of every matrix of the config-3 history (ranks from the rank
+    profile, its 4 profiled chunks repeated)."""
+    tokens = 4680
+    return [(c, layer, which, tokens, profile[which][c % 4][layer] if profile is not None else 64)
+            for c in range(args.sp_chunks) for layer in range(args.layers) for which in ("K", "V")]
+
+
+def sp_factor(tile, device, generator):
+    """Synthetic factors of one tile: 8-bit coefficients, an FP16 basis and its per-column affine."""
     import torch
-    import torch.distributed as dist
+    coeff = torch.randint(0, 256, (tile.tokens, tile.rank), generator=generator, device=device, dtype=torch.uint8)
+    basis = (torch.randn(tile.rank, tile.channels, generator=generator, device=device) / 40).half()
+    scale = np.full(tile.rank, 0.02, dtype=np.float32)
+    offset = np.full(tile.rank, -2.5, dtype=np.float32)
+    return coeff, basis, scale, offset
+
+
+def run_sp(args, rank, world, local):
+    """a 24-chunk (112k-token) CausVid history restored under sequence parallelism SP = N.
+    Every matrix's factors live on its factor owner; rank r restores the KV of its contiguous range of whole
+    chunks (its sequence shard), its unpack kernel loading the owners' coefficients and its basis preparation
+    loading their bases straight from peer memory, then the tcgen05 restore GEMM (strong scaling)."""
+    import torch
     from reelcache_b200 import restore_kernels as rk
-    from reelcache_b200.ops import _ext
-    from reelcache_b200.ops.peer_restore import PeerRestoreDomain, column_basis, plan_tiles
-    from reelcache_b200.ops.restore import RestoreProgram
-    from reelcache_b200.restore_kernels import restore_rope_item
+    from reelcache_b200.parallel.sp_restore import FusedHistoryRestore, HistoryLayout, plan_history
 
     device = torch.device("cuda", local)
-    layers, chunks, heads, head_dim = args.layers, args.sp_chunks, 12, 128
-    frames, h, w = 3, 30, 52
-    tokens, channels = frames * h * w, heads * head_dim
-    if heads < world:
-        return {"impl": "ours", "unavailable": f"{heads} heads cannot cover {world} ranks"}
-    first, last = rank * heads // world, (rank + 1) * heads // world  # uneven splits: 12 heads over 8 ranks
-    local_heads = last - first
-    cols = slice(first * head_dim, last * head_dim)
-    profile = load_rank_profile(layers, 4)
-    gen = torch.Generator(device=device).manual_seed(0)
-    table = rk.RopeTable.wan(head_dim, 4 * chunks, device=device)
-    shapes, meta = [], []
-    for layer in range(layers):
-        for c in range(chunks):
-            for which in ("K", "V"):
-                rank_k = profile[which][c % 4][layer] if profile is not None else 64
-                shapes.append((len(shapes) % world, tokens, rank_k))
-                meta.append((layer, c, which, rank_k))
-    tiles = plan_tiles(shapes)
-    capacity = max((t.offset + t.nbytes for t in tiles if t.owner == rank), default=256)
-    capacity = max(capacity, 256)
-    if world > 1:
-        cap = torch.tensor([capacity], dtype=torch.int64, device=device)
-        dist.all_reduce(cap, op=dist.ReduceOp.MAX)
-        capacity = int(cap.item())
-        domain = PeerRestoreDomain(None, device, capacity)
-    else:
-        domain = None
-        buffer = torch.empty(capacity, dtype=torch.uint8, device=device)
-    sources, keep = {}, []
-    cache_k = [torch.zeros((1, chunks * tokens, local_heads, head_dim), dtype=torch.bfloat16, device=device)
-               for _ in range(layers)]
-    cache_v = [torch.zeros_like(cache_k[0]) for _ in range(layers)]
+    heads, head_dim, grid = 12, 128, (3, 30, 52)
+    tokens, channels = 4680, heads * head_dim
+    profile = load_rank_profile(args.layers, 4)
+    plan = plan_history(sp_shapes(args, profile), world, channels)
+    layout = HistoryLayout(args.sp_layout, world, chunks=args.sp_chunks, tokens=tokens, heads=heads,
+                           head_dim=head_dim)
+    fused = FusedHistoryRestore.create(plan, layout, grid, device)
+    gen = torch.Generator(device=device).manual_seed(100 + rank)
+    fused.stage({tile.index: sp_factor(tile, device, gen) for tile in plan.owned(rank)})
+    cache = {(layer, which): torch.zeros((1, layout.local_tokens(rank), layout.local_heads(rank), head_dim),
+                                         dtype=torch.bfloat16, device=device)
+             for layer in range(args.layers) for which in ("K", "V")}
+    table = rk.RopeTable.wan(head_dim, 3 * args.sp_chunks + 3, device=device)
+    fused.build(lambda layer, which: cache[(layer, which)],
+                lambda tile: rk.RopePositions(table, (3 * tile.chunk, 0, 0)))
     stream = torch.cuda.current_stream(device)
-    program = RestoreProgram(device, stream, precision="fp16")
-    unpack_rows = []
-    for i, (tile, (layer, c, which, rank_k)) in enumerate(zip(tiles, meta)):
-        if tile.owner == rank:
-            src = torch.randint(0, 256, (tokens, rank_k), generator=gen, device=device, dtype=torch.uint8)
-            sources[i] = src
-            out = (domain.buffer if domain is not None else buffer)[tile.offset:tile.offset + tile.nbytes]
-            unpack_rows.append([0, 0, 0, src.data_ptr(), out.data_ptr(), src.stride(0), tokens, tile.k_pad, rank_k,
-                                1, 1, tokens])
-        basis = (torch.randn(rank_k, channels, generator=gen, device=device) / 40).half()
-        b = column_basis(basis, rank_k, cols)
-        keep.append(b)
-        scale = np.full(rank_k, 0.02, dtype=np.float32)
-        offset = np.full(rank_k, -2.5, dtype=np.float32)
-        dest = (cache_k if which == "K" else cache_v)[layer][0, c * tokens:(c + 1) * tokens]
-        rope = restore_rope_item(rk.RopePositions(table, (3 * c, 0, 0)), (frames, h, w), device, None, keep) \
-            if which == "K" else None
-        a = domain.a_view(tile) if domain is not None else \
-            buffer[tile.offset:tile.offset + tile.nbytes].view(torch.float16).view(tokens, tile.k_pad)
-        program.add({"kind": "a16", "a": a, "tokens": tokens, "rank": rank_k, "grid": (frames, h, w), "basis": b,
-                     "qmax": float(b.abs().amax().item()), "scale": scale, "offset": offset, "rope": rope,
-                     "dest": (dest.data_ptr(), (dest.stride(0), dest.stride(1), dest.stride(2)), dest.dtype,
-                              local_heads * head_dim, head_dim)}, group=layer)
-    unpack_tables = [torch.tensor(unpack_rows[i:i + 48], dtype=torch.int64) for i in range(0, len(unpack_rows), 48)]
-    program.prepare(run_aux=False)
-    torch.cuda.synchronize()
 
-    def step():
-        for table_rows in unpack_tables:  # owners stage their tiles (unpack into the symmetric buffer)
-            _ext.ext().unpack_launch(table_rows, local)
-        if world > 1:
-            torch.cuda.synchronize()
-            dist.barrier()
-        program.run_aux(stream)
-        program.launch_all(stream)
-        if world > 1:
-            torch.cuda.synchronize()
-            dist.barrier()
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    def timed(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
-        for _ in range(args.steps):
-            step()
+        for _ in range(steps):
+            fn()
         stop.record(stream)
         torch.cuda.synchronize()
-    barrier(world)
-    ms = reduce_max(start.elapsed_time(stop) / args.steps, world)
-    _ext.check_status(device)
-    restored = 2 * layers * chunks * tokens * channels * 2
-    remote = sum(t.nbytes for t in tiles if t.owner != rank)
-    launches = len(unpack_tables) + len(program.aux[0]) + len(program.aux[1]) + \
-        sum(len(b) for b in program.blobs.values())
+        barrier(world)
+        return start.elapsed_time(stop) / steps
+
+    with ClockSampler(local) as clocks:
+        ms = timed(lambda: fused.restore(stream), args.steps, args.warmup)
+    fused.check()
+    launches = fused.launch_count()
+    restored = 2 * args.layers * args.sp_chunks * tokens * channels * 2
+    probe_layers = (0, args.layers - 1)
+
+    def e2e_step():  # public restore from pinned host coefficients, then a D2H checksum of this rank's KV
+        fused.restore(stream, from_host=True)
+        probe = torch.stack([cache[(layer, which)][0, -1, 0, :4].float() for layer in probe_layers
+                             for which in ("K", "V")])
+        return probe.to("cpu")
+
+    mirror = fused.host_mirror()
+    ms_e2e = timed(e2e_step, max(1, args.steps // 2), max(3, args.warmup))
+    fused.check()
+    ms, ms_e2e = reduce_max(ms, world), reduce_max(ms_e2e, world)
+    stats = {key: fused.stats.get("plan_" + key, 0) for key in ("remote_coeff_bytes", "local_coeff_bytes",
+                                                                "remote_basis_bytes")}
+    fused.close()
     return {"metric": METRIC, "value": round(restored / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "ms_per_step": round(ms, 4), "gpu_launches": launches, "clocks": clocks.summary(),
-            "restored_bytes_per_step": restored, "remote_a_bytes_per_rank": remote,
-            "note": f"Ulysses SP{world}: {chunks}-chunk history; every rank restores its heads ({heads} heads split "
-                    f"{heads // world}-{-(-heads // world)} per rank) of every tile, A operands read by the fused "
-                    "restore straight from the owners' symmetric buffers",
+            "ms_per_step": round(ms, 4),
+            "e2e": {"value": round(restored / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": int(mirror.numel()),
+                    "d2h_bytes_per_step": 4 * len(probe_layers) * 2 * 4,
+                    "includes": "FusedHistoryRestore.restore(from_host=True) on every rank: H2D of the owner's "
+                                "coefficients from pinned memory, one device barrier, the fused restore; D2H "
+                                "checksum; bytes of rank 0"},
+            "gpu_launches": launches, "clocks": clocks.summary(), "restored_bytes_per_step": restored,
+            "precision": "fp16x2", "per_rank_plan_bytes": stats,
+            "note": f"SP{world}, layout '{args.sp_layout}': {args.sp_chunks}-chunk history; each rank restores "
+                    "its native part, the coefficient and basis all-gather fused into the restore pipeline's "
+                    "kernels (peer loads over NVLink); no host synchronization or barrier in the timed loop",
+            "scaling_kind": "strong"}
+
+
+def run_reference_sp(args, rank, world, local):
+    """Config 3 on the reference: its FactorShardDomain.reconstruct (reelcache/factor_sharding.py:1893, default
+    ``mode="factors"``: NCCL point-to-point rounds of coefficient rows and basis columns, FP32 GEMMs per token
+    tile, FP32 RoPE callback, cast) over the same 24-chunk history, whole-matrix owners with the same rotation,
+    native row shards (its only layout valid for 12 heads on 8 ranks), node by node."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "reelcache")):
+        return {"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}
+    sys.path.insert(0, ref_dir)
+    try:
+        import torch
+        import torch.distributed as dist
+        from reelcache import restore_kernels as rrk
+        from reelcache.distributed import DistributedOwner, KVLayout
+        from reelcache.factor_sharding import FactorShardDomain, FactorShardSpec, NativeOwners, OwnerShard
+        from reelcache.types import MatrixKey, ModelIdentity, TensorContext
+    except Exception as error:  # noqa: BLE001
+        return {"impl": "reference", "unavailable": f"reference import failed: {type(error).__name__}: {error}"}
+    device = torch.device("cuda", local)
+    heads, head_dim, tokens, channels = 12, 128, 4680, 1536
+    profile = load_rank_profile(args.layers, 4)
+    control = dist.new_group(backend="gloo") if world > 1 else None
+    coordinator = DistributedOwner(control, device="cpu")
+    domain = FactorShardDomain(coordinator, data_group=dist.group.WORLD if world > 1 else None, device=device)
+    # KVLayout insists that the head count divides the ranks even for row shards, whose ranks own every
+    # channel; 24 heads of 64 describe the same 1536 channels at 8 ranks (the rows own all of them).
+    kv_heads, kv_dim = (heads, head_dim) if heads % world == 0 else (24, 64)
+    native = NativeOwners(KVLayout(tokens=tokens, kv_heads=kv_heads, head_dim=kv_dim, world_size=world), "rows")
+    model = ModelIdentity("causvid-wan2.1-1.3b-synthetic", "random-init", args.layers, channels, "BTHD", "bfloat16")
+    table = rrk.RopeTable.from_complex(wan_freqs(head_dim, 3 * args.sp_chunks + 64).to(device))
+    gen = torch.Generator(device=device).manual_seed(100 + rank)
+    nodes = []
+    host_tiles = []
+    mine = native.shape(rank)[0]
+    for chunk in range(args.sp_chunks):
+        cos, sin = rrk.rope_cos_sin(rrk.RopePositions(table, (3 * chunk, 0, 0)), (3, 30, 52), dtype=torch.float32,
+                                    device=device)
+
+        def rope(entry, values, positions, columns, cos=cos, sin=sin):
+            c, s_ = cos[positions][:, None, :], sin[positions][:, None, :]
+            x = values.reshape(values.shape[0], heads, head_dim)
+            out = torch.empty_like(x)
+            out[..., 0::2] = x[..., 0::2] * c - x[..., 1::2] * s_
+            out[..., 1::2] = x[..., 0::2] * s_ + x[..., 1::2] * c
+            return out.reshape(values.shape[0], -1)
+
+        shards, outs = {}, {}
+        for layer in range(args.layers):
+            for which in ("K", "V"):
+                key = MatrixKey(layer, which)
+                r = profile[which][chunk % 4][layer] if profile is not None else 64
+                spec = FactorShardSpec.fresh(key, channels=channels, rank=r, world_size=world)
+                context = TensorContext(model, key, chunk * tokens, 3, 30, 52, "pre_rope" if which == "K" else "none")
+                coeff = basis = None
+                if spec.view_rows(rank):
+                    pixels = torch.randint(0, 256, (tokens, r), generator=gen, device=device, dtype=torch.uint8)
+                    host = pixels.cpu().pin_memory()
+                    coeff = torch.empty((tokens, r), dtype=torch.float32, device=device)
+                    host_tiles.append((host, pixels, coeff))
+                    coeff.copy_(pixels.float() * 0.02 - 2.5)
+                    basis = (torch.randn(r, channels, generator=gen, device=device) / 40).half()
+                shards[key] = OwnerShard(key, spec, context, rank, coeff, basis)
+                outs[key] = torch.empty((mine, channels), dtype=torch.bfloat16, device=device)
+        nodes.append((shards, outs, rope))
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        for shards, outs, rope in nodes:
+            domain.reconstruct(shards, native, dtype=torch.bfloat16, rope=rope, out=outs)
+
+    def e2e_step():  # H2D of the owned 8-bit coefficients, dequantization, reconstruct, D2H checksum
+        for host, pixels, coeff in host_tiles:
+            pixels.copy_(host, non_blocking=True)
+            coeff.copy_(pixels.float() * 0.02 - 2.5)
+        step()
+        last = nodes[-1][1]
+        probe = torch.stack([last[MatrixKey(layer, which)][-1, :4].float() for layer in (0, args.layers - 1)
+                             for which in ("K", "V")])
+        return probe.to("cpu")
+
+    def timed(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            fn()
+        stop.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return start.elapsed_time(stop) / steps
+
+    with ClockSampler(local) as clocks:
+        ms = timed(step, args.steps, args.warmup)
+    ms_e2e = timed(e2e_step, max(1, args.steps // 2), max(3, args.warmup))
+    ms, ms_e2e = reduce_max(ms, world), reduce_max(ms_e2e, world)
+    restored = 2 * args.layers * args.sp_chunks * tokens * channels * 2
+    h2d = sum(host.numel() for host, _, _ in host_tiles)
+    if control is not None:
+        dist.destroy_process_group(control)
+    return {"metric": METRIC, "value": round(restored / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(ms, 4), "impl": "reference", "clocks": clocks.summary(),
+            "e2e": {"value": round(restored / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms_e2e, 3),
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 64,
+                    "includes": "H2D of the owned 8-bit coefficients + dequantization + reconstruct + D2H checksum"},
+            "restored_bytes_per_step": restored,
+            "note": f"reference FactorShardDomain.reconstruct (mode factors, NCCL data group, Gloo control group), "
+                    f"SP{world}, native row shards of every node, {args.sp_chunks} nodes per step",
             "scaling_kind": "strong"}
 
 
 def main():
     args = parse()
     rank, world, local = dist_setup(args)
+    if args.mode == "auto":
+        args.mode = "dp" if world == 1 else "sp"
     if args.impl == "reference":
-        out = run_reference(args, rank, world, local) if args.mode == "dp" else \
-            {"impl": "reference", "unavailable": "the sp mode has no reference arm (its SP restore needs the "
-                                                 "reference's full SGLang engine)"}
+        out = run_reference(args, rank, world, local) if args.mode == "dp" else run_reference_sp(args, rank, world,
+                                                                                                   local)
     elif args.mode == "sp":
         out = run_sp(args, rank, world, local)
     else:

@@ -23,8 +23,10 @@ namespace prep {
 
 constexpr int kMaxJobs = 48;
 constexpr int kThreads = 256;
-constexpr int kChannels = 32;   // channels per block (one warp-width of coalesced basis reads)
-constexpr int kKLanes = kThreads / kChannels;  // 8
+constexpr int kVec = 8;                          // channels per thread (one 16-byte basis load)
+constexpr int kGroups = 32;                      // channel groups per block: one warp spans 256 channels
+constexpr int kChannels = kGroups * kVec;        // channels per block
+constexpr int kKLanes = kThreads / kGroups;      // 8: warp w handles K rows w*8 .. w*8+7 of every 64
 
 struct Job {
   const __half* q;       // [R, C] basis rows
@@ -35,60 +37,97 @@ struct Job {
   int64_t q_stride;      // elements between basis rows
   int rank, k_pad, channels;
   float prescale;
+  int vec;               // basis rows 16-byte aligned: one 16-byte load per thread and row
 };
 
 struct Params {
   Job jobs[kMaxJobs];
 };
 
+// One warp reads 512 contiguous bytes of a basis row (a basis in a peer's memory then crosses NVLink in
+// whole lines); each thread owns 8 channels and, per 64-row K block, 8 consecutive K rows, so it writes
+// one 16-byte hi and one 16-byte lo chunk of each of its 8 Bt rows. The bias of a channel accumulates in
+// FP64 in a fixed order: ascending K within a lane, then lanes 0..7.
 __global__ void __launch_bounds__(kThreads) prep_kernel(const __grid_constant__ Params p) {
   const Job& jb = p.jobs[blockIdx.y];
-  const int c0 = blockIdx.x * kChannels;
-  if (c0 >= jb.channels) return;
-  const int c = c0 + (threadIdx.x % kChannels);
-  const int lane_k = threadIdx.x / kChannels;
+  const int c0 = blockIdx.x * kChannels + (threadIdx.x % kGroups) * kVec;
+  if (blockIdx.x * kChannels >= jb.channels) return;
+  const int lane_k = threadIdx.x / kGroups;
   __shared__ double partial[kKLanes][kChannels];
-  double acc = 0.0;
-  const bool live_c = c < jb.channels;
+  double acc[kVec];
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) acc[j] = 0.0;
+  const bool live = c0 < jb.channels;
   for (int k0 = lane_k * 8; k0 < jb.k_pad; k0 += kKLanes * 8) {
-    uint32_t hi[4], lo[4];
+    float v[8][kVec];  // [k][channel]
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-      float v[2];
+    for (int i = 0; i < 8; ++i) {
+      const int k = k0 + i;
+      float q[kVec];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int k = k0 + i + h;
-        float val = 0.0f;
-        if (live_c && k < jb.rank) {
-          const float q = __half2float(jb.q[static_cast<int64_t>(k) * jb.q_stride + c]);
-          const float s = jb.scale[k];
-          val = (s * jb.prescale) * q;
-          acc += (static_cast<double>(jb.offset[k]) + 128.0 * static_cast<double>(s)) * static_cast<double>(q);
+      for (int j = 0; j < kVec; ++j) q[j] = 0.0f;
+      if (live && k < jb.rank) {
+        const __half* row = jb.q + static_cast<int64_t>(k) * jb.q_stride + c0;
+        if (jb.vec) {
+          const uint4 raw = __ldg(reinterpret_cast<const uint4*>(row));
+          const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+          for (int j = 0; j < kVec / 2; ++j) {
+            const float2 f = __half22float2(h2[j]);
+            q[2 * j] = f.x;
+            q[2 * j + 1] = f.y;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < kVec; ++j)
+            if (c0 + j < jb.channels) q[j] = __half2float(row[j]);
         }
-        v[h] = val;
+        const float s = jb.scale[k];
+        const double shift = static_cast<double>(jb.offset[k]) + 128.0 * static_cast<double>(s);
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+          v[i][j] = (s * jb.prescale) * q[j];
+          acc[j] += shift * static_cast<double>(q[j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) v[i][j] = 0.0f;
       }
-      const __half h0 = __float2half_rn(v[0]);
-      const __half h1 = __float2half_rn(v[1]);
-      const __half l0 = __float2half_rn(v[0] - __half2float(h0));
-      const __half l1 = __float2half_rn(v[1] - __half2float(h1));
-      hi[i / 2] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
-      lo[i / 2] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
     }
-    if (live_c) {
-      __half* row = jb.bt + static_cast<int64_t>(c) * 2 * jb.k_pad;
-      *reinterpret_cast<uint4*>(row + k0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      *reinterpret_cast<uint4*>(row + jb.k_pad + k0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    if (live) {
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        if (c0 + j >= jb.channels) break;
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          const __half h0 = __float2half_rn(v[i][j]);
+          const __half h1 = __float2half_rn(v[i + 1][j]);
+          const __half l0 = __float2half_rn(v[i][j] - __half2float(h0));
+          const __half l1 = __float2half_rn(v[i + 1][j] - __half2float(h1));
+          hi[i / 2] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
+          lo[i / 2] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+        }
+        __half* out = jb.bt + static_cast<int64_t>(c0 + j) * 2 * jb.k_pad;
+        *reinterpret_cast<uint4*>(out + k0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(out + jb.k_pad + k0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
     }
   }
-  partial[lane_k][threadIdx.x % kChannels] = acc;
+  const int local_c = (threadIdx.x % kGroups) * kVec;
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) partial[lane_k][local_c + j] = acc[j];
   __syncthreads();
-  if (threadIdx.x < kChannels && live_c) {
+  const int c = blockIdx.x * kChannels + threadIdx.x;  // kThreads == kChannels: one thread per channel
+  if (c < jb.channels) {
     double sum = 0.0;
 #pragma unroll
     for (int i = 0; i < kKLanes; ++i) sum += partial[i][threadIdx.x];
     jb.bias[c] = static_cast<float>(sum);
   }
 }
+
+static_assert(kThreads == kChannels, "the bias reduction assigns one thread per channel");
 
 }  // namespace prep
 
@@ -119,6 +158,7 @@ void prep_launch(const at::Tensor& jobs, int64_t device) {
     memcpy(&jb.prescale, &bits, 4);
     RC_CHECK(jb.k_pad % 64 == 0 && jb.rank <= jb.k_pad && jb.rank >= 1, "k_pad must be a multiple of 64 >= rank");
     RC_CHECK(reinterpret_cast<uintptr_t>(jb.bt) % 16 == 0, "prepared basis must be 16-byte aligned");
+    jb.vec = reinterpret_cast<uintptr_t>(jb.q) % 16 == 0 && jb.q_stride % 8 == 0 && jb.channels % 8 == 0;
     max_channels = std::max(max_channels, jb.channels);
   }
   c10::cuda::CUDAGuard guard(static_cast<int>(device));
@@ -146,6 +186,7 @@ const char* prep_one(const __half* q, int64_t q_stride, const float* scale, cons
   jb.k_pad = k_pad;
   jb.channels = channels;
   jb.prescale = prescale;
+  jb.vec = reinterpret_cast<uintptr_t>(q) % 16 == 0 && q_stride % 8 == 0 && channels % 8 == 0;
   dim3 grid((channels + prep::kChannels - 1) / prep::kChannels, 1);
   prep::prep_kernel<<<grid, prep::kThreads, 0, stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? nullptr : "prep: launch failed";

@@ -30,6 +30,8 @@ struct Job {
   __half* out;               // [tokens, k_pad]
   int64_t row_stride;        // pictures: picture row stride; dense: matrix row stride (bytes)
   int tokens, k_pad, rank, frames, height, width;
+  int vec8;                  // dense, rows >= k_pad bytes apart: 2 = 16-byte aligned rows (unpack_dense16),
+                             // 1 = 8-byte aligned (one 8-byte load per thread), 0 = byte loads
 };
 
 struct Params {
@@ -41,8 +43,38 @@ __device__ __forceinline__ uint32_t centered_pair(uint32_t a, uint32_t b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// Dense sources with 16-byte aligned rows at least k_pad bytes apart: one thread per 16 consecutive
+// columns of one token, lanes walking along a row first, so a warp loads whole 64-byte row segments
+// (full sectors: a source in a peer's memory crosses NVLink once, without over-fetch) and stores 32
+// contiguous bytes per thread.
+__device__ __forceinline__ void unpack_dense16(const Job& jb, int64_t item) {
+  const int groups = jb.k_pad >> 4;
+  if (item >= static_cast<int64_t>(jb.tokens) * groups) return;
+  const int token = static_cast<int>(item / groups);
+  const int group = static_cast<int>(item - static_cast<int64_t>(token) * groups);
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(jb.matrix + static_cast<int64_t>(token) * jb.row_stride +
+                                                         group * 16));
+  const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int k = group * 16 + 2 * i;
+    const uint32_t word = words[i >> 1];
+    const uint32_t a = k < jb.rank ? (word >> (16 * (i & 1))) & 0xffu : 128u;
+    const uint32_t b = k + 1 < jb.rank ? (word >> (16 * (i & 1) + 8)) & 0xffu : 128u;
+    w[i] = centered_pair(a, b);
+  }
+  uint4* out = reinterpret_cast<uint4*>(jb.out + static_cast<int64_t>(token) * jb.k_pad + group * 16);
+  out[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  out[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
 __global__ void __launch_bounds__(kThreads) unpack_kernel(const __grid_constant__ Params p) {
   const Job& jb = p.jobs[blockIdx.y];
+  if (jb.vec8 == 2) {
+    unpack_dense16(jb, static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x);
+    return;
+  }
   const int groups = jb.k_pad >> 3;
   const int64_t item = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   if (item >= static_cast<int64_t>(jb.tokens) * groups) return;
@@ -52,10 +84,22 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const __grid_constant_
   bool live[8];
   if (jb.matrix != nullptr) {
     const uint8_t* rowp = jb.matrix + static_cast<int64_t>(token) * jb.row_stride + group * 8;
+    if (jb.vec8) {
+      // one 8-byte load: a source in a peer's memory (the sequence-parallel restore) then costs one
+      // NVLink request per 8 coefficients instead of eight byte loads
+      const uint2 raw = __ldg(reinterpret_cast<const uint2*>(rowp));
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      live[i] = group * 8 + i < jb.rank;
-      px[i] = live[i] ? __ldg(rowp + i) : 128u;
+      for (int i = 0; i < 8; ++i) {
+        live[i] = group * 8 + i < jb.rank;
+        const uint32_t word = i < 4 ? raw.x : raw.y;
+        px[i] = live[i] ? (word >> (8 * (i & 3))) & 0xffu : 128u;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        live[i] = group * 8 + i < jb.rank;
+        px[i] = live[i] ? __ldg(rowp + i) : 128u;
+      }
     }
   } else {
     const int per_frame = jb.height * jb.width;
@@ -118,6 +162,12 @@ void unpack_launch(const at::Tensor& jobs, int64_t device) {
     jb.frames = static_cast<int>(r[9]);
     jb.height = static_cast<int>(r[10]);
     jb.width = static_cast<int>(r[11]);
+    jb.vec8 = 0;
+    if (jb.matrix != nullptr && jb.row_stride >= jb.k_pad) {
+      const uintptr_t base = reinterpret_cast<uintptr_t>(jb.matrix);
+      if (base % 16 == 0 && jb.row_stride % 16 == 0) jb.vec8 = 2;
+      else if (base % 8 == 0 && jb.row_stride % 8 == 0) jb.vec8 = 1;
+    }
     RC_CHECK(jb.k_pad % 64 == 0 && jb.k_pad > 0 && jb.rank <= jb.k_pad, "k_pad must be a multiple of 64 >= rank");
     RC_CHECK(reinterpret_cast<uintptr_t>(jb.out) % 16 == 0, "unpack output must be 16-byte aligned");
     RC_CHECK(jb.matrix != nullptr || jb.frames * jb.height * jb.width == jb.tokens, "grid does not match the tokens");

@@ -247,3 +247,35 @@ def test_gram_rs_host_helpers():
     gram = x @ x.t()
     upper_only = torch.triu(gram) + torch.tril(torch.full_like(gram, 7.0), -1)
     assert torch.allclose(symmetric_from_upper(upper_only), gram)
+
+
+def test_history_plan_and_layouts():
+    """Sequence-parallel restore plan (parallel/sp_restore.py): owners, aligned arena offsets, and layouts that
+    partition the history exactly (every token and channel of every matrix restored by exactly one rank)."""
+    from reelcache_b200.parallel.sp_restore import HistoryLayout, default_owner, plan_history
+    shapes = [(c, l, t, 4680, 30 + 7 * (c + l)) for c in range(5) for l in range(3) for t in ("K", "V")]
+    for world in (1, 2, 3, 4):
+        plan = plan_history(shapes, world, 1536)
+        for tile in plan.tiles:
+            assert tile.owner == default_owner(tile.layer, tile.target, world)
+            assert tile.coeff_offset % 256 == 0 and tile.basis_offset % 256 == 0
+            assert tile.coeff_offset >= plan.basis_bytes[tile.owner]
+            end = tile.coeff_offset + plan.region_shift(tile.owner) + tile.coeff_bytes
+            assert end <= plan.capacity
+        for owner in range(world):  # regions of one owner do not overlap
+            spans = sorted((t.coeff_offset, t.coeff_offset + t.coeff_bytes) for t in plan.owned(owner))
+            spans += sorted((t.basis_offset, t.basis_offset + t.basis_bytes) for t in plan.owned(owner))
+            spans.sort()
+            assert all(a[1] <= b[0] for a, b in zip(spans, spans[1:]))
+        for kind in ("sequence", "heads", "rows"):
+            if kind == "sequence" and world > 5:
+                continue
+            layout = HistoryLayout(kind, world, chunks=5, tokens=4680, heads=12, head_dim=128)
+            for tile in plan.tiles:
+                cover = torch.zeros((4680, 1536), dtype=torch.int32)
+                for rank in range(world):
+                    for piece in layout.pieces(rank, tile):
+                        cover[piece.row0:piece.row0 + piece.rows, piece.col0:piece.col0 + piece.cols] += 1
+                        assert piece.dest_row + piece.rows <= layout.local_tokens(rank)
+                        assert piece.cols == layout.local_heads(rank) * 128
+                assert bool((cover == 1).all()), (kind, world, tile)
