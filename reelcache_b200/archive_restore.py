@@ -273,6 +273,31 @@ class LineageRestorer:
                     program.add(job, group=layer)
         return program
 
+    def node_factors(self, node_ref: str, keys: Sequence[MatrixKey], *, ranges=None, stream=None,
+                     stream_label: str | None = None) -> dict:
+        """The stored factors of ``keys`` for every history piece of ``node_ref`` (within ``ranges``):
+        ``{(token_start, key): (uint8 coefficients [tokens, rank] on the device, FP16 basis [rank, C], scale,
+        offset)}`` -- what a sequence-parallel owner stages for its peers' fused restores."""
+        stream = stream or torch.cuda.current_stream(self.device)
+        out, device_raw = {}, {}
+        for item in self.history(node_ref, ranges):
+            if item.packet_ref not in device_raw:
+                prepared = self.prepared_pack(item.packet_ref)
+                with torch.cuda.stream(stream):
+                    device_raw[item.packet_ref] = prepared.raw.to(self.device, non_blocking=True)
+                self.stats_["h2d_bytes"] += prepared.nbytes
+            prepared = self.prepared_pack(item.packet_ref)
+            piece = item.piece
+            tokens = piece.token_end - piece.token_start
+            for key in keys:
+                entry = key if stream_label is None else (key, stream_label)
+                tile_index, record = item.tiles[entry]
+                values = prepared.tile_view(device_raw[item.packet_ref], tile_index)[piece.offset:piece.offset + tokens]
+                basis, _ = self.bases.get(record.basis_version_ref, record.rank_view, stream)
+                out[(piece.token_start, key)] = (values, basis[:record.rank_view], prepared.scales[tile_index],
+                                                 prepared.offsets[tile_index])
+        return out
+
     def _plan_key(self, node_ref, destination, rope, ranges, slot_of=None):
         """Identity of a restore plan: the node, its ranges, every destination tensor (address, shape,
         strides, dtype) and every piece's RoPE table and positions."""

@@ -8,8 +8,8 @@ x K/V of ``[T, 4096]``).
 * :class:`RowShardedCacheArchive`: **capture** keeps the rank's rows on the host; **flush** (collective) archives
   every pending epoch matrix by matrix -- the rows are gathered to the fit owner, which fits the rank reaching the
   energy target (FP64 Gram eigh) and scatters the factor blocks to their owners (whole-matrix owners alternating
-  by layer and target, :class:`FactorShardSpec`); each owner writes its blocks as one fragment pack into its own
-  store (:class:`OwnerFactorStore`). Publication is two-phase: every rank stages its fragment, a checkpoint agrees,
+  by layer and target, :class:`~.factor_sharding.FactorShardSpec`); each owner writes its blocks as one fragment
+  pack into its own store (:class:`~.factor_sharding.OwnerFactorStore`). Publication is two-phase: every rank stages its fragment, a checkpoint agrees,
   then every rank sets its epoch ref; a failure anywhere discards every staged fragment. **restore** (collective)
   loads the fragments and delivers every rank its native rows (``P[rows] @ Q`` with the pieces moved to the
   native owner).
@@ -31,77 +31,16 @@ from typing import Any, Mapping
 import torch
 
 from ..errors import ConfigurationError, IntegrityError, StateError
-from ..serialization import deserialize_tensors, serialize_tensors
-from ..types import MatrixKey
-from .distributed import DistributedOwner, PeerFailure
-from .factor_sharding import FactorShardDomain, FactorShardSpec
+from ..types import MatrixKey, ModelIdentity, TensorContext
+from .distributed import DistributedOwner, KVLayout, PeerFailure
+from .factor_sharding import FactorShardDomain, NativeOwners, OwnerFactorStore, OwnershipPolicy
 
-FRAGMENT_SCHEMA = "reelcache.row_shard_fragment.v1"
-REF_PREFIX = "cp_cache/epochs/"
 TIERS = ("host_raw", "compressed")
+DOMAIN = "cp_cache"
 
 
 def _label(key: MatrixKey) -> str:
     return f"{key.layer}:{key.target}"
-
-
-class IndexedNativeOwners:
-    """Native owners by explicit token indices (a CP rank's spatial block of every frame)."""
-
-    kind = "rows"
-
-    def __init__(self, token_indices: list[torch.Tensor], channels: int):
-        self.token_indices = [idx.long() for idx in token_indices]
-        self.channels = channels
-
-    def rows(self, rank: int) -> torch.Tensor:
-        return self.token_indices[rank]
-
-    def columns(self, rank: int) -> slice:
-        return slice(0, self.channels)
-
-
-class OwnerFactorStore:
-    """One rank's factor fragments, one pack per epoch, published by ref (two-phase)."""
-
-    def __init__(self, store, rank: int):
-        self.store, self.rank = store, rank
-
-    def ref(self, epoch_id: str) -> str:
-        return f"{REF_PREFIX}{epoch_id}/rank{self.rank}"
-
-    def stage(self, epoch_id: str, blocks: Mapping[MatrixKey, list], ranks: Mapping[MatrixKey, int]) -> str:
-        tensors = {}
-        for key, items in blocks.items():
-            for rows, p, q in items:
-                tensors[f"{_label(key)}:{rows.start}:{rows.stop}:P"] = p.detach().cpu().contiguous()
-                tensors[f"{_label(key)}:{rows.start}:{rows.stop}:Q"] = q.detach().cpu().contiguous()
-        pack = self.store.put(serialize_tensors(tensors))
-        return self.store.put_manifest({"schema": FRAGMENT_SCHEMA, "epoch": epoch_id, "rank": self.rank,
-                                        "ranks": {_label(k): int(v) for k, v in ranks.items()}, "pack": pack},
-                                       references=[pack])
-
-    def publish(self, epoch_id: str, manifest: str) -> None:
-        self.store.set_ref(self.ref(epoch_id), manifest)
-
-    def load(self, epoch_id: str, device) -> tuple[dict, dict]:
-        manifest_ref = self.store.get_ref(self.ref(epoch_id))
-        if manifest_ref is None:
-            raise StateError(f"epoch {epoch_id} has no fragment on rank {self.rank}")
-        manifest = self.store.get_manifest(manifest_ref)
-        if manifest.get("schema") != FRAGMENT_SCHEMA:
-            raise IntegrityError("not a row-shard fragment")
-        tensors = deserialize_tensors(self.store.get(manifest["pack"]), device=device)
-        blocks: dict[MatrixKey, list] = {}
-        for name, value in tensors.items():
-            layer, target, start, stop, which = name.split(":")
-            if which != "P":
-                continue
-            key = MatrixKey(int(layer), target)
-            q = tensors[f"{layer}:{target}:{start}:{stop}:Q"]
-            blocks.setdefault(key, []).append((slice(int(start), int(stop)), value, q))
-        ranks = {MatrixKey(int(k.split(":")[0]), k.split(":")[1]): v for k, v in manifest["ranks"].items()}
-        return blocks, ranks
 
 
 @dataclass
@@ -112,29 +51,39 @@ class _Pending:
 
 class RowShardedCacheArchive:
     """Row-sharded CP cache archive (see the module docstring). ``token_indices[r]`` lists rank ``r``'s token
-    rows of the canonical ``[tokens, channels]`` matrices; ``store`` is this rank's own object store."""
+    rows of the canonical ``[tokens, channels]`` matrices; ``store`` is this rank's own object store, which
+    holds this rank's fragment packs (``svd``: exact FP32 coefficients) and basis segments under
+    ``factor_shard/cp_cache/<epoch>/...``."""
 
     def __init__(self, transport: DistributedOwner, store, token_indices: list[torch.Tensor], *, tokens: int,
                  channels: int, energy_target: float = 0.98, max_rank: int | None = None, fit_owner: int = 0,
-                 spec: FactorShardSpec | None = None):
-        if len(token_indices) != transport.world_size:
+                 policy: OwnershipPolicy | None = None, kind: str = "svd", model: ModelIdentity | None = None):
+        world = transport.world_size
+        if len(token_indices) != world:
             raise ConfigurationError("one token index list per rank")
-        covered = torch.cat([idx.long() for idx in token_indices]).sort().values
-        if covered.numel() != tokens or not torch.equal(covered, torch.arange(tokens)):
-            raise ConfigurationError("the ranks' token rows must partition the matrix rows")
         if not 0.0 < energy_target <= 1.0:
             raise ConfigurationError("energy_target must lie in (0, 1]")
+        if channels % world:
+            raise ConfigurationError("row shards describe channels divisible by the ranks")
         self.transport = transport
         self.tokens, self.channels = tokens, channels
-        self.natives = IndexedNativeOwners(token_indices, channels)
-        self.spec = spec or FactorShardSpec(transport.world_size)
+        # the head split of this layout is bookkeeping only: row owners keep every channel
+        layout = KVLayout(tokens=tokens, kv_heads=world, head_dim=channels // world, world_size=world)
+        self.natives = NativeOwners(layout, "rows", [idx.long().tolist() for idx in token_indices])
         self.energy_target = energy_target
         self.max_rank = max_rank
         self.fit_owner = fit_owner
-        self.fragments = OwnerFactorStore(store, transport.rank)
+        self.kind = kind
+        self.model = model or ModelIdentity("cp-row-cache", "row-shards", 4096, channels, "BTHD", "float32")
+        self.fragments = OwnerFactorStore(store, transport.rank, world, domain=DOMAIN)
+        self.domain = FactorShardDomain(transport, device=transport.device, store=self.fragments,
+                                        policy=policy or OwnershipPolicy(world))
         self.pending: OrderedDict[str, _Pending] = OrderedDict()
         self.archived: set[str] = set()
         self.records: list[dict] = []
+
+    def _context(self, key: MatrixKey) -> TensorContext:
+        return TensorContext(self.model, key, 0, 1, 1, self.tokens, "pre_rope" if key.target == "K" else "none")
 
     def capture(self, epoch_id: str, rows: Mapping[MatrixKey, torch.Tensor]) -> None:
         """Keep this rank's rows of one epoch (host copies) for the next :meth:`flush`."""
@@ -155,73 +104,49 @@ class RowShardedCacheArchive:
                 canonical[self.natives.rows(source)] = piece
         return canonical
 
-    def _rank_for(self, canonical: torch.Tensor) -> int:
-        x = canonical.double()
-        values = torch.linalg.eigvalsh(x.t() @ x).flip(0).clamp_min(0)
-        total = float(values.sum())
-        if total == 0.0:
-            return 1
-        cumulative = torch.cumsum(values, 0) / total
-        rank = int(torch.searchsorted(cumulative, torch.tensor(self.energy_target, dtype=torch.float64))) + 1
-        rank = min(rank, self.channels, self.tokens)
-        return min(rank, self.max_rank) if self.max_rank else rank
-
     def flush(self) -> list[str]:
-        """Collective: archive every pending epoch (two-phase); returns the epochs archived by this call."""
+        """Collective: archive every pending epoch -- gather each matrix to the fit owner, fit it there (the
+        smallest rank reaching the energy target), scatter the blocks to their owners, then publish the epoch's
+        fragments in two phases (all owners or none). Returns the epochs archived by this call."""
         t = self.transport
         done = []
         epochs = t.broadcast_json(list(self.pending), operation="row_archive:epochs", source=self.fit_owner)
         for epoch_id in epochs:
             started = time.perf_counter()
-            domain = FactorShardDomain(t, self.spec, self.natives)
             pending = self.pending.get(epoch_id)
             error = None if pending is not None else f"epoch {epoch_id} was not captured on rank {t.rank}"
             keys = t.broadcast_json(sorted(_label(k) for k in pending.rows) if pending else [],
                                     operation=f"row_archive:{epoch_id}:keys", source=self.fit_owner)
             t.checkpoint(f"row_archive:{epoch_id}:captured", error=error)
+            shards = {}
             for label in keys:
                 layer, target = label.split(":")
                 key = MatrixKey(int(layer), target)
                 canonical = self._gather(key, pending.rows[key], f"row_archive:{epoch_id}")
-                rank = self._rank_for(canonical) if t.rank == self.fit_owner else 0
-                domain.fit_and_scatter(key, canonical, rank, fit_owner=self.fit_owner,
-                                       operation=f"row_archive:{epoch_id}:{label}")
-            staged, error = None, None
-            try:
-                staged = self.fragments.stage(epoch_id, domain.factors, domain.ranks)
-            except Exception as exc:  # noqa: BLE001 - phase one failed here: every rank discards
-                error = exc
-            t.checkpoint(f"row_archive:{epoch_id}:staged", error=error)   # raises on every rank on failure
-            self.fragments.publish(epoch_id, staged)
-            t.checkpoint(f"row_archive:{epoch_id}:published")
+                shards.update(self.domain.fit_and_scatter(
+                    [key], {key: canonical} if canonical is not None else None, {key: self._context(key)},
+                    energy=self.energy_target, fit_owner=self.fit_owner, max_rank=self.max_rank,
+                    operation=f"row_archive:{epoch_id}:{label}"))
+            self.domain.publish_node(epoch_id, shards, kind=self.kind)
             self.pending.pop(epoch_id, None)
             self.archived.add(epoch_id)
             self.records.append({"epoch": epoch_id, "matrices": len(keys), "seconds": time.perf_counter() - started,
-                                 "ranks": {_label(k): v for k, v in domain.ranks.items()}})
+                                 "ranks": {_label(k): s.spec.rank_view for k, s in shards.items()}})
             done.append(epoch_id)
         return done
 
     def restore(self, epoch_id: str, *, dtype=torch.float32) -> dict[MatrixKey, torch.Tensor]:
-        """Collective: this rank's native rows of every matrix of an archived epoch."""
-        t = self.transport
-        error = None
-        blocks, ranks = {}, {}
+        """Collective: this rank's native rows of every matrix of an archived epoch (owners send their
+        coefficient rows and basis rows to each native owner, which multiplies)."""
+        error, shards = None, {}
         try:
-            blocks, ranks = self.fragments.load(epoch_id, t.device)
-        except Exception as exc:  # noqa: BLE001
+            node_map = self.domain.node_map(epoch_id)
+            shards = self.domain.load_node(node_map, quantized=False)
+        except Exception as exc:  # noqa: BLE001 - agreed before the reconstruction's payloads
             error = exc
-        t.checkpoint(f"row_restore:{epoch_id}:loaded", error=error)
-        all_ranks = t.broadcast_json({_label(k): v for k, v in ranks.items()},
-                                     operation=f"row_restore:{epoch_id}:ranks", source=self.fit_owner)
-        domain = FactorShardDomain(t, self.spec, self.natives)
-        domain.factors = blocks
-        out = {}
-        for label in sorted(all_ranks):
-            layer, target = label.split(":")
-            key = MatrixKey(int(layer), target)
-            domain.ranks[key] = all_ranks[label]
-            out[key] = domain.reconstruct(key, mode="factors", dtype=dtype)
-        return out
+        self.transport.checkpoint(f"row_restore:{epoch_id}:loaded", error=error)
+        return self.domain.reconstruct(shards, self.natives, mode="factors", dtype=dtype,
+                                       operation=f"row_restore:{epoch_id}")
 
 
 @dataclass(eq=False)
@@ -310,4 +235,4 @@ class TieredRowArchive:
         return "compressed", rows
 
 
-__all__ = ["IndexedNativeOwners", "OwnerFactorStore", "RowEntry", "RowShardedCacheArchive", "TieredRowArchive"]
+__all__ = ["RowEntry", "RowShardedCacheArchive", "TieredRowArchive"]

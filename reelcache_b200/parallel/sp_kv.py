@@ -10,7 +10,10 @@ Under Ulysses every rank owns a **head slice** of every chunk's K and V.
    collectively (every rank evicts the same chunks, so a chunk is hot on all ranks or on none).
 3. **Cold tier**: a chunk that is not hot is decoded on exactly one rank -- round robin by chunk,
    rotated by layer (``(chunk + layer) % world``) -- from the shared store of the node, and its head
-   columns are scattered to their ranks.
+   columns are scattered to their ranks (:meth:`SPTieredHistory.load_layer`: point-to-point transfers of the
+   dense slices). On CUDA, :meth:`SPTieredHistory.prepare_fused` instead keeps the decoder's 8-bit
+   coefficients and basis in its symmetric arena and every rank's fused restore reads its heads from there
+   over NVLink (parallel/sp_restore.py): the scatter disappears into the restore kernels.
 """
 
 from __future__ import annotations
@@ -107,6 +110,54 @@ class SPTieredHistory:
                 parts.append(self._cold(chunk, layer, target))
             out[target] = torch.cat(parts) if parts else torch.empty(0, self.layout.local_channels)
         return out
+
+    def prepare_fused(self, destination, *, chunks: int | None = None, rope=None, stream=None):
+        """Stage the cold history for fused restores (CUDA, one process per GPU): the decoder rank of every
+        (chunk, layer) -- ``(chunk + layer) % world``, as for :meth:`load_layer` -- loads the stored 8-bit
+        coefficients and basis into its symmetric arena, and every rank's restore kernels read its own head
+        columns from there over NVLink (no scatter collective). Returns a
+        :class:`~.sp_restore.FusedHistoryRestore`; each ``restore()`` writes ``destination(layer, target)``
+        (``[1, chunks * chunk_tokens, local_heads, head_dim]``). ``rope(chunk)`` gives the ``RopePositions`` of
+        a chunk's K (None: no rotation). Collective."""
+        from ..archive_restore import LineageRestorer
+        from .sp_restore import FusedHistoryRestore, HistoryLayout, plan_history
+
+        chunks = len(self.nodes) if chunks is None else chunks
+        world = self.t.world_size
+        tokens = self.layout.tokens
+        shapes, owners, keys = [], [], []
+        ranks = {}
+        error = None
+        mine = {}
+        try:
+            restorer = LineageRestorer(self.runtime, self.t.device)
+            for chunk in range(chunks):
+                span = [(chunk * tokens, (chunk + 1) * tokens)]
+                wanted = [MatrixKey(layer, target) for layer in range(self.layers) for target in ("K", "V")
+                          if (chunk + layer) % world == self.t.rank]
+                if wanted:
+                    factors = restorer.node_factors(self.nodes[chunk], wanted, ranges=span, stream=stream)
+                    for (start, key), value in factors.items():
+                        mine[(chunk, key.layer, key.target)] = value
+                        ranks[f"{chunk}:{key.layer}:{key.target}"] = int(value[0].shape[1])
+        except Exception as exc:  # noqa: BLE001 - agreed before any payload moves
+            error = exc
+        reported = self.t.checkpoint("fused:ranks", error=error, details=ranks)
+        every = {k: v for rows in reported for k, v in rows.items()}
+        for chunk in range(chunks):
+            for layer in range(self.layers):
+                for target in ("K", "V"):
+                    shapes.append((chunk, layer, target, tokens, every[f"{chunk}:{layer}:{target}"]))
+                    owners.append((chunk + layer) % world)
+        plan = plan_history(shapes, world, self.layout.channels, owners=owners)
+        layout = HistoryLayout("heads", world, chunks=chunks, tokens=tokens, heads=self.layout.kv_heads,
+                               head_dim=self.layout.head_dim)
+        fused = FusedHistoryRestore.create(plan, layout, self.grid, self.t.device,
+                                           group=self.t.group if world > 1 else None)
+        fused.stage({tile.index: mine[(tile.chunk, tile.layer, tile.target)] for tile in plan.owned(self.t.rank)})
+        fused.build(destination, None if rope is None else (lambda tile: rope(tile.chunk)), stream=stream)
+        self.stats["fused_prepared"] = self.stats.get("fused_prepared", 0) + 1
+        return fused
 
     def _cold(self, chunk: int, layer: int, target: str) -> torch.Tensor:
         decoder = (chunk + layer) % self.t.world_size

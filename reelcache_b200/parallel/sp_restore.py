@@ -192,18 +192,24 @@ class HistoryPlan:
 
 
 def plan_history(shapes: Sequence[tuple[int, int, str, int, int]], world: int, channels: int, *,
-                 owner: Callable[[int, str, int], int] = default_owner, regions: int = 2) -> HistoryPlan:
-    """``shapes``: ``(chunk, layer, target, tokens, rank)`` of every matrix of the history. Offsets are
-    256-byte aligned (TMA and vector loads), bases first so that they stay put across regions."""
+                 owner: Callable[[int, str, int], int] = default_owner, owners: Sequence[int] | None = None,
+                 regions: int = 2) -> HistoryPlan:
+    """``shapes``: ``(chunk, layer, target, tokens, rank)`` of every matrix of the history; ``owners`` (one per
+    shape) overrides the ``owner`` rule. Offsets are 256-byte aligned (TMA and vector loads), bases first so
+    that they stay put across regions."""
+    if owners is not None and len(owners) != len(shapes):
+        raise ConfigurationError("one owner per matrix")
     if regions not in (1, 2):
         raise ConfigurationError("one or two coefficient regions")
     basis_cursor = [0] * world
     coeff_cursor = [0] * world
     staged = []
-    for chunk, layer, target, tokens, rank in shapes:
+    for index, (chunk, layer, target, tokens, rank) in enumerate(shapes):
         if rank < 1 or rank > channels or tokens < 1:
             raise ConfigurationError("tile rank must be in [1, channels] and tokens positive")
-        o = owner(layer, target, world)
+        o = owner(layer, target, world) if owners is None else owners[index]
+        if not 0 <= o < world:
+            raise ConfigurationError("matrix owner outside the group")
         staged.append((chunk, layer, target, tokens, rank, o, coeff_cursor[o], basis_cursor[o]))
         basis_cursor[o] += align(rank * channels * 2)
         coeff_cursor[o] += align(tokens * k_pad_of(rank))

@@ -125,3 +125,115 @@ def test_fused_history_restore_two_gpus(tmp_path, kind):
     result = tmp_path / "failures.txt"
     mp.spawn(_worker, args=(world, _free_port(), kind, str(result)), nprocs=world, join=True)
     assert result.read_text() == "0"
+
+
+def _domain_worker(rank, world, port, root, result_path):
+    """FactorShardDomain.reconstruct(mode="fused") against the NCCL "factors" mode, and the SP tiered
+    history's fused cold restore against its point-to-point load_layer, on real archived factors."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from reelcache_b200 import restore_kernels as rk
+    from reelcache_b200.lineage import LineageRuntime
+    from reelcache_b200.parallel.distributed import DistributedOwner, KVLayout
+    from reelcache_b200.parallel.factor_sharding import FactorShardDomain, NativeOwners, OwnerFactorStore
+    from reelcache_b200.parallel.sp_kv import SPTieredHistory
+    from reelcache_b200.store import ObjectStore
+    from reelcache_b200.types import MatrixKey, ModelIdentity, TensorContext
+    from tests.lineage_support import FRAMES, HEIGHT, MODEL, TOKENS, WIDTH, chunk, method
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=device)
+    errors = []
+    try:
+        control = dist.new_group(backend="gloo")
+        t = DistributedOwner(None, control_group=control, device=device)
+        # -- factor-sharded node: fused vs factors --------------------------------------------------------
+        heads, head_dim = 4, 128
+        channels, grid = heads * head_dim, GRID
+        tokens = grid[0] * grid[1] * grid[2]
+        model = ModelIdentity("tiny-cp", "fp", 2, channels, "BTHD", "bfloat16")
+        gen = torch.Generator().manual_seed(5)
+        keys = [MatrixKey(l, tg) for l in range(2) for tg in ("K", "V")]
+        canon = {k: (torch.randn(tokens, 24, generator=gen) @ torch.randn(24, channels, generator=gen)) for k in keys}
+        contexts = {k: TensorContext(model, k, 0, *grid, "pre_rope" if k.target == "K" else "none") for k in keys}
+        store = ObjectStore(f"{root}/owner{rank}")
+        domain = FactorShardDomain(t, device=device, store=OwnerFactorStore(store, rank, world))
+        shards = domain.fit_and_scatter(keys, canon if rank == 0 else None, contexts, ranks={k: 24 for k in keys})
+        node_map = domain.publish_node("n0", shards, kind="svd_hevc")
+        loaded = domain.load_node(node_map, quantized=True)
+        table = rk.RopeTable.wan(head_dim, 16, device=device)
+        for kind in ("heads", "rows"):
+            native = NativeOwners(KVLayout(tokens, heads, head_dim, world), kind)
+            fused = domain.reconstruct(loaded, native, mode="fused", dtype=torch.float32,
+                                       rope_positions=lambda key: rk.RopePositions(table, (0, 0, 0)))
+            plain = domain.reconstruct(loaded, native, mode="factors", dtype=torch.float32)
+            for key in keys:
+                want = plain[key]
+                if key.target == "K":  # the factors path leaves K pre-RoPE: rotate it the reference way
+                    view = want.reshape(want.shape[0], -1, head_dim).double()
+                    rows = native.rows(rank)
+                    job_rows = rk.RopePositions(table, (0, 0, 0))
+                    cos, sin = rk.rope_cos_sin(job_rows, grid, dtype=torch.float64, device=device)
+                    cos, sin = cos[rows.to(device)][:, None, :], sin[rows.to(device)][:, None, :]
+                    rot = torch.empty_like(view)
+                    rot[..., 0::2] = view[..., 0::2] * cos - view[..., 1::2] * sin
+                    rot[..., 1::2] = view[..., 0::2] * sin + view[..., 1::2] * cos
+                    want = rot.reshape(want.shape).float()
+                err = float((fused[key] - want).norm() / want.norm())
+                if err > 1e-3:
+                    errors.append(("domain", kind, str(key), err))
+        store.close()
+        # -- SP tiered history: fused cold restore vs point-to-point load_layer ----------------------------
+        shared = ObjectStore(f"{root}/shared")
+        runtime = LineageRuntime(shared, MODEL)
+        if rank == 0:
+            runtime.create_lineage("sp")
+        t.checkpoint("created")
+        hist_heads = 2
+        hd = MODEL.channels_for("K") // hist_heads
+        hist = SPTieredHistory(t, runtime, "sp", layers=MODEL.layers, kv_heads=hist_heads, head_dim=hd,
+                               chunk_tokens=TOKENS, grid=(FRAMES, HEIGHT, WIDTH), hot_budget_bytes=0,
+                               method=method(), device=device)
+        cols = slice(rank * (MODEL.channels_for("K") // world), (rank + 1) * (MODEL.channels_for("K") // world))
+        for index in range(3):
+            matrices, _ = chunk(index)
+            hist.capture(index, {(k.layer, k.target): v[:, cols].contiguous().to(device) for k, v in matrices.items()})
+        local = {(l, tg): torch.zeros((1, 3 * TOKENS, hist_heads // world, hd), dtype=torch.float32, device=device)
+                 for l in range(MODEL.layers) for tg in ("K", "V")}
+        fused_hist = hist.prepare_fused(lambda l, tg: local[(l, tg)])
+        fused_hist.restore()
+        torch.cuda.synchronize(device)
+        fused_hist.check()
+        for layer in range(MODEL.layers):
+            dense = hist.load_layer(layer)
+            for target in ("K", "V"):
+                got = local[(layer, target)][0].reshape(3 * TOKENS, -1)
+                want = dense[target].to(device).float()
+                err = float((got - want).norm() / want.norm())
+                if err > 2e-3:
+                    errors.append(("sp_history", layer, target, err))
+        fused_hist.close()
+        shared.close()
+        flag = torch.tensor([len(errors)], device=device)
+        dist.all_reduce(flag)
+        if rank == 0:
+            with open(result_path, "w") as handle:
+                handle.write(f"{int(flag.item())} {errors}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_factor_domain_and_sp_history_fused_two_gpus(tmp_path):
+    world = 2
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    result = tmp_path / "failures.txt"
+    mp.spawn(_domain_worker, args=(world, _free_port(), str(tmp_path), str(result)), nprocs=world, join=True)
+    text = result.read_text()
+    assert text.startswith("0 "), text
