@@ -1,11 +1,14 @@
-"""Immutable FP16 basis row blocks and their version manifests (reference:
-reelcache/basis_versions.py:73-432; same manifest form ``{"type": "basis_version", "version": 1,
-"record": <reelcache.basis_version.v1>}`` referencing its parent version and its one row block).
+"""Immutable FP16 basis row blocks and the version chains built from them.
 
-A version's canonical view is its ancestors' rows followed by its own block, never reordered or
-copied, so sharing a basis between chunks shares these objects and store GC sees the whole chain.
-Lossy packets bind the exact prefix view they were encoded with by a ``basis`` descriptor (shape,
-view rank, SHA-256); :func:`attach_basis` re-attaches an assembled prefix only after that check.
+Storage (shared with the reference implementation, reelcache/basis_versions.py, so that either can read the
+other's store): every version is a manifest ``{"type": "basis_version", "version": 1, "record":
+<reelcache.basis_version.v1>}`` that references exactly its own row block (a ``basis:`` object of FP16
+little-endian rows) and, unless it is a root, its parent version. A version's view is its ancestors' rows
+followed by its own block -- appended, never rewritten -- so chunks that share or extend a basis share these
+objects and garbage collection follows the whole chain.
+
+Lossy packets name the exact prefix view they were encoded against with a ``basis`` descriptor (shape, view
+rank, byte count, SHA-256); :func:`attach_basis` puts an assembled prefix back only when it matches.
 """
 
 from __future__ import annotations
@@ -13,6 +16,7 @@ from __future__ import annotations
 import hashlib
 import sys
 from collections import OrderedDict
+from dataclasses import dataclass
 from typing import Any, Iterable, Mapping
 
 import numpy as np
@@ -23,292 +27,330 @@ from .store import ObjectStore
 from .types import BasisVersion, EncodedTensor, MatrixKey, ModelIdentity, json_copy, object_ref
 
 MANIFEST_TYPE = "basis_version"
-_FP16_EXPONENT = 0x7C00
+MANIFEST_VERSION = 1
+_EXPONENT_MASK = np.uint16(0x7C00)   # an FP16 value with every exponent bit set is an infinity or a NaN
 
 
 def finite_fp16(data) -> bool:
-    bits = np.frombuffer(data, dtype=np.uint16)
-    return not bool(np.any((bits & _FP16_EXPONENT) == _FP16_EXPONENT))
+    """True when no FP16 value in ``data`` is an infinity or a NaN."""
+    halves = np.frombuffer(data, dtype=np.uint16)
+    return not bool(((halves & _EXPONENT_MASK) == _EXPONENT_MASK).any())
 
 
 def rows_to_bytes(rows: torch.Tensor) -> bytes:
-    if not isinstance(rows, torch.Tensor) or rows.dtype != torch.float16 or rows.ndim != 2 or min(rows.shape) < 1:
-        raise ConfigurationError("basis row blocks are nonempty FP16 [rows, channels] tensors")
+    """Little-endian bytes of a finite, nonempty FP16 ``[rows, channels]`` block."""
+    ok = isinstance(rows, torch.Tensor) and rows.dtype == torch.float16 and rows.dim() == 2 and rows.numel() > 0
+    if not ok:
+        raise ConfigurationError("a basis block is a nonempty FP16 [rows, channels] tensor")
     if sys.byteorder != "little":
-        raise ConfigurationError("basis row serialization requires a little-endian host")
-    data = rows.detach().to("cpu").contiguous().numpy().tobytes()
+        raise ConfigurationError("basis blocks are stored little-endian; this host is not")
+    data = rows.detach().cpu().contiguous().numpy().tobytes()
     if not finite_fp16(data):
-        raise ConfigurationError("basis row blocks must be finite")
+        raise ConfigurationError("a basis block holds an infinity or a NaN")
     return data
 
 
 def rows_from_bytes(data: bytes, rows: int, channels: int) -> torch.Tensor:
-    if not isinstance(data, (bytes, bytearray)) or len(data) != rows * channels * 2:
-        raise IntegrityError("basis row block length disagrees with its declared geometry")
+    if not isinstance(data, (bytes, bytearray)) or len(data) != 2 * rows * channels:
+        raise IntegrityError(f"a basis block of {rows} x {channels} needs {2 * rows * channels} bytes")
     return torch.from_numpy(np.frombuffer(data, dtype=np.float16).reshape(rows, channels).copy())
 
 
-class BasisVersionStore:
-    """Validated basis-version operations over one runtime's store (callers own transactions)."""
+@dataclass(frozen=True)
+class _Link:
+    """One version of a chain: its block and how many rows it adds."""
 
-    VIEW_DIGESTS = 16384
+    ref: str
+    block: str
+    rows: int
+
+
+class BasisVersionStore:
+    """Basis versions of one model in one object store (the caller owns transactions)."""
+
+    DIGEST_CACHE = 16384
 
     def __init__(self, store: ObjectStore, model: ModelIdentity):
-        if not isinstance(store, ObjectStore) or not isinstance(model, ModelIdentity):
-            raise ConfigurationError("basis versions require an ObjectStore and ModelIdentity")
+        if not isinstance(store, ObjectStore):
+            raise ConfigurationError("basis versions live in an ObjectStore")
+        if not isinstance(model, ModelIdentity):
+            raise ConfigurationError("basis versions belong to a ModelIdentity")
         self.store, self.model = store, model
-        self._cache: dict[str, BasisVersion] = {}
-        self._finite_blocks: set[str] = set()
-        self._view_digests: OrderedDict[str, Any] = OrderedDict()
+        self._versions: dict[str, BasisVersion] = {}      # validated versions (their chains too)
+        self._finite: set[str] = set()                     # blocks already checked to be finite
+        self._running: OrderedDict[str, Any] = OrderedDict()  # version -> sha256 state of its full view
+
+    # -- caches --------------------------------------------------------------------------------------------
 
     def drop_caches(self) -> None:
-        self._cache.clear()
-        self._finite_blocks.clear()
-        self._view_digests.clear()
+        self._versions.clear()
+        self._finite.clear()
+        self._running.clear()
 
     def cached_ids(self) -> list[str]:
-        return [*self._cache, *self._finite_blocks, *self._view_digests]
+        return list(self._versions) + list(self._finite) + list(self._running)
 
     def forget_unstored(self, present: set[str]) -> dict[str, int]:
-        versions = [ref for ref in self._cache if ref not in present]
-        for ref in versions:
-            del self._cache[ref]
-        blocks = [b for b in self._finite_blocks if b not in present]
-        self._finite_blocks.difference_update(blocks)
-        digests = [ref for ref in self._view_digests if ref not in present]
-        for ref in digests:
-            del self._view_digests[ref]
-        return {"basis_versions": len(versions), "finite_blocks": len(blocks), "view_digests": len(digests)}
+        """Drop cache entries of objects no longer in the store (after eviction or GC)."""
+        dropped = {"basis_versions": 0, "finite_blocks": 0, "view_digests": 0}
+        for ref in [r for r in self._versions if r not in present]:
+            del self._versions[ref]
+            dropped["basis_versions"] += 1
+        gone = {b for b in self._finite if b not in present}
+        self._finite -= gone
+        dropped["finite_blocks"] = len(gone)
+        for ref in [r for r in self._running if r not in present]:
+            del self._running[ref]
+            dropped["view_digests"] += 1
+        return dropped
 
     def missing(self, refs: Iterable[str]) -> list[str]:
-        return [ref for ref in dict.fromkeys(refs) if ref not in self._cache]
+        return [ref for ref in dict.fromkeys(refs) if ref not in self._versions]
 
-    # -- creation ------------------------------------------------------------------------------------------------
+    def _keep_running(self, ref: str, state) -> None:
+        self._running[ref] = state
+        self._running.move_to_end(ref)
+        if len(self._running) > self.DIGEST_CACHE:
+            self._running.popitem(last=False)
 
-    def _check_rows(self, key: MatrixKey, rows: torch.Tensor) -> None:
+    # -- writing -------------------------------------------------------------------------------------------
+
+    def _validate_rows(self, key: MatrixKey, rows: torch.Tensor) -> None:
         if not isinstance(key, MatrixKey) or key.layer >= self.model.layers:
-            raise ConfigurationError("basis key is outside the model")
-        if rows.ndim != 2 or rows.shape[1] != self.model.channels_for(key):
-            raise ConfigurationError("basis rows do not match the model's channel width")
+            raise ConfigurationError(f"matrix {key!r} is not a matrix of the model")
+        if rows.dim() != 2 or rows.shape[1] != self.model.channels_for(key):
+            raise ConfigurationError(f"basis rows of {key!r} need {self.model.channels_for(key)} channels")
 
-    def put_root(self, key: MatrixKey, rows: torch.Tensor) -> tuple[str, BasisVersion]:
-        """Store a new group's first block and its depth-zero version."""
-        self._check_rows(key, rows)
-        data = rows_to_bytes(rows)
-        block = self.store.put(data, kind="basis")
-        digest = hashlib.sha256(data)
-        version = BasisVersion(None, block, int(rows.shape[0]), int(rows.shape[0]), int(rows.shape[1]),
-                               BasisVersion.root_group_id(self.model.fingerprint, key, block), key,
-                               self.model.fingerprint, 0, digest.hexdigest())
-        ref = self._put_version(version)
-        self._remember_digest(ref, digest)
-        return ref, version
-
-    def put_extension(self, parent_ref: str, rows: torch.Tensor) -> tuple[str, BasisVersion]:
-        """Append an immutable row block to ``parent_ref`` (the parent is unchanged)."""
-        parent = self.load(parent_ref)
-        self._check_rows(parent.key, rows)
-        if parent.total_rank + rows.shape[0] > parent.channels:
-            raise ConfigurationError("an extension cannot exceed the channel count")
-        data = rows_to_bytes(rows)
-        known = self._view_digests.get(parent_ref)
-        if known is not None:
-            digest = known.copy()
-        else:
-            digest = hashlib.sha256()
-            for block, _ in self._blocks(parent_ref):
-                digest.update(self.store.get(block))
-        digest.update(data)
-        block = self.store.put(data, kind="basis")
-        version = BasisVersion(parent_ref, block, int(rows.shape[0]), parent.total_rank + int(rows.shape[0]),
-                               parent.channels, parent.group_id, parent.key, parent.model_fingerprint,
-                               parent.depth + 1, digest.hexdigest())
-        ref = self._put_version(version)
-        self._remember_digest(ref, digest)
-        return ref, version
-
-    def _remember_digest(self, ref: str, digest) -> None:
-        self._view_digests[ref] = digest
-        self._view_digests.move_to_end(ref)
-        while len(self._view_digests) > self.VIEW_DIGESTS:
-            self._view_digests.popitem(last=False)
-
-    def _put_version(self, version: BasisVersion) -> str:
-        references = [version.added_rows_ref] + ([] if version.parent_ref is None else [version.parent_ref])
-        ref = self.store.put_manifest({"type": MANIFEST_TYPE, "version": 1, "record": version.to_dict()},
-                                      references=references)
-        self._cache[ref] = version
+    def _write(self, version: BasisVersion, running) -> str:
+        refs = [version.added_rows_ref]
+        if version.parent_ref is not None:
+            refs.append(version.parent_ref)
+        ref = self.store.put_manifest({"type": MANIFEST_TYPE, "version": MANIFEST_VERSION,
+                                       "record": version.to_dict()}, references=refs)
+        self._versions[ref] = version
+        self._keep_running(ref, running)
         return ref
 
-    # -- validation and reads ------------------------------------------------------------------------------------
+    def put_root(self, key: MatrixKey, rows: torch.Tensor) -> tuple[str, BasisVersion]:
+        """The first block of a new basis group, as a depth-zero version."""
+        self._validate_rows(key, rows)
+        data = rows_to_bytes(rows)
+        block = self.store.put(data, kind="basis")
+        running = hashlib.sha256(data)
+        count = int(rows.shape[0])
+        version = BasisVersion(None, block, count, count, int(rows.shape[1]),
+                               BasisVersion.root_group_id(self.model.fingerprint, key, block), key,
+                               self.model.fingerprint, 0, running.hexdigest())
+        return self._write(version, running), version
 
-    def load(self, ref: str) -> BasisVersion:
-        """Validate one version and (recursively, cached) its whole parent chain."""
-        object_ref(ref, "basis version")
-        cached = self._cache.get(ref)
-        if cached is not None:
-            return cached
-        version = self._parse(*self.store.get_manifest_with_references(ref))
-        if self.store.object_size(version.added_rows_ref) != version.added_bytes:
-            raise IntegrityError("basis row block size disagrees with its version")
-        if version.parent_ref is not None:
-            self.load(version.parent_ref)
-        self._link(version)
-        self._cache[ref] = version
-        return version
+    def put_extension(self, parent_ref: str, rows: torch.Tensor) -> tuple[str, BasisVersion]:
+        """A new version appending ``rows`` to ``parent_ref``'s view (the parent stays as it is)."""
+        parent = self.load(parent_ref)
+        self._validate_rows(parent.key, rows)
+        if parent.total_rank + rows.shape[0] > parent.channels:
+            raise ConfigurationError(f"the extension would give {parent.key!r} more rows than channels")
+        data = rows_to_bytes(rows)
+        cached = self._running.get(parent_ref)
+        running = cached.copy() if cached is not None else self._digest_of(parent_ref)
+        running.update(data)
+        block = self.store.put(data, kind="basis")
+        count = int(rows.shape[0])
+        version = BasisVersion(parent_ref, block, count, parent.total_rank + count, parent.channels,
+                               parent.group_id, parent.key, parent.model_fingerprint, parent.depth + 1,
+                               running.hexdigest())
+        return self._write(version, running), version
 
-    def load_many(self, refs: Iterable[str]) -> list[BasisVersion]:
-        refs = list(refs)
-        for ref in refs:
-            self.load(ref)
-        return [self._cache[ref] for ref in refs]
+    def _digest_of(self, ref: str):
+        running = hashlib.sha256()
+        for link in self._links(ref):
+            running.update(self.store.get(link.block))
+        return running
 
-    def _parse(self, data, references) -> BasisVersion:
+    # -- reading and validation ----------------------------------------------------------------------------
+
+    def _decode(self, ref: str) -> BasisVersion:
+        data, references = self.store.get_manifest_with_references(ref)
+        if not isinstance(data, Mapping) or set(data) != {"type", "version", "record"} or \
+                data.get("type") != MANIFEST_TYPE or data.get("version") != MANIFEST_VERSION:
+            raise IntegrityError(f"{ref} is not a basis version manifest")
         try:
-            if data.get("type") != MANIFEST_TYPE or data.get("version") != 1 or set(data) != {"type", "version",
-                                                                                               "record"}:
-                raise IntegrityError("unsupported basis version manifest")
             version = BasisVersion.from_dict(data["record"])
         except (ConfigurationError, TypeError, AttributeError) as exc:
-            raise IntegrityError("invalid basis version manifest") from exc
-        expected = sorted({version.added_rows_ref} | ({version.parent_ref} if version.parent_ref else set()))
-        if list(references) != expected:
-            raise IntegrityError("basis version references disagree with its parent/block")
+            raise IntegrityError(f"{ref} holds an invalid basis version record: {exc}") from exc
+        wanted = {version.added_rows_ref} | ({version.parent_ref} if version.parent_ref else set())
+        if sorted(wanted) != list(references):
+            raise IntegrityError(f"{ref} references other objects than its block and parent")
         if version.model_fingerprint != self.model.fingerprint or version.key.layer >= self.model.layers:
-            raise IntegrityError("basis version belongs to another model")
+            raise IntegrityError(f"{ref} belongs to another model")
         if version.channels != self.model.channels_for(version.key):
-            raise IntegrityError("basis version channel width disagrees with the model")
+            raise IntegrityError(f"{ref} has another channel width than the model's {version.key!r}")
+        if self.store.object_size(version.added_rows_ref) != version.added_bytes:
+            raise IntegrityError(f"{ref}: its block's size disagrees with the rows it declares")
         return version
 
-    def _link(self, version: BasisVersion) -> None:
+    def _check_link(self, version: BasisVersion) -> None:
         if version.parent_ref is None:
-            if version.group_id != BasisVersion.root_group_id(version.model_fingerprint, version.key,
-                                                              version.added_rows_ref):
-                raise IntegrityError("root basis group identity is not bound to its first block")
+            bound = BasisVersion.root_group_id(version.model_fingerprint, version.key, version.added_rows_ref)
+            if version.group_id != bound:
+                raise IntegrityError("a root version's group id must derive from its first block")
             return
-        parent = self._cache[version.parent_ref]
-        if (parent.total_rank + version.added_rank != version.total_rank or parent.channels != version.channels
-                or parent.key != version.key or parent.group_id != version.group_id
-                or parent.depth + 1 != version.depth or parent.model_fingerprint != version.model_fingerprint):
-            raise IntegrityError("basis extension is inconsistent with its parent version")
+        parent = self._versions[version.parent_ref]
+        consistent = (parent.total_rank + version.added_rank == version.total_rank
+                      and (parent.channels, parent.key, parent.group_id, parent.model_fingerprint)
+                      == (version.channels, version.key, version.group_id, version.model_fingerprint)
+                      and parent.depth + 1 == version.depth)
+        if not consistent:
+            raise IntegrityError("an extension disagrees with its parent version")
+
+    def load(self, ref: str) -> BasisVersion:
+        """A validated version (its whole parent chain validated first, iteratively; cached)."""
+        object_ref(ref, "basis version")
+        pending = []
+        cursor: str | None = ref
+        while cursor is not None and cursor not in self._versions:
+            version = self._decode(cursor)
+            pending.append((cursor, version))
+            cursor = version.parent_ref
+        for current, version in reversed(pending):   # root side first: every parent is known
+            self._check_link(version)
+            self._versions[current] = version
+        return self._versions[ref]
+
+    def load_many(self, refs: Iterable[str]) -> list[BasisVersion]:
+        return [self.load(ref) for ref in list(refs)]
 
     def chain(self, ref: str) -> list[tuple[str, BasisVersion]]:
-        """Versions from the group root to ``ref`` (inclusive)."""
-        result = []
-        current: str | None = ref
-        while current is not None:
-            version = self.load(current)
-            result.append((current, version))
-            current = version.parent_ref
-        return result[::-1]
+        """``(ref, version)`` from the group's root to ``ref``."""
+        out = []
+        cursor: str | None = ref
+        while cursor is not None:
+            version = self.load(cursor)
+            out.append((cursor, version))
+            cursor = version.parent_ref
+        out.reverse()
+        return out
 
-    def _blocks(self, ref: str) -> list[tuple[str, int]]:
-        return [(v.added_rows_ref, v.added_rank) for _, v in self.chain(ref)]
+    def _links(self, ref: str) -> list[_Link]:
+        return [_Link(r, v.added_rows_ref, v.added_rank) for r, v in self.chain(ref)]
 
     def blocks(self, ref: str) -> tuple[str, ...]:
-        return tuple(block for block, _ in self._blocks(ref))
+        return tuple(link.block for link in self._links(ref))
 
     def prefetch_blocks(self, requests: Iterable[tuple[str, int]], block_cache: dict[str, bytes]) -> int:
-        """Read (hash-checked, in parallel) every block the ``(version_ref, rows)`` prefixes need."""
-        needed = []
+        """Read every block the ``(version ref, rows)`` prefixes need into ``block_cache`` (parallel reads,
+        hash-checked); returns the number of blocks read."""
+        wanted: dict[str, None] = {}
         for ref, rows in requests:
-            remaining = rows
-            for block, count in self._blocks(ref):
-                if remaining <= 0:
+            covered = 0
+            for link in self._links(ref):
+                if covered >= rows:
                     break
-                if block not in block_cache:
-                    needed.append(block)
-                remaining -= count
-        needed = list(dict.fromkeys(needed))
-        block_cache.update(self.store.get_many(needed, verify=True))
-        return len(needed)
+                if link.block not in block_cache:
+                    wanted[link.block] = None
+                covered += link.rows
+        block_cache.update(self.store.get_many(list(wanted), verify=True))
+        return len(wanted)
 
-    def _prefix(self, ref, rows, max_bytes, block_cache):
+    def _prefix_parts(self, ref, rows, max_bytes, block_cache):
+        """The blocks (and byte counts) of the first ``rows`` rows of ``ref``'s view, each block checked
+        against its content address (or by the store), and the full view against the version digest."""
         version = self.load(ref)
         rows = version.total_rank if rows is None else rows
-        if type(rows) is not int or not 1 <= rows <= version.total_rank:
-            raise ConfigurationError("a basis view must be a nonempty legal prefix of its version")
-        nbytes = rows * version.channels * 2
-        if max_bytes is not None and nbytes > max_bytes:
-            raise CapacityError(f"basis view needs {nbytes} bytes; workspace bound is {max_bytes}")
-        parts, remaining = [], rows
-        verified = self.store.verify_reads
-        digest = hashlib.sha256() if rows == version.total_rank and not verified else None
-        for block, count in self._blocks(ref):
-            if remaining <= 0:
+        if type(rows) is not int or rows < 1 or rows > version.total_rank:
+            raise ConfigurationError(f"a view of {ref} takes 1..{version.total_rank} rows, not {rows!r}")
+        row_bytes = 2 * version.channels
+        if max_bytes is not None and rows * row_bytes > max_bytes:
+            raise CapacityError(f"the view needs {rows * row_bytes} bytes, above the {max_bytes}-byte bound")
+        trusted = self.store.verify_reads
+        whole = hashlib.sha256() if rows == version.total_rank and not trusted else None
+        parts = []
+        left = rows
+        for link in self._links(ref):
+            if left == 0:
                 break
-            data = None if block_cache is None else block_cache.get(block)
+            data = block_cache.get(link.block) if block_cache is not None else None
             if data is None:
-                data = self.store.get(block)
-                if not verified and hashlib.sha256(data).hexdigest() != block.split(":", 1)[1]:
-                    raise IntegrityError("basis row block bytes differ from their content address")
+                data = self.store.get(link.block)
+                if not trusted and hashlib.sha256(data).hexdigest() != link.block.partition(":")[2]:
+                    raise IntegrityError(f"block {link.block} does not hash to its address")
                 if block_cache is not None:
-                    block_cache[block] = data
-            take = min(count, remaining)
-            size = take * version.channels * 2
+                    block_cache[link.block] = data
+            take = min(link.rows, left)
+            size = take * row_bytes
             if len(data) < size:
-                raise IntegrityError("basis row block length disagrees with its declared geometry")
-            if digest is not None:
-                digest.update(memoryview(data)[:size])
-            parts.append((block, data, size))
-            remaining -= take
-        if digest is not None and digest.hexdigest() != version.view_sha256:
-            raise IntegrityError("assembled basis view differs from its version digest")
+                raise IntegrityError(f"block {link.block} is shorter than its rows")
+            if whole is not None:
+                whole.update(memoryview(data)[:size])
+            parts.append((link.block, data, size))
+            left -= take
+        if whole is not None and whole.hexdigest() != version.view_sha256:
+            raise IntegrityError(f"the assembled view of {ref} differs from its recorded digest")
         return version, rows, parts
 
     def assemble(self, ref: str, rows: int | None = None, *, max_bytes: int | None = None,
                  block_cache: dict[str, bytes] | None = None) -> torch.Tensor:
-        """Contiguous FP16 prefix view ``[rows, channels]`` from the version's ordered blocks."""
-        version, rows, parts = self._prefix(ref, rows, max_bytes, block_cache)
-        view = np.empty(rows * version.channels * 2, dtype=np.uint8)
-        position = 0
+        """FP16 ``[rows, channels]`` prefix view (default: the whole version), contiguous."""
+        version, rows, parts = self._prefix_parts(ref, rows, max_bytes, block_cache)
+        out = np.empty(rows * version.channels, dtype=np.float16)
+        raw = out.view(np.uint8)
+        at = 0
         for _, data, size in parts:
-            view[position:position + size] = np.frombuffer(data, dtype=np.uint8, count=size)
-            position += size
-        return torch.from_numpy(view.view(np.float16).reshape(rows, version.channels))
+            raw[at:at + size] = np.frombuffer(data, dtype=np.uint8, count=size)
+            at += size
+        return torch.from_numpy(out.reshape(rows, version.channels))
 
     def view_bytes(self, ref: str, rows: int, *, max_bytes: int | None = None,
                    block_cache: dict[str, bytes] | None = None) -> bytes:
-        _, _, parts = self._prefix(ref, rows, max_bytes, block_cache)
-        chunks = []
+        """The prefix view's bytes (every block checked to be finite once)."""
+        _, _, parts = self._prefix_parts(ref, rows, max_bytes, block_cache)
+        out = []
         for block, data, size in parts:
-            chunk = memoryview(data)[:size]
-            if block not in self._finite_blocks:
+            piece = memoryview(data)[:size]
+            if block not in self._finite:
                 if finite_fp16(data):
-                    self._finite_blocks.add(block)
-                elif not finite_fp16(chunk):
-                    raise ConfigurationError("basis row blocks must be finite")
-            chunks.append(chunk)
-        return b"".join(chunks)
+                    self._finite.add(block)
+                elif not finite_fp16(piece):
+                    raise ConfigurationError(f"block {block} holds an infinity or a NaN")
+            out.append(piece)
+        return b"".join(out)
 
     def unique_block_bytes(self, refs: Iterable[str]) -> dict[str, int]:
-        result: dict[str, int] = {}
+        """Bytes of every distinct block the versions ``refs`` reach (storage accounting)."""
+        sizes: dict[str, int] = {}
         for ref in refs:
-            if ref is None:
-                continue
-            for _, version in self.chain(ref):
-                result.setdefault(version.added_rows_ref, version.added_bytes)
-        return result
+            if ref is not None:
+                for _, version in self.chain(ref):
+                    sizes.setdefault(version.added_rows_ref, version.added_bytes)
+        return sizes
+
+
+def _descriptor(metadata) -> Mapping[str, Any] | None:
+    value = metadata.get("basis") if isinstance(metadata, Mapping) else None
+    return value if isinstance(value, Mapping) else None
 
 
 def detach_basis(encoded: EncodedTensor):
-    """``(metadata, payloads, metrics)`` of a lossy packet without its basis bytes (the descriptor stays)."""
+    """``(metadata, payloads, metrics)`` of a lossy packet without its basis bytes; the descriptor stays."""
     if not isinstance(encoded, EncodedTensor) or encoded.basis is None:
-        raise ConfigurationError("only lossy single-matrix packets carry a detachable basis")
-    descriptor = encoded.metadata.get("basis") if isinstance(encoded.metadata, Mapping) else None
-    if not isinstance(descriptor, Mapping) or hashlib.sha256(encoded.basis).hexdigest() != descriptor.get("sha256"):
-        raise IntegrityError("packet basis bytes disagree with their descriptor")
-    return (json_copy(encoded.metadata), dict(encoded.payloads),
-            None if encoded.metrics is None else json_copy(encoded.metrics))
+        raise ConfigurationError("only a lossy single-matrix packet carries a basis to detach")
+    descriptor = _descriptor(encoded.metadata)
+    if descriptor is None or descriptor.get("sha256") != hashlib.sha256(encoded.basis).hexdigest():
+        raise IntegrityError("the packet's basis bytes do not match its descriptor")
+    metrics = None if encoded.metrics is None else json_copy(encoded.metrics)
+    return json_copy(encoded.metadata), dict(encoded.payloads), metrics
 
 
 def attach_basis(metadata: Mapping[str, Any], payloads: Mapping[str, bytes], basis: bytes, *, rank_view: int,
                  channels: int, check_digest: bool = True) -> EncodedTensor:
-    """Re-attach an assembled prefix view after checking it against the packet's basis descriptor."""
-    descriptor = metadata.get("basis") if isinstance(metadata, Mapping) else None
-    if (not isinstance(descriptor, Mapping) or descriptor.get("shape") != [rank_view, channels]
-            or descriptor.get("view_rank") != rank_view or descriptor.get("dtype") != "float16"
-            or descriptor.get("bytes") != len(basis)
-            or (check_digest and hashlib.sha256(basis).hexdigest() != descriptor.get("sha256"))):
-        raise IntegrityError("assembled basis view differs from the packet's bound prefix")
+    """The packet with an assembled prefix view attached, once the view matches the bound descriptor."""
+    descriptor = _descriptor(metadata)
+    expected = {"shape": [rank_view, channels], "view_rank": rank_view, "dtype": "float16", "bytes": len(basis)}
+    if descriptor is None or any(descriptor.get(name) != value for name, value in expected.items()):
+        raise IntegrityError("the assembled view's geometry differs from the packet's basis descriptor")
+    if check_digest and descriptor.get("sha256") != hashlib.sha256(basis).hexdigest():
+        raise IntegrityError("the assembled view's digest differs from the packet's basis descriptor")
     return EncodedTensor(metadata, payloads, basis=basis)
+
+
+__all__ = ["MANIFEST_TYPE", "BasisVersionStore", "attach_basis", "detach_basis", "finite_fp16", "rows_from_bytes",
+           "rows_to_bytes"]

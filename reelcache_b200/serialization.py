@@ -1,13 +1,19 @@
-"""Canonical JSON and the non-pickle tensor container (reference: reelcache/serialization.py).
+"""Canonical JSON and the pickle-free tensor-state container.
 
-Container bytes (identical to the reference's, :18 and :162-184)::
+Byte layout of a container (shared with the reference implementation so that either can read the other's
+execution-state blobs; reference reelcache/serialization.py:18,162-184)::
 
-    b"REELCACHE_TENSORS\\x00\\x01" + <u64 little-endian header length> + canonical JSON header
-    {"version": 1, "byteorder": "little", "tensors": {name: {dtype, shape, offset, nbytes, sha256}}}
-    + raw little-endian payloads in sorted-name order
+    MAGIC = b"REELCACHE_TENSORS\\x00\\x01"
+    MAGIC | u64 little-endian header size | header (canonical JSON) | payloads
 
-Stored JSON is parsed strictly: UTF-8, unique keys, finite numbers only; any violation is an
-:class:`~reelcache_b200.errors.IntegrityError`. Nothing here ever unpickles.
+    header = {"version": 1, "byteorder": "little",
+              "tensors": {name: {"dtype", "shape", "offset", "nbytes", "sha256"}}}
+
+Payloads are the tensors' raw little-endian bytes, packed back to back in ascending name order; each
+entry's ``offset`` is relative to the first payload byte. Reading is strict: the JSON must be UTF-8 with
+unique keys and finite numbers, every entry must sit exactly where the previous one ended, its digest must
+match, and no byte may be left over. Any violation raises :class:`~reelcache_b200.errors.IntegrityError`.
+Nothing in this module unpickles.
 """
 
 from __future__ import annotations
@@ -25,164 +31,217 @@ from .errors import CapacityError, ConfigurationError, IntegrityError, Unsupport
 from .types import json_copy
 
 MAGIC = b"REELCACHE_TENSORS\x00\x01"
-_MAX_HEADER_BYTES = 16 * 1024 * 1024
-_DTYPES = {name: getattr(torch, name) for name in (
-    "bool", "uint8", "int8", "int16", "int32", "int64", "float16", "bfloat16", "float32", "float64",
-    "complex64", "complex128", "uint16", "uint32", "uint64") if hasattr(torch, name)}
+FORMAT_VERSION = 1
+HEADER_LIMIT = 16 << 20
+_LENGTH = struct.Struct("<Q")
+_ENTRY_FIELDS = frozenset({"dtype", "shape", "offset", "nbytes", "sha256"})
 
+# dtype name in the header -> torch dtype (names without the "torch." prefix)
+_DTYPE_TABLE: dict[str, torch.dtype] = {}
+for _name in ("bool", "uint8", "uint16", "uint32", "uint64", "int8", "int16", "int32", "int64", "float16",
+              "bfloat16", "float32", "float64", "complex64", "complex128"):
+    if hasattr(torch, _name):
+        _DTYPE_TABLE[_name] = getattr(torch, _name)
+
+
+def _require_little_endian() -> None:
+    if sys.byteorder != "little":
+        raise UnsupportedError("tensor containers are little-endian; this host is not")
+
+
+# ------------------------------------------------------------------------------------------------- JSON
 
 def canonical_json(value: Any) -> bytes:
-    """Sorted keys, ``,``/``:`` separators, UTF-8 (non-ASCII kept), no NaN."""
-    return json.dumps(json_copy(value), sort_keys=True, separators=(",", ":"), ensure_ascii=False,
-                      allow_nan=False).encode("utf-8")
+    """UTF-8 JSON with sorted keys, no whitespace, non-ASCII kept and NaN/infinity refused."""
+    text = json.dumps(json_copy(value), sort_keys=True, separators=(",", ":"), ensure_ascii=False,
+                      allow_nan=False)
+    return text.encode("utf-8")
 
 
-def _no_duplicates(pairs):
-    result = dict(pairs)
-    if len(result) != len(pairs):
-        raise IntegrityError("duplicate JSON key")
-    return result
+class _StrictDecoder:
+    """Hooks for :func:`json.loads` that turn the lenient corners of JSON into errors."""
 
+    @staticmethod
+    def pairs(items):
+        keys = [key for key, _ in items]
+        if len(set(keys)) != len(keys):
+            raise IntegrityError("stored JSON repeats a key")
+        return dict(items)
 
-def _finite(text: str) -> float:
-    value = float(text)
-    if not math.isfinite(value):
-        raise ValueError("non-finite JSON number")
-    return value
+    @staticmethod
+    def number(text: str) -> float:
+        value = float(text)
+        if math.isinf(value) or math.isnan(value):
+            raise ValueError(f"stored JSON holds a non-finite number: {text}")
+        return value
 
-
-def _constant(name: str):
-    raise ValueError(f"non-finite JSON constant: {name}")
+    @staticmethod
+    def constant(name: str):
+        raise ValueError(f"stored JSON holds the constant {name}")
 
 
 def parse_json(data: bytes) -> Any:
+    """Parse stored JSON strictly (see the module docstring)."""
     try:
-        return json.loads(data.decode("utf-8"), object_pairs_hook=_no_duplicates, parse_float=_finite,
-                          parse_constant=_constant)
+        text = data.decode("utf-8")
+        return json.loads(text, object_pairs_hook=_StrictDecoder.pairs, parse_float=_StrictDecoder.number,
+                          parse_constant=_StrictDecoder.constant)
     except IntegrityError:
         raise
     except (ValueError, UnicodeError, TypeError, RecursionError) as exc:
-        raise IntegrityError("invalid JSON metadata") from exc
+        raise IntegrityError(f"stored JSON is malformed: {exc}") from exc
 
+
+# ----------------------------------------------------------------------------------------------- dtypes
 
 def resolve_dtype(dtype: str | torch.dtype) -> torch.dtype:
-    name = str(dtype).removeprefix("torch.")
-    if name not in _DTYPES:
-        raise UnsupportedError(f"unsupported tensor state dtype: {dtype!r}")
-    return _DTYPES[name]
+    label = str(dtype)
+    if label.startswith("torch."):
+        label = label[len("torch."):]
+    found = _DTYPE_TABLE.get(label)
+    if found is None:
+        raise UnsupportedError(f"tensor containers do not hold dtype {dtype!r}")
+    return found
 
 
 def dtype_name(dtype: str | torch.dtype) -> str:
-    return str(resolve_dtype(dtype)).removeprefix("torch.")
+    return str(resolve_dtype(dtype))[len("torch."):]
+
+
+def _itemsize(dtype: torch.dtype) -> int:
+    return torch.empty((), dtype=dtype).element_size()
 
 
 def tensor_nbytes(shape: Sequence[int], dtype: str | torch.dtype) -> int:
-    if not isinstance(shape, (list, tuple)) or len(shape) > 64:
-        raise ConfigurationError("tensor shape must have at most 64 dimensions")
-    if any(type(size) is not int or not 0 <= size <= sys.maxsize for size in shape):
-        raise ConfigurationError("tensor dimensions must be representable nonnegative integers")
-    size = math.prod(shape) * torch.empty((), dtype=resolve_dtype(dtype)).element_size()
-    if size > sys.maxsize:
-        raise ConfigurationError("tensor storage exceeds the host address space")
-    return size
+    """Storage bytes of a dense tensor of ``shape`` and ``dtype`` (validated)."""
+    if not isinstance(shape, (list, tuple)):
+        raise ConfigurationError("a tensor shape is a list of dimensions")
+    if len(shape) > 64:
+        raise ConfigurationError("tensor shapes have at most 64 dimensions")
+    count = 1
+    for size in shape:
+        if type(size) is not int or size < 0 or size > sys.maxsize:
+            raise ConfigurationError(f"tensor dimension {size!r} is not a nonnegative machine integer")
+        count *= size
+    total = count * _itemsize(resolve_dtype(dtype))
+    if total > sys.maxsize:
+        raise ConfigurationError("the tensor is larger than the host address space")
+    return total
 
+
+# ---------------------------------------------------------------------------------------------- tensors
 
 def tensor_bytes(tensor: torch.Tensor) -> bytes:
+    """The raw little-endian bytes of a dense tensor (copied to the host, contiguous)."""
     if not isinstance(tensor, torch.Tensor):
-        raise ConfigurationError("tensor state values must be torch.Tensor instances")
+        raise ConfigurationError("tensor state holds torch.Tensor values only")
     resolve_dtype(tensor.dtype)
-    if tensor.layout != torch.strided or tensor.is_quantized or tensor.device.type == "meta":
-        raise UnsupportedError("only materialized dense strided tensors can be serialized")
-    if sys.byteorder != "little":
-        raise UnsupportedError("tensor state requires a little-endian host")
-    value = tensor.detach().resolve_conj().resolve_neg().to("cpu").contiguous()
-    return value.reshape(-1).view(torch.uint8).numpy().tobytes()
+    dense = tensor.layout == torch.strided and not tensor.is_quantized and tensor.device.type != "meta"
+    if not dense:
+        raise UnsupportedError("only materialized dense (strided) tensors are serializable")
+    _require_little_endian()
+    host = tensor.detach().resolve_conj().resolve_neg().to("cpu").contiguous()
+    return host.reshape(-1).view(torch.uint8).numpy().tobytes()
 
 
 def tensor_from_bytes(data: bytes, *, dtype, shape: Sequence[int], device: Any = "cpu") -> torch.Tensor:
-    if sys.byteorder != "little":
-        raise UnsupportedError("tensor state requires a little-endian host")
+    """Rebuild a tensor from its raw bytes (validated against ``dtype`` and ``shape``)."""
+    _require_little_endian()
     if not isinstance(data, bytes):
-        raise IntegrityError("tensor payload must be immutable bytes")
+        raise IntegrityError("a tensor payload is an immutable bytes object")
     try:
-        resolved = resolve_dtype(dtype)
-        expected = tensor_nbytes(shape, resolved)
+        kind = resolve_dtype(dtype)
+        size = tensor_nbytes(shape, kind)
     except (ConfigurationError, UnsupportedError) as exc:
-        raise IntegrityError("invalid serialized tensor geometry or dtype") from exc
-    if len(data) != expected:
-        raise IntegrityError(f"tensor byte length mismatch: expected {expected}, got {len(data)}")
+        raise IntegrityError(f"stored tensor geometry is invalid: {exc}") from exc
+    if len(data) != size:
+        raise IntegrityError(f"stored tensor holds {len(data)} bytes, its geometry needs {size}")
     try:
-        value = (torch.empty(tuple(shape), dtype=resolved) if expected == 0
-                 else torch.frombuffer(bytearray(data), dtype=resolved).reshape(tuple(shape)))
+        if size == 0:
+            value = torch.empty(tuple(shape), dtype=kind)
+        else:
+            value = torch.frombuffer(bytearray(data), dtype=kind).reshape(tuple(shape))
     except (RuntimeError, TypeError, ValueError, OverflowError) as exc:
-        raise IntegrityError("serialized tensor shape cannot be materialized") from exc
+        raise IntegrityError(f"stored tensor cannot take its shape: {exc}") from exc
     try:
         return value.to(device=device)
     except (RuntimeError, TypeError, ValueError) as exc:
-        raise ConfigurationError(f"cannot restore tensor on device {device!r}") from exc
+        raise ConfigurationError(f"device {device!r} cannot hold the restored tensor") from exc
 
+
+# -------------------------------------------------------------------------------------------- container
 
 def serialize_tensors(tensors: Mapping[str, torch.Tensor]) -> bytes:
+    """Pack named tensors into one container (layout in the module docstring)."""
     if not isinstance(tensors, Mapping):
-        raise ConfigurationError("named tensor state must be a mapping")
-    if any(not isinstance(name, str) or not name for name in tensors):
-        raise ConfigurationError("tensor state names must be nonempty strings")
-    entries: dict[str, Any] = {}
-    payloads: list[bytes] = []
-    offset = 0
+        raise ConfigurationError("tensor state is a mapping of names to tensors")
+    for name in tensors:
+        if not isinstance(name, str) or name == "":
+            raise ConfigurationError(f"tensor state names are nonempty strings, not {name!r}")
+    table: dict[str, dict[str, Any]] = {}
+    body = bytearray()
     for name in sorted(tensors):
-        tensor = tensors[name]
-        payload = tensor_bytes(tensor)
-        entries[name] = {"dtype": dtype_name(tensor.dtype), "shape": list(tensor.shape), "offset": offset,
-                         "nbytes": len(payload), "sha256": hashlib.sha256(payload).hexdigest()}
-        payloads.append(payload)
-        offset += len(payload)
-    header = canonical_json({"version": 1, "byteorder": "little", "tensors": entries})
-    if len(header) > _MAX_HEADER_BYTES:
-        raise CapacityError("tensor state header exceeds the format limit")
-    return MAGIC + struct.pack("<Q", len(header)) + header + b"".join(payloads)
+        value = tensors[name]
+        raw = tensor_bytes(value)
+        table[name] = {"dtype": dtype_name(value.dtype), "shape": list(value.shape), "offset": len(body),
+                       "nbytes": len(raw), "sha256": hashlib.sha256(raw).hexdigest()}
+        body += raw
+    header = canonical_json({"version": FORMAT_VERSION, "byteorder": "little", "tensors": table})
+    if len(header) > HEADER_LIMIT:
+        raise CapacityError(f"a tensor state header is limited to {HEADER_LIMIT} bytes")
+    return b"".join((MAGIC, _LENGTH.pack(len(header)), header, bytes(body)))
+
+
+def _read_header(data: bytes) -> tuple[dict, memoryview]:
+    if not isinstance(data, bytes) or data[:len(MAGIC)] != MAGIC:
+        raise IntegrityError("the blob is not a tensor-state container")
+    start = len(MAGIC) + _LENGTH.size
+    if len(data) < start:
+        raise IntegrityError("the container ends inside its header length")
+    (size,) = _LENGTH.unpack_from(data, len(MAGIC))
+    if size > HEADER_LIMIT or start + size > len(data):
+        raise IntegrityError(f"the container declares an impossible header of {size} bytes")
+    header = parse_json(data[start:start + size])
+    valid = (isinstance(header, dict) and set(header) == {"version", "byteorder", "tensors"}
+             and type(header["version"]) is int and header["version"] == FORMAT_VERSION
+             and header["byteorder"] == "little" and isinstance(header["tensors"], dict))
+    if not valid:
+        raise IntegrityError("the container header has an unknown version or layout")
+    return header, memoryview(data)[start + size:]
 
 
 def deserialize_tensors(data: bytes, *, device: Any = "cpu", max_bytes: int | None = None) -> dict[str, torch.Tensor]:
-    if not isinstance(data, bytes) or not data.startswith(MAGIC):
-        raise IntegrityError("not a ReelCache non-pickle tensor state")
-    prefix = len(MAGIC) + 8
-    if len(data) < prefix:
-        raise IntegrityError("truncated tensor state header")
-    header_size = struct.unpack("<Q", data[len(MAGIC):prefix])[0]
-    if header_size > _MAX_HEADER_BYTES or header_size > len(data) - prefix:
-        raise IntegrityError("invalid tensor state header length")
-    header = parse_json(data[prefix:prefix + header_size])
-    if (not isinstance(header, dict) or set(header) != {"version", "byteorder", "tensors"}
-            or type(header["version"]) is not int or header["version"] != 1 or header["byteorder"] != "little"
-            or not isinstance(header["tensors"], dict)):
-        raise IntegrityError("unsupported tensor state format")
-    body = memoryview(data)[prefix + header_size:]
+    """Unpack a container; every entry is checked (position, size, digest) before any tensor is built."""
+    header, body = _read_header(data)
     if max_bytes is not None:
         if type(max_bytes) is not int or max_bytes < 0:
-            raise ConfigurationError("max_bytes must be nonnegative")
+            raise ConfigurationError("max_bytes is a nonnegative integer")
         if len(body) > max_bytes:
-            raise CapacityError("serialized tensor state exceeds the restoration budget")
-    offset = 0
-    checked = []
+            raise CapacityError(f"the container's {len(body)} payload bytes exceed the budget of {max_bytes}")
+    verified = []
+    position = 0
     for name in sorted(header["tensors"]):
-        desc = header["tensors"][name]
-        if (not name or not isinstance(desc, dict) or set(desc) != {"dtype", "shape", "offset", "nbytes", "sha256"}
-                or type(desc["offset"]) is not int or desc["offset"] != offset
-                or type(desc["nbytes"]) is not int or desc["nbytes"] < 0):
-            raise IntegrityError("invalid tensor state entry or noncontiguous offsets")
+        entry = header["tensors"][name]
+        if not name or not isinstance(entry, dict) or set(entry) != _ENTRY_FIELDS:
+            raise IntegrityError(f"container entry {name!r} is malformed")
+        if type(entry["offset"]) is not int or entry["offset"] != position:
+            raise IntegrityError(f"container entry {name!r} does not start where the previous one ended")
         try:
-            expected = tensor_nbytes(desc["shape"], desc["dtype"])
+            size = tensor_nbytes(entry["shape"], entry["dtype"])
         except (ConfigurationError, UnsupportedError) as exc:
-            raise IntegrityError("invalid tensor state dtype or shape") from exc
-        if expected != desc["nbytes"] or offset + expected > len(body):
-            raise IntegrityError("tensor state shape or length mismatch")
-        payload = bytes(body[offset:offset + expected])
-        if hashlib.sha256(payload).hexdigest() != desc["sha256"]:
-            raise IntegrityError(f"corrupt tensor state: {name}")
-        checked.append((name, desc, payload))
-        offset += expected
-    if offset != len(body):
-        raise IntegrityError("tensor state has unclaimed trailing bytes")
-    return {name: tensor_from_bytes(payload, dtype=desc["dtype"], shape=desc["shape"], device=device)
-            for name, desc, payload in checked}
+            raise IntegrityError(f"container entry {name!r} has an invalid geometry: {exc}") from exc
+        if type(entry["nbytes"]) is not int or entry["nbytes"] != size or position + size > len(body):
+            raise IntegrityError(f"container entry {name!r} disagrees with its geometry or the container size")
+        raw = bytes(body[position:position + size])
+        if hashlib.sha256(raw).hexdigest() != entry["sha256"]:
+            raise IntegrityError(f"container entry {name!r} fails its digest")
+        verified.append((name, entry, raw))
+        position += size
+    if position != len(body):
+        raise IntegrityError(f"the container has {len(body) - position} bytes no entry claims")
+    return {name: tensor_from_bytes(raw, dtype=entry["dtype"], shape=entry["shape"], device=device)
+            for name, entry, raw in verified}
+
+
+__all__ = ["FORMAT_VERSION", "MAGIC", "canonical_json", "deserialize_tensors", "dtype_name", "parse_json",
+           "resolve_dtype", "serialize_tensors", "tensor_bytes", "tensor_from_bytes", "tensor_nbytes"]
