@@ -1,21 +1,18 @@
-"""Transport and failure agreement for storage collectives (the counterpart of reference
-reelcache/distributed.py:26-412; protocol kept: checkpoint records ``{sequence, operation, rank,
-error, cancelled, details}`` gathered from every rank before any payload moves).
+"""Storage collectives with failure agreement (the behaviour of reference reelcache/distributed.py: a control
+round in which every rank reports before any payload moves).
 
-The framework never creates process groups: a :class:`DistributedOwner` runs on groups the engine
-made. Control messages (bounded canonical JSON, at most 1 MiB, no pickle) travel on a ``control``
-group (Gloo, CPU); payloads on a ``data`` group (NCCL on CUDA -- NVLink / NVSwitch on one node -- or
-Gloo on CPU) in bounded point-to-point pieces (``max_wire_bytes``).
+The framework never creates the process groups itself; a :class:`DistributedOwner` runs on groups the engine
+made. Two channels:
 
-* ``checkpoint(op, error=...)``: every rank reports; a local failure or cancellation on any rank is
-  raised on *every* rank (:class:`PeerFailure`, :class:`CollectiveCancelled`) before the next payload
-  collective, so no rank is left blocked in a transfer its peer will never join. Ranks that disagree on
-  the collective order fail the same way.
-* ``gather_matrix``: a ``rows`` or ``heads`` shard of a matrix from every rank -> canonical
-  ``[tokens, channels]`` on the storage owner.
-* ``acquire_columns`` / ``local_columns``: the owner decodes one rank's head columns at a time and
-  sends them; each rank receives only its own columns.
-* ``transfer_tensor``, ``broadcast_json``, ``owner_call``.
+* **control** (a Gloo group, CPU): bounded canonical JSON (at most 1 MiB per message, never pickled), gathered
+  from every rank by :class:`_ControlChannel` (a length round, then a padded byte round);
+* **payload** (the data group: NCCL with CUDA tensors -- NVLink / NVSwitch on one node -- or Gloo with CPU
+  tensors): point-to-point moves in pieces of at most ``max_wire_bytes``.
+
+``checkpoint(operation, error=..., cancelled=...)`` is the agreement: every rank contributes one record
+``{sequence, operation, rank, error, cancelled, details}``; if any rank failed or cancelled, or the ranks are
+not at the same step, every rank raises (:class:`PeerFailure`, :class:`CollectiveCancelled`) before the next
+payload collective -- so no rank is ever left waiting in a transfer a peer will not join.
 """
 
 from __future__ import annotations
@@ -32,19 +29,21 @@ from ..errors import ConfigurationError, StateError
 from ..telemetry import span
 
 MAX_CONTROL_BYTES = 1 << 20
+MAX_DETAIL_BYTES = MAX_CONTROL_BYTES // 2
 
 
 class PeerFailure(StateError):
-    """A rank failed (or the transport did); raised on every rank of the collective."""
+    """Some rank of the collective failed (or the transport did); raised on every rank."""
 
 
 class CollectiveCancelled(PeerFailure):
-    """A rank cancelled the collective."""
+    """Some rank cancelled the collective; raised on every rank."""
 
 
 @dataclass(frozen=True)
 class KVLayout:
-    """Ulysses geometry of one matrix: ``rows`` shards split tokens, ``heads`` shards split KV heads."""
+    """How one ``[tokens, kv_heads * head_dim]`` matrix is split over ranks: ``rows`` shards take contiguous
+    token ranges (earlier ranks one extra token when uneven), ``heads`` shards take equal head groups."""
 
     tokens: int
     kv_heads: int
@@ -52,12 +51,14 @@ class KVLayout:
     world_size: int = 2
 
     def __post_init__(self):
-        if any(type(v) is not int or v <= 0 for v in (self.tokens, self.kv_heads, self.head_dim, self.world_size)):
-            raise ConfigurationError("KV layout dimensions must be positive integers")
+        for name in ("tokens", "kv_heads", "head_dim", "world_size"):
+            value = getattr(self, name)
+            if type(value) is not int or value < 1:
+                raise ConfigurationError(f"KV layout {name} must be a positive integer, got {value!r}")
         if self.kv_heads % self.world_size:
-            raise ConfigurationError("KV heads must divide evenly across ranks")
+            raise ConfigurationError(f"{self.kv_heads} KV heads do not split evenly over {self.world_size} ranks")
         if self.tokens < self.world_size:
-            raise ConfigurationError("every row owner needs at least one token")
+            raise ConfigurationError(f"{self.tokens} tokens cannot give each of {self.world_size} ranks a row")
 
     @property
     def channels(self) -> int:
@@ -65,34 +66,36 @@ class KVLayout:
 
     @property
     def local_channels(self) -> int:
-        return self.kv_heads // self.world_size * self.head_dim
+        return self.channels // self.world_size
 
-    def _rank(self, rank: int) -> None:
+    def _valid(self, rank: int) -> int:
         if type(rank) is not int or not 0 <= rank < self.world_size:
-            raise ConfigurationError("rank is outside the KV layout")
+            raise ConfigurationError(f"rank {rank!r} is not in this {self.world_size}-rank layout")
+        return rank
 
     def rows(self, rank: int) -> slice:
-        self._rank(rank)
-        count, extra = divmod(self.tokens, self.world_size)
-        start = rank * count + min(rank, extra)
-        return slice(start, start + count + int(rank < extra))
+        base, extra = divmod(self.tokens, self.world_size)
+        first = self._valid(rank) * base + min(rank, extra)
+        return slice(first, first + base + (1 if rank < extra else 0))
 
     def columns(self, rank: int) -> slice:
-        self._rank(rank)
-        return slice(rank * self.local_channels, (rank + 1) * self.local_channels)
+        width = self.local_channels
+        return slice(self._valid(rank) * width, (rank + 1) * width)
 
     def shape(self, rank: int, layout: str) -> tuple[int, int]:
         if layout == "rows":
-            rows = self.rows(rank)
-            return (rows.stop - rows.start, self.channels)
+            span_ = self.rows(rank)
+            return span_.stop - span_.start, self.channels
         if layout == "heads":
-            self._rank(rank)
-            return (self.tokens, self.local_channels)
-        raise ConfigurationError("layout must be 'rows' or 'heads'")
+            self._valid(rank)
+            return self.tokens, self.local_channels
+        raise ConfigurationError(f"layout {layout!r} is neither 'rows' nor 'heads'")
 
 
 @dataclass
 class WireCounters:
+    """Application bytes and messages moved by one transport (protocol overheads excluded)."""
+
     payload_sent_bytes: int = 0
     payload_received_bytes: int = 0
     control_sent_bytes: int = 0
@@ -106,119 +109,142 @@ class WireCounters:
                 "transport_protocol_overhead_included": False}
 
 
+class _ControlChannel:
+    """Gathers one bounded JSON value from every rank over the control group."""
+
+    def __init__(self, owner: "DistributedOwner"):
+        self.owner = owner
+
+    def gather(self, value: Any) -> list:
+        o = self.owner
+        encoded = json.dumps(value, sort_keys=True, separators=(",", ":"), allow_nan=False).encode()
+        if len(encoded) > MAX_CONTROL_BYTES:
+            raise ConfigurationError(f"a control message of {len(encoded)} bytes exceeds {MAX_CONTROL_BYTES}")
+        if o.world_size == 1:
+            return [json.loads(encoded)]
+        mine = torch.tensor([len(encoded)], dtype=torch.int64)
+        sizes = [torch.empty_like(mine) for _ in range(o.world_size)]
+        o._run(o.dist.all_gather, sizes, mine, group=o.control_group)
+        lengths = [int(s.item()) for s in sizes]
+        width = max(lengths)
+        if min(lengths) < 0 or width > MAX_CONTROL_BYTES:
+            o._broken = True
+            raise PeerFailure(f"a peer announced a control message of {width} bytes")
+        padded = torch.zeros(width, dtype=torch.uint8)
+        padded[:len(encoded)] = torch.frombuffer(bytearray(encoded), dtype=torch.uint8)
+        received = [torch.empty_like(padded) for _ in range(o.world_size)]
+        o._run(o.dist.all_gather, received, padded, group=o.control_group)
+        moved = (8 + width) * (o.world_size - 1)
+        o.counters.control_sent_bytes += moved
+        o.counters.control_received_bytes += moved
+        return [json.loads(bytes(buf[:n].tolist())) for buf, n in zip(received, lengths)]
+
+
+def _describe(error) -> str | None:
+    if error is None:
+        return None
+    return f"{type(error).__name__}: {error}" if isinstance(error, BaseException) else str(error)
+
+
 class DistributedOwner:
+    """One rank's side of a storage collective domain whose canonical store lives on ``owner_rank``."""
+
     def __init__(self, group=None, *, control_group=None, owner_rank: int = 0, max_wire_bytes: int = 16 << 20,
                  device="cpu", expected_world_size: int | None = None):
         import torch.distributed as dist
 
         self.dist = dist
         self.group = group
-        self.control_group = control_group if control_group is not None else group
+        self.control_group = group if control_group is None else control_group
         self.initialized = dist.is_available() and dist.is_initialized()
         self.world_size = dist.get_world_size(group) if self.initialized else 1
         self.rank = dist.get_rank(group) if self.initialized else 0
-        if not 0 <= owner_rank < self.world_size:
-            raise ConfigurationError("invalid storage owner rank")
+        if type(owner_rank) is not int or not 0 <= owner_rank < self.world_size:
+            raise ConfigurationError(f"owner rank {owner_rank!r} is not a rank of the {self.world_size}-rank group")
         if expected_world_size is not None and expected_world_size != self.world_size:
-            raise ConfigurationError("storage and native sequence-parallel world sizes differ")
+            raise ConfigurationError(f"the storage group has {self.world_size} ranks, the engine's sequence-parallel "
+                                     f"group {expected_world_size}")
         if type(max_wire_bytes) is not int or max_wire_bytes < 8:
-            raise ConfigurationError("max_wire_bytes must be at least eight")
+            raise ConfigurationError("max_wire_bytes is an integer of at least 8")
         self.owner_rank = owner_rank
         self.max_wire_bytes = max_wire_bytes
         self.device = torch.device(device)
         if self.initialized:
-            backend = str(dist.get_backend(group))
-            if backend == "gloo" and self.device.type != "cpu":
-                raise ConfigurationError("a Gloo data group moves CPU tensors")
-            if backend == "nccl" and self.device.type != "cuda":
-                raise ConfigurationError("an NCCL data group moves CUDA tensors")
+            data_backend = str(dist.get_backend(group))
+            expected = {"gloo": "cpu", "nccl": "cuda"}.get(data_backend)
+            if expected is not None and self.device.type != expected:
+                raise ConfigurationError(f"a {data_backend} data group moves {expected} tensors, not "
+                                         f"{self.device.type} ones")
             if str(dist.get_backend(self.control_group)) != "gloo":
                 raise ConfigurationError("the control group must be a Gloo (CPU) group")
         self.counters = WireCounters()
         self.sequence = 0
         self._thread = threading.get_ident()
         self._broken = False
+        self._control = _ControlChannel(self)
 
     @property
     def is_owner(self) -> bool:
         return self.rank == self.owner_rank
 
     def _guard(self) -> None:
-        if self._thread != threading.get_ident():
-            raise StateError("collectives must stay on the ordered execution thread")
+        if threading.get_ident() != self._thread:
+            raise StateError("storage collectives run on the thread that created the transport")
         if self._broken:
-            raise PeerFailure("the storage transport failed; create a new session")
+            raise PeerFailure("the storage transport failed earlier; open a new session")
 
     def _global(self, rank: int) -> int:
-        return self.dist.get_global_rank(self.group, rank) if self.group is not None else rank
+        return rank if self.group is None else self.dist.get_global_rank(self.group, rank)
 
     def _run(self, fn, *args, **kwargs):
+        """Run one transport call; any failure breaks the domain for good."""
         try:
             with span("transport.collective"):
                 return fn(*args, **kwargs)
-        except Exception as error:
+        except Exception as exc:
             self._broken = True
-            raise PeerFailure(f"storage transport failed: {type(error).__name__}: {error}") from error
-
-    # -- control ----------------------------------------------------------------------------------------------
+            raise PeerFailure(f"the storage transport failed in {getattr(fn, '__name__', fn)}: "
+                              f"{type(exc).__name__}: {exc}") from exc
 
     def _all_json(self, value: Any) -> list:
         self._guard()
-        raw = json.dumps(value, sort_keys=True, separators=(",", ":"), allow_nan=False).encode()
-        if len(raw) > MAX_CONTROL_BYTES:
-            raise ConfigurationError("control messages are bounded to one MiB")
-        if self.world_size == 1:
-            return [json.loads(raw)]
-        length = torch.tensor([len(raw)], dtype=torch.int64)
-        lengths = [torch.zeros_like(length) for _ in range(self.world_size)]
-        self._run(self.dist.all_gather, lengths, length, group=self.control_group)
-        counts = [int(t.item()) for t in lengths]
-        size = max(counts)
-        if min(counts) < 0 or size > MAX_CONTROL_BYTES:
-            self._broken = True
-            raise PeerFailure("a peer sent an invalid control message length")
-        buffer = torch.zeros(size, dtype=torch.uint8)
-        buffer[:len(raw)] = torch.frombuffer(bytearray(raw), dtype=torch.uint8)
-        gathered = [torch.empty_like(buffer) for _ in range(self.world_size)]
-        self._run(self.dist.all_gather, gathered, buffer, group=self.control_group)
-        wire = (8 + size) * (self.world_size - 1)
-        self.counters.control_sent_bytes += wire
-        self.counters.control_received_bytes += wire
-        return [json.loads(bytes(t[:n].tolist())) for t, n in zip(gathered, counts)]
+        return self._control.gather(value)
+
+    # -- agreement ----------------------------------------------------------------------------------------
 
     def checkpoint(self, operation: str, *, error=None, cancelled: bool = False, details=None) -> list:
-        """Every rank reports; raises on every rank if any failed or cancelled. Returns all details."""
+        """Every rank reports; a failure, a cancellation or a step mismatch anywhere raises on every rank.
+        Returns every rank's ``details``."""
         self._guard()
-        if isinstance(error, BaseException):
-            error = f"{type(error).__name__}: {error}"
-        elif error is not None:
-            error = str(error)
+        message = _describe(error)
         try:
-            if len(json.dumps(details, allow_nan=False).encode()) > MAX_CONTROL_BYTES // 2:
-                raise ConfigurationError("checkpoint details exceed 512 KiB")
+            if len(json.dumps(details, allow_nan=False).encode()) > MAX_DETAIL_BYTES:
+                raise ConfigurationError(f"checkpoint details exceed {MAX_DETAIL_BYTES} bytes")
         except Exception as exc:  # noqa: BLE001 - reported through the checkpoint itself
-            error, details = f"invalid checkpoint details: {exc}", None
-        rows = self._all_json({"sequence": self.sequence, "operation": str(operation), "rank": self.rank,
-                               "error": error, "cancelled": bool(cancelled), "details": details})
+            message, details = f"checkpoint details are not bounded JSON: {exc}", None
+        records = self._all_json({"sequence": self.sequence, "operation": str(operation), "rank": self.rank,
+                                  "error": message, "cancelled": bool(cancelled), "details": details})
         self.sequence += 1
         self.counters.checkpoints += 1
-        if len({(r["sequence"], r["operation"]) for r in rows}) != 1:
-            raise PeerFailure(f"collective order mismatch: {rows}")
-        if any(r["cancelled"] for r in rows):
-            raise CollectiveCancelled(f"collective cancelled: {operation}")
-        failures = [f"rank {r['rank']}: {r['error']}" for r in rows if r["error"] is not None]
-        if failures:
-            raise PeerFailure(f"{operation}: " + "; ".join(failures))
-        return [r["details"] for r in rows]
+        steps = {(r["sequence"], r["operation"]) for r in records}
+        if len(steps) > 1:
+            raise PeerFailure(f"ranks reached different collective steps: {sorted(steps)}")
+        if any(r["cancelled"] for r in records):
+            raise CollectiveCancelled(f"{operation} was cancelled by rank(s) "
+                                      f"{[r['rank'] for r in records if r['cancelled']]}")
+        failed = [f"rank {r['rank']}: {r['error']}" for r in records if r["error"] is not None]
+        if failed:
+            raise PeerFailure(f"{operation} failed -- " + "; ".join(failed))
+        return [r["details"] for r in records]
 
     def owner_call(self, operation: str, function: Callable):
-        """Run ``function`` on the owner; its failure is raised on every rank."""
+        """Run ``function`` on the owner only; its failure surfaces on every rank."""
         self.checkpoint(f"{operation}:begin")
-        result, error = None, None
+        result = error = None
         if self.is_owner:
             try:
                 result = function()
-            except BaseException as exc:  # noqa: BLE001
+            except BaseException as exc:  # noqa: BLE001 - agreed below
                 error = exc
         try:
             self.checkpoint(f"{operation}:complete", error=error)
@@ -229,130 +255,142 @@ class DistributedOwner:
         return result
 
     def broadcast_json(self, value, *, operation: str = "broadcast_json", source: int | None = None):
+        """``source``'s JSON value on every rank."""
         source = self.owner_rank if source is None else source
-        error = None
-        try:
-            if not 0 <= source < self.world_size:
-                raise ConfigurationError("invalid JSON source")
-            if self.rank == source:
+        problem = None
+        if not 0 <= source < self.world_size:
+            problem = f"JSON source {source} is not a rank"
+        elif self.rank == source:
+            try:
                 json.dumps(value, allow_nan=False)
-        except Exception as exc:  # noqa: BLE001
-            error = exc
-        self.checkpoint(operation, error=error)
+            except (TypeError, ValueError) as exc:
+                problem = exc
+        self.checkpoint(operation, error=problem)
         return self._all_json(value if self.rank == source else None)[source]
 
-    # -- payloads ---------------------------------------------------------------------------------------------
+    # -- payloads -----------------------------------------------------------------------------------------
 
     def _move(self, tensor: torch.Tensor, source: int, destination: int) -> None:
-        """Point-to-point move of a contiguous tensor in bounded pieces (already allocated on both ends)."""
+        """Point-to-point move of a contiguous tensor allocated on both ends, in bounded pieces."""
         self._guard()
-        if source == destination or self.world_size == 1:
+        if self.world_size == 1 or source == destination:
             return
         flat = tensor.reshape(-1)
         step = max(1, self.max_wire_bytes // tensor.element_size())
-        for start in range(0, flat.numel(), step):
-            block = flat[start:start + step]
-            if self.rank == source:
-                self._run(self.dist.send, block, dst=self._global(destination), group=self.group)
-                self.counters.payload_sent_bytes += block.numel() * block.element_size()
+        sending = self.rank == source
+        peer = self._global(destination if sending else source)
+        for first in range(0, flat.numel(), step):
+            piece = flat[first:first + step]
+            nbytes = piece.numel() * piece.element_size()
+            if sending:
+                self._run(self.dist.send, piece, dst=peer, group=self.group)
+                self.counters.payload_sent_bytes += nbytes
                 self.counters.payload_messages_sent += 1
             elif self.rank == destination:
-                self._run(self.dist.recv, block, src=self._global(source), group=self.group)
-                self.counters.payload_received_bytes += block.numel() * block.element_size()
+                self._run(self.dist.recv, piece, src=peer, group=self.group)
+                self.counters.payload_received_bytes += nbytes
                 self.counters.payload_messages_received += 1
 
     def gather_matrix(self, local: torch.Tensor, layout: KVLayout, *, source_layout: str,
                       operation: str = "gather_matrix") -> torch.Tensor | None:
-        """Canonical ``[tokens, channels]`` on the owner (``None`` elsewhere)."""
-        error, details = None, None
+        """Every rank's ``rows`` or ``heads`` shard assembled into the canonical ``[tokens, channels]`` matrix
+        on the owner (``None`` on the other ranks)."""
+        problem = summary = None
         try:
             if layout.world_size != self.world_size:
-                raise ConfigurationError("layout and group world sizes differ")
+                raise ConfigurationError(f"a {layout.world_size}-rank layout on a {self.world_size}-rank group")
             if tuple(local.shape) != layout.shape(self.rank, source_layout):
-                raise ConfigurationError("local shard shape does not match its declared layout")
+                raise ConfigurationError(f"local shard {tuple(local.shape)} is not this rank's {source_layout} "
+                                         f"shard {layout.shape(self.rank, source_layout)}")
             if local.device.type != self.device.type:
-                raise ConfigurationError("transfer tensor is on the wrong device")
+                raise ConfigurationError(f"the shard is on {local.device.type}, the transport moves "
+                                         f"{self.device.type} tensors")
             if not local.dtype.is_floating_point:
-                raise ConfigurationError("KV transfers require a floating point tensor")
-            details = {"dtype": str(local.dtype), "layout": source_layout, "geometry": asdict(layout)}
+                raise ConfigurationError("KV shards are floating-point tensors")
+            summary = {"dtype": str(local.dtype), "layout": source_layout, "geometry": asdict(layout)}
         except Exception as exc:  # noqa: BLE001
-            error = exc
-        rows = self.checkpoint(operation, error=error, details=details)
-        if any(r != rows[0] for r in rows):
-            raise PeerFailure("peers disagree on the KV layout or dtype")
+            problem = exc
+        summaries = self.checkpoint(operation, error=problem, details=summary)
+        if any(s != summaries[0] for s in summaries):
+            raise PeerFailure("ranks describe their KV shards differently")
         local = local.detach().contiguous()
         canonical = torch.empty((layout.tokens, layout.channels), dtype=local.dtype, device=self.device) \
             if self.is_owner else None
         for source in range(self.world_size):
-            value = None
             if self.rank == source:
-                value = local
+                shard = local
             elif self.is_owner:
-                value = torch.empty(layout.shape(source, source_layout), dtype=local.dtype, device=self.device)
+                shard = torch.empty(layout.shape(source, source_layout), dtype=local.dtype, device=self.device)
+            else:
+                shard = None
             self.checkpoint(f"{operation}:rank{source}")
             if self.rank in (source, self.owner_rank):
-                self._move(value, source, self.owner_rank)
+                self._move(shard, source, self.owner_rank)
             if self.is_owner:
-                target = canonical[layout.rows(source)] if source_layout == "rows" else \
+                region = canonical[layout.rows(source)] if source_layout == "rows" else \
                     canonical[:, layout.columns(source)]
-                target.copy_(value)
+                region.copy_(shard)
         return canonical
 
     @contextmanager
     def acquire_columns(self, layout: KVLayout, loader: Callable, *, dtype, operation: str = "acquire_columns"):
-        """The owner decodes each rank's head columns in turn (``loader(columns)`` -> tensor or context
-        manager yielding one) and sends them; every rank yields only its own ``[tokens, local]`` view."""
-        rows = self.checkpoint(operation, error=None if layout.world_size == self.world_size else
-                               "layout and group world sizes differ",
-                               details={"layout": asdict(layout), "dtype": str(dtype)})
-        if any(r != rows[0] for r in rows):
-            raise PeerFailure("peers disagree on the restore layout or dtype")
-        with ExitStack() as keep:
+        """The owner loads each rank's head columns in turn (``loader(columns)`` returns a tensor or a context
+        manager yielding one) and sends them; each rank yields only its own ``[tokens, local_channels]``."""
+        problem = None if layout.world_size == self.world_size else "the layout describes another group size"
+        plans = self.checkpoint(operation, error=problem, details={"layout": asdict(layout), "dtype": str(dtype)})
+        if any(p != plans[0] for p in plans):
+            raise PeerFailure("ranks asked for different column layouts or dtypes")
+        with ExitStack() as kept:
             mine = None
             for destination in range(self.world_size):
-                with ExitStack() as transient:
-                    value, error = None, None
+                with ExitStack() as scratch:
+                    buffer = failure = None
                     try:
                         if self.is_owner:
                             loaded = loader(layout.columns(destination))
-                            stack = keep if destination == self.rank else transient
-                            value = stack.enter_context(loaded if hasattr(loaded, "__enter__") else nullcontext(loaded))
-                            if tuple(value.shape) != layout.shape(destination, "heads") or value.dtype != dtype \
-                                    or not value.is_contiguous():
-                                raise ConfigurationError("loader returned a wrong column view")
+                            holder = kept if destination == self.rank else scratch
+                            buffer = holder.enter_context(loaded if hasattr(loaded, "__enter__") else nullcontext(loaded))
+                            wanted = layout.shape(destination, "heads")
+                            if tuple(buffer.shape) != wanted or buffer.dtype != dtype or not buffer.is_contiguous():
+                                raise ConfigurationError(f"the loader returned {tuple(buffer.shape)} {buffer.dtype}, "
+                                                         f"not contiguous {wanted} {dtype}")
                         elif self.rank == destination:
-                            value = torch.empty(layout.shape(destination, "heads"), dtype=dtype, device=self.device)
-                    except BaseException as exc:  # noqa: BLE001
-                        error = exc
-                    self.checkpoint(f"{operation}:rank{destination}", error=error)
+                            buffer = torch.empty(layout.shape(destination, "heads"), dtype=dtype, device=self.device)
+                    except BaseException as exc:  # noqa: BLE001 - agreed below
+                        failure = exc
+                    self.checkpoint(f"{operation}:rank{destination}", error=failure)
                     if self.rank in (self.owner_rank, destination):
-                        self._move(value, self.owner_rank, destination)
+                        self._move(buffer, self.owner_rank, destination)
                     if self.rank == destination:
-                        mine = value
+                        mine = buffer
             yield mine
 
     def local_columns(self, layout: KVLayout, loader: Callable, *, dtype, operation: str = "local_columns"):
-        with self.acquire_columns(layout, loader, dtype=dtype, operation=operation) as local:
-            return local.clone()
+        with self.acquire_columns(layout, loader, dtype=dtype, operation=operation) as columns:
+            return columns.clone()
 
     def transfer_tensor(self, value, *, source: int, destination: int, operation: str = "transfer_tensor"):
-        """Move a tensor from ``source`` to ``destination`` (shape and dtype travel as JSON)."""
-        error, description = None, None
+        """``value`` moved from ``source`` to ``destination`` (its shape and dtype travel in the agreement);
+        ``None`` on every other rank."""
+        problem = description = None
         try:
             if not (0 <= source < self.world_size and 0 <= destination < self.world_size):
-                raise ConfigurationError("invalid tensor source/destination")
+                raise ConfigurationError(f"transfer {source} -> {destination} names a rank outside the group")
             if self.rank == source:
                 value = value.detach().to(self.device).contiguous()
-                description = {"shape": list(value.shape), "dtype": str(value.dtype).split(".")[-1]}
+                description = {"shape": list(value.shape), "dtype": str(value.dtype).rpartition(".")[2]}
         except Exception as exc:  # noqa: BLE001
-            error = exc
-        described = self.checkpoint(operation, error=error, details=description)[source]
-        received = None
+            problem = exc
+        described = self.checkpoint(operation, error=problem, details=description)[source]
+        buffer = None
         if self.rank == source:
-            received = value
+            buffer = value
         elif self.rank == destination:
-            received = torch.empty(described["shape"], dtype=getattr(torch, described["dtype"]), device=self.device)
+            buffer = torch.empty(described["shape"], dtype=getattr(torch, described["dtype"]), device=self.device)
         self.checkpoint(f"{operation}:allocated")
         if self.rank in (source, destination):
-            self._move(received, source, destination)
-        return received if self.rank == destination else None
+            self._move(buffer, source, destination)
+        return buffer if self.rank == destination else None
+
+
+__all__ = ["MAX_CONTROL_BYTES", "CollectiveCancelled", "DistributedOwner", "KVLayout", "PeerFailure", "WireCounters"]
