@@ -1,38 +1,20 @@
-"""Batched, fused reconstruction of restored KV matrices into native caches.
+"""The restore entry point: reconstruct many restored KV matrices straight into native cache slots.
 
-Same contract as the reference's restore-kernel API (reelcache/restore_kernels.py:1-89, public
-names at :2336-2447): one call reconstructs any number of restored matrices -- one layer's K or V
-of one chunk each -- straight into native cache slots::
+Public names follow the reference's restore-kernel API (reelcache/restore_kernels.py: ``reconstruct``,
+``RopeTable``, ``RestoreHandle``, ``warmup`` and the job classes re-exported from :mod:`.restore_jobs`), so
+engine code written against it carries over. One :func:`reconstruct` call takes any number of jobs -- each one
+chunk's K or V of one layer -- and, per job, writes ``cast(RoPE(dequantize(coefficients) @ basis[:rank]))``
+(K) or ``cast(dequantize(coefficients) @ basis[:rank])`` (V) into its slot.
 
-    pre-RoPE K or V  =  dequantize(unpack(pixels)) @ Q[:rank]
-    native slot      <- cast(RoPE(K at its original positions))    (K)
-    native slot      <- cast(V)                                    (V)
-
-* A canonical matrix is ``[N, C]``: ``N = frames * height * width`` tokens in (frame, row,
-  column) order and ``C = heads * head_dim`` channels.
-* The basis is the immutable FP16 row matrix ``Q[R, C]``; a job uses the prefix view ``Q[:rank]``.
-* Coefficients ``P[N, rank]``; 8-bit pixels carry them with an FP32 affine per rank column and are
-  dequantized as ``float(pixel) * scale + offset`` with two roundings (no FMA).
-* Pictures use the ``reelcache.channel_tiles.v1`` mosaic: rank column ``k`` lives in segment
-  ``k // channels_per_segment``; inside a segment, cell ``i`` uses plane ``i % planes`` and grid cell
-  ``divmod(i // planes, grid_columns)``; each frame is one picture per segment.
-* RoPE rotates interleaved pairs ``(2j, 2j + 1)`` from FP32 cos/sin tables with separable
-  (t, h, w) sections (Wan / LongCat) or a dense per-token table.
-* Native layouts ``BTHD``, ``THD`` and ``BHTD`` with any strides.
-
-Backends:
-
-* ``fused`` (CUDA; the ``auto`` choice on CUDA): one persistent sm_100a kernel per launch group
-  (csrc/restore/restore_sm100.cu) -- a gather producer unpacks and dequantizes the pixels into
-  swizzled shared memory, TMA streams the transposed FP16 basis, ``tcgen05.mma`` accumulates in TMEM
-  and the epilogue applies RoPE, casts and stores. Dense sources use csrc/restore/rope_store.cu.
-* ``reference`` (plain torch, FP64 or FP32 math; CPU or GPU; the ``auto`` choice on CPU).
-
-Precisions of the fused kernel: ``fp16x2`` (default; coefficients prescaled by an exact power of two
-and split into FP16 hi + lo, two tensor-core products, FP32 accumulation) and ``fp16`` (hi only).
-:func:`error_bound` gives the elementwise bound each mode satisfies (same first-order analysis as the
-reference, :1176-1230). There is no silent fallback: CUDA jobs raise
-:class:`~reelcache_b200.errors.UnsupportedError` when the native extension is missing.
+Backends: ``fused`` (CUDA; chosen by ``auto`` on CUDA) runs the sm_100a pipeline of csrc/restore -- an unpack
+kernel turns 8-bit pixels (mosaic pictures or dense) into the exact FP16 operand ``p - 128``, a preparation
+kernel folds each column's scale into a hi/lo FP16 split of the basis and its offset into a per-channel bias,
+and a persistent TMA + tcgen05 GEMM adds the bias, rotates K from FP32 tables in its epilogue, casts and stores
+with TMA. Dense sources go through csrc/restore/rope_store.cu. ``reference`` (chosen by ``auto`` on the CPU)
+is the plain-torch FP64/FP32 computation of :mod:`.restore_reference`. Precisions of the fused kernel:
+``fp16x2`` (two products, the default) and ``fp16`` (one); the bound each meets is
+:func:`~reelcache_b200.restore_reference.kernel_error_bound`. A CUDA job never falls back silently: without
+the native extension it raises :class:`~reelcache_b200.errors.UnsupportedError`.
 """
 
 from __future__ import annotations
@@ -48,13 +30,19 @@ import numpy as np
 import torch
 
 from .errors import ConfigurationError, IntegrityError, UnsupportedError
+from .restore_jobs import (COEFFICIENT_DTYPES, LAYOUTS, OUTPUT_DTYPES, CoefficientSource, DenseSource, NativeView,
+                           PictureSource, ReconstructionJob, RopePositions, expand_affine, wan_sections)
+from .restore_jobs import host_affine as _host_vector  # noqa: F401  (used by the fused backend's checks)
+from .restore_reference import (OUTPUT_FLOOR as _OUTPUT_FLOOR, UNIT_ROUNDOFF as _UNIT_ROUNDOFF,
+                                apply_rope_reference, dequantize, error_bound, gemm_gamma as _gemm_gamma,
+                                kernel_error_bound, reconstruct_reference, reference_coefficients, reference_values,
+                                rope_cos_sin, unpack_pictures)
+from .restore_reference import check_disjoint as _check_disjoint  # noqa: F401
+from .restore_reference import validate_jobs as _validate
 
-LAYOUTS = ("BTHD", "THD", "BHTD")
 PRECISIONS = ("fp32", "tf32", "tf32x3", "fp16", "fp16x2", "bf16")
 KERNEL_PRECISIONS = ("fp16", "fp16x2")
 BACKENDS = ("auto", "reference", "fused")
-OUTPUT_DTYPES = (torch.bfloat16, torch.float16, torch.float32)
-COEFFICIENT_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 DEFAULT_PRECISION = "fp16x2"
 MAX_JOBS_PER_LAUNCH = 16
 MAX_DENSE_JOBS_PER_LAUNCH = 48
@@ -75,45 +63,6 @@ def _require_tensor(value, name):
     return value
 
 
-def _host_vector(value, length, name):
-    if isinstance(value, torch.Tensor):
-        if value.device.type != "cpu":
-            raise ConfigurationError(f"{name} must be a host array (the packet's affine payload)")
-        value = value.detach().numpy()
-    array = np.asarray(value)
-    if array.dtype != np.float32 or array.shape != (length,):
-        raise ConfigurationError(f"{name} must be a float32 vector with one entry per rank column")
-    if not np.isfinite(array).all():
-        raise ConfigurationError(f"{name} must be finite")
-    return np.ascontiguousarray(array)
-
-
-def expand_affine(affine, normalization, rank):
-    """Per-column ``(scale, offset)`` from a packet's ``[2, records]`` affine payload.
-
-    ``per_channel``: one record per rank column. ``global`` / ``leading_columns``: record 0 is the
-    shared affine and records 1.. cover the ``protected_count`` leading columns.
-    """
-    affine = np.asarray(affine)
-    if affine.dtype != np.dtype("<f4") or affine.ndim != 2 or affine.shape[0] != 2:
-        raise ConfigurationError("affine must be a little-endian float32 [2, records] array")
-    if not isinstance(normalization, Mapping) or "mode" not in normalization:
-        raise ConfigurationError("normalization must be the packet normalization layout")
-    _int(rank, "rank", minimum=1)
-    if normalization["mode"] == "per_channel":
-        if affine.shape[1] != rank:
-            raise ConfigurationError("per-channel affine must have one record per rank column")
-        return affine[0].copy(), affine[1].copy()
-    scale = np.full(rank, affine[0, 0], dtype=np.float32)
-    offset = np.full(rank, affine[1, 0], dtype=np.float32)
-    count = normalization.get("protected_count")
-    if type(count) is not int or not 0 <= count <= rank or affine.shape[1] != count + 1:
-        raise ConfigurationError("affine record count differs from the protected columns")
-    if count:
-        scale[:count], offset[:count] = affine[0, 1:], affine[1, 1:]
-    return scale, offset
-
-
 # (cos, sin) entries of one job's separable tables that the fused epilogue stages in shared memory
 PACKED_ROPE_ENTRIES = 3072
 
@@ -131,88 +80,6 @@ def restore_rope_item(positions, grid, device, stream, keepalive):
     cos, sin = table.token_tables(positions.rows, grid, device, stream)
     keepalive.extend((cos, sin))
     return ("tokens", cos.data_ptr(), sin.data_ptr(), table.pairs)
-
-
-def wan_sections(pairs):
-    """Wan / LongCat 3-D split of ``pairs = head_dim // 2`` into (t, h, w) pair counts."""
-    _int(pairs, "pairs", minimum=1)
-    return (pairs - 2 * (pairs // 3), pairs // 3, pairs // 3)
-
-
-# ---------------------------------------------------------------------------------------------
-# Destinations, RoPE tables and sources
-# ---------------------------------------------------------------------------------------------
-
-
-@dataclass(frozen=True, eq=False)
-class NativeView:
-    """A native cache tensor, its layout and the first destination token."""
-
-    tensor: torch.Tensor
-    layout: str = "BTHD"
-    token_offset: int = 0
-    batch_index: int = 0
-
-    def __post_init__(self):
-        tensor = _require_tensor(self.tensor, "destination tensor")
-        if self.layout not in LAYOUTS:
-            raise ConfigurationError(f"destination layout must be one of {LAYOUTS}")
-        if tensor.ndim != (3 if self.layout == "THD" else 4):
-            raise ConfigurationError(f"{self.layout} destination has the wrong number of dimensions")
-        if tensor.dtype not in OUTPUT_DTYPES:
-            raise ConfigurationError("destination dtype must be bfloat16, float16 or float32")
-        _int(self.token_offset, "token_offset")
-        _int(self.batch_index, "batch_index")
-        if self.layout == "THD" and self.batch_index:
-            raise ConfigurationError("a packed THD destination has no batch dimension")
-        if self.layout != "THD" and self.batch_index >= tensor.shape[0]:
-            raise ConfigurationError("batch_index is outside the destination")
-        if self.head_dim % 2:
-            raise ConfigurationError("head_dim must be even")
-        if any(size > 1 and stride == 0 for size, stride in zip(tensor.shape, tensor.stride())):
-            raise ConfigurationError("destination views with broadcast (zero) strides alias")
-
-    @property
-    def heads(self):
-        return self.tensor.shape[1] if self.layout == "BHTD" else self.tensor.shape[-2]
-
-    @property
-    def head_dim(self):
-        return self.tensor.shape[-1]
-
-    @property
-    def channels(self):
-        return self.heads * self.head_dim
-
-    @property
-    def capacity(self):
-        return self.tensor.shape[2] if self.layout == "BHTD" else self.tensor.shape[-3]
-
-    def strides(self):
-        """Element strides of (token, head, dim)."""
-        stride = self.tensor.stride()
-        if self.layout == "BHTD":
-            return stride[2], stride[1], stride[3]
-        return stride[-3], stride[-2], stride[-1]
-
-    def element_offset(self):
-        """Element offset (from the tensor's data pointer) of (batch_index, token_offset, 0, 0)."""
-        base = 0
-        if self.layout != "THD":
-            base += self.batch_index * self.tensor.stride(0)
-        return base + self.token_offset * self.strides()[0]
-
-    def address(self):
-        return self.tensor.data_ptr() + self.element_offset() * self.tensor.element_size()
-
-    def slot(self, tokens):
-        """A ``[tokens, H, D]`` view of the destination slot."""
-        stop = self.token_offset + tokens
-        if self.layout == "THD":
-            return self.tensor[self.token_offset:stop]
-        if self.layout == "BTHD":
-            return self.tensor[self.batch_index, self.token_offset:stop]
-        return self.tensor[self.batch_index, :, self.token_offset:stop].transpose(0, 1)
 
 
 @dataclass(frozen=True, eq=False)
@@ -460,270 +327,6 @@ class RopeTable:
         return entry[0], entry[1]
 
 
-@dataclass(frozen=True, eq=False)
-class RopePositions:
-    """Original positions of one chunk in a :class:`RopeTable` (separable: ``(t_row, h_row, w_row)``)."""
-
-    table: RopeTable
-    rows: Any = 0
-
-    def __post_init__(self):
-        if not isinstance(self.table, RopeTable):
-            raise ConfigurationError("RoPE positions require a RopeTable")
-        if self.table.sections is None:
-            _int(self.rows, "dense RoPE row")
-        else:
-            rows = self.rows
-            if type(rows) is int:
-                rows = (rows, 0, 0)
-            rows = tuple(rows)
-            if len(rows) != 3:
-                raise ConfigurationError("separable RoPE positions are (t_row, h_row, w_row)")
-            for value in rows:
-                _int(value, "RoPE row")
-            object.__setattr__(self, "rows", rows)
-
-
-@dataclass(frozen=True, eq=False)
-class CoefficientSource:
-    """Coefficients ``[N, >= rank]`` already unpacked from their pictures (uint8 + affine or float)."""
-
-    values: torch.Tensor
-    scale: Any = None
-    offset: Any = None
-    bound: float | None = None
-
-    def __post_init__(self):
-        values = _require_tensor(self.values, "coefficients")
-        if values.ndim != 2:
-            raise ConfigurationError("coefficients must be a [tokens, rank] matrix")
-        if self.bound is not None and (isinstance(self.bound, bool) or not isinstance(self.bound, (int, float))
-                                       or not math.isfinite(self.bound) or self.bound < 0):
-            raise ConfigurationError("bound must be a finite nonnegative upper bound on |coefficients|")
-        if values.dtype == torch.uint8:
-            if self.scale is None or self.offset is None:
-                raise ConfigurationError("quantized coefficients require their affine scale and offset")
-            object.__setattr__(self, "scale", _host_vector(self.scale, values.shape[1], "scale"))
-            object.__setattr__(self, "offset", _host_vector(self.offset, values.shape[1], "offset"))
-            if np.any(self.scale < 0):
-                raise ConfigurationError("affine scales must be nonnegative")
-        elif values.dtype in COEFFICIENT_DTYPES:
-            if self.scale is not None or self.offset is not None:
-                raise ConfigurationError("dequantized coefficients take no affine")
-        else:
-            raise ConfigurationError("coefficients must be uint8 pixels or float32/float16/bfloat16 values")
-
-    @property
-    def quantized(self):
-        return self.values.dtype == torch.uint8
-
-
-@dataclass(frozen=True, eq=False)
-class PictureSource:
-    """Quantized coefficients read in place from decoded pictures ``pictures[segment][frame]``
-    (uint8 views ``[planes, rows, columns]`` whose origin is this matrix's rectangle)."""
-
-    pictures: Any
-    layout: Mapping
-    scale: Any
-    offset: Any
-
-    def __post_init__(self):
-        layout = self.layout
-        required = ("frames", "height", "width", "rank", "planes", "grid", "channels_per_segment", "segments")
-        if not isinstance(layout, Mapping) or any(name not in layout for name in required):
-            raise ConfigurationError("picture layout must be a reelcache.channel_tiles.v1 layout")
-        frames, height, width, rank = (layout[n] for n in ("frames", "height", "width", "rank"))
-        planes, slots, segments = layout["planes"], layout["channels_per_segment"], layout["segments"]
-        for value, name in ((frames, "frames"), (height, "height"), (width, "width"), (rank, "rank"),
-                            (planes, "planes"), (slots, "channels_per_segment"), (segments, "segments")):
-            _int(value, f"layout {name}", minimum=1)
-        columns, rows = layout["grid"]
-        _int(columns, "grid columns", minimum=1)
-        _int(rows, "grid rows", minimum=1)
-        if slots != columns * rows * planes or segments != math.ceil(rank / slots):
-            raise ConfigurationError("picture layout slot/segment counts are inconsistent")
-        pictures = tuple(tuple(segment) for segment in self.pictures)
-        if len(pictures) != segments or any(len(segment) != frames for segment in pictures):
-            raise ConfigurationError("pictures must be indexed [segment][frame] for every segment and frame")
-        strides = None
-        device = None
-        for segment in pictures:
-            for picture in segment:
-                _require_tensor(picture, "picture")
-                if picture.dtype != torch.uint8 or picture.ndim != 3:
-                    raise ConfigurationError("pictures must be uint8 [planes, rows, columns] views")
-                if picture.shape[0] < planes or picture.shape[1] < rows * height or picture.shape[2] < columns * width:
-                    raise ConfigurationError("picture view does not cover the matrix rectangle")
-                if picture.stride(2) != 1:
-                    raise ConfigurationError("picture rows must be contiguous (unit column stride)")
-                current = (picture.stride(0), picture.stride(1))
-                if strides is None:
-                    strides, device = current, picture.device
-                elif current != strides or picture.device != device:
-                    raise ConfigurationError("pictures of one matrix must share plane/row strides and device")
-        object.__setattr__(self, "pictures", pictures)
-        object.__setattr__(self, "scale", _host_vector(self.scale, rank, "scale"))
-        object.__setattr__(self, "offset", _host_vector(self.offset, rank, "offset"))
-        if np.any(self.scale < 0):
-            raise ConfigurationError("affine scales must be nonnegative")
-
-    @property
-    def device(self):
-        return self.pictures[0][0].device
-
-    @property
-    def rank(self):
-        return self.layout["rank"]
-
-    @property
-    def plane_stride(self):
-        return self.pictures[0][0].stride(0)
-
-    @property
-    def row_stride(self):
-        return self.pictures[0][0].stride(1)
-
-    @classmethod
-    def from_canvases(cls, canvases, layout, picture_indices, origins, scale, offset):
-        """Views on decoded canvases ``[pictures, planes, height, width]``; ``origins`` is one
-        ``(y, x)`` or a ``[segment][frame]`` table of origins (schema v2 tile map)."""
-        canvases = _require_tensor(canvases, "canvases")
-        if canvases.ndim != 4 or canvases.dtype != torch.uint8:
-            raise ConfigurationError("canvases must be uint8 [pictures, planes, height, width]")
-        single = len(origins) == 2 and all(type(v) is int for v in origins)
-        pictures = []
-        for s_index, segment in enumerate(picture_indices):
-            row = []
-            for f_index, picture in enumerate(segment):
-                y, x = origins if single else origins[s_index][f_index]
-                _int(picture, "picture index")
-                _int(y, "rectangle y")
-                _int(x, "rectangle x")
-                if picture >= canvases.shape[0]:
-                    raise ConfigurationError("picture index is outside the canvases")
-                row.append(canvases[picture, :, y:, x:])
-            pictures.append(tuple(row))
-        return cls(tuple(pictures), layout, scale, offset)
-
-
-@dataclass(frozen=True, eq=False)
-class DenseSource:
-    """An uncompressed canonical ``[N, C]`` matrix (RAW archive, raw tier)."""
-
-    values: torch.Tensor
-
-    def __post_init__(self):
-        values = _require_tensor(self.values, "dense values")
-        if values.ndim != 2 or values.dtype not in COEFFICIENT_DTYPES:
-            raise ConfigurationError("dense values must be a float32/float16/bfloat16 [tokens, channels] matrix")
-
-
-@dataclass(frozen=True, eq=False)
-class ReconstructionJob:
-    """Reconstruct one restored matrix into one native destination slot.
-
-    ``basis_t`` optionally supplies the kernel's operand layout of the same basis: the transposed,
-    zero-padded FP16 matrix ``[C, ceil(R / 64) * 64]`` (the device basis cache keeps it), saving the
-    per-call transpose.
-    """
-
-    source: Any
-    destination: NativeView
-    grid: tuple
-    basis: torch.Tensor | None = None
-    rank: int | None = None
-    rope: RopePositions | None = None
-    label: str | None = None
-    basis_t: torch.Tensor | None = None
-
-    def __post_init__(self):
-        if not isinstance(self.source, (CoefficientSource, PictureSource, DenseSource)):
-            raise ConfigurationError("source must be a CoefficientSource, PictureSource or DenseSource")
-        if not isinstance(self.destination, NativeView):
-            raise ConfigurationError("destination must be a NativeView")
-        grid = tuple(self.grid)
-        if len(grid) != 3:
-            raise ConfigurationError("grid must be (frames, height, width)")
-        for value in grid:
-            _int(value, "grid size", minimum=1)
-        object.__setattr__(self, "grid", grid)
-        tokens = self.tokens
-        channels = self.destination.channels
-        if self.destination.token_offset + tokens > self.destination.capacity:
-            raise ConfigurationError("destination slot exceeds the native cache capacity")
-        if isinstance(self.source, DenseSource):
-            if self.basis is not None or self.rank is not None:
-                raise ConfigurationError("dense sources take no basis or rank")
-            if tuple(self.source.values.shape) != (tokens, channels):
-                raise ConfigurationError("dense values must be [tokens, heads * head_dim]")
-        else:
-            basis = _require_tensor(self.basis, "basis")
-            if basis.ndim != 2 or basis.shape[1] != channels:
-                raise ConfigurationError("basis must be [rows, heads * head_dim] of the destination")
-            if basis.dtype not in (torch.float16, torch.float32):
-                raise ConfigurationError("basis must be the canonical float16 rows (float32 for reference use)")
-            if isinstance(self.source, PictureSource):
-                layout = self.source.layout
-                if (layout["frames"], layout["height"], layout["width"]) != grid:
-                    raise ConfigurationError("picture layout geometry differs from the job grid")
-                columns = layout["rank"]
-            else:
-                if self.source.values.shape[0] != tokens:
-                    raise ConfigurationError("coefficient rows differ from the job token count")
-                columns = self.source.values.shape[1]
-            rank = columns if self.rank is None else self.rank
-            _int(rank, "rank", minimum=1)
-            if rank > basis.shape[0]:
-                raise ConfigurationError("rank view exceeds the basis rows")
-            if rank > columns or (isinstance(self.source, PictureSource) and rank != columns):
-                raise ConfigurationError("rank view exceeds the available coefficient columns")
-            object.__setattr__(self, "rank", rank)
-            if self.basis_t is not None:
-                bt = self.basis_t
-                if (bt.dtype != torch.float16 or bt.ndim != 2 or bt.shape[0] != channels or bt.shape[1] % 64
-                        or bt.shape[1] < rank or bt.stride(1) != 1):
-                    raise ConfigurationError("basis_t must be float16 [channels, rank_pad] (rank_pad % 64 == 0)")
-        if self.rope is not None:
-            if not isinstance(self.rope, RopePositions):
-                raise ConfigurationError("rope must be RopePositions")
-            table = self.rope.table
-            if table.head_dim != self.destination.head_dim:
-                raise ConfigurationError("RoPE table pairs differ from head_dim // 2")
-            if table.sections is None:
-                if self.rope.rows + tokens > table.rows:
-                    raise ConfigurationError("dense RoPE rows exceed the table")
-            else:
-                limits = table.section_rows
-                needed = (self.rope.rows[0] + grid[0], self.rope.rows[1] + grid[1], self.rope.rows[2] + grid[2])
-                if any(need > limit for need, limit, pairs in zip(needed, limits, table.sections) if pairs):
-                    raise ConfigurationError("separable RoPE rows exceed the table")
-
-    @property
-    def tokens(self):
-        frames, height, width = self.grid
-        return frames * height * width
-
-    @property
-    def channels(self):
-        return self.destination.channels
-
-    def tensors(self):
-        result = [self.destination.tensor]
-        source = self.source
-        if isinstance(source, PictureSource):
-            result.extend(picture for segment in source.pictures for picture in segment)
-        else:
-            result.append(source.values)
-        if self.basis is not None:
-            result.append(self.basis)
-        if self.basis_t is not None:
-            result.append(self.basis_t)
-        if self.rope is not None:
-            result.extend((self.rope.table.cos, self.rope.table.sin))
-        return result
-
-
 # ---------------------------------------------------------------------------------------------
 # Completion handle
 # ---------------------------------------------------------------------------------------------
@@ -797,211 +400,6 @@ class RestoreHandle:
                         _DEFERRED.append((self._event, self._keepalive))
         except Exception:  # noqa: BLE001 - interpreter shutdown
             pass
-
-
-# ---------------------------------------------------------------------------------------------
-# Validation and the reference backend
-# ---------------------------------------------------------------------------------------------
-
-
-def _storage_key(tensor):
-    try:
-        return tensor.untyped_storage().data_ptr(), tensor.device
-    except (RuntimeError, NotImplementedError):
-        return tensor.data_ptr(), tensor.device
-
-
-def _check_disjoint(jobs):
-    """Reject jobs whose slots in the same destination view overlap (their writes would race)."""
-    spans = {}
-    for index, job in enumerate(jobs):
-        view = job.destination
-        tensor = view.tensor
-        key = (*_storage_key(tensor), tensor.storage_offset(), tuple(tensor.shape), tensor.stride(),
-               view.layout, view.batch_index)
-        spans.setdefault(key, []).append((view.token_offset, view.token_offset + job.tokens, index))
-    for intervals in spans.values():
-        intervals.sort()
-        for (_, stop, first), (start, _, second) in zip(intervals, intervals[1:]):
-            if start < stop:
-                raise ConfigurationError(f"jobs {first} and {second} write overlapping destination tokens")
-
-
-def _validate(jobs):
-    if isinstance(jobs, ReconstructionJob):
-        jobs = (jobs,)
-    if not isinstance(jobs, Sequence) or isinstance(jobs, (str, bytes)):
-        raise ConfigurationError("jobs must be a sequence of ReconstructionJob")
-    jobs = tuple(jobs)
-    if any(not isinstance(job, ReconstructionJob) for job in jobs):
-        raise ConfigurationError("jobs must be ReconstructionJob instances")
-    devices = set()
-    for job in jobs:
-        devices.add(job.destination.tensor.device)
-        source = job.source
-        devices.add(source.device if isinstance(source, PictureSource) else source.values.device)
-        if job.basis is not None:
-            devices.add(job.basis.device)
-    if len(devices) > 1:
-        raise ConfigurationError("all job tensors (except RoPE tables) must share one device")
-    _check_disjoint(jobs)
-    return jobs, (devices.pop() if devices else None)
-
-
-def unpack_pictures(source):
-    """Quantized pixels ``[N, rank]`` of a :class:`PictureSource` (mosaic cell mapping)."""
-    layout = source.layout
-    frames, height, width, rank = layout["frames"], layout["height"], layout["width"], layout["rank"]
-    columns, rows = layout["grid"]
-    planes, slots = layout["planes"], layout["channels_per_segment"]
-    values = torch.empty((frames, height, width, rank), dtype=torch.uint8, device=source.device)
-    for segment, pictures in enumerate(source.pictures):
-        first = segment * slots
-        count = min(slots, rank - first)
-        for frame, picture in enumerate(pictures):
-            cropped = picture[:planes, :rows * height, :columns * width]
-            tiled = cropped.reshape(planes, rows, height, columns, width)
-            values[frame, :, :, first:first + count] = tiled.permute(2, 4, 1, 3, 0).reshape(height, width, -1)[:, :, :count]
-    return values.reshape(-1, rank)
-
-
-def dequantize(pixels, scale, offset):
-    """``float(pixel) * scale + offset`` with the eager (multiply, then add) rounding."""
-    scale = torch.from_numpy(np.ascontiguousarray(scale)).to(pixels.device)
-    offset = torch.from_numpy(np.ascontiguousarray(offset)).to(pixels.device)
-    return pixels.float().mul_(scale).add_(offset)
-
-
-def reference_coefficients(job):
-    source = job.source
-    if isinstance(source, PictureSource):
-        return dequantize(unpack_pictures(source), source.scale, source.offset)
-    if isinstance(source, CoefficientSource):
-        if source.quantized:
-            return dequantize(source.values[:, :job.rank], source.scale[:job.rank], source.offset[:job.rank])
-        return source.values[:, :job.rank].float()
-    raise ConfigurationError("dense sources have no coefficients")
-
-
-def rope_cos_sin(positions, grid, *, dtype=torch.float64, device=None):
-    """Per-token ``(cos, sin)`` ``[N, head_dim // 2]`` of a job's positions."""
-    table = positions.table
-    device = table.cos.device if device is None else device
-    cos = table.cos.to(device=device, dtype=dtype)
-    sin = table.sin.to(device=device, dtype=dtype)
-    frames, height, width = grid
-    tokens = frames * height * width
-    if table.sections is None:
-        first = positions.rows
-        return cos[first:first + tokens], sin[first:first + tokens]
-    index = torch.arange(tokens, device=device)
-    frame, rest = index // (height * width), index % (height * width)
-    coordinates = (frame, rest // width, rest % width)
-    out_cos = torch.empty((tokens, table.pairs), dtype=dtype, device=device)
-    out_sin = torch.empty_like(out_cos)
-    column = 0
-    for axis, pairs in enumerate(table.sections):
-        rows = positions.rows[axis] + coordinates[axis]
-        out_cos[:, column:column + pairs] = cos[rows, column:column + pairs]
-        out_sin[:, column:column + pairs] = sin[rows, column:column + pairs]
-        column += pairs
-    return out_cos, out_sin
-
-
-def apply_rope_reference(values, positions, grid, *, dtype=torch.float64):
-    """Rotate interleaved pairs of ``values[N, H, D]`` in ``dtype`` (complex product)."""
-    cos, sin = rope_cos_sin(positions, grid, dtype=dtype, device=values.device)
-    x = values.to(dtype)
-    even, odd = x[..., 0::2], x[..., 1::2]
-    cos, sin = cos[:, None, :], sin[:, None, :]
-    out = torch.empty_like(x)
-    out[..., 0::2] = even * cos - odd * sin
-    out[..., 1::2] = even * sin + odd * cos
-    return out
-
-
-def _reference_job(job, compute, native_rope, native_rope_dtype):
-    heads, head_dim = job.destination.heads, job.destination.head_dim
-    tokens = job.tokens
-    slot = job.destination.slot(tokens)
-    if isinstance(job.source, DenseSource):
-        values = job.source.values
-    else:
-        coefficients = reference_coefficients(job)
-        basis = job.basis[:job.rank]
-        values = coefficients.to(compute) @ basis.to(device=coefficients.device, dtype=compute)
-    if native_rope is not None and job.rope is not None:
-        dtype = slot.dtype if native_rope_dtype is None else native_rope_dtype
-        result = native_rope(values.to(dtype).reshape(tokens, heads, head_dim), job)
-        if not isinstance(result, torch.Tensor) or result.numel() != tokens * heads * head_dim:
-            raise IntegrityError("native RoPE callable returned a tensor of the wrong size")
-        slot.copy_(result.reshape(tokens, heads, head_dim))
-        return
-    values = values.reshape(tokens, heads, head_dim)
-    if job.rope is not None:
-        values = apply_rope_reference(values, job.rope, job.grid, dtype=compute)
-    slot.copy_(values)
-
-
-def reconstruct_reference(jobs, *, compute_dtype=torch.float64, native_rope=None, native_rope_dtype=None):
-    """Plain-torch reference: FP64 (default) or FP32 math, then one cast."""
-    jobs, _ = _validate(jobs)
-    if compute_dtype not in (torch.float32, torch.float64):
-        raise ConfigurationError("reference compute dtype must be float32 or float64")
-    with torch.no_grad():
-        for job in jobs:
-            _reference_job(job, compute_dtype, native_rope, native_rope_dtype)
-
-
-_UNIT_ROUNDOFF = {torch.bfloat16: 2.0 ** -8, torch.float16: 2.0 ** -11, torch.float32: 2.0 ** -24}
-_OUTPUT_FLOOR = {torch.bfloat16: 2.0 ** -134, torch.float16: 2.0 ** -25, torch.float32: 2.0 ** -150}
-
-
-def _gemm_gamma(precision, rank):
-    """Relative GEMM error per unit of ``sum_k |a_k| |q_k|`` of each precision mode."""
-    accumulate = (rank + 1) * 2.0 ** -24
-    return {
-        "fp32": accumulate,
-        "tf32": 2.0 ** -10 + accumulate,
-        "tf32x3": 2.0 ** -20 + 3 * accumulate,
-        "fp16": 2.0 ** -11 + accumulate,
-        "fp16x2": 2.0 ** -21 + 2 * accumulate,
-        "bf16": 2.0 ** -7 + 2.0 ** -16 + accumulate,
-        "reference32": accumulate,
-    }[precision]
-
-
-def reference_values(job):
-    """FP64 values ``y*[N, C]`` a job writes before the final cast, and ``sum_k |p_k| |q_k|``."""
-    tokens, heads, head_dim = job.tokens, job.destination.heads, job.destination.head_dim
-    if isinstance(job.source, DenseSource):
-        values = job.source.values.double()
-        magnitude = torch.zeros_like(values)
-    else:
-        coefficients = reference_coefficients(job).double()
-        basis = job.basis[:job.rank].to(device=coefficients.device, dtype=torch.float64)
-        values = coefficients @ basis
-        magnitude = coefficients.abs() @ basis.abs()
-    if job.rope is not None:
-        values = apply_rope_reference(values.reshape(tokens, heads, head_dim), job.rope, job.grid).reshape(tokens, -1)
-        pairs = magnitude.reshape(tokens, -1, 2)
-        magnitude = (pairs[..., 0] + pairs[..., 1]).repeat_interleave(2, dim=-1)
-    return values, magnitude
-
-
-def error_bound(job, precision, out_dtype=None):
-    """Elementwise bound on ``|written - y*|`` (first-order): ``u_out |y*| + (1 + u_out) E + floor``
-    with ``E = gamma(precision, rank) * S + 2**-21 (|y_e| + |y_o|)`` for RoPE jobs. Returns
-    ``(y*, bound)`` in FP64."""
-    values, magnitude = reference_values(job)
-    out_dtype = job.destination.tensor.dtype if out_dtype is None else out_dtype
-    unit = _UNIT_ROUNDOFF[out_dtype]
-    rank = job.rank or 0
-    error = _gemm_gamma(precision, rank) * magnitude
-    if job.rope is not None:
-        pairs = values.reshape(job.tokens, -1, 2).abs()
-        error = error + 2.0 ** -21 * (pairs[..., 0] + pairs[..., 1]).repeat_interleave(2, dim=-1)
-    return values, unit * values.abs() + (1 + unit) * error + _OUTPUT_FLOOR[out_dtype]
 
 
 # ---------------------------------------------------------------------------------------------
@@ -1310,33 +708,3 @@ def warmup(device, shapes, *, backend="auto", precision="auto", stream=None, **_
         reconstruct([job], backend=backend, precision=precision, stream=stream).release()
         count += 1
     return {"warmed": count}
-
-
-def kernel_error_bound(job, precision="fp16x2", out_dtype=None):
-    """Elementwise bound of the fused sm_100a kernel (same first-order form as :func:`error_bound`).
-
-    For 8-bit sources the kernel multiplies the exact centered pixel ``p - 128`` by the FP16 hi/lo split
-    of ``s[k] Q[k, c]`` and adds the bias ``sum_k (o[k] + 128 s[k]) Q[k, c]``, so its rounding is
-    charged to ``S' = sum_k (|a_k| + |o_k + 128 s_k|) |q_k|`` instead of ``sum_k |a_k| |q_k|`` (``a_k`` the
-    dequantized coefficient); float sources keep the reference's ``S``. Returns ``(y*, bound)`` in FP64.
-    """
-    values, magnitude = reference_values(job)
-    source = job.source
-    quantized = isinstance(source, PictureSource) or (isinstance(source, CoefficientSource) and source.quantized)
-    if quantized:
-        scale = torch.from_numpy(np.asarray(source.scale[:job.rank], dtype=np.float64))
-        offset = torch.from_numpy(np.asarray(source.offset[:job.rank], dtype=np.float64))
-        shifted = (offset + 128.0 * scale).abs().to(magnitude.device)
-        basis = job.basis[:job.rank].to(device=magnitude.device, dtype=torch.float64).abs()
-        extra = (shifted @ basis).expand(job.tokens, -1)
-        if job.rope is not None:
-            pairs = extra.reshape(job.tokens, -1, 2)
-            extra = (pairs[..., 0] + pairs[..., 1]).repeat_interleave(2, dim=-1)
-        magnitude = magnitude + extra
-    out_dtype = job.destination.tensor.dtype if out_dtype is None else out_dtype
-    unit = _UNIT_ROUNDOFF[out_dtype]
-    error = _gemm_gamma(precision, job.rank or 0) * magnitude
-    if job.rope is not None:
-        pairs = values.reshape(job.tokens, -1, 2).abs()
-        error = error + 2.0 ** -21 * (pairs[..., 0] + pairs[..., 1]).repeat_interleave(2, dim=-1)
-    return values, unit * values.abs() + (1 + unit) * error + _OUTPUT_FLOOR[out_dtype]
