@@ -23,12 +23,13 @@ in the store). A submitted chunk is a checkpoint only once it is published.
 
 from __future__ import annotations
 
+import os
 import threading
 import time
 from collections import deque
 from contextlib import contextmanager
 from dataclasses import dataclass, field
-from typing import Any, Mapping
+from typing import Any, Callable, Mapping
 
 import torch
 
@@ -71,9 +72,23 @@ class ArchiveTicket:
 class ArchivePipeline:
     def __init__(self, runtime: LineageRuntime, *, method: RankMethodConfig, device: Any = "cuda",
                  options: ArchiveOptions | None = None, raw_tier=None, max_unpublished: int = 4,
-                 submit_timeout: float | None = None, encode_workers: int = 1, registry=None):
+                 submit_timeout: float | None = None, encode_workers: int = 1, registry=None,
+                 max_source_chunks: int | None = None, stream_priority: int | None = None,
+                 dedicated_stream: bool = True, encode_cpus: set[int] | None = None,
+                 on_publish: Callable[[str, str], None] | None = None):
+        """``max_source_chunks``: captured chunks that may wait for planning (submit blocks beyond it; default:
+        unbounded apart from ``max_unpublished``). ``stream_priority`` / ``dedicated_stream``: the fitter's
+        CUDA stream (a dedicated stream of that priority -- default -1, above the engine's -- or the device's
+        current stream). ``encode_cpus``: CPUs the encode worker threads run on. ``on_publish(lineage,
+        node_ref)`` runs after every publication (the session archive prepares new packs for restores)."""
         if type(max_unpublished) is not int or max_unpublished < 1:
             raise ConfigurationError("max_unpublished must be a positive integer")
+        if max_source_chunks is not None and (type(max_source_chunks) is not int or max_source_chunks < 1):
+            raise ConfigurationError("max_source_chunks must be a positive integer or None")
+        self.max_source_chunks = max_source_chunks
+        self.encode_cpus = None if encode_cpus is None else set(encode_cpus)
+        self.on_publish = on_publish
+        self._affinity_set = threading.local()
         self.runtime = runtime
         self.method = method
         self.device = torch.device(device)
@@ -99,7 +114,9 @@ class ArchivePipeline:
         self._closed = False
         self._counts = {"submitted": 0, "published": 0, "failed": 0, "cancelled": 0, "backpressure_waits": 0,
                         "backpressure_seconds": 0.0}
-        self._stream = torch.cuda.Stream(self.device, priority=-1) if self.device.type == "cuda" else None
+        self._stream = None
+        if self.device.type == "cuda" and dedicated_stream:
+            self._stream = torch.cuda.Stream(self.device, priority=-1 if stream_priority is None else stream_priority)
         self._encoders = BoundedExecutor(max_workers=encode_workers, max_pending=max(2, 2 * encode_workers))
         self._fitter = threading.Thread(target=self._fitter_loop, name="reelcache-fitter", daemon=True)
         self._fitter.start()
@@ -120,7 +137,8 @@ class ArchivePipeline:
             if lineage in self._failed:
                 raise StateError(f"lineage {lineage} has a failed archival: {self._failed[lineage]}")
             waited = None
-            while self._unpublished() >= self.max_unpublished:
+            while self._unpublished() >= self.max_unpublished or (
+                    self.max_source_chunks is not None and len(self._queue) >= self.max_source_chunks):
                 if waited is None:
                     waited = time.monotonic()
                     self._counts["backpressure_waits"] += 1
@@ -196,6 +214,8 @@ class ArchivePipeline:
             job.plan().finalize()
             if self._stream is not None:
                 self._stream.synchronize()
+            elif self.device.type == "cuda":
+                torch.cuda.current_stream(self.device).synchronize()
         ticket._job = job
         ticket.matrices = None
         ticket.timings["plan_seconds"] = time.perf_counter() - started
@@ -203,6 +223,12 @@ class ArchivePipeline:
         self._encoders.submit(self._encode_and_publish, ticket, block=True)
 
     def _encode_and_publish(self, ticket: ArchiveTicket) -> None:
+        if self.encode_cpus and not getattr(self._affinity_set, "done", False):
+            try:
+                os.sched_setaffinity(0, self.encode_cpus)  # this worker thread only
+            except (AttributeError, OSError):
+                pass
+            self._affinity_set.done = True
         try:
             started = time.perf_counter()
             job = ticket._job
@@ -226,6 +252,12 @@ class ArchivePipeline:
                 self.cv.notify_all()
         except BaseException as error:  # noqa: BLE001
             self._fail(ticket, error)
+            return
+        if self.on_publish is not None:
+            try:
+                self.on_publish(ticket.lineage, ticket.node_ref)
+            except Exception:  # noqa: BLE001 - preparation for later restores is best effort
+                self._counts["publish_hook_errors"] = self._counts.get("publish_hook_errors", 0) + 1
 
     def _fail(self, ticket: ArchiveTicket, error: BaseException) -> None:
         with self.cv:

@@ -127,7 +127,12 @@ class LineageRestorer:
 
     def __init__(self, runtime: LineageRuntime, device, *, precision: str = "auto",
                  prepared_budget_bytes: int = 4 << 30, basis_budget_bytes: int = 4 << 30, pin_memory: bool = True,
-                 plan_budget_bytes: int = 2 << 30):
+                 plan_budget_bytes: int = 2 << 30, staging=None, verify_packs: bool = True):
+        """``staging``: a :class:`~reelcache_b200.restore_staging.StagingEngine` that reads cold packs with
+        parallel native ``pread`` into its pinned ring (default: the store's reads). ``verify_packs``: check
+        every tile of a decoded pack against its digest."""
+        self.staging = staging
+        self.verify_packs = verify_packs
         self.runtime = runtime
         self.device = torch.device(device)
         self.precision = precision
@@ -153,7 +158,15 @@ class LineageRestorer:
             if hit is not None:
                 self._prepared.move_to_end(packet_ref)
                 return hit
-        _, pack = self.runtime.node_pack(packet_ref)
+        reader = None
+        if self.staging is not None:
+            def reader(ids):
+                staged = self.staging.stage(ids)
+                try:
+                    return {object_id: staged.bytes(object_id) for object_id in ids}
+                finally:
+                    staged.release()
+        _, pack = self.runtime.node_pack(packet_ref, verify=self.verify_packs, reader=reader)
         raw = torch.from_numpy(np.array(pack.raw, dtype=np.uint8, copy=True))
         if self.pin_memory:
             raw = raw.pin_memory()

@@ -79,6 +79,7 @@ class BasisVersionStore:
         self._versions: dict[str, BasisVersion] = {}      # validated versions (their chains too)
         self._finite: set[str] = set()                     # blocks already checked to be finite
         self._running: OrderedDict[str, Any] = OrderedDict()  # version -> sha256 state of its full view
+        self.verify_blocks = True   # hash blocks (and whole views) on assembly unless the store verifies reads
 
     # -- caches --------------------------------------------------------------------------------------------
 
@@ -261,7 +262,7 @@ class BasisVersionStore:
         row_bytes = 2 * version.channels
         if max_bytes is not None and rows * row_bytes > max_bytes:
             raise CapacityError(f"the view needs {rows * row_bytes} bytes, above the {max_bytes}-byte bound")
-        trusted = self.store.verify_reads
+        trusted = self.store.verify_reads or not self.verify_blocks
         whole = hashlib.sha256() if rows == version.total_rank and not trusted else None
         parts = []
         left = rows

@@ -16,7 +16,7 @@ from typing import Any
 import torch
 
 from ...archive_pipeline import ArchivePipeline, RawArchive
-from ...archive_restore import LineageRestorer, RawLineageRestorer
+from ...archive_restore import LineageRestorer, RawLineageRestorer, SoftwareLineageRestorer
 from ...factor_packs import FactorLineageRestorer
 from ...errors import ConfigurationError
 from ...lineage import LineageRuntime
@@ -26,11 +26,13 @@ from ...rank_method import RankMethodConfig
 from ...raw_tier import RawChunkTier
 from ...store import ObjectStore
 from ...types import CodecSpec, EnergyTargets, MatrixKey, ModelIdentity, energy_targets
-from .config import ReelCacheRuntimeConfig
+from .config import LATENTS_ONLY, ReelCacheRuntimeConfig
 from .profiles import ModelProfile
 
 
 def method_for(config: ReelCacheRuntimeConfig, profile: ModelProfile, fit_device) -> RankMethodConfig:
+    """The rank method of a session archive: energy targets (profile or explicit), fixed-rank policies, and the
+    codec parameters recorded with every lossy matrix (QP, pixel format, preset, normalization)."""
     if config.energy_key is not None:
         targets = EnergyTargets("custom", config.energy_key, config.energy_value, True, "explicit energy fractions")
     else:
@@ -43,53 +45,113 @@ def method_for(config: ReelCacheRuntimeConfig, profile: ModelProfile, fit_device
         fixed = {"fixed_rank_k": max(1, round(fractions["K"] * profile.channels)),
                  "fixed_rank_v": max(1, round(fractions["V"] * profile.channels))}
     kind = "svd" if config.representation == "svd" else "svd_hevc"
-    return RankMethodConfig(targets, CodecSpec(kind, 32, normalization=config.normalization),
-                            reuse=config.reuse, refit=config.refit, refit_rule=config.refit_rule,
-                            rate_lag=config.rate_lag, matmul_precision=config.matmul_precision or "fp32", **fixed)
+    codec = CodecSpec(kind, 32, normalization=config.normalization, pix_fmt=config.hevc_pix_fmt, qp=config.hevc_qp,
+                      preset=config.hevc_preset)
+    return RankMethodConfig(targets, codec, reuse=config.reuse, refit=config.refit, refit_rule=config.refit_rule,
+                            rate_lag=config.rate_lag, matmul_precision=config.matmul_precision or "fp32",
+                            orthogonalizer=config.orthogonalizer, **fixed)
 
 
 class LineageSessionArchive:
+    """Every session's lineage in one store, with its archival pipeline, raw tier and restorer, built from the
+    runtime configuration (each field is consumed here, in the bridge or in the session controller)."""
+
     def __init__(self, config: ReelCacheRuntimeConfig, identity: ModelIdentity, profile: ModelProfile, device):
+        import os
+
         self.config = config
         self.profile = profile
         self.device = torch.device(device)
+        cuda = self.device.type == "cuda"
         self.store = ObjectStore(config.store_root, max_bytes=config.max_store_bytes, verify_reads=config.verify_reads,
                                  on_damage="keep" if config.on_open_error == "quarantine" else "raise")
+        self.store.set_io_policy(config.store_io)
+        self.audit = self._audit() if config.audit_on_open else None
         self.registry = RankPredictorRegistry(config.predictor_registry_id)
         self.runtime = LineageRuntime(self.store, identity, registry=self.registry)
-        fit_device = self.device if config.fit_device == "cuda" and self.device.type == "cuda" else torch.device("cpu")
+        self.runtime.basis.verify_blocks = config.verify_bases
+        fit_device = self.device if config.fit_device == "cuda" and cuda else torch.device("cpu")
         self.method = method_for(config, profile, fit_device)
         self.raw_tier = None
         if config.raw_tier:
             gpu = config.gpu_raw_budget_bytes
             if gpu is None:
-                gpu = (4 << 30) if self.device.type == "cuda" else (256 << 20)
-            host = config.host_raw_budget_bytes if config.host_raw_budget_bytes is not None else (8 << 30)
-            self.raw_tier = RawChunkTier(self.device, gpu_budget_bytes=gpu, host_budget_bytes=host,
+                gpu = (4 << 30) if cuda else (256 << 20)
+            self.raw_tier = RawChunkTier(self.device, gpu_budget_bytes=gpu, host_budget_bytes=config.host_raw_budget_bytes,
                                          host_pinned=config.host_raw_pinned, retain=config.raw_tier_retain,
-                                         promote=config.raw_tier_promote)
+                                         promote=config.raw_tier_promote, reserve_bytes=config.gpu_raw_reserve_bytes)
+        self.eviction = None
+        if config.archive_budget_bytes is not None:
+            from .archive_eviction import ArchiveEviction
+            self.eviction = ArchiveEviction(self.store, config.archive_budget_bytes)
         representation = config.representation
-        if representation in ("raw", "raw_offload"):
+        if representation in ("raw", "raw_offload", LATENTS_ONLY):
             self.pipeline = RawArchive(self.runtime, raw_tier=self.raw_tier,
                                        write_behind=representation == "raw_offload",
                                        max_unwritten=config.max_unpublished)
         else:
-            self.pipeline = ArchivePipeline(self.runtime, method=self.method, device=fit_device,
-                                            options=ArchiveOptions(), raw_tier=self.raw_tier,
-                                            max_unpublished=config.max_unpublished,
+            options = ArchiveOptions(encode_threads=config.resolved_x265_threads(),
+                                     plan_memory_bytes=config.plan_memory_bytes)
+            cpus = set(os.sched_getaffinity(0)) if (config.archival_cpus == "job" and hasattr(os, "sched_getaffinity")) \
+                else None
+            self.pipeline = ArchivePipeline(self.runtime, method=self.method, device=fit_device, options=options,
+                                            raw_tier=self.raw_tier, max_unpublished=config.max_unpublished,
                                             submit_timeout=config.submit_timeout,
-                                            encode_workers=config.resolved_encode_workers(), registry=self.registry)
+                                            encode_workers=config.resolved_encode_workers(), registry=self.registry,
+                                            max_source_chunks=config.max_source_chunks,
+                                            stream_priority=config.stream_priority,
+                                            dedicated_stream=config.fitter_stream == "dedicated", encode_cpus=cpus,
+                                            on_publish=self._published)
         self.restorer = None
-        if self.device.type == "cuda":
+        if cuda:
             if representation in ("raw", "raw_offload"):
                 self.restorer = RawLineageRestorer(self.runtime, self.device)
             elif representation == "svd":
                 self.restorer = FactorLineageRestorer(self.runtime, self.device)
-            else:
+            elif representation == "svd_hevc" and config.decoder == "software":
+                self.restorer = SoftwareLineageRestorer(self.runtime, self.device)
+            elif representation == "svd_hevc":
+                staging = None
+                if config.staging_engine:
+                    from ...restore_staging import StagingEngine
+                    staging = StagingEngine(self.store, pinned_bytes=config.staging_pinned_bytes,
+                                            threads=config.staging_threads or 8)
                 self.restorer = LineageRestorer(self.runtime, self.device,
                                                 prepared_budget_bytes=config.prepared_budget_bytes,
-                                                basis_budget_bytes=config.basis_budget_bytes)
-        self.stats_ = {"raw_installs": 0, "archive_installs": 0, "commits": 0}
+                                                basis_budget_bytes=config.basis_budget_bytes,
+                                                plan_budget_bytes=config.restore_arena_bytes, staging=staging,
+                                                verify_packs=config.validate_decode)
+            if config.warmup or (config.warmup is None and self.restorer is not None):
+                self._warm_kernels()
+        self.stats_ = {"raw_installs": 0, "archive_installs": 0, "commits": 0, "prepared_on_publish": 0}
+
+    def _audit(self) -> dict:
+        """Hash every object every ref reaches (``audit_on_open``); damaged graphs are quarantined."""
+        damaged = {}
+        for name, ref in self.store.list_refs().items():
+            try:
+                self.store.verify(ref)
+            except Exception as exc:  # noqa: BLE001 - recorded per ref; on_open_error decides below
+                damaged[name] = str(exc)
+        if damaged and self.config.on_open_error == "raise":
+            raise ConfigurationError(f"store audit found damaged refs: {sorted(damaged)[:5]}")
+        return {"refs": len(self.store.list_refs()), "damaged": damaged}
+
+    def _warm_kernels(self) -> None:
+        from ...restore_kernels import WarmupShape, warmup
+        p = self.profile
+        warmup(self.device, [WarmupShape(p.num_heads, p.head_dim)])
+
+    def _published(self, lineage: str, node_ref: str) -> None:
+        """After a node is published: account its payloads under the archive budget, and (``seal_prepare``)
+        decode its pack into the restorer's prepared cache so a later restore skips that work."""
+        node = self.runtime.load_node(node_ref)
+        if self.eviction is not None and node.packet_ref is not None:
+            payloads = frozenset(r for r in self.store.references(node.packet_ref) if r.startswith("blob:"))
+            self.eviction.published(node_ref, payloads)
+        if self.config.seal_prepare and isinstance(self.restorer, LineageRestorer) and node.packet_ref is not None:
+            self.restorer.prepared_pack(node.packet_ref)
+            self.stats_["prepared_on_publish"] += 1
 
     # -- lineages -------------------------------------------------------------------------------------------------
 

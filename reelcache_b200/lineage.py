@@ -21,7 +21,7 @@ from __future__ import annotations
 import threading
 import time
 from dataclasses import dataclass
-from typing import Any, Mapping, Sequence
+from typing import Callable, Any, Mapping, Sequence
 
 import numpy as np
 import torch
@@ -441,13 +441,17 @@ class LineageRuntime:
             ranges = [(0, node.frontier)] if node.frontier else []
         return resolve(self.node_path(node_ref), ranges)
 
-    def node_pack(self, packet_ref: str, *, verify: bool = True) -> tuple[Mapping[str, Any], codecs.DecodedPack]:
-        """(packet manifest, decoded coefficient pack) of a node pack."""
+    def node_pack(self, packet_ref: str, *, verify: bool = True,
+                  reader: Callable[[list[str]], Mapping[str, bytes]] | None = None
+                  ) -> tuple[Mapping[str, Any], codecs.DecodedPack]:
+        """(packet manifest, decoded coefficient pack) of a node pack; ``reader(ids)`` reads its payload objects
+        (default: the store's parallel reads; a restore staging engine passes its own)."""
         packet = self.load_packet(packet_ref)
         metadata = packet["metadata"]
         if metadata.get("schema") != codecs.PACK_SCHEMA:
             raise IntegrityError("packet is not a node pack")
-        blobs = self.store.get_many([packet["payloads"]["stream"], packet["payloads"]["affines"]])
+        ids = [packet["payloads"]["stream"], packet["payloads"]["affines"]]
+        blobs = (reader or self.store.get_many)(ids)
         pack = codecs.DecodedPack(metadata, blobs[packet["payloads"]["stream"]], blobs[packet["payloads"]["affines"]],
                                   verify=verify)
         return packet, pack

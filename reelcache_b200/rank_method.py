@@ -27,6 +27,9 @@ run on the batched Jacobi kernel (FP64 LAPACK on the host).
 
 from __future__ import annotations
 
+import contextlib
+import threading
+
 import math
 import time
 from dataclasses import dataclass, field, replace
@@ -45,6 +48,7 @@ SOLVERS = ("gram_eigh", "topk_rr")
 REFIT_RULES = ("cumulative", "paper")
 DECISIONS = ("fresh", "share", "augment", "refit", "zero_input", "diagnostic_full_width")
 MATMUL_PRECISIONS = ("fp32", "fp32_verified_fp64")
+ORTHOGONALIZERS = ("batched", "householder")
 FIXED_BASES = ("fitted", "identity")
 
 
@@ -77,6 +81,7 @@ class RankMethodConfig:
     fixed_rank_k: int | None = None
     fixed_rank_v: int | None = None
     fixed_basis: str = "fitted"
+    orthogonalizer: str = "batched"
 
     def __post_init__(self) -> None:
         if not isinstance(self.targets, EnergyTargets):
@@ -91,6 +96,8 @@ class RankMethodConfig:
             raise ConfigurationError(f"matmul_precision must be one of {MATMUL_PRECISIONS}")
         if self.fixed_basis not in FIXED_BASES:
             raise ConfigurationError(f"fixed_basis must be one of {FIXED_BASES}")
+        if self.orthogonalizer not in ORTHOGONALIZERS:
+            raise ConfigurationError(f"orthogonalizer must be one of {ORTHOGONALIZERS}")
         for name, low, high in (("anchor_rank", 1, 4096), ("bucket", 1, 4096), ("power_iterations", 0, 8),
                                 ("tile_rows", 1, 1 << 20), ("batch_size", 1, 256), ("rate_lag", 0, 8),
                                 ("topk_margin", 0, 4096), ("topk_steps", 0, 16)):
@@ -120,6 +127,8 @@ class RankMethodConfig:
                 data[name] = getattr(self, name)
         if self.fixed_basis != "fitted":
             data["fixed_basis"] = self.fixed_basis
+        if self.orthogonalizer != "batched":
+            data["orthogonalizer"] = self.orthogonalizer
         return data
 
     @property
@@ -172,12 +181,27 @@ def _rr_eigh(t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return values[order], vectors[:, order].float()
 
 
+_ORTHO = threading.local()
+
+
+@contextlib.contextmanager
+def orthogonalizer_scope(name: str):
+    """Select the orthogonalizer of the planning calls made on this thread inside the scope."""
+    previous = getattr(_ORTHO, "name", "batched")
+    _ORTHO.name = name
+    try:
+        yield
+    finally:
+        _ORTHO.name = previous
+
+
 def _orthonormalize(b: torch.Tensor) -> torch.Tensor:
-    """Column-orthonormal basis of ``b[C, k]`` (Householder QR in FP32, signs canonical)."""
-    q, r = torch.linalg.qr(b.float())
-    signs = torch.sign(torch.diagonal(r))
-    signs[signs == 0] = 1
-    return q * signs
+    """Column-orthonormal basis of ``b[C, k]``: CholeskyQR2 (``batched``: FP32-accurate tensor-core Grams and
+    triangular solves, Householder only when a Gram is not positive definite) or Householder QR in FP32; signs
+    canonical (positive diagonal of R) either way."""
+    if getattr(_ORTHO, "name", "batched") == "householder":
+        return exact_blas.householder_qr(b)
+    return exact_blas.cholesky_qr2(b)
 
 
 def _generator(seed: int, key: MatrixKey, salt: str) -> torch.Generator:
@@ -497,6 +521,11 @@ def plan_chunk(matrices: Mapping[Any, torch.Tensor], contexts: Mapping[Any, Tens
                inherited: Mapping[Any, torch.Tensor | None], *, chunk_id: str = "chunk",
                device: Any = None) -> dict[Any, MatrixPlan]:
     """Plan every matrix of a chunk (entries in canonical order)."""
+    with orthogonalizer_scope(cfg.orthogonalizer):
+        return _plan_chunk(matrices, contexts, cfg, view, bindings, inherited, chunk_id=chunk_id, device=device)
+
+
+def _plan_chunk(matrices, contexts, cfg, view, bindings, inherited, *, chunk_id, device):
     plans = {}
     for entry in sorted(contexts, key=lambda e: (getattr(e, "layer", None) if isinstance(e, MatrixKey) else e[0].layer,
                                                   getattr(e, "target", None) if isinstance(e, MatrixKey) else e[0].target,

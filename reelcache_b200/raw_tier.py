@@ -34,6 +34,129 @@ from .errors import CapacityError, ConfigurationError, StateError
 TIER_NAMES = ("gpu", "host")
 
 
+# -- budgets from the machine ------------------------------------------------------------------------------------
+
+def cgroup_memory_limit(root: str = "/sys/fs/cgroup") -> int | None:
+    """The memory limit of this process's cgroup (v2 ``memory.max`` or v1 ``memory.limit_in_bytes``), or
+    None when unlimited or unknown."""
+    import os
+    candidates = []
+    try:
+        with open("/proc/self/cgroup") as handle:
+            for line in handle:
+                parts = line.strip().split(":", 2)
+                if len(parts) == 3 and (parts[1] == "" or "memory" in parts[1].split(",")):
+                    candidates.append((parts[1], parts[2]))
+    except OSError:
+        pass
+    paths = []
+    for controllers, rel in candidates:
+        rel = rel.lstrip("/")
+        if controllers == "":                               # v2 unified hierarchy
+            paths.append(os.path.join(root, rel, "memory.max"))
+        else:
+            paths.append(os.path.join(root, "memory", rel, "memory.limit_in_bytes"))
+    paths += [os.path.join(root, "memory.max"), os.path.join(root, "memory", "memory.limit_in_bytes")]
+    for path in paths:
+        try:
+            with open(path) as handle:
+                text = handle.read().strip()
+        except OSError:
+            continue
+        if text == "max":
+            return None
+        try:
+            value = int(text)
+        except ValueError:
+            continue
+        return None if value >= (1 << 60) else value   # v1 reports "unlimited" as a huge number
+    return None
+
+
+def meminfo_available(path: str = "/proc/meminfo") -> int | None:
+    """``MemAvailable`` of the host in bytes (None when unknown)."""
+    try:
+        with open(path) as handle:
+            for line in handle:
+                if line.startswith("MemAvailable:"):
+                    return int(line.split()[1]) * 1024
+    except (OSError, ValueError, IndexError):
+        pass
+    return None
+
+
+def auto_host_budget(*, fraction: float = 0.5, workers: int | None = None, cgroup_root: str = "/sys/fs/cgroup",
+                     meminfo: str = "/proc/meminfo") -> int:
+    """A host raw-tier budget for one worker: ``fraction`` of the smaller of the cgroup limit and the host's
+    available memory, shared by the node's workers (``LOCAL_WORLD_SIZE`` by default)."""
+    import os
+    if not 0 < fraction <= 1:
+        raise ConfigurationError("fraction must lie in (0, 1]")
+    if workers is None:
+        workers = int(os.environ.get("LOCAL_WORLD_SIZE", "1") or 1)
+    limits = [v for v in (cgroup_memory_limit(cgroup_root), meminfo_available(meminfo)) if v is not None]
+    if not limits:
+        return 8 << 30
+    return max(0, int(min(limits) * fraction) // max(1, workers))
+
+
+def device_headroom(device, reserve_bytes: int = 0) -> int | None:
+    """Free device memory beyond ``reserve_bytes`` (negative when the reserve is already eaten into); None
+    off CUDA."""
+    device = torch.device(device)
+    if device.type != "cuda" or not torch.cuda.is_available():
+        return None
+    free, _ = torch.cuda.mem_get_info(device)
+    return int(free) - int(reserve_bytes)
+
+
+class HostPool:
+    """Pinned host blocks recycled by power-of-two size class: registering pinned memory is slow, so a
+    demoted chunk reuses the blocks a dropped one gave back. At most ``cached_bytes`` stay cached."""
+
+    def __init__(self, *, pinned: bool, cached_bytes: int = 4 << 30, min_block: int = 1 << 20):
+        self.pinned = pinned
+        self.cached_limit = cached_bytes
+        self.min_block = min_block
+        self._free: dict[int, list[torch.Tensor]] = {}
+        self.cached = 0
+        self.stats = {"allocated": 0, "reused": 0, "released": 0}
+        self._lock = threading.Lock()
+
+    def _class(self, nbytes: int) -> int:
+        size = self.min_block
+        while size < nbytes:
+            size <<= 1
+        return size
+
+    def take(self, nbytes: int) -> torch.Tensor:
+        size = self._class(max(1, nbytes))
+        with self._lock:
+            blocks = self._free.get(size)
+            if blocks:
+                self.cached -= size
+                self.stats["reused"] += 1
+                return blocks.pop()
+        self.stats["allocated"] += 1
+        return torch.empty(size, dtype=torch.uint8, pin_memory=self.pinned)
+
+    def give(self, block: torch.Tensor) -> None:
+        size = block.numel()
+        with self._lock:
+            if self.cached + size <= self.cached_limit:
+                self._free.setdefault(size, []).append(block)
+                self.cached += size
+            else:
+                self.stats["released"] += 1
+
+    def view(self, block: torch.Tensor, shape, dtype) -> torch.Tensor:
+        count = 1
+        for dim in shape:
+            count *= int(dim)
+        nbytes = count * torch.empty((), dtype=dtype).element_size()
+        return block[:nbytes].view(dtype).view(tuple(shape))
+
+
 @dataclass
 class RawEntry:
     token: int
@@ -43,6 +166,7 @@ class RawEntry:
     gpu: dict | None = None          # entry key -> tensor on the capture device
     host: dict | None = None         # entry key -> host tensor
     host_ready: Any = None           # event after which the host copy is complete
+    host_blocks: list = field(default_factory=list)   # pooled pinned blocks behind the host copy
     node_ref: str | None = None      # set at publication
     holders: set = field(default_factory=set)
     last_used: float = field(default_factory=time.monotonic)
@@ -76,9 +200,19 @@ class RawLease:
 
 
 class RawChunkTier:
-    def __init__(self, device, *, gpu_budget_bytes: int, host_budget_bytes: int, host_pinned: bool = True,
+    def __init__(self, device, *, gpu_budget_bytes: int, host_budget_bytes: int | None, host_pinned: bool = True,
                  retain: str = "drop", promote: str = "off", gpu_only: bool = False,
-                 backpressure_timeout: float | None = 60.0):
+                 backpressure_timeout: float | None = 60.0, reserve_bytes: int | None = None,
+                 pool_cached_bytes: int | None = None):
+        """``host_budget_bytes=None``: :func:`auto_host_budget`. ``reserve_bytes``: device memory the tier keeps
+        free -- published device copies are demoted while :func:`device_headroom` is below it.
+        ``promote="host"``: a restore that finds an entry only in host memory copies it back to the device
+        and keeps it there (budget and reserve permitting); :meth:`promote_host` does so ahead of time."""
+        if host_budget_bytes is None:
+            host_budget_bytes = auto_host_budget()
+        if reserve_bytes is not None and (type(reserve_bytes) is not int or reserve_bytes < 0):
+            raise ConfigurationError("reserve_bytes must be a nonnegative byte count or None")
+        self.reserve = reserve_bytes
         if retain not in ("drop", "lru") or promote not in ("off", "host"):
             raise ConfigurationError("retain must be drop|lru and promote off|host")
         for name, value in (("gpu_budget_bytes", gpu_budget_bytes), ("host_budget_bytes", host_budget_bytes)):
@@ -104,6 +238,10 @@ class RawChunkTier:
                         "misses": 0, "retained_hits": 0, "backpressure_waits": 0, "backpressure_seconds": 0.0,
                         "restaged": 0, "trimmed_bytes": 0}
         self._closed = False
+        self.pool = HostPool(pinned=self.host_pinned,
+                             cached_bytes=min(self.host_budget, 4 << 30) if pool_cached_bytes is None
+                             else pool_cached_bytes)
+        self.records.update(promoted=0, reserve_demotions=0)
         self._trim = register_device_trim("raw_tier", self.trim_device_cache, device=self.device)
 
     # -- admission ------------------------------------------------------------------------------------------------
@@ -153,11 +291,22 @@ class RawChunkTier:
             return (0 if e.published and not e.holders else 1 if e.published else 2, e.last_used)
         return sorted((e for e in self._entries.values() if self._pins.get(e.token, 0) == 0), key=rank)
 
+    def _short_of_reserve(self) -> bool:
+        if self.reserve is None:
+            return False
+        headroom = device_headroom(self.device, self.reserve)
+        return headroom is not None and headroom < 0
+
     def _enforce(self, extra: int = 0) -> None:
-        # device over budget: demote to host (I1: the host copy exists before the device copy goes)
+        # device over budget (or eating into the reserve): demote to host (I1: the host copy exists before
+        # the device copy goes)
         for entry in self._order():
-            if self.gpu_bytes + extra <= self.gpu_budget:
+            over_budget = self.gpu_bytes + extra > self.gpu_budget
+            reserve_short = entry.published and entry.gpu is not None and self._short_of_reserve()
+            if not over_budget and not reserve_short:
                 break
+            if not over_budget:
+                self.records["reserve_demotions"] += 1
             if entry.gpu is None:
                 continue
             if entry.published and (self.gpu_only or self.host_budget == 0):
@@ -190,7 +339,9 @@ class RawChunkTier:
                 self._stream.wait_stream(torch.cuda.current_stream(self.device))
                 with torch.cuda.stream(self._stream):
                     for key, t in entry.gpu.items():
-                        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=self.host_pinned)
+                        block = self.pool.take(t.numel() * t.element_size())
+                        entry.host_blocks.append(block)
+                        h = self.pool.view(block, t.shape, t.dtype)
                         h.copy_(t, non_blocking=True)
                         host[key] = h
                     event = torch.cuda.Event()
@@ -212,6 +363,9 @@ class RawChunkTier:
                 entry.host_ready.synchronize()
             entry.host = None
             entry.host_ready = None
+            for block in entry.host_blocks:
+                self.pool.give(block)
+            entry.host_blocks = []
             self.host_bytes -= entry.nbytes
             self.records["evicted"] += 1
 
@@ -302,13 +456,35 @@ class RawChunkTier:
                 raise StateError("raw entry is gone")
             return self._device_copy(entry)
 
-    def _device_copy(self, entry: RawEntry) -> dict:
+    def _device_copy(self, entry: RawEntry, *, keep: bool | None = None) -> dict:
         if entry.gpu is not None:
             return dict(entry.gpu)
         self.records["restaged"] += 1
         if entry.host_ready is not None:
             torch.cuda.current_stream(self.device).wait_event(entry.host_ready)
-        return {key: t.to(self.device, non_blocking=True) for key, t in entry.host.items()}
+        copy = {key: t.to(self.device, non_blocking=True) for key, t in entry.host.items()}
+        keep = (self.promote == "host") if keep is None else keep
+        if keep and self.device.type == "cuda" and self.gpu_bytes + entry.nbytes <= self.gpu_budget \
+                and not self._short_of_reserve():
+            entry.gpu = copy               # promoted: the device copy stays (the host copy too, until evicted)
+            self.gpu_bytes += entry.nbytes
+            self.records["promoted"] += 1
+        return dict(copy)
+
+    def promote_host(self, node_refs: Iterable[str]) -> int:
+        """Copy the host-only entries of ``node_refs`` back to the device ahead of a restore (within the device
+        budget and reserve); returns how many were promoted."""
+        promoted = 0
+        with self.cv:
+            for ref in node_refs:
+                token = self._by_node.get(ref)
+                entry = None if token is None else self._entries.get(token)
+                if entry is None or entry.gpu is not None or entry.host is None:
+                    continue
+                before = self.records["promoted"]
+                self._device_copy(entry, keep=True)
+                promoted += self.records["promoted"] - before
+        return promoted
 
     def _unpin(self, entry: RawEntry) -> None:
         with self.cv:
@@ -338,6 +514,7 @@ class RawChunkTier:
         with self.cv:
             return {"entries": len(self._entries), "gpu_bytes": self.gpu_bytes, "host_bytes": self.host_bytes,
                     "gpu_budget_bytes": self.gpu_budget, "host_budget_bytes": self.host_budget,
+                    "reserve_bytes": self.reserve, "host_pool": dict(self.pool.stats, cached_bytes=self.pool.cached),
                     "unpublished": sum(1 for e in self._entries.values() if not e.published),
                     **self.records}
 

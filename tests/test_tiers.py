@@ -175,3 +175,32 @@ def test_layer_prefetch_packed_prefetch_and_paired_decode(archived):
                                                                                 prep.raw_shape))
     assert k.tobytes() == v.tobytes() and paired.stats()["pairs"] == 1
     pool.close()
+
+
+def test_raw_tier_machine_budgets_and_host_pool(tmp_path):
+    """Host budgets come from the cgroup limit (v2 or v1) and MemAvailable, split over the node's workers; the
+    pinned host pool hands back blocks by size class."""
+    from reelcache_b200.raw_tier import HostPool, auto_host_budget, cgroup_memory_limit, meminfo_available
+    root = tmp_path / "cg"
+    (root).mkdir()
+    (root / "memory.max").write_text("8589934592\n")
+    meminfo = tmp_path / "meminfo"
+    meminfo.write_text("MemTotal: 100000000 kB\nMemAvailable: 4194304 kB\n")
+    assert cgroup_memory_limit(str(root)) == 8 << 30
+    assert meminfo_available(str(meminfo)) == 4 << 30
+    # the smaller of the two (4 GiB), half of it, over two workers
+    assert auto_host_budget(fraction=0.5, workers=2, cgroup_root=str(root), meminfo=str(meminfo)) == 1 << 30
+    (root / "memory.max").write_text("max\n")
+    assert cgroup_memory_limit(str(root)) is None
+    v1 = tmp_path / "v1"
+    (v1 / "memory").mkdir(parents=True)
+    (v1 / "memory" / "memory.limit_in_bytes").write_text(str(2 << 30))
+    assert cgroup_memory_limit(str(v1)) == 2 << 30
+    pool = HostPool(pinned=False, cached_bytes=8 << 20, min_block=1 << 20)
+    a = pool.take(3 << 20)
+    assert a.numel() == 4 << 20
+    view = pool.view(a, (1024, 256), torch.float32)
+    assert view.shape == (1024, 256)
+    pool.give(a)
+    b = pool.take((3 << 20) + 5)
+    assert b.data_ptr() == a.data_ptr() and pool.stats["reused"] == 1
