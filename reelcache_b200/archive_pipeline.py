@@ -281,6 +281,36 @@ class ArchivePipeline:
 
     # -- control --------------------------------------------------------------------------------------------------
 
+    def commit_recache(self, lineage: str, recache_id: str, ranges, *, epoch_id: str, details=None,
+                       execution_state=None, holder: Any = None) -> str:
+        """Publish a ``kv_recache`` epoch after every submitted chunk of the lineage (exact RAW ranges, or none
+        for a latents-only archive); the tier keeps each range's KV under :func:`range_holder`."""
+        self.drain(lineage)
+        commit = self.runtime.commit_raw_recache(lineage, recache_id, ranges, epoch_id=epoch_id, details=details,
+                                                 execution_state=execution_state, kv_objects=self.kv_objects)
+        admit_ranges(self.raw_tier, commit.node_ref, ranges, holder)
+        return commit.node_ref
+
+    def commit_recache(self, lineage: str, recache_id: str, ranges, *, epoch_id: str, details=None,
+                       execution_state=None, holder: Any = None) -> str:
+        """Publish a ``kv_recache`` epoch (the re-materialized chunk ranges of a prompt switch) after every
+        submitted chunk of the lineage, planned and encoded like a chunk; the raw tier keeps each range's source
+        under :func:`range_holder` until evicted."""
+        self.drain(lineage)
+        with self.cv:
+            self._defer += 1   # the fitter takes no other work while the recache plans on the GPU
+        try:
+            commit = self.runtime.commit_recache(lineage, recache_id, ranges, method=self.method,
+                                                 registry=self.registry, epoch_id=epoch_id, details=details,
+                                                 execution_state=execution_state, device=self.device,
+                                                 options=self.options)
+        finally:
+            with self.cv:
+                self._defer -= 1
+                self.cv.notify_all()
+        admit_ranges(self.raw_tier, commit.node_ref, ranges, holder)
+        return commit.node_ref
+
     def frontiers(self, lineage: str) -> dict:
         with self.cv:
             tickets = self._tickets.get(lineage, [])
@@ -440,6 +470,20 @@ class ArchivePipeline:
         self._encoders.close(cancel_pending=True)
 
 
+def range_holder(node_ref: str, range_id: str) -> str:
+    """The raw-tier key of one epoch range (a chunk node's own range is keyed by its node ref)."""
+    return f"{node_ref}#{range_id}"
+
+
+def admit_ranges(raw_tier, node_ref: str, ranges, holder: Any) -> None:
+    """Keep each published epoch range's exact source in the raw tier (published at once)."""
+    if raw_tier is None:
+        return
+    for range_id, matrices, _contexts in ranges:
+        token = raw_tier.admit({entry: tensor.clone() for entry, tensor in matrices.items()}, range_id, holder)
+        raw_tier.published(token, range_holder(node_ref, range_id))
+
+
 class _Null:
     def __enter__(self):
         return self
@@ -460,12 +504,16 @@ class RawArchive:
     published, and ``submit`` waits only while the writer's queue is full. RAW is the identity reference of the
     capture / restore / install path, not a compression path."""
 
-    def __init__(self, runtime: LineageRuntime, *, raw_tier=None, write_behind: bool = False, max_unwritten: int = 4):
+    def __init__(self, runtime: LineageRuntime, *, raw_tier=None, write_behind: bool = False, max_unwritten: int = 4,
+                 kv_objects: bool = True):
         if type(max_unwritten) is not int or max_unwritten < 1:
             raise ConfigurationError("max_unwritten must be a positive integer")
         if write_behind and raw_tier is None:
             raise ConfigurationError("write-behind RAW archival needs a raw tier")
+        if write_behind and not kv_objects:
+            raise ConfigurationError("a latents-only archive writes no KV behind the tier")
         self.runtime, self.raw_tier, self.write_behind = runtime, raw_tier, write_behind
+        self.kv_objects = kv_objects
         self.max_unpublished = max_unwritten
         self.cv = threading.Condition()
         self._queue: deque[ArchiveTicket] = deque()
@@ -482,7 +530,7 @@ class RawArchive:
     def _commit(self, ticket: ArchiveTicket, matrices) -> None:
         started = time.perf_counter()
         commit = self.runtime.commit_raw_node(ticket.lineage, ticket.chunk_id, matrices, ticket.contexts,
-                                              execution_state=ticket.execution_state)
+                                              execution_state=ticket.execution_state, kv_objects=self.kv_objects)
         ticket.node_ref = commit.node_ref
         ticket.state = "published"
         with self.cv:
@@ -507,6 +555,9 @@ class RawArchive:
             self._tickets[lineage].append(ticket)
             self._counts["submitted"] += 1
         if not self.write_behind:
+            if not self.kv_objects and self.raw_tier is not None:
+                # the tier keeps the only KV copy of a latents-only node (a miss replays the path)
+                ticket.raw_token = self.raw_tier.admit(matrices, chunk_id, holder)
             try:
                 self._commit(ticket, matrices)
             except BaseException as error:  # noqa: BLE001 - delivered to the ticket and raised
@@ -549,6 +600,16 @@ class RawArchive:
         if ticket.raw_token is not None:
             self.raw_tier.failed(ticket.raw_token)
         ticket._done.set()
+
+    def commit_recache(self, lineage: str, recache_id: str, ranges, *, epoch_id: str, details=None,
+                       execution_state=None, holder: Any = None) -> str:
+        """Publish a ``kv_recache`` epoch after every submitted chunk of the lineage (exact RAW ranges, or none
+        for a latents-only archive); the tier keeps each range's KV under :func:`range_holder`."""
+        self.drain(lineage)
+        commit = self.runtime.commit_raw_recache(lineage, recache_id, ranges, epoch_id=epoch_id, details=details,
+                                                 execution_state=execution_state, kv_objects=self.kv_objects)
+        admit_ranges(self.raw_tier, commit.node_ref, ranges, holder)
+        return commit.node_ref
 
     def frontiers(self, lineage: str) -> dict:
         with self.cv:

@@ -4,7 +4,9 @@ configuration, model profiles, sessions and their controls, archival and restore
 ``create_sglang_backend(config=, pipeline=, server_args=)`` validates the configuration, picks the
 model profile and returns a :class:`CausalWanKVBridge` around an engine: ``pipeline`` is a chunk
 engine (:class:`CausalWanEngine`, :class:`SyntheticEngine`) or a :class:`CausalWanDiT` with its
-encoded text context (``(model, text_kv)``).
+encoded text context (``(model, text_kv)``). An engine drives each request through the bridge's seam
+(:mod:`.seam`: ``begin_request`` / ``restore`` / capture / ``end_chunk`` / ``finish``); ``bridge.request`` is that
+loop over the bridge's own engine.
 """
 
 from __future__ import annotations
@@ -12,11 +14,13 @@ from __future__ import annotations
 from typing import Any, Mapping
 
 from ...errors import ConfigurationError
-from .bridge import CausalWanKVBridge
+from .bridge import CausalWanKVBridge, PlanCache, ResidentKV
 from .config import ReelCacheRuntimeConfig
 from .controls import SessionControlError, session_control
 from .engine import CausalWanEngine, SyntheticEngine, model_identity_for
 from .profiles import ModelProfile, get_profile, register_profile
+from .seam import (CausalKVRequest, CaptureScope, ChunkSlot, KVRecache, RecachePlan, RestoreTarget, drive_request,
+                   plan_recache)
 from .session import SGLangSessionController, SGLangSessionState, checkpoint_ref
 
 
@@ -41,6 +45,8 @@ def create_sglang_backend(config: ReelCacheRuntimeConfig | Mapping[str, Any], pi
     return CausalWanKVBridge(config, engine, profile, **kwargs)
 
 
-__all__ = ["CausalWanKVBridge", "CausalWanEngine", "ModelProfile", "ReelCacheRuntimeConfig", "SGLangSessionController",
-           "SGLangSessionState", "SessionControlError", "SyntheticEngine", "checkpoint_ref", "create_sglang_backend",
-           "get_profile", "register_profile", "session_control"]
+__all__ = ["CaptureScope", "CausalKVRequest", "CausalWanKVBridge", "CausalWanEngine", "ChunkSlot", "KVRecache",
+           "ModelProfile", "PlanCache", "RecachePlan", "ReelCacheRuntimeConfig", "ResidentKV", "RestoreTarget",
+           "SGLangSessionController", "SGLangSessionState", "SessionControlError", "SyntheticEngine", "checkpoint_ref",
+           "create_sglang_backend", "drive_request", "get_profile", "plan_recache", "register_profile",
+           "session_control"]

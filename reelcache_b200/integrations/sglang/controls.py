@@ -56,7 +56,8 @@ def session_control(bridge, op: str, payload: Mapping[str, Any] | None = None) -
         if op == "request":
             report = bridge.request(_str(payload, "session"), chunks=int(payload.get("chunks", 1)),
                                     action=payload.get("action", "resume"), checkpoint=payload.get("checkpoint"),
-                                    source=payload.get("source"), seed=int(payload.get("seed", 0)))
+                                    source=payload.get("source"), seed=int(payload.get("seed", 0)),
+                                    prompt=payload.get("prompt"), request_id=payload.get("request_id"))
             report.pop("latents", None)
             return report
         if op == "pause":

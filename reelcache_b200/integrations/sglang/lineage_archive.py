@@ -88,7 +88,8 @@ class LineageSessionArchive:
         if representation in ("raw", "raw_offload", LATENTS_ONLY):
             self.pipeline = RawArchive(self.runtime, raw_tier=self.raw_tier,
                                        write_behind=representation == "raw_offload",
-                                       max_unwritten=config.max_unpublished)
+                                       max_unwritten=config.max_unpublished,
+                                       kv_objects=representation != LATENTS_ONLY)
         else:
             options = ArchiveOptions(encode_threads=config.resolved_x265_threads(),
                                      plan_memory_bytes=config.plan_memory_bytes)
@@ -183,6 +184,13 @@ class LineageSessionArchive:
         self.stats_["commits"] += 1
         return self.pipeline.submit(session_id, chunk_id, matrices, contexts, execution_state=execution_state,
                                     capture_event=capture_event, holder=session_id)
+
+    def commit_recache(self, session_id: str, recache_id: str, ranges, *, epoch_id: str, details=None,
+                       execution_state=None) -> str:
+        """Publish a prompt switch's ``kv_recache`` epoch after the session's submitted chunks; returns its node."""
+        self.stats_["recaches"] = self.stats_.get("recaches", 0) + 1
+        return self.pipeline.commit_recache(session_id, recache_id, ranges, epoch_id=epoch_id, details=details,
+                                            execution_state=execution_state, holder=session_id)
 
     def drain(self, session_id: str | None = None, timeout: float | None = None) -> float:
         return self.pipeline.drain(session_id, timeout)

@@ -15,6 +15,8 @@ import time
 from dataclasses import dataclass, field
 from typing import Any
 
+import torch
+
 from ...errors import ConfigurationError, StateError
 from .nodes import chunk_nodes, path_nodes
 
@@ -39,6 +41,8 @@ class SGLangSessionState:
     resident_chunks: int = 0           # chunks of history the resident cache holds (of the generated path)
     resident_used: int = 0             # request counter of the last use of the resident cache (LRU order)
     pending: list = field(default_factory=list)   # archive tickets not yet published
+    prompt: str | None = None          # conditioning of the newest chunk / recache (None: the default)
+    recaches: list = field(default_factory=list)  # chunk counts at which the resident cache was recached
     failure: BaseException | None = None
     pause_requested: bool = False
     events: list = field(default_factory=list)
@@ -54,11 +58,33 @@ class SGLangSessionState:
                 "failure": None if self.failure is None else str(self.failure)}
 
 
+RETAINED_PREFIX = "sglang/retained/"
+
+
+def node_prompt(runtime, node_ref: str) -> str | None:
+    """The prompt a node was generated (or recached) under, from its execution state (None: the default)."""
+    state = runtime.execution_state(node_ref)
+    prompt = state.get("prompt")
+    return None if prompt is None else bytes(prompt.to(torch.uint8).tolist()).decode()
+
+
+def prompt_tensor(prompt: str | None) -> dict:
+    """The execution-state entry recording a prompt (none for the default conditioning)."""
+    return {} if prompt is None else {"prompt": torch.tensor(list(prompt.encode()), dtype=torch.uint8)}
+
+
 class SGLangSessionController:
-    def __init__(self, archive):
+    """``retention="full"`` keeps every abandoned branch reachable: a rewind first pins the head it leaves under
+    ``sglang/retained/<session>/<n>`` (garbage collection keeps what refs reach); ``"head"`` keeps the current
+    head (and named checkpoints) only."""
+
+    def __init__(self, archive, *, retention: str = "head"):
+        if retention not in ("head", "full"):
+            raise ConfigurationError("retention is 'head' or 'full'")
         self.archive = archive
         self.store = archive.store
         self.runtime = archive.runtime
+        self.retention = retention
         self._lock = threading.RLock()
         self._states: dict[str, SGLangSessionState] = {}
 
@@ -80,7 +106,8 @@ class SGLangSessionController:
 
     def _reopen(self, session_id: str) -> SGLangSessionState:
         head = self.archive.head(session_id)
-        state = SGLangSessionState(session_id, generated=len(chunk_nodes(self.runtime, head)))
+        state = SGLangSessionState(session_id, generated=len(chunk_nodes(self.runtime, head)),
+                                   prompt=node_prompt(self.runtime, head))
         state.log("reopened", head=head)
         self._states[session_id] = state
         return state
@@ -169,6 +196,11 @@ class SGLangSessionController:
             info["name"] = name
         return info
 
+    def retained(self, session_id: str) -> list[str]:
+        """Heads a rewind left behind (``retention="full"``), oldest first."""
+        refs = self.store.list_refs(f"{RETAINED_PREFIX}{session_id}/")
+        return [refs[name] for name in sorted(refs, key=lambda name: int(name.rsplit("/", 1)[1]))]
+
     def checkpoints(self, session_id: str) -> list[dict]:
         """Every chunk checkpoint of the session's published path, plus its named checkpoints."""
         named = {ref.rsplit("/", 1)[1]: node for ref, node in
@@ -209,7 +241,8 @@ class SGLangSessionController:
             if self.archive.exists(session_id):
                 raise StateError(f"session {session_id!r} already exists")
             self.archive.fork(node, session_id)
-            state = SGLangSessionState(session_id, generated=len(chunk_nodes(self.runtime, node)))
+            state = SGLangSessionState(session_id, generated=len(chunk_nodes(self.runtime, node)),
+                                       prompt=node_prompt(self.runtime, node))
             state.log("forked", source=source_id, node=node)
             self._states[session_id] = state
             return state
@@ -220,9 +253,18 @@ class SGLangSessionController:
             self.check_ready(state)
             self.archive.drain(session_id)
             node = self.resolve(session_id, checkpoint)
+            left = self.head(session_id)
+            if self.retention == "full" and left != node:
+                taken = self.store.list_refs(f"{RETAINED_PREFIX}{session_id}/")
+                self.store.set_ref(f"{RETAINED_PREFIX}{session_id}/{len(taken)}", left)
             self.archive.rewind(session_id, node)
             state.generated = len(chunk_nodes(self.runtime, node))
-            if state.resident_chunks > state.generated:
+            state.prompt = node_prompt(self.runtime, node)
+            if any(at >= state.generated for at in state.recaches):
+                state.resident = None  # the resident cache holds KV recached after the rewind point
+                state.resident_chunks = 0
+                state.recaches = []
+            elif state.resident_chunks > state.generated:
                 state.resident_chunks = state.generated  # the resident prefix stays valid (same path)
             state.status = "idle"
             state.log("rewound", node=node)
@@ -241,8 +283,9 @@ class SGLangSessionController:
             state.status = "closed"
             result = {"session": session_id, "deleted": delete}
             if delete:
-                for ref in self.store.list_refs(f"{CHECKPOINT_PREFIX}{session_id}/"):
-                    self.store.delete_ref(ref)
+                for prefix in (CHECKPOINT_PREFIX, RETAINED_PREFIX):
+                    for ref in self.store.list_refs(f"{prefix}{session_id}/"):
+                        self.store.delete_ref(ref)
                 self.archive.delete(session_id)
                 self._states.pop(session_id, None)
             else:

@@ -86,3 +86,25 @@ def build_visibility_plan(profile: ModelProfile, chunk_nodes: Sequence[str], nex
             slot += chunk_end - cursor
             cursor = chunk_end
     return VisibilityPlan(next_chunk, tuple(spans))
+
+
+def resolve_plan(runtime, head_ref: str, plan: VisibilityPlan) -> VisibilityPlan:
+    """The plan with every span cut at KV-version boundaries: each piece names the holder of the newest version on
+    the head's path (a chunk node ref, or ``node#range`` of a recache epoch range, the raw tier's keys) and its
+    offset inside that holder's range. Spans keep their chunk index (RoPE rows) and cache slots."""
+    from ...archive_pipeline import range_holder
+    if not plan.spans:
+        return plan
+    pieces = runtime.resolve_history(head_ref, plan.ranges())
+    spans: list[TokenSpan] = []
+    for span in plan.spans:
+        end = span.token_start + span.length
+        for piece in pieces:
+            left, right = max(piece.token_start, span.token_start), min(piece.token_end, end)
+            if left >= right:
+                continue
+            entry = piece.entry
+            holder = entry.node_ref if entry.source == "chunk" else range_holder(entry.node_ref, entry.chunk_id)
+            spans.append(TokenSpan(holder, span.chunk_index, left - entry.token_start, right - left,
+                                   span.slot_start + left - span.token_start, left, span.role))
+    return VisibilityPlan(plan.next_chunk, tuple(spans))

@@ -392,33 +392,42 @@ class LineageRuntime:
         records = dict(job.stored["ranges"][0][1]) if job.stored["ranges"] else {}
         return LineageCommit(node_ref, node, records, job.plan_summary(), dict(job.timings))
 
+    def _raw_records(self, matrices: Mapping[Any, torch.Tensor], contexts: Mapping[Any, TensorContext]) -> dict:
+        """Exact RAW packets and records of one range (inside the caller's store transaction)."""
+        raw = CodecSpec(kind="raw")
+        records = {}
+        for entry in sorted(contexts, key=entry_order):
+            context = contexts[entry]
+            encoded = codecs.encode_raw(matrices[entry].detach().to("cpu").reshape(context.shape), context)
+            blobs = {name: self.store.put(value) for name, value in encoded.payloads.items()}
+            packet_ref = self.put_content({"type": "packet", "version": 1, "model": self.model.to_dict(),
+                                           "metadata": encoded.metadata, "payloads": blobs,
+                                           "metrics": json_copy(encoded.metrics), "basis_storage": "none"},
+                                          field="metrics", references=sorted(blobs.values()))
+            record = MatrixRecord(context, raw, packet_ref, None, None, None, None,
+                                  {"schema": "reelcache.raw_record.v1", "representation": "raw"},
+                                  stream=entry_parts(entry)[1])
+            records[entry] = self.put_record(record)
+        return records
+
     def commit_raw_node(self, branch_id: str, chunk_id: str, matrices: Mapping[Any, torch.Tensor],
                         contexts: Mapping[Any, TensorContext], *,
                         execution_state: Mapping[str, torch.Tensor] | None = None,
-                        expected_head: str | None = None) -> LineageCommit:
-        """Commit one chunk as exact RAW packets (the identity reference; extends RAW lineages only)."""
+                        expected_head: str | None = None, kv_objects: bool = True) -> LineageCommit:
+        """Commit one chunk as exact RAW packets (the identity reference; extends RAW lineages only).
+        ``kv_objects=False`` stores no KV at all: a latents-only node that a restore replays from its execution
+        state (which must then be given)."""
         started = time.perf_counter()
+        if not kv_objects and not execution_state:
+            raise ConfigurationError("a latents-only node needs the execution state it is replayed from")
         with self._lock:
             head = self.lineage_head(branch_id) if expected_head is None else expected_head
             head_node = self.load_node(head)
             self._check_inputs(head_node, matrices, contexts)
             if any(binding.version_ref is not None for _, binding in head_node.active_basis):
                 raise UnsupportedError("RAW nodes extend RAW lineages only (this head has active lossy bases)")
-            raw = CodecSpec(kind="raw")
             with self.store.transaction():
-                records = {}
-                for entry in sorted(contexts, key=entry_order):
-                    context = contexts[entry]
-                    encoded = codecs.encode_raw(matrices[entry].detach().to("cpu").reshape(context.shape), context)
-                    blobs = {name: self.store.put(value) for name, value in encoded.payloads.items()}
-                    packet_ref = self.put_content({"type": "packet", "version": 1, "model": self.model.to_dict(),
-                                                   "metadata": encoded.metadata, "payloads": blobs,
-                                                   "metrics": json_copy(encoded.metrics), "basis_storage": "none"},
-                                                  field="metrics", references=sorted(blobs.values()))
-                    record = MatrixRecord(context, raw, packet_ref, None, None, None, None,
-                                          {"schema": "reelcache.raw_record.v1", "representation": "raw"},
-                                          stream=entry_parts(entry)[1])
-                    records[entry] = self.put_record(record)
+                records = self._raw_records(matrices, contexts) if kv_objects else {}
                 state_ref = self.store.put(serialize_tensors(dict(execution_state))) if execution_state else None
                 context = next(iter(contexts.values()))
                 if context.token_start != head_node.frontier:
@@ -427,10 +436,47 @@ class LineageRuntime:
                                  context.token_start, context.token_end, context.frames, context.height, context.width,
                                  context.token_end, tuple(records.items()), head_node.active_basis, state_ref,
                                  head_node.streams)
-                node_ref = self._put_node(node, {"kind": "raw_chunk",
+                node_ref = self._put_node(node, {"kind": "raw_chunk" if kv_objects else "latents_chunk",
                                                  "timings": {"store": time.perf_counter() - started}})
                 self.store.set_ref(self._lineage_name(branch_id), node_ref, expected=head)
         return LineageCommit(node_ref, node, records, {"decisions": {"raw": len(records)}}, {})
+
+    def commit_raw_recache(self, branch_id: str, recache_id: str, ranges, *, epoch_id: str,
+                           details: Mapping[str, Any] | None = None,
+                           execution_state: Mapping[str, torch.Tensor] | None = None,
+                           expected_head: str | None = None, kv_objects: bool = True) -> LineageCommit:
+        """Publish a ``kv_recache`` epoch of exact RAW ranges (``ranges``: ``(range_id, matrices, contexts)`` per
+        re-materialized chunk range). ``kv_objects=False`` records the ranges without KV (a latents-only
+        lineage re-runs the recache on replay); the epoch's details then say ``kv_objects: false``."""
+        details = dict(details or {})
+        if not kv_objects:
+            details["kv_objects"] = False
+        with self._lock:
+            head = self.lineage_head(branch_id) if expected_head is None else expected_head
+            head_node = self.load_node(head)
+            if any(binding.version_ref is not None for _, binding in head_node.active_basis):
+                raise UnsupportedError("RAW recaches extend RAW lineages only (this head has active lossy bases)")
+            with self.store.transaction():
+                epoch_ranges = []
+                for range_id, matrices, contexts in ranges:
+                    self._check_inputs(head_node, matrices, contexts)
+                    context = next(iter(contexts.values()))
+                    if context.token_end > head_node.frontier:
+                        raise ConfigurationError("a recache re-materializes generated tokens only")
+                    records = self._raw_records(matrices, contexts) if kv_objects else {}
+                    epoch_ranges.append(TokenRangeRecords(range_id, context.token_start, context.token_end,
+                                                          context.frames, context.height, context.width,
+                                                          tuple(records.items()), head_node.streams))
+                epoch = CacheEpoch(epoch_id, head_node.epoch_ref, "kv_recache", "global",
+                                   tuple(sorted(epoch_ranges, key=lambda r: r.token_start)), details)
+                epoch_ref = self._put_epoch(epoch)
+                state_ref = self.store.put(serialize_tensors(dict(execution_state))) if execution_state else None
+                node = ChunkNode("recache", recache_id, head, epoch_id, epoch_ref, head_node.frontier,
+                                 head_node.frontier, 0, 0, 0, head_node.frontier, (), head_node.active_basis, state_ref,
+                                 head_node.streams)
+                node_ref = self._put_node(node, {"kind": "raw_recache" if kv_objects else "latents_recache"})
+                self.store.set_ref(self._lineage_name(branch_id), node_ref, expected=head)
+        return LineageCommit(node_ref, node, {}, {"decisions": {"raw_ranges": len(epoch_ranges)}}, {})
 
     # -- history -------------------------------------------------------------------------------------------------
 

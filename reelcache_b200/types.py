@@ -970,8 +970,6 @@ class TokenRangeRecords:
         if self.token_end - self.token_start != self.frames * self.height * self.width:
             _fail("a range spans exactly its frames x height x width tokens")
         records = _keyed_pairs(self.records, "range records", _record_id)
-        if not records:
-            _fail("a re-materialized range lists its matrix records")
         object.__setattr__(self, "records", records)
         object.__setattr__(self, "streams", _check_streams(self.streams, [e for e, _ in records], "range records"))
 
@@ -1025,6 +1023,10 @@ class CacheEpoch:
                   "positions")
         if self.cause == "longcat_segment" and (len(ranges) != 1 or ranges[0].token_start != 0):
             _fail("a segment epoch holds exactly one range starting at token 0")
+        latents_only = isinstance(self.details, Mapping) and self.details.get("kv_objects") is False
+        if any(not r.records for r in ranges) and not latents_only:
+            _fail("a re-materialized range lists its matrix records (only a latents-only epoch, details "
+                  "kv_objects=false, stores none)")
         object.__setattr__(self, "ranges", ranges)
         object.__setattr__(self, "details", frozen_json(self.details, name="epoch details"))
 
@@ -1099,8 +1101,10 @@ class ChunkNode:
         _check_streams(streams, [e for e, _ in bindings], "active basis bindings")
         object.__setattr__(self, "streams", streams)
         kind = self.node_kind
-        if kind == "chunk" and (span == 0 or not records or self.frontier != self.token_end):
-            _fail("a chunk node appends frames and records their matrices; its frontier is its end")
+        if kind == "chunk" and (span == 0 or self.frontier != self.token_end
+                                or (not records and self.execution_state_ref is None)):
+            _fail("a chunk node appends frames and records their matrices (a latents-only node instead names "
+                  "the execution state it is replayed from); its frontier is its end")
         if kind != "chunk" and records:
             _fail("only chunk nodes carry matrix records of their own")
         if kind in ("root", "recache") and span:

@@ -82,11 +82,11 @@ def test_restore_matches_resident_history(tmp_path):
     bridge = make_bridge(tmp_path, raw_tier=False)
     try:
         bridge.request("a", chunks=3, action="create", seed=7)
-        resident = bridge.sessions.get("a").resident
+        resident = bridge.sessions.get("a").resident.cache
         bridge.pause("a")
         bridge.drop_resident("a")
         bridge.request("a", chunks=0, seed=7)  # restore only
-        restored = bridge.sessions.get("a").resident
+        restored = bridge.sessions.get("a").resident.cache
         tokens = 3 * TINY.chunk_tokens
         for layer in range(TINY.num_layers):
             a, b = resident["k"][layer][:tokens], restored["k"][layer][:tokens]
@@ -119,12 +119,12 @@ def test_other_representations_restore(tmp_path, representation, raw_tier, bound
                          if raw_tier else "prefer")
     try:
         bridge.request("a", chunks=3, action="create", seed=7)
-        resident = bridge.sessions.get("a").resident
+        resident = bridge.sessions.get("a").resident.cache
         bridge.pause("a")
         bridge.drop_resident("a")
         report = bridge.request("a", chunks=0, seed=7)
         assert report["route"] == "archive"
-        restored = bridge.sessions.get("a").resident
+        restored = bridge.sessions.get("a").resident.cache
         tokens = 3 * TINY.chunk_tokens
         for layer in range(TINY.num_layers):
             for which in ("k", "v"):
