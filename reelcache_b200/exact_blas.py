@@ -91,19 +91,31 @@ def householder_qr(b: torch.Tensor) -> torch.Tensor:
     return _canonical(q, r)
 
 
-def cholesky_qr2(b: torch.Tensor) -> torch.Tensor:
-    """Column-orthonormal basis of ``b[C, k]`` by two CholeskyQR passes (FP64 Cholesky of the FP32-accurate
-    Gram, FP32-accurate triangular solve); Householder QR when a Gram is not positive definite."""
+def cholesky_qr2_routine(b: torch.Tensor):
+    """Lockstep routine form of :func:`cholesky_qr2`: both passes are queued, then the two factorizations'
+    status is read in one host round (yielded); a Gram that is not positive definite in either pass gives the
+    Householder basis, exactly as when each pass is checked on the spot (a failed first pass never reaches the
+    second's result)."""
     STATS["cholesky_qr2"] += 1
     q = b.float()
+    flags = []
     for _ in range(2):
         g = gram(q).double()
         factor, info = torch.linalg.cholesky_ex(g, upper=True)
-        if int(info) != 0 or not bool(torch.isfinite(factor).all()):
-            STATS["qr_fallbacks"] += 1
-            return householder_qr(b)
+        flags.append((info != 0) | ~torch.isfinite(factor).all())
         q = trsm_right_upper(q, factor)
+    (bad,) = yield (torch.stack(flags).any(),)
+    if bad:
+        STATS["qr_fallbacks"] += 1
+        return householder_qr(b)
     return q
 
 
-__all__ = ["STATS", "cholesky_qr2", "gram", "householder_qr", "mm", "trsm_right_upper"]
+def cholesky_qr2(b: torch.Tensor) -> torch.Tensor:
+    """Column-orthonormal basis of ``b[C, k]`` by two CholeskyQR passes (FP64 Cholesky of the FP32-accurate
+    Gram, FP32-accurate triangular solve); Householder QR when a Gram is not positive definite."""
+    from .deferred_reads import run_one
+    return run_one(cholesky_qr2_routine(b))
+
+
+__all__ = ["STATS", "cholesky_qr2", "cholesky_qr2_routine", "gram", "householder_qr", "mm", "trsm_right_upper"]

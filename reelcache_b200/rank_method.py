@@ -35,6 +35,7 @@ import time
 from dataclasses import dataclass, field, replace
 from typing import Any, Mapping
 
+import numpy as np
 import torch
 
 from . import exact_blas
@@ -167,15 +168,32 @@ def _sum_squares(x: torch.Tensor, r: torch.Tensor | None = None) -> torch.Tensor
     return torch.stack([xf.square().sum(), resid])
 
 
-def _rr_eigh(t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+def _jacobi_batch(mats: list[torch.Tensor]) -> list[tuple[torch.Tensor, torch.Tensor]]:
+    """One Jacobi launch for a round's Rayleigh-Ritz problems of one size (each matrix is solved by its own
+    CTA, so a matrix's eigenpairs do not depend on the batch it rides in). Returns per matrix the FP32
+    ascending values, row eigenvectors and the convergence status (0 converged)."""
+    from .gpu_fitting import _count
+    from .ops.fitter import jacobi_eigh
+    values, vectors, info, _ = jacobi_eigh(torch.stack([m.float() for m in mats]))
+    _count("jacobi_calls")
+    _count("jacobi_matrices", len(mats))
+    return [(values[i], vectors[i], info[i]) for i in range(len(mats))]
+
+
+def _rr_eigh_routine(t: torch.Tensor):
     """Descending eigenvalues (FP64) and column eigenvectors (FP32) of a symmetric ``k x k`` matrix: the
-    sm_100a Jacobi kernel on CUDA for k <= 160, FP64 LAPACK/cuSOLVER otherwise."""
-    from .gpu_fitting import JACOBI_MAX_N, jacobi_rows_eigh
+    sm_100a Jacobi kernel on CUDA for k <= 160 (batched with the round's other problems of the same size; an
+    unconverged matrix is re-solved by LAPACK / cuSOLVER), FP64 LAPACK/cuSOLVER otherwise."""
+    from .deferred_reads import BatchedCall
+    from .gpu_fitting import JACOBI_MAX_N
     if t.is_cuda and t.shape[0] <= JACOBI_MAX_N:
         from .ops import _ext
         if _ext.available():
-            values, rows = jacobi_rows_eigh(t.float().unsqueeze(0))
-            return values[0].flip(0).double(), rows[0].flip(0).t().contiguous()
+            values, columns, info = yield BatchedCall(("rr_eigh", t.shape[0], t.device), _jacobi_batch, t)
+            (status,) = yield (info,)
+            if status != 0:
+                values, columns = torch.linalg.eigh(t.float())
+            return values.flip(0).double(), columns.flip(1).contiguous()
     values, vectors = torch.linalg.eigh(t.double())
     order = torch.argsort(values, descending=True)
     return values[order], vectors[:, order].float()
@@ -195,13 +213,13 @@ def orthogonalizer_scope(name: str):
         _ORTHO.name = previous
 
 
-def _orthonormalize(b: torch.Tensor) -> torch.Tensor:
+def _orthonormalize_routine(b: torch.Tensor):
     """Column-orthonormal basis of ``b[C, k]``: CholeskyQR2 (``batched``: FP32-accurate tensor-core Grams and
-    triangular solves, Householder only when a Gram is not positive definite) or Householder QR in FP32; signs
-    canonical (positive diagonal of R) either way."""
+    triangular solves, one host round for both passes' status, Householder only when a Gram is not positive
+    definite) or Householder QR in FP32; signs canonical (positive diagonal of R) either way."""
     if getattr(_ORTHO, "name", "batched") == "householder":
         return exact_blas.householder_qr(b)
-    return exact_blas.cholesky_qr2(b)
+    return (yield from exact_blas.cholesky_qr2_routine(b))
 
 
 def _generator(seed: int, key: MatrixKey, salt: str) -> torch.Generator:
@@ -211,21 +229,22 @@ def _generator(seed: int, key: MatrixKey, salt: str) -> torch.Generator:
     return gen
 
 
-def anchor_sketch(g: torch.Tensor, m: int, q: int, gen: torch.Generator) -> torch.Tensor:
+def anchor_sketch_routine(g: torch.Tensor, m: int, q: int, gen: torch.Generator):
     """``orth(G^(q+1) Omega)`` with a private Gaussian ``Omega[C, m]``."""
     channels = g.shape[0]
     omega = torch.randn((channels, min(m, channels)), generator=gen, dtype=torch.float32).to(g.device)
-    s = _orthonormalize(exact_blas.mm(g, omega))
+    s = yield from _orthonormalize_routine(exact_blas.mm(g, omega))
     for _ in range(q):
-        s = _orthonormalize(exact_blas.mm(g, s))
+        s = yield from _orthonormalize_routine(exact_blas.mm(g, s))
     return s
 
 
-def span_energy(g: torch.Tensor, s: torch.Tensor, total: float) -> float:
+def span_energy_routine(g: torch.Tensor, s: torch.Tensor, total: float):
     """``||A S||^2 / ||A||^2 = trace(S^T G S) / trace(G)`` for column-orthonormal ``S``."""
     if total <= 0:
         return 1.0
-    return float((exact_blas.mm(g, s) * s).sum(dtype=torch.float64)) / total
+    (value,) = yield ((exact_blas.mm(g, s) * s).sum(dtype=torch.float64),)
+    return value / total
 
 
 def fp16_rows(directions: torch.Tensor) -> torch.Tensor:
@@ -233,7 +252,7 @@ def fp16_rows(directions: torch.Tensor) -> torch.Tensor:
     return directions.t().contiguous().to(torch.float16)
 
 
-def stored_energy(x: torch.Tensor, rows: torch.Tensor, total: float, tile_rows: int = 16384) -> tuple[float, torch.Tensor]:
+def stored_energy_routine(x: torch.Tensor, rows: torch.Tensor, total: float, tile_rows: int = 16384):
     """Energy of the actual stored representation: FP16 ``rows``, FP32 ``P = A Q^T``, direct residual
     ``||A - P Q||^2`` accumulated in FP64 over row tiles. Returns (energy, P)."""
     q = rows.float()
@@ -248,7 +267,8 @@ def stored_energy(x: torch.Tensor, rows: torch.Tensor, total: float, tile_rows: 
         residual = part if residual is None else residual + part
     if total <= 0:
         return 1.0, coefficients
-    return 1.0 - float(residual) / total, coefficients
+    (value,) = yield (residual,)
+    return 1.0 - value / total, coefficients
 
 
 def _bucketed(rank: float, bucket: int, limit: int) -> int:
@@ -264,8 +284,8 @@ class Fit:
     exact: bool                   # True when the directions span the full width
 
 
-def fit_directions(g: torch.Tensor, wanted: int, cfg: RankMethodConfig, gen: torch.Generator,
-                   warm: torch.Tensor | None = None) -> Fit:
+def fit_directions_routine(g: torch.Tensor, wanted: int, cfg: RankMethodConfig, gen: torch.Generator,
+                           warm: torch.Tensor | None = None):
     """Energy-ordered candidate directions of a Gram matrix."""
     channels = g.shape[0]
     k = min(channels, wanted + cfg.topk_margin)
@@ -277,14 +297,34 @@ def fit_directions(g: torch.Tensor, wanted: int, cfg: RankMethodConfig, gen: tor
     if warm is not None:
         cols = min(k, warm.shape[1])
         start[:, :cols] = warm[:, :cols]
-    b = _orthonormalize(exact_blas.mm(g, start))
+    b = yield from _orthonormalize_routine(exact_blas.mm(g, start))
     for _ in range(cfg.topk_steps):
-        b = _orthonormalize(exact_blas.mm(g, b))
+        b = yield from _orthonormalize_routine(exact_blas.mm(g, b))
     t = exact_blas.mm(b.t(), exact_blas.mm(g, b))
     t = 0.5 * (t + t.t())
-    values, vectors = _rr_eigh(t)
+    values, vectors = yield from _rr_eigh_routine(t)
     directions = exact_blas.mm(b, vectors)
-    return Fit(_orthonormalize(directions), values.clamp_min(0), False)
+    directions = yield from _orthonormalize_routine(directions)
+    return Fit(directions, values.clamp_min(0), False)
+
+
+def _sync(routine_factory):
+    """The blocking form of a routine (one host read per yield)."""
+    from .deferred_reads import run_one
+
+    def call(*args, **kwargs):
+        return run_one(routine_factory(*args, **kwargs))
+    call.__name__ = routine_factory.__name__.replace("_routine", "")
+    call.__doc__ = routine_factory.__doc__
+    return call
+
+
+anchor_sketch = _sync(anchor_sketch_routine)
+span_energy = _sync(span_energy_routine)
+stored_energy = _sync(stored_energy_routine)
+fit_directions = _sync(fit_directions_routine)
+_rr_eigh = _sync(_rr_eigh_routine)
+_orthonormalize = _sync(_orthonormalize_routine)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -326,7 +366,7 @@ def _predict(view: RegistryView | None, pkey: PredictorKey, anchor: float, targe
     return _bucketed(use.predicted_rank, cfg.bucket, limit), x, use.predicted_rank, use
 
 
-def _fresh(x: torch.Tensor, g: torch.Tensor, total: float, target: float, cfg: RankMethodConfig,
+def _fresh_routine(x: torch.Tensor, g: torch.Tensor, total: float, target: float, cfg: RankMethodConfig,
            view: RegistryView | None, pkey: PredictorKey, key: MatrixKey, *, inherited: torch.Tensor | None = None,
            full_x: torch.Tensor | None = None, full_total: float | None = None, full_target: float | None = None):
     """Fit ``x`` (the matrix, or the residual after inherited rows) to ``target``; when ``inherited``
@@ -335,15 +375,14 @@ def _fresh(x: torch.Tensor, g: torch.Tensor, total: float, target: float, cfg: R
     Returns (rows_new [k, C] FP16, energy_report, coefficients, observation_fields, details)."""
     channels = x.shape[1]
     gen = _generator(cfg.seed, key, pkey.regime)
-    sketch = anchor_sketch(g, cfg.anchor_rank, cfg.power_iterations, gen)
-    anchor = min(max(span_energy(g, sketch, total), 0.0), 1.0 - 1e-12)
+    sketch = yield from anchor_sketch_routine(g, cfg.anchor_rank, cfg.power_iterations, gen)
+    anchor = min(max((yield from span_energy_routine(g, sketch, total)), 0.0), 1.0 - 1e-12)
     limit = channels - (0 if inherited is None else inherited.shape[0])
     predicted, xval, predicted_rank, use = _predict(view, pkey, anchor, target, cfg, limit)
-    fit = fit_directions(g, predicted, cfg, gen, warm=sketch)
-    cumulative = torch.cumsum(fit.energies, 0) / max(total, 1e-300)
+    fit = yield from fit_directions_routine(g, predicted, cfg, gen, warm=sketch)
+    (cumulative,) = yield (torch.cumsum(fit.energies, 0) / max(total, 1e-300),)   # host FP64 vector
     available = fit.directions.shape[1]
-    ideal_rank = int(torch.searchsorted(cumulative, torch.tensor(target - cfg.decision_band, dtype=torch.float64,
-                                                                 device=cumulative.device)).item()) + 1
+    ideal_rank = int(np.searchsorted(cumulative, target - cfg.decision_band, side="left")) + 1
     ideal_rank = min(ideal_rank, available)
     verify_x = x if inherited is None else full_x
     verify_total = total if inherited is None else full_total
@@ -361,7 +400,7 @@ def _fresh(x: torch.Tensor, g: torch.Tensor, total: float, target: float, cfg: R
     grown = 0
     while True:
         new, rows = rows_at(rank)
-        energy, coefficients = stored_energy(verify_x, rows, verify_total, cfg.tile_rows)
+        energy, coefficients = yield from stored_energy_routine(verify_x, rows, verify_total, cfg.tile_rows)
         if energy >= verify_target - cfg.decision_band or rank >= available:
             break
         rank = min(rank + cfg.bucket, available)
@@ -385,18 +424,19 @@ def _bytes_estimate(tokens: int, rank: int, new_rows: int, channels: int, cfg: R
     return tokens * rank * per_value + new_rows * channels * 2 + 8 * rank + cfg.metadata_bytes_estimate
 
 
-def plan_matrix(matrix: torch.Tensor, context: TensorContext, cfg: RankMethodConfig, view: RegistryView | None,
-                binding: ActiveBasisBinding, inherited_rows: torch.Tensor | None, *, entry: Any = None,
-                source_id: str | None = None, chunk_id: str = "chunk", model_fingerprint: str | None = None
-                ) -> MatrixPlan:
-    """Plan one matrix against its lineage's active binding (``inherited_rows``: its stored view)."""
+def plan_matrix_routine(matrix: torch.Tensor, context: TensorContext, cfg: RankMethodConfig,
+                        view: RegistryView | None, binding: ActiveBasisBinding, inherited_rows: torch.Tensor | None, *,
+                        entry: Any = None, source_id: str | None = None, chunk_id: str = "chunk",
+                        model_fingerprint: str | None = None):
+    """Plan one matrix against its lineage's active binding (``inherited_rows``: its stored view). A lockstep
+    routine: it yields each group of device values whose host copies its next decision needs."""
     started = time.perf_counter()
     entry = context.key if entry is None else entry
     key = context.key
     x = matrix.reshape(context.token_count, context.channels)
     tokens, channels = x.shape
     target = cfg.targets.for_target(key.target)
-    total = float(_sum_squares(x)[0])
+    (total,) = yield (_sum_squares(x)[0],)
     fingerprint = model_fingerprint or context.model.fingerprint
     pkey_fresh = PredictorKey(fingerprint, key.layer, key.target, tokens, channels, cfg.solver, "sketch", "fresh")
     pkey_resid = replace(pkey_fresh, regime="residual")
@@ -428,7 +468,7 @@ def plan_matrix(matrix: torch.Tensor, context: TensorContext, cfg: RankMethodCon
             order = torch.argsort(values, descending=True)
             rows = fp16_rows(vectors[:, order[:min(fixed, channels)]].float())
             reason = "fixed_rank_policy"
-        energy, coefficients = stored_energy(x, rows, total, cfg.tile_rows)
+        energy, coefficients = yield from stored_energy_routine(x, rows, total, cfg.tile_rows)
         report = EnergyReport(target, min(energy, 1.0), min(energy, 1.0), None, None, 0, rows.shape[0],
                               diagnostic_full_width=True)
         return MatrixPlan(entry, context, "fresh", rows, rows, None, rows.shape[0], coefficients, report, None,
@@ -438,14 +478,14 @@ def plan_matrix(matrix: torch.Tensor, context: TensorContext, cfg: RankMethodCon
     # -------- inherit / certify / augment --------
     if cfg.reuse and inherited_rows is not None and binding.version_ref is not None:
         inherited_rows = inherited_rows.to(x.device)
-        energy_all, coefficients_all = stored_energy(x, inherited_rows, total, cfg.tile_rows)
+        energy_all, coefficients_all = yield from stored_energy_routine(x, inherited_rows, total, cfg.tile_rows)
         if energy_all >= target - cfg.decision_band:
             # shortest bucket-aligned prefix that verifies
             rank = inherited_rows.shape[0]
             candidates = list(range(cfg.bucket, rank, cfg.bucket)) + [rank]
             chosen, chosen_energy, chosen_p = rank, energy_all, coefficients_all
             for candidate in candidates:
-                energy_c, p_c = stored_energy(x, inherited_rows[:candidate], total, cfg.tile_rows)
+                energy_c, p_c = yield from stored_energy_routine(x, inherited_rows[:candidate], total, cfg.tile_rows)
                 if energy_c >= target - cfg.decision_band:
                     chosen, chosen_energy, chosen_p = candidate, energy_c, p_c
                     break
@@ -457,20 +497,20 @@ def plan_matrix(matrix: torch.Tensor, context: TensorContext, cfg: RankMethodCon
         # augment: fit the residual at (E_t - e) / (1 - e)
         q = inherited_rows.float()
         residual = x.float() - exact_blas.mm(coefficients_all, q)
-        r_total = float(_sum_squares(residual)[0])
+        (r_total,) = yield (_sum_squares(residual)[0],)
         residual_target = min(max((target - energy_all) / max(1.0 - energy_all, 1e-300), 1e-6), 1.0)
         rg = gram(residual)
-        new, report, coefficients, fields, details = _fresh(
+        new, report, coefficients, fields, details = yield from _fresh_routine(
             residual, rg, r_total, residual_target, cfg, view, pkey_resid, key, inherited=inherited_rows,
             full_x=x, full_total=total, full_target=target)
         # re-orthogonalize the new rows against the inherited span (two Gram-Schmidt passes in FP32)
         w = new.float()
         for _ in range(2):
             w = w - exact_blas.mm(exact_blas.mm(w, q.t()), q)
-        w = _orthonormalize(w.t()).t()
+        w = (yield from _orthonormalize_routine(w.t())).t()
         new = w.to(torch.float16)
         rows = torch.cat([inherited_rows, new], 0)
-        energy, coefficients = stored_energy(x, rows, total, cfg.tile_rows)
+        energy, coefficients = yield from stored_energy_routine(x, rows, total, cfg.tile_rows)
         report = replace(report, stored_factor_energy=min(energy, 1.0), ideal_subspace_energy=min(energy, 1.0),
                          rank_view=rows.shape[0])
         augment_plan = MatrixPlan(entry, context, "augment", rows, new, binding.version_ref, rows.shape[0],
@@ -501,7 +541,8 @@ def plan_matrix(matrix: torch.Tensor, context: TensorContext, cfg: RankMethodCon
             augment_plan.details.update(refit_estimate=estimate, planner_seconds=time.perf_counter() - started)
             return augment_plan
         g = gram(x)
-        new, report, coefficients, fields, details = _fresh(x, g, total, target, cfg, view, pkey_fresh, key)
+        new, report, coefficients, fields, details = yield from _fresh_routine(x, g, total, target, cfg, view,
+                                                                               pkey_fresh, key)
         return MatrixPlan(entry, context, "refit", new, new, None, new.shape[0], coefficients, report,
                           observation_of(fields, pkey_fresh),
                           ActiveBasisBinding(None, 0, None, new.shape[0], chunk_id),
@@ -509,30 +550,46 @@ def plan_matrix(matrix: torch.Tensor, context: TensorContext, cfg: RankMethodCon
 
     # -------- fresh fit --------
     g = gram(x) if g is None else g
-    new, report, coefficients, fields, details = _fresh(x, g, total, target, cfg, view, pkey_fresh, key)
+    new, report, coefficients, fields, details = yield from _fresh_routine(x, g, total, target, cfg, view, pkey_fresh,
+                                                                           key)
     details["planner_seconds"] = time.perf_counter() - started
     return MatrixPlan(entry, context, "fresh", new, new, None, new.shape[0], coefficients, report,
                       observation_of(fields, pkey_fresh), ActiveBasisBinding(None, 0, None, new.shape[0], chunk_id),
                       details)
 
 
+plan_matrix = _sync(plan_matrix_routine)
+
+
 def plan_chunk(matrices: Mapping[Any, torch.Tensor], contexts: Mapping[Any, TensorContext], cfg: RankMethodConfig,
                view: RegistryView | None, bindings: Mapping[Any, ActiveBasisBinding],
                inherited: Mapping[Any, torch.Tensor | None], *, chunk_id: str = "chunk",
                device: Any = None) -> dict[Any, MatrixPlan]:
-    """Plan every matrix of a chunk (entries in canonical order)."""
+    """Plan every matrix of a chunk (entries in canonical order), ``cfg.batch_size`` matrices in lockstep: the
+    matrices of a group run their decision routines together, so each round of host reads (an energy, a
+    factorization status, a cumulative spectrum) is one device-to-host transfer for the whole group, and the
+    round's Rayleigh-Ritz problems of one size share one Jacobi launch. Each matrix's kernels, host values and
+    decisions are those of planning it alone (``batch_size=1``)."""
+    from .deferred_reads import run_lockstep
+    entries = sorted(contexts, key=_entry_order)
+    plans: dict[Any, MatrixPlan] = {}
     with orthogonalizer_scope(cfg.orthogonalizer):
-        return _plan_chunk(matrices, contexts, cfg, view, bindings, inherited, chunk_id=chunk_id, device=device)
-
-
-def _plan_chunk(matrices, contexts, cfg, view, bindings, inherited, *, chunk_id, device):
-    plans = {}
-    for entry in sorted(contexts, key=lambda e: (getattr(e, "layer", None) if isinstance(e, MatrixKey) else e[0].layer,
-                                                  getattr(e, "target", None) if isinstance(e, MatrixKey) else e[0].target,
-                                                  "" if isinstance(e, MatrixKey) else e[1])):
-        matrix = matrices[entry]
-        if device is not None:
-            matrix = matrix.to(device)
-        plans[entry] = plan_matrix(matrix, contexts[entry], cfg, view, bindings.get(entry, ActiveBasisBinding()),
-                                   inherited.get(entry), entry=entry, chunk_id=chunk_id)
+        for start in range(0, len(entries), cfg.batch_size):
+            group = entries[start:start + cfg.batch_size]
+            routines = []
+            for entry in group:
+                matrix = matrices[entry]
+                if device is not None:
+                    matrix = matrix.to(device)
+                routines.append(plan_matrix_routine(matrix, contexts[entry], cfg, view,
+                                                    bindings.get(entry, ActiveBasisBinding()), inherited.get(entry),
+                                                    entry=entry, chunk_id=chunk_id))
+            for entry, plan in zip(group, run_lockstep(routines)):
+                plans[entry] = plan
     return plans
+
+
+def _entry_order(e) -> tuple:
+    if isinstance(e, MatrixKey):
+        return e.layer, e.target, ""
+    return e[0].layer, e[0].target, e[1]
