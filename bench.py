@@ -181,6 +181,7 @@ def build_archive(args, device):
     sampler = ChunkGenerator(model, cache, text_kv, seed=2)
     nodes = []
     archive_seconds = 0.0
+    phases: dict = {}
     ranks = []
     for index in range(args.chunks):
         latents = sampler.denoise(index)
@@ -199,10 +200,13 @@ def build_archive(args, device):
         commit = runtime.commit_node("session", f"chunk-{index}", captured, contexts, method=method, device=device,
                                      options=options)
         archive_seconds += time.perf_counter() - started
+        for phase, seconds in commit.timings.items():
+            if isinstance(seconds, (int, float)):
+                phases[phase] = phases.get(phase, 0.0) + seconds
         ranks.append(commit.plan["mean_rank"])
         nodes.append(commit.node_ref)
     return {"cfg": cfg, "model": model, "runtime": runtime, "nodes": nodes, "text_kv": text_kv, "context": context,
-            "archive_seconds": archive_seconds, "ranks": ranks, "store_root": root}
+            "archive_seconds": archive_seconds, "archive_phases": phases, "ranks": ranks, "store_root": root}
 
 
 def write_rank_profile(restorer, target, cfg):
@@ -361,6 +365,8 @@ def run_ours(args, rank, world, local):
                       "ms_per_step": round(ms_device16, 4), "precision": "fp16"},
         "ttfc_p50_ms": round(ttfc_p50, 2), "first_step_without_restore_ms": round(first_step_ms, 2),
         "archived_chunks_per_s": round(archived_per_s, 4),
+        "archive_phase_ms_per_chunk": {k: round(1e3 * v / max(args.chunks, 1), 2)
+                                       for k, v in state.get("archive_phases", {}).items()},
         "mean_rank": round(float(np.mean(state["ranks"])), 1), "gpu_launches": launches_per_step,
         "clocks": clock_summary, "restored_bytes_per_step": restored_bytes,
     }

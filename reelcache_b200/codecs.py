@@ -53,15 +53,59 @@ def default_stream_codec() -> str:
 # ---------------------------------------------------------------------------------------------
 
 
+_RAW_PAYLOAD = "tensor.bin"
+_COEFFICIENT_PAYLOAD = "coefficients.f32"
+
+
+def _payload_descriptor(payload: bytes, dtype: str, shape) -> dict[str, Any]:
+    return {"bytes": len(payload), "dtype": dtype, "sha256": hashlib.sha256(payload).hexdigest(),
+            "shape": [int(v) for v in shape]}
+
+
 def encode_raw(matrix: torch.Tensor, context: TensorContext) -> EncodedTensor:
-    """RAW packet: the canonical matrix bit for bit."""
+    """RAW packet: the canonical matrix bit for bit, in the ``reelcache.tensor.v1`` layout both implementations
+    read (one ``tensor.bin`` payload described by its bytes, dtype, SHA-256 and shape; the factorization fields
+    present and null)."""
     if tuple(matrix.shape) != context.shape:
         raise ConfigurationError("matrix shape differs from its context")
     payload = tensor_bytes(matrix)
-    metadata = {"schema": TENSOR_V1, "representation": "raw", "context": context.to_dict(),
-                "dtype": str(matrix.dtype).removeprefix("torch."), "shape": list(matrix.shape),
-                "sha256": hashlib.sha256(payload).hexdigest()}
-    return EncodedTensor(metadata, {"values": payload}, metrics={"bytes": len(payload)})
+    dtype = str(matrix.dtype).removeprefix("torch.")
+    codec = _portable_codec(CodecSpec("raw"))
+    metadata = {"schema": TENSOR_V1, "kind": "raw", "factorization_domain": "raw", "byte_order": "little",
+                "codec": codec, "context": context.to_dict(), "dtype": dtype, "shape": list(matrix.shape),
+                "payloads": {_RAW_PAYLOAD: _payload_descriptor(payload, dtype, matrix.shape)},
+                "basis": None, "coefficient_shape": None, "normalization": None, "video": None,
+                "decoded_coefficients_sha256": None}
+    metrics = {"payload_bytes": len(payload), "source_bytes": len(payload), "basis_bytes": 0,
+               "reuse_reason": "raw", "reuse_accepted": False}
+    return EncodedTensor(metadata, {_RAW_PAYLOAD: payload}, metrics=metrics)
+
+
+def _checked_payload(encoded: EncodedTensor, name: str) -> bytes:
+    payload = encoded.payloads[name]
+    described = encoded.metadata.get("payloads", {}).get(name)
+    digest = encoded.metadata.get("sha256") if described is None else described["sha256"]
+    if hashlib.sha256(payload).hexdigest() != digest:
+        raise IntegrityError(f"packet payload {name} differs from its digest")
+    return payload
+
+
+def decode_v1(encoded: EncodedTensor, *, device: Any = "cpu") -> tuple[torch.Tensor, torch.Tensor | None]:
+    """A ``reelcache.tensor.v1`` packet: ``(values, None)`` for RAW (``tensor.bin``, or the ``values`` payload of
+    stores written before the layout was aligned), ``(coefficients FP32 [N, r], None)`` for a per-matrix SVD
+    packet (``coefficients.f32``; its basis is the record's version prefix)."""
+    meta = encoded.metadata
+    kind = meta.get("kind", meta.get("representation", "raw"))
+    if kind == "raw":
+        name = _RAW_PAYLOAD if _RAW_PAYLOAD in encoded.payloads else "values"
+        payload = _checked_payload(encoded, name)
+        return tensor_from_bytes(payload, dtype=meta["dtype"], shape=meta["shape"], device=device), None
+    if kind == "svd":
+        payload = _checked_payload(encoded, _COEFFICIENT_PAYLOAD)
+        shape = meta["payloads"][_COEFFICIENT_PAYLOAD]["shape"]
+        values = np.frombuffer(payload, dtype="<f4").reshape(shape)
+        return torch.from_numpy(values.copy()).to(device), None
+    raise UnsupportedError(f"tensor.v1 packets of kind {kind!r} are not decoded here")
 
 
 def quantize(coefficients: torch.Tensor, normalization: str = "per_channel", protected_fraction: float = 1.0):
@@ -80,7 +124,9 @@ def encode_factorized(coefficients: torch.Tensor, basis_view: bytes, context: Te
     rank = coefficients.shape[1]
     if spec.kind not in ("svd", "svd_hevc") or spec.rank != rank:
         raise ConfigurationError("factorized packets need an svd/svd_hevc spec at the coefficient rank")
-    stream_codec = stream_codec or ("raw8" if spec.kind == "svd" else default_stream_codec())
+    if spec.kind == "svd":
+        return _encode_svd_v1(coefficients, basis_view, context, spec, metrics)
+    stream_codec = stream_codec or default_stream_codec()
     if stream_codec not in STREAM_CODECS:
         raise ConfigurationError(f"stream codec must be one of {STREAM_CODECS}")
     pixels, affine, layout = quantize(coefficients, spec.normalization, spec.protected_fraction)
@@ -92,6 +138,35 @@ def encode_factorized(coefficients: torch.Tensor, basis_view: bytes, context: Te
                                  "sha256": hashlib.sha256(np.ascontiguousarray(pixels).tobytes()).hexdigest()}}
     payloads = {"stream": stream, "affine": np.ascontiguousarray(affine, dtype="<f4").tobytes()}
     return EncodedTensor(metadata, payloads, basis=basis_view, metrics=dict(metrics or {}, bytes=len(stream)))
+
+
+def _encode_svd_v1(coefficients: torch.Tensor, basis_view: bytes, context: TensorContext, spec: CodecSpec,
+                   metrics: Mapping[str, Any] | None) -> EncodedTensor:
+    """An SVD-only matrix: FP32 coefficients ``coefficients.f32`` in the ``reelcache.tensor.v1`` layout, the FP16
+    basis view described (``basis``) and stored as the record's version prefix."""
+    values = np.ascontiguousarray(coefficients.detach().to("cpu", torch.float32).numpy()).astype("<f4", copy=False)
+    payload = values.tobytes()
+    codec = _portable_codec(spec)
+    metadata = {"schema": TENSOR_V1, "kind": "svd", "factorization_domain": _domain(context),
+                "byte_order": "little", "codec": codec, "context": context.to_dict(),
+                "dtype": context.dtype, "shape": list(context.shape), "coefficient_shape": list(values.shape),
+                "payloads": {_COEFFICIENT_PAYLOAD: _payload_descriptor(payload, "float32", values.shape)},
+                "basis": descriptor(basis_view, values.shape[1], context.channels), "normalization": None,
+                "video": None, "decoded_coefficients_sha256": hashlib.sha256(payload).hexdigest()}
+    return EncodedTensor(metadata, {_COEFFICIENT_PAYLOAD: payload}, basis=basis_view,
+                         metrics=dict(metrics or {}, payload_bytes=len(payload)))
+
+
+def _domain(context: TensorContext) -> str:
+    """The factorization domain label of a matrix (factorized K is always the normalized pre-RoPE K)."""
+    return "normalized_pre_rope_k" if context.key.target == "K" else "direct_v"
+
+
+def _portable_codec(spec: CodecSpec) -> dict[str, Any]:
+    """The codec header a tensor packet records: the spec without run-local fields (the encoder path)."""
+    codec = spec.to_dict()
+    codec.pop("ffmpeg_path", None)
+    return codec
 
 
 def _encode_stream(pixels: np.ndarray, context: TensorContext, stream_codec: str, spec: CodecSpec) -> bytes:
@@ -144,9 +219,14 @@ def decode_tensor(encoded: EncodedTensor, *, device: Any = "cpu", dtype: torch.d
     """The canonical matrix of a packet: RAW bitwise; factorized ``dequantize(P) @ Q`` (FP32)."""
     meta = encoded.metadata
     if meta.get("schema") == TENSOR_V1:
-        values = tensor_from_bytes(encoded.payloads["values"], dtype=meta["dtype"], shape=meta["shape"], device=device)
-        if hashlib.sha256(encoded.payloads["values"]).hexdigest() != meta["sha256"]:
-            raise IntegrityError("RAW packet payload differs from its digest")
+        values, _ = decode_v1(encoded, device=device)
+        if meta.get("kind", "raw") == "svd":
+            if encoded.basis is None:
+                raise IntegrityError("factorized packets decode only with their attached basis view")
+            rank, channels = meta["basis"]["shape"]
+            basis = np.frombuffer(encoded.basis, dtype=np.float16).reshape(rank, channels)
+            values = values @ torch.from_numpy(basis.copy()).to(device).float()
+            return values.to(dtype)
         return values
     pixels, affine, layout = decode_coefficient_pixels(encoded)
     if encoded.basis is None:

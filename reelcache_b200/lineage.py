@@ -4,8 +4,8 @@ A lineage is a named head ref (``lineages/<id>``) over immutable nodes. Nodes, e
 and packets are content-addressed manifests:
 
 * node     ``{"type": "node", "version": 1, "model", "node": ChunkNode, "commit": report}``
-* epoch    ``{"type": "epoch", "version": 1, "epoch": CacheEpoch}``
-* record   ``{"type": "record", "version": 1, "record": MatrixRecord}``
+* epoch    ``{"type": "cache_epoch", "version": 1, "model", "epoch": CacheEpoch}``
+* record   ``{"type": "matrix_record", "version": 1, "model", "record": MatrixRecord}``
 * packet   ``{"type": "packet", "version": 1, "model", "metadata", "payloads": {name: blob id},
              "metrics", "basis_storage", ...}``
 
@@ -39,6 +39,10 @@ from .types import (ActiveBasisBinding, CacheEpoch, ChunkNode, CodecSpec, Matrix
                     TensorContext, TokenRangeRecords, entry_order, entry_parts, json_copy)
 
 LINEAGE_PREFIX = "lineages/"
+#: Manifest ``type`` names each loader accepts: the names both implementations write (``cache_epoch``,
+#: ``matrix_record``), and the short names of stores this package wrote before the layouts were aligned.
+_MANIFEST_TYPES = {"node": ("node",), "epoch": ("cache_epoch", "epoch"), "record": ("matrix_record", "record"),
+                   "packet": ("packet",)}
 _TELEMETRY_KEYS = ("timings", "seconds", "planner_seconds", "started", "published")
 
 
@@ -86,8 +90,8 @@ class LineageRuntime:
 
     def put_record(self, record: MatrixRecord) -> str:
         references = [record.packet_ref] + ([record.basis_version_ref] if record.basis_version_ref else [])
-        return self.store.put_manifest({"type": "record", "version": 1, "record": record.to_dict()},
-                                       references=sorted(set(references)))
+        return self.store.put_manifest({"type": "matrix_record", "version": 1, "model": self.model.to_dict(),
+                                        "record": record.to_dict()}, references=sorted(set(references)))
 
     def _put_epoch(self, epoch: CacheEpoch) -> str:
         references = [epoch.parent_epoch_ref] if epoch.parent_epoch_ref else []
@@ -95,8 +99,8 @@ class LineageRuntime:
             references.extend(ref for _, ref in item.records)
             if item.packet_ref:
                 references.append(item.packet_ref)
-        return self.store.put_manifest({"type": "epoch", "version": 1, "epoch": epoch.to_dict()},
-                                       references=sorted(set(references)))
+        return self.store.put_manifest({"type": "cache_epoch", "version": 1, "model": self.model.to_dict(),
+                                        "epoch": epoch.to_dict()}, references=sorted(set(references)))
 
     def _put_node(self, node: ChunkNode, commit: Mapping[str, Any]) -> str:
         references = [node.parent_ref, node.epoch_ref, node.execution_state_ref, node.packet_ref,
@@ -111,8 +115,10 @@ class LineageRuntime:
         if hit is not None:
             return hit
         data = self.store.get_manifest(ref)
-        if data.get("type") != kind or data.get("version") != 1:
+        if data.get("type") not in _MANIFEST_TYPES[kind] or data.get("version") != 1:
             raise IntegrityError(f"{ref} is not a {kind} manifest")
+        if "model" in data and kind in ("epoch", "record") and ModelIdentity.from_dict(data["model"]) != self.model:
+            raise IntegrityError(f"{kind} manifest {ref} belongs to another model")
         if kind == "node":
             if ModelIdentity.from_dict(data["model"]) != self.model:
                 raise IntegrityError("node belongs to another model")
@@ -534,10 +540,16 @@ class LineageRuntime:
                 from .types import EncodedTensor
                 values = codecs.decode_tensor(EncodedTensor(packet["metadata"], blobs), device=device).float()
             elif record.codec.kind == "svd":
-                if record.packet_ref not in packs:
-                    packs[record.packet_ref] = self.factor_pack(record.packet_ref)[1]
-                factors = packs[record.packet_ref].factors(record.decision["packet"]["tile"])
-                coefficients = torch.from_numpy(factors.astype(np.float32)).to(device)
+                if packet["metadata"].get("schema") == codecs.TENSOR_V1:
+                    # a per-matrix SVD packet: FP32 coefficients, the basis is the record's version prefix
+                    blobs = {name: self.store.get(ref) for name, ref in packet["payloads"].items()}
+                    from .types import EncodedTensor
+                    coefficients, _ = codecs.decode_v1(EncodedTensor(packet["metadata"], blobs), device=device)
+                else:
+                    if record.packet_ref not in packs:
+                        packs[record.packet_ref] = self.factor_pack(record.packet_ref)[1]
+                    factors = packs[record.packet_ref].factors(record.decision["packet"]["tile"])
+                    coefficients = torch.from_numpy(factors.astype(np.float32)).to(device)
                 basis = self.basis.assemble(record.basis_version_ref, record.rank_view).to(device).float()
                 values = coefficients @ basis
             else:

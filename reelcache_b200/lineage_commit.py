@@ -206,8 +206,9 @@ class CommitJob:
         spec = self.method.codec
         for staged in self.tiles:
             for tile in staged:
-                if spec.kind == "svd":  # SVD-only baseline: FP16 factors, no quantization
-                    tile.factors = tile.plan.coefficients.detach().to(torch.float16).cpu().numpy()
+                if spec.kind == "svd":  # SVD-only baseline: FP16 factors (FP32 per matrix), no quantization
+                    dtype = torch.float16 if self.options.packed else torch.float32
+                    tile.factors = tile.plan.coefficients.detach().to(dtype).cpu().numpy()
                     tile.plan.coefficients = None
                     continue
                 pixels, affine, layout = codecs.quantize(tile.plan.coefficients, spec.normalization,
@@ -232,7 +233,13 @@ class CommitJob:
                               "pixels": tile.pixels, "affine": tile.affine, "normalization": tile.normalization,
                               "basis": codecs.descriptor(view_bytes, rank, tile.context.channels),
                               "coefficients": tile.factors})
-            if spec.kind == "svd":
+            if spec.kind == "svd" and not self.options.packed:
+                # one reelcache.tensor.v1 packet per matrix (FP32 coefficients, basis = the version prefix)
+                self.packs.append([codecs.encode_factorized(torch.from_numpy(t["coefficients"]),
+                                                            tile.plan.rows.detach().cpu().contiguous().numpy().tobytes(),
+                                                            t["context"], t["codec"])
+                                   for t, tile in zip(tiles, staged)])
+            elif spec.kind == "svd":
                 self.packs.append(codecs.encode_factor_pack(tiles))
             else:
                 self.packs.append(codecs.encode_node_pack(tiles, stream_codec=self.options.stream_codec,
@@ -271,8 +278,9 @@ class CommitJob:
                         new_binding = binding
                     rate_identity = canonical_digest({"codec": spec.to_dict(), "stream": self.options.stream_codec,
                                                       "shape": list(tile.context.shape)})
-                    # measured stream bytes per coefficient value of this pack
-                    rate = max(pack.metadata["stream_bytes"] / max(pack.metadata["raw_bytes"], 1), 1e-9)
+                    # measured stream bytes per coefficient value of this pack (FP32 per-matrix packets: 4)
+                    rate = 4.0 if isinstance(pack, list) else \
+                        max(pack.metadata["stream_bytes"] / max(pack.metadata["raw_bytes"], 1), 1e-9)
                     if new_binding.version_ref is not None and new_binding.fresh_rank is not None:
                         new_binding = ActiveBasisBinding(new_binding.version_ref, new_binding.total_rank,
                                                          new_binding.group_id, new_binding.fresh_rank,
@@ -280,6 +288,9 @@ class CommitJob:
                                                          new_binding.refit_debt)
                     version_refs[tile.entry] = ref
                     bindings[tile.entry] = new_binding
+                if isinstance(pack, list):
+                    results.append((None, self._store_per_matrix(staged, pack, version_refs)))
+                    continue
                 blobs = {name: store.put(value) for name, value in pack.payloads.items()}
                 basis_refs = sorted({r for r in version_refs.values() if r is not None})
                 packet_ref = runtime.put_content({"type": "packet", "version": 1, "model": runtime.model.to_dict(),
@@ -313,6 +324,29 @@ class CommitJob:
         self.stored = {"ranges": results, "bindings": bindings, "execution_state": state_ref}
         self.timings["store"] = time.perf_counter() - started
         return self
+
+    def _store_per_matrix(self, staged, packets, version_refs) -> dict:
+        """Per-matrix SVD packets and their records, in the layout both implementations read: a packet manifest
+        holds exactly ``type, version, model, metadata, payloads, metrics, basis_storage`` and references only its
+        payload blobs; the record names the basis version whose prefix the packet's basis descriptor covers."""
+        runtime, store, spec = self.runtime, self.runtime.store, self.method.codec
+        records = {}
+        for tile, packet in zip(staged, packets):
+            blobs = {name: store.put(value) for name, value in packet.payloads.items()}
+            packet_ref = runtime.put_content({"type": "packet", "version": 1, "model": runtime.model.to_dict(),
+                                              "metadata": packet.metadata, "payloads": blobs,
+                                              "metrics": json_copy(packet.metrics or {}),
+                                              "basis_storage": "external_version_prefix"},
+                                             field="metrics", references=sorted(blobs.values()))
+            plan = tile.plan
+            rank = plan.rank_view
+            codec = CodecSpec(**{**spec.to_dict(), "rank": rank, "inter_prediction": spec.inter_prediction})
+            energy = plan.energy if plan.energy.rank_view == rank else EnergyReport(
+                **{**plan.energy.to_dict(), "rank_view": rank})
+            record = MatrixRecord(tile.context, codec, packet_ref, version_refs[tile.entry], rank, energy, None,
+                                  json_copy(plan.decision_record()), stream=entry_parts(tile.entry)[1])
+            records[tile.entry] = runtime.put_record(record)
+        return records
 
     def release(self) -> None:
         if self.lease is not None:

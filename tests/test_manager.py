@@ -150,7 +150,7 @@ def test_quarantine_on_open(tmp_path, bases):
     bad_head = runtime.branch_info("bad")["head_id"]
     chunk = runtime.branch_info("bad")["chunk_manifests"][0]
     tensor = runtime.store.get_manifest(chunk)["matrices"][0]["tensor"]
-    payload = runtime.store.get_manifest(tensor)["encoded"]["payloads"]["values"]
+    payload = runtime.store.get_manifest(tensor)["encoded"]["payloads"]["tensor.bin"]
     runtime.close()
     path = runtime.store.path_for(payload)
     path.write_bytes(b"corrupt" + path.read_bytes()[7:])
