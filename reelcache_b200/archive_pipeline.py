@@ -39,6 +39,11 @@ from .lineage import LineageRuntime
 from .lineage_commit import ArchiveOptions
 from .rank_method import RankMethodConfig
 
+#: Seconds a pause waits by default for the planning node to reach a step boundary.
+PAUSE_ACK_TIMEOUT = 0.5
+#: Seconds after which open pauses expire and the fitter resumes (a pause never starves archival).
+PAUSE_MAX_SECONDS = 30.0
+
 
 @dataclass
 class ArchiveTicket:
@@ -114,6 +119,13 @@ class ArchivePipeline:
         self._closed = False
         self._counts = {"submitted": 0, "published": 0, "failed": 0, "cancelled": 0, "backpressure_waits": 0,
                         "backpressure_seconds": 0.0}
+        # pauses of the node on the GPU (pause_gpu_work): open pauses, whether the fitter sits at a boundary
+        self._pauses = 0
+        self._pause_opened = 0.0
+        self._fitter_paused = False
+        self._pause_counts = {"requests": 0, "acked": 0, "ack_timeouts": 0, "paused_seconds": 0.0, "expired": 0}
+        self._detaching: set[str] = set()
+        self._prewarm: list[dict] = []
         self._stream = None
         if self.device.type == "cuda" and dedicated_stream:
             self._stream = torch.cuda.Stream(self.device, priority=-1 if stream_priority is None else stream_priority)
@@ -172,6 +184,8 @@ class ArchivePipeline:
                 if self._closed and not self._queue:
                     return None
                 for ticket in list(self._queue):
+                    if ticket.lineage in self._detaching:
+                        continue
                     earlier = [t for t in self._tickets[ticket.lineage] if t.index < ticket.index]
                     if any(not t.done() for t in earlier):
                         continue  # planned after its predecessor is published
@@ -182,7 +196,29 @@ class ArchivePipeline:
                     return ticket
                 self.cv.wait(0.05)
 
+    def _step_boundary(self) -> None:
+        """Runs on the fitter thread between lockstep rounds of a node's planning: while a pause is open the node
+        waits here (no device read pending, no lock held), until the last pause closes, a caller drains, the
+        pipeline closes, or the pause outlives ``PAUSE_MAX_SECONDS``."""
+        with self.cv:
+            if not self._pauses:
+                return
+            self._fitter_paused = True
+            self.cv.notify_all()
+            started = time.monotonic()
+            while self._pauses and not self._closed and not self._drain_waiters:
+                if time.monotonic() - self._pause_opened > PAUSE_MAX_SECONDS:
+                    self._pauses = 0
+                    self._pause_counts["expired"] += 1
+                    break
+                self.cv.wait(0.01)
+            self._fitter_paused = False
+            self._pause_counts["paused_seconds"] += time.monotonic() - started
+            self.cv.notify_all()
+
     def _fitter_loop(self) -> None:
+        from .deferred_reads import set_step_hook
+        set_step_hook(lambda: self._step_boundary())
         while True:
             ticket = self._next()
             if ticket is None:
@@ -386,6 +422,103 @@ class ArchivePipeline:
                 self._defer -= 1
                 self.cv.notify_all()
 
+    @contextmanager
+    def pause_gpu_work(self, *, ack_timeout: float | None = None):
+        """Pause archival GPU work for the caller's section (a decode or another memory-critical section): queued
+        nodes are held like :meth:`defer_gpu_work`, and a node already planning stops at its next step boundary (a
+        round of its lockstep planner). Waits at most ``ack_timeout`` seconds (default ``PAUSE_ACK_TIMEOUT``) for
+        that boundary and yields ``{"acked", "ack_seconds", "inflight", "landed"}`` (``landed``: ``"idle"`` when no
+        node was on the GPU, ``"boundary"`` otherwise). The node resumes when the last pause exits, a caller
+        drains, or the pause outlives ``PAUSE_MAX_SECONDS``."""
+        timeout = PAUSE_ACK_TIMEOUT if ack_timeout is None else ack_timeout
+        if isinstance(timeout, bool) or not isinstance(timeout, (int, float)) or timeout < 0:
+            raise ConfigurationError("ack_timeout must be a nonnegative number of seconds")
+        started = time.monotonic()
+        with self.cv:
+            self._defer += 1
+            if not self._pauses:
+                self._pause_opened = started
+            self._pauses += 1
+            self._pause_counts["requests"] += 1
+            inflight = self._planning
+            while self._planning and not self._fitter_paused and time.monotonic() - started < timeout:
+                self.cv.wait(0.002)
+            acked = not self._planning or self._fitter_paused
+            self._pause_counts["acked" if acked else "ack_timeouts"] += 1
+            record = {"acked": acked, "ack_seconds": time.monotonic() - started, "inflight": inflight,
+                      "landed": "idle" if not inflight else ("boundary" if acked else None)}
+        try:
+            yield record
+        finally:
+            with self.cv:
+                self._defer -= 1
+                self._pauses = max(0, self._pauses - 1)
+                self.cv.notify_all()
+
+    def detach(self, lineage: str, new_lineage: str) -> dict:
+        """Hand ``lineage``'s unpublished chunks to a new lineage ``new_lineage`` that starts at its published head
+        (the cut): they keep publishing in order there and never move ``lineage``'s head (which the caller may then
+        rewind). Waits for the node in flight, if any, to publish first. Returns ``{"branch", "moved", "cut"}``."""
+        with self.cv:
+            if new_lineage in self._tickets and self._tickets[new_lineage]:
+                raise StateError(f"lineage {new_lineage} is already in the pipeline")
+            self._detaching.add(lineage)
+            try:
+                while any(t.state in ("planning", "encoding", "stored") for t in self._tickets.get(lineage, [])):
+                    self.cv.wait(0.01)
+                if lineage in self._failed:
+                    raise StateError(f"lineage {lineage} has a failed archival: {self._failed[lineage]}")
+                cut = self.runtime.lineage_head(lineage)
+                moved = [t for t in self._tickets.get(lineage, []) if not t.done()]
+                if not moved:
+                    return {"branch": new_lineage, "moved": [], "cut": cut}
+                self.runtime.fork_lineage(cut, new_lineage)
+                kept = [t for t in self._tickets[lineage] if t.done()]
+                self._tickets[lineage] = kept
+                self._generated[lineage] = len(kept)
+                for index, ticket in enumerate(moved):
+                    ticket.lineage, ticket.index = new_lineage, index
+                self._tickets[new_lineage] = list(moved)
+                self._generated[new_lineage] = len(moved)
+                return {"branch": new_lineage, "moved": [t.chunk_id for t in moved], "cut": cut}
+            finally:
+                self._detaching.discard(lineage)
+                self.cv.notify_all()
+
+    def prewarm(self, contexts: Mapping[Any, Any], *, seed: int = 0) -> dict:
+        """Pay the archive path's cold start before the first chunk: plan and finalize two synthetic chunks of
+        ``contexts``' geometry on the fitter's stream (fresh, then against the first's rows; nothing is stored or
+        learned), so kernels, library handles and allocator pools exist. Returns per-phase seconds."""
+        from .lineage_commit import ArchiveOptions  # noqa: F401 - the options the warm-up mirrors
+        from .rank_method import plan_chunk
+        from .types import ActiveBasisBinding
+        started = time.perf_counter()
+        gen = torch.Generator().manual_seed(seed)
+        matrices = {}
+        for entry, context in contexts.items():
+            rows, channels = context.token_count, context.channels
+            rank = max(1, min(32, channels // 4))
+            x = torch.randn(rows, rank, generator=gen) @ torch.randn(rank, channels, generator=gen)
+            matrices[entry] = (x + 1e-3 * torch.randn(rows, channels, generator=gen)).to(self.device)
+        report = {}
+        ctx = torch.cuda.stream(self._stream) if self._stream is not None else _Null()
+        with ctx:
+            clock = time.perf_counter()
+            first = plan_chunk(matrices, contexts, self.method, None, {}, {}, chunk_id="prewarm", device=self.device)
+            report["fresh_seconds"] = time.perf_counter() - clock
+            clock = time.perf_counter()
+            bindings = {e: ActiveBasisBinding("manifest:" + "0" * 64, p.rows.shape[0], "0" * 64) for e, p in
+                        first.items() if p.rows is not None and p.decision != "zero_input"}
+            plan_chunk(matrices, contexts, self.method, None, bindings, {e: first[e].rows for e in bindings},
+                       chunk_id="prewarm", device=self.device)
+            report["reuse_seconds"] = time.perf_counter() - clock
+            if self._stream is not None:
+                self._stream.synchronize()
+        report["total_seconds"] = time.perf_counter() - started
+        with self.cv:
+            self._prewarm.append(dict(report))
+        return report
+
     # -- generation holds ---------------------------------------------------------------------------------------
 
     def _held(self) -> bool:
@@ -451,7 +584,8 @@ class ArchivePipeline:
         with self.cv:
             return {**self._counts, "unpublished": self._unpublished(), "lineages": len(self._tickets),
                     "failed_lineages": sorted(self._failed), "encoders": self._encoders.stats(),
-                    "generation_defer": {**self._defer_counts, "open_holds": len(self._holds)}}
+                    "generation_defer": {**self._defer_counts, "open_holds": len(self._holds)},
+                    "fitter_pause": dict(self._pause_counts), "prewarm": list(self._prewarm)}
 
     def close(self, *, drain: bool = True, timeout: float | None = None) -> None:
         if drain:

@@ -47,6 +47,14 @@ def _host_value(values: np.ndarray, tensor: torch.Tensor):
 
 STATS = {"rounds": 0, "transfers": 0, "values": 0}
 _STATS_LOCK = threading.Lock()
+_STEP = threading.local()
+
+
+def set_step_hook(hook) -> None:
+    """Install ``hook()`` (None: remove) for this thread: :func:`run_lockstep` calls it between rounds, where no
+    device read is pending and no lock is held -- the step boundary at which a pause of the caller's GPU work
+    lands."""
+    _STEP.hook = hook
 
 
 def read_host(requests: Sequence[Sequence[torch.Tensor]]) -> list[tuple]:
@@ -133,6 +141,9 @@ def run_lockstep(routines: Iterable[Routine]) -> list:
                 requests = [r for _, r in kept]
             if not waiting:
                 break
+            hook = getattr(_STEP, "hook", None)
+            if hook is not None:
+                hook()
             with _STATS_LOCK:
                 STATS["rounds"] += 1
             served, raised = _serve(requests)
@@ -240,4 +251,4 @@ def span_energy_routine(gram: torch.Tensor, directions: torch.Tensor, total: flo
 
 
 __all__ = ["BatchedCall", "Routine", "STATS", "TileWorkspace", "projection_routine", "read_host", "run_lockstep",
-           "run_one", "source_energy_routine", "span_energy_routine", "stored_energy_routine"]
+           "run_one", "set_step_hook", "source_energy_routine", "span_energy_routine", "stored_energy_routine"]

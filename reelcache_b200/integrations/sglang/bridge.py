@@ -149,7 +149,8 @@ class CausalWanKVBridge:
             total = torch.cuda.get_device_properties(self.device).total_memory
             torch.cuda.set_per_process_memory_fraction(min(1.0, config.cuda_memory_limit_bytes / total), self.device)
         self.archive = LineageSessionArchive(config, engine.identity, profile, self.device)
-        self.sessions = SGLangSessionController(self.archive, retention=config.tree_retention)
+        self.sessions = SGLangSessionController(self.archive, retention=config.tree_retention,
+                                                tree_switch=config.tree_switch)
         self.cache_chunks = cache_chunks
         self.telemetry = WorkloadTelemetry(enabled=config.workload_telemetry)
         self.defer = GenerationDefer.from_config(config, getattr(self.archive, "pipeline", None))
@@ -444,7 +445,10 @@ class CausalWanKVBridge:
         key = key if key is not None else (None if run is None else run.key)
         with contextlib.ExitStack() as stack:
             if self.config.defer_archival_during_decode and pipeline is not None:
-                stack.enter_context(pipeline.defer_gpu_work())
+                if self.config.decode_entry_guard and hasattr(pipeline, "pause_gpu_work"):
+                    record["archival_pause"] = stack.enter_context(pipeline.pause_gpu_work())
+                else:
+                    stack.enter_context(pipeline.defer_gpu_work())
             if self.defer is not None and key is not None:
                 stack.enter_context(self.defer.decode_seam(key, reason))
             try:
@@ -583,14 +587,19 @@ class _BridgeRun:
         overlapped = bridge.config.overlap_restore if self.request.overlap_restore is None \
             else self.request.overlap_restore
         pipeline = bridge.archive.pipeline
+        paused = None
         if bridge.config.archival_pump_pause and hasattr(pipeline, "defer_gpu_work"):
-            self._deferral = pipeline.defer_gpu_work()   # released when the install is joined
-            self._deferral.__enter__()
+            # released when the install is joined; a node already planning pauses at its next step boundary
+            self._deferral = pipeline.pause_gpu_work() if hasattr(pipeline, "pause_gpu_work") else \
+                pipeline.defer_gpu_work()
+            paused = self._deferral.__enter__()
         self.install = target.engine.install(target.cache, bridge.archive, head, plan, overlapped=overlapped)
         target.layer_wait = self.install.wait
         self.route = "archive"
         self.restore_report = {"mode": "archive", "head": head, "attended_tokens": plan.attended_tokens,
                                "spans": len(plan.spans), "overlapped": bool(overlapped)}
+        if self._deferral is not None and isinstance(paused, dict):
+            self.restore_report["archival_pause"] = paused
 
     def _tier_holds(self, plan: VisibilityPlan) -> bool:
         tier = self.bridge.archive.raw_tier

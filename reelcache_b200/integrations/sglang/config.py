@@ -216,8 +216,7 @@ FIELDS: dict[str, Field] = {
     "durability": Field(_choice("pause", "always", "never")),
     "resident_reuse": Field(_flag),
     "tree_retention": Field(_choice("head", "full")),
-    "tree_switch": Field(_choice("drain", "detach"), omit_at_default=True,
-                         pinned="switching trees without draining the old branch is " + _NOT_BUILT),
+    "tree_switch": Field(_choice("drain", "detach"), omit_at_default=True),
     "restore_mode": Field(_choice("archive", "recompute")),
     "store_io": Field(_choice("buffered", "nocache")),
     # restore

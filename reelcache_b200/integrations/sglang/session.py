@@ -59,6 +59,8 @@ class SGLangSessionState:
 
 
 RETAINED_PREFIX = "sglang/retained/"
+#: Infix of the side lineages a detaching rewind hands a session's unpublished chunks to.
+DETACHED = ".detached."
 
 
 def node_prompt(runtime, node_ref: str) -> str | None:
@@ -78,13 +80,17 @@ class SGLangSessionController:
     ``sglang/retained/<session>/<n>`` (garbage collection keeps what refs reach); ``"head"`` keeps the current
     head (and named checkpoints) only."""
 
-    def __init__(self, archive, *, retention: str = "head"):
+    def __init__(self, archive, *, retention: str = "head", tree_switch: str = "drain"):
         if retention not in ("head", "full"):
             raise ConfigurationError("retention is 'head' or 'full'")
+        if tree_switch not in ("drain", "detach"):
+            raise ConfigurationError("tree_switch is 'drain' or 'detach'")
         self.archive = archive
         self.store = archive.store
         self.runtime = archive.runtime
         self.retention = retention
+        self.tree_switch = tree_switch
+        self.detached: dict[str, list[dict]] = {}
         self._lock = threading.RLock()
         self._states: dict[str, SGLangSessionState] = {}
 
@@ -115,6 +121,7 @@ class SGLangSessionController:
     def sessions(self) -> dict[str, dict]:
         with self._lock:
             names = {name.split("/", 1)[1] for name in self.store.list_refs("lineages/")}
+            names = {name for name in names if DETACHED not in name}
             return {name: self.get(name).describe() for name in sorted(names)}
 
     def head(self, session_id: str) -> str:
@@ -251,8 +258,7 @@ class SGLangSessionController:
         with self._lock:
             state = self.get(session_id)
             self.check_ready(state)
-            self.archive.drain(session_id)
-            node = self.resolve(session_id, checkpoint)
+            node = self._switch_point(session_id, checkpoint)
             left = self.head(session_id)
             if self.retention == "full" and left != node:
                 taken = self.store.list_refs(f"{RETAINED_PREFIX}{session_id}/")
@@ -269,6 +275,25 @@ class SGLangSessionController:
             state.status = "idle"
             state.log("rewound", node=node)
             return state
+
+    def _switch_point(self, session_id: str, checkpoint: Any) -> str:
+        """The node a rewind moves to. ``tree_switch="drain"`` first waits until every submitted chunk is
+        published; ``"detach"`` resolves against the published head when it can and hands the unpublished chunks
+        to a side lineage (``<session>.detached.<n>``) that keeps publishing them, so the rewind does not wait."""
+        pipeline = getattr(self.archive, "pipeline", None)
+        if self.tree_switch == "detach" and hasattr(pipeline, "detach"):
+            try:
+                node = self.resolve(session_id, checkpoint)
+            except (ConfigurationError, StateError):
+                node = None  # the checkpoint is not published yet: drain for it
+            if node is not None:
+                history = self.detached.setdefault(session_id, [])
+                record = pipeline.detach(session_id, f"{session_id}{DETACHED}{len(history)}")
+                if record["moved"]:
+                    history.append(record)
+                return node
+        self.archive.drain(session_id)
+        return self.resolve(session_id, checkpoint)
 
     def close(self, session_id: str, *, delete: bool = False, drain: bool = True) -> dict:
         with self._lock:

@@ -126,3 +126,67 @@ def test_raw_tier_backpressure_when_full_of_unpublished():
     tier.admit(_tensors(8), "c2")  # admitted once the first entry is published (and dropped: no holders)
     assert done.is_set()
     tier.close()
+
+
+def test_pause_lands_at_a_planning_boundary(runtime):
+    """A pause taken while a node plans is acknowledged at the planner's next lockstep round; the node waits
+    there until the pause ends, then publishes."""
+    import time
+    runtime.create_lineage("a")
+    pipe = ArchivePipeline(runtime, method=method(solver="topk_rr"), device="cpu", max_unpublished=2)
+    entered, release = threading.Event(), threading.Event()
+    original = pipe._step_boundary
+
+    def gated():
+        entered.set()
+        release.wait(30)
+        original()
+    pipe._step_boundary = gated
+    try:
+        m, c = chunk(0)
+        ticket = pipe.submit("a", "c0", m, c)
+        assert entered.wait(30)
+        records = []
+
+        def pause():
+            with pipe.pause_gpu_work(ack_timeout=20) as record:
+                records.append(record)
+                time.sleep(0.3)
+                records.append(ticket.state)
+        worker = threading.Thread(target=pause)
+        worker.start()
+        time.sleep(0.05)
+        release.set()
+        worker.join(60)
+        assert records[0]["acked"] and records[0]["inflight"] and records[0]["landed"] == "boundary"
+        assert records[1] == "planning"            # held at the boundary for the whole section
+        assert ticket.result(60)
+        stats = pipe.stats()["fitter_pause"]
+        assert stats["requests"] == 1 and stats["acked"] == 1 and stats["paused_seconds"] > 0.2
+        with pipe.pause_gpu_work() as record:      # nothing on the GPU: acknowledged at once
+            assert record["landed"] == "idle"
+    finally:
+        release.set()
+        pipe.close()
+
+
+def test_detach_hands_unpublished_chunks_to_a_side_lineage(runtime):
+    runtime.create_lineage("a")
+    pipe = ArchivePipeline(runtime, method=method(), device="cpu", max_unpublished=4)
+    try:
+        m, c = chunk(0)
+        pipe.submit("a", "c0", m, c).result(120)
+        cut = runtime.lineage_head("a")
+        with pipe.defer_gpu_work():                 # keep the next chunks queued
+            tickets = [pipe.submit("a", f"c{i}", *chunk(i)) for i in (1, 2)]
+            record = pipe.detach("a", "a-side")
+        assert record == {"branch": "a-side", "moved": ["c1", "c2"], "cut": cut}
+        pipe.drain("a-side", timeout=120)
+        assert runtime.lineage_head("a") == cut    # the original head never moved
+        side = runtime.lineage_head("a-side")
+        assert tickets[1].result(0) == side and runtime.load_node(side).frontier == 3 * c[MatrixKey(0, "K")].token_count
+        assert pipe.detach("a", "a-other")["moved"] == []
+        report = pipe.prewarm(c)
+        assert report["fresh_seconds"] > 0 and pipe.stats()["prewarm"][0]["total_seconds"] >= report["fresh_seconds"]
+    finally:
+        pipe.close()

@@ -34,7 +34,8 @@ def test_config_round_trip_and_validation(tmp_path):
     with pytest.raises(ConfigurationError):
         ReelCacheRuntimeConfig.from_dict({"store_root": str(tmp_path), "unknown_field": 1})
     with pytest.raises(ConfigurationError):
-        ReelCacheRuntimeConfig(store_root=str(tmp_path), tree_switch="detach")
+        ReelCacheRuntimeConfig(store_root=str(tmp_path), tree_switch="merge")
+    assert ReelCacheRuntimeConfig(store_root=str(tmp_path), tree_switch="detach").to_dict()["tree_switch"] == "detach"
 
 
 def test_session_lifecycle(tmp_path):
