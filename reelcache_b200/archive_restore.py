@@ -226,8 +226,9 @@ class LineageRestorer:
         """Plan the restore of ``node_ref``: one job per (layer, K/V, piece) reading the history's packs
         from ``device_raw`` (packet ref -> device uint8 copy of the pack; default: copied now on
         ``stream``). ``destination(layer, "K"|"V")`` returns the native BTHD cache tensor
-        ``[1, capacity, heads, head_dim]``; ``rope(piece)`` returns the (table, (t_row, h_row, w_row)) of its positions;
-        ``slot_of(piece)`` the first cache row of the piece (default: its global token index)."""
+        ``[1, capacity, heads, head_dim]``; ``rope(piece)`` returns the (table, (t_row, h_row, w_row)) of its positions
+        (``rope=None``: the destination receives pre-RoPE K, and ranges may cut frames); ``slot_of(piece)`` the first
+        cache row of the piece (default: its global token index)."""
         stream = stream or torch.cuda.current_stream(self.device)
         entries = self.history(node_ref, ranges)
         model = self.runtime.model
@@ -264,10 +265,12 @@ class LineageRestorer:
                     context = record.context
                     if piece.offset or tokens != context.token_count:
                         values = values[piece.offset:piece.offset + tokens]
-                        if tokens % (context.height * context.width):
-                            raise UnsupportedError("partial-frame history ranges are not restorable by the fused path")
-                    frames = tokens // (context.height * context.width)
-                    grid = (frames, context.height, context.width)
+                        if tokens % (context.height * context.width) and rope is not None:
+                            raise UnsupportedError("partial-frame history ranges are not restorable with RoPE")
+                    if tokens % (context.height * context.width):
+                        grid = (1, 1, tokens)  # rows of frames (no RoPE: the grid only shapes the job)
+                    else:
+                        grid = (tokens // (context.height * context.width), context.height, context.width)
                     basis, qmax = self.bases.get(record.basis_version_ref, record.rank_view, stream)
                     first_row = piece.token_start if slot_of is None else slot_of(piece)
                     slot = rows[first_row:first_row + tokens]  # [tokens, heads, head_dim]
@@ -277,13 +280,48 @@ class LineageRestorer:
                            "dest": (slot.data_ptr(), (slot.stride(0), slot.stride(1), slot.stride(2)), slot.dtype,
                                     slot.shape[1] * slot.shape[2], head_dim),
                            "rope": None}
-                    if target == "K" and context.key_space == "pre_rope":
+                    if target == "K" and context.key_space == "pre_rope" and rope is not None:
                         table, rope_rows = rope(piece)
                         first = piece.offset // (context.height * context.width)
                         rope_rows = (rope_rows[0] + first, rope_rows[1], rope_rows[2])
                         job["rope"] = restore_rope_item(RopePositions(table, rope_rows), grid, self.device, stream,
                                                         program.keepalive)
                     program.add(job, group=layer)
+        return program
+
+    def gather_program(self, node_ref: str, destination: Callable[[int, str], torch.Tensor],
+                       gathers: Sequence[tuple[int, int, int, int, int]], *, stream=None) -> RestoreProgram:
+        """Restore a rank's token subset of a single-range history (a LongCat segment) without RoPE:
+        ``gathers`` = ``(dest_row, tokens, run_len, run_stride, run_offset)`` jobs per matrix, each reading
+        coefficient rows ``(t // run_len) * run_stride + run_offset + t % run_len`` of the range and writing
+        ``tokens`` compact rows from ``dest_row`` of ``destination(layer, "K"|"V")`` ([1, rows, heads, head_dim])."""
+        stream = stream or torch.cuda.current_stream(self.device)
+        entries = self.history(node_ref)
+        if len(entries) != 1 or entries[0].piece.offset:
+            raise UnsupportedError("gathered restores read one whole history range (a segment)")
+        item = entries[0]
+        prepared = self.prepared_pack(item.packet_ref)
+        with torch.cuda.stream(stream):
+            device_raw = prepared.raw.to(self.device, non_blocking=True)
+        self.stats_["h2d_bytes"] += prepared.nbytes
+        program = RestoreProgram(self.device, stream, precision=DEFAULT_PRECISION if self.precision == "auto"
+                                 else self.precision)
+        program.keepalive.append(device_raw)
+        for layer in range(self.runtime.model.layers):
+            for target in ("K", "V"):
+                rows = destination(layer, target)[0]
+                tile_index, record = item.tiles[MatrixKey(layer, target)]
+                values = prepared.tile_view(device_raw, tile_index)
+                basis, qmax = self.bases.get(record.basis_version_ref, record.rank_view, stream)
+                for dest_row, tokens, run_len, run_stride, run_offset in gathers:
+                    slot = rows[dest_row:dest_row + tokens]
+                    program.add({"kind": "u8", "values": values, "tokens": tokens, "rank": record.rank_view,
+                                 "grid": (1, 1, tokens), "basis": basis, "qmax": qmax,
+                                 "scale": prepared.scales[tile_index], "offset": prepared.offsets[tile_index],
+                                 "runs": (run_len, run_stride, run_offset),
+                                 "dest": (slot.data_ptr(), (slot.stride(0), slot.stride(1), slot.stride(2)),
+                                          slot.dtype, slot.shape[1] * slot.shape[2], slot.shape[2]),
+                                 "rope": None}, group=layer)
         return program
 
     def node_factors(self, node_ref: str, keys: Sequence[MatrixKey], *, ranges=None, stream=None,
@@ -322,9 +360,12 @@ class LineageRestorer:
                 dests.append((t.data_ptr(), tuple(t.shape), t.stride(), t.dtype))
         ropes = []
         for item in self.history(node_ref, ranges):
+            slot = None if slot_of is None else slot_of(item.piece)
+            if rope is None:
+                ropes.append((None, slot))
+                continue
             table, rows = rope(item.piece)
-            ropes.append((id(table), table._stamp(), tuple(rows),
-                          None if slot_of is None else slot_of(item.piece)))
+            ropes.append((id(table), table._stamp(), tuple(rows), slot))
         return (node_ref, None if ranges is None else tuple(map(tuple, ranges)), tuple(dests), tuple(ropes))
 
     def _layer_copies(self, entries, layer_count):

@@ -32,7 +32,17 @@ struct Job {
   int tokens, k_pad, rank, frames, height, width;
   int vec8;                  // dense, rows >= k_pad bytes apart: 2 = 16-byte aligned rows (unpack_dense16),
                              // 1 = 8-byte aligned (one 8-byte load per thread), 0 = byte loads
+  int run_len;               // dense gather (0: none): token t reads source row
+  int64_t run_stride;        //   (t / run_len) * run_stride + run_offset + t % run_len
+  int64_t run_offset;        //   (a rank's column or row block of a frame grid)
 };
+
+// The dense source row a job's token reads: itself, or its place in the job's runs.
+__device__ __forceinline__ int64_t source_row(const Job& jb, int token) {
+  if (jb.run_len == 0) return token;
+  const int run = token / jb.run_len;
+  return static_cast<int64_t>(run) * jb.run_stride + jb.run_offset + (token - run * jb.run_len);
+}
 
 struct Params {
   Job jobs[kMaxJobs];
@@ -52,7 +62,7 @@ __device__ __forceinline__ void unpack_dense16(const Job& jb, int64_t item) {
   if (item >= static_cast<int64_t>(jb.tokens) * groups) return;
   const int token = static_cast<int>(item / groups);
   const int group = static_cast<int>(item - static_cast<int64_t>(token) * groups);
-  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(jb.matrix + static_cast<int64_t>(token) * jb.row_stride +
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(jb.matrix + source_row(jb, token) * jb.row_stride +
                                                          group * 16));
   const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
   uint32_t w[8];
@@ -83,7 +93,7 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const __grid_constant_
   uint32_t px[8];
   bool live[8];
   if (jb.matrix != nullptr) {
-    const uint8_t* rowp = jb.matrix + static_cast<int64_t>(token) * jb.row_stride + group * 8;
+    const uint8_t* rowp = jb.matrix + source_row(jb, token) * jb.row_stride + group * 8;
     if (jb.vec8) {
       // one 8-byte load: a source in a peer's memory (the sequence-parallel restore) then costs one
       // NVLink request per 8 coefficients instead of eight byte loads
@@ -136,11 +146,13 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const __grid_constant_
 
 }  // namespace unpack
 
-// jobs: CPU int64 [n, 12]: pic_addr, col_off, col_seg, matrix, out, row_stride, tokens, k_pad, rank,
-// frames, height, width. Pointers are device addresses on `device`.
+// jobs: CPU int64 [n, 12 or 15]: pic_addr, col_off, col_seg, matrix, out, row_stride, tokens, k_pad, rank,
+// frames, height, width[, run_len, run_stride, run_offset]. Pointers are device addresses on `device`.
 void unpack_launch(const at::Tensor& jobs, int64_t device) {
-  RC_CHECK(jobs.device().is_cpu() && jobs.scalar_type() == at::kLong && jobs.dim() == 2 && jobs.size(1) == 12,
-           "jobs must be a CPU int64 [n, 12] table");
+  RC_CHECK(jobs.device().is_cpu() && jobs.scalar_type() == at::kLong && jobs.dim() == 2 &&
+               (jobs.size(1) == 12 || jobs.size(1) == 15),
+           "jobs must be a CPU int64 [n, 12 or 15] table");
+  const int width = static_cast<int>(jobs.size(1));
   const int n = static_cast<int>(jobs.size(0));
   RC_CHECK(n >= 1 && n <= unpack::kMaxJobs, "between 1 and 48 unpack jobs per launch");
   unpack::Params p;
@@ -148,7 +160,7 @@ void unpack_launch(const at::Tensor& jobs, int64_t device) {
   const int64_t* f = jobs.data_ptr<int64_t>();
   int64_t max_items = 0;
   for (int i = 0; i < n; ++i) {
-    const int64_t* r = f + i * 12;
+    const int64_t* r = f + i * width;
     unpack::Job& jb = p.jobs[i];
     jb.pic_addr = reinterpret_cast<const int64_t*>(r[0]);
     jb.col_off = reinterpret_cast<const int32_t*>(r[1]);
@@ -162,6 +174,12 @@ void unpack_launch(const at::Tensor& jobs, int64_t device) {
     jb.frames = static_cast<int>(r[9]);
     jb.height = static_cast<int>(r[10]);
     jb.width = static_cast<int>(r[11]);
+    if (width == 15 && r[12] > 0) {
+      RC_CHECK(jb.matrix != nullptr && r[13] >= 0 && r[14] >= 0, "row runs apply to dense sources");
+      jb.run_len = static_cast<int>(r[12]);
+      jb.run_stride = r[13];
+      jb.run_offset = r[14];
+    }
     jb.vec8 = 0;
     if (jb.matrix != nullptr && jb.row_stride >= jb.k_pad) {
       const uintptr_t base = reinterpret_cast<uintptr_t>(jb.matrix);

@@ -358,7 +358,11 @@ class ReelCacheConditioningCacheBackend:
     newest segment node of that epoch (this rank's rows only under CP), or returns None."""
 
     def __init__(self, runtime, lineage: str, method, *, head_dim: int, grid: tuple[int, int], device="cpu",
-                 cp_shard: RowShard | None = None):
+                 cp_shard: RowShard | None = None, restorer=None):
+        """``restorer``: a :class:`~reelcache_b200.archive_restore.LineageRestorer` on ``device``; with it a
+        segment restores on the fused sm_100a kernels, each CP rank gathering only its rows of the coefficient
+        tiles (:func:`shard_runs`), instead of decoding every row on the host."""
+        self.restorer = restorer
         self.runtime = runtime
         self.lineage = lineage
         self.method = method
@@ -394,6 +398,8 @@ class ReelCacheConditioningCacheBackend:
         if node is None:
             self.stats["missed"] += 1
             return None
+        if self.restorer is not None and self.device.type == "cuda":
+            return self._restore_fused(epoch, node)
         ks, vs = [], []
         packs: dict = {}
         for layer in range(self.runtime.model.layers):
@@ -406,3 +412,43 @@ class ReelCacheConditioningCacheBackend:
             vs.append(v.reshape(v.shape[0], -1, self.head_dim))
         self.stats["restored"] += 1
         return LongCatConditioningCache(epoch, ks, vs) if ks else None
+
+    def _restore_fused(self, epoch: ConditioningCacheEpoch, node: str) -> LongCatConditioningCache:
+        """The segment's K / V straight from its node pack on the fused kernels (no RoPE: the cache is pre-RoPE),
+        this rank's rows only."""
+        model = self.runtime.model
+        h, w = self.grid
+        shard = self.cp_shard if self.cp_shard is None else RowShard(self.cp_shard.rank, self.cp_shard.cp,
+                                                                      epoch.frames, h, w)
+        runs = shard_runs(shard, epoch.frames, h, w)
+        tokens = sum(job[1] for job in runs)
+        heads = model.channels_for("K") // self.head_dim
+        ks = [torch.empty((1, tokens, heads, self.head_dim), dtype=torch.bfloat16, device=self.device)
+              for _ in range(model.layers)]
+        vs = [torch.empty_like(k) for k in ks]
+        stream = torch.cuda.current_stream(self.device)
+        program = self.restorer.gather_program(node, lambda layer, t: ks[layer] if t == "K" else vs[layer], runs,
+                                               stream=stream)
+        program.prepare()
+        program.launch_all()
+        self.stats["restored"] += 1
+        self.stats["fused"] = self.stats.get("fused", 0) + 1
+        self.last_program = program  # keeps the staging alive until the caller's stream moves on
+        return LongCatConditioningCache(epoch, [k[0] for k in ks], [v[0] for v in vs])
+
+
+def shard_runs(shard: RowShard | None, frames: int, height: int, width: int) -> list[tuple[int, int, int, int, int]]:
+    """Row-run gathers ``(dest_row, tokens, run_len, run_stride, run_offset)`` that read a CP rank's block of a
+    ``frames x height x width`` token grid in its local order (frame-major, then rows, then columns): one job when
+    the block spans whole rows or whole columns of every frame, else one job per frame."""
+    if shard is None:
+        total = frames * height * width
+        return [(0, total, total, total, 0)]
+    rows, cols = shard.block
+    bh, bw = rows.stop - rows.start, cols.stop - cols.start
+    per_frame = height * width
+    if bh == height:        # column block: runs of bw columns, one per (frame, row)
+        return [(0, frames * bh * bw, bw, width, cols.start)]
+    if bw == width:         # row block: one run of bh whole rows per frame
+        return [(0, frames * bh * bw, bh * width, per_frame, rows.start * width)]
+    return [(f * bh * bw, bh * bw, bw, width, f * per_frame + rows.start * width + cols.start) for f in range(frames)]

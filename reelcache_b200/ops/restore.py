@@ -119,7 +119,9 @@ class RestoreProgram:
     (frames, height, width), ``basis`` (FP16 [R, C]), optional ``basis_t`` (FP16 [C, k_pad]) and
     ``qmax``, ``scale``/``offset`` (host float32 [>= rank]), ``dest`` (address, (ts, hs, ds), dtype,
     channels, head_dim), ``rope`` (restore_kernels.restore_rope_item) or None, and the source
-    (``pictures``: (addresses, plane_stride, row_stride, layout) | ``values``: device tensor).
+    (``pictures``: (addresses, plane_stride, row_stride, layout) | ``values``: device tensor, with optional
+    ``runs`` = (run_len, run_stride, run_offset): token t reads coefficient row
+    ``(t // run_len) * run_stride + run_offset + t % run_len`` -- one job restores a rank's block of a frame grid).
     """
 
     def __init__(self, device, stream, *, precision: str = "fp16x2"):
@@ -214,13 +216,18 @@ class RestoreProgram:
                     col_off, col_seg = column_tables(layout, plane_stride, row_stride, k_pad)
                     unpack_owner.append(len(self.rows))
                     unpack_rows.append([arena.add(addresses), arena.add(col_off), arena.add(col_seg), 0,
-                                        a.data_ptr(), row_stride, tokens, k_pad, rank, frames, height, width])
+                                        a.data_ptr(), row_stride, tokens, k_pad, rank, frames, height, width, 0, 0, 0])
                 else:
                     values = job["values"]
                     self.keepalive.append(values)
                     unpack_owner.append(len(self.rows))
+                    runs = job.get("runs") or (0, 0, 0)   # (run_len, run_stride, run_offset): a row gather
+                    if runs[0]:
+                        last = (tokens - 1) // runs[0] * runs[1] + runs[2] + (tokens - 1) % runs[0]
+                        if last >= values.shape[0] or min(runs) < 0:
+                            raise ConfigurationError("row runs reach past the job's coefficient rows")
                     unpack_rows.append([-1, -1, -1, values.data_ptr(), a.data_ptr(), values.stride(0), tokens,
-                                        k_pad, rank, frames, height, width])
+                                        k_pad, rank, frames, height, width, *runs])
                 basis = job["basis"]
                 scale_off = arena.add(np.ascontiguousarray(job["scale"][:rank], dtype=np.float32))
                 offset_off = arena.add(np.ascontiguousarray(job["offset"][:rank], dtype=np.float32))
