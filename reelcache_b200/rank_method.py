@@ -271,6 +271,28 @@ def stored_energy_routine(x: torch.Tensor, rows: torch.Tensor, total: float, til
     return 1.0 - value / total, coefficients
 
 
+def prefix_energies_routine(x: torch.Tensor, rows: torch.Tensor, coefficients: torch.Tensor, prefixes, total: float,
+                            tile_rows: int = 16384):
+    """Stored energies of the row prefixes ``rows[:c]`` (``c`` ascending) in one pass: the coefficients of a prefix
+    are the leading columns of ``coefficients = A Q^T``, and its reconstruction grows by one block of rows at a
+    time, each prefix's direct residual summed in FP64 -- one host round for every prefix."""
+    q = rows.float()
+    sums = []
+    for start in range(0, x.shape[0], tile_rows):
+        a = x[start:start + tile_rows]
+        p = coefficients[start:start + tile_rows]
+        recon = torch.zeros(a.shape, dtype=torch.float32, device=a.device)
+        previous = 0
+        for index, c in enumerate(prefixes):
+            recon += exact_blas.mm(p[:, previous:c], q[previous:c])
+            previous = c
+            part = _sum_squares(a, recon)[1]
+            sums[index:index + 1] = [part if len(sums) <= index else sums[index] + part]
+        del recon
+    (values,) = yield (torch.stack(sums),)
+    return [1.0 - float(v) / total for v in values]
+
+
 def _bucketed(rank: float, bucket: int, limit: int) -> int:
     if not math.isfinite(rank):
         return limit
@@ -482,13 +504,16 @@ def plan_matrix_routine(matrix: torch.Tensor, context: TensorContext, cfg: RankM
         if energy_all >= target - cfg.decision_band:
             # shortest bucket-aligned prefix that verifies
             rank = inherited_rows.shape[0]
-            candidates = list(range(cfg.bucket, rank, cfg.bucket)) + [rank]
+            candidates = list(range(cfg.bucket, rank, cfg.bucket))
             chosen, chosen_energy, chosen_p = rank, energy_all, coefficients_all
-            for candidate in candidates:
-                energy_c, p_c = yield from stored_energy_routine(x, inherited_rows[:candidate], total, cfg.tile_rows)
-                if energy_c >= target - cfg.decision_band:
-                    chosen, chosen_energy, chosen_p = candidate, energy_c, p_c
-                    break
+            if candidates:
+                energies = yield from prefix_energies_routine(x, inherited_rows, coefficients_all, candidates, total,
+                                                              cfg.tile_rows)
+                for candidate, energy_c in zip(candidates, energies):
+                    if energy_c >= target - cfg.decision_band:
+                        chosen, chosen_energy = candidate, energy_c
+                        chosen_p = coefficients_all[:, :candidate].contiguous()
+                        break
             report = EnergyReport(target, min(chosen_energy, 1.0), min(chosen_energy, 1.0), None, None,
                                   _bucketed(chosen, cfg.bucket, channels), chosen)
             return MatrixPlan(entry, context, "share", inherited_rows[:chosen], None, binding.version_ref, chosen,
@@ -576,17 +601,62 @@ def plan_chunk(matrices: Mapping[Any, torch.Tensor], contexts: Mapping[Any, Tens
     with orthogonalizer_scope(cfg.orthogonalizer):
         for start in range(0, len(entries), cfg.batch_size):
             group = entries[start:start + cfg.batch_size]
-            routines = []
-            for entry in group:
+            routines, lanes = [], None
+            for index, entry in enumerate(group):
                 matrix = matrices[entry]
                 if device is not None:
                     matrix = matrix.to(device)
-                routines.append(plan_matrix_routine(matrix, contexts[entry], cfg, view,
-                                                    bindings.get(entry, ActiveBasisBinding()), inherited.get(entry),
-                                                    entry=entry, chunk_id=chunk_id))
+                routine = plan_matrix_routine(matrix, contexts[entry], cfg, view,
+                                              bindings.get(entry, ActiveBasisBinding()), inherited.get(entry),
+                                              entry=entry, chunk_id=chunk_id)
+                if matrix.is_cuda and len(group) > 1:
+                    lanes = lanes or _stream_lanes(matrix.device, min(PLANNER_STREAMS, len(group)))
+                    routine = _on_stream(routine, lanes[index % len(lanes)])
+                routines.append(routine)
             for entry, plan in zip(group, run_lockstep(routines)):
                 plans[entry] = plan
+            if lanes:
+                current = torch.cuda.current_stream(lanes[0].device)
+                for lane in lanes:
+                    current.wait_stream(lane)
     return plans
+
+
+#: CUDA streams a lockstep group spreads its matrices over: a matrix's planning kernels are small (thin
+#: ``C x k`` products, k x k factorizations) and fill a fraction of the SMs, so several matrices run side by side.
+PLANNER_STREAMS = 8
+_LANES: dict = {}
+
+
+def _stream_lanes(device: torch.device, count: int) -> list:
+    """Side streams of ``device`` (created once per device), each ordered after the current stream's work."""
+    lanes = _LANES.setdefault(device, [])
+    while len(lanes) < count:
+        lanes.append(torch.cuda.Stream(device))
+    current = torch.cuda.current_stream(device)
+    for lane in lanes[:count]:
+        lane.wait_stream(current)
+    return lanes[:count]
+
+
+def _on_stream(routine, stream):
+    """Run a routine's device work on ``stream``. Each step first orders the stream after the current one (a
+    batched call of the round ran there), and the current stream waits for the step's work before the round's
+    host reads and batched calls are issued on it; errors of a batched call are thrown into the routine."""
+    current = torch.cuda.current_stream(stream.device)
+    send, throw = None, None
+    while True:
+        stream.wait_stream(current)
+        with torch.cuda.stream(stream):
+            try:
+                request = routine.throw(throw) if throw is not None else routine.send(send)
+            except StopIteration as stop:
+                return stop.value
+        current.wait_stream(stream)
+        try:
+            send, throw = (yield request), None
+        except Exception as error:  # noqa: BLE001 - delivered to the wrapped routine
+            send, throw = None, error
 
 
 def _entry_order(e) -> tuple:
