@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import math
 import threading
+from contextlib import contextmanager
 from collections.abc import Generator, Iterable, Sequence
 from typing import Any
 
@@ -55,6 +56,35 @@ def set_step_hook(hook) -> None:
     device read is pending and no lock is held -- the step boundary at which a pause of the caller's GPU work
     lands."""
     _STEP.hook = hook
+
+
+def yield_point() -> None:
+    """A step boundary outside the lockstep runner (long host loops call it): runs this thread's step hook."""
+    hook = getattr(_STEP, "hook", None)
+    if hook is not None:
+        hook()
+
+
+def step_phase(label: str) -> None:
+    """Name the phase this thread's GPU work is in (reported by a pause that times out)."""
+    _STEP.phase = label
+
+
+def current_phase() -> str | None:
+    return getattr(_STEP, "phase", None)
+
+
+@contextmanager
+def blocked_wait(label: str):
+    """Mark a wait that allocates nothing (a host read's synchronization, a staging-slot wait): its end is a step
+    boundary, so the step hook runs there."""
+    previous = getattr(_STEP, "phase", None)
+    _STEP.phase = f"wait:{label}"
+    try:
+        yield
+    finally:
+        _STEP.phase = previous
+        yield_point()
 
 
 def read_host(requests: Sequence[Sequence[torch.Tensor]]) -> list[tuple]:
@@ -163,6 +193,80 @@ def run_one(routine: Routine) -> Any:
     return run_lockstep([routine])[0]
 
 
+def upload(tensors: Sequence[torch.Tensor], device: Any) -> list[torch.Tensor]:
+    """Host tensors to ``device`` in one transfer: packed into one pinned staging buffer (bytes), copied once,
+    split into views of their own dtypes and shapes on the device."""
+    device = torch.device(device)
+    if device.type != "cuda" or not tensors:
+        return [t.to(device) for t in tensors]
+    parts = [t.detach().contiguous().view(-1).view(torch.uint8) for t in tensors]
+    sizes = [p.numel() for p in parts]
+    aligned = [(n + 15) // 16 * 16 for n in sizes]
+    staging = torch.empty(sum(aligned), dtype=torch.uint8, pin_memory=True)
+    offset = 0
+    for part, width in zip(parts, aligned):
+        staging[offset:offset + part.numel()].copy_(part)
+        offset += width
+    flat = staging.to(device, non_blocking=True)
+    out, offset = [], 0
+    for t, n, width in zip(tensors, sizes, aligned):
+        out.append(flat[offset:offset + n].view(t.dtype).view(t.shape))
+        offset += width
+    return out
+
+
+def download(tensors: Sequence[torch.Tensor]) -> list[torch.Tensor]:
+    """Device tensors to the host in one transfer per device (byte-packed, then split into their own dtypes)."""
+    out: list = [None] * len(tensors)
+    by_device: dict = {}
+    for i, t in enumerate(tensors):
+        if t.device.type == "cpu":
+            out[i] = t
+        else:
+            by_device.setdefault(t.device, []).append(i)
+    for device, indices in by_device.items():
+        parts = [tensors[i].detach().contiguous().view(-1).view(torch.uint8) for i in indices]
+        host = torch.cat(parts).cpu()
+        offset = 0
+        for i, part in zip(indices, parts):
+            n = part.numel()
+            out[i] = host[offset:offset + n].view(tensors[i].dtype).view(tensors[i].shape)
+            offset += n
+        with _STATS_LOCK:
+            STATS["transfers"] += 1
+    return out
+
+
+def finite_flag(tensor: torch.Tensor) -> torch.Tensor:
+    """Device 0-d boolean: every element of ``tensor`` is finite."""
+    return torch.isfinite(tensor).all()
+
+
+def condition_terms(basis: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Device terms of the conditioning of stored rows ``basis[k, C]`` (FP16 or FP32): ``eta = ||Q Q^T - I||_F``
+    from an FP32-accurate Gram, and the largest row norm."""
+    from .exact_blas import gram
+    q = basis.float()
+    g = gram(q.t())
+    eta = (g - torch.eye(g.shape[0], dtype=g.dtype, device=g.device)).norm()
+    return eta, q.norm(dim=1).max()
+
+
+def finish_condition(basis: torch.Tensor, eta: float, norm: float) -> float:
+    """An upper bound on the 2-norm condition number of the rows: with ``||Q Q^T - I|| <= eta < 1`` the singular
+    values lie in ``[sqrt(1 - eta), sqrt(1 + eta)]``; ``inf`` otherwise."""
+    if not math.isfinite(eta) or eta >= 1.0 or basis.shape[0] == 0:
+        return math.inf
+    return math.sqrt((1.0 + eta) / (1.0 - eta))
+
+
+def condition_routine(basis: torch.Tensor):
+    """Yields once; returns the condition bound of :func:`finish_condition`."""
+    eta, norm = condition_terms(basis)
+    (eta_value, norm_value) = yield (eta, norm)
+    return finish_condition(basis, eta_value, norm_value)
+
+
 class TileWorkspace:
     """Reusable named buffers (one allocation per name, shape class, dtype and device)."""
 
@@ -250,5 +354,6 @@ def span_energy_routine(gram: torch.Tensor, directions: torch.Tensor, total: flo
     return 1.0 if total <= 0 else float(values[0]) / total
 
 
-__all__ = ["BatchedCall", "Routine", "STATS", "TileWorkspace", "projection_routine", "read_host", "run_lockstep",
-           "run_one", "set_step_hook", "source_energy_routine", "span_energy_routine", "stored_energy_routine"]
+__all__ = ["BatchedCall", "Routine", "STATS", "TileWorkspace", "blocked_wait", "condition_routine", "condition_terms",
+           "current_phase", "download", "finish_condition", "finite_flag", "projection_routine", "read_host",
+           "run_lockstep", "run_one", "set_step_hook", "step_phase", "upload", "yield_point", "source_energy_routine", "span_energy_routine", "stored_energy_routine"]

@@ -63,3 +63,23 @@ def test_lockstep_plans_equal_sequential_on_cuda():
     for entry in alone:
         _same(alone[entry], together[entry])
     assert rounds[1] * 2 <= rounds[0]
+
+
+def test_condition_transfers_and_step_points():
+    import math
+    q = torch.linalg.qr(torch.randn(64, 16, generator=torch.Generator().manual_seed(0)))[0].t()
+    assert abs(deferred_reads.run_one(deferred_reads.condition_routine(q)) - 1.0) < 1e-5
+    assert math.isinf(deferred_reads.run_one(deferred_reads.condition_routine(torch.ones(2, 8))))
+    tensors = [torch.randn(3, 4), torch.arange(5, dtype=torch.int32), torch.randn(2, dtype=torch.float64)]
+    for a, b in zip(deferred_reads.download(tensors), tensors):
+        assert torch.equal(a, b) and a.dtype == b.dtype
+    seen = []
+    deferred_reads.set_step_hook(lambda: seen.append(deferred_reads.current_phase()))
+    try:
+        deferred_reads.step_phase("plan")
+        with deferred_reads.blocked_wait("staging"):
+            pass
+        deferred_reads.run_lockstep([deferred_reads.source_energy_routine(torch.ones(4, 4))])
+    finally:
+        deferred_reads.set_step_hook(None)
+    assert seen[0] == "plan" and len(seen) >= 2
