@@ -49,7 +49,7 @@ from .seam import (CLEAN_COMMIT, KV_RECACHE, CaptureScope, CausalKVRequest, Chun
                    ReplayStep, RestoreTarget, check_capture, drive_request, plan_recache)
 from .session import SGLangSessionController, SGLangSessionState, prompt_tensor
 from .visibility import VisibilityPlan, build_visibility_plan, resolve_plan
-from .workload_telemetry import WorkloadTelemetry
+from .workload_telemetry import RequestTelemetry, WorkloadTelemetry, bytes_per_token, drain_span, request_scope
 
 ACTIONS = ("create", "resume", "rewind", "fork")
 #: Recent request summaries kept for ``request_summary`` (oldest dropped first).
@@ -191,14 +191,19 @@ class CausalWanKVBridge:
             started = time.perf_counter()
             sessions = self.sessions
             action, sid = request.action, request.session_id
-            if action == "create":
-                state = sessions.create(sid)
-            elif action == "fork":
-                state = sessions.fork(request.source, sid, checkpoint=request.checkpoint)
-            elif action == "rewind":
-                state = sessions.rewind(sid, request.checkpoint)
-            else:
-                state = sessions.get(sid, required=False) or sessions.create(sid)
+            workload = RequestTelemetry(self.device) if self.config.workload_telemetry else None
+            with request_scope(workload), (workload.span("request_begin", gpu=False) if workload is not None
+                                           else contextlib.nullcontext()):
+                if action == "create":
+                    state = sessions.create(sid)
+                elif action == "fork":
+                    with drain_span():
+                        state = sessions.fork(request.source, sid, checkpoint=request.checkpoint)
+                elif action == "rewind":
+                    with drain_span():
+                        state = sessions.rewind(sid, request.checkpoint)
+                else:
+                    state = sessions.get(sid, required=False) or sessions.create(sid)
             sessions.check_ready(state)
             if state.status == "running":
                 raise PendingError(f"session {sid!r} is already running")
@@ -209,7 +214,7 @@ class CausalWanKVBridge:
             state.status = "running"
             state.pause_requested = False
             state.log("request", action=action, request_id=request.request_id)
-            run = _BridgeRun(self, request, state, started)
+            run = _BridgeRun(self, request, state, started, workload=workload)
             self._active = run
             return run
 
@@ -489,8 +494,10 @@ class CausalWanKVBridge:
 class _BridgeRun:
     """One session request in flight (returned by :meth:`CausalWanKVBridge.begin_request`)."""
 
-    def __init__(self, bridge: CausalWanKVBridge, request: CausalKVRequest, state: SGLangSessionState, started: float):
+    def __init__(self, bridge: CausalWanKVBridge, request: CausalKVRequest, state: SGLangSessionState, started: float,
+                 *, workload: RequestTelemetry | None = None):
         self.bridge, self.request, self.state = bridge, request, state
+        self.workload = workload
         self.session_id = state.session_id
         self.key = (state.session_id, request.request_id)
         self.started = started
@@ -575,10 +582,20 @@ class _BridgeRun:
                 target.latents = _PathLatents(runtime, nodes)
                 plan = self._plan(head, done)
                 self.span.mark("restore_issue")
-                if bridge.config.restore_mode == "recompute":
-                    self._recompute(target, head, plan, done)
-                else:
-                    self._archive_install(target, head, plan)
+                with (self.workload.span("restore_sync") if self.workload is not None
+                      else contextlib.nullcontext()), request_scope(self.workload):
+                    if bridge.config.restore_mode == "recompute":
+                        self._recompute(target, head, plan, done)
+                    else:
+                        self._archive_install(target, head, plan)
+                if self.workload is not None:
+                    p = bridge.profile
+                    self.workload.set_restore(self.restore_report, tokens=plan.attended_tokens,
+                                              per_token=bytes_per_token(num_layers=p.num_layers, num_heads=p.num_heads,
+                                                                        head_dim=p.head_dim,
+                                                                        capture_dtypes=p.capture_dtypes))
+        if self.workload is not None and target.layer_wait is not None:
+            target.layer_wait = self.workload.wrap_wait(target.layer_wait)
         self.restore_report["seconds"] = time.perf_counter() - clock
         return done
 
@@ -646,12 +663,15 @@ class _BridgeRun:
             raise StateError("no replay is pending for this request")
         self._replaying = True
         self._replay_started = time.perf_counter()
+        self._replay_span = None if self.workload is None else self.workload.begin("replay")
         return {"steps": len(self.target.replay)}
 
     def end_replay(self) -> dict[str, Any]:
         if not self._replaying:
             raise StateError("end_replay without begin_replay")
         self._replaying = False
+        if self.workload is not None:
+            self.workload.end(self._replay_span)
         seconds = time.perf_counter() - self._replay_started
         self.restore_report["replay_seconds"] = seconds
         return {"steps": len(self.target.replay), "seconds": seconds}
@@ -699,6 +719,7 @@ class _BridgeRun:
             builder = CleanChunkBuilder(bridge.engine.identity, index, written_start, frames, h, w,
                                         profile.cfg_streams)
         epoch = f"recache-{index}-{hashlib.sha256(self.prompt.encode()).hexdigest()[:12]}"
+        self._recache_span = None if self.workload is None else self.workload.begin("recache")
         return KVRecache(plan, epoch, self.prompt, CaptureScope(KV_RECACHE, ChunkSlot.of(profile, index), builder))
 
     def end_recache(self, recache: KVRecache) -> dict[str, Any]:
@@ -733,6 +754,8 @@ class _BridgeRun:
                                                      execution_state=prompt_tensor(recache.prompt))
             record["ranges"] = [r[0] for r in ranges]
         record["node"] = node_ref
+        if self.workload is not None:
+            self.workload.end(getattr(self, "_recache_span", None))
         state.prompt = recache.prompt
         state.recaches.append(plan.before_chunk)
         state.log("recache", epoch=recache.epoch_id, node=node_ref)
@@ -748,6 +771,9 @@ class _BridgeRun:
         h, w = profile.grid
         builder = CleanChunkBuilder(self.bridge.engine.identity, slot.index, slot.token_start, slot.num_frames, h, w,
                                     profile.cfg_streams)
+        if self.workload is not None and slot.index == self.first_new:
+            self.workload.mark_generation()
+            self._first_span = self.workload.begin("first_forward")
         return CaptureScope(CLEAN_COMMIT, slot, builder)
 
     @staticmethod
@@ -785,7 +811,12 @@ class _BridgeRun:
                     self.ttfc_gpu_ms = self._start_event.elapsed_time(first)
             self.ttfc_ms = (time.perf_counter() - self.started) * 1e3
             self.span.mark("first_chunk")
-        return self._commit(slot, latents, capture)
+            if self.workload is not None:
+                self.workload.end(getattr(self, "_first_span", None))
+        if self.workload is None:
+            return self._commit(slot, latents, capture)
+        with self.workload.span("chunk_commit", gpu=False):
+            return self._commit(slot, latents, capture)
 
     def _commit(self, slot: ChunkSlot, latents: torch.Tensor, capture: CaptureScope | None) -> bool:
         bridge, state = self.bridge, self.state
@@ -866,6 +897,8 @@ class _BridgeRun:
             }
             if self.ttfc_gpu_ms is not None:
                 summary["ttfc_gpu_ms"] = self.ttfc_gpu_ms
+            if self.workload is not None:
+                summary["workload"] = self.workload.resolve()
             if deferral is not None:
                 summary["archival_defer"] = deferral
             bridge.telemetry.end(self.span, summary)

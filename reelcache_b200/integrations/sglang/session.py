@@ -111,6 +111,14 @@ class SGLangSessionController:
             return state
 
     def _reopen(self, session_id: str) -> SGLangSessionState:
+        from .workload_telemetry import active_telemetry
+        record = active_telemetry()
+        if record is not None:
+            with record.span("session_open", gpu=False):
+                return self._reopen_state(session_id)
+        return self._reopen_state(session_id)
+
+    def _reopen_state(self, session_id: str) -> SGLangSessionState:
         head = self.archive.head(session_id)
         state = SGLangSessionState(session_id, generated=len(chunk_nodes(self.runtime, head)),
                                    prompt=node_prompt(self.runtime, head))

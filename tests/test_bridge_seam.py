@@ -213,3 +213,20 @@ def test_inflight_pause_retention_sections_and_plan_cache(tmp_path):
     finally:
         bridge._active = None
         bridge.shutdown()
+
+
+def test_workload_record_of_a_restoring_request(tmp_path):
+    bridge = make_bridge(tmp_path, profile=PLAIN, workload_telemetry=True)
+    try:
+        bridge.request("s", action="create", chunks=2, seed=1)
+        bridge.pause("s")
+        bridge.drop_resident("s")
+        report = bridge.request("s", action="rewind", checkpoint=1, chunks=1, seed=1)
+        record = report["workload"]
+        names = [s["name"] for s in record["spans"]]
+        assert {"request_begin", "drain", "restore_sync", "first_forward", "chunk_commit"} <= set(names)
+        assert len(record["exposed_stalls"]) == PLAIN.num_layers and record["exposed_stall_ms"] >= 0
+        assert record["bytes"]["restored_native_bytes"] == PLAIN.chunk_tokens * 2 * PLAIN.num_layers * PLAIN.channels * 2
+        assert bridge.workload_record(report["request"]) is not None
+    finally:
+        bridge.shutdown()
