@@ -45,6 +45,8 @@ from .generation_defer import GenerationDefer
 from .lineage_archive import LineageSessionArchive
 from .nodes import chunk_nodes, path_nodes
 from .profiles import ModelProfile
+from .restore import (GC_PAUSES, configured_verification_mode, decoder_pool_record, decoder_pool_snapshot,
+                      gc_pause_record, install_gc_pauses, resident_lease_record, tier_record)
 from .seam import (CLEAN_COMMIT, KV_RECACHE, CaptureScope, CausalKVRequest, ChunkSlot, KVRecache, RecachePlan,
                    ReplayStep, RestoreTarget, check_capture, drive_request, plan_recache)
 from .session import SGLangSessionController, SGLangSessionState, prompt_tensor
@@ -166,6 +168,7 @@ class CausalWanKVBridge:
         self._unattributed: list[dict] = []
         self._boundary_hook = None
         self._inflight: list[tuple[str, dict]] = []
+        install_gc_pauses()
         from ...device_pressure import register_device_trim
         self._trims = [register_device_trim("raw_tier", self._trim_raw_tier, order=5, device=self.device),
                        register_device_trim("restorer", self._trim_restorer, device=self.device),
@@ -555,6 +558,9 @@ class _BridgeRun:
             self._start_event.record()
         claim = bridge._take_resident(state, need)
         runtime = bridge.archive.runtime
+        self._gc_before = GC_PAUSES.snapshot()
+        self._pool_before = decoder_pool_snapshot(getattr(bridge.archive, "decoder_pool", None))
+        verification = configured_verification_mode(bridge.config)
         if claim is not None:
             target.cache = claim.cache
             self.route = "resident"
@@ -564,7 +570,8 @@ class _BridgeRun:
                 bridge.archive.drain(state.session_id)
                 return chunk_nodes(runtime, bridge.sessions.head(state.session_id))
             target.latents = _PathLatents(runtime, published_nodes, known)
-            self.restore_report = {"mode": "resident", "chunks": done, "from_request": claim.request_id}
+            self.restore_report = {"mode": "resident", "chunks": done, "from_request": claim.request_id,
+                                   "lease": resident_lease_record(range(done), verification_mode=verification)}
         else:
             bridge._drop(state)
             capacity = max(need, bridge.cache_chunks)
@@ -587,7 +594,16 @@ class _BridgeRun:
                     if bridge.config.restore_mode == "recompute":
                         self._recompute(target, head, plan, done)
                     else:
+                        tier = bridge.archive.raw_tier
+                        held = set()
+                        if tier is not None and bridge.config.raw_restore == "prefer":
+                            for holder in {span.node_ref for span in plan.spans}:
+                                lease = tier.lookup(holder)
+                                if lease is not None:
+                                    held.add(holder)
+                                    lease.release()
                         self._archive_install(target, head, plan)
+                        self.restore_report["lease"] = tier_record(plan, held, verification_mode=verification)
                 if self.workload is not None:
                     p = bridge.profile
                     self.workload.set_restore(self.restore_report, tokens=plan.attended_tokens,
@@ -687,6 +703,10 @@ class _BridgeRun:
                 stats = install.join()
                 self.restore_report["stats"] = stats if stats is not None else install.stats
         finally:
+            if getattr(self, "_gc_before", None) is not None:
+                self.restore_report["gc"] = gc_pause_record(self._gc_before, GC_PAUSES.snapshot())
+                self.restore_report["decoder_pool"] = decoder_pool_record(
+                    self._pool_before, decoder_pool_snapshot(getattr(self.bridge.archive, "decoder_pool", None)))
             self._release_deferral()
             if self.bridge.defer is not None and error is None:
                 self.bridge.defer.after_restore(self.key)

@@ -25,7 +25,7 @@ from typing import Any, Callable, Mapping, Sequence
 import torch
 
 from ... import restore_kernels as rk
-from ...errors import ConfigurationError, StateError
+from ...errors import ConfigurationError, StateError, UnsupportedError
 from ...types import MatrixKey
 
 ROPE_TABLE_CACHE_BYTES = 64 << 20
@@ -316,5 +316,117 @@ def kernel_warmup_shapes(profile: Any, *, paths: Sequence[str] = ("pictures", "d
                            max_rank=max_rank) for path in paths]
 
 
-__all__ = ["AttentionKVLease", "BoundRopeTables", "DenseInstall", "DenseLayer", "LineageInstall", "RopeTableCache",
+# -- per-restore records (records only: a restore never waits for, changes or frees anything for them) ------------
+
+class GcPauses:
+    """Python's garbage collections and the seconds spent in them, per generation, counted by one ``gc.callbacks``
+    hook per process; a restore reports the change over its window. It never freezes, disables or runs a
+    collection."""
+
+    def __init__(self) -> None:
+        self.collections = [0, 0, 0]
+        self.seconds = [0.0, 0.0, 0.0]
+        self._open: float | None = None
+
+    def __call__(self, phase: str, info: Mapping[str, Any]) -> None:
+        if phase == "start":
+            self._open = time.perf_counter()
+        elif phase == "stop" and self._open is not None:
+            generation = max(0, min(2, int(info.get("generation", 2))))
+            self.collections[generation] += 1
+            self.seconds[generation] += time.perf_counter() - self._open
+            self._open = None
+
+    def snapshot(self) -> tuple[tuple[int, ...], tuple[float, ...]]:
+        return tuple(self.collections), tuple(self.seconds)
+
+
+GC_PAUSES = GcPauses()
+_GC_LOCK = threading.Lock()
+
+
+def install_gc_pauses() -> GcPauses:
+    """Install the process's collection counter once, however many bridges ask."""
+    import gc
+    with _GC_LOCK:
+        if all(callback is not GC_PAUSES for callback in gc.callbacks):
+            gc.callbacks.append(GC_PAUSES)
+    return GC_PAUSES
+
+
+def gc_pause_record(before, after) -> dict[str, Any]:
+    """The collections (per generation) and their seconds between two snapshots."""
+    if before is None or after is None:
+        return {"available": False}
+    collections = [b - a for a, b in zip(before[0], after[0])]
+    seconds = [b - a for a, b in zip(before[1], after[1])]
+    return {"available": True, "collections": collections, "seconds": seconds, "total_seconds": sum(seconds)}
+
+
+#: The tier of a resume that continues on the session's resident engine cache.
+RESIDENT_TIER = "resident"
+
+
+def configured_verification_mode(config: Any) -> str:
+    """How a restore verifies the payloads it reads: ``sync`` (hash every read, ``verify_reads``) or ``off``."""
+    return "sync" if getattr(config, "verify_reads", False) else "off"
+
+
+def resident_lease_record(chunks: Sequence[int], *, verification_mode: str) -> dict[str, Any]:
+    """A resident resume in the archive restore's record shape: every chunk ``resident``, nothing read or
+    verified."""
+    per_chunk = [{"chunk": index, "node": None, "tier": RESIDENT_TIER} for index in chunks]
+    return {"tiers": {"per_chunk": per_chunk, "chunks": {RESIDENT_TIER: len(per_chunk)} if per_chunk else {},
+                      "bytes": {}},
+            "verification": {"mode": verification_mode, "payload_wait_seconds": 0.0, "verified_payloads": 0}}
+
+
+def tier_record(plan, raw_holders: set, *, verification_mode: str) -> dict[str, Any]:
+    """An archive restore's per-span tiers: ``gpu_raw`` where the raw tier held the exact capture, else
+    ``compressed``."""
+    per_chunk, counts = [], {}
+    for span in plan.spans:
+        tier = "gpu_raw" if span.node_ref in raw_holders else "compressed"
+        per_chunk.append({"chunk": span.chunk_index, "node": span.node_ref, "tier": tier,
+                          "token_start": span.token_start, "tokens": span.length})
+        counts[tier] = counts.get(tier, 0) + 1
+    return {"tiers": {"per_chunk": per_chunk, "chunks": counts},
+            "verification": {"mode": verification_mode}}
+
+
+def check_restorable(plan, *, rope: bool = True) -> None:
+    """The fused restore installs whole latent frames when it applies RoPE: a span that cuts a frame is refused
+    before anything is issued (a RoPE-free install takes any rows)."""
+    if not rope:
+        return
+    for span in plan.spans:
+        frame = getattr(span, "frame_tokens", None)
+        if frame and (span.node_offset % frame or span.length % frame):
+            raise UnsupportedError(f"span of chunk {span.chunk_index} (offset {span.node_offset}, length {span.length})"
+                                   " cuts a latent frame")
+
+
+def decoder_pool_snapshot(pool: Any) -> dict[str, Any] | None:
+    """The decoder pool's counters now (None without a pool or readable stats: a record never fails a restore)."""
+    stats = getattr(pool, "stats", None)
+    if not callable(stats):
+        return None
+    try:
+        return dict(stats())
+    except Exception:  # noqa: BLE001 - records only
+        return None
+
+
+def decoder_pool_record(before: Mapping[str, Any] | None, after: Mapping[str, Any] | None) -> dict[str, Any]:
+    """The pool's numeric counters' change over one restore."""
+    if before is None or after is None:
+        return {"available": False}
+    delta = {k: after[k] - before[k] for k in after if isinstance(after.get(k), (int, float))
+             and isinstance(before.get(k), (int, float))}
+    return {"available": True, "delta": delta}
+
+
+__all__ = ["GC_PAUSES", "GcPauses", "RESIDENT_TIER", "check_restorable", "configured_verification_mode",
+           "decoder_pool_record", "decoder_pool_snapshot", "gc_pause_record", "install_gc_pauses",
+           "resident_lease_record", "tier_record", "AttentionKVLease", "BoundRopeTables", "DenseInstall", "DenseLayer", "LineageInstall", "RopeTableCache",
            "kernel_warmup_shapes", "restore_dense"]

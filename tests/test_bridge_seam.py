@@ -230,3 +230,26 @@ def test_workload_record_of_a_restoring_request(tmp_path):
         assert bridge.workload_record(report["request"]) is not None
     finally:
         bridge.shutdown()
+
+
+def test_restore_records_tiers_gc_and_verification(tmp_path):
+    import gc
+    from reelcache_b200.integrations.sglang.restore import GC_PAUSES, check_restorable, gc_pause_record
+    bridge = make_bridge(tmp_path, profile=PLAIN, verify_reads=True)
+    try:
+        bridge.request("s", action="create", chunks=2, seed=1)
+        resident = bridge.request("s", chunks=1, seed=1)
+        assert resident["restore"]["lease"]["tiers"]["chunks"] == {"resident": 2}
+        bridge.pause("s")
+        bridge.drop_resident("s")
+        restored = bridge.request("s", chunks=0)
+        lease = restored["restore"]["lease"]
+        assert lease["verification"]["mode"] == "sync" and sum(lease["tiers"]["chunks"].values()) == 3
+        assert set(lease["tiers"]["chunks"]) <= {"gpu_raw", "compressed"}
+        assert restored["restore"]["gc"]["available"]
+        before = GC_PAUSES.snapshot()
+        gc.collect()
+        assert gc_pause_record(before, GC_PAUSES.snapshot())["collections"][2] >= 1
+        check_restorable(bridge.plans.get((bridge.sessions.head("s"), 3)) or type("P", (), {"spans": ()})())
+    finally:
+        bridge.shutdown()
