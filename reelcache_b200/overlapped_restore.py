@@ -170,6 +170,39 @@ def start_overlapped_restore(issue: Callable[[int], Any], layers: int, *, stream
     return handle
 
 
+def start_overlapped_install(install: Callable[[int], Any], layers: int, *, stream=None, thread: bool = True,
+                             readiness: LayerReadiness | None = None, after: OverlappedRestore | None = None,
+                             finish: Callable[[], Any] | None = None) -> OverlappedRestore:
+    """A RAW (dense) install alone, layer-overlapped: ``install(layer)`` writes that layer's exact captured rows
+    (the dense RoPE-and-store kernel), each layer marked as a ``raw`` source so a forward that also waits for a
+    compressed restore (``sources=("restore", "raw")``) sees both."""
+    readiness = readiness or LayerReadiness(layers, sources=("raw",))
+    if "raw" not in readiness.sources:
+        raise StateError("an overlapped RAW install marks the 'raw' source of its readiness")
+
+    def issue(layer):
+        install(layer)
+
+    handle = start_overlapped_restore(issue, layers, stream=stream, thread=thread, readiness=_SourceView(readiness,
+                                                                                                          "raw"),
+                                      after=after, finish=finish)
+    handle.readiness = readiness
+    return handle
+
+
+class _SourceView:
+    """A readiness seen through one of its sources: ``mark`` marks that source."""
+
+    def __init__(self, readiness: LayerReadiness, source: str):
+        self._readiness, self._source = readiness, source
+
+    def mark(self, layer: int, event=None) -> None:
+        self._readiness.mark(layer, event, source=self._source)
+
+    def __getattr__(self, name):
+        return getattr(self._readiness, name)
+
+
 class _Null:
     def __enter__(self):
         return self

@@ -177,3 +177,21 @@ def test_lineage_install_places_pieces_at_plan_slots(runtime):
     v = caches[(1, "V")][0].reshape(2 * TOKENS, -1)
     assert relative_error(v[:TOKENS], dense[:TOKENS]) < 5e-3
     assert relative_error(v[TOKENS:], dense[2 * TOKENS:]) < 5e-3
+
+
+def test_overlapped_raw_install_marks_its_source():
+    from reelcache_b200.errors import StateError
+    from reelcache_b200.overlapped_restore import LayerReadiness, start_overlapped_install
+    issued = []
+    readiness = LayerReadiness(4, sources=("restore", "raw"))
+    handle = start_overlapped_install(issued.append, 4, readiness=readiness, thread=True)
+    for layer in range(4):
+        readiness.mark(layer, None, source="restore")
+    handle.join(30)
+    for layer in range(4):
+        readiness.wait(layer)
+    assert issued == [0, 1, 2, 3]
+    alone = start_overlapped_install(issued.append, 2, thread=False)
+    alone.readiness.wait(1)
+    with pytest.raises(StateError):
+        start_overlapped_install(issued.append, 2, readiness=LayerReadiness(2), thread=False)
