@@ -10,7 +10,8 @@
 // csrc/fit/fitter.cu (FP32 = hi + mid + lo, six cross products as K-concatenated segments) this is an
 // FP32 GEMM on the tensor cores.
 //
-// Roles (192 threads, one CTA per SM, persistent over 128 x 128 tiles):
+// Roles (192 threads, one CTA per SM, persistent over 128 x 128 tiles, or over (tile, K-split) items when the
+// tiles alone fill less than half of the SMs):
 //   warp 0      TMA producer (A and B tiles of 64 K per stage, 128-byte swizzle; plain loads).
 //   warp 1      TMEM owner and MMA issuer: chunk g of the CTA accumulates into TMEM buffer g % 4
 //               (4 x 128 columns), committed to acc_full[g % 4].
@@ -50,9 +51,19 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m_
   n_idx = r / gsize;
 }
 
+// Split-K: work item w covers tile w / splits and the chunks [s * per, min(chunks, (s + 1) * per)) of split
+// s = w % splits, storing its FP32 partial at out + s * split_stride (the host sums the partials in split order).
+__device__ __forceinline__ void item_range(int w, int splits, int per, int chunks, int& tile, int& c0, int& c1) {
+  tile = w / splits;
+  const int s = w - tile * splits;
+  c0 = s * per;
+  c1 = min(chunks, c0 + per);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_promoted_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
-                         int N, int K, float* __restrict__ out, int64_t ldo, float alpha, int* status) {
+                         int N, int K, float* __restrict__ out, int64_t ldo, float alpha, int* status, int splits,
+                         int64_t split_stride) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
@@ -69,6 +80,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_tiles = num_m * num_n;
   const int kblocks = (K + kBK - 1) / kBK;
   const int chunks = (kblocks + kChunk - 1) / kChunk;
+  const int per = (chunks + splits - 1) / splits;
+  const int num_items = num_tiles * splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -98,10 +111,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+        int t, c0, c1;
+        item_range(w, splits, per, chunks, t, c0, c1);
         int m_idx, n_idx;
         tile_coords(t, num_m, num_n, m_idx, n_idx);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int kb_stop = min(kblocks, c1 * kChunk);
+        for (int kb = c0 * kChunk; kb < kb_stop; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, status, kTimeoutProducer)) {
             ok = false;
             break;
@@ -123,8 +139,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     int g = 0;  // chunk counter of this CTA
     bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-      for (int c = 0; c < chunks && ok; ++c, ++g) {
+    for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+      int t, c0, c1;
+      item_range(w, splits, per, chunks, t, c0, c1);
+      for (int c = c0; c < c1 && ok; ++c, ++g) {
         const int buf = g % kBufs;
         const uint32_t acc_phase = (g / kBufs) & 1;
         if (lane == 0) ok = mbar_wait(&acc_empty[buf], acc_phase ^ 1, status, kTimeoutMma);
@@ -167,13 +185,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     int g = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+    for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+      int t, c0, c1;
+      item_range(w, splits, per, chunks, t, c0, c1);
       int m_idx, n_idx;
       tile_coords(t, num_m, num_n, m_idx, n_idx);
+      float* part = out + static_cast<int64_t>(w - t * splits) * split_stride;
       float acc[kBN];
 #pragma unroll
       for (int j = 0; j < kBN; ++j) acc[j] = 0.0f;
-      for (int c = 0; c < chunks; ++c, ++g) {
+      for (int c = c0; c < c1; ++c, ++g) {
         const int buf = g % kBufs;
         const uint32_t acc_phase = (g / kBufs) & 1;
         if (lane == 0) ok = mbar_wait(&acc_full[buf], acc_phase, status, kTimeoutEpilogue);
@@ -196,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       const int row = m_idx * kBM + quarter * 32 + lane;
       if (row < M) {
-        float* orow = out + static_cast<int64_t>(row) * ldo + n_idx * kBN;
+        float* orow = part + static_cast<int64_t>(row) * ldo + n_idx * kBN;
         const int valid = min(kBN, N - n_idx * kBN);
         if (valid == kBN && (reinterpret_cast<uintptr_t>(orow) & 15) == 0) {
 #pragma unroll
@@ -245,12 +266,34 @@ void gemm_bf16_promoted(const at::Tensor& A, const at::Tensor& B, at::Tensor& ou
     configured = true;
   }
   const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-  const int grid = std::min(tiles, sm_count(A.get_device()));
+  const int sms = sm_count(A.get_device());
+  const int chunks = ((K + kBK - 1) / kBK + kChunk - 1) / kChunk;
+  // Split K when the tiles fill less than half of the SMs: each split keeps >= 2 chunks (256 K-elements), the
+  // partials land in a workspace and are summed in split order (IEEE FP32 adds of FP32-accurate partials).
+  int splits = 1;
+  if (tiles * 2 <= sms && chunks >= 4) splits = std::min(chunks / 2, (sms + tiles - 1) / tiles);
+  if (splits > 1) {
+    const int per = (chunks + splits - 1) / splits;
+    splits = (chunks + per - 1) / per;  // no empty split
+  }
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream(A.get_device()).stream();
-  gemm_promoted_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmA, tmB, M, N, K, out.data_ptr<float>(),
-                                                                out.stride(0), static_cast<float>(alpha),
-                                                                status_ptr(status));
+  if (splits == 1) {
+    const int grid = std::min(tiles, sms);
+    gemm_promoted_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmA, tmB, M, N, K, out.data_ptr<float>(),
+                                                                  out.stride(0), static_cast<float>(alpha),
+                                                                  status_ptr(status), 1, 0);
+    RC_CUDA(cudaGetLastError());
+    return;
+  }
+  at::Tensor work = at::empty({splits, M, N}, out.options());
+  const int grid = std::min(tiles * splits, sms);
+  gemm_promoted_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmA, tmB, M, N, K, work.data_ptr<float>(), N,
+                                                                static_cast<float>(alpha), status_ptr(status),
+                                                                splits, static_cast<int64_t>(M) * N);
   RC_CUDA(cudaGetLastError());
+  at::Tensor sum = work.select(0, 0).clone();
+  for (int s = 1; s < splits; ++s) sum.add_(work.select(0, s));  // split order: fixed, deterministic
+  out.copy_(sum);
 }
 
 }  // namespace rc
