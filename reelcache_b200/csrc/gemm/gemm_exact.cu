@@ -52,7 +52,7 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m_
 }
 
 // Split-K: work item w covers tile w / splits and the chunks [s * per, min(chunks, (s + 1) * per)) of split
-// s = w % splits, storing its FP32 partial at out + s * split_stride (the host sums the partials in split order).
+// s = w % splits, storing its FP32 partial at out + s * split_stride (one reduction sums the partials).
 __device__ __forceinline__ void item_range(int w, int splits, int per, int chunks, int& tile, int& c0, int& c1) {
   tile = w / splits;
   const int s = w - tile * splits;
@@ -269,7 +269,7 @@ void gemm_bf16_promoted(const at::Tensor& A, const at::Tensor& B, at::Tensor& ou
   const int sms = sm_count(A.get_device());
   const int chunks = ((K + kBK - 1) / kBK + kChunk - 1) / kChunk;
   // Split K when the tiles fill less than half of the SMs: each split keeps >= 2 chunks (256 K-elements), the
-  // partials land in a workspace and are summed in split order (IEEE FP32 adds of FP32-accurate partials).
+  // partials land in a workspace and one deterministic reduction sums them (FP32 adds of FP32-accurate partials).
   int splits = 1;
   if (tiles * 2 <= sms && chunks >= 4) splits = std::min(chunks / 2, (sms + tiles - 1) / tiles);
   if (splits > 1) {
@@ -291,9 +291,7 @@ void gemm_bf16_promoted(const at::Tensor& A, const at::Tensor& B, at::Tensor& ou
                                                                 static_cast<float>(alpha), status_ptr(status),
                                                                 splits, static_cast<int64_t>(M) * N);
   RC_CUDA(cudaGetLastError());
-  at::Tensor sum = work.select(0, 0).clone();
-  for (int s = 1; s < splits; ++s) sum.add_(work.select(0, s));  // split order: fixed, deterministic
-  out.copy_(sum);
+  at::sum_out(out, work, {0});  // one deterministic reduction over the splits
 }
 
 }  // namespace rc

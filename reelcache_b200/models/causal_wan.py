@@ -107,6 +107,28 @@ class KVCache:
         return 2 * self.cfg.layers * self.k[0].numel() * self.k[0].element_size()
 
 
+class SPKVCache(KVCache):
+    """A Ulysses rank's native caches: every token of the history for this rank's ``heads / world`` heads
+    (``[1, capacity, heads / world, head_dim]``), the "heads" layout a sequence-parallel restore writes."""
+
+    def __init__(self, cfg: WanConfig, capacity_chunks: int, device, *, world: int, rank: int,
+                 dtype=torch.bfloat16):
+        if cfg.heads % world:
+            raise ValueError("heads must divide evenly across the Ulysses ranks")
+        self.cfg = cfg
+        self.world, self.rank = world, rank
+        self.heads = cfg.heads // world
+        self.capacity = capacity_chunks * cfg.chunk_tokens
+        self.k = [torch.zeros((1, self.capacity, self.heads, cfg.head_dim), dtype=dtype, device=device)
+                  for _ in range(cfg.layers)]
+        self.v = [torch.zeros_like(self.k[0]) for _ in range(cfg.layers)]
+        self.length = 0
+
+    def rows(self, layer: int, which: str) -> torch.Tensor:
+        t = self.k[layer] if which == "K" else self.v[layer]
+        return t.view(self.capacity, self.heads * self.cfg.head_dim)
+
+
 class CausalWanDiT:
     """The causal DiT (weights as plain tensors; forward uses the sm_100a ops)."""
 
@@ -242,6 +264,75 @@ class CausalWanDiT:
         y = norms.ln_modulate(x, shift=shift, scale=scale, eps=cfg.eps)
         out = gemm.linear(y, self.head_w, self.head_b, out_dtype=torch.float32)
         return self.unpatchify(out)
+
+    def forward_chunk_sp(self, latents: torch.Tensor, t: float, chunk_index: int, cache: SPKVCache, text_kv, *,
+                         group, capture=None, layer_wait=None, attention_backend: str = "auto") -> torch.Tensor:
+        """:meth:`forward_chunk` under Ulysses sequence parallelism over ``group``: this rank projects, normalizes
+        and ropes its contiguous ``tokens / world`` rows (the full-width q / k RMSNorm needs every head of a
+        token, so it runs before the head split), one all-to-all per layer hands every rank all tokens of its
+        ``heads / world`` heads (K and V land in its cache slot), attention runs over the full history of those
+        heads, one all-to-all returns the outputs to their token rows, and cross-attention and the FFN stay on
+        the rank's rows. ``capture(layer, k_pre, v)`` receives this rank's token rows (all heads). Returns the
+        full flow prediction on every rank (one all-gather)."""
+        import torch.distributed as dist
+        cfg = self.cfg
+        world, rank = cache.world, cache.rank
+        tokens = cfg.chunk_tokens
+        if tokens % world:
+            raise ValueError("the chunk's tokens must divide evenly across the Ulysses ranks")
+        n_loc, hp, d = tokens // world, cache.heads, cfg.head_dim
+        rows = slice(rank * n_loc, (rank + 1) * n_loc)
+        start = chunk_index * tokens
+        end = start + tokens
+        if end > cache.capacity:
+            raise ValueError("chunk exceeds the KV cache capacity")
+        x = gemm.linear(self.patchify(latents)[rows].to(torch.bfloat16).contiguous(), self.patch_w, self.patch_b)
+        e, e0 = self.time_modulation(t)
+        cos_tok, sin_tok = self.token_rope(chunk_index)
+        cos_loc, sin_loc = cos_tok[rows].contiguous(), sin_tok[rows].contiguous()
+        q = torch.empty((n_loc, cfg.dim), dtype=torch.bfloat16, device=self.device)
+        k_loc, v_loc = torch.empty_like(q), torch.empty_like(q)
+        k_pre = torch.empty_like(q) if capture is not None else None
+        send = torch.empty((world, 3, n_loc, hp, d), dtype=torch.bfloat16, device=self.device)
+        recv = torch.empty_like(send)
+        back = torch.empty((world, n_loc, hp, d), dtype=torch.bfloat16, device=self.device)
+        stream = torch.cuda.current_stream(self.device)
+        for layer, blk in enumerate(self.blocks):
+            mod = blk["modulation"] + e0
+            y = norms.ln_modulate(x, shift=mod[0], scale=mod[1], eps=cfg.eps)
+            qkv = gemm.linear(y, blk["qkv_w"], blk["qkv_b"])
+            norms.qkv_norm_rope(qkv, blk["norm_q"], blk["norm_k"], cos_loc, sin_loc, q, k_loc, v_loc,
+                                head_dim=d, k_pre=k_pre, eps=cfg.eps)
+            if capture is not None:
+                capture(layer, k_pre, v_loc)
+            for index, part in enumerate((q, k_loc, v_loc)):   # [n_loc, world, hp, d] -> [world, n_loc, hp, d]
+                send[:, index].copy_(part.view(n_loc, world, hp, d).transpose(0, 1))
+            dist.all_to_all_single(recv, send, group=group)
+            cache.k[layer][0, start:end].view(world, n_loc, hp, d).copy_(recv[:, 1])
+            cache.v[layer][0, start:end].view(world, n_loc, hp, d).copy_(recv[:, 2])
+            if layer_wait is not None:
+                layer_wait(layer, stream)
+            o = attn_ops.attention(recv[:, 0].reshape(tokens, hp, d), cache.k[layer][0, :end],
+                                   cache.v[layer][0, :end], backend=attention_backend)
+            dist.all_to_all_single(back, o.view(world, n_loc, hp, d), group=group)
+            o_loc = back.transpose(0, 1).reshape(n_loc, cfg.dim)
+            gemm.linear_gated_residual(o_loc, blk["o_w"], blk["o_b"], mod[2].contiguous(), x)
+            y = norms.ln_modulate(x, weight=blk["norm3_w"], bias=blk["norm3_b"], eps=cfg.eps)
+            cq = norms.rms_norm(gemm.linear(y, blk["cq_w"], blk["cq_b"]), blk["cnorm_q"], eps=cfg.eps)
+            ck, cv = text_kv[layer]
+            co = attn_ops.attention(cq.view(n_loc, cfg.heads, d), ck.view(-1, cfg.heads, d),
+                                    cv.view(-1, cfg.heads, d), backend=attention_backend)
+            gemm.linear_gated_residual(co.view(n_loc, cfg.dim), blk["co_w"], blk["co_b"], None, x)
+            y = norms.ln_modulate(x, shift=mod[3], scale=mod[4], eps=cfg.eps)
+            h = gemm.linear_gelu(y, blk["ffn1_w"], blk["ffn1_b"])
+            gemm.linear_gated_residual(h, blk["ffn2_w"], blk["ffn2_b"], mod[5].contiguous(), x)
+        shift = (self.head_mod[0] + e).contiguous()
+        scale = (self.head_mod[1] + e).contiguous()
+        y = norms.ln_modulate(x, shift=shift, scale=scale, eps=cfg.eps)
+        out = gemm.linear(y, self.head_w, self.head_b, out_dtype=torch.float32)
+        full = torch.empty((world, n_loc, out.shape[1]), dtype=out.dtype, device=self.device)
+        dist.all_gather_into_tensor(full, out.contiguous(), group=group)
+        return self.unpatchify(full.view(tokens, out.shape[1]))
 
     def flops_per_forward(self, history_tokens: int) -> float:
         cfg = self.cfg

@@ -31,13 +31,21 @@ class ChunkGenerator:
     """Drives :class:`CausalWanDiT` chunk by chunk over one :class:`KVCache`."""
 
     def __init__(self, model: CausalWanDiT, cache: KVCache, text_kv, *, timesteps=CAUSVID_TIMESTEPS, seed: int = 0,
-                 attention_backend: str = "auto"):
+                 attention_backend: str = "auto", group=None):
+        """``group``: a Ulysses sequence-parallel process group (the cache is then this rank's
+        :class:`~reelcache_b200.models.causal_wan.SPKVCache`; every rank draws the same noise)."""
+        self.group = group
         self.model = model
         self.cache = cache
         self.text_kv = text_kv
         self.timesteps = tuple(timesteps)
         self.generator = torch.Generator(device=model.device).manual_seed(seed)
         self.attention_backend = attention_backend
+
+    def _forward(self, *args, **kwargs):
+        if self.group is None:
+            return self.model.forward_chunk(*args, **kwargs)
+        return self.model.forward_chunk_sp(*args, group=self.group, **kwargs)
 
     def noise(self) -> torch.Tensor:
         cfg = self.model.cfg
@@ -51,7 +59,7 @@ class ChunkGenerator:
         x0 = x
         for step, t in enumerate(self.timesteps):
             sigma = t / 1000.0
-            flow = self.model.forward_chunk(x, t, index, self.cache, self.text_kv,
+            flow = self._forward(x, t, index, self.cache, self.text_kv,
                                             layer_wait=layer_wait if step == 0 else None,
                                             attention_backend=self.attention_backend)
             x0 = x - sigma * flow
@@ -63,7 +71,7 @@ class ChunkGenerator:
     def commit_clean(self, index: int, latents: torch.Tensor, *, capture: Callable | None = None) -> None:
         """The clean (t = 0) forward: writes the chunk's clean K/V into its slot; ``capture(layer, k_pre, v)``
         receives the archive inputs."""
-        self.model.forward_chunk(latents, 0.0, index, self.cache, self.text_kv, capture=capture,
+        self._forward(latents, 0.0, index, self.cache, self.text_kv, capture=capture,
                                  attention_backend=self.attention_backend)
         self.cache.length = max(self.cache.length, (index + 1) * self.model.cfg.chunk_tokens)
 

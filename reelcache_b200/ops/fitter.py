@@ -51,12 +51,75 @@ SPLIT_A_BF16 = (0, 0, 0)
 SPLIT_B_BF16 = (2, 1, 0)
 
 
+class _SplitCache:
+    """Split operands of tensors that are multiplied again and again (a Gram matrix through a subspace iteration,
+    a source matrix through its projections), kept while the tensor lives and is unchanged.
+
+    An entry is keyed by the operand's root tensor (held weakly: a freed tensor's entry never matches the tensor
+    that reuses its memory), its view geometry, the split parts and the root's version counter (an in-place write
+    invalidates it); entries are bounded in bytes, least recently used first out."""
+
+    def __init__(self, max_bytes: int = 4 << 30):
+        import threading
+        from collections import OrderedDict
+        self.max_bytes = max_bytes
+        self._entries: "OrderedDict[tuple, tuple]" = OrderedDict()
+        self._bytes = 0
+        self._lock = threading.Lock()
+        self.hits = self.misses = 0
+
+    @staticmethod
+    def _key(x: torch.Tensor, parts) -> tuple:
+        root = x._base if x._base is not None else x
+        return (id(root), x.data_ptr(), tuple(x.shape), tuple(x.stride()), x.dtype, tuple(parts)), root
+
+    def get(self, x: torch.Tensor, parts) -> torch.Tensor:
+        import weakref
+        key, root = self._key(x, parts)
+        with self._lock:
+            entry = self._entries.get(key)
+            if entry is not None:
+                ref, version, value = entry
+                if ref() is root and version == root._version:
+                    self._entries.move_to_end(key)
+                    self.hits += 1
+                    return value
+                self._bytes -= value.numel() * value.element_size()
+                del self._entries[key]
+        value, _ = split_operand(x, parts)
+        size = value.numel() * value.element_size()
+        with self._lock:
+            self.misses += 1
+            if size <= self.max_bytes // 4:
+                self._entries[key] = (weakref.ref(root), root._version, value)
+                self._bytes += size
+                while self._bytes > self.max_bytes and self._entries:
+                    _, (_, _, old) = self._entries.popitem(last=False)
+                    self._bytes -= old.numel() * old.element_size()
+            self._sweep()
+        return value
+
+    def _sweep(self) -> None:
+        """Drop entries whose tensors died (called under the lock)."""
+        for key in [k for k, (ref, _, _) in self._entries.items() if ref() is None]:
+            value = self._entries.pop(key)[2]
+            self._bytes -= value.numel() * value.element_size()
+
+    def clear(self) -> None:
+        with self._lock:
+            self._entries.clear()
+            self._bytes = 0
+
+
+SPLITS = _SplitCache()
+
+
 def mm_fp32(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """FP32-accurate ``a @ b`` (``a[M, K]``, ``b[K, N]``): split-bf16 operands, one tcgen05 GEMM with promoted
-    accumulation."""
+    """FP32-accurate ``a @ b`` (``a[M, K]``, ``b[K, N]``): split-bf16 operands (reused while an operand's tensor is
+    unchanged), one tcgen05 GEMM with promoted accumulation."""
     parts_a, parts_b = (SPLIT_A_BF16, SPLIT_B_BF16) if a.dtype == torch.bfloat16 else (SPLIT_A, SPLIT_B)
-    a_split, _ = split_operand(a, parts_a)
-    b_split, _ = split_operand(b.t(), parts_b)
+    a_split = SPLITS.get(a, parts_a)
+    b_split = SPLITS.get(b.t(), parts_b)
     return matmul_promoted(a_split, b_split)
 
 
