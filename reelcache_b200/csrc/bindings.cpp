@@ -24,6 +24,8 @@ void qkv_norm_rope(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor
                    const at::Tensor& sin_tok, at::Tensor& q_out, const c10::optional<at::Tensor>& k_pre,
                    at::Tensor& k_cache, at::Tensor& v_cache, int64_t head_dim, double eps);
 void rms_norm(const at::Tensor& x, at::Tensor& y, const at::Tensor& w, double eps);
+void head_norm_rope(const at::Tensor& x, at::Tensor& y, const c10::optional<at::Tensor>& w,
+                    const c10::optional<at::Tensor>& cos_tok, const c10::optional<at::Tensor>& sin_tok, double eps);
 void quantize_columns(const at::Tensor& p, const at::Tensor& scale, const at::Tensor& offset, at::Tensor& out);
 void rope_store_launch(const at::Tensor& jobs);
 void unpack_launch(const at::Tensor& jobs, int64_t device);
@@ -85,6 +87,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_norm_rope", &rc::qkv_norm_rope, "q/k RMSNorm + RoPE from fused qkv into q and KV-cache slots",
         py::arg("qkv"), py::arg("wq"), py::arg("wk"), py::arg("cos_tok"), py::arg("sin_tok"), py::arg("q_out"),
         py::arg("k_pre"), py::arg("k_cache"), py::arg("v_cache"), py::arg("head_dim"), py::arg("eps") = 1e-6);
+  m.def("head_norm_rope", &rc::head_norm_rope, "per-head RMSNorm and / or interleaved RoPE of [T, H, D]",
+        py::arg("x"), py::arg("y"), py::arg("w"), py::arg("cos_tok"), py::arg("sin_tok"), py::arg("eps"));
   m.def("rms_norm", &rc::rms_norm, "y = RMSNorm(x) * w", py::arg("x"), py::arg("y"), py::arg("w"),
         py::arg("eps") = 1e-6);
   m.def("prep_launch", &rc::prep_launch, "scaled hi/lo basis + bias preparation over <= 48 jobs", py::arg("jobs"),

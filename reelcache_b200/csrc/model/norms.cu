@@ -201,6 +201,54 @@ __global__ void rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx
   store_row<VEC>(y + static_cast<int64_t>(row) * ldy, C, lane, v);
 }
 
+// Per-head RMSNorm and / or interleaved-pair RoPE of [tokens, heads, head_dim] rows (LongCat's q / k): one warp
+// per (token, head); lane l holds head_dim / 32 consecutive elements, so every rotated pair stays in one lane.
+template <int PER>
+__global__ void head_norm_rope_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_ts, int64_t x_hs,
+                                      __nv_bfloat16* __restrict__ y, int64_t y_ts, int64_t y_hs, int tokens,
+                                      int heads, const float* __restrict__ w, const float* __restrict__ cos_tok,
+                                      const float* __restrict__ sin_tok, float eps) {
+  const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (item >= tokens * heads) return;
+  const int token = item / heads;
+  const int head = item - token * heads;
+  constexpr int kHeadDim = PER * 32;
+  const __nv_bfloat16* src = x + static_cast<int64_t>(token) * x_ts + static_cast<int64_t>(head) * x_hs + lane * PER;
+  float v[PER];
+#pragma unroll
+  for (int i = 0; i < PER; i += 2) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + i));
+    v[i] = f.x;
+    v[i + 1] = f.y;
+  }
+  if (w != nullptr) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) ss = fmaf(v[i], v[i], ss);
+#pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, offset);
+    const float r = rsqrtf(ss / kHeadDim + eps);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) v[i] = v[i] * r * __ldg(w + lane * PER + i);
+  }
+  if (cos_tok != nullptr) {
+    const float* cs = cos_tok + static_cast<int64_t>(token) * (kHeadDim / 2) + lane * (PER / 2);
+    const float* sn = sin_tok + static_cast<int64_t>(token) * (kHeadDim / 2) + lane * (PER / 2);
+#pragma unroll
+    for (int i = 0; i < PER / 2; ++i) {
+      const float c = __ldg(cs + i), s = __ldg(sn + i);
+      const float a = v[2 * i], b = v[2 * i + 1];
+      v[2 * i] = a * c - b * s;
+      v[2 * i + 1] = a * s + b * c;
+    }
+  }
+  __nv_bfloat16* dst = y + static_cast<int64_t>(token) * y_ts + static_cast<int64_t>(head) * y_hs + lane * PER;
+#pragma unroll
+  for (int i = 0; i < PER; i += 2)
+    *reinterpret_cast<__nv_bfloat162*>(dst + i) = __floats2bfloat162_rn(v[i], v[i + 1]);
+}
+
 }  // namespace norms
 
 namespace {
@@ -297,6 +345,52 @@ void rms_norm(const at::Tensor& x, at::Tensor& y, const at::Tensor& w, double ep
   RC_VEC_DISPATCH(C, norms::rms_norm_kernel, reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
                   reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), rows, C, opt_f32(w, C, "w"),
                   static_cast<float>(eps));
+}
+
+void head_norm_rope(const at::Tensor& x, at::Tensor& y, const c10::optional<at::Tensor>& w,
+                    const c10::optional<at::Tensor>& cos_tok, const c10::optional<at::Tensor>& sin_tok, double eps) {
+  RC_CHECK(x.is_cuda() && y.is_cuda() && x.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16 &&
+               x.dim() == 3 && y.dim() == 3 && x.sizes() == y.sizes() && x.stride(2) == 1 && y.stride(2) == 1,
+           "x and y must be CUDA bfloat16 [tokens, heads, head_dim] with unit inner stride");
+  const int tokens = static_cast<int>(x.size(0)), heads = static_cast<int>(x.size(1));
+  const int head_dim = static_cast<int>(x.size(2));
+  RC_CHECK(head_dim == 64 || head_dim == 128 || head_dim == 256, "head_dim must be 64, 128 or 256");
+  RC_CHECK(x.stride(0) % 2 == 0 && x.stride(1) % 2 == 0 && y.stride(0) % 2 == 0 && y.stride(1) % 2 == 0 &&
+               reinterpret_cast<uintptr_t>(x.data_ptr()) % 4 == 0 && reinterpret_cast<uintptr_t>(y.data_ptr()) % 4 == 0,
+           "rows must be 4-byte aligned");
+  const float* wp = opt_f32(w, head_dim, "w");
+  RC_CHECK(cos_tok.has_value() == sin_tok.has_value(), "cos and sin come together");
+  const float* cp = nullptr;
+  const float* sp = nullptr;
+  if (cos_tok.has_value() && cos_tok->defined()) {
+    RC_CHECK(cos_tok->is_cuda() && cos_tok->scalar_type() == at::kFloat && cos_tok->is_contiguous() &&
+                 sin_tok->is_contiguous() && cos_tok->numel() == static_cast<int64_t>(tokens) * (head_dim / 2) &&
+                 sin_tok->numel() == cos_tok->numel(),
+             "cos / sin must be contiguous CUDA float32 [tokens, head_dim / 2]");
+    cp = cos_tok->data_ptr<float>();
+    sp = sin_tok->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(x.get_device()).stream();
+  const int64_t items = static_cast<int64_t>(tokens) * heads;
+  if (items == 0) return;
+  dim3 grid(static_cast<unsigned>((items + 7) / 8));
+  const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  auto* yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  switch (head_dim) {
+    case 64:
+      norms::head_norm_rope_kernel<2><<<grid, 256, 0, stream>>>(xp, x.stride(0), x.stride(1), yp, y.stride(0),
+                                                                y.stride(1), tokens, heads, wp, cp, sp, (float)eps);
+      break;
+    case 128:
+      norms::head_norm_rope_kernel<4><<<grid, 256, 0, stream>>>(xp, x.stride(0), x.stride(1), yp, y.stride(0),
+                                                                y.stride(1), tokens, heads, wp, cp, sp, (float)eps);
+      break;
+    default:
+      norms::head_norm_rope_kernel<8><<<grid, 256, 0, stream>>>(xp, x.stride(0), x.stride(1), yp, y.stride(0),
+                                                                y.stride(1), tokens, heads, wp, cp, sp, (float)eps);
+  }
+  RC_CUDA(cudaGetLastError());
 }
 
 }  // namespace rc

@@ -481,9 +481,19 @@ __global__ void __launch_bounds__(kThreads, 1) restore_kernel(const __grid_const
 #pragma unroll
               for (int i = 0; i < 16; ++i) finish(16 * h + i, __ldg(cos_row + pair0 + i), __ldg(sin_row + pair0 + i));
             }
-          } else {
+          } else {  // no RoPE (V, or a RoPE-free K): scale, bias and pack only
 #pragma unroll
-            for (int i = 0; i < 32; ++i) finish(i, 1.0f, 0.0f);
+            for (int i = 0; i < 32; ++i) {
+              const float2 b = bias_in_smem ? bias2[i] : __ldg(bias2 + i);
+              const float e = fmaf(__uint_as_float(r[2 * i]), inv, b.x);
+              const float o = fmaf(__uint_as_float(r[2 * i + 1]), inv, b.y);
+              if constexpr (OUT == kOutF32) {
+                r[2 * i] = __float_as_uint(e);
+                r[2 * i + 1] = __float_as_uint(o);
+              } else {
+                r[i] = OUT == kOutBF16 ? pack_bf16x2(e, o) : pack_f16x2(e, o);
+              }
+            }
           }
           if constexpr (OUT != kOutF32) {
             if (p.ablate == 1) {

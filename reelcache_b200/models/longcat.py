@@ -128,8 +128,26 @@ class _Ops:
 
     def rms_norm_heads(self, x, weight, eps):
         """Per-head RMSNorm in FP32 of ``[tokens, heads, head_dim]``."""
+        if self.kernels:
+            from ..ops.norms import head_norm_rope
+            return head_norm_rope(x, weight, eps=eps)
         xf = x.float()
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * weight.float()).to(x.dtype)
+
+    def norm_rope(self, x, weight, cos, sin, eps, *, out=None):
+        """Per-head RMSNorm (``weight`` None: none) then RoPE of ``[tokens, heads, head_dim]``: one fused kernel on
+        CUDA (FP32 throughout), two eager steps otherwise."""
+        if self.kernels:
+            from ..ops.norms import head_norm_rope
+            return head_norm_rope(x, weight, cos, sin, eps=eps, out=out)
+        y = _rope(self.rms_norm_heads(x, weight, eps) if weight is not None else x, cos, sin)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+
+    def rope(self, x, cos, sin):
+        return self.norm_rope(x, None, cos, sin, 0.0)
 
     def attention(self, q, k, v):
         """``[Tq, H, D]`` x ``[Tk, H, D]`` -> ``[Tq, H, D]`` (non-causal)."""
@@ -231,7 +249,7 @@ class LongCatDiT:
         cshards = [RowShard(sh.rank, sh.cp, cache.epoch.frames, *self.cfg.grid) for sh in shards]
         rank = dist_rank(cp_group)
         cos_c, sin_c = self.rope_tables(cache.epoch.first_frame, cache.epoch.frames, cshards[rank])
-        layers = [(ulysses_in(_rope(cache.k[layer].to(self.dtype), cos_c, sin_c).contiguous(), cp_group),
+        layers = [(ulysses_in(self.ops.rope(cache.k[layer].to(self.dtype), cos_c, sin_c).contiguous(), cp_group),
                    ulysses_in(cache.v[layer].to(self.dtype).contiguous(), cp_group)) for layer in range(len(self.blocks))]
         self._ulysses_memo = (key, layers)
         return layers
@@ -278,8 +296,8 @@ class LongCatDiT:
             if ulysses is not None:
                 rows = ulysses.world * n
                 q_u, k_u, _ = ulysses.qkv(y.to(self.dtype), blk["qkv_w"], blk["qkv_b"])
-                q = _rope(self.ops.rms_norm_heads(q_u, blk["q_norm"], cfg.eps), cos_g, sin_g)
-                k_u.copy_(_rope(self.ops.rms_norm_heads(k_u, blk["k_norm"], cfg.eps), cos_g, sin_g))
+                q = self.ops.norm_rope(q_u, blk["q_norm"], cos_g, sin_g, cfg.eps)
+                self.ops.norm_rope(k_u, blk["k_norm"], cos_g, sin_g, cfg.eps, out=k_u)  # in place: row by row
                 if cache_u is not None:
                     ulysses.set_cache(*cache_u[layer])
                 k_all, v_all = ulysses.kv_all(rows)
@@ -294,11 +312,12 @@ class LongCatDiT:
             if return_kv:
                 kvs.append((k.clone(), v.clone()))
             if cache is not None:  # conditioning-cache branch: RoPE applied at read time
-                k_all = torch.cat([_rope(cache.k[layer].to(k.dtype), cos_c, sin_c), _rope(k, cos_cur, sin_cur)])
+                k_all = torch.cat([self.ops.rope(cache.k[layer].to(k.dtype), cos_c, sin_c),
+                                   self.ops.rope(k, cos_cur, sin_cur)])
                 v_all = torch.cat([cache.v[layer].to(v.dtype), v])
             else:
-                k_all, v_all = _rope(k, cos_cur, sin_cur), v
-            q = _rope(q, cos_cur, sin_cur)
+                k_all, v_all = self.ops.rope(k, cos_cur, sin_cur), v
+            q = self.ops.rope(q, cos_cur, sin_cur)
             if shard is not None:
                 o = ulysses_out(self.ops.attention(ulysses_in(q, cp_group), ulysses_in(k_all.contiguous(), cp_group),
                                                    ulysses_in(v_all.contiguous(), cp_group)), cp_group)

@@ -27,3 +27,13 @@ def rms_norm(x, w, *, eps=1e-6, out=None):
     out = torch.empty_like(x2) if out is None else out.reshape(-1, x.shape[-1])
     ext().rms_norm(x2, out, w, float(eps))
     return out.reshape(x.shape)
+
+
+def head_norm_rope(x, weight=None, cos=None, sin=None, *, eps=1e-6, out=None):
+    """Per-head RMSNorm (``weight`` [head_dim], optional) then interleaved-pair RoPE (``cos`` / ``sin``
+    [tokens, head_dim / 2], optional) of ``x[tokens, heads, head_dim]`` in one pass; FP32 math, bf16 out."""
+    out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device) if out is None else out
+    ext().head_norm_rope(x, out, None if weight is None else weight.float().contiguous(),
+                         None if cos is None else cos.float().contiguous(),
+                         None if sin is None else sin.float().contiguous(), float(eps))
+    return out

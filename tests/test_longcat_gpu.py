@@ -47,3 +47,28 @@ def test_fused_segment_restore_matches_host_decode(tmp_path, cp):
             err = float((a.float() - b.float()).abs().max())
             assert err <= 2e-2 * float(a.float().abs().max()) + 1e-3, err
     store.close()
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_head_norm_rope_matches_fp32_reference(head_dim):
+    from reelcache_b200.ops.norms import head_norm_rope
+    g = torch.Generator(device="cuda").manual_seed(1)
+    tokens, heads = 300, 6
+    base = torch.randn(tokens, 3, heads, head_dim, generator=g, device="cuda").to(torch.bfloat16)
+    x = base[:, 1]                                   # a strided view, as a fused qkv's K
+    w = torch.rand(head_dim, generator=g, device="cuda") + 0.5
+    angle = torch.rand(tokens, head_dim // 2, generator=g, device="cuda") * 6.28
+    cos, sin = angle.cos(), angle.sin()
+    xf = x.float()
+    normed = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w
+    e, o = normed[..., 0::2], normed[..., 1::2]
+    ref = torch.stack((e * cos[:, None] - o * sin[:, None], e * sin[:, None] + o * cos[:, None]), -1).flatten(-2)
+    got = head_norm_rope(x, w, cos, sin, eps=1e-6).float()
+    assert float((got - ref).abs().max()) <= 1e-2 * float(ref.abs().max())
+    only_norm = head_norm_rope(x, w, eps=1e-6).float()
+    assert float((only_norm - normed).abs().max()) <= 1e-2 * float(normed.abs().max())
+    inplace = x.clone()
+    head_norm_rope(inplace, None, cos, sin, out=inplace)
+    xe, xo = xf[..., 0::2], xf[..., 1::2]
+    rot = torch.stack((xe * cos[:, None] - xo * sin[:, None], xe * sin[:, None] + xo * cos[:, None]), -1).flatten(-2)
+    assert float((inplace.float() - rot).abs().max()) <= 1e-2 * float(rot.abs().max())
