@@ -10,7 +10,8 @@ below 2^-24 relative). CPU tensors use torch's FP32 matmul (IEEE on the host).
 
 ``trsm_right_upper(x, r)`` = ``x @ inv(r)`` for upper-triangular ``r``: the small ``k x k`` inverse is
 formed in FP64 by triangular substitution and applied with :func:`mm`. ``cholesky_qr2`` orthonormalizes
-columns with two CholeskyQR passes (Householder QR when the Gram is not positive definite).
+columns with two CholeskyQR passes -- FP32-accurate Gram, FP64 Cholesky and FP64 triangular solve -- and falls
+back to Householder QR when a Gram is not positive definite.
 """
 
 from __future__ import annotations
@@ -92,19 +93,19 @@ def householder_qr(b: torch.Tensor) -> torch.Tensor:
 
 
 def cholesky_qr2_routine(b: torch.Tensor):
-    """Lockstep routine form of :func:`cholesky_qr2`: both passes are queued, then the two factorizations'
-    status is read in one host round (yielded); a Gram that is not positive definite in either pass gives the
-    Householder basis, exactly as when each pass is checked on the spot (a failed first pass never reaches the
-    second's result)."""
+    """Lockstep routine form of :func:`cholesky_qr2`: both passes are queued, then the factorizations' status and
+    the result's finiteness are read in one host round (yielded); a Gram that is not positive definite in either
+    pass (or a non-finite result) gives the Householder basis, as when each pass is checked on the spot."""
     STATS["cholesky_qr2"] += 1
     q = b.float()
-    flags = []
+    status = None
     for _ in range(2):
-        g = gram(q).double()
-        factor, info = torch.linalg.cholesky_ex(g, upper=True)
-        flags.append((info != 0) | ~torch.isfinite(factor).all())
-        q = trsm_right_upper(q, factor)
-    (bad,) = yield (torch.stack(flags).any(),)
+        # the factorization reads the upper triangle only, so the Gram needs no symmetrization; the triangular
+        # solve runs in FP64 (q R^-1 directly, no explicit inverse)
+        factor, info = torch.linalg.cholesky_ex(mm(q.t(), q).double(), upper=True)
+        status = info if status is None else status + info
+        q = torch.linalg.solve_triangular(factor, q.double(), upper=True, left=False).float()
+    (bad,) = yield ((status != 0) | ~torch.isfinite(q).all(),)
     if bad:
         STATS["qr_fallbacks"] += 1
         return householder_qr(b)

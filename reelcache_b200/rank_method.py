@@ -257,14 +257,18 @@ def stored_energy_routine(x: torch.Tensor, rows: torch.Tensor, total: float, til
     ``||A - P Q||^2`` accumulated in FP64 over row tiles. Returns (energy, P)."""
     q = rows.float()
     qt = q.t()
-    coefficients = torch.empty((x.shape[0], rows.shape[0]), dtype=torch.float32, device=x.device)
-    residual = None
-    for start in range(0, x.shape[0], tile_rows):
-        a = x[start:start + tile_rows]
-        p = exact_blas.mm(a, qt)
-        coefficients[start:start + tile_rows] = p
-        part = _sum_squares(a, exact_blas.mm(p, q))[1]
-        residual = part if residual is None else residual + part
+    if x.shape[0] <= tile_rows:  # one tile: the projection is the coefficient matrix itself
+        coefficients = exact_blas.mm(x, qt)
+        residual = _sum_squares(x, exact_blas.mm(coefficients, q))[1]
+    else:
+        coefficients = torch.empty((x.shape[0], rows.shape[0]), dtype=torch.float32, device=x.device)
+        residual = None
+        for start in range(0, x.shape[0], tile_rows):
+            a = x[start:start + tile_rows]
+            p = exact_blas.mm(a, qt)
+            coefficients[start:start + tile_rows] = p
+            part = _sum_squares(a, exact_blas.mm(p, q))[1]
+            residual = part if residual is None else residual + part
     if total <= 0:
         return 1.0, coefficients
     (value,) = yield (residual,)
