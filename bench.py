@@ -583,8 +583,9 @@ def run_sp(args, rank, world, local):
                     "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": int(mirror.numel()),
                     "d2h_bytes_per_step": 4 * len(probe_layers) * 2 * 4,
                     "includes": "FusedHistoryRestore.restore(from_host=True) on every rank: H2D of the owner's "
-                                "coefficients from pinned memory, one device barrier, the fused restore; D2H "
-                                "checksum; bytes of rank 0"},
+                                "coefficients from pinned memory in layer stages, a device barrier per stage, the "
+                                "fused restore of each stage overlapping the next stage's upload; D2H checksum; "
+                                "bytes of rank 0"},
             "gpu_launches": launches, "clocks": clocks.summary(), "restored_bytes_per_step": restored,
             "precision": "fp16x2", "per_rank_plan_bytes": stats,
             "note": f"SP{world}, layout '{args.sp_layout}': {args.sp_chunks}-chunk history; each rank restores "

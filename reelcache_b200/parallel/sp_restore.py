@@ -203,14 +203,17 @@ def plan_history(shapes: Sequence[tuple[int, int, str, int, int]], world: int, c
         raise ConfigurationError("one or two coefficient regions")
     basis_cursor = [0] * world
     coeff_cursor = [0] * world
-    staged = []
-    for index, (chunk, layer, target, tokens, rank) in enumerate(shapes):
+    staged: list = [None] * len(shapes)
+    # coefficients layer-major in every owner's region: a stage of consecutive layers is one contiguous upload
+    order = sorted(range(len(shapes)), key=lambda i: (shapes[i][1], shapes[i][2], shapes[i][0]))
+    for index in order:
+        chunk, layer, target, tokens, rank = shapes[index]
         if rank < 1 or rank > channels or tokens < 1:
             raise ConfigurationError("tile rank must be in [1, channels] and tokens positive")
         o = owner(layer, target, world) if owners is None else owners[index]
         if not 0 <= o < world:
             raise ConfigurationError("matrix owner outside the group")
-        staged.append((chunk, layer, target, tokens, rank, o, coeff_cursor[o], basis_cursor[o]))
+        staged[index] = (chunk, layer, target, tokens, rank, o, coeff_cursor[o], basis_cursor[o])
         basis_cursor[o] += align(rank * channels * 2)
         coeff_cursor[o] += align(tokens * k_pad_of(rank))
     tiles = tuple(HistoryTile(i, c, l, t, n, r, channels, o, align(basis_cursor[o]) + co, bo)
@@ -278,6 +281,8 @@ class FusedHistoryRestore:
         self.programs: dict[tuple[int, int], Any] = {}
         self.current = 0          # coefficient region written by the latest upload
         self.mirror = None        # pinned host copy of this owner's coefficient region
+        self.stages = 4           # upload / barrier / restore stages of an end-to-end restore
+        self._copies = None       # copy stream of the staged uploads
         self.stats = {"restores": 0, "uploads": 0, "remote_coeff_bytes": 0, "local_coeff_bytes": 0,
                       "remote_basis_bytes": 0}
 
@@ -452,29 +457,72 @@ class FusedHistoryRestore:
     def restore(self, stream=None, *, from_host: bool = False) -> int:
         """One restore of the whole history into every rank's native KV.
 
-        ``from_host``: first upload this owner's coefficients from pinned host memory into the region the
-        previous upload did not write, then a bounded device barrier (every owner's upload done before any
-        peer's unpack reads it; the region written here was last read before the previous upload's barrier).
-        Without it the resident coefficients of the latest upload are restored again. Collective only with
-        ``from_host`` (the barrier); returns the kernels this rank launched."""
+        ``from_host``: upload this owner's coefficients from pinned host memory into the region the previous
+        upload did not write, in stages of consecutive layers, each followed by a bounded device barrier before
+        that stage's restore launches (every owner's upload of the stage done before any peer's unpack reads it;
+        the region written here was last read before the previous upload's barriers), so a stage restores
+        while the next one uploads. Without it the resident coefficients of the latest upload are restored
+        again. Collective only with ``from_host`` (the barriers); returns the kernels this rank launched."""
         stream = stream or torch.cuda.current_stream(self.device)
         if self.emulated and from_host:
             raise ConfigurationError("an emulated arena restores resident factors only")
         if from_host:
-            mirror = self.host_mirror()
-            owner = self.arena.rank
-            region = 1 - self.current if self.plan.regions == 2 else 0
-            base = align(self.plan.basis_bytes[owner]) + region * self.plan.region_shift(owner)
-            with torch.cuda.stream(stream):
-                self.arena.view(owner, base, (mirror.numel(),), torch.uint8).copy_(mirror, non_blocking=True)
-            self.arena.barrier(stream)
-            self.current = region
-            self.stats["uploads"] += 1
-        launches = self.launch(stream)
+            launches = self._pipelined_upload_and_launch(stream)
+        else:
+            launches = self.launch(stream)
         self.stats["restores"] += 1
         for key in ("remote_coeff_bytes", "local_coeff_bytes", "remote_basis_bytes"):
             self.stats[key] += self.stats.get("plan_" + key, 0)
-        return launches + (1 if from_host else 0)
+        return launches
+
+    def _stages(self) -> list[list[int]]:
+        """The history's layers in ``self.stages`` contiguous groups (the same on every rank)."""
+        layers = sorted({tile.layer for tile in self.plan.tiles})
+        count = max(1, min(self.stages, len(layers)))
+        size = -(-len(layers) // count)
+        return [layers[i:i + size] for i in range(0, len(layers), size)]
+
+    def _pipelined_upload_and_launch(self, stream) -> int:
+        """Upload this owner's coefficients stage by stage (consecutive layers, contiguous bytes) on a copy
+        stream into the region the previous upload did not write; before a stage's restore launches, a bounded
+        device barrier (every owner's upload of that stage has landed). Stage s's restore runs while stage s + 1
+        crosses PCIe."""
+        mirror = self.host_mirror()
+        owner = self.arena.rank
+        region = 1 - self.current if self.plan.regions == 2 else 0
+        base0 = align(self.plan.basis_bytes[owner])
+        shift = region * self.plan.region_shift(owner)
+        if self._copies is None:
+            self._copies = torch.cuda.Stream(self.device)
+        copies = self._copies
+        copies.wait_stream(stream)   # the region was last read before the previous upload's barriers
+        stages = self._stages()
+        events = []
+        with torch.cuda.stream(copies):
+            for layers in stages:
+                wanted = set(layers)
+                mine = [t for t in self.plan.tiles if t.owner == owner and t.layer in wanted]
+                if mine:
+                    lo = min(t.coeff_offset for t in mine)
+                    hi = max(t.coeff_offset + align(t.tokens * t.k_pad) for t in mine)
+                    hi = min(hi, base0 + mirror.numel())
+                    self.arena.view(owner, lo + shift, (hi - lo,), torch.uint8).copy_(
+                        mirror[lo - base0:hi - base0], non_blocking=True)
+                event = torch.cuda.Event()
+                event.record(copies)
+                events.append(event)
+        self.current = region
+        self.stats["uploads"] += 1
+        program = self.programs[(owner, region)]
+        launches = 0
+        for layers, event in zip(stages, events):
+            stream.wait_event(event)
+            self.arena.barrier(stream)
+            launches += 1
+            present = [layer for layer in layers if layer in program.groups]
+            for batch in (program.batches(present) if present else ()):
+                launches += program.launch_batch(batch, stream, aux=True)
+        return launches
 
     def check(self) -> None:
         self.arena.check()
