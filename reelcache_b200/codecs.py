@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import hashlib
 import zlib
+from dataclasses import dataclass
 from typing import Any, Mapping, Sequence
 
 import numpy as np
@@ -28,7 +29,7 @@ import torch
 from . import _hevc
 from .errors import ConfigurationError, IntegrityError, UnsupportedError
 from .serialization import tensor_bytes, tensor_from_bytes
-from .types import CodecSpec, EncodedTensor, TensorContext, json_copy
+from .types import CodecSpec, EncodedTensor, TensorContext, entry_order, json_copy
 
 TENSOR_V1 = "reelcache.tensor.v1"
 TENSOR_V2 = "reelcache.tensor.v2"
@@ -391,3 +392,147 @@ class FactorPack:
         rank = int(tile["rank"])
         view = self.raw[tile["offset"]:tile["offset"] + tile["bytes"]].view(np.float16)
         return view.reshape(-1, rank)
+
+
+# ---------------------------------------------------------------------------------------------
+# Node codec API: many matrices of one node, packed or per matrix
+# ---------------------------------------------------------------------------------------------
+
+PACKING_MODES = ("node", "layer_group", "per_matrix")
+
+
+@dataclass(frozen=True)
+class NodeEncoding:
+    """The packets of one node and where each matrix went: ``locations[entry] = (packet index, tile index)``
+    (tile index None: a single-matrix packet). Entries are ``MatrixKey`` or ``(MatrixKey, stream)``."""
+
+    packets: tuple
+    locations: Mapping[Any, tuple[int, int | None]]
+    packing: str
+
+
+def _entry_json(entry) -> dict:
+    from .types import MatrixKey
+    if isinstance(entry, MatrixKey):
+        return {"key": entry.to_dict()}
+    key, stream = entry
+    return {"key": key.to_dict(), "stream": stream}
+
+
+def _entry_of(record: Mapping[str, Any]):
+    from .types import MatrixKey
+    key = MatrixKey.from_dict(record["key"])
+    return key if "stream" not in record else (key, record["stream"])
+
+
+def _factor(matrix: torch.Tensor, context: TensorContext, spec: CodecSpec, basis: torch.Tensor | None):
+    """(coefficients FP32 [N, r], FP16 basis rows [r, C]) of one matrix: on the given rows, or on its own
+    truncated eigenbasis at ``spec.rank``."""
+    x = matrix.reshape(context.shape).float()
+    if basis is None:
+        if spec.rank is None:
+            raise ConfigurationError("a matrix without a basis needs a codec rank")
+        g = x.t() @ x
+        values, vectors = torch.linalg.eigh(g.double())
+        order = torch.argsort(values, descending=True)[:spec.rank]
+        basis = vectors[:, order].t().contiguous().to(torch.float16)
+    basis = basis.to(torch.float16)
+    if spec.rank is not None:
+        basis = basis[:spec.rank]
+    return x @ basis.float().t().to(x.device), basis.cpu()
+
+
+def encode_packed(matrices: Mapping[Any, torch.Tensor], contexts: Mapping[Any, TensorContext],
+                  specs: Mapping[Any, CodecSpec] | CodecSpec, *, bases: Mapping[Any, torch.Tensor] | None = None,
+                  stream_codec: str = "raw8", node_id: str | None = None) -> EncodedTensor:
+    """Several ``svd_hevc`` matrices of one node in ONE ``reelcache.tensor_pack.v2`` packet: each factorized on its
+    FP16 basis rows (``bases``; default its own eigenbasis at the spec's rank), quantized with its covering affine
+    and stored as one tile of the pack's coefficient stream. The packet is complete in memory: each tile's basis
+    view travels as a ``basis.NNN.f16`` payload (a store keeps bases as versions instead)."""
+    if not matrices or set(matrices) != set(contexts):
+        raise ConfigurationError("encode_packed needs the same nonempty entries in matrices and contexts")
+    tiles, payloads = [], {}
+    for index, entry in enumerate(sorted(matrices, key=entry_order)):
+        spec = specs if isinstance(specs, CodecSpec) else specs[entry]
+        if spec.kind != "svd_hevc":
+            raise ConfigurationError("node packs hold svd_hevc matrices (RAW and SVD travel as single packets)")
+        context = contexts[entry]
+        coefficients, basis = _factor(matrices[entry], context, spec, None if bases is None else bases.get(entry))
+        pixels, affine, layout = quantize(coefficients, spec.normalization, spec.protected_fraction)
+        view = basis.numpy().tobytes()
+        name = f"basis.{index:03d}.f16"
+        payloads[name] = view
+        tiles.append({"entry": _entry_json(entry), "context": context, "pixels": pixels, "affine": affine,
+                      "normalization": layout, "codec": CodecSpec(**{**spec.to_dict(), "rank": basis.shape[0]}),
+                      "basis": {**descriptor(view, basis.shape[0], context.channels), "payload": name}})
+    packed = encode_node_pack(tiles, stream_codec=stream_codec, details={"node_id": node_id} if node_id else None)
+    return EncodedTensor(packed.metadata, {**packed.payloads, **payloads}, metrics=packed.metrics)
+
+
+def encode_node(matrices: Mapping[Any, torch.Tensor], contexts: Mapping[Any, TensorContext],
+                specs: Mapping[Any, CodecSpec] | CodecSpec, *, packing: str = "node",
+                layer_group_size: int | None = None, bases: Mapping[Any, torch.Tensor] | None = None,
+                stream_codec: str = "raw8") -> NodeEncoding:
+    """Every matrix of one node under a packing mode: ``node`` (all ``svd_hevc`` matrices in one pack),
+    ``layer_group`` (one pack per run of ``layer_group_size`` layers) or ``per_matrix`` (one packet each, as
+    :func:`encode_tensor`). RAW and SVD-only matrices are always single packets."""
+    if packing not in PACKING_MODES:
+        raise ConfigurationError(f"packing must be one of {PACKING_MODES}")
+    if (packing == "layer_group") != (layer_group_size is not None):
+        raise ConfigurationError("layer_group_size goes with layer_group packing, and only with it")
+    if layer_group_size is not None and (type(layer_group_size) is not int or layer_group_size < 1):
+        raise ConfigurationError("layer_group_size must be a positive integer")
+    spec_of = (lambda e: specs) if isinstance(specs, CodecSpec) else (lambda e: specs[e])
+    packets, locations = [], {}
+    grouped: dict[int, list] = {}
+    for entry in sorted(matrices, key=entry_order):
+        spec = spec_of(entry)
+        if spec.kind != "svd_hevc" or packing == "per_matrix":
+            basis = None if bases is None else bases.get(entry)
+            if spec.kind == "raw":
+                packets.append(encode_raw(matrices[entry].reshape(contexts[entry].shape), contexts[entry]))
+            else:
+                coefficients, rows = _factor(matrices[entry], contexts[entry], spec, basis)
+                packets.append(encode_factorized(coefficients, rows.numpy().tobytes(), contexts[entry],
+                                                 CodecSpec(**{**spec.to_dict(), "rank": rows.shape[0]}),
+                                                 stream_codec=None if spec.kind == "svd" else stream_codec))
+            locations[entry] = (len(packets) - 1, None)
+            continue
+        layer = (entry if not isinstance(entry, tuple) else entry[0]).layer
+        group = 0 if packing == "node" else layer // layer_group_size
+        grouped.setdefault(group, []).append(entry)
+    for group in sorted(grouped):
+        members = grouped[group]
+        pack = encode_packed({e: matrices[e] for e in members}, {e: contexts[e] for e in members},
+                             {e: spec_of(e) for e in members}, bases=bases, stream_codec=stream_codec)
+        packets.append(pack)
+        for tile, entry in enumerate(sorted(members, key=entry_order)):
+            locations[entry] = (len(packets) - 1, tile)
+    return NodeEncoding(tuple(packets), locations, packing)
+
+
+def decode_packed(encoded: EncodedTensor, *, keys=None, device: Any = "cpu",
+                  dtype: torch.dtype = torch.float32) -> dict:
+    """The selected (default: all) matrices of an in-memory node pack, ``{entry: dequantize(P) @ Q}`` in tile
+    order; the tiles' bases come from the packet's ``basis.NNN.f16`` payloads."""
+    pack = DecodedPack(encoded.metadata, encoded.payloads["stream"], encoded.payloads["affines"])
+    wanted = None if keys is None else set(keys)
+    out = {}
+    for index, tile in enumerate(pack.tiles):
+        entry = _entry_of(tile["entry"])
+        if wanted is not None and entry not in wanted:
+            continue
+        name = tile["basis"].get("payload")
+        if name is None or name not in encoded.payloads:
+            raise IntegrityError(f"tile {index} has no basis payload: decode it through its store record")
+        rank, channels = tile["basis"]["shape"]
+        view = encoded.payloads[name]
+        if hashlib.sha256(view).hexdigest() != tile["basis"]["sha256"]:
+            raise IntegrityError(f"basis of tile {index} differs from its digest")
+        basis = torch.from_numpy(np.frombuffer(view, dtype=np.float16).reshape(rank, channels).copy()).to(device)
+        scale, offset = pack.scale_offset(index)
+        coefficients = torch.from_numpy(pack.pixels(index).astype(np.float32) * scale + offset).to(device)
+        out[entry] = (coefficients @ basis.float()).to(dtype)
+    if wanted is not None and set(out) != wanted:
+        raise ConfigurationError(f"the pack holds none of {sorted(map(str, wanted - set(out)))}")
+    return out

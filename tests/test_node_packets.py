@@ -38,3 +38,41 @@ def test_pack_bases_detach_attach():
     detached, bases = detach_pack_bases(meta)
     assert all("basis" not in t for t in detached["tiles"]) and bases == [{"sha": "a"}, {"sha": "b"}]
     assert attach_pack_bases(detached, bases) == meta
+
+
+def test_node_codec_api_packed_layer_groups_and_per_matrix():
+    import torch
+    from reelcache_b200.codecs import decode_packed, decode_tensor, encode_node, encode_packed
+    from reelcache_b200.types import CodecSpec, MatrixKey, ModelIdentity, TensorContext
+    model = ModelIdentity("tiny", "fp", 4, 64, "BTHD", "bfloat16")
+    g = torch.Generator().manual_seed(0)
+    matrices, contexts = {}, {}
+    for layer in range(4):
+        for target in "KV":
+            key = MatrixKey(layer, target)
+            rows = torch.randn(128, 6, generator=g) @ torch.linalg.qr(torch.randn(64, 6, generator=g))[0].t()
+            matrices[key] = rows.to(torch.bfloat16)
+            contexts[key] = TensorContext(model, key, 0, 2, 8, 8, "pre_rope" if target == "K" else "none")
+    spec = CodecSpec("svd_hevc", 8)
+    pack = encode_packed(matrices, contexts, spec, node_id="n0")
+    decoded = decode_packed(pack)
+    assert list(decoded) == sorted(matrices, key=lambda k: (k.layer, k.target))
+    for key, value in decoded.items():
+        source = matrices[key].float()
+        assert float((value - source).norm() / source.norm()) < 0.02
+    one = decode_packed(pack, keys=[MatrixKey(2, "V")])
+    assert list(one) == [MatrixKey(2, "V")] and torch.equal(one[MatrixKey(2, "V")], decoded[MatrixKey(2, "V")])
+    node = encode_node(matrices, contexts, spec)
+    assert len(node.packets) == 1 and node.locations[MatrixKey(3, "V")] == (0, 7)
+    groups = encode_node(matrices, contexts, spec, packing="layer_group", layer_group_size=2)
+    assert len(groups.packets) == 2 and groups.locations[MatrixKey(2, "K")] == (1, 0)
+    mixed = {k: (CodecSpec("raw") if k.layer == 0 else CodecSpec("svd", 8) if k.layer == 1 else spec)
+             for k in matrices}
+    per = encode_node(matrices, contexts, mixed, packing="per_matrix")
+    assert len(per.packets) == 8 and all(tile is None for _, tile in per.locations.values())
+    raw = decode_tensor(per.packets[per.locations[MatrixKey(0, "K")][0]])
+    assert torch.equal(raw, matrices[MatrixKey(0, "K")])
+    svd = decode_tensor(per.packets[per.locations[MatrixKey(1, "V")][0]])
+    assert float((svd - matrices[MatrixKey(1, "V")].float()).norm() / matrices[MatrixKey(1, "V")].float().norm()) < 0.02
+    mixed_node = encode_node(matrices, contexts, mixed)
+    assert len(mixed_node.packets) == 4 + 1   # RAW and SVD single packets, the svd_hevc matrices in one pack
