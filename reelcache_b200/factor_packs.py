@@ -24,6 +24,98 @@ from .lineage import LineageRuntime
 from .types import MatrixKey
 
 
+COEFFICIENT_DTYPE = "float16"
+
+
+def factor_codec(spec) -> dict[str, Any]:
+    """The codec header a factor pack records for an ``svd`` spec (the run-local encoder path dropped)."""
+    if spec.kind != "svd":
+        raise UnsupportedError("factor packs hold svd (SVD-only) matrices")
+    codec = spec.to_dict()
+    codec.pop("ffmpeg_path", None)
+    return codec
+
+
+def is_factor_pack(value: Any) -> bool:
+    """Whether ``value`` (an encoded packet or its metadata) is a ``reelcache.factor_pack.v1`` pack."""
+    from .codecs import FACTOR_PACK_SCHEMA
+    metadata = getattr(value, "metadata", value)
+    return isinstance(metadata, dict) and metadata.get("schema") == FACTOR_PACK_SCHEMA
+
+
+def validate_factor_pack(encoded, *, verify: bool = False) -> list[dict]:
+    """The tile table of a factor pack after checking its layout (contiguous, non-overlapping tiles whose byte
+    counts match ``tokens x rank`` FP16 values) and, with ``verify``, each tile's SHA-256."""
+    import hashlib
+
+    from .errors import IntegrityError
+    if not is_factor_pack(encoded):
+        raise IntegrityError("not a factor pack")
+    factors = encoded.payloads["factors"]
+    metadata = encoded.metadata
+    cursor = 0
+    for index, tile in enumerate(metadata["tiles"]):
+        tokens = tile["context"]["frames"] * tile["context"]["height"] * tile["context"]["width"]
+        if (tile["tile"] != index or tile["offset"] != cursor or tile["bytes"] != tokens * int(tile["rank"]) * 2):
+            raise IntegrityError(f"factor pack tile {index} is inconsistent with its table")
+        if verify and hashlib.sha256(factors[cursor:cursor + tile["bytes"]]).hexdigest() != tile["sha256"]:
+            raise IntegrityError(f"factor pack tile {index} fails its hash")
+        cursor += tile["bytes"]
+    if cursor != int(metadata["bytes"]) or len(factors) != cursor:
+        raise IntegrityError("factor pack size differs from its tiles")
+    return list(metadata["tiles"])
+
+
+class FactorTile:
+    """One prepared tile of a factor pack: its entry, rank, and FP16 coefficients ``[tokens, rank]`` (a view of the
+    packet's staging buffer)."""
+
+    __slots__ = ("entry", "rank", "values", "basis")
+
+    def __init__(self, entry, rank: int, values: torch.Tensor, basis: dict):
+        self.entry, self.rank, self.values, self.basis = entry, rank, values, basis
+
+
+def prepare_factor_packet(encoded, *, verify: bool = False, pin_memory: bool = False,
+                          device: Any = None) -> list[FactorTile]:
+    """Every tile of a factor pack as a view of ONE buffer holding the packet's coefficients (pinned host memory,
+    or copied once to ``device``)."""
+    from .codecs import _entry_of
+    tiles = validate_factor_pack(encoded, verify=verify)
+    raw = torch.frombuffer(bytearray(encoded.payloads["factors"]), dtype=torch.uint8)
+    if pin_memory:
+        raw = raw.pin_memory()
+    if device is not None:
+        raw = raw.to(device, non_blocking=pin_memory)
+    out = []
+    for tile in tiles:
+        rank = int(tile["rank"])
+        values = raw[tile["offset"]:tile["offset"] + tile["bytes"]].view(torch.float16).view(-1, rank)
+        out.append(FactorTile(_entry_of(tile["entry"]), rank, values, tile["basis"]))
+    return out
+
+
+def decode_factor_pack(encoded, bases: dict, *, keys=None, device: Any = "cpu",
+                       dtype: torch.dtype = torch.float32) -> dict:
+    """``{entry: P @ Q}`` of the selected tiles (default: all); ``bases[entry]`` gives each tile's FP16 rows
+    (the record's basis-version prefix), checked against the tile's basis digest."""
+    import hashlib
+
+    from .errors import IntegrityError
+    wanted = None if keys is None else set(keys)
+    out = {}
+    for tile in prepare_factor_packet(encoded, verify=True, device=device):
+        if wanted is not None and tile.entry not in wanted:
+            continue
+        rows = bases[tile.entry].to(torch.float16).contiguous()
+        if rows.shape[0] != tile.rank:
+            raise IntegrityError(f"basis of {tile.entry} has {rows.shape[0]} rows, the tile rank is {tile.rank}")
+        if "sha256" in tile.basis and hashlib.sha256(rows.cpu().numpy().tobytes()).hexdigest() != tile.basis["sha256"]:
+            raise IntegrityError(f"basis of {tile.entry} differs from the tile's digest")
+        out[tile.entry] = (tile.values.float() @ rows.to(tile.values.device).float()).to(dtype)
+    return out
+
+
 class FactorRestorer:
     """Dense reconstructions of ``svd`` records (decoded packs cached LRU under a byte budget)."""
 

@@ -76,3 +76,33 @@ def test_node_codec_api_packed_layer_groups_and_per_matrix():
     assert float((svd - matrices[MatrixKey(1, "V")].float()).norm() / matrices[MatrixKey(1, "V")].float().norm()) < 0.02
     mixed_node = encode_node(matrices, contexts, mixed)
     assert len(mixed_node.packets) == 4 + 1   # RAW and SVD single packets, the svd_hevc matrices in one pack
+
+
+def test_factor_pack_validate_prepare_decode():
+    import torch
+    from reelcache_b200.codecs import descriptor, encode_factor_pack
+    from reelcache_b200.errors import IntegrityError
+    from reelcache_b200.factor_packs import (decode_factor_pack, factor_codec, is_factor_pack, prepare_factor_packet,
+                                             validate_factor_pack)
+    from reelcache_b200.types import CodecSpec, MatrixKey, ModelIdentity, TensorContext
+    model = ModelIdentity("tiny", "fp", 2, 64, "BTHD", "bfloat16")
+    g = torch.Generator().manual_seed(1)
+    tiles, bases, sources = [], {}, {}
+    for layer in range(2):
+        key = MatrixKey(layer, "K")
+        rows = torch.linalg.qr(torch.randn(64, 8, generator=g))[0].t().to(torch.float16)
+        coeff = torch.randn(128, 8, generator=g)
+        bases[key], sources[key] = rows, coeff.half().float() @ rows.float()
+        tiles.append({"entry": {"key": key.to_dict()}, "context": TensorContext(model, key, 0, 2, 8, 8, "pre_rope"),
+                      "coefficients": coeff.numpy(), "basis": descriptor(rows.numpy().tobytes(), 8, 64)})
+    pack = encode_factor_pack(tiles)
+    assert is_factor_pack(pack) and factor_codec(CodecSpec("svd", 8))["kind"] == "svd"
+    assert len(validate_factor_pack(pack, verify=True)) == 2
+    prepared = prepare_factor_packet(pack)
+    assert prepared[1].entry == MatrixKey(1, "K") and prepared[1].values.shape == (128, 8)
+    decoded = decode_factor_pack(pack, bases)
+    for key, value in decoded.items():
+        assert torch.allclose(value, sources[key], atol=1e-3)
+    bad = type(pack)(pack.metadata, {"factors": pack.payloads["factors"][:-2]})
+    with pytest.raises(IntegrityError):
+        validate_factor_pack(bad)
