@@ -485,36 +485,18 @@ class ArchivePipeline:
                 self._detaching.discard(lineage)
                 self.cv.notify_all()
 
-    def prewarm(self, contexts: Mapping[Any, Any], *, seed: int = 0) -> dict:
-        """Pay the archive path's cold start before the first chunk: plan and finalize two synthetic chunks of
-        ``contexts``' geometry on the fitter's stream (fresh, then against the first's rows; nothing is stored or
-        learned), so kernels, library handles and allocator pools exist. Returns per-phase seconds."""
-        from .lineage_commit import ArchiveOptions  # noqa: F401 - the options the warm-up mirrors
-        from .rank_method import plan_chunk
-        from .types import ActiveBasisBinding
-        started = time.perf_counter()
-        gen = torch.Generator().manual_seed(seed)
-        matrices = {}
-        for entry, context in contexts.items():
-            rows, channels = context.token_count, context.channels
-            rank = max(1, min(32, channels // 4))
-            x = torch.randn(rows, rank, generator=gen) @ torch.randn(rank, channels, generator=gen)
-            matrices[entry] = (x + 1e-3 * torch.randn(rows, channels, generator=gen)).to(self.device)
-        report = {}
+    def prewarm(self, contexts: Mapping[Any, Any], *, seed: int = 0, max_frames: int | None = None) -> dict:
+        """Pay the archive path's cold start before the first chunk: :func:`~reelcache_b200.lineage_commit.
+        warm_commit_path` (plan and finalize two synthetic chunks of ``contexts``' geometry, fresh then against
+        the first one's rows; nothing stored or learned) on the fitter's stream, so kernels, library handles and
+        allocator pools exist. Returns per-phase seconds (also in ``stats()["prewarm"]``)."""
+        from .lineage_commit import warm_commit_path
         ctx = torch.cuda.stream(self._stream) if self._stream is not None else _Null()
         with ctx:
-            clock = time.perf_counter()
-            first = plan_chunk(matrices, contexts, self.method, None, {}, {}, chunk_id="prewarm", device=self.device)
-            report["fresh_seconds"] = time.perf_counter() - clock
-            clock = time.perf_counter()
-            bindings = {e: ActiveBasisBinding("manifest:" + "0" * 64, p.rows.shape[0], "0" * 64) for e, p in
-                        first.items() if p.rows is not None and p.decision != "zero_input"}
-            plan_chunk(matrices, contexts, self.method, None, bindings, {e: first[e].rows for e in bindings},
-                       chunk_id="prewarm", device=self.device)
-            report["reuse_seconds"] = time.perf_counter() - clock
+            report = warm_commit_path(self.method, contexts, options=self.options, device=self.device,
+                                      max_frames=max_frames, seed=seed)
             if self._stream is not None:
                 self._stream.synchronize()
-        report["total_seconds"] = time.perf_counter() - started
         with self.cv:
             self._prewarm.append(dict(report))
         return report

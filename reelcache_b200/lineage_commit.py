@@ -362,3 +362,67 @@ class CommitJob:
                 ranks.append(tile.plan.rank_view)
         return {"decisions": decisions, "mean_rank": float(np.mean(ranks)) if ranks else 0.0,
                 "max_rank": int(max(ranks)) if ranks else 0, "matrices": len(ranks)}
+
+
+def warm_commit_path(method: RankMethodConfig, contexts: Mapping[Any, TensorContext], *,
+                     options: ArchiveOptions | None = None, device: Any = "cpu", max_frames: int | None = None,
+                     seed: int = 0) -> dict[str, Any]:
+    """Pay a commit path's first-use costs before the first real chunk: plan and finalize two synthetic chunks of
+    ``contexts``' geometry on this thread (the fresh path, then the active-basis paths against the first one's rows);
+    nothing is stored and nothing is learned. ``max_frames`` caps the frames of each context (less transient memory,
+    the same kernels and library handles warmed). Returns per-phase seconds, the decisions and the synthetic bytes."""
+    import time
+    from dataclasses import replace as _replace
+
+    from .rank_method import plan_chunk
+    from .types import ActiveBasisBinding
+    options = ArchiveOptions() if options is None else options
+    if not isinstance(method, RankMethodConfig) or not isinstance(options, ArchiveOptions):
+        raise ConfigurationError("a commit warm-up needs a RankMethodConfig and ArchiveOptions")
+    if max_frames is not None and (type(max_frames) is not int or max_frames < 1):
+        raise ConfigurationError("max_frames must be None or a positive integer")
+    if not contexts:
+        raise ConfigurationError("a commit warm-up needs the commit's contexts")
+    device = torch.device(device)
+    gen = torch.Generator().manual_seed(seed)
+    capped, matrices = {}, {}
+    for entry, context in contexts.items():
+        if max_frames is not None and context.frames > max_frames:
+            context = _replace(context, frames=max_frames)
+        capped[entry] = context
+        rows, channels = context.token_count, context.channels
+        rank = max(1, min(channels // 4, 64))
+        x = torch.randn(rows, rank, generator=gen) @ torch.randn(rank, channels, generator=gen)
+        matrices[entry] = (x + 1e-2 * torch.randn(rows, channels, generator=gen)).to(torch.bfloat16).to(device)
+    report: dict[str, Any] = {"source_bytes": sum(m.numel() * m.element_size() for m in matrices.values())}
+    started = time.perf_counter()
+
+    def finalize(plans):
+        for plan in plans.values():
+            if method.codec.kind == "svd":
+                plan.coefficients.to(torch.float16).cpu()
+            else:
+                codecs.quantize(plan.coefficients, method.codec.normalization, method.codec.protected_fraction)
+
+    clock = time.perf_counter()
+    fresh = plan_chunk(matrices, capped, method, None, {}, {}, chunk_id="warm-0", device=device)
+    report["fresh_plan_seconds"] = time.perf_counter() - clock
+    clock = time.perf_counter()
+    finalize(fresh)
+    report["fresh_finalize_seconds"] = time.perf_counter() - clock
+    bindings = {e: ActiveBasisBinding("manifest:" + "0" * 64, p.rows.shape[0], "0" * 64, p.rows.shape[0], "warm-0")
+                for e, p in fresh.items() if p.decision in ("fresh", "refit")}
+    clock = time.perf_counter()
+    reuse = plan_chunk(matrices, capped, method, None, bindings, {e: fresh[e].rows for e in bindings},
+                       chunk_id="warm-1", device=device)
+    report["reuse_plan_seconds"] = time.perf_counter() - clock
+    clock = time.perf_counter()
+    finalize(reuse)
+    report["reuse_finalize_seconds"] = time.perf_counter() - clock
+    if device.type == "cuda":
+        torch.cuda.synchronize(device)
+    decisions: dict[str, int] = {}
+    for plan in list(fresh.values()) + list(reuse.values()):
+        decisions[plan.decision] = decisions.get(plan.decision, 0) + 1
+    report.update(decisions=decisions, total_seconds=time.perf_counter() - started)
+    return report

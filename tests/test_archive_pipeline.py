@@ -187,6 +187,6 @@ def test_detach_hands_unpublished_chunks_to_a_side_lineage(runtime):
         assert tickets[1].result(0) == side and runtime.load_node(side).frontier == 3 * c[MatrixKey(0, "K")].token_count
         assert pipe.detach("a", "a-other")["moved"] == []
         report = pipe.prewarm(c)
-        assert report["fresh_seconds"] > 0 and pipe.stats()["prewarm"][0]["total_seconds"] >= report["fresh_seconds"]
+        assert report["fresh_plan_seconds"] > 0 and report["decisions"] and pipe.stats()["prewarm"][0]["total_seconds"] > 0
     finally:
         pipe.close()
