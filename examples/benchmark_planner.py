@@ -3,7 +3,7 @@ chunk and a second chunk against the first one's rows (share / augment), planned
 and in lockstep over CUDA stream lanes; plus the thin FP32-accurate products the planner issues (split-K promoted
 GEMM) against cuBLAS SGEMM.
 
-    python examples/benchmark_planner.py [--out result.json] [--gemm-only]
+    python examples/benchmark_planner.py [--out result.json] [--gemm-only] [--shape "G B"]
 
 Times are host wall clock around each plan (synchronized on both sides) and CUDA-event means for the GEMMs; the
 plans of every mode are checked bitwise equal.
@@ -18,7 +18,7 @@ import time
 from pathlib import Path
 
 
-def gemm_shapes(device) -> list[dict]:
+def gemm_shapes(device, only: str | None = None) -> list[dict]:
     import torch
     from reelcache_b200.ops.fitter import SPLIT_A, SPLIT_A_BF16, SPLIT_B, SPLIT_B_BF16, matmul_promoted, split_operand
 
@@ -41,6 +41,8 @@ def gemm_shapes(device) -> list[dict]:
                                     (4680, 1536, 112, torch.float32, "reconstruction P Q"),
                                     (1536, 176, 1536, torch.float32, "subspace step G B"),
                                     (1536, 32, 1536, torch.float32, "sketch G Omega")):
+        if only is not None and only not in label:
+            continue
         a = torch.randn(m, k, device=device).to(a_dtype)
         b = torch.randn(k, n, device=device)
         parts_a, parts_b = (SPLIT_A_BF16, SPLIT_B_BF16) if a_dtype == torch.bfloat16 else (SPLIT_A, SPLIT_B)
@@ -126,9 +128,10 @@ def main(argv=None) -> None:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--out", default=None)
     parser.add_argument("--gemm-only", action="store_true")
+    parser.add_argument("--shape", default=None, help="only the GEMM shapes whose label contains this text")
     args = parser.parse_args(argv)
     device = torch.device("cuda")
-    result = {"gemms": gemm_shapes(device)}
+    result = {"gemms": gemm_shapes(device, args.shape)}
     if not args.gemm_only:
         result["plans"] = plans(device)
     text = json.dumps(result, indent=2)
