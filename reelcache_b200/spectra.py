@@ -179,6 +179,83 @@ class StreamingGramAccumulator:
                               self._hasher.hexdigest(), budget, {"algorithm": "fp64_streaming_gram_eigvalsh"})
 
 
+@dataclass(frozen=True)
+class SpectrumDiagnostics:
+    """The numerical health of one spectrum: the Gram's asymmetry before symmetrization, the most negative
+    eigenvalue before clamping, the trace against the eigenvalue sum, all relative to the total energy, and the
+    FP64 rounding budget the rank brackets use."""
+
+    asymmetry: float
+    negative_eigenvalue: float
+    trace_residual: float
+    rounding_budget: float
+
+    @classmethod
+    def of(cls, gram: torch.Tensor, values: torch.Tensor, total: float, budget: float) -> "SpectrumDiagnostics":
+        scale = max(total, 1e-300)
+        return cls(float((gram - gram.t()).abs().max()) / scale, float(min(0.0, float(values.min()))) / scale,
+                   abs(total - float(values.sum())) / scale, budget)
+
+    def to_dict(self) -> dict[str, float]:
+        return {"asymmetry": self.asymmetry, "negative_eigenvalue": self.negative_eigenvalue,
+                "trace_residual": self.trace_residual, "rounding_budget": self.rounding_budget}
+
+
+@dataclass
+class SpectrumRowShard:
+    """One rank's rows of a sequence-parallel matrix, reduced to what its spectrum needs: the rows' FP64 Gram and
+    column sums, the first row's index, the row count and the SHA-256 of the rows."""
+
+    rank: int
+    row_start: int
+    rows: int
+    gram: torch.Tensor
+    column_sums: torch.Tensor
+    sha256: str
+
+
+def row_shard(tensor: torch.Tensor, *, rank: int, row_start: int, tile_rows: int = 1024) -> SpectrumRowShard:
+    """This rank's :class:`SpectrumRowShard` of ``tensor`` (its rows ``[row_start, row_start + rows)``)."""
+    accumulator = StreamingGramAccumulator(int(tensor.shape[1]))
+    for start in range(0, tensor.shape[0], tile_rows):
+        accumulator.add(tensor[start:start + tile_rows])
+    return SpectrumRowShard(rank, row_start, accumulator.rows, accumulator.gram, accumulator.column_sums,
+                            accumulator._hasher.hexdigest())
+
+
+def spectrum_from_row_shards(shards) -> SpectrumResult:
+    """The spectrum of a matrix whose rows are split over ranks, from every rank's shard: the shards must tile the
+    rows without gaps or overlaps; Grams and column sums are summed in row order (deterministic), the source digest
+    is the SHA-256 of the shards' digests in row order, and the result carries its diagnostics."""
+    shards = sorted(shards, key=lambda shard: shard.row_start)
+    if not shards:
+        raise ConfigurationError("a spectrum needs at least one row shard")
+    channels = int(shards[0].gram.shape[0])
+    cursor = 0
+    gram = torch.zeros((channels, channels), dtype=torch.float64)
+    sums = torch.zeros(channels, dtype=torch.float64)
+    digest = hashlib.sha256()
+    for shard in shards:
+        if shard.row_start != cursor or shard.gram.shape != (channels, channels):
+            raise ConfigurationError("row shards must tile the matrix rows in order, with one channel count")
+        cursor += shard.rows
+        gram += shard.gram.double()
+        sums += shard.column_sums.double()
+        digest.update(bytes.fromhex(shard.sha256))
+    symmetric = 0.5 * (gram + gram.t())
+    raw_values = torch.linalg.eigvalsh(symmetric).flip(0)
+    total = float(torch.diagonal(symmetric).sum())
+    if not math.isfinite(total):
+        raise SpectrumNumericalError("row-shard spectrum energy is not finite")
+    budget = _gamma(cursor + channels) * total
+    diagnostics = SpectrumDiagnostics.of(gram, raw_values, total, budget)
+    mean = sums / max(1, cursor)
+    return SpectrumResult(cursor, channels, tuple(float(v) for v in raw_values.clamp_min(0.0)), total,
+                          float(cursor * mean.square().sum()), digest.hexdigest(), budget,
+                          {"algorithm": "fp64_row_shard_gram_eigvalsh", "shards": len(shards),
+                           "diagnostics": diagnostics.to_dict()})
+
+
 def exact_spectrum(tensor: torch.Tensor, *, tile_rows: int = 1024) -> SpectrumResult:
     if tensor.ndim != 2 or min(tensor.shape) < 1:
         raise ConfigurationError("spectra take a nonempty matrix")

@@ -223,3 +223,18 @@ def test_accel_options():
     total = float(x.double().square().sum())
     value = accel.span_energy_fp32(p, rows, total)
     assert value is not None and math.isclose(value, direct / total, rel_tol=1e-6)
+
+
+def test_row_shard_spectrum_matches_whole_matrix():
+    from reelcache_b200.spectra import exact_spectrum, row_shard, spectrum_from_row_shards
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(300, 8, generator=g) @ torch.randn(8, 48, generator=g) + 1e-3 * torch.randn(300, 48, generator=g)
+    whole = exact_spectrum(x)
+    shards = [row_shard(x[a:b], rank=r, row_start=a) for r, (a, b) in enumerate(((0, 100), (100, 170), (170, 300)))]
+    merged = spectrum_from_row_shards(list(reversed(shards)))
+    assert merged.rows == 300 and merged.r95 == whole.r95 and merged.r99 == whole.r99
+    assert max(abs(a - b) for a, b in zip(merged.eigenvalues, whole.eigenvalues)) <= 1e-9 * whole.total_energy
+    diagnostics = merged.metrics["diagnostics"]
+    assert diagnostics["asymmetry"] < 1e-12 and diagnostics["trace_residual"] < 1e-10
+    with pytest.raises(Exception):
+        spectrum_from_row_shards([shards[0], shards[2]])   # a gap
