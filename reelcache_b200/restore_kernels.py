@@ -49,18 +49,47 @@ MAX_DENSE_JOBS_PER_LAUNCH = 48
 _OUT_CODE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 
 
+def _nonnegative(value) -> bool:
+    return type(value) is int and value >= 0
+
+
 def _int(value, name, *, minimum=0):
-    if type(value) is not int or value < minimum:
-        raise ConfigurationError(f"{name} must be an integer >= {minimum}")
-    return value
+    if type(value) is int and value >= minimum:
+        return value
+    raise ConfigurationError(f"{name}={value!r}: expected an int of at least {minimum}")
 
 
 def _require_tensor(value, name):
-    if not isinstance(value, torch.Tensor) or value.layout != torch.strided:
-        raise ConfigurationError(f"{name} must be a strided torch.Tensor")
-    if value.device.type == "meta":
-        raise ConfigurationError(f"{name} cannot be a meta tensor")
+    """``value`` if it is a strided tensor with storage (not a meta tensor)."""
+    ok = isinstance(value, torch.Tensor) and value.layout == torch.strided and value.device.type != "meta"
+    if not ok:
+        raise ConfigurationError(f"{name}: expected a strided torch.Tensor with storage, got {type(value).__name__}")
     return value
+
+
+def _axis_dims(head_dim: int) -> tuple[int, int, int]:
+    """Rotary dims of the (frame, row, column) axes used by Wan and LongCat: the two spatial axes get
+    ``2 * (head_dim // 6)`` each and the frame axis the rest (44 / 42 / 42 for head_dim 128)."""
+    spatial = 2 * (head_dim // 6)
+    return head_dim - 2 * spatial, spatial, spatial
+
+
+def _separable(angle_tables, *, cos_sin=None):
+    """``(cos, sin, sections, section_rows)`` of a separable table assembled from per-axis tables placed side by
+    side; ``angle_tables`` hold angles ``[positions, pairs]`` (``cos_sin`` instead gives the per-axis
+    ``(cos, sin)`` pairs). Cells past an axis's last position are NaN, so a lookup outside the axis shows."""
+    parts = cos_sin if cos_sin is not None else [(a.cos(), a.sin()) for a in angle_tables]
+    lengths = tuple(c.shape[0] for c, _ in parts)
+    widths = tuple(c.shape[1] for c, _ in parts)
+    first = parts[0][0]
+    cos = torch.full((max(lengths), sum(widths)), float("nan"), dtype=first.dtype, device=first.device)
+    sin = cos.clone()
+    offset = 0
+    for (c, s), width in zip(parts, widths):
+        cos[:c.shape[0], offset:offset + width] = c
+        sin[:s.shape[0], offset:offset + width] = s
+        offset += width
+    return cos, sin, widths, lengths
 
 
 # (cos, sin) entries of one job's separable tables that the fused epilogue stages in shared memory
@@ -84,12 +113,13 @@ def restore_rope_item(positions, grid, device, stream, keepalive):
 
 @dataclass(frozen=True, eq=False)
 class RopeTable:
-    """cos/sin rotation tables ``[rows, head_dim // 2]`` for interleaved pairs.
+    """Rotation tables ``cos, sin [rows, head_dim // 2]`` for interleaved (even, odd) channel pairs.
 
-    ``sections=(t, h, w)`` makes the table separable: pair ``j`` of the token at (frame f, row y,
-    column x) uses row ``t_row + f`` when ``j < t``, ``h_row + y`` when ``j < t + h`` and
-    ``w_row + x`` otherwise. ``sections=None`` is a dense per-token table. FP32 device copies are
-    cached per device (:meth:`kernel_tables`) and refreshed when the tables change in place.
+    Dense (``sections=None``): row ``r`` holds the angles of position ``r``. Separable
+    (``sections=(t, h, w)`` pair counts): the first ``t`` columns are indexed by frame, the next ``h`` by
+    latent row and the last ``w`` by latent column, each from its own first row (``RopePositions.rows``);
+    ``section_rows`` records how many rows each axis really has. Device copies in FP32 are cached per device
+    (:meth:`kernel_tables`) and rebuilt when the tables are modified in place.
     """
 
     cos: torch.Tensor
@@ -99,23 +129,24 @@ class RopeTable:
     _device_cache: dict = field(default_factory=dict, init=False, repr=False, compare=False)
 
     def __post_init__(self):
-        cos, sin = _require_tensor(self.cos, "RoPE cos"), _require_tensor(self.sin, "RoPE sin")
-        if (cos.ndim != 2 or cos.shape != sin.shape or cos.dtype != sin.dtype
-                or cos.dtype not in (torch.float32, torch.float64) or cos.device != sin.device
-                or min(cos.shape) < 1):
-            raise ConfigurationError("RoPE cos/sin must be matching float32/float64 [rows, head_dim // 2] tensors")
+        cos, sin = _require_tensor(self.cos, "RopeTable.cos"), _require_tensor(self.sin, "RopeTable.sin")
+        same = (cos.shape == sin.shape and cos.dtype == sin.dtype and cos.device == sin.device)
+        if not (same and cos.ndim == 2 and cos.numel() > 0 and cos.dtype in (torch.float32, torch.float64)):
+            raise ConfigurationError(f"RopeTable: cos {tuple(cos.shape)} {cos.dtype} and sin {tuple(sin.shape)} "
+                                     f"{sin.dtype} must be equal non-empty 2-D float32/float64 tensors on one device")
         rows, pairs = cos.shape
-        if self.sections is not None:
-            sections = tuple(self.sections)
-            if len(sections) != 3 or any(type(v) is not int or v < 0 for v in sections) or sum(sections) != pairs:
-                raise ConfigurationError("RoPE sections must be three nonnegative pair counts summing to head_dim // 2")
-            object.__setattr__(self, "sections", sections)
-            limits = (rows, rows, rows) if self.section_rows is None else tuple(self.section_rows)
-            if len(limits) != 3 or any(type(v) is not int or not 0 <= v <= rows for v in limits):
-                raise ConfigurationError("section_rows must be three row counts within the table")
-            object.__setattr__(self, "section_rows", limits)
-        elif self.section_rows is not None:
-            raise ConfigurationError("section_rows requires separable sections")
+        if self.sections is None:
+            if self.section_rows is not None:
+                raise ConfigurationError("RopeTable: section_rows describes a separable table; give sections too")
+            return
+        sections = tuple(self.sections)
+        if not (len(sections) == 3 and all(_nonnegative(v) for v in sections) and sum(sections) == pairs):
+            raise ConfigurationError(f"RopeTable: sections {sections} must be three pair counts adding up to {pairs}")
+        lengths = (rows,) * 3 if self.section_rows is None else tuple(self.section_rows)
+        if not (len(lengths) == 3 and all(_nonnegative(v) and v <= rows for v in lengths)):
+            raise ConfigurationError(f"RopeTable: section_rows {lengths} must be three counts of at most {rows}")
+        object.__setattr__(self, "sections", sections)
+        object.__setattr__(self, "section_rows", lengths)
 
     @property
     def rows(self):
@@ -131,33 +162,29 @@ class RopeTable:
 
     @classmethod
     def from_complex(cls, freqs, sections="wan"):
+        """From unit complex rotations ``[rows, head_dim // 2]`` (``sections="wan"``: the Wan 3-axis split)."""
         freqs = _require_tensor(freqs, "freqs")
-        if not freqs.is_complex() or freqs.ndim != 2:
-            raise ConfigurationError("freqs must be a complex [rows, head_dim // 2] tensor")
-        real = torch.view_as_real(freqs.resolve_conj())
-        dtype = torch.float64 if freqs.dtype == torch.complex128 else torch.float32
+        if not (freqs.is_complex() and freqs.ndim == 2):
+            raise ConfigurationError(f"freqs: expected a 2-D complex tensor, got {tuple(freqs.shape)} {freqs.dtype}")
+        parts = torch.view_as_real(freqs.resolve_conj())
+        real_dtype = torch.float64 if freqs.dtype == torch.complex128 else torch.float32
         if sections == "wan":
             sections = wan_sections(freqs.shape[1])
-        return cls(real[..., 0].to(dtype).contiguous(), real[..., 1].to(dtype).contiguous(), sections)
+        return cls(parts[..., 0].to(real_dtype).contiguous(), parts[..., 1].to(real_dtype).contiguous(), sections)
 
     @classmethod
     def from_axes(cls, temporal, height, width):
-        """Separable table from per-axis complex tensors ``[positions, pairs]`` (unused cells NaN)."""
-        axes = [_require_tensor(v, "axis freqs") for v in (temporal, height, width)]
-        if any(not v.is_complex() or v.ndim != 2 for v in axes):
-            raise ConfigurationError("axis frequencies must be complex [positions, pairs] tensors")
-        dtype = torch.float64 if all(v.dtype == torch.complex128 for v in axes) else torch.float32
-        rows = max(v.shape[0] for v in axes)
-        pairs = sum(v.shape[1] for v in axes)
-        cos = torch.full((rows, pairs), float("nan"), dtype=dtype, device=axes[0].device)
-        sin = torch.full_like(cos, float("nan"))
-        column = 0
+        """Separable table from per-axis complex rotations ``[positions, pairs]`` (frame, row, column)."""
+        axes = [_require_tensor(v, "axis rotations") for v in (temporal, height, width)]
+        if not all(v.is_complex() and v.ndim == 2 for v in axes):
+            raise ConfigurationError("from_axes: each axis is a 2-D complex tensor [positions, pairs]")
+        real_dtype = torch.float64 if all(v.dtype == torch.complex128 for v in axes) else torch.float32
+        pairs = []
         for v in axes:
-            real = torch.view_as_real(v.resolve_conj()).to(dtype)
-            cos[:v.shape[0], column:column + v.shape[1]] = real[..., 0]
-            sin[:v.shape[0], column:column + v.shape[1]] = real[..., 1]
-            column += v.shape[1]
-        return cls(cos, sin, tuple(v.shape[1] for v in axes), tuple(v.shape[0] for v in axes))
+            parts = torch.view_as_real(v.resolve_conj()).to(real_dtype)
+            pairs.append((parts[..., 0], parts[..., 1]))
+        cos, sin, widths, lengths = _separable(None, cos_sin=pairs)
+        return cls(cos, sin, widths, lengths)
 
     @classmethod
     def from_cos_sin(cls, cos, sin, sections=None):
@@ -165,42 +192,28 @@ class RopeTable:
 
     @classmethod
     def wan(cls, head_dim, max_positions=1024, *, theta=10000.0, device="cpu"):
-        """Wan / causal-Wan 3-axis tables: per-axis ``1 / theta ** (2j / dim_axis)`` frequencies with
-        axis dims ``[d - 4 (d // 6), 2 (d // 6), 2 (d // 6)]`` (44/42/42 for d = 128), FP64."""
+        """Wan / causal-Wan tables in FP64: axis ``a`` of rotary dim ``d_a`` turns pair ``j`` by
+        ``position / theta ** (2 j / d_a)``; every axis has ``max_positions`` rows."""
         _int(head_dim, "head_dim", minimum=8)
-        dims = (head_dim - 4 * (head_dim // 6), 2 * (head_dim // 6), 2 * (head_dim // 6))
-        positions = torch.arange(max_positions, dtype=torch.float64)
-        parts = []
-        for dim in dims:
-            inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim))
-            parts.append(torch.outer(positions, inv))
-        angles = torch.cat(parts, dim=1)
-        return cls(torch.cos(angles).to(device), torch.sin(angles).to(device), tuple(d // 2 for d in dims))
+        position = torch.arange(max_positions, dtype=torch.float64)
+        angles = [torch.outer(position, 1.0 / theta ** (torch.arange(0, d, 2, dtype=torch.float64) / d))
+                  for d in _axis_dims(head_dim)]
+        joined = torch.cat(angles, dim=1)
+        return cls(joined.cos().to(device), joined.sin().to(device), tuple(a.shape[1] for a in angles))
 
     @classmethod
     def longcat(cls, head_dim, num_frames, height, width, *, base=10000.0, device="cpu"):
-        """LongCat-Video ``rope_3d`` tables computed in float32 (per-axis grids and frequencies)."""
+        """LongCat-Video 3-D tables, computed in FP32 as its ``rope_3d`` does, one axis per grid extent."""
         _int(head_dim, "head_dim", minimum=8)
         if head_dim % 8:
-            raise ConfigurationError("LongCat 3D RoPE requires head_dim divisible by 8")
-        dims = (head_dim - 4 * (head_dim // 6), 2 * (head_dim // 6), 2 * (head_dim // 6))
-        tables = []
-        for dim, count in zip(dims, (num_frames, height, width)):
-            _int(count, "axis length", minimum=1)
-            inverse = 1.0 / (base ** (torch.arange(0, dim, 2)[: dim // 2].float() / dim))
-            grid = torch.arange(count, dtype=torch.float32)
-            tables.append(torch.outer(grid, inverse))
-        rows = max(t.shape[0] for t in tables)
-        pairs = sum(t.shape[1] for t in tables)
-        cos = torch.full((rows, pairs), float("nan"), dtype=torch.float32)
-        sin = torch.full_like(cos, float("nan"))
-        column = 0
-        for t in tables:
-            cos[:t.shape[0], column:column + t.shape[1]] = t.cos()
-            sin[:t.shape[0], column:column + t.shape[1]] = t.sin()
-            column += t.shape[1]
-        return cls(cos.to(device), sin.to(device), tuple(t.shape[1] for t in tables),
-                   tuple(t.shape[0] for t in tables))
+            raise ConfigurationError(f"LongCat RoPE: head_dim {head_dim} is not a multiple of 8")
+        angles = []
+        for d, extent in zip(_axis_dims(head_dim), (num_frames, height, width)):
+            _int(extent, "grid extent", minimum=1)
+            frequency = 1.0 / (base ** (torch.arange(0, d, 2)[:d // 2].float() / d))
+            angles.append(torch.outer(torch.arange(extent, dtype=torch.float32), frequency))
+        cos, sin, widths, lengths = _separable(angles)
+        return cls(cos.to(device), sin.to(device), widths, lengths)
 
     def _stamp(self):
         if self.cos.is_inference() or self.sin.is_inference():
@@ -331,74 +344,79 @@ class RopeTable:
 # Completion handle
 # ---------------------------------------------------------------------------------------------
 
-_DEFERRED = []
-_DEFERRED_LOCK = threading.RLock()
+class _Graveyard:
+    """Keepalives of handles dropped before their GPU work finished: each stays referenced until its event
+    completes, so no tensor a queued kernel reads is freed under it. Swept on every restore call."""
+
+    def __init__(self):
+        self._lock = threading.RLock()
+        self._entries: list = []
+
+    def bury(self, event, refs) -> None:
+        with self._lock:
+            self._entries.append((event, refs))
+
+    def sweep(self) -> None:
+        with self._lock:
+            self._entries = [(event, refs) for event, refs in self._entries if not event.query()]
+
+    def __len__(self) -> int:
+        with self._lock:
+            return len(self._entries)
+
+
+_GRAVEYARD = _Graveyard()
 
 
 def _sweep_deferred():
-    with _DEFERRED_LOCK:
-        if _DEFERRED:
-            _DEFERRED[:] = [(event, refs) for event, refs in _DEFERRED if not event.query()]
+    _GRAVEYARD.sweep()
 
 
 def pending_deferred():
-    with _DEFERRED_LOCK:
-        return len(_DEFERRED)
+    """Number of dropped handles whose GPU work has not been seen to finish."""
+    return len(_GRAVEYARD)
 
 
 class RestoreHandle:
-    """Completion of one :func:`reconstruct` call: a CUDA event recorded after the last write, and a
-    keepalive of every input and temporary until :meth:`release` (or, when dropped unreleased, until
-    the event completes)."""
+    """What one :func:`reconstruct` call returns: the event recorded after its last write on ``stream`` and
+    the references that keep its inputs and temporaries alive. :meth:`release` waits for the event and drops
+    them; a handle dropped without release hands them to the graveyard until the event completes.
+    ``stats``: jobs, launches, FLOPs, backend and precision of the call."""
 
     def __init__(self, *, event, stream, keepalive, stats):
-        self._event = event
-        self._stream = stream
-        self._keepalive = keepalive
+        self._event, self._stream, self._keepalive = event, stream, keepalive
         self._released = False
         self.stats = stats
 
-    @property
-    def event(self):
-        return self._event
-
-    @property
-    def stream(self):
-        return self._stream
-
-    @property
-    def released(self):
-        return self._released
+    event = property(lambda self: self._event)
+    stream = property(lambda self: self._stream)
+    released = property(lambda self: self._released)
 
     def query(self):
-        return self._event is None or self._event.query()
+        """True once every write of the call has finished (always True on the host path)."""
+        return self._event.query() if self._event is not None else True
 
     def synchronize(self):
         if self._event is not None:
             self._event.synchronize()
 
     def wait(self, stream=None):
-        if self._event is None:
-            return
-        if stream is None:
-            stream = torch.cuda.current_stream(self._stream.device)
-        stream.wait_event(self._event)
+        """Order ``stream`` (default: the current stream of the call's device) after the call's writes."""
+        if self._event is not None:
+            (stream or torch.cuda.current_stream(self._stream.device)).wait_event(self._event)
 
     def release(self):
-        if self._released:
-            return
-        self.synchronize()
-        self._keepalive = None
-        self._released = True
-        _sweep_deferred()
+        if not self._released:
+            self.synchronize()
+            self._keepalive, self._released = None, True
+            _GRAVEYARD.sweep()
 
     def __del__(self):
         try:
-            if not self._released and self._event is not None and self._keepalive is not None:
-                if not self._event.query():
-                    with _DEFERRED_LOCK:
-                        _DEFERRED.append((self._event, self._keepalive))
-        except Exception:  # noqa: BLE001 - interpreter shutdown
+            unfinished = self._event is not None and self._keepalive is not None and not self._event.query()
+            if not self._released and unfinished:
+                _GRAVEYARD.bury(self._event, self._keepalive)
+        except Exception:  # noqa: BLE001 -- torch may already be torn down at interpreter exit
             pass
 
 
@@ -516,90 +534,108 @@ def _matrix_flops(jobs):
 
 
 def _resolve_backend(backend, cuda):
+    """``reference`` for host jobs (or on request); ``fused`` for CUDA jobs, which needs the native
+    extension: a missing library raises (naming it) instead of quietly running the host math."""
     if backend == "reference" or (backend == "auto" and not cuda):
         return "reference"
     if not cuda:
-        raise UnsupportedError(f"the {backend} backend needs CUDA tensors; use 'reference'")
+        raise UnsupportedError(f"backend {backend!r} runs CUDA jobs only; these are on the host")
     from .ops._ext import ext
 
-    ext()  # raises UnsupportedError naming the missing library: never a silent fallback
+    ext()
     return "fused"
+
+
+def _resolve_precision(precision, backend):
+    if precision != "auto" and precision not in PRECISIONS:
+        raise ConfigurationError(f"precision {precision!r}: expected 'auto' or one of {PRECISIONS}")
+    # "auto" is the two-product split for every destination dtype: its bound does not grow with the
+    # cancellation inside sum_k a_k q_k, while a single FP16 product's does.
+    resolved = DEFAULT_PRECISION if precision == "auto" else precision
+    if backend == "fused" and resolved not in KERNEL_PRECISIONS:
+        raise UnsupportedError(f"the sm_100a restore kernel computes {KERNEL_PRECISIONS}; {resolved!r} is "
+                               f"available with backend='reference'")
+    return resolved
+
+
+def _launch_fused(jobs, device, precision, stream, keepalive):
+    """Launch factorized jobs in groups of ``MAX_JOBS_PER_LAUNCH`` and dense ones in groups of
+    ``MAX_DENSE_JOBS_PER_LAUNCH``; returns the number of launches."""
+    factor = [job for job in jobs if not isinstance(job.source, DenseSource)]
+    dense = [job for job in jobs if isinstance(job.source, DenseSource)]
+    launches = 0
+    for first in range(0, len(factor), MAX_JOBS_PER_LAUNCH):
+        launches += _fused_factor_group(factor[first:first + MAX_JOBS_PER_LAUNCH], device, precision, stream,
+                                        keepalive)
+    for first in range(0, len(dense), MAX_DENSE_JOBS_PER_LAUNCH):
+        launches += _fused_dense_group(dense[first:first + MAX_DENSE_JOBS_PER_LAUNCH], device, stream, keepalive)
+    return launches
 
 
 def reconstruct(jobs, *, backend="auto", precision="auto", stream=None, wait_events=(), native_rope=None,
                 native_rope_dtype=None, compute_dtype=torch.float64, stage_events=None, config=None):
-    """Reconstruct restored matrices into their native cache slots.
+    """Write every job's restored matrix into its native cache slot; returns a :class:`RestoreHandle`.
 
-    One call should cover all restored chunks of a layer (K and V): the fused backend runs one
-    persistent launch per 16 factorized jobs (and one per 48 dense jobs). ``stream`` (default:
-    current) first waits on ``wait_events``. ``native_rope(pre_rope[N, H, D], job)`` replaces the
-    built-in rotation for RoPE jobs (the exact engine path). Returns a :class:`RestoreHandle`.
+    Pass all restored chunks of a layer (its K and V) in one call: the fused backend issues one persistent
+    launch per ``MAX_JOBS_PER_LAUNCH`` factorized jobs and per ``MAX_DENSE_JOBS_PER_LAUNCH`` dense ones.
+    The work is queued on ``stream`` (default: the device's current stream) after ``wait_events``.
+    ``native_rope(pre_rope [N, H, D], job)``, when given, rotates RoPE jobs with the engine's own function
+    instead of the kernel's tables (those jobs reconstruct into scratch first). ``stage_events``, a list,
+    receives ``("start", event)`` and ``("fused", event)`` timing events around the launches.
     """
-    _sweep_deferred()
+    _GRAVEYARD.sweep()
     jobs, device = _validate(jobs)
     if backend not in BACKENDS:
-        raise ConfigurationError(f"backend must be one of {BACKENDS}")
-    if precision != "auto" and precision not in PRECISIONS:
-        raise ConfigurationError(f"precision must be 'auto' or one of {PRECISIONS}")
+        raise ConfigurationError(f"backend {backend!r}: expected one of {BACKENDS}")
     if native_rope is not None and not callable(native_rope):
-        raise ConfigurationError("native_rope must be callable")
+        raise ConfigurationError("native_rope must be a callable (pre_rope, job) -> tensor")
     stats = {"jobs": len(jobs), "matrices": len(jobs), "flops": _matrix_flops(jobs), "launches": 0}
     if not jobs:
-        stats.update(backend="none", precision=None)
-        return RestoreHandle(event=None, stream=None, keepalive=None, stats=stats)
+        return RestoreHandle(event=None, stream=None, keepalive=None,
+                             stats={**stats, "backend": "none", "precision": None})
     cuda = device.type == "cuda"
     backend = _resolve_backend(backend, cuda)
-    if precision == "auto":
-        # Every destination dtype takes the two-product split: its error bound does not depend on the
-        # cancellation in sum_k a_k q_k, which a single FP16 product's bound does.
-        precision = DEFAULT_PRECISION
-    if backend == "fused" and precision not in KERNEL_PRECISIONS:
-        raise UnsupportedError(f"the fused sm_100a kernel runs {KERNEL_PRECISIONS}; use backend='reference' "
-                               f"for {precision}")
-    if cuda:
-        stream = torch.cuda.current_stream(device) if stream is None else stream
-        if not isinstance(stream, torch.cuda.Stream) or stream.device != device:
-            raise ConfigurationError("stream must be a torch.cuda.Stream on the jobs' device")
-    elif stream is not None or wait_events:
-        raise ConfigurationError("host execution takes no CUDA stream or events")
-    keepalive = [tensor for job in jobs for tensor in job.tensors()]
-    stats.update(backend=backend, precision=precision if backend != "reference" else str(compute_dtype))
-    if cuda:
+    precision = _resolve_precision(precision, backend)
+    if not cuda:
+        if stream is not None or wait_events:
+            raise ConfigurationError("host jobs run synchronously: pass no stream and no wait_events")
+    else:
+        stream = stream if stream is not None else torch.cuda.current_stream(device)
+        if not (isinstance(stream, torch.cuda.Stream) and stream.device == device):
+            raise ConfigurationError(f"stream must be a torch.cuda.Stream of {device}")
         for event in wait_events:
             stream.wait_event(event)
-    if stage_events is not None and cuda:
-        start = torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        stage_events.append(("start", start))
+    keepalive = [tensor for job in jobs for tensor in job.tensors()]
+    stats["backend"] = backend
+    stats["precision"] = str(compute_dtype) if backend == "reference" else precision
+
+    def mark(name):
+        if stage_events is not None and cuda:
+            event = torch.cuda.Event(enable_timing=True)
+            event.record(stream)
+            stage_events.append((name, event))
+
+    mark("start")
     if backend == "reference":
         with torch.cuda.stream(stream) if cuda else _null():
             reconstruct_reference(jobs, compute_dtype=compute_dtype, native_rope=native_rope,
                                   native_rope_dtype=native_rope_dtype)
     else:
+        by_engine = [native_rope is not None and job.rope is not None for job in jobs]
+        engine_rope = [job for job, engine in zip(jobs, by_engine) if engine]
         try:
-            exact = [job for job in jobs if native_rope is not None and job.rope is not None]
-            ordinary = [job for job in jobs if not (native_rope is not None and job.rope is not None)]
-            factor = [job for job in ordinary if not isinstance(job.source, DenseSource)]
-            dense = [job for job in ordinary if isinstance(job.source, DenseSource)]
-            for i in range(0, len(factor), MAX_JOBS_PER_LAUNCH):
-                stats["launches"] += _fused_factor_group(factor[i:i + MAX_JOBS_PER_LAUNCH], device, precision,
-                                                         stream, keepalive)
-            for i in range(0, len(dense), MAX_DENSE_JOBS_PER_LAUNCH):
-                stats["launches"] += _fused_dense_group(dense[i:i + MAX_DENSE_JOBS_PER_LAUNCH], device, stream,
-                                                        keepalive)
-            if exact:
-                stats["launches"] += _native_rope_jobs(exact, native_rope, native_rope_dtype, precision, device,
-                                                       stream, keepalive)
+            stats["launches"] += _launch_fused([job for job, engine in zip(jobs, by_engine) if not engine], device,
+                                               precision, stream, keepalive)
+            if engine_rope:
+                stats["launches"] += _native_rope_jobs(engine_rope, native_rope, native_rope_dtype, precision,
+                                                       device, stream, keepalive)
         except BaseException:
+            # kernels of earlier groups may still read the inputs: keep them until the stream passes here
             failed = torch.cuda.Event()
             failed.record(stream)
-            with _DEFERRED_LOCK:
-                _DEFERRED.append((failed, keepalive))
+            _GRAVEYARD.bury(failed, keepalive)
             raise
-    if stage_events is not None and cuda:
-        stop = torch.cuda.Event(enable_timing=True)
-        stop.record(stream)
-        stage_events.append(("fused", stop))
+    mark("fused")
     event = None
     if cuda:
         event = torch.cuda.Event()
@@ -608,35 +644,31 @@ def reconstruct(jobs, *, backend="auto", precision="auto", stream=None, wait_eve
 
 
 def _native_rope_jobs(jobs, native_rope, native_rope_dtype, precision, device, stream, keepalive):
-    """Pre-RoPE reconstruction into scratch slots, then the engine's own RoPE callable into the slot."""
-    launches = 0
-    scratch_jobs = []
-    pending = []
+    """RoPE jobs rotated by the engine: reconstruct each without rotation into a ``[T, H, D]`` scratch (a
+    dense source already in the scratch dtype is used as it is), then write ``native_rope(scratch, job)``
+    into the slot."""
+    staged, rotations = [], []
     for job in jobs:
         view = job.destination
-        dtype = view.tensor.dtype if native_rope_dtype is None else native_rope_dtype
+        dtype = native_rope_dtype or view.tensor.dtype
+        if isinstance(job.source, DenseSource) and job.source.values.dtype == dtype:
+            rotations.append((job, job.source.values.reshape(job.tokens, view.heads, view.head_dim)))
+            continue
         with torch.cuda.stream(stream):
             scratch = torch.empty((job.tokens, view.heads, view.head_dim), dtype=dtype, device=device)
         keepalive.append(scratch)
-        if isinstance(job.source, DenseSource) and job.source.values.dtype == dtype:
-            pending.append((job, job.source.values.reshape(job.tokens, view.heads, view.head_dim)))
-            continue
-        scratch_jobs.append(ReconstructionJob(job.source, NativeView(scratch, "THD"), job.grid, job.basis, job.rank,
-                                              None, job.label, job.basis_t))
-        pending.append((job, scratch))
-    factor = [j for j in scratch_jobs if not isinstance(j.source, DenseSource)]
-    dense = [j for j in scratch_jobs if isinstance(j.source, DenseSource)]
-    for i in range(0, len(factor), MAX_JOBS_PER_LAUNCH):
-        launches += _fused_factor_group(factor[i:i + MAX_JOBS_PER_LAUNCH], device, precision, stream, keepalive)
-    for i in range(0, len(dense), MAX_DENSE_JOBS_PER_LAUNCH):
-        launches += _fused_dense_group(dense[i:i + MAX_DENSE_JOBS_PER_LAUNCH], device, stream, keepalive)
+        staged.append(ReconstructionJob(job.source, NativeView(scratch, "THD"), job.grid, job.basis, job.rank,
+                                        None, job.label, job.basis_t))
+        rotations.append((job, scratch))
+    launches = _launch_fused(staged, device, precision, stream, keepalive)
     with torch.cuda.stream(stream):
-        for job, pre in pending:
-            result = native_rope(pre, job)
-            if not isinstance(result, torch.Tensor) or result.numel() != pre.numel():
-                raise IntegrityError("native RoPE callable returned a tensor of the wrong size")
-            job.destination.slot(job.tokens).copy_(result.reshape(pre.shape))
-            keepalive.append(result)
+        for job, pre in rotations:
+            rotated = native_rope(pre, job)
+            if not isinstance(rotated, torch.Tensor) or rotated.numel() != pre.numel():
+                raise IntegrityError(f"native_rope returned {getattr(rotated, 'shape', type(rotated))} for a "
+                                     f"{tuple(pre.shape)} input")
+            job.destination.slot(job.tokens).copy_(rotated.reshape(pre.shape))
+            keepalive.append(rotated)
     return launches
 
 
@@ -663,14 +695,10 @@ class WarmupShape:
     def __post_init__(self):
         _int(self.heads, "heads", minimum=1)
         _int(self.head_dim, "head_dim", minimum=2)
-        if self.dtype not in OUTPUT_DTYPES:
-            raise ConfigurationError("warm-up dtype must be an output dtype")
-        if self.layout not in LAYOUTS:
-            raise ConfigurationError("warm-up layout must be a native layout")
-        if self.source not in WARMUP_SOURCES:
-            raise ConfigurationError(f"warm-up source must be one of {WARMUP_SOURCES}")
-        if self.rope not in WARMUP_ROPE_MODES:
-            raise ConfigurationError(f"warm-up rope must be one of {WARMUP_ROPE_MODES}")
+        for name, value, allowed in (("dtype", self.dtype, OUTPUT_DTYPES), ("layout", self.layout, LAYOUTS),
+                                     ("source", self.source, WARMUP_SOURCES), ("rope", self.rope, WARMUP_ROPE_MODES)):
+            if value not in allowed:
+                raise ConfigurationError(f"WarmupShape.{name}={value!r}: expected one of {tuple(allowed)}")
 
 
 def warmup(device, shapes, *, backend="auto", precision="auto", stream=None, **_ignored):
