@@ -104,6 +104,26 @@ def main(argv=None):
                flops=flops)
         record(f"gemm_{name}_cublas", timed(lambda i: torch.matmul(a_ring[i], wt.t(), out=outs[i % 2]), len(a_ring)),
                flops=flops)
+    # the block's GEMMs with the epilogues the DiT uses: bias + tanh-GELU (FFN up), bias + gate * (.) + residual
+    # (out-projection, FFN down); the library rows are cuBLAS followed by the same elementwise math in torch
+    fused = () if args.only == "norms" else (("ffn_up_gelu", F, C, "gelu"), ("out_proj_gated", C, C, "gated"),
+                                             ("ffn_down_gated", C, F, "gated"))
+    for name, n, k, kind in fused:
+        a_ring = ring(lambda: torch.randn(T, k, device=device).bfloat16(), T * k * 2)
+        wt = (torch.randn(n, k, device=device) / k ** 0.5).bfloat16()
+        bias = (0.02 * torch.randn(n, device=device)).bfloat16()
+        gate = 1.0 + 0.05 * torch.randn(n, device=device)
+        resid = [torch.randn(T, n, device=device).bfloat16() for _ in range(2)]
+        flops = 2.0 * T * n * k
+        if kind == "gelu":
+            outs = [torch.empty(T, n, device=device, dtype=torch.bfloat16) for _ in range(2)]
+            ours = lambda i: gemm.linear_gelu(a_ring[i], wt, bias, out=outs[i % 2])
+            library = lambda i: torch.nn.functional.gelu(torch.addmm(bias, a_ring[i], wt.t()), approximate="tanh")
+        else:
+            ours = lambda i: gemm.linear_gated_residual(a_ring[i], wt, bias, gate, resid[i % 2])
+            library = lambda i: resid[i % 2].add_((torch.addmm(bias, a_ring[i], wt.t()).float() * gate).bfloat16())
+        record(f"gemm_{name}_tcgen05", timed(ours, len(a_ring)), flops=flops)
+        record(f"gemm_{name}_cublas_torch", timed(library, len(a_ring)), flops=flops)
     # raw-tier staging: one chunk's 60 K/V matrices device -> pinned host -> device on a side stream
     mats = [torch.randn(T, C, device=device).bfloat16() for _ in range(60 if args.only == "all" else 0)]
     hosts = [torch.empty(T, C, dtype=torch.bfloat16, pin_memory=True) for _ in range(len(mats))]

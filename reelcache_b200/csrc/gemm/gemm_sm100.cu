@@ -2,11 +2,13 @@
 // operands (both K-major, i.e. torch's x @ W^T for a Linear weight W[N, K]), fp32 accumulation in
 // TMEM, and a fused epilogue (bias, tanh-GELU, gated residual, fp32 or bf16 output).
 //
-// Roles (192 threads, one CTA per SM):
+// Roles (320 threads, one CTA per SM):
 //   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per stage, 128-byte swizzle.
 //   warp 1      TMEM owner and MMA issuer (one elected lane issues tcgen05.mma, 4 per K block).
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31),
-//               fused math, vectorized global stores.
+//   warps 2..9  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31; the two
+//               warps of one lane quarter take alternate 32-column chunks), fused math, vectorized global
+//               stores. The chunk's bias, gate and residual are loaded with 16-byte loads before its
+//               TMEM read, so their latency overlaps it.
 // The accumulator is double-buffered in TMEM (2 x BN fp32 columns) so the epilogue of tile t
 // overlaps the main loop of tile t+1.
 #include <ATen/ATen.h>
@@ -38,7 +40,8 @@ struct EpiParams {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kGroupM = 8;
 
 template <int BN>
@@ -51,12 +54,44 @@ struct Config {
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+// tanh-approximated GELU; tanh from the hardware approximation (relative error below 2^-10, far under the
+// bfloat16 rounding of the output).
 __device__ __forceinline__ float gelu_tanh(float x) {
-  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
-  const float k1 = 0.044715f;
-  float u = k0 * (x + k1 * x * x * x);
-  return 0.5f * x * (1.0f + tanhf(u));
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);  // sqrt(2/pi) (x + 0.044715 x^3)
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * x * (1.0f + t);
 }
+
+__device__ __forceinline__ float bf16_lo(uint32_t pair) { return __uint_as_float(pair << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t pair) { return __uint_as_float(pair & 0xffff0000u); }
+
+// 32 consecutive bfloat16 values as 16 packed pairs; ``vec``: four 16-byte loads (aligned, all in range),
+// else element loads of the first ``valid`` values (the rest zero).
+template <bool kReadOnly>
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* p, bool vec, int valid, uint32_t (&out)[16]) {
+  if (vec) {
+    const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 u = kReadOnly ? __ldg(q + i) : q[i];
+      out[4 * i] = u.x;
+      out[4 * i + 1] = u.y;
+      out[4 * i + 2] = u.z;
+      out[4 * i + 3] = u.w;
+    }
+  } else {
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(p);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t lo = 2 * j < valid ? h[2 * j] : 0u;
+      const uint32_t hi = 2 * j + 1 < valid ? h[2 * j + 1] : 0u;
+      out[j] = lo | (hi << 16);
+    }
+  }
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m_idx, int& n_idx) {
   const int per_group = kGroupM * num_n;
@@ -97,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], kEpiWarps);
     }
     mbar_init(drained, 1);
     fence_barrier_init();
@@ -189,7 +224,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ---------------- Epilogue ----------------
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int quarter = warp & 3;         // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;     // this warp's alternate 32-column chunks: half, half + 2, ...
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       int m_idx, n_idx;
@@ -204,9 +240,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = m_idx * kBM + quarter * 32 + lane;
       const bool row_ok = row < M;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half; c < BN / 32; c += 2) {
         const int n0 = n_idx * BN + c * 32;
         if (n0 >= N) break;  // uniform across the warp
+        const int valid = min(32, N - n0);
+        uint32_t bias2[16], res2[16];
+        float g[32];
+        if (EPI != kStore && ep.bias != nullptr)
+          load_bf16x32<true>(ep.bias + n0, valid == 32 && aligned16(ep.bias + n0), valid, bias2);
+        if (EPI == kBiasGateResid) {
+          const __nv_bfloat16* rrow = ep.resid + static_cast<int64_t>(row) * ep.ldr + n0;
+          if (row_ok) load_bf16x32<false>(rrow, valid == 32 && aligned16(rrow), valid, res2);
+          if (ep.gate != nullptr) {
+            if (valid == 32 && aligned16(ep.gate + n0)) {
+              const float4* q = reinterpret_cast<const float4*>(ep.gate + n0);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 u = __ldg(q + i);
+                g[4 * i] = u.x;
+                g[4 * i + 1] = u.y;
+                g[4 * i + 2] = u.z;
+                g[4 * i + 3] = u.w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) g[j] = j < valid ? ep.gate[n0 + j] : 0.0f;
+            }
+          }
+        }
         uint32_t raw[32];
         tmem_ld_32x32b_x32(tmem_base + buf * BN + c * 32 + (static_cast<uint32_t>(quarter * 32) << 16), raw);
         tmem_wait_ld();
@@ -214,14 +275,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) * ep.alpha;
-        const bool full_chunk = (n0 + 32 <= N);
-        if (EPI != kStore) {
+        if (EPI != kStore && ep.bias != nullptr) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = n0 + j;
-            if (full_chunk || n < N) {
-              if (ep.bias != nullptr) v[j] += __bfloat162float(ep.bias[n]);
-            }
+          for (int j = 0; j < 16; ++j) {
+            v[2 * j] += bf16_lo(bias2[j]);
+            v[2 * j + 1] += bf16_hi(bias2[j]);
           }
         }
         if (EPI == kBiasGelu) {
@@ -229,29 +287,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
         }
         if (EPI == kBiasGateResid) {
-          const __nv_bfloat16* rrow = ep.resid + static_cast<int64_t>(row) * ep.ldr + n0;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = n0 + j;
-            if (full_chunk || n < N) {
-              const float g = ep.gate != nullptr ? ep.gate[n] : 1.0f;
-              v[j] = __bfloat162float(rrow[j]) + v[j] * g;
-            }
+          for (int j = 0; j < 16; ++j) {
+            const float g0 = ep.gate != nullptr ? g[2 * j] : 1.0f;
+            const float g1 = ep.gate != nullptr ? g[2 * j + 1] : 1.0f;
+            v[2 * j] = fmaf(v[2 * j], g0, bf16_lo(res2[j]));
+            v[2 * j + 1] = fmaf(v[2 * j + 1], g1, bf16_hi(res2[j]));
           }
         }
         if (OUT_F32) {
           float* orow = reinterpret_cast<float*>(ep.out) + static_cast<int64_t>(row) * ep.ldo + n0;
-          if (full_chunk && (reinterpret_cast<uintptr_t>(orow) & 15) == 0) {
+          if (valid == 32 && aligned16(orow)) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
               *reinterpret_cast<float4*>(orow + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
           } else {
+#pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (n0 + j < N) orow[j] = v[j];
+              if (j < valid) orow[j] = v[j];
           }
         } else {
           __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(ep.out) + static_cast<int64_t>(row) * ep.ldo + n0;
-          if (full_chunk && (reinterpret_cast<uintptr_t>(orow) & 15) == 0) {
+          if (valid == 32 && aligned16(orow)) {
 #pragma unroll
             for (int j = 0; j < 32; j += 8) {
               uint4 pk;
@@ -262,8 +319,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               *reinterpret_cast<uint4*>(orow + j) = pk;
             }
           } else {
+#pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (n0 + j < N) orow[j] = __float2bfloat16(v[j]);
+              if (j < valid) orow[j] = __float2bfloat16(v[j]);
           }
         }
       }

@@ -173,77 +173,81 @@ class LineageRuntime:
 
     @staticmethod
     def _lineage_name(branch_id: str) -> str:
-        if not isinstance(branch_id, str) or not branch_id or "\x00" in branch_id:
-            raise ConfigurationError("lineage ids must be nonempty strings")
-        return LINEAGE_PREFIX + branch_id
+        if isinstance(branch_id, str) and branch_id and "\x00" not in branch_id:
+            return LINEAGE_PREFIX + branch_id
+        raise ConfigurationError(f"lineage id {branch_id!r} is not a non-empty string without NUL")
 
     def _entries(self, streams: Sequence[str]) -> list:
         keys = [MatrixKey(layer, target) for layer in range(self.model.layers) for target in ("K", "V")]
-        return keys if not streams else [(key, stream) for key in keys for stream in streams]
+        return [(key, stream) for key in keys for stream in streams] if streams else keys
+
+    def _idle(self, branch_id: str, action: str) -> None:
+        if branch_id in self._lineage_pending:
+            raise PendingError(f"lineage {branch_id!r} has a commit in flight; {action} after it publishes")
 
     def create_lineage(self, branch_id: str, *, epoch_id: str = "e0", details: Mapping[str, Any] | None = None,
                        streams: Sequence[str] = ()) -> str:
-        """Create a root node (initial epoch, empty active bases) and its head."""
+        """A new lineage whose head is a root node: zero tokens, the initial global epoch ``epoch_id`` and no
+        active basis for any matrix (of any of ``streams``)."""
+        streams = tuple(streams)
         with self._lock:
             name = self._lineage_name(branch_id)
-            streams = tuple(streams)
             with self.store.transaction():
                 if self.store.get_ref(name) is not None:
-                    raise StateError(f"lineage already exists: {branch_id}")
-                epoch = CacheEpoch(epoch_id, None, "initial", "global", (), details or {})
-                epoch_ref = self._put_epoch(epoch)
-                node = ChunkNode("root", "root", None, epoch_id, epoch_ref, 0, 0, 0, 0, 0, 0, (),
-                                 tuple((entry, ActiveBasisBinding()) for entry in self._entries(streams)),
+                    raise StateError(f"lineage {branch_id!r} exists already")
+                epoch_ref = self._put_epoch(CacheEpoch(epoch_id, None, "initial", "global", (), details or {}))
+                unbound = tuple((entry, ActiveBasisBinding()) for entry in self._entries(streams))
+                root = ChunkNode("root", "root", None, epoch_id, epoch_ref, 0, 0, 0, 0, 0, 0, (), unbound,
                                  streams=streams)
-                ref = self._put_node(node, {"kind": "root"})
-                self.store.set_ref(name, ref, expected=None)
-                return ref
+                root_ref = self._put_node(root, {"kind": "root"})
+                self.store.set_ref(name, root_ref, expected=None)
+                return root_ref
 
     def lineage_head(self, branch_id: str) -> str:
         head = self.store.get_ref(self._lineage_name(branch_id))
         if head is None:
-            raise StateError(f"lineage does not exist: {branch_id}")
+            raise StateError(f"no lineage named {branch_id!r}")
         return head
 
     def list_lineages(self) -> dict[str, str]:
-        return {name[len(LINEAGE_PREFIX):]: ref for name, ref in self.store.list_refs(LINEAGE_PREFIX).items()}
+        return {name.removeprefix(LINEAGE_PREFIX): ref for name, ref in self.store.list_refs(LINEAGE_PREFIX).items()}
 
     def fork_lineage(self, node_ref: str, branch_id: str) -> None:
-        """New head at any validated node; the source lineage is untouched."""
+        """Start lineage ``branch_id`` at ``node_ref`` (any readable node); other lineages do not move."""
         with self._lock:
             name = self._lineage_name(branch_id)
             with self.store.transaction():
                 self.load_node(node_ref)
                 if self.store.get_ref(name) is not None:
-                    raise StateError(f"fork target already exists: {branch_id}")
+                    raise StateError(f"cannot fork into {branch_id!r}: the lineage exists")
                 self.store.set_ref(name, node_ref, expected=None)
 
     def set_lineage_ownership(self, prefix: Any) -> None:
+        """``prefix(branch_id)`` names a ref folder whose heads count as the lineage's own for rewinds (a
+        detached side lineage keeps the chunks it took over reachable to the lineage it came from)."""
         self._lineage_owned_prefix = prefix
 
+    def _reachable(self, node_ref: str, heads) -> bool:
+        return any(node_ref in {ref for ref, _, _ in self.node_path(head)} for head in heads)
+
     def rewind_lineage(self, branch_id: str, node_ref: str) -> None:
-        """Move a head to one of its own ancestors (compare-and-swap)."""
+        """Move the lineage's head back to one of its ancestors (or to a node of a lineage it owns)."""
         with self._lock:
             name = self._lineage_name(branch_id)
-            if branch_id in self._lineage_pending:
-                raise PendingError("cannot rewind a lineage with a commit in flight")
+            self._idle(branch_id, "rewind")
             with self.store.transaction():
-                head = self.store.get_ref(name)
-                if head is None:
-                    raise StateError(f"lineage does not exist: {branch_id}")
-                if node_ref not in {ref for ref, _, _ in self.node_path(head)}:
-                    prefix = None if self._lineage_owned_prefix is None else self._lineage_owned_prefix(branch_id)
-                    owned = prefix is not None and any(
-                        node_ref in {r for r, _, _ in self.node_path(ref)}
-                        for ref in self.store.list_refs(prefix).values())
-                    if not owned:
-                        raise StateError("rewind target is not an ancestor of the lineage head")
+                head = self.lineage_head(branch_id)
+                allowed = self._reachable(node_ref, [head])
+                if not allowed and self._lineage_owned_prefix is not None:
+                    prefix = self._lineage_owned_prefix(branch_id)
+                    allowed = prefix is not None and self._reachable(node_ref, self.store.list_refs(prefix).values())
+                if not allowed:
+                    raise StateError(f"{node_ref} is not on lineage {branch_id!r}'s path; fork to reach it")
                 self.store.set_ref(name, node_ref, expected=head)
 
     def delete_lineage(self, branch_id: str) -> None:
         with self._lock:
-            if branch_id in self._lineage_pending:
-                raise PendingError("cannot delete a lineage with a commit in flight")
+            self._idle(branch_id, "delete it")
             self.store.delete_ref(self._lineage_name(branch_id))
 
     # -- commits -------------------------------------------------------------------------------------------------
@@ -266,13 +270,14 @@ class LineageRuntime:
                       contexts: Mapping[Any, TensorContext]) -> None:
         expected = set(self._entries(node.streams))
         if set(matrices) != expected or set(contexts) != expected:
-            raise ConfigurationError("a commit must cover every layer's K and V (every stream)")
+            raise ConfigurationError(f"a commit names {len(matrices)} matrices and {len(contexts)} contexts; the "
+                                     f"node expects exactly its {len(expected)} (layer, K/V[, stream]) entries")
         for entry, context in contexts.items():
             key, _ = entry_parts(entry)
             if context.key != key or context.model != self.model:
-                raise ConfigurationError("matrix context disagrees with its entry or the model")
+                raise ConfigurationError(f"context of {entry} describes {context.key} of {context.model.name!r}")
             if tuple(matrices[entry].reshape(-1, context.channels).shape) != context.shape:
-                raise ConfigurationError("matrix shape differs from its context")
+                raise ConfigurationError(f"{entry}: matrix does not reshape to its context's {context.shape}")
 
     def prepare_commit(self, node_kind: str, branch_id: str, chunk_id: str, ranges, *, method: RankMethodConfig,
                        registry: RankPredictorRegistry | None, epoch_id: str | None = None,
@@ -425,19 +430,19 @@ class LineageRuntime:
         state (which must then be given)."""
         started = time.perf_counter()
         if not kv_objects and not execution_state:
-            raise ConfigurationError("a latents-only node needs the execution state it is replayed from")
+            raise ConfigurationError("kv_objects=False stores no KV: pass the execution_state the node is replayed from")
         with self._lock:
             head = self.lineage_head(branch_id) if expected_head is None else expected_head
             head_node = self.load_node(head)
             self._check_inputs(head_node, matrices, contexts)
             if any(binding.version_ref is not None for _, binding in head_node.active_basis):
-                raise UnsupportedError("RAW nodes extend RAW lineages only (this head has active lossy bases)")
+                raise UnsupportedError(f"head {head} binds lossy bases; exact RAW nodes go on RAW lineages")
             with self.store.transaction():
                 records = self._raw_records(matrices, contexts) if kv_objects else {}
                 state_ref = self.store.put(serialize_tensors(dict(execution_state))) if execution_state else None
                 context = next(iter(contexts.values()))
                 if context.token_start != head_node.frontier:
-                    raise ConfigurationError("RAW chunk does not start at the head's frontier")
+                    raise ConfigurationError(f"RAW chunk starts at {context.token_start}; the head ends at {head_node.frontier}")
                 node = ChunkNode("chunk", chunk_id, head, head_node.cache_epoch_id, head_node.epoch_ref,
                                  context.token_start, context.token_end, context.frames, context.height, context.width,
                                  context.token_end, tuple(records.items()), head_node.active_basis, state_ref,
@@ -461,14 +466,15 @@ class LineageRuntime:
             head = self.lineage_head(branch_id) if expected_head is None else expected_head
             head_node = self.load_node(head)
             if any(binding.version_ref is not None for _, binding in head_node.active_basis):
-                raise UnsupportedError("RAW recaches extend RAW lineages only (this head has active lossy bases)")
+                raise UnsupportedError(f"head {head} binds lossy bases; exact RAW recaches go on RAW lineages")
             with self.store.transaction():
                 epoch_ranges = []
                 for range_id, matrices, contexts in ranges:
                     self._check_inputs(head_node, matrices, contexts)
                     context = next(iter(contexts.values()))
                     if context.token_end > head_node.frontier:
-                        raise ConfigurationError("a recache re-materializes generated tokens only")
+                        raise ConfigurationError(f"range {range_id!r} ends at {context.token_end}, past the generated "
+                                                 f"{head_node.frontier} tokens")
                     records = self._raw_records(matrices, contexts) if kv_objects else {}
                     epoch_ranges.append(TokenRangeRecords(range_id, context.token_start, context.token_end,
                                                           context.frames, context.height, context.width,
