@@ -40,6 +40,15 @@ __device__ __forceinline__ uint4 pack8(const float* f) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// Eight consecutive FP32 parameters p[c0 .. c0 + 8) with two 16-byte read-only loads (p 16-byte aligned,
+// c0 a multiple of 8; the launchers check the alignment).
+__device__ __forceinline__ void load_f32x8(const float* __restrict__ p, int c0, float* out) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p + c0));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p + c0) + 1);
+  out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+  out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -86,15 +95,19 @@ __global__ void ln_modulate_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
   for (int i = 0; i < VEC; ++i) {
     const int c0 = (i * 32 + lane) * 8;
     if (c0 >= C) continue;
-    float o[8];
+    float o[8], wt[8], bs[8], sc[8], sh[8];
+    if (weight != nullptr) {
+      load_f32x8(weight, c0, wt);
+      load_f32x8(bias, c0, bs);
+    }
+    if (scale != nullptr) load_f32x8(scale, c0, sc);
+    if (shift != nullptr) load_f32x8(shift, c0, sh);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const int c = c0 + e;
       float t = (v[i * 8 + e] - mean) * rstd;
-      if (weight != nullptr) t = t * weight[c] + bias[c];
-      const float sc = scale != nullptr ? scale[c] : 0.0f;
-      const float sh = shift != nullptr ? shift[c] : 0.0f;
-      o[e] = t * (1.0f + sc) + sh;
+      if (weight != nullptr) t = fmaf(t, wt[e], bs[e]);
+      if (scale != nullptr) t = fmaf(t, sc[e], t);
+      o[e] = shift != nullptr ? t + sh[e] : t;
     }
     dst[i * 32 + lane] = pack8(o);
   }
@@ -110,8 +123,11 @@ __device__ __forceinline__ void rms_row(float* v, int C, int lane, const float* 
 #pragma unroll
   for (int i = 0; i < VEC; ++i) {
     const int c0 = (i * 32 + lane) * 8;
+    if (c0 >= C) continue;  // C is a multiple of 8: a lane's 8 channels are all in range or all out
+    float wt[8];
+    load_f32x8(w, c0, wt);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[i * 8 + e] = c0 + e < C ? v[i * 8 + e] * r * w[c0 + e] : 0.0f;
+    for (int e = 0; e < 8; ++e) v[i * 8 + e] = v[i * 8 + e] * r * wt[e];
   }
 }
 
@@ -147,9 +163,12 @@ __device__ __forceinline__ void rope_row(float* v, int C, int lane, int head_dim
     const int c0 = (i * 32 + lane) * 8;
     if (c0 >= C) continue;
     const int pair0 = (c0 % head_dim) >> 1;
+    const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + pair0));
+    const float4 s4 = __ldg(reinterpret_cast<const float4*>(sn + pair0));
+    const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float c = cs[pair0 + e], s = sn[pair0 + e];
+      const float c = cv[e], s = sv[e];
       const float a = v[i * 8 + 2 * e], b = v[i * 8 + 2 * e + 1];
       v[i * 8 + 2 * e] = a * c - b * s;
       v[i * 8 + 2 * e + 1] = a * s + b * c;
@@ -254,8 +273,9 @@ __global__ void head_norm_rope_kernel(const __nv_bfloat16* __restrict__ x, int64
 namespace {
 const float* opt_f32(const c10::optional<at::Tensor>& t, int64_t n, const char* name) {
   if (!t.has_value() || !t->defined()) return nullptr;
-  RC_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == n,
-           std::string(name) + " must be a contiguous CUDA float32 vector of the row width");
+  RC_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == n &&
+               reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+           std::string(name) + " must be a contiguous, 16-byte aligned CUDA float32 vector of the row width");
   return t->data_ptr<float>();
 }
 
@@ -314,8 +334,9 @@ void qkv_norm_rope(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor
            "qkv is [T, 3C]; outputs are [T, C]");
   RC_CHECK(cos_tok.is_cuda() && cos_tok.scalar_type() == at::kFloat && cos_tok.is_contiguous() &&
                cos_tok.size(0) == rows && cos_tok.size(1) * 2 == head_dim && sin_tok.sizes() == cos_tok.sizes() &&
-               sin_tok.is_contiguous(),
-           "cos/sin must be float32 [T, head_dim / 2] per-token tables");
+               sin_tok.is_contiguous() && reinterpret_cast<uintptr_t>(cos_tok.data_ptr()) % 16 == 0 &&
+               reinterpret_cast<uintptr_t>(sin_tok.data_ptr()) % 16 == 0 && head_dim % 8 == 0,
+           "cos/sin must be 16-byte aligned float32 [T, head_dim / 2] per-token tables");
   __nv_bfloat16* kp = nullptr;
   int64_t ld_kp = 0;
   if (k_pre.has_value() && k_pre->defined()) {
