@@ -50,8 +50,8 @@ def size_scaled_timeout(samples, *, seconds_per_megasample=_ENCODE_SECONDS_PER_M
 
 def encoder_record(inter_prediction):
     """The portable x265 contract of a version-2 coefficient stream (recorded in packet metadata)."""
-    if type(inter_prediction) is not bool:
-        raise ConfigurationError("inter_prediction must be a bool")
+    if inter_prediction not in (True, False) or type(inter_prediction) is not bool:
+        raise ConfigurationError(f"inter_prediction={inter_prediction!r}: expected True or False")
     gop = _INTER_GOP if inter_prediction else _ALL_INTRA_GOP
     return {
         "schema": ENCODER_SCHEMA, "encoder": "libx265", "preset": "ultrafast", "qp": 8,
@@ -69,10 +69,10 @@ def x265_parameter_string(inter_prediction, threads, frames):
 
 
 def x265_thread_params(threads, frames):
-    if type(threads) is not int or not 1 <= threads <= 64:
-        raise ConfigurationError("x265 threads must be an integer in [1, 64]")
-    frame_threads = 1 if threads < 4 else max(1, min(3, frames))
-    return f"pools={threads}:frame-threads={frame_threads}"
+    """Thread-pool part of the x265 parameters: frame threading only with 4+ pool threads, at most 3."""
+    if not (type(threads) is int and 0 < threads <= 64):
+        raise ConfigurationError(f"x265 pool threads {threads!r}: expected an int from 1 to 64")
+    return f"pools={threads}:frame-threads={min(3, max(1, frames)) if threads >= 4 else 1}"
 
 
 def discover_ffmpeg(path=None) -> str:
@@ -92,10 +92,16 @@ def ffmpeg_available(path=None) -> bool:
 
 
 def validate_parameters(pix_fmt, qp=8, preset="ultrafast"):
+    """The stream contract is pinned: a pixel format of ``PIXEL_FORMATS``, QP 8 and x265's ultrafast preset."""
+    problems = []
     if pix_fmt not in PIXEL_FORMATS:
-        raise UnsupportedError(f"HEVC supports exactly {PIXEL_FORMATS}, not {pix_fmt!r}")
-    if type(qp) is not int or qp != 8 or preset != "ultrafast":
-        raise UnsupportedError("this HEVC provider supports only QP8 with preset='ultrafast'")
+        problems.append(f"pixel format {pix_fmt!r} (supported: {', '.join(PIXEL_FORMATS)})")
+    if not (type(qp) is int and qp == 8):
+        problems.append(f"qp {qp!r} (pinned to 8)")
+    if preset != "ultrafast":
+        problems.append(f"preset {preset!r} (pinned to ultrafast)")
+    if problems:
+        raise UnsupportedError("HEVC coefficient streams cannot use " + ", ".join(problems))
 
 
 # ---------------------------------------------------------------------------------------------
@@ -115,8 +121,9 @@ def covering_affine(lo, hi):
         upper = np.float32(255) * scale + offset
         scale = np.where(upper.astype(np.float64) < hi, np.nextafter(scale, np.float32(np.inf)), scale)
         upper = np.float32(255) * scale + offset
-    if not np.isfinite(scale).all() or not np.isfinite(upper).all() or np.any(upper.astype(np.float64) < hi):
-        raise ConfigurationError("coefficient range cannot use a finite covering FP32 affine")
+    covered = np.isfinite(scale).all() and np.isfinite(upper).all() and not np.any(upper.astype(np.float64) < hi)
+    if not covered:
+        raise ConfigurationError("no finite FP32 (scale, offset) maps 0..255 over this coefficient range")
     return np.stack((scale, offset)).astype("<f4", copy=False)
 
 
@@ -124,13 +131,14 @@ _covering_affine = covering_affine
 
 
 def normalization_layout(rank, normalization, protected_fraction):
-    if type(rank) is not int or rank < 1:
-        raise ConfigurationError("coefficient rank must be a positive integer")
-    if normalization not in {"per_channel", "global", "leading_columns"}:
-        raise UnsupportedError("normalization must be per_channel, global, or leading_columns")
-    if (isinstance(protected_fraction, bool) or not isinstance(protected_fraction, (int, float))
-            or not math.isfinite(protected_fraction) or not 0 <= protected_fraction <= 1):
-        raise ConfigurationError("protected_fraction must be in [0, 1]")
+    if not (type(rank) is int and rank > 0):
+        raise ConfigurationError(f"coefficient rank {rank!r}: expected an int >= 1")
+    if normalization not in ("per_channel", "global", "leading_columns"):
+        raise UnsupportedError(f"normalization {normalization!r}: expected per_channel, global or leading_columns")
+    fraction_ok = (isinstance(protected_fraction, (int, float)) and not isinstance(protected_fraction, bool)
+                   and math.isfinite(protected_fraction) and 0 <= protected_fraction <= 1)
+    if not fraction_ok:
+        raise ConfigurationError(f"protected_fraction {protected_fraction!r}: expected a number in [0, 1]")
     if normalization == "per_channel":
         count, records = rank, rank
     elif normalization == "global":
@@ -173,8 +181,8 @@ def affine_for(lo, hi, layout):
 def quantize_coefficients(values, normalization, protected_fraction=1.0):
     """``(pixels uint8 [N, r], affine [2, records], layout)`` of FP32 coefficients."""
     values = np.asarray(values, dtype=np.float32)
-    if values.ndim != 2 or min(values.shape) < 1 or not np.isfinite(values).all():
-        raise ConfigurationError("coefficients must be a nonempty finite FP32 matrix")
+    if not (values.ndim == 2 and values.size and np.isfinite(values).all()):
+        raise ConfigurationError(f"quantize_coefficients takes a non-empty finite 2-D array, got shape {values.shape}")
     layout = normalization_layout(values.shape[1], normalization, protected_fraction)
     affine = affine_for(values.min(0), values.max(0), layout)
     scale, offset = expanded_affine(affine, layout, values.shape[1])
@@ -186,27 +194,30 @@ def quantize_coefficients(values, normalization, protected_fraction=1.0):
 
 def validate_affine(affine, layout, rank):
     affine = np.asarray(affine)
-    if (affine.dtype != np.dtype("<f4") or list(affine.shape) != layout["affine_shape"]
-            or not np.isfinite(affine).all() or np.any(affine[0] < 0)):
-        raise IntegrityError("invalid coefficient affine payload")
-    if layout["mode"] == "leading_columns" and layout["protected_count"] == rank and np.any(affine[:, 0] != 0):
-        raise IntegrityError("unused global affine must be zero when all columns are protected")
+    shape_ok = affine.dtype == np.dtype("<f4") and list(affine.shape) == layout["affine_shape"]
+    if not (shape_ok and np.isfinite(affine).all() and (affine[0] >= 0).all()):
+        raise IntegrityError(f"affine payload {affine.dtype} {list(affine.shape)} is not a finite little-endian FP32 "
+                             f"{layout['affine_shape']} with non-negative scales")
+    everything_protected = layout["mode"] == "leading_columns" and layout["protected_count"] == rank
+    if everything_protected and (affine[:, 0] != 0).any():
+        raise IntegrityError("the shared affine column must be zero when every column has its own affine")
     with np.errstate(over="ignore", invalid="ignore"):
-        upper = np.float32(255) * affine[0] + affine[1]
-    if not np.isfinite(upper).all():
-        raise IntegrityError("coefficient affine endpoints are nonfinite")
+        top = np.float32(255) * affine[0] + affine[1]
+    if not np.isfinite(top).all():
+        raise IntegrityError("an affine maps pixel 255 to a non-finite value")
     return affine
 
 
 def dequantize_coefficients(pixels, affine, layout):
     pixels = np.asarray(pixels)
-    if pixels.dtype != np.uint8 or pixels.ndim != 2 or min(pixels.shape) < 1:
-        raise IntegrityError("decoded coefficient pixels must be a nonempty uint8 matrix")
+    if not (pixels.dtype == np.uint8 and pixels.ndim == 2 and pixels.size):
+        raise IntegrityError(f"coefficient pixels must be a non-empty 2-D uint8 array, got {pixels.dtype} "
+                             f"{pixels.shape}")
     affine = validate_affine(affine, layout, pixels.shape[1])
     scale, offset = expanded_affine(affine, layout, pixels.shape[1])
     result = pixels.astype(np.float32) * scale + offset
     if not np.isfinite(result).all():
-        raise IntegrityError("decoded coefficients are nonfinite")
+        raise IntegrityError("dequantized coefficients contain non-finite values")
     return np.ascontiguousarray(result)
 
 
@@ -217,10 +228,12 @@ def dequantize_coefficients(pixels, affine, layout):
 
 def video_layout(frames, height, width, rank, pix_fmt="yuv444p"):
     validate_parameters(pix_fmt)
-    if any(type(v) is not int or v < 1 for v in (frames, height, width, rank)):
-        raise ConfigurationError("HEVC dimensions must be positive integers")
-    if height > MAX_DIMENSION or width > MAX_DIMENSION:
-        raise UnsupportedError(f"coefficient tiles cannot exceed {MAX_DIMENSION}x{MAX_DIMENSION}")
+    dims = {"frames": frames, "height": height, "width": width, "rank": rank}
+    bad = [name for name, value in dims.items() if not (type(value) is int and value > 0)]
+    if bad:
+        raise ConfigurationError(f"channel-tile layout: {', '.join(bad)} must be ints >= 1 ({dims})")
+    if max(height, width) > MAX_DIMENSION:
+        raise UnsupportedError(f"a {height}x{width} cell does not fit a {MAX_DIMENSION}-pixel picture")
     planes = 3 if pix_fmt == "yuv444p" else 1
     columns = min(MAX_DIMENSION // width, max(1, math.ceil(math.sqrt(rank / planes))))
     rows = min(MAX_DIMENSION // height, max(1, math.ceil(rank / (planes * columns))))
@@ -228,8 +241,8 @@ def video_layout(frames, height, width, rank, pix_fmt="yuv444p"):
     if pix_fmt == "yuv420p":
         image_width += image_width % 2
         image_height += image_height % 2
-    if image_width > MAX_DIMENSION or image_height > MAX_DIMENSION:
-        raise UnsupportedError("padded HEVC frame dimensions exceed provider support")
+    if max(image_width, image_height) > MAX_DIMENSION:
+        raise UnsupportedError(f"the {image_width}x{image_height} mosaic picture exceeds {MAX_DIMENSION} pixels")
     slots = columns * rows * planes
     return {
         "schema": "reelcache.channel_tiles.v1", "frames": frames, "height": height, "width": width, "rank": rank,
@@ -320,8 +333,9 @@ def nal_units(stream):
     """``[(offset, length, nal_type)]`` of an Annex-B HEVC stream, integrity-checked."""
     data = bytes(stream)
     positions = start_code_positions(data)
-    if not positions or positions[0] > 1 or (positions[0] == 1 and data[0] != 0):
-        raise IntegrityError("HEVC stream does not start with a start code")
+    leading = positions[0] if positions else None
+    if leading is None or leading > 1 or (leading == 1 and data[0] != 0):
+        raise IntegrityError("an Annex-B HEVC stream must begin with a 3- or 4-byte start code")
     units = []
     for i, pos in enumerate(positions):
         begin = pos + 3
@@ -329,10 +343,10 @@ def nal_units(stream):
         while end > begin and data[end - 1] == 0 and i + 1 < len(positions):
             end -= 1
         if end - begin < 2:
-            raise IntegrityError("truncated HEVC NAL unit header")
+            raise IntegrityError(f"NAL unit at byte {begin} is shorter than its 2-byte header")
         header = data[begin]
         if header & 0x80:
-            raise IntegrityError("HEVC forbidden_zero_bit is set")
+            raise IntegrityError(f"NAL unit at byte {begin} sets the forbidden zero bit")
         units.append((begin, end - begin, (header >> 1) & 0x3F))
     return units
 
@@ -365,11 +379,11 @@ def access_units(stream):
 def all_intra_access_units(stream, pictures):
     units = access_units(stream)
     if len(units) != pictures:
-        raise IntegrityError(f"HEVC stream holds {len(units)} pictures, expected {pictures}")
-    for offset, length in units:
-        kinds = {kind for _, _, kind in nal_units(stream[offset:offset + length]) if kind < 32}
-        if not kinds or not kinds <= _IDR_TYPES:
-            raise IntegrityError("all-intra HEVC stream contains a non-IDR picture")
+        raise IntegrityError(f"expected {pictures} access units, the stream has {len(units)}")
+    for number, (offset, length) in enumerate(units):
+        slices = {kind for _, _, kind in nal_units(stream[offset:offset + length]) if kind < 32}
+        if not slices or not slices <= _IDR_TYPES:
+            raise IntegrityError(f"picture {number} of an all-intra stream has slice types {sorted(slices)}, not IDR")
     return units
 
 
@@ -386,7 +400,8 @@ def _run(command, *, data=None, timeout=None):
     except subprocess.TimeoutExpired as error:
         raise UnsupportedError(f"ffmpeg timed out after {timeout} s") from error
     if result.returncode != 0:
-        raise UnsupportedError(f"ffmpeg failed: {result.stderr.decode(errors='replace')[-400:]}")
+        tail = result.stderr.decode(errors="replace")[-400:]
+        raise UnsupportedError(f"ffmpeg exited with {result.returncode}: {tail}")
     return result
 
 
@@ -396,7 +411,7 @@ def encode_pictures(pictures, pix_fmt="yuv444p", *, ffmpeg_path=None, threads=1,
     pictures = np.ascontiguousarray(pictures, dtype=np.uint8)
     frames, planes, height, width = pictures.shape
     if pix_fmt == "yuv444p" and planes != 3:
-        raise ConfigurationError("yuv444p pictures have three planes")
+        raise ConfigurationError(f"yuv444p pictures carry 3 planes, these carry {planes}")
     if pix_fmt == "yuv444p":
         raw = pictures.tobytes()
     else:
@@ -409,7 +424,7 @@ def encode_pictures(pictures, pix_fmt="yuv444p", *, ffmpeg_path=None, threads=1,
                "pipe:1"]
     result = _run(command, data=raw, timeout=size_scaled_timeout(pictures.size))
     if not result.stdout:
-        raise UnsupportedError("FFmpeg produced an empty HEVC stream")
+        raise UnsupportedError("ffmpeg returned no HEVC bytes")
     if not inter_prediction:
         all_intra_access_units(result.stdout, frames)
     return result.stdout
@@ -425,7 +440,7 @@ def decode_pictures(stream, *, pictures, height, width, pix_fmt="yuv444p", ffmpe
     frame_bytes = height * width * (3 if pix_fmt == "yuv444p" else 1) if pix_fmt == "yuv444p" else height * width * 3 // 2
     data = np.frombuffer(result.stdout, dtype=np.uint8)
     if data.size != pictures * frame_bytes:
-        raise IntegrityError("decoded HEVC picture count or size differs from the packet")
+        raise IntegrityError(f"decoder returned {data.size} bytes for {pictures} pictures of {frame_bytes} bytes")
     if pix_fmt == "yuv444p":
         return data.reshape(pictures, planes, height, width).copy()
     return data.reshape(pictures, frame_bytes)[:, :height * width].reshape(pictures, 1, height, width).copy()

@@ -46,15 +46,17 @@ def _key(label: str) -> MatrixKey:
 
 
 def _finite(value: Any, name: str) -> float:
-    if isinstance(value, bool) or not isinstance(value, (int, float)) or not math.isfinite(float(value)):
-        raise ConfigurationError(f"{name} must be a finite number")
-    return float(value)
+    number = isinstance(value, (int, float)) and not isinstance(value, bool)
+    if number and math.isfinite(value):
+        return float(value)
+    raise ConfigurationError(f"{name}={value!r} is not a finite int or float")
 
 
 def _keyed(values: Mapping, name: str) -> Mapping:
-    if not isinstance(values, Mapping) or any(not isinstance(k, MatrixKey) for k in values):
-        raise ConfigurationError(f"{name} must be a MatrixKey-keyed mapping")
-    return MappingProxyType(dict(values))
+    """A read-only copy of a mapping whose keys are all :class:`MatrixKey`."""
+    if isinstance(values, Mapping) and all(isinstance(key, MatrixKey) for key in values):
+        return MappingProxyType(dict(values))
+    raise ConfigurationError(f"{name} must map MatrixKey -> value")
 
 
 @dataclass(frozen=True)
@@ -71,8 +73,9 @@ class RankPredictorProfile:
     schema_version: str = PREDICTOR_SCHEMA
 
     def __post_init__(self) -> None:
-        if self.target not in ("K", "V") or self.history_regime not in ("startup", "later"):
-            raise ConfigurationError("predictor profiles are per K/V and startup/later regime")
+        if (self.target, self.history_regime) not in {(t, r) for t in "KV" for r in ("startup", "later")}:
+            raise ConfigurationError(f"predictor profile ({self.target!r}, {self.history_regime!r}): the target is K "
+                                     f"or V and the regime startup or later")
         object.__setattr__(self, "layer_template", tuple(_finite(v, "template rank") for v in self.layer_template))
         object.__setattr__(self, "anchor_layers", tuple(int(v) for v in self.anchor_layers))
         object.__setattr__(self, "rank_buckets", tuple(int(v) for v in self.rank_buckets))
@@ -116,53 +119,57 @@ class RankPolicy:
     schema_version: str = POLICY_SCHEMA
 
     def __post_init__(self) -> None:
+        def reject(problem):
+            raise ConfigurationError(f"RankPolicy {self.policy_id!r}: {problem}")
+
         if self.schema_version != POLICY_SCHEMA:
-            raise ConfigurationError("unsupported rank policy schema")
-        if not isinstance(self.policy_id, str) or not self.policy_id:
-            raise ConfigurationError("policy_id must be a nonempty string")
+            reject(f"schema {self.schema_version!r} is not {POLICY_SCHEMA}")
+        if not (isinstance(self.policy_id, str) and self.policy_id):
+            raise ConfigurationError("RankPolicy: policy_id must be a non-empty string")
         if not isinstance(self.model, ModelIdentity):
-            raise ConfigurationError("rank policy requires a ModelIdentity")
-        if len(self.geometry) != 3 or any(int(g) < 1 for g in self.geometry):
-            raise ConfigurationError("geometry must be frames, height, width")
-        object.__setattr__(self, "geometry", tuple(int(g) for g in self.geometry))
-        energy = _finite(self.energy_target, "energy_target")
-        if not 0 < energy <= 1:
-            raise ConfigurationError("energy_target must lie in (0, 1]")
+            reject(f"model is {type(self.model).__name__}, not ModelIdentity")
+        grid = tuple(int(g) for g in self.geometry)
+        if len(grid) != 3 or min(grid) < 1:
+            reject(f"geometry {self.geometry!r} is not a positive (frames, height, width)")
+        object.__setattr__(self, "geometry", grid)
+        if not 0 < _finite(self.energy_target, "energy_target") <= 1:
+            reject(f"energy_target {self.energy_target} is outside (0, 1]")
         if self.energy_targets is not None:
             if set(self.energy_targets) != {"K", "V"}:
-                raise ConfigurationError("energy_targets must cover exactly K and V")
+                reject(f"energy_targets names {sorted(self.energy_targets)}; it needs K and V")
             object.__setattr__(self, "energy_targets", MappingProxyType(
-                {k: _finite(v, "target energy") for k, v in self.energy_targets.items()}))
+                {target: _finite(value, f"energy_targets[{target}]") for target, value in self.energy_targets.items()}))
         if self.codec.kind == "raw":
-            raise ConfigurationError("adaptive ranks require a lossy codec, never a RAW fallback")
+            reject("the codec is raw; adaptive ranks need svd or svd_hevc")
         templates = _keyed(self.template_ranks, "template_ranks")
-        allowed = _keyed(self.allowed_ranks, "allowed_ranks")
-        if set(templates) != set(allowed) or not templates:
-            raise ConfigurationError("template and allowed ranks must cover the same matrices")
+        allowed = {key: tuple(int(r) for r in ranks) for key, ranks in _keyed(self.allowed_ranks, "allowed_ranks").items()}
+        if not templates or set(templates) != set(allowed):
+            reject("template_ranks and allowed_ranks must name the same non-empty set of matrices")
         for key, ranks in allowed.items():
-            ranks = tuple(int(r) for r in ranks)
-            limit = min(self.tokens, self.model.channels_for(key))
-            if not ranks or any(b <= a for a, b in zip(ranks, ranks[1:])) or ranks[0] < 1 or ranks[-1] > limit:
-                raise ConfigurationError("allowed ranks must increase strictly within the matrix dimensions")
+            ceiling = min(self.tokens, self.model.channels_for(key))
+            increasing = all(lo < hi for lo, hi in zip(ranks, ranks[1:]))
+            if not (ranks and increasing and 1 <= ranks[0] and ranks[-1] <= ceiling):
+                reject(f"allowed ranks {ranks} of {key} must increase strictly inside [1, {ceiling}]")
         object.__setattr__(self, "template_ranks", templates)
-        object.__setattr__(self, "allowed_ranks", MappingProxyType({k: tuple(int(r) for r in v)
-                                                                   for k, v in allowed.items()}))
+        object.__setattr__(self, "allowed_ranks", MappingProxyType(allowed))
         anchors = tuple(self.anchors)
-        if any(a not in templates for a in anchors) or len(set(anchors)) != len(anchors):
-            raise ConfigurationError("anchors must be unique policy keys")
+        if len(set(anchors)) != len(anchors) or not set(anchors) <= set(templates):
+            reject(f"anchors {anchors} must be distinct matrices of the policy")
         object.__setattr__(self, "anchors", anchors)
         if self.anchor_mode not in ANCHOR_MODES:
-            raise ConfigurationError(f"anchor_mode must be one of {ANCHOR_MODES}")
-        if self.anchor_mode == "none" and anchors:
-            raise ConfigurationError("no-anchor mode cannot declare anchors")
+            reject(f"anchor_mode {self.anchor_mode!r} is not one of {ANCHOR_MODES}")
+        if anchors and self.anchor_mode == "none":
+            reject("anchor_mode 'none' declares anchors")
         if self.solver not in SOLVERS:
-            raise ConfigurationError("solver must be qr_q2 or exact_oracle")
+            reject(f"solver {self.solver!r} is not one of {SOLVERS}")
         if not 1 <= self.history_min <= self.history_max:
-            raise ConfigurationError("history support interval is reversed")
-        if self.fit_growth <= 1.0 or self.prediction_margin <= 0:
-            raise ConfigurationError("fit_growth must exceed one and prediction_margin be positive")
-        if max(self.source_bytes_for(k) for k in templates) > self.source_limit_bytes:
-            raise CapacityError("policy matrix exceeds its source allowance")
+            reject(f"history window [{self.history_min}, {self.history_max}] is empty or starts below 1")
+        if not (self.fit_growth > 1.0 and self.prediction_margin > 0):
+            reject(f"fit_growth {self.fit_growth} must be > 1 and prediction_margin {self.prediction_margin} > 0")
+        largest = max(self.source_bytes_for(key) for key in templates)
+        if largest > self.source_limit_bytes:
+            raise CapacityError(f"RankPolicy {self.policy_id!r}: a {largest}-byte source matrix exceeds "
+                                f"source_limit_bytes={self.source_limit_bytes}")
 
     @property
     def keys(self) -> tuple[MatrixKey, ...]:
@@ -206,7 +213,7 @@ class RankPolicy:
     @classmethod
     def from_dict(cls, data: Mapping[str, Any]) -> "RankPolicy":
         if data.get("schema") != POLICY_SCHEMA:
-            raise ConfigurationError("not a rank policy record")
+            raise ConfigurationError(f"record schema {data.get('schema')!r} is not {POLICY_SCHEMA}")
         return cls(data["policy_id"], ModelIdentity.from_dict(data["model"]), tuple(data["geometry"]),
                    data["energy_target"], {_key(k): v for k, v in data["template_ranks"].items()},
                    {_key(k): tuple(v) for k, v in data["allowed_ranks"].items()}, CodecSpec.from_dict(data["codec"]),
@@ -242,13 +249,15 @@ def predict_rank(policy: RankPolicy, key: MatrixKey, *, chunk_ordinal: int, curr
     measured/template ratios (current anchors where the mode allows them -- ``staged`` any, ``causal`` lower
     layers only -- else the previous chunk's), times ``prediction_margin`` plus ``additive_margin``."""
     if key not in policy.template_ranks:
-        raise ConfigurationError("prediction key is outside the policy")
-    if not policy.history_min <= chunk_ordinal <= policy.history_max:
-        raise StateError("prediction is outside the policy's history support")
-    if set(previous_anchors) != set(previous_anchor_chunks):
-        raise ConfigurationError("previous anchors need their source chunks")
-    if any(chunk >= chunk_ordinal for chunk in previous_anchor_chunks.values()):
-        raise ConfigurationError("previous anchors cannot come from the current or a future chunk")
+        raise ConfigurationError(f"{key} has no template rank in policy {policy.policy_id!r}")
+    if chunk_ordinal < policy.history_min or chunk_ordinal > policy.history_max:
+        raise StateError(f"chunk {chunk_ordinal} lies outside the policy's history window "
+                         f"[{policy.history_min}, {policy.history_max}]")
+    if previous_anchors.keys() != previous_anchor_chunks.keys():
+        raise ConfigurationError("every previous anchor value needs the chunk it was measured on, and only those")
+    late = [chunk for chunk in previous_anchor_chunks.values() if chunk >= chunk_ordinal]
+    if late:
+        raise ConfigurationError(f"previous anchors measured on chunk {late[0]} are not before chunk {chunk_ordinal}")
     regime = "startup" if chunk_ordinal == 1 else "later"
     profile = policy.predictor_profiles.get(f"{regime}:{key.target}")
     if profile is not None and profile.uniform_rank is not None:
@@ -294,18 +303,19 @@ class RankState:
 
     def __post_init__(self) -> None:
         if self.schema_version != STATE_SCHEMA:
-            raise ConfigurationError("unsupported rank state schema")
+            raise ConfigurationError(f"RankState schema {self.schema_version!r} is not {STATE_SCHEMA}")
         for name in ("anchor_ranks", "anchor_chunks", "selected_ranks"):
             object.__setattr__(self, name, _keyed(getattr(self, name), name))
-        if set(self.anchor_ranks) != set(self.anchor_chunks):
-            raise ConfigurationError("anchor values and their chunks differ")
-        if any(c > self.completed_chunks or c < 1 for c in self.anchor_chunks.values()):
-            raise ConfigurationError("a saved anchor cannot come from the future")
-        if self.completed_chunks == 0:
-            if self.last_chunk_id is not None or self.parent_head is not None or self.selected_ranks:
-                raise ConfigurationError("an empty rank state contains committed history")
-        elif self.last_chunk_id is None or not self.selected_ranks or self.token_end < 1:
-            raise ConfigurationError("a committed rank state is incomplete")
+        if self.anchor_ranks.keys() != self.anchor_chunks.keys():
+            raise ConfigurationError("RankState: anchor_ranks and anchor_chunks name different matrices")
+        if not all(1 <= chunk <= self.completed_chunks for chunk in self.anchor_chunks.values()):
+            raise ConfigurationError(f"RankState: anchor chunks must lie in [1, {self.completed_chunks}]")
+        history = (self.last_chunk_id, self.parent_head, dict(self.selected_ranks))
+        if self.completed_chunks == 0 and history != (None, None, {}):
+            raise ConfigurationError("RankState: zero completed chunks but a last chunk, parent head or ranks")
+        if self.completed_chunks and (self.last_chunk_id is None or not self.selected_ranks or self.token_end < 1):
+            raise ConfigurationError("RankState: a state after committed chunks needs last_chunk_id, selected ranks "
+                                     "and token_end")
 
     def to_dict(self) -> dict[str, Any]:
         return {"schema": self.schema_version, "policy_hash": self.policy_hash, "last_chunk_id": self.last_chunk_id,
@@ -318,7 +328,7 @@ class RankState:
     @classmethod
     def from_dict(cls, data: Mapping[str, Any]) -> "RankState":
         if data.get("schema") != STATE_SCHEMA:
-            raise ConfigurationError("not a rank state record")
+            raise ConfigurationError(f"record schema {data.get('schema')!r} is not {STATE_SCHEMA}")
         return cls(data["policy_hash"], data["last_chunk_id"], data["parent_head"], data["token_end"],
                    data["completed_chunks"], {_key(k): v for k, v in data["anchor_ranks"].items()},
                    {_key(k): v for k, v in data["anchor_chunks"].items()},
@@ -355,10 +365,12 @@ class RankDecision:
     schema_version: str = DECISION_SCHEMA
 
     def __post_init__(self) -> None:
-        if self.status not in ("accepted", "abstained"):
-            raise ConfigurationError("decision status is accepted or abstained")
-        if self.status == "accepted" and (self.rank is None or not self.guard_passed):
-            raise ConfigurationError("an accepted decision carries a guarded rank")
+        if self.status == "abstained":
+            return
+        if self.status != "accepted":
+            raise ConfigurationError(f"RankDecision status {self.status!r}: expected accepted or abstained")
+        if self.rank is None or not self.guard_passed:
+            raise ConfigurationError(f"accepted RankDecision of {self.context.key} lacks a rank that passed its guard")
 
     @property
     def key(self) -> MatrixKey:
@@ -391,7 +403,7 @@ class RankAbstention(StateError):
     """A matrix exhausted its guard attempts; the chunk cannot be prepared under the policy."""
 
     def __init__(self, decision: RankDecision):
-        super().__init__(f"rank abstention for {decision.key}: {decision.reason}")
+        super().__init__(f"{decision.key} abstained ({decision.reason}) after {len(decision.attempts)} fit/guard steps")
         self.decision = decision
 
 
@@ -402,18 +414,20 @@ class RankPreparation:
     def __init__(self, policy: RankPolicy, prior_state: RankState | None = None, *, chunk_id: str,
                  parent_head: str | None, token_start: int, device: Any = None):
         if not isinstance(policy, RankPolicy):
-            raise ConfigurationError("preparation requires a RankPolicy")
-        prior = RankState(policy.fingerprint) if prior_state is None else prior_state
-        if not isinstance(prior, RankState) or prior.policy_hash != policy.fingerprint:
-            raise ConfigurationError("the prior state belongs to another policy")
-        if prior.completed_chunks:
-            if parent_head is None or token_start != prior.token_end or chunk_id == prior.last_chunk_id:
-                raise ConfigurationError("the prior rank state does not match the requested history boundary")
-        elif parent_head is not None:
-            raise ConfigurationError("adaptive history cannot start on an unbound existing head")
+            raise ConfigurationError(f"RankPreparation needs a RankPolicy, got {type(policy).__name__}")
+        prior = prior_state if prior_state is not None else RankState(policy.fingerprint)
+        if not (isinstance(prior, RankState) and prior.policy_hash == policy.fingerprint):
+            raise ConfigurationError(f"prior state was made under another policy than {policy.policy_id!r}")
+        if not prior.completed_chunks and parent_head is not None:
+            raise ConfigurationError(f"a first adaptive chunk cannot extend head {parent_head}, which has no rank state")
+        continues = parent_head is not None and token_start == prior.token_end and chunk_id != prior.last_chunk_id
+        if prior.completed_chunks and not continues:
+            raise ConfigurationError(f"chunk {chunk_id!r} at token {token_start} does not continue the prior state "
+                                     f"(ends at {prior.token_end} after {prior.last_chunk_id!r})")
         ordinal = prior.completed_chunks + 1
-        if not policy.history_min <= ordinal <= policy.history_max:
-            raise StateError("the clean chunk is outside the policy's history support")
+        if ordinal < policy.history_min or ordinal > policy.history_max:
+            raise StateError(f"chunk {ordinal} lies outside the policy's history window "
+                             f"[{policy.history_min}, {policy.history_max}]")
         self.policy, self.prior_state = policy, prior
         self.chunk_id, self.parent_head, self.token_start = chunk_id, parent_head, int(token_start)
         self.ordinal = ordinal
@@ -440,15 +454,18 @@ class RankPreparation:
         return MappingProxyType(dict(self._metrics))
 
     def _check_context(self, context: TensorContext) -> None:
-        policy = self.policy
-        if context.model != policy.model or context.key not in policy.template_ranks:
-            raise ConfigurationError("the matrix is outside the policy")
+        policy, key = self.policy, context.key
+        problems = []
+        if context.model != policy.model or key not in policy.template_ranks:
+            problems.append("is not a matrix of the policy")
         if (context.frames, context.height, context.width) != policy.geometry:
-            raise ConfigurationError("the matrix geometry differs from the policy")
+            problems.append(f"has grid {(context.frames, context.height, context.width)}, not {policy.geometry}")
         if context.token_start != self.token_start:
-            raise ConfigurationError("the matrix does not start at the chunk's first token")
-        if context.key in self._decisions:
-            raise StateError("the matrix was prepared already")
+            problems.append(f"starts at token {context.token_start}, not {self.token_start}")
+        if problems:
+            raise ConfigurationError(f"{key} " + "; ".join(problems))
+        if key in self._decisions:
+            raise StateError(f"{key} was prepared already in this chunk")
 
     def prediction(self, key: MatrixKey) -> RankPrediction:
         return predict_rank(self.policy, key, chunk_ordinal=self.ordinal, current_anchors=self._anchors,
@@ -458,7 +475,7 @@ class RankPreparation:
     def prepare_matrix(self, tensor: torch.Tensor, context: TensorContext) -> PreparedRankMatrix:
         """Predict, fit and guard one matrix; raises :class:`RankAbstention` when no allowed rank passes."""
         if self._closed:
-            raise StateError("the preparation is closed")
+            raise StateError(f"preparation of chunk {self.chunk_id!r} was closed")
         self._check_context(context)
         policy, key = self.policy, context.key
         x = validate_matrix(tensor, context)
@@ -527,11 +544,12 @@ class RankPreparation:
 
     def next_state(self) -> RankState:
         """The scalar state after this chunk (every matrix accepted)."""
-        missing = set(self.policy.keys) - set(self._decisions)
-        if missing:
-            raise StateError(f"{len(missing)} policy matrices are not prepared")
-        if any(d.status != "accepted" for d in self._decisions.values()):
-            raise StateError("an abstained chunk has no next state")
+        unprepared = [key for key in self.policy.keys if key not in self._decisions]
+        if unprepared:
+            raise StateError(f"{len(unprepared)} matrices (first {unprepared[0]}) are not prepared yet")
+        abstained = [key for key, d in self._decisions.items() if d.status != "accepted"]
+        if abstained:
+            raise StateError(f"{abstained[0]} abstained; the chunk has no next rank state")
         anchors = dict(self.prior_state.anchor_ranks)
         chunks = dict(self.prior_state.anchor_chunks)
         for key, value in self._anchors.items():
