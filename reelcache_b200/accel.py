@@ -38,20 +38,23 @@ SPAN_MAX_TERMS = 12
 
 
 def parse_fitter_fp64(value: Any) -> frozenset:
-    """``"on"`` (FP64 passes), ``"off"`` (:data:`OFF_PASSES` in FP32) or ``"fp32:<pass>[+<pass>...]"``."""
-    if value == "on":
-        return frozenset()
-    if value == "off":
-        return frozenset(OFF_PASSES)
-    if isinstance(value, str) and value.startswith("fp32:"):
-        names = [name for name in value[5:].split("+") if name]
-        if names and all(name in FP32_PASSES for name in names):
-            return frozenset(names)
-    raise ConfigurationError(f"fitter_fp64 must be 'on', 'off' or 'fp32:<pass>[+<pass>...]' from {FP32_PASSES}")
+    """The FP32-replaced passes named by the ``fitter_fp64`` setting: ``"on"`` keeps every measurement pass in
+    FP64, ``"off"`` moves :data:`OFF_PASSES` to FP32, ``"fp32:a+b"`` moves exactly the listed passes."""
+    presets = {"on": frozenset(), "off": frozenset(OFF_PASSES)}
+    if value in presets:
+        return presets[value]
+    listed = value.removeprefix("fp32:").split("+") if isinstance(value, str) and value.startswith("fp32:") else []
+    listed = [name for name in listed if name]
+    if listed and set(listed) <= set(FP32_PASSES):
+        return frozenset(listed)
+    raise ConfigurationError(f"fitter_fp64={value!r}: use 'on', 'off' or 'fp32:' followed by '+'-joined names "
+                             f"from {FP32_PASSES}")
 
 
 @dataclasses.dataclass(frozen=True)
 class FitterAccel:
+    """Opt-in fitter levers; the all-default instance means "none" (:meth:`from_config` returns None)."""
+
     green_sms: int | None = None
     green_workqueue: str | None = None
     cuda_graphs: bool = False
@@ -61,20 +64,24 @@ class FitterAccel:
     fp32_passes: frozenset = frozenset()
 
     def __post_init__(self) -> None:
-        if self.green_sms is not None and (type(self.green_sms) is not int or self.green_sms < 1):
-            raise ConfigurationError("fitter_green_context_sms must be None or a positive SM count")
-        if self.green_workqueue is not None and self.green_workqueue not in GREEN_WORKQUEUES:
-            raise ConfigurationError(f"fitter_green_workqueue must be None or one of {GREEN_WORKQUEUES}")
-        if self.green_workqueue is not None and self.green_sms is None:
-            raise ConfigurationError("fitter_green_workqueue needs fitter_green_context_sms")
-        for name in ("cuda_graphs", "fused_fingerprints", "finalize_on_fit_device"):
-            if type(getattr(self, name)) is not bool:
-                raise ConfigurationError(f"{name} must be a bool")
-        if self.cuda_graphs:
-            raise ConfigurationError("CUDA-graph replay of the fitter's FP64 passes is not provided")
+        problems = []
+        if not (self.green_sms is None or (type(self.green_sms) is int and self.green_sms > 0)):
+            problems.append(f"green_sms={self.green_sms!r} is not None or an SM count >= 1")
+        if self.green_workqueue is not None:
+            if self.green_workqueue not in GREEN_WORKQUEUES:
+                problems.append(f"green_workqueue={self.green_workqueue!r} is not one of {GREEN_WORKQUEUES}")
+            if self.green_sms is None:
+                problems.append("green_workqueue applies to a green context: set green_sms too")
+        flags = ("cuda_graphs", "fused_fingerprints", "finalize_on_fit_device")
+        problems += [f"{flag}={getattr(self, flag)!r} is not a bool" for flag in flags
+                     if type(getattr(self, flag)) is not bool]
+        if self.cuda_graphs is True:
+            problems.append("cuda_graphs: graph replay of the FP64 passes is not offered (it slows them down)")
         passes = frozenset(self.fp32_passes)
-        if not passes <= set(FP32_PASSES):
-            raise ConfigurationError(f"unknown FP32 passes {sorted(passes - set(FP32_PASSES))}")
+        if passes - set(FP32_PASSES):
+            problems.append(f"fp32_passes names unknown passes {sorted(passes - set(FP32_PASSES))}")
+        if problems:
+            raise ConfigurationError("FitterAccel: " + "; ".join(problems))
         object.__setattr__(self, "fp32_passes", passes)
 
     @property
@@ -82,45 +89,61 @@ class FitterAccel:
         return self == FitterAccel()
 
     def to_dict(self) -> dict[str, Any]:
-        data = dataclasses.asdict(self)
-        data["fp32_passes"] = sorted(self.fp32_passes)
-        return data
+        return {**dataclasses.asdict(self), "fp32_passes": sorted(self.fp32_passes)}
 
     @classmethod
     def from_config(cls, config: Any) -> "FitterAccel | None":
-        accel = cls(green_sms=getattr(config, "fitter_green_context_sms", None),
-                    green_workqueue=getattr(config, "fitter_green_workqueue", None),
-                    fused_fingerprints=getattr(config, "fused_fingerprints", False),
-                    finalize_on_fit_device=getattr(config, "finalize_on_fit_device", False),
-                    fp32_passes=parse_fitter_fp64(getattr(config, "fitter_fp64", "on")))
+        """The levers a runtime config selects (its ``fitter_*`` / fingerprint / finalize fields), or None."""
+        read = lambda name, default: getattr(config, name, default)  # noqa: E731
+        accel = cls(green_sms=read("fitter_green_context_sms", None),
+                    green_workqueue=read("fitter_green_workqueue", None),
+                    fused_fingerprints=read("fused_fingerprints", False),
+                    finalize_on_fit_device=read("finalize_on_fit_device", False),
+                    fp32_passes=parse_fitter_fp64(read("fitter_fp64", "on")))
         return None if accel.default else accel
 
 
+class _Counters:
+    """Thread-safe event counts of the accelerated paths (exposed as :func:`stats`)."""
+
+    NAMES = ("energy_fused", "residual_fused_tiles", "span_neumann", "span_fallbacks", "span_terms",
+             "fingerprints_fused", "dot2_gemms")
+
+    def __init__(self):
+        self._lock = threading.Lock()
+        self.values = dict.fromkeys(self.NAMES, 0)
+
+    def add(self, name: str, amount: int = 1) -> None:
+        with self._lock:
+            self.values[name] = self.values.get(name, 0) + amount
+
+    def snapshot(self) -> dict[str, int]:
+        with self._lock:
+            return dict(self.values)
+
+
 _LOCAL = threading.local()
-_STATS_LOCK = threading.Lock()
-STATS: dict[str, int] = {"energy_fused": 0, "residual_fused_tiles": 0, "span_neumann": 0, "span_fallbacks": 0,
-                         "span_terms": 0, "fingerprints_fused": 0, "dot2_gemms": 0}
+_COUNTERS = _Counters()
+STATS = _COUNTERS.values
 
 
 def _count(name: str, value: int = 1) -> None:
-    with _STATS_LOCK:
-        STATS[name] = STATS.get(name, 0) + value
+    _COUNTERS.add(name, value)
 
 
 def stats() -> dict[str, int]:
-    with _STATS_LOCK:
-        return dict(STATS)
+    return _COUNTERS.snapshot()
 
 
 @contextlib.contextmanager
 def scope(accel: FitterAccel | None, *, fit_device: Any = None):
-    previous = (getattr(_LOCAL, "accel", None), getattr(_LOCAL, "fit_device", None))
-    _LOCAL.accel = accel
-    _LOCAL.fit_device = None if fit_device is None else torch.device(fit_device)
+    """Apply ``accel`` (and the fit device) to the archival routines this thread runs inside the block."""
+    saved = getattr(_LOCAL, "accel", None), getattr(_LOCAL, "fit_device", None)
+    _LOCAL.accel, _LOCAL.fit_device = accel, (torch.device(fit_device) if fit_device is not None else None)
     try:
         yield
     finally:
-        _LOCAL.accel, _LOCAL.fit_device = previous
+        _LOCAL.accel, _LOCAL.fit_device = saved
 
 
 def current() -> FitterAccel | None:
@@ -234,31 +257,34 @@ _GREEN: dict = {}
 _GREEN_LOCK = threading.Lock()
 
 
+def _make_green_stream(index: int, sms: int, workqueue: str | None):
+    try:
+        from torch.cuda import green_contexts
+    except ImportError as exc:
+        raise ConfigurationError(f"green contexts need a newer torch than {torch.__version__}") from exc
+    options: dict[str, Any] = {"num_sms": sms, "device_id": index}
+    if workqueue is not None:
+        options["workqueue_scope"] = workqueue
+    try:
+        with torch.cuda.device(index):
+            context = green_contexts.GreenContext.create(**options)
+            return context, context.Stream()
+    except Exception as exc:  # noqa: BLE001 -- the driver's refusal becomes a configuration error
+        raise ConfigurationError(f"cuda:{index} refused a green context of {sms} SMs: {exc}") from exc
+
+
 def green_stream(device: Any, sms: int, workqueue: str | None = None):
-    """The stream of this process's green context of ``sms`` SMs on ``device`` (created once, kept)."""
+    """A stream of a green context limited to ``sms`` SMs on ``device``; one context per (device, SMs,
+    work queue), created on first use and kept for the life of the process."""
     device = torch.device(device)
     if device.type != "cuda":
-        raise ConfigurationError("a green context needs a CUDA device")
-    index = device.index if device.index is not None else torch.cuda.current_device()
+        raise ConfigurationError(f"green contexts exist on CUDA devices, not {device}")
+    index = torch.cuda.current_device() if device.index is None else device.index
     key = (index, int(sms), workqueue)
     with _GREEN_LOCK:
-        entry = _GREEN.get(key)
-        if entry is None:
-            try:
-                from torch.cuda import green_contexts
-            except ImportError as exc:
-                raise ConfigurationError(f"torch {torch.__version__} has no green contexts") from exc
-            kwargs: dict[str, Any] = {"num_sms": int(sms), "device_id": index}
-            if workqueue is not None:
-                kwargs["workqueue_scope"] = workqueue
-            try:
-                with torch.cuda.device(index):
-                    context = green_contexts.GreenContext.create(**kwargs)
-                    stream = context.Stream()
-            except Exception as exc:  # noqa: BLE001 - surfaced as a configuration error
-                raise ConfigurationError(f"a green context of {sms} SMs is unsupported here: {exc}") from exc
-            entry = _GREEN[key] = (context, stream)
-    return entry[1]
+        if key not in _GREEN:
+            _GREEN[key] = _make_green_stream(index, int(sms), workqueue)
+        return _GREEN[key][1]
 
 
 __all__ = ["FP32_PASSES", "FitterAccel", "OFF_PASSES", "current", "dot2_gemm", "energy_fp32",
