@@ -25,7 +25,7 @@ T = TypeVar("T")
 
 def _check_timeout(value):
     if value is not None and (isinstance(value, bool) or not isinstance(value, (int, float)) or value < 0):
-        raise ConfigurationError("timeout must be a nonnegative number or None")
+        raise ConfigurationError(f"timeout={value!r}: expected None or a number of seconds >= 0")
 
 
 @dataclass
@@ -91,9 +91,11 @@ class BoundedExecutor:
 
     def __init__(self, *, max_workers: int = 1, max_pending: int = 2, max_staging_bytes: int = 1 << 30,
                  history_size: int = 128) -> None:
-        for value in (max_workers, max_pending, max_staging_bytes, history_size):
-            if type(value) is not int or value <= 0:
-                raise ConfigurationError("executor capacities must be positive integers")
+        sizes = {"max_workers": max_workers, "max_pending": max_pending, "max_staging_bytes": max_staging_bytes,
+                 "history_size": history_size}
+        bad = {name: value for name, value in sizes.items() if not (type(value) is int and value > 0)}
+        if bad:
+            raise ConfigurationError(f"BoundedExecutor sizes must be ints >= 1: {bad}")
         self.max_workers = max_workers
         self.max_pending = max_pending
         self.max_staging_bytes = max_staging_bytes
@@ -112,29 +114,30 @@ class BoundedExecutor:
     def submit(self, function: Callable[..., T], *args, staging_bytes: int = 0, label: str | None = None,
                block: bool = False, timeout: float | None = None, **kwargs) -> Job[T]:
         if not callable(function):
-            raise ConfigurationError("submitted function must be callable")
+            raise ConfigurationError(f"submit() needs a callable, got {type(function).__name__}")
         if type(block) is not bool or (label is not None and (not isinstance(label, str) or not label.strip())):
-            raise ConfigurationError("block must be boolean and label a nonempty string")
+            raise ConfigurationError(f"block={block!r} must be True/False and label={label!r} a non-blank string or None")
         if type(staging_bytes) is not int or staging_bytes < 0:
-            raise ConfigurationError("staging_bytes must be a nonnegative integer")
+            raise ConfigurationError(f"staging_bytes={staging_bytes!r}: expected an int >= 0")
         _check_timeout(timeout)
         if timeout is not None and not block:
-            raise ConfigurationError("an admission timeout requires block=True")
+            raise ConfigurationError("timeout bounds the wait for admission, so it needs block=True")
         if staging_bytes > self.max_staging_bytes:
-            raise CapacityError("one job exceeds the entire staging budget")
+            raise CapacityError(f"a job staging {staging_bytes} bytes can never fit max_staging_bytes={self.max_staging_bytes}")
         deadline = None if timeout is None else time.monotonic() + timeout
         with self._cv:
             while True:
                 if self._closed:
-                    raise StateError("executor is closed")
+                    raise StateError("BoundedExecutor was closed")
                 self._raise_unread()
                 if len(self._pending) < self.max_pending and self._staging + staging_bytes <= self.max_staging_bytes:
                     break
                 if not block:
-                    raise CapacityError("executor job or staging capacity is exhausted")
+                    raise CapacityError(f"executor full: {len(self._pending)}/{self.max_pending} jobs, "
+                                        f"{self._staging}/{self.max_staging_bytes} staging bytes")
                 left = None if deadline is None else deadline - time.monotonic()
                 if left is not None and left <= 0:
-                    raise CapacityError("timed out waiting for executor admission")
+                    raise CapacityError(f"no executor capacity freed up within {timeout} s")
                 self._cv.wait(left)
             state = _JobState(self._next, label or getattr(function, "__name__", type(function).__name__),
                               staging_bytes, time.monotonic(), function, args, kwargs,

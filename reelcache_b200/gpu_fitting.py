@@ -106,12 +106,15 @@ class BoundedEigh:
     def __init__(self, label: str, solver: Callable, *, memory_fraction: float = EIGH_MEMORY_FRACTION,
                  workspace: Callable | None = None, total_memory: int | None = None,
                  sub_batch_size: Callable | None = None):
+        problems = []
         if not 0 < memory_fraction <= 1:
-            raise ConfigurationError("eigh memory fraction must be in (0, 1]")
-        if total_memory is not None and (type(total_memory) is not int or total_memory <= 0):
-            raise ConfigurationError("total_memory must be a positive byte count")
-        if sub_batch_size is not None and not callable(sub_batch_size):
-            raise ConfigurationError("sub_batch_size maps n to a fixed sub-batch size or None")
+            problems.append(f"memory_fraction={memory_fraction!r} is outside (0, 1]")
+        if not (total_memory is None or (type(total_memory) is int and total_memory > 0)):
+            problems.append(f"total_memory={total_memory!r} is not None or a byte count >= 1")
+        if not (sub_batch_size is None or callable(sub_batch_size)):
+            problems.append("sub_batch_size must be None or a callable n -> sub-batch size")
+        if problems:
+            raise ConfigurationError(f"BoundedEigh {label!r}: " + "; ".join(problems))
         self.label, self.solver, self.memory_fraction = label, solver, memory_fraction
         self._workspace = workspace or (lambda batch, n, device: eigh_workspace_bytes(batch, n, label))
         self.total_memory = total_memory
@@ -181,9 +184,10 @@ def gram_bases(sources, ranks, *, eigh=None):
     one batched eigensolve of their FP32-accurate Grams."""
     from .exact_blas import gram
     if not sources or len(sources) != len(ranks):
-        raise ConfigurationError("batched Gram fitting needs one rank per source")
-    if len({int(x.shape[1]) for x in sources}) != 1:
-        raise ConfigurationError("one Gram batch shares the channel count")
+        raise ConfigurationError(f"{len(sources)} sources and {len(ranks)} ranks: give one rank per source")
+    widths = sorted({int(x.shape[1]) for x in sources})
+    if len(widths) != 1:
+        raise ConfigurationError(f"one batched Gram solve needs one channel count, got {widths}")
     grams = torch.stack([gram(x) for x in sources])
     _, rows = (eigh or rows_eigh)(grams)
     return [rows[index, -rank:].flip(0) for index, rank in enumerate(ranks)]
@@ -198,20 +202,23 @@ class GPUFitter:
     def __init__(self, *, gpu_id: int, gpu_uuid: str, method: str = "randomized",
                  max_workspace_bytes: int = 2 * 1024 ** 3, seed: int = 0, power_iterations: int = 2,
                  batch_size: int = 60, side_stream: bool = False, shared: bool = False, eigh_solver: str = "auto"):
-        if type(gpu_id) is not int or gpu_id < 0 or not isinstance(gpu_uuid, str) or not gpu_uuid.startswith("GPU-"):
-            raise ConfigurationError("GPU fitting requires an explicit device index and UUID")
-        if method not in GPU_FIT_METHODS:
-            raise ConfigurationError(f"GPU fitting method must be one of {GPU_FIT_METHODS}")
-        if type(max_workspace_bytes) is not int or max_workspace_bytes <= 0:
-            raise ConfigurationError("GPU fitting workspace budget must be positive")
-        if type(seed) is not int or seed < 0 or type(power_iterations) is not int or not 0 <= power_iterations <= 8:
-            raise ConfigurationError("invalid GPU fitting seed or iteration count")
-        if type(batch_size) is not int or not 1 <= batch_size <= 256:
-            raise ConfigurationError("GPU fitting batch size must be an integer in [1, 256]")
-        if type(side_stream) is not bool or type(shared) is not bool:
-            raise ConfigurationError("side_stream and shared are booleans")
-        if eigh_solver not in EIGH_SOLVERS:
-            raise ConfigurationError(f"eigh_solver must be one of {EIGH_SOLVERS}")
+        def whole(value, low, high=None):
+            return type(value) is int and value >= low and (high is None or value <= high)
+
+        checks = (
+            (whole(gpu_id, 0) and isinstance(gpu_uuid, str) and gpu_uuid.startswith("GPU-"),
+             f"device index {gpu_id!r} and UUID {gpu_uuid!r} (a 'GPU-...' string) are both required"),
+            (method in GPU_FIT_METHODS, f"method {method!r} is not one of {GPU_FIT_METHODS}"),
+            (whole(max_workspace_bytes, 1), f"max_workspace_bytes={max_workspace_bytes!r} is not a byte count >= 1"),
+            (whole(seed, 0), f"seed={seed!r} is not an int >= 0"),
+            (whole(power_iterations, 0, 8), f"power_iterations={power_iterations!r} is not an int in [0, 8]"),
+            (whole(batch_size, 1, 256), f"batch_size={batch_size!r} is not an int in [1, 256]"),
+            (type(side_stream) is bool and type(shared) is bool, "side_stream and shared take True or False"),
+            (eigh_solver in EIGH_SOLVERS, f"eigh_solver {eigh_solver!r} is not one of {EIGH_SOLVERS}"),
+        )
+        problems = [message for ok, message in checks if not ok]
+        if problems:
+            raise ConfigurationError("GPUFitter: " + "; ".join(problems))
         self.gpu_id, self.gpu_uuid, self.method = gpu_id, gpu_uuid, method
         self.max_workspace_bytes, self.seed, self.power_iterations = max_workspace_bytes, seed, power_iterations
         self.batch_size, self.eigh_solver = batch_size, eigh_solver

@@ -37,7 +37,7 @@ class HistoryLease:
     @property
     def tensor(self) -> torch.Tensor:
         if not self._active:
-            raise StateError("history tensor is available only while its lease is active")
+            raise StateError("this history lease was released; its tensor is gone")
         return self._tensor
 
     def release(self) -> None:
@@ -66,7 +66,7 @@ class HistoryLease:
 class ResidencyPool:
     def __init__(self, max_bytes: int) -> None:
         if type(max_bytes) is not int or max_bytes < 0:
-            raise ConfigurationError("max resident bytes must be nonnegative")
+            raise ConfigurationError(f"ResidencyPool budget {max_bytes!r}: expected an int >= 0")
         self.max_bytes = max_bytes
         self._lock = threading.Lock()
         self._resident = 0
@@ -99,14 +99,14 @@ class ResidencyPool:
     def acquire(self, nbytes: int, loader: Callable[[], torch.Tensor], *, scratch_bytes: int = 0,
                 metadata: dict | None = None) -> HistoryLease:
         if type(nbytes) is not int or nbytes < 0:
-            raise ConfigurationError("lease size must be a nonnegative integer")
+            raise ConfigurationError(f"lease of {nbytes!r} bytes: expected an int >= 0")
         if type(scratch_bytes) is not int or scratch_bytes < 0:
-            raise ConfigurationError("scratch size must be a nonnegative integer")
+            raise ConfigurationError(f"scratch of {scratch_bytes!r} bytes: expected an int >= 0")
         if not callable(loader):
-            raise ConfigurationError("lease loader must be callable")
+            raise ConfigurationError(f"the lease loader is a {type(loader).__name__}, not a callable")
         with self._lock:
             if self._closed:
-                raise StateError("residency pool is closed")
+                raise StateError("the residency pool was closed")
             if self._resident + self._reserved + nbytes + scratch_bytes > self.max_bytes:
                 self._counts["rejected"] += 1
                 raise CapacityError(f"history of {nbytes} bytes (+{scratch_bytes} scratch) exceeds the residency "
@@ -116,9 +116,10 @@ class ResidencyPool:
         try:
             tensor = loader()
             if not isinstance(tensor, torch.Tensor):
-                raise IntegrityError("history decoder did not return a tensor")
+                raise IntegrityError(f"the history loader returned {type(tensor).__name__}, not a tensor")
             if tensor.numel() * tensor.element_size() != nbytes:
-                raise IntegrityError("history decoder returned unaccounted tensor storage")
+                raise IntegrityError(f"the history loader returned {tensor.numel() * tensor.element_size()} bytes; the lease "
+                                     f"reserved {nbytes}")
         except BaseException:
             with self._lock:
                 self._reserved -= nbytes + scratch_bytes
@@ -126,7 +127,7 @@ class ResidencyPool:
         with self._lock:
             self._reserved -= nbytes + scratch_bytes
             if self._closed:
-                raise StateError("residency pool closed during restoration")
+                raise StateError("the residency pool was closed while this history was loading")
             self._resident += nbytes
             self._leases += 1
             self._counts["acquired"] += 1
@@ -148,7 +149,7 @@ class ResidencyPool:
 
     def __enter__(self) -> "ResidencyPool":
         if self._closed:
-            raise StateError("residency pool is closed")
+            raise StateError("the residency pool was closed")
         return self
 
     def __exit__(self, *args: Any) -> None:
