@@ -125,6 +125,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// mbar_wait without the back-off sleep: for the single thread of a pipeline role (TMA producer, MMA
+// issuer) whose wake-up latency sits on the critical path and whose polls take issue slots from no one
+// else in its warp. Same bound and status handling.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* status, int code) {
+  uint64_t start = 0;
+#pragma unroll 1
+  for (uint32_t iter = 1;; ++iter) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((iter & 16383u) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (start == 0) {
+        start = now;
+      } else if (now - start > kWaitLimitNs) {
+        record_status(status, code);
+        return false;
+      }
+      if (status_set(status)) return false;
+    }
+  }
+}
+
 // Waits with mbarrier.try_wait, which parks the thread in hardware until the phase completes (or a
 // hardware time window passes) instead of re-issuing probes: the lowest wake-up latency for pipelines
 // with many short waits per tile, without taking issue slots from the warps doing the math. Bounded by
@@ -282,6 +303,112 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
       "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
       "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
+// CTA pairs: a cluster of two CTAs issuing tcgen05.mma.cta_group::2 (M = 256 split 128 / 128 across the
+// pair's TMEM, each CTA holding its own half of A and half of B in shared memory). Only the leader (rank 0)
+// issues MMAs; both CTAs load their halves with TMA (no multicast) and count the bytes on the leader's
+// barrier. Barrier addresses of the other CTA are shared::cluster addresses obtained with mapa.
+// ---------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of every CTA of the cluster (release / acquire at cluster scope).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of this CTA's shared variable `p` as seen in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+
+// Arrive on an mbarrier of any CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t cluster_bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_bar),
+               "r"(bytes)
+               : "memory");
+}
+
+// mbar_wait for a barrier whose arrivals come from other CTAs of the cluster (release.cluster arrivals):
+// the completed phase is observed with cluster-scope acquire. Same bound and status handling as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* status, int code) {
+  uint64_t start = 0;
+#pragma unroll 1
+  for (uint32_t iter = 1;; ++iter) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((iter & 16383u) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (start == 0) {
+        start = now;
+      } else if (now - start > kWaitLimitNs) {
+        record_status(status, code);
+        return false;
+      }
+      if (status_set(status)) return false;
+    }
+  }
+}
+
+// Whole warp, in both CTAs of the pair (same warp index, same `slot` offset).
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A[smem of both] * B[smem of both]^T with M = 256 (leader CTA only).
+__device__ __forceinline__ void mma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the mbarrier at shared::cluster address `cluster_bar` (either CTA of the pair) when every
+// pair MMA this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
+// This CTA's half of a pair tile: a 2-D TMA load into its own shared memory whose transaction bytes are
+// counted on the leader's barrier (`leader_bar`, a shared::cluster address). Same coordinate rule as
+// tma_load_2d.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t leader_bar, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(c0), "r"(c1)
       : "memory");
 }
 
