@@ -67,6 +67,7 @@ def main(argv=None) -> dict:
         runtime = LineageRuntime(store, identity)
         runtime.create_lineage("main")
         method = RankMethodConfig(energy_targets("longcat_720p"), CodecSpec("svd_hevc", 32), solver="topk_rr")
+        # on CUDA the backend restores segments on the fused kernels (restorer="auto")
         backend = ReelCacheConditioningCacheBackend(runtime, "main", method, head_dim=cfg.head_dim, grid=cfg.grid,
                                                     device=device)
         tiers = EpochRawTiers(gpu_raw_budget_bytes=0, host_raw_budget_bytes=int(args.host_gb * (1 << 30)),

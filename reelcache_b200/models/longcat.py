@@ -377,10 +377,11 @@ class ReelCacheConditioningCacheBackend:
     newest segment node of that epoch (this rank's rows only under CP), or returns None."""
 
     def __init__(self, runtime, lineage: str, method, *, head_dim: int, grid: tuple[int, int], device="cpu",
-                 cp_shard: RowShard | None = None, restorer=None):
+                 cp_shard: RowShard | None = None, restorer="auto"):
         """``restorer``: a :class:`~reelcache_b200.archive_restore.LineageRestorer` on ``device``; with it a
         segment restores on the fused sm_100a kernels, each CP rank gathering only its rows of the coefficient
-        tiles (:func:`shard_runs`), instead of decoding every row on the host."""
+        tiles (:func:`shard_runs`), instead of decoding every row on the host. ``"auto"`` (default) creates one
+        on the first restore when ``device`` is a CUDA device; ``None`` keeps the host decode (FP32 reference)."""
         self.restorer = restorer
         self.runtime = runtime
         self.lineage = lineage
@@ -417,6 +418,11 @@ class ReelCacheConditioningCacheBackend:
         if node is None:
             self.stats["missed"] += 1
             return None
+        if self.restorer == "auto":
+            self.restorer = None
+            if self.device.type == "cuda":
+                from ..archive_restore import LineageRestorer
+                self.restorer = LineageRestorer(self.runtime, self.device)
         if self.restorer is not None and self.device.type == "cuda":
             return self._restore_fused(epoch, node)
         ks, vs = [], []

@@ -35,7 +35,7 @@ def test_fused_segment_restore_matches_host_decode(tmp_path, cp):
     for rank in range(cp):
         shard = None if cp == 1 else RowShard(rank, cp, 3, *cfg.grid)
         host = ReelCacheConditioningCacheBackend(runtime, "s", method, head_dim=cfg.head_dim, grid=cfg.grid,
-                                                 device="cuda", cp_shard=shard)
+                                                 device="cuda", cp_shard=shard, restorer=None)
         fused = ReelCacheConditioningCacheBackend(runtime, "s", method, head_dim=cfg.head_dim, grid=cfg.grid,
                                                   device="cuda", cp_shard=shard, restorer=restorer)
         want = host.restore(epoch, node)
