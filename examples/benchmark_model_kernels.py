@@ -26,6 +26,7 @@ def main(argv=None):
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--only", choices=("all", "norms"), default="all",
                     help="norms: only the memory-bound ops (a short run for profiling)")
+    ap.add_argument("--gemm", help="M,N,K: only run gemm.linear on this shape three times (a small case for ncu)")
     ap.add_argument("--out", type=Path)
     args = ap.parse_args(argv)
     root = Path(__file__).resolve().parents[1]
@@ -35,6 +36,15 @@ def main(argv=None):
     from reelcache_b200.ops import _ext, gemm, norms
 
     device = torch.device("cuda", 0)
+    if args.gemm:
+        m, n, k = (int(v) for v in args.gemm.split(","))
+        a = torch.randn(m, k, device=device).bfloat16()
+        w = (torch.randn(n, k, device=device) / k ** 0.5).bfloat16()
+        for _ in range(3):
+            gemm.linear(a, w)
+        torch.cuda.synchronize()
+        _ext.check_status(device)
+        return
     peaks_path = root / "MEASURED_PEAKS.json"
     peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
     hbm, tflops = peaks["hbm_gbs"], peaks["bf16_tflops"]
