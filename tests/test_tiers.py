@@ -2,6 +2,7 @@
 decoded tier behind the packed-decode restorer, archive eviction under a budget, device-pressure trims
 and runtime telemetry."""
 
+import numpy as np
 import pytest
 import torch
 
@@ -9,7 +10,7 @@ from reelcache_b200 import restore_kernels as rk
 from reelcache_b200.decoded_tier import DecodedTier
 from reelcache_b200.decoder_pool import DecoderPool
 from reelcache_b200.device_pressure import DeviceTrimRegistry
-from reelcache_b200.errors import CapacityError, IntegrityError
+from reelcache_b200.errors import CapacityError, ConfigurationError, IntegrityError
 from reelcache_b200.integrations.sglang.archive_eviction import ArchiveEviction
 from reelcache_b200.lineage import LineageRuntime
 from reelcache_b200.packed_decode import PackedRestorer
@@ -204,3 +205,30 @@ def test_raw_tier_machine_budgets_and_host_pool(tmp_path):
     pool.give(a)
     b = pool.take((3 << 20) + 5)
     assert b.data_ptr() == a.data_ptr() and pool.stats["reused"] == 1
+
+
+def test_layer_compute_model_lookup_and_route_record():
+    from reelcache_b200.decoded_tier import LAYER_COMPUTE_MS, layer_compute_model, offer_decoded, open_tiers
+
+    assert layer_compute_model("Wan-LongLive2-1.3B")[3] == "default:longlive2"      # longest contained name wins
+    assert layer_compute_model("longlive1-x")[:3] == LAYER_COMPUTE_MS["longlive1"]
+    assert layer_compute_model("unknown")[3].startswith("default:causvid")
+    assert layer_compute_model("causvid", [1.0, 0.25]) == (1.0, 0.25, None, "configured")
+    with pytest.raises(ConfigurationError):
+        layer_compute_model(None, [1.0])
+    tier = DecodedTier(1 << 20, route="deficit", layer_ms=[1.0, 0.0], decode_gbps=1.0, register=True)
+    try:
+        tiles = [np.full((100, 8), 3, dtype=np.uint8)]
+        assert offer_decoded("digest-a", tiles) == 1 and tier in open_tiers()
+        tier.bind("pack-a", "digest-a")
+        # two packs of 2 MB over 1 layer at 1 GB/s: 4 ms predicted; the target is 0.85 x 1 ms
+        chosen = tier.route([("pack-a", 2_000_000), ("pack-b", 2_000_000)], layers=1)
+        assert chosen == ["pack-a"]
+        record = tier.last_route
+        assert record["hits"] == 1 and record["misses"] == 1 and record["c_model"] == "configured"
+        assert record["predicted_decode_ms_per_layer"] == pytest.approx(4.0)
+        assert record["predicted_decode_ms_per_layer_after"] == pytest.approx(2.0)
+        tier.release(chosen)
+    finally:
+        tier.close()
+    assert tier not in open_tiers()
