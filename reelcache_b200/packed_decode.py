@@ -18,9 +18,36 @@ from typing import Any, Callable
 import numpy as np
 import torch
 
+from . import _hevc
 from . import restore_kernels as rk
-from .errors import IntegrityError
+from .errors import ConfigurationError, IntegrityError
 from .types import MatrixKey, entry_parts
+
+
+@dataclass(frozen=True, eq=False)
+class PreparedTile:
+    """One matrix of a prepared node pack: where its 8-bit coefficients sit in the pack (``offset``, ``nbytes``,
+    ``shape`` = ``[tokens, rank]``), their per-column affine and the basis the record binds (the version ref and
+    rank view; resolved by the restorer's basis cache). ``grid`` and ``token_start`` place it in the history."""
+
+    key: Any
+    layer: int
+    target: str
+    index: int
+    offset: int
+    nbytes: int
+    shape: tuple[int, int]
+    scale: np.ndarray
+    bias: np.ndarray
+    basis_version_ref: str | None
+    rank: int
+    grid: tuple[int, int, int]
+    token_start: int
+
+    def pixels(self, raw) -> Any:
+        """This tile's ``[tokens, rank]`` uint8 view of a pack's decoded bytes (host array or device tensor)."""
+        flat = raw.reshape(-1)
+        return flat[self.offset:self.offset + self.nbytes].reshape(self.shape)
 
 
 @dataclass
@@ -32,6 +59,82 @@ class PreparedPacket:
     tiles: list                        # per tile: {"entry", "coefficients": {offset, bytes, shape}, ...}
     affines: list                      # per tile: (scale, offset) float32 host arrays
     raw_shape: tuple[int, int]
+
+    def tile(self, index: int) -> dict:
+        """The pack's tile entry ``index`` (coefficient placement and its matrix entry)."""
+        if not 0 <= index < len(self.tiles):
+            raise ConfigurationError(f"pack {self.packet_ref} has {len(self.tiles)} tiles, not {index + 1}")
+        return self.tiles[index]
+
+
+def prepared_tiles(runtime, prepared: "PreparedPacket", records) -> list[PreparedTile]:
+    """The :class:`PreparedTile` of every ``(entry, record ref)`` of a history piece that lives in ``prepared``."""
+    out = []
+    for entry, record_ref in records:
+        record = runtime.load_record(record_ref)
+        if record.packet_ref != prepared.packet_ref:
+            continue
+        key, _ = entry_parts(entry)
+        index = record.decision["packet"]["tile"]
+        coeff = prepared.tiles[index]["coefficients"]
+        scale, bias = prepared.affines[index]
+        ctx = record.context
+        out.append(PreparedTile(entry, key.layer, key.target, index, int(coeff["offset"]), int(coeff["bytes"]),
+                                tuple(coeff["shape"]), scale, bias, record.basis_version_ref, int(record.rank_view),
+                                (ctx.frames, ctx.height, ctx.width), ctx.token_start))
+    return out
+
+
+def canonical_canvas_shapes(frames: int, height: int, width: int, pix_fmt: str = "yuv444p", *, channels: int,
+                            max_rank: int | None = None) -> list[tuple[int, int, str]]:
+    """``(width, height, pix_fmt)`` of every canonical node canvas of one tile geometry, smallest first: one per
+    rank step of the canvas ladder up to ``max_rank`` (default ``channels``), leaving out canvases beyond the
+    largest HEVC picture. Warming a decoder for each covers every pack of the geometry."""
+    from .node_packets import CANVAS_RANK_LADDER, canvas_layout
+
+    if not (type(channels) is int and channels > 0):
+        raise ConfigurationError(f"channels={channels!r}: expected an int >= 1")
+    limit = channels if max_rank is None else max_rank
+    if not (type(limit) is int and 1 <= limit <= channels):
+        raise ConfigurationError(f"max_rank={max_rank!r}: expected an int in [1, {channels}]")
+    _hevc.validate_parameters(pix_fmt)
+    shapes: list[tuple[int, int, str]] = []
+    for step in CANVAS_RANK_LADDER:
+        try:
+            layout = canvas_layout(frames, height, width, min(step, channels), pix_fmt)
+        except Exception:  # noqa: BLE001 -- a mosaic larger than the HEVC maximum picture: no pack uses it
+            break
+        shape = (layout["image_width"], layout["image_height"], pix_fmt)
+        if shape not in shapes:
+            shapes.append(shape)
+        if step >= limit:
+            break
+    return shapes
+
+
+def device_tile_pixels(canvas: torch.Tensor, first: int, layout, rank: int | None = None) -> torch.Tensor:
+    """One tile's ``[tokens, rank]`` uint8 coefficients gathered on the device from its decoded canvas pictures
+    (``canvas[first:first + segments * frames]`` of ``[pictures, planes, image_h, image_w]``; ``layout`` the
+    tile's ``reelcache.channel_tiles.v1`` layout). The inverse of the mosaic kernel, for diagnostics and for
+    decoders that leave pictures on the device."""
+    frames, height, width = layout["frames"], layout["height"], layout["width"]
+    planes, (columns, _) = layout["planes"], layout["grid"]
+    slots, segments = layout["channels_per_segment"], layout["segments"]
+    rank = layout.get("tile_rank", layout["rank"]) if rank is None else rank
+    if canvas.dim() != 4 or canvas.dtype != torch.uint8:
+        raise ConfigurationError(f"canvas must be uint8 [pictures, planes, H, W], got {canvas.dtype} "
+                                 f"{tuple(canvas.shape)}")
+    if canvas.shape[0] < first + segments * frames or canvas.shape[1] < planes or \
+            canvas.shape[2] < layout["image_height"] or canvas.shape[3] < layout["image_width"]:
+        raise IntegrityError(f"canvas {tuple(canvas.shape)} is smaller than the tile's layout")
+    out = torch.empty((frames, height, width, rank), dtype=torch.uint8, device=canvas.device)
+    for channel in range(rank):
+        segment, cell = divmod(channel, slots)
+        plane = cell % planes
+        row, column = divmod(cell // planes, columns)
+        pictures = canvas[first + segment * frames:first + (segment + 1) * frames, plane]
+        out[..., channel] = pictures[:, row * height:(row + 1) * height, column * width:(column + 1) * width]
+    return out.reshape(frames * height * width, rank)
 
 
 def prepare_packet(runtime, packet_ref: str) -> PreparedPacket:
@@ -149,3 +252,7 @@ class PackedRestorer:
     def release(self, batch: RestoreBatch) -> None:
         if self.tier is not None and batch.routed:
             self.tier.release(batch.routed)
+
+
+__all__ = ["PackedRestorer", "PreparedPacket", "PreparedTile", "RestoreBatch", "canonical_canvas_shapes",
+           "device_tile_pixels", "prepare_packet", "prepared_tiles"]

@@ -106,3 +106,24 @@ def test_factor_pack_validate_prepare_decode():
     bad = type(pack)(pack.metadata, {"factors": pack.payloads["factors"][:-2]})
     with pytest.raises(IntegrityError):
         validate_factor_pack(bad)
+
+
+def test_device_tile_pixels_inverts_the_mosaic_and_canvas_shapes():
+    import numpy as np
+    import torch
+    from reelcache_b200 import _hevc
+    from reelcache_b200.node_packets import canvas_layout, mosaic_host
+    from reelcache_b200.packed_decode import canonical_canvas_shapes, device_tile_pixels
+
+    frames, height, width, rank = 2, 6, 10, 45
+    layout = canvas_layout(frames, height, width, rank)
+    pixels = np.random.default_rng(0).integers(0, 256, (frames * height * width, rank), dtype=np.uint8)
+    canvas = torch.from_numpy(mosaic_host(pixels, layout, rank))
+    padded = torch.cat([torch.zeros((3,) + tuple(canvas.shape[1:]), dtype=torch.uint8), canvas])
+    back = device_tile_pixels(padded, 3, layout)
+    assert back.shape == (frames * height * width, rank) and np.array_equal(back.numpy(), pixels)
+    shapes = canonical_canvas_shapes(frames, height, width, channels=256)
+    assert shapes == sorted(shapes, key=lambda s: s[0] * s[1]) and len(shapes) == len(set(shapes))
+    assert (layout["image_width"], layout["image_height"], "yuv444p") in shapes
+    assert len(canonical_canvas_shapes(frames, height, width, channels=256, max_rank=32)) == 1
+    assert _hevc.PIXEL_FORMATS[0] == "yuv444p"
