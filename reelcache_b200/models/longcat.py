@@ -294,6 +294,8 @@ class LongCatDiT:
                                   out_dtype=torch.float32).reshape(6, cfg.dim)
             y = F.layer_norm(x, (cfg.dim,), eps=cfg.eps) * (1 + mod[1]) + mod[0]
             if ulysses is not None:
+                if blk.get("lora", {}).keys() & {"qkv", "proj"}:
+                    raise ValueError("LoRA branches on qkv / proj need the unfused Ulysses path (ulysses=None)")
                 rows = ulysses.world * n
                 q_u, k_u, _ = ulysses.qkv(y.to(self.dtype), blk["qkv_w"], blk["qkv_b"])
                 q = self.ops.norm_rope(q_u, blk["q_norm"], cos_g, sin_g, cfg.eps)
@@ -305,7 +307,7 @@ class LongCatDiT:
                 ulysses.out(x, blk["proj_w"], blk["proj_b"], mod[2])
                 self._cross_and_ffn(x, blk, mod, text, n)
                 continue
-            qkv = self.ops.linear(y.to(self.dtype), blk["qkv_w"], blk["qkv_b"]).reshape(n, 3, h, hd)
+            qkv = self._proj(blk, "qkv", y.to(self.dtype), blk["qkv_w"], blk["qkv_b"]).reshape(n, 3, h, hd)
             q = self.ops.rms_norm_heads(qkv[:, 0], blk["q_norm"], cfg.eps)
             k = self.ops.rms_norm_heads(qkv[:, 1], blk["k_norm"], cfg.eps)
             v = qkv[:, 2]
@@ -323,7 +325,7 @@ class LongCatDiT:
                                                    ulysses_in(v_all.contiguous(), cp_group)), cp_group)
             else:
                 o = self.ops.attention(q, k_all, v_all)
-            x = x + mod[2] * self.ops.linear(o.reshape(n, cfg.dim), blk["proj_w"], blk["proj_b"]).float()
+            x = x + mod[2] * self._proj(blk, "proj", o.reshape(n, cfg.dim), blk["proj_w"], blk["proj_b"]).float()
             self._cross_and_ffn(x, blk, mod, text, n)
         fmod = self.ops.linear(F.silu(temb.float()).to(self.dtype), self.final_ada_w, self.final_ada_b,
                                out_dtype=torch.float32).reshape(2, cfg.dim)
@@ -334,6 +336,30 @@ class LongCatDiT:
         pred = self.unpatchify(out, frames)
         return (pred, kvs) if return_kv else pred
 
+    # -- LoRA ------------------------------------------------------------------------------------------------------
+
+    def _proj(self, blk: dict, name: str, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None):
+        """A projection of the block plus its LoRA branches (none attached: the plain GEMM)."""
+        out = self.ops.linear(x, w, b)
+        if "lora" not in blk:
+            return out
+        from .longcat_lora import apply_branches
+        return apply_branches(blk, name, x, out, self.ops.linear)
+
+    def attach_lora(self, state_dict, *, multiplier: float = 1.0) -> list[str]:
+        """Attach the branches of a native LongCat LoRA state dict (e.g. ``cfg_step_lora``); returns the targeted
+        module paths. Branches stay separate from the weights (models/longcat_lora.py)."""
+        from .longcat_lora import attach
+        return attach(self.blocks, state_dict, multiplier=multiplier, dtype=self.dtype, device=self.device)
+
+    def detach_loras(self) -> int:
+        from .longcat_lora import detach
+        return detach(self.blocks)
+
+    def set_loras_enabled(self, enabled: bool) -> None:
+        from .longcat_lora import set_enabled
+        set_enabled(self.blocks, enabled)
+
     def _cross_and_ffn(self, x: torch.Tensor, blk: dict, mod: torch.Tensor, text: torch.Tensor, n: int) -> None:
         """Cross-attention over the text (skipped when ``text`` is None) and the SwiGLU FFN on this rank's
         rows, in place on ``x``."""
@@ -341,15 +367,16 @@ class LongCatDiT:
         h, hd = cfg.heads, cfg.head_dim
         if text is not None:
             y = F.layer_norm(x, (cfg.dim,), eps=cfg.eps).to(self.dtype)
-            cq = self.ops.rms_norm_heads(self.ops.linear(y, blk["cq_w"], blk["cq_b"]).reshape(n, h, hd),
+            cq = self.ops.rms_norm_heads(self._proj(blk, "cq", y, blk["cq_w"], blk["cq_b"]).reshape(n, h, hd),
                                          blk["cq_norm"], cfg.eps)
-            ckv = self.ops.linear(text, blk["ckv_w"], blk["ckv_b"]).reshape(-1, 2, h, hd)
+            ckv = self._proj(blk, "ckv", text, blk["ckv_w"], blk["ckv_b"]).reshape(-1, 2, h, hd)
             ck = self.ops.rms_norm_heads(ckv[:, 0], blk["ck_norm"], cfg.eps)
             co = self.ops.attention(cq, ck, ckv[:, 1])
-            x.add_(self.ops.linear(co.reshape(n, cfg.dim), blk["cproj_w"], blk["cproj_b"]).float())
+            x.add_(self._proj(blk, "cproj", co.reshape(n, cfg.dim), blk["cproj_w"], blk["cproj_b"]).float())
         y = (F.layer_norm(x, (cfg.dim,), eps=cfg.eps) * (1 + mod[4]) + mod[3]).to(self.dtype)
-        hidden = (F.silu(self.ops.linear(y, blk["w1"]).float()) * self.ops.linear(y, blk["w3"]).float()).to(self.dtype)
-        x.add_(mod[5] * self.ops.linear(hidden, blk["w2"]).float())
+        hidden = (F.silu(self._proj(blk, "w1", y, blk["w1"]).float())
+                  * self._proj(blk, "w3", y, blk["w3"]).float()).to(self.dtype)
+        x.add_(mod[5] * self._proj(blk, "w2", hidden, blk["w2"]).float())
 
     def build_conditioning_cache(self, cond_latents: torch.Tensor, epoch: ConditioningCacheEpoch,
                                  *, cp_group=None) -> LongCatConditioningCache:
