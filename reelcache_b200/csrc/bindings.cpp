@@ -14,7 +14,7 @@ void gemm_bf16_tn(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
                   const c10::optional<at::Tensor>& status);
 at::Tensor restore_build(const at::Tensor& jobs, const std::vector<at::Tensor>& a_ops,
                          const std::vector<at::Tensor>& b_ops, const at::Tensor& inverse);
-void restore_run(const at::Tensor& blob, int64_t device, const c10::optional<at::Tensor>& status, int64_t ablate);
+void restore_run(const at::Tensor& blob, int64_t device, const c10::optional<at::Tensor>& status, int64_t options);
 void prep_launch(const at::Tensor& jobs, int64_t device);
 void colminmax(const at::Tensor& p, at::Tensor& lo, at::Tensor& hi, at::Tensor& bad);
 void ln_modulate(const at::Tensor& x, at::Tensor& y, const c10::optional<at::Tensor>& shift,
@@ -36,7 +36,7 @@ void sq_partials(const at::Tensor& x, const c10::optional<at::Tensor>& r, double
 void fingerprint_partials(const at::Tensor& bits, at::Tensor& out, int64_t row_start, int64_t prime);
 void dot2_gemm(const at::Tensor& x, const at::Tensor& rows, at::Tensor& out);
 void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& out, double scale,
-                   const c10::optional<at::Tensor>& status, int64_t ablate);
+                   const c10::optional<at::Tensor>& status, int64_t options, const c10::optional<at::Tensor>& trace);
 void mosaic_u8(const at::Tensor& pixels, at::Tensor& canvas, const std::vector<int64_t>& geometry);
 void gemm_bf16_promoted(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, double alpha,
                         const c10::optional<at::Tensor>& status);
@@ -76,7 +76,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("restore_build", &rc::restore_build, "launch parameters of a fused restore over <= 48 jobs",
         py::arg("jobs"), py::arg("a_ops"), py::arg("b_ops"), py::arg("inverse"));
   m.def("restore_run", &rc::restore_run, "launch a fused restore from restore_build parameters", py::arg("blob"),
-        py::arg("device"), py::arg("status") = py::none(), py::arg("ablate") = 0);
+        py::arg("device"), py::arg("status") = py::none(), py::arg("options") = 0);
   m.def("colminmax", &rc::colminmax, "per-column extrema of FP32 coefficients", py::arg("p"), py::arg("lo"),
         py::arg("hi"), py::arg("bad"));
   m.def("quantize_columns", &rc::quantize_columns, "FP64 rint quantization of coefficients to uint8",
@@ -114,7 +114,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("A"), py::arg("B"), py::arg("out"), py::arg("alpha") = 1.0, py::arg("status") = py::none());
   m.def("attention_fwd", &rc::attention_fwd, "flash-attention forward on tcgen05 (bf16, head_dim 128)",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("scale"), py::arg("status") = py::none(),
-        py::arg("ablate") = 0);
+        py::arg("options") = 0, py::arg("trace") = py::none());
   m.def("mosaic_u8", &rc::mosaic_u8, "channel-tile mosaic of u8 coefficients into a canvas", py::arg("pixels"),
         py::arg("canvas"), py::arg("geometry"));
   m.def("dot2_gemm", &rc::dot2_gemm, "compensated FP32 GEMM out = x @ rows^T", py::arg("x"), py::arg("rows"),

@@ -56,3 +56,37 @@ def test_attention_peaked_scores_rescale():
     got = attention(q, k, v, backend="fused", scale=1.0)
     ref = _reference(q, k, v, 1.0)
     assert float((got.float() - ref).norm() / ref.norm()) < 2e-2
+
+
+@pytest.mark.parametrize("tq,tk,ranges", [(300, 1000, 2), (4680, 4680, 3), (256, 2000, 4), (700, 390, 3)])
+def test_attention_key_ranges_match_fp32(tq, tk, ranges):
+    """Key ranges forced through the option word: each range's normalized partial output and log2-sum-exp,
+    combined by the merge kernel, equal the single-pass result."""
+    from reelcache_b200.ops import _ext
+    from reelcache_b200.ops.attention import attention
+    g = torch.Generator(device="cuda").manual_seed(7 * tq + tk)
+    heads = 3
+    q = torch.randn(tq, heads, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(tk, heads, 128, device="cuda", generator=g).bfloat16() * 2
+    v = torch.randn(tk, heads, 128, device="cuda", generator=g).bfloat16()
+    scale = 1.0 / math.sqrt(128)
+    got = attention(q, k, v, backend="fused", scale=scale, options=ranges)
+    single = attention(q, k, v, backend="fused", scale=scale, options=1)
+    _ext.check_status(q.device)
+    ref = _reference(q, k, v, scale)
+    assert float((got.float() - ref).norm() / ref.norm()) < 2e-2
+    assert float((got.float() - single.float()).abs().max()) < 3e-2
+
+
+def test_attention_fma_exponentials_match_fp32():
+    """A quarter of the exponentials on the FMA pipe (cubic fit of 2^f) stays within bf16 rounding of P."""
+    from reelcache_b200.ops import _ext
+    from reelcache_b200.ops.attention import OPT_POLY_EXP, attention
+    g = torch.Generator(device="cuda").manual_seed(11)
+    q = torch.randn(1000, 2, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(3000, 2, 128, device="cuda", generator=g).bfloat16() * 2
+    v = torch.randn(3000, 2, 128, device="cuda", generator=g).bfloat16()
+    got = attention(q, k, v, backend="fused", scale=0.1, options=OPT_POLY_EXP)
+    _ext.check_status(q.device)
+    ref = _reference(q, k, v, 0.1)
+    assert float((got.float() - ref).norm() / ref.norm()) < 2e-2
