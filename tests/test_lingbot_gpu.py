@@ -32,8 +32,9 @@ def test_fused_restore_overlapped_equals_synchronous(tmp_path):
         parent = f"s/{chunk}"
     assert archive.stats()["restorer"] == "LineageRestorer"
     sync_model = StandInWorldModel(GEOMETRY, device=dev)
-    archive.restore(parent, sync_model)
-    for c in range(3):
+    record = archive.restore(parent, sync_model)
+    assert record["chunks"] == [1, 2]  # the window before chunk 3 (3 chunks of 3 latent frames)
+    for c in record["chunks"]:
         start, end = sync_model.cache.place(c)
         for layer in range(GEOMETRY.layers):
             for ours, theirs in ((sync_model.cache.k[layer], live.cache.k[layer]),
