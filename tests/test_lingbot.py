@@ -14,6 +14,10 @@ from reelcache_b200.integrations.lingbot import (ArchiveError, LINGBOT_WORLD_FAS
                                                  StallEvents, StandInWorldModel)
 from reelcache_b200.overlapped_restore import LayerReadiness, RestoreFailure, start_overlapped_restore
 
+# The stand-in's K / V have no low-rank structure, so the representation keeps exactly its energy targets
+# (K 98 %, V 95 %): relative error sqrt(1 - target), plus 8-bit coefficient quantization.
+K_BOUND = (1 - 0.98) ** 0.5 + 0.03
+V_BOUND = (1 - 0.95) ** 0.5 + 0.03
 GEOMETRY = LINGBOT_WORLD_FAST.scaled(layers=3, heads=2, head_dim=16, frames_per_chunk=1, latent_height=4,
                                      latent_width=4, window_latents=3, sink_latents=1)
 
@@ -205,9 +209,9 @@ def test_compressed_representation_within_its_energy_target(tmp_path):
     for c in record["chunks"]:
         start, end = restored.cache.place(c)
         for layer in range(GEOMETRY.layers):
-            for ours, theirs in ((restored.cache.k[layer], live.cache.k[layer]),
-                                 (restored.cache.v[layer], live.cache.v[layer])):
+            for ours, theirs, bound in ((restored.cache.k[layer], live.cache.k[layer], K_BOUND),
+                                        (restored.cache.v[layer], live.cache.v[layer], V_BOUND)):
                 a, b = ours[0, start:end], theirs[0, start:end]
-                assert float((a - b).norm() / b.norm()) < 0.2
+                assert float((a - b).norm() / b.norm()) < bound
     assert archive.stats()["restorer"] == "SoftwareLineageRestorer"
     archive.close()

@@ -9,6 +9,10 @@ from reelcache_b200.integrations.lingbot import LINGBOT_WORLD_FAST, LingBotArchi
 
 pytestmark = pytest.mark.gpu
 
+# The stand-in's K / V have no low-rank structure, so the representation keeps exactly its energy targets
+# (K 98 %, V 95 %): relative error sqrt(1 - target), plus 8-bit coefficient quantization.
+K_BOUND = (1 - 0.98) ** 0.5 + 0.03
+V_BOUND = (1 - 0.95) ** 0.5 + 0.03
 GEOMETRY = LINGBOT_WORLD_FAST.scaled(layers=2, heads=2, window_latents=9)
 
 
@@ -37,10 +41,10 @@ def test_fused_restore_overlapped_equals_synchronous(tmp_path):
     for c in record["chunks"]:
         start, end = sync_model.cache.place(c)
         for layer in range(GEOMETRY.layers):
-            for ours, theirs in ((sync_model.cache.k[layer], live.cache.k[layer]),
-                                 (sync_model.cache.v[layer], live.cache.v[layer])):
+            for ours, theirs, bound in ((sync_model.cache.k[layer], live.cache.k[layer], K_BOUND),
+                                        (sync_model.cache.v[layer], live.cache.v[layer], V_BOUND)):
                 a, b = ours[0, start:end].float(), theirs[0, start:end].float()
-                assert float((a - b).norm() / b.norm()) < 0.2
+                assert float((a - b).norm() / b.norm()) < bound
     sync_out, _ = sync_model.generate(3, xs[3], capture=False)
     over_model = StandInWorldModel(GEOMETRY, device=dev)
     anchor = torch.cuda.Event(enable_timing=True)
