@@ -257,18 +257,23 @@ def svd_archive_rate(package, device, chunks, layers):
         runtime.create_lineage("a")
         method = method_class(types.energy_targets("causvid"), types.CodecSpec("svd", 32))
         seconds = 0.0
+        phases: dict = {}
         for index in range(chunks + 1):
             matrices, contexts = synthetic_lowrank_chunk(types, runtime.model, index, layers, device)
             torch.cuda.synchronize()
             started = time.perf_counter()
-            runtime.commit_node("a", f"c{index}", matrices, contexts, method=method, registry=registry, device=device,
-                                **extra)
+            commit = runtime.commit_node("a", f"c{index}", matrices, contexts, method=method, registry=registry,
+                                         device=device, **extra)
             torch.cuda.synchronize()
             if index:
                 seconds += time.perf_counter() - started
+                for phase, value in (getattr(commit, "timings", None) or {}).items():
+                    if isinstance(value, (int, float)):
+                        phases[phase] = phases.get(phase, 0.0) + value
         stored = sum(os.path.getsize(os.path.join(d, f)) for d, _, files in os.walk(root) for f in files)
         return {"chunks_per_s": round(chunks / seconds, 3), "ms_per_chunk": round(1e3 * seconds / chunks, 1),
                 "stored_bytes_per_chunk": int(stored / (chunks + 1)), "chunks_timed": chunks,
+                "phase_ms_per_chunk": {k: round(1e3 * v / chunks, 1) for k, v in phases.items()},
                 "representation": "per-matrix SVD packets, CodecSpec('svd', 32), K 98 % / V 95 % energy",
                 "data": "synthetic rank-64 CausVid-shaped K/V (30 x 2 x 4680 x 1536 bf16), drifting bases"}
     except Exception as error:  # noqa: BLE001 - reported in the JSON line, the headline stands
