@@ -47,6 +47,7 @@ def main(argv=None):
     xt = torch.cat([x.t() for x in shards]).contiguous()
     slots = GramReduceScatter.slots_for(owners)
     fused = GramReduceScatter(None, device, channels=args.channels, max_slots=max(slots) + 1)
+    in_switch = GramReduceScatter(None, device, channels=args.channels, max_slots=max(slots) + 1, nvls="auto")
 
     def library():
         out = {}
@@ -86,6 +87,16 @@ def main(argv=None):
 
     res = {"world": world, "matrices": args.matrices, "tokens_per_rank": n_r, "channels": args.channels,
            "library_ms": timed(library), "fused_ms": timed(run_fused), "max_rel_diff": float(errt)}
+    if in_switch.nvls:
+        got_nvls = in_switch.run(xt, owners)
+        torch.cuda.synchronize()
+        in_switch.check()
+        err_n = max((float((got_nvls[b] - ref[b]).norm() / ref[b].norm()) for b in got_nvls), default=0.0)
+        errn = torch.tensor([err_n], device=device)
+        dist.all_reduce(errn, op=dist.ReduceOp.MAX)
+        res.update(nvls_ms=timed(lambda: in_switch.run(xt, owners)), nvls_max_rel_diff=float(errn))
+    else:
+        res.update(nvls_ms=None, nvls_note="no NVLink multicast object on these GPUs")
     fused.check()
     nt = args.channels // 128
     tiles = nt * (nt + 1) // 2

@@ -49,9 +49,10 @@ void ulysses_out(const std::vector<at::Tensor>& o_owners, const at::Tensor& w, c
                  int64_t epilogue, const at::Tensor& stage, const at::Tensor& tile_flags, int64_t call,
                  const c10::optional<at::Tensor>& status);
 void peer_barrier(const at::Tensor& flags, int64_t rank, int64_t epoch, const c10::optional<at::Tensor>& status);
+void nvls_reduce_upper(int64_t mc_ptr, int64_t buffer_elems, const at::Tensor& offsets, at::Tensor& out, int64_t C);
 void gram_reduce_scatter(const at::Tensor& xt, int64_t matrices, const std::vector<at::Tensor>& partials,
                          const at::Tensor& owners, const at::Tensor& slots, int64_t rank,
-                         const c10::optional<at::Tensor>& status);
+                         const c10::optional<at::Tensor>& status, bool to_local);
 }  // namespace rc
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -67,12 +68,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("o_owners"), py::arg("w"), py::arg("bias"), py::arg("gate"), py::arg("out"), py::arg("rank"),
         py::arg("n_loc"), py::arg("epilogue"), py::arg("stage"), py::arg("tile_flags"), py::arg("call"),
         py::arg("status") = py::none());
+  m.def("nvls_reduce_upper", &rc::nvls_reduce_upper,
+        "in-switch (NVLS multimem.ld_reduce) sum of symmetric C x C partials, upper 128 x 128 tiles",
+        py::arg("mc_ptr"), py::arg("buffer_elems"), py::arg("offsets"), py::arg("out"), py::arg("C"));
   m.def("peer_barrier", &rc::peer_barrier, "bounded device-side barrier over peer flag words", py::arg("flags"),
         py::arg("rank"), py::arg("epoch"), py::arg("status") = py::none());
   m.def("gram_reduce_scatter", &rc::gram_reduce_scatter,
         "upper-triangular partial Grams of this rank's token shard stored into the owners' buffers (peer stores)",
         py::arg("xt"), py::arg("matrices"), py::arg("partials"), py::arg("owners"), py::arg("slots"), py::arg("rank"),
-        py::arg("status") = py::none());
+        py::arg("status") = py::none(), py::arg("to_local") = false);
   m.def("restore_build", &rc::restore_build, "launch parameters of a fused restore over <= 48 jobs",
         py::arg("jobs"), py::arg("a_ops"), py::arg("b_ops"), py::arg("inverse"));
   m.def("restore_run", &rc::restore_run, "launch a fused restore from restore_build parameters", py::arg("blob"),

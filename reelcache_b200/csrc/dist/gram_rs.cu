@@ -226,9 +226,13 @@ __global__ void __launch_bounds__(kThreads, 1) gram_rs_kernel(const __grid_const
 // Partial Grams of this rank's shard of every matrix, delivered to the owners: xt = X^T stacked [B * C, n_r]
 // bf16 (C a multiple of 128), partials[p] = owner p's FP32 [world, slots, C, C] buffer (peer views),
 // owners / slots = int64 [B] on the CPU. Only the upper-triangular 128 x 128 tiles are written.
+//
+// to_local: every tile goes into this rank's own buffer instead (`partials` = that one buffer, [1, slots, C, C];
+// slots[b] numbers the matrices globally, the same on every rank), for the in-switch reduction
+// (nvls_reduce.cu), which then reads every rank's copy of a slot through the multicast address.
 void gram_reduce_scatter(const at::Tensor& xt, int64_t matrices, const std::vector<at::Tensor>& partials,
                          const at::Tensor& owners, const at::Tensor& slots, int64_t rank,
-                         const c10::optional<at::Tensor>& status) {
+                         const c10::optional<at::Tensor>& status, bool to_local) {
   using namespace gram_rs;
   check_cuda_tensor(xt, "xt");
   RC_CHECK(xt.scalar_type() == at::kBFloat16 && xt.dim() == 2 && xt.stride(1) == 1 && (xt.stride(0) * 2) % 16 == 0 &&
@@ -237,8 +241,10 @@ void gram_reduce_scatter(const at::Tensor& xt, int64_t matrices, const std::vect
   RC_CHECK(matrices >= 1 && matrices <= kMaxMatrices && xt.size(0) % matrices == 0, "1..64 stacked matrices");
   const int C = static_cast<int>(xt.size(0) / matrices);
   RC_CHECK(C % 128 == 0, "channels must be a multiple of 128");
-  const int world = static_cast<int>(partials.size());
-  RC_CHECK(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world, "one partial buffer per rank (<= 8)");
+  const int world = to_local ? kMaxPeers : static_cast<int>(partials.size());
+  RC_CHECK(!to_local || partials.size() == 1, "to_local takes this rank's own buffer only");
+  RC_CHECK(to_local || (world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world),
+           "one partial buffer per rank (<= 8)");
   RC_CHECK(owners.device().is_cpu() && owners.scalar_type() == at::kLong && owners.numel() == matrices &&
                slots.device().is_cpu() && slots.scalar_type() == at::kLong && slots.numel() == matrices,
            "owners and slots must be CPU int64 [B]");
@@ -250,7 +256,7 @@ void gram_reduce_scatter(const at::Tensor& xt, int64_t matrices, const std::vect
   RC_CHECK(p.K % 8 == 0 && p.K > 0, "tokens must be a positive multiple of 8");
   p.nt = C / 128;
   p.tiles_per_matrix = p.nt * (p.nt + 1) / 2;
-  p.rank = static_cast<int>(rank);
+  p.rank = to_local ? 0 : static_cast<int>(rank);
   p.world = world;
   const int64_t* own = owners.data_ptr<int64_t>();
   const int64_t* sl = slots.data_ptr<int64_t>();
@@ -262,8 +268,8 @@ void gram_reduce_scatter(const at::Tensor& xt, int64_t matrices, const std::vect
     max_slot = std::max(max_slot, p.slot[b]);
   }
   for (int r = 0; r < world; ++r) {
-    const at::Tensor& t = partials[r];
-    RC_CHECK(t.scalar_type() == at::kFloat && t.is_contiguous() && t.dim() == 4 && t.size(0) == world &&
+    const at::Tensor& t = partials[to_local ? 0 : r];
+    RC_CHECK(t.scalar_type() == at::kFloat && t.is_contiguous() && t.dim() == 4 && t.size(0) == (to_local ? 1 : world) &&
                  t.size(2) == C && t.size(3) == C && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
              "partial buffers must be contiguous float32 [world, slots, C, C]");
     RC_CHECK(t.size(1) > max_slot, "a slot index exceeds the partial buffer");

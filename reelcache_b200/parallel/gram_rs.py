@@ -9,6 +9,12 @@ to IEEE adds every 256 tokens) and stores each tile into the owner's symmetric b
 ``partials[rank][slot]`` as it finishes (NVLink stores for a peer owner), so the transfer overlaps the GEMM and
 only half of each symmetric Gram crosses NVLink. After a bounded device barrier the owner sums the ranks'
 partials in rank order in FP32 and mirrors the upper triangle: deterministic, FP32-accurate Grams.
+
+``nvls="auto"`` (default: where the GPUs share an NVLink multicast object) or ``True``: the in-switch variant. Each rank's
+kernel stores its tiles into its *own* symmetric buffer, every matrix at the same offset on every rank; after the
+barrier the owner reads the matrix through the buffer's multicast address with ``multimem.ld_reduce``
+(csrc/dist/nvls_reduce.cu), so the NVSwitch adds the ranks' partials and returns one reduced stream. The sum's
+order is the switch's (it may differ in the last bit from the rank-ordered one).
 """
 
 from __future__ import annotations
@@ -20,7 +26,7 @@ from ..ops._ext import check_status, ext, status_word
 
 
 class GramReduceScatter:
-    def __init__(self, group, device, *, channels: int, max_slots: int):
+    def __init__(self, group, device, *, channels: int, max_slots: int, nvls="auto"):
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm
 
@@ -56,6 +62,13 @@ class GramReduceScatter:
                 self.partials.append(self.handle.get_buffer(peer, shape, torch.float32, 0))
                 flags.append(self.handle.get_buffer(peer, (self.world,), torch.int32, self._flags_offset // 4))
         self.flag_table = torch.tensor([f.data_ptr() for f in flags], dtype=torch.int64, device=self.device)
+        self.mc_ptr = int(getattr(self.handle, "multicast_ptr", 0) or 0) if nvls else 0
+        if nvls is True and not self.mc_ptr:
+            raise ConfigurationError("NVLS was requested but these GPUs share no NVLink multicast object")
+        self.nvls = bool(self.mc_ptr)
+        # in-switch mode: this rank's buffer viewed as one slot per matrix of a call (world * max_slots of them)
+        self._local_slots = self.buffer[:self._flags_offset].view(torch.float32).view(
+            1, self.world * max_slots, channels, channels)
         self.epoch = 0
         self.status = status_word(self.device)
         torch.cuda.synchronize(self.device)
@@ -85,6 +98,8 @@ class GramReduceScatter:
         # that sum (the sum precedes this barrier on the owner's stream).
         self.epoch += 1
         ext().peer_barrier(self.flag_table, self.rank, self.epoch, self.status)
+        if self.nvls:
+            return self._run_nvls(xt, owners)
         ext().gram_reduce_scatter(xt.contiguous(), matrices, self.partials,
                                   torch.tensor(owners, dtype=torch.int64), torch.tensor(slots, dtype=torch.int64),
                                   self.rank, self.status)
@@ -102,6 +117,25 @@ class GramReduceScatter:
             sums += local[rank, :count]
         grams = symmetric_from_upper(sums)
         return {b: grams[slots[b]] for b in owned}
+
+    def _run_nvls(self, xt: torch.Tensor, owners: list[int]) -> dict[int, torch.Tensor]:
+        matrices = len(owners)
+        if matrices > self._local_slots.shape[1]:
+            raise ConfigurationError(f"{matrices} matrices exceed the {self._local_slots.shape[1]} slots of the buffer")
+        ext().gram_reduce_scatter(xt.contiguous(), matrices, [self._local_slots],
+                                  torch.tensor(owners, dtype=torch.int64), torch.arange(matrices, dtype=torch.int64),
+                                  self.rank, self.status, to_local=True)
+        self.epoch += 1
+        ext().peer_barrier(self.flag_table, self.rank, self.epoch, self.status)
+        owned = [b for b, owner in enumerate(owners) if owner == self.rank]
+        if not owned:
+            return {}
+        c = self.channels
+        out = torch.empty((len(owned), c, c), dtype=torch.float32, device=self.device)
+        offsets = torch.tensor([b * c * c for b in owned], dtype=torch.int64)
+        ext().nvls_reduce_upper(self.mc_ptr, self._flags_offset // 4, offsets, out, c)
+        grams = symmetric_from_upper(out)
+        return {b: grams[i] for i, b in enumerate(owned)}
 
     def check(self) -> None:
         check_status(self.device)

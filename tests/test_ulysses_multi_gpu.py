@@ -75,6 +75,27 @@ def _worker(rank, world, port, result_path):
         grs.check()
         errors.append(gram_err)
         grs.close()
+        # the in-switch (NVLS multimem.ld_reduce) variant, where the GPUs share an NVLink multicast object
+        nvls = GramReduceScatter(None, device, channels=channels, max_slots=matrices, nvls="auto")
+        nvls_err = -1.0
+        if nvls.nvls:
+            nvls_err = 0.0
+            for call in range(4):
+                gen_r = torch.Generator(device=device).manual_seed(20 + 89 * call + rank)
+                shards = [torch.randn(64 + 32 * call, channels, device=device, generator=gen_r).bfloat16()
+                          for _ in range(matrices)]
+                grams = nvls.run(torch.cat([x.t() for x in shards]).contiguous(), owners)
+                gathered = [[torch.empty_like(x) for _ in range(world)] for x in shards]
+                for b in range(matrices):
+                    dist.all_gather(gathered[b], shards[b])
+                for b, gram in grams.items():
+                    full = torch.cat(gathered[b]).double()
+                    ref = full.t() @ full
+                    nvls_err = max(nvls_err, float((gram.double() - ref).norm() / ref.norm()))
+            torch.cuda.synchronize()
+            nvls.check()
+        errors.append(nvls_err)
+        nvls.close()
         if rank == 0:
             with open(result_path, "w") as handle:
                 handle.write(",".join(str(e) for e in errors))
@@ -92,3 +113,4 @@ def test_fused_ulysses_forward_matches_nccl(tmp_path, world):
     errors = [float(v) for v in result.read_text().split(",")]
     assert all(e < 2e-2 for e in errors[:2]), errors
     assert errors[2] < 1e-6, errors
+    assert errors[3] < 1e-6, errors  # -1: no NVLink multicast object on these GPUs (the NVLS variant did not run)
