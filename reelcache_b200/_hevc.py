@@ -294,6 +294,19 @@ def mosaic_all(pixels, layout):
 
 
 def unmosaic_all(images, layout):
+    """``[frames * height * width, rank]`` coefficients of a segment-major picture stack (native, without the
+    GIL, when the extension is built)."""
+    native = _native("unmosaic_all")
+    if native is not None:
+        import torch
+        pictures = np.require(images, dtype=np.uint8, requirements=["C", "W"])
+        columns, _ = layout["grid"]
+        return native(torch.from_numpy(pictures), layout["frames"], layout["height"], layout["width"], layout["rank"],
+                      columns, layout["planes"], layout["channels_per_segment"]).numpy()
+    return _unmosaic_all_python(images, layout)
+
+
+def _unmosaic_all_python(images, layout):
     values = np.empty((layout["frames"], layout["height"], layout["width"], layout["rank"]), dtype=np.uint8)
     frames = layout["frames"]
     for s in range(layout["segments"]):
@@ -329,9 +342,33 @@ def _native_scanner():
         return None
 
 
+def _native(name):
+    try:
+        from .ops._ext import ext
+        return getattr(ext(), name)
+    except Exception:  # noqa: BLE001 - the host fast paths are optional
+        return None
+
+
 def nal_units(stream):
-    """``[(offset, length, nal_type)]`` of an Annex-B HEVC stream, integrity-checked."""
+    """``[(offset, length, nal_type)]`` of an Annex-B HEVC stream, integrity-checked (in the native extension,
+    without the GIL, when it is built; the same checks and table either way)."""
     data = bytes(stream)
+    native = _native("nal_units") if len(data) >= 4096 else None
+    if native is not None:
+        import torch
+        try:
+            table = native(torch.frombuffer(bytearray(data), dtype=torch.uint8))
+        except RuntimeError as error:
+            message = str(error)
+            if "integrity: " in message:
+                raise IntegrityError(message.split("integrity: ", 1)[1].splitlines()[0]) from None
+            raise
+        return [tuple(row) for row in table.tolist()]
+    return _nal_units_python(data)
+
+
+def _nal_units_python(data: bytes):
     positions = start_code_positions(data)
     leading = positions[0] if positions else None
     if leading is None or leading > 1 or (leading == 1 and data[0] != 0):

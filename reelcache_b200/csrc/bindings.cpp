@@ -8,6 +8,9 @@ namespace rc {
 int64_t pread_many(const std::vector<std::string>& paths, const std::vector<int64_t>& offsets,
                    const std::vector<int64_t>& sizes, const std::vector<int64_t>& dest, int64_t threads);
 std::vector<int64_t> start_codes(const at::Tensor& data);
+at::Tensor nal_units(const at::Tensor& data);
+at::Tensor unmosaic_all(const at::Tensor& images, int64_t frames, int64_t height, int64_t width, int64_t rank,
+                        int64_t columns, int64_t planes, int64_t slots);
 void gemm_bf16_tn(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epilogue,
                   const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& gate,
                   const c10::optional<at::Tensor>& resid, double alpha, int64_t bn,
@@ -104,6 +107,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("pread_many", &rc::pread_many, "parallel positioned reads into host memory (GIL released)",
         py::arg("paths"), py::arg("offsets"), py::arg("sizes"), py::arg("dest"), py::arg("threads") = 8);
   m.def("start_codes", &rc::start_codes, "Annex-B start-code offsets of a CPU uint8 tensor", py::arg("data"));
+  m.def("nal_units", &rc::nal_units, "NAL-unit table [n, 3] (offset, length, type) of an Annex-B stream (GIL released)",
+        py::arg("data"), py::call_guard<py::gil_scoped_release>());
+  m.def("unmosaic_all", &rc::unmosaic_all, "channel-tile pictures back to [tokens, rank] coefficients (GIL released)",
+        py::arg("images"), py::arg("frames"), py::arg("height"), py::arg("width"), py::arg("rank"), py::arg("columns"),
+        py::arg("planes"), py::arg("slots"), py::call_guard<py::gil_scoped_release>());
   m.def("split_bf16x3", &rc::split_bf16x3, "FP32 -> K-concatenated bf16 hi/mid/lo segments", py::arg("x"),
         py::arg("out"), py::arg("kp"), py::arg("parts"));
   m.def("jacobi_eigh", &rc::jacobi_eigh, "batched FP32 Jacobi eigendecomposition (n <= 160)", py::arg("a"),
