@@ -1,4 +1,5 @@
-"""Headline benchmark: KV restore of an archived CausVid-shaped history.
+"""Headline benchmark: KV restore of an archived CausVid-shaped history (one GPU: 12 chunks generated and archived, a
+rewind to chunk 4 restored and resumed).
 
 Workload (synthetic data, random-init weights of the named architecture): a CausVid-shaped causal DiT
 (30 x 1536, 12 x 128 heads, FFN 8960, 480p -> 4680 tokens per 3-latent-frame chunk, text [512, 4096])
@@ -38,7 +39,7 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "KV restore GB/s (rewind-to-chunk-4 resume; p50 TTFC and archived chunks/s reported alongside)"
-BASELINE_PUBLISHED = None  # the reference publishes no absolute restore GB/s figure
+PUBLISHED_REFERENCE_VALUE = None  # the reference publishes no absolute restore GB/s figure
 
 
 def parse():
@@ -593,7 +594,7 @@ def sp_factor(tile, device, generator):
 
 
 def run_sp(args, rank, world, local):
-    """a 24-chunk (112k-token) CausVid history restored under sequence parallelism SP = N.
+    """Sequence-parallel restore: a 24-chunk (112k-token) CausVid history restored under sequence parallelism SP = N.
     Every matrix's factors live on its factor owner; rank r restores the KV of its contiguous range of whole
     chunks (its sequence shard), its unpack kernel loading the owners' coefficients and its basis preparation
     loading their bases straight from peer memory, then the tcgen05 restore GEMM (strong scaling)."""
@@ -801,7 +802,7 @@ def main():
         sp = args.mode == "sp"
         out.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
                     "scaling": "strong" if sp else "weak",
-                    "vs_baseline": None if BASELINE_PUBLISHED is None else out["value"] / BASELINE_PUBLISHED,
+                    "vs_baseline": None if PUBLISHED_REFERENCE_VALUE is None else out["value"] / PUBLISHED_REFERENCE_VALUE,
                     "dtype": "bf16", "data": "synthetic (random-init CausVid-shaped DiT generates the archived history)",
                     "config": {"model": "CausVid-shaped causal DiT (Wan2.1-T2V-1.3B geometry), random-init bf16",
                                "global_batch": 1 if sp else world,

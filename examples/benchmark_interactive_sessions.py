@@ -1,4 +1,4 @@
-"""Interactive session mix on one GPU (scaled to one device; the counterpart of reference
+"""Interactive session mix on one GPU (the 64-session resume / rewind / fork mix scaled to one device; the counterpart of reference
 examples/benchmark_interactive_sessions.py): sessions of the CausVid-shaped DiT (random-init bf16, full-history
 visibility) created with histories of ``--min-history..--max-history`` chunks, then a Poisson trace of resume /
 rewind-to-an-earlier-chunk / fork requests (50 / 30 / 20 %) served through the bridge

@@ -1,4 +1,4 @@
-"""Interactive session-mix workload generator (the counterpart of reference
+"""Interactive session-mix workload generator (64 sessions, Poisson arrivals, resume / rewind / fork mix; the counterpart of reference
 reelcache/workloads.py): concurrent sessions with Poisson arrivals, an action mix of resume / rewind
 to a uniform earlier chunk / fork, histories of ``min_history..max_history`` chunks, driven through
 a serving bridge (:class:`CausalWanKVBridge`). Records per-action time to first chunk and summarizes
