@@ -346,3 +346,303 @@ def bundle_summary(sessions: Sequence[Mapping[str, Any]]) -> dict[str, Any]:
 __all__ = ["CHANGE_TYPES", "CONTROL_SCHEMA", "HISTORY_LENGTHS", "OPERATIONS", "TRACE_SCHEMA", "bundle_summary",
            "compile_session", "normalized_prompt", "read_sessions", "replay_cpu_control", "validate_session",
            "validate_workload"]
+
+
+# -- recorded browser traces ------------------------------------------------------------------------------------------
+# A browser session recorded as events (WebLINX-style replays) mapped onto clean-boundary video operations under an
+# explicit policy (reference reelcache/workloads.py:21-272): every content-producing action of the active tab
+# generates ``chunks_per_action`` clean chunks; a new tab forks a branch from its opener's (or the active tab's)
+# newest checkpoint; switching tabs resumes that tab's branch; closing an inactive tab retires its branch; loading a
+# document the branch produced before rewinds (or resumes) to the checkpoint it was seen at; an idle gap of at least
+# ``pause_gap_seconds`` pauses and resumes the branch. Events the policy cannot map stay in the source audit with
+# the reason, never as invented operations. The output is the same trace-mapped workload schema as above.
+
+from dataclasses import asdict, dataclass  # noqa: E402
+import math  # noqa: E402
+
+
+@dataclass(frozen=True)
+class WorkloadPolicy:
+    chunk_seconds: float
+    prompt_seconds: float = 10.0
+    chunks_per_action: int = 1
+    pause_gap_seconds: float = 30.0
+    seed: int = 0
+    branch_content: str = "new_seed"
+    generation_intents: tuple[str, ...] = ("load", "click", "scroll", "paste")
+    infer_url_rewind: bool = False
+
+    def __post_init__(self):
+        def seconds(value, name, *, positive):
+            ok = not isinstance(value, bool) and isinstance(value, (int, float)) and math.isfinite(value)
+            if not ok or (value <= 0 if positive else value < 0):
+                raise ConfigurationError(f"workload policy: {name} must be {'positive' if positive else 'nonnegative'}"
+                                         f" finite seconds, got {value!r}")
+        seconds(self.chunk_seconds, "chunk_seconds", positive=True)
+        seconds(self.prompt_seconds, "prompt_seconds", positive=True)
+        seconds(self.pause_gap_seconds, "pause_gap_seconds", positive=False)
+        if type(self.chunks_per_action) is not int or self.chunks_per_action < 1:
+            raise ConfigurationError(f"workload policy: chunks_per_action must be >= 1, got {self.chunks_per_action!r}")
+        if type(self.seed) is not int or not 0 <= self.seed < 2 ** 63:
+            raise ConfigurationError(f"workload policy: seed must be in [0, 2**63), got {self.seed!r}")
+        if self.branch_content not in ("new_seed", "next_prompt"):
+            raise ConfigurationError(f"workload policy: branch_content {self.branch_content!r} is neither new_seed "
+                                     "nor next_prompt")
+        if type(self.infer_url_rewind) is not bool:
+            raise ConfigurationError("workload policy: infer_url_rewind is a boolean")
+        if not self.generation_intents or not all(isinstance(i, str) and i for i in self.generation_intents):
+            raise ConfigurationError("workload policy: generation_intents are nonempty strings")
+
+
+def read_narratives(text: str) -> list[dict[str, Any]]:
+    """Narratives (JSONL of ``{"prompts": [...]}``), each identified by the SHA-256 of its canonical prompt list;
+    a repeated narrative is refused (split datasets at whole narratives)."""
+    out, ids = [], set()
+    for number, line in enumerate(text.splitlines(), 1):
+        if not line.strip():
+            continue
+        try:
+            row = json.loads(line)
+        except ValueError as error:
+            raise ConfigurationError(f"narrative line {number} is not JSON") from error
+        prompts = row.get("prompts") if isinstance(row, dict) else None
+        if not isinstance(prompts, list) or not prompts or not all(isinstance(p, str) and p.strip() for p in prompts):
+            raise ConfigurationError(f"narrative line {number} needs a nonempty list of nonempty prompts")
+        prompts = json.loads(json.dumps(prompts))
+        identity = hashlib.sha256(json.dumps(prompts, ensure_ascii=True).encode()).hexdigest()
+        if identity in ids:
+            raise ConfigurationError(f"narrative line {number} repeats an earlier narrative")
+        ids.add(identity)
+        out.append({"narrative_id": identity, "prompts": prompts})
+    if not out:
+        raise ConfigurationError("there are no narratives")
+    return out
+
+
+def _tab_id(value) -> str | None:
+    if isinstance(value, bool) or not isinstance(value, (str, int)):
+        return None
+    text = str(value)
+    return None if text in ("", "-1") else text
+
+
+def _opaque(value) -> str | None:
+    """A short digest standing for a document or URL (the trace keeps no page content)."""
+    return hashlib.sha256(str(value).encode()).hexdigest()[:24] if value else None
+
+
+def browser_observations(replay: Mapping[str, Any]) -> list[dict[str, Any]]:
+    """Timing and navigation metadata of a browser replay (``{"data": [rows]}``), without dialogue or page content."""
+    rows = replay.get("data") if isinstance(replay, Mapping) else None
+    if not isinstance(rows, list):
+        raise ConfigurationError("a browser replay is a mapping with a 'data' list of events")
+    out = []
+    for index, row in enumerate(rows):
+        if not isinstance(row, Mapping):
+            raise ConfigurationError(f"replay row {index} is not a mapping")
+        stamp = row.get("timestamp")
+        if stamp is not None and (isinstance(stamp, bool) or not isinstance(stamp, (int, float))
+                                  or not math.isfinite(stamp)):
+            raise ConfigurationError(f"replay row {index} has a non-finite timestamp")
+        action = row.get("action", {})
+        arguments = action.get("arguments", {}) if isinstance(action, Mapping) else None
+        properties = arguments.get("properties", {}) if isinstance(arguments, Mapping) else None
+        metadata = arguments.get("metadata", {}) if isinstance(arguments, Mapping) else None
+        if not isinstance(properties, Mapping) or not isinstance(metadata, Mapping):
+            raise ConfigurationError(f"replay row {index} has malformed action arguments")
+        qualifiers = properties.get("transitionQualifiers", [])
+        if not isinstance(qualifiers, list):
+            raise ConfigurationError(f"replay row {index} has malformed navigation qualifiers")
+        out.append({
+            "source_event_index": index, "source_timestamp": stamp, "source_type": row.get("type"),
+            "source_action": action.get("intent", row.get("type")),
+            "tab_id": _tab_id(properties.get("tabId")) or _tab_id(metadata.get("tabId")),
+            "origin_tab_id": _tab_id(properties.get("openerTabId")) or _tab_id(properties.get("tabIdOrigin")),
+            "source_state_id": _opaque(properties.get("documentId")),
+            "source_url_id": _opaque(metadata.get("url") or properties.get("url")),
+            "back_forward": "forward_back" in qualifiers,
+        })
+    return out
+
+
+class _BrowserMapper:
+    """The mapping state of one browser trace: branches (cursor, seed, prompt offset, newest checkpoint), the
+    live tabs, the checkpoints documents and URLs were seen at, the emitted events and the audit rows."""
+
+    def __init__(self, prompts, policy: WorkloadPolicy, source_id: str, episode_id: str):
+        self.prompts, self.policy = prompts, policy
+        self.source_id, self.episode_id = source_id, episode_id
+        self.branches = {"main": {"cursor": 0, "seed": policy.seed, "prompt_offset": 0, "checkpoint": "main:0"}}
+        self.tabs: dict[str, str] = {}
+        self.seen_state: dict[tuple, tuple] = {}
+        self.seen_url: dict[tuple, tuple] = {}
+        self.events: list[dict[str, Any]] = []
+        self.audit: list[dict[str, Any]] = []
+        self.active = "main"
+
+    def prompt_index(self, branch: str) -> int:
+        state = self.branches[branch]
+        seconds = state["cursor"] * self.policy.chunk_seconds
+        return min(len(self.prompts) - 1, int(seconds / self.policy.prompt_seconds) + state["prompt_offset"])
+
+    def emit(self, operation: str, obs, rule: str, branch: str | None = None, **extra) -> None:
+        branch = self.active if branch is None else branch
+        state = self.branches[branch]
+        self.events.append({
+            "event_id": len(self.events), "operation": operation, "branch_id": branch, "source_id": self.source_id,
+            "source_event_index": obs["source_event_index"], "source_timestamp": obs.get("source_timestamp"),
+            "source_action": obs.get("source_action"), "source_state_id": obs.get("source_state_id"),
+            "mapping_rule": rule, "provenance_class": "trace_mapped", "target_clean_chunk": state["cursor"],
+            "checkpoint_id": state["checkpoint"], "prompt_index": self.prompt_index(branch), "seed": state["seed"],
+            **extra})
+
+    # each handler returns the audit reason when the event cannot be mapped (None when it was)
+    def tab_create(self, obs):
+        tab = obs.get("tab_id")
+        if tab is None:
+            return "missing_new_tab_id"
+        if tab in self.tabs:
+            raise ConfigurationError(f"source event {obs['source_event_index']} creates tab {tab}, which is open")
+        if self.branches[self.active]["cursor"] == 0:
+            return "no_clean_video_checkpoint_yet"
+        opener = obs.get("origin_tab_id")
+        inferred = opener not in self.tabs
+        parent = self.active if inferred else self.tabs[opener]
+        child = f"branch-{len(self.branches)}"
+        index = obs["source_event_index"]
+        digest = hashlib.sha256(f"{self.episode_id}:{index}:{self.policy.seed}".encode()).digest()
+        offset = self.branches[parent]["prompt_offset"] + (1 if self.policy.branch_content == "next_prompt" else 0)
+        self.branches[child] = {"cursor": self.branches[parent]["cursor"],
+                                "seed": int.from_bytes(digest[:8], "little") % (2 ** 63),
+                                "prompt_offset": offset, "checkpoint": f"{child}:fork-{index}"}
+        self.emit("fork", obs, "tabcreate_from_active_tab" if inferred else "tabcreate_from_opener", branch=child,
+                  parent_branch_id=parent, target_checkpoint=self.branches[parent]["checkpoint"],
+                  provenance_class="inferred_relationship" if inferred else "trace_mapped", seed_policy="new_seed",
+                  content_policy=self.policy.branch_content)
+        self.tabs[tab] = child
+        return None
+
+    def tab_switch(self, obs):
+        branch = self.tabs.get(obs.get("tab_id"))
+        if branch is None:
+            return "target_tab_has_no_mapped_branch"
+        if branch != self.active:
+            self.active = branch
+            if self.branches[branch]["cursor"] > 0:
+                self.emit("resume", obs, "reactivate_recorded_tab", target_checkpoint=self.branches[branch]["checkpoint"])
+        return None
+
+    def tab_remove(self, obs):
+        branch = self.tabs.get(obs.get("tab_id"))
+        if branch is None or branch == self.active:
+            return "cannot_retire_active_or_unknown_tab_without_a_recorded_switch"
+        self.emit("retire", obs, "close_recorded_inactive_tab", branch=branch)
+        del self.tabs[obs["tab_id"]]
+        return None
+
+    def revisit(self, obs):
+        state_id, url_id = obs.get("source_state_id"), obs.get("source_url_id")
+        target = self.seen_state.get((self.active, state_id)) if state_id else None
+        inferred = False
+        if target is None and self.policy.infer_url_rewind and obs.get("back_forward"):
+            target = self.seen_url.get((self.active, url_id))
+            inferred = target is not None
+        current = self.branches[self.active]
+        if target is not None and target[2] != current["checkpoint"]:
+            operation = "rewind" if target[1] < current["cursor"] else "resume"
+            self.emit(operation, obs, "back_to_visited_url" if inferred else "revisit_recorded_document",
+                      target_checkpoint=target[2], target_clean_chunk=target[1],
+                      provenance_class="inferred_relationship" if inferred else "trace_mapped")
+            current["cursor"], current["checkpoint"] = target[1], target[2]
+            return None
+        return "back_forward_has_no_identifiable_checkpoint_target" if obs.get("back_forward") else None
+
+    def generate(self, obs):
+        if self.tabs.get(obs.get("tab_id")) != self.active:
+            return "generation_event_belongs_to_inactive_tab"
+        state = self.branches[self.active]
+        for _ in range(self.policy.chunks_per_action):
+            produced = f"{self.active}:generated-{len(self.events)}"
+            self.emit("generate", obs, "native_clean_chunks_per_selected_action", output_checkpoint=produced)
+            state["cursor"] += 1
+            state["checkpoint"] = produced
+        seen = (self.active, state["cursor"], state["checkpoint"])
+        if obs.get("source_state_id"):
+            self.seen_state.setdefault((self.active, obs["source_state_id"]), seen)
+        if obs.get("source_url_id"):
+            self.seen_url.setdefault((self.active, obs["source_url_id"]), seen)
+        return None
+
+
+def compile_browser_workload(observations: Sequence[Mapping[str, Any]], narrative: Mapping[str, Any],
+                             policy: WorkloadPolicy, *, source_id: str, episode_id: str,
+                             source_provenance: str = "recorded_trace") -> dict[str, Any]:
+    """A recorded browser trace (:func:`browser_observations`) as a trace-mapped video workload over the
+    narrative's prompts (see the section comment); validated before it is returned."""
+    if not source_id or not episode_id:
+        raise ConfigurationError("a browser workload needs a source id and an episode id")
+    if not isinstance(policy, WorkloadPolicy):
+        raise ConfigurationError("the mapping policy must be a WorkloadPolicy")
+    if source_provenance not in ("recorded_trace", "authored_fixture"):
+        raise ConfigurationError(f"source_provenance {source_provenance!r} is neither recorded_trace nor "
+                                 "authored_fixture")
+    prompts = narrative.get("prompts")
+    if not isinstance(prompts, list) or not prompts or not all(isinstance(p, str) and p.strip() for p in prompts):
+        raise ConfigurationError("the narrative needs a nonempty list of nonempty prompts")
+    mapper = _BrowserMapper(prompts, policy, source_id, episode_id)
+    last_index, last_stamp = -1, None
+    for raw in observations:
+        obs = json.loads(json.dumps(raw))
+        index, stamp = obs.get("source_event_index"), obs.get("source_timestamp")
+        if type(index) is not int or index <= last_index:
+            raise ConfigurationError("source event indices must increase strictly (the trace keeps its order)")
+        last_index = index
+        if stamp is not None and (isinstance(stamp, bool) or not isinstance(stamp, (int, float))
+                                  or not math.isfinite(stamp)):
+            raise ConfigurationError(f"source event {index} has a non-finite timestamp")
+        if stamp is not None and stamp < 0:
+            mapper.audit.append({**obs, "mapping_status": "pre_recording", "event_ids": []})
+            continue
+        first = len(mapper.events)
+        if stamp is not None and last_stamp is not None:
+            gap = stamp - last_stamp
+            if gap < 0:
+                raise ConfigurationError(f"source event {index}: timestamps go backwards (audit the clock first)")
+            active = mapper.branches[mapper.active]
+            if gap > 0 and gap >= policy.pause_gap_seconds and active["cursor"] > 0:
+                mapper.emit("pause", obs, "interaction_gap_threshold", idle_seconds=gap,
+                            target_checkpoint=active["checkpoint"])
+                mapper.emit("resume", obs, "same_branch_after_measured_gap", target_checkpoint=active["checkpoint"])
+        if stamp is not None:
+            last_stamp = stamp
+        intent, tab = obs.get("source_action"), obs.get("tab_id")
+        if obs.get("source_type") == "browser" and tab is not None and not mapper.tabs and intent != "tabcreate":
+            mapper.tabs[tab] = mapper.active  # the first browser tab seen carries the main branch
+        reason = None
+        if intent == "tabcreate":
+            reason = mapper.tab_create(obs)
+        elif intent == "tabswitch":
+            reason = mapper.tab_switch(obs)
+        elif intent == "tabremove":
+            reason = mapper.tab_remove(obs)
+        if intent == "load":
+            reason = mapper.revisit(obs) or reason
+        if obs.get("source_type") == "browser" and intent in policy.generation_intents and tab in mapper.tabs:
+            reason = mapper.generate(obs) or reason
+        mapped = len(mapper.events) > first
+        mapper.audit.append({**obs, "mapping_status": reason or ("mapped" if mapped else "audit_only"),
+                             "event_ids": list(range(first, len(mapper.events)))})
+    skipped = Counter(r["mapping_status"] for r in mapper.audit
+                      if r["mapping_status"] not in ("mapped", "audit_only", "pre_recording"))
+    workload = {
+        "schema": TRACE_SCHEMA, "episode_id": episode_id, "source_id": source_id,
+        "source_provenance": source_provenance, "narrative_id": narrative.get("narrative_id"),
+        "prompts": list(prompts), "policy": asdict(policy), "events": mapper.events, "source_audit": mapper.audit,
+        "claims": {"recorded_video_user_trace": False, "source_interaction_order_preserved": True,
+                   "native_model_executed": False, "video_quality_measured": False},
+        "summary": {"source_events": len(observations),
+                    "operations": dict(Counter(e["operation"] for e in mapper.events)),
+                    "branches": len(mapper.branches), "unmapped_reasons": dict(skipped)},
+    }
+    validate_workload(workload)
+    return workload

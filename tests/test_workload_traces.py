@@ -83,3 +83,59 @@ def test_compilation_matches_the_reference():
     for chunks, seed in ((1, 0), (2, 5)):
         assert compile_session(s, chunks_per_prompt=chunks, seed=seed) == \
             theirs.compile_session(s, chunks_per_prompt=chunks, seed=seed)
+
+
+def _browser_replay():
+    """An authored browser replay: two tabs, a pause, a revisit of an earlier document, a closed tab."""
+    def row(t, intent, tab, **props):
+        return {"timestamp": t, "type": "browser",
+                "action": {"intent": intent, "arguments": {"properties": {"tabId": tab, **props}, "metadata": {}}}}
+    return {"data": [
+        {"timestamp": -1.0, "type": "chat", "action": {"intent": "say", "arguments": {}}},
+        row(0.0, "load", 1, documentId="doc-a"),
+        row(2.0, "click", 1),
+        row(4.0, "scroll", 1),
+        row(5.0, "tabcreate", 2, openerTabId=1),
+        row(6.0, "tabswitch", 2),
+        row(7.0, "load", 2, documentId="doc-b"),
+        row(8.0, "tabswitch", 1),
+        row(60.0, "click", 1),
+        row(61.0, "load", 1, documentId="doc-a"),
+        row(62.0, "tabremove", 2),
+        row(63.0, "click", 2),
+    ]}
+
+
+def test_browser_trace_compiles_into_a_valid_workload(tmp_path):
+    from reelcache_b200.workload_traces import (WorkloadPolicy, browser_observations, compile_browser_workload,
+                                                read_narratives, replay_cpu_control, validate_workload)
+    narrative = read_narratives('{"prompts": ["a quiet street", "rain starts", "night falls"]}\n')[0]
+    observations = browser_observations(_browser_replay())
+    workload = compile_browser_workload(observations, narrative, WorkloadPolicy(chunk_seconds=5.0),
+                                        source_id="fixture", episode_id="e1", source_provenance="authored_fixture")
+    validate_workload(workload)
+    ops = [e["operation"] for e in workload["events"]]
+    assert ops.count("fork") == 1 and ops.count("retire") == 1 and ops.count("rewind") == 1
+    assert ("pause", "resume") in list(zip(ops, ops[1:]))
+    fork = next(e for e in workload["events"] if e["operation"] == "fork")
+    assert fork["parent_branch_id"] == "main" and fork["mapping_rule"] == "tabcreate_from_opener"
+    statuses = {r["source_event_index"]: r["mapping_status"] for r in workload["source_audit"]}
+    assert statuses[0] == "pre_recording"
+    assert statuses[11] == "audit_only"  # tab 2 was closed before this click: nothing is invented for it
+    assert statuses[10] == "mapped"  # closing the inactive tab 2 retired its branch
+    assert workload["claims"]["native_model_executed"] is False
+    report = replay_cpu_control(workload, tmp_path / "store")
+    assert report["schema"] == "reelcache.workload_cpu_control.v1"
+
+
+def test_browser_policy_and_narratives_are_checked():
+    from reelcache_b200.errors import ConfigurationError
+    from reelcache_b200.workload_traces import WorkloadPolicy, read_narratives
+    with pytest.raises(ConfigurationError):
+        WorkloadPolicy(chunk_seconds=0)
+    with pytest.raises(ConfigurationError):
+        WorkloadPolicy(chunk_seconds=1.0, branch_content="remix")
+    with pytest.raises(ConfigurationError):
+        read_narratives('{"prompts": ["x"]}\n{"prompts": ["x"]}\n')
+    with pytest.raises(ConfigurationError):
+        read_narratives("")
