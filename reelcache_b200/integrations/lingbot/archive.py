@@ -121,15 +121,21 @@ class LingBotArchive:
         try:
             k_copy = [t.detach().reshape(g.chunk_tokens, g.channels).clone() for t in k_pre]
             v_copy = [t.detach().reshape(g.chunk_tokens, g.channels).clone() for t in v]
-            self._futures[key] = self._worker.submit(self._publish, key, k_copy, v_copy)
+            copied = None
+            if k_copy[0].is_cuda:  # the worker's stream must not read the copies before the caller's stream made them
+                copied = torch.cuda.Event()
+                copied.record(torch.cuda.current_stream(k_copy[0].device))
+            self._futures[key] = self._worker.submit(self._publish, key, k_copy, v_copy, copied)
         except BaseException:
             self._slots.release()
             raise
 
-    def _publish(self, key: Hashable, k_pre: list, v: list) -> str:
+    def _publish(self, key: Hashable, k_pre: list, v: list, copied=None) -> str:
         info = self._keys[key]
         g = self.geometry
         try:
+            if copied is not None:
+                torch.cuda.current_stream(k_pre[0].device).wait_event(copied)
             if info["fork_at"] is not None:
                 parent = self._keys[info["fork_at"]]
                 if parent["node"] is None:
